@@ -1,0 +1,337 @@
+// extern "C" entry points of liballoy_ssd (declared in include/alloy_ssd.h):
+// argument validation on the host, then dispatch to the kernels.
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace alloy {
+
+std::string& last_error() {
+  static thread_local std::string msg;
+  return msg;
+}
+
+int current_device_checked(int* dev) {
+  int d = 0;
+  ALLOY_CUDA(cudaGetDevice(&d));
+  cudaDeviceProp prop;
+  ALLOY_CUDA(cudaGetDeviceProperties(&prop, d));
+  if (prop.major != 10)
+    return fail(ALLOY_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", d,
+                prop.major, prop.minor);
+  if (dev) *dev = d;
+  return ALLOY_OK;
+}
+
+namespace {
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+int check_vec(const alloy_tensor_t* t, const char* name, int64_t n, unsigned mask, bool optional) {
+  if (optional && !present(t)) return ALLOY_OK;
+  const int64_t shape[1] = {n};
+  return check_tensor(t, name, 1, shape, mask);
+}
+
+int check_dims(const alloy_ssd_dims_t* d, int64_t* h0, int64_t* hc) {
+  if (d == nullptr) return fail(ALLOY_ERR_INVALID_ARG, "dims: null");
+  if (d->n_heads <= 0 || d->head_dim <= 0 || d->d_state <= 0 || d->n_groups <= 0)
+    return fail(ALLOY_ERR_INVALID_ARG, "dims: n_heads, head_dim, d_state, n_groups must be > 0");
+  if (d->n_heads % d->n_groups != 0)
+    return fail(ALLOY_ERR_INVALID_ARG, "dims: n_heads (%lld) not divisible by n_groups (%lld)",
+                (long long)d->n_heads, (long long)d->n_groups);
+  if (d->d_conv < 2 || d->d_conv > 8)
+    return fail(ALLOY_ERR_UNSUPPORTED, "dims: d_conv must be in [2, 8]");
+  if (d->chunk_size <= 0) return fail(ALLOY_ERR_INVALID_ARG, "dims: chunk_size must be > 0");
+  const int64_t count = d->head_count == 0 ? d->n_heads - d->head_begin : d->head_count;
+  if (d->head_begin < 0 || count <= 0 || d->head_begin + count > d->n_heads)
+    return fail(ALLOY_ERR_INVALID_ARG, "dims: head range [%lld, +%lld) outside [0, %lld)",
+                (long long)d->head_begin, (long long)count, (long long)d->n_heads);
+  if (d->n_heads * d->head_dim > (1 << 24) || d->d_state > 1024 || d->head_dim > 1024)
+    return fail(ALLOY_ERR_UNSUPPORTED, "dims: sizes out of the supported range");
+  *h0 = d->head_begin;
+  *hc = count;
+  return ALLOY_OK;
+}
+
+}  // namespace
+}  // namespace alloy
+
+using namespace alloy;
+
+extern "C" {
+
+int alloy_abi_version(void) { return ALLOY_SSD_ABI_VERSION; }
+
+const char* alloy_build_info(void) {
+  return "liballoy_ssd " __DATE__ " sm_100a (tcgen05 SSD, conv1d+SiLU, decode step)";
+}
+
+size_t alloy_get_last_error(char* buf, size_t len) {
+  const std::string& m = last_error();
+  if (buf && len) {
+    const size_t n = std::min(len - 1, m.size());
+    memcpy(buf, m.data(), n);
+    buf[n] = '\0';
+  }
+  return m.size();
+}
+
+namespace {
+int conv_entry(const alloy_tensor_t* x_padded, const alloy_tensor_t* weight,
+               const alloy_tensor_t* bias, alloy_tensor_t* out, bool silu, void* stream) {
+  last_error().clear();
+  ALLOY_TRY(check_tensor(x_padded, "x_padded", 3, nullptr, kAnyFloat));
+  ALLOY_TRY(check_tensor(weight, "weight", 2, nullptr, kAnyFloat));
+  const int64_t B = x_padded->shape[0], Lp = x_padded->shape[1], C = x_padded->shape[2];
+  const int64_t K = weight->shape[1];
+  if (weight->shape[0] != C)
+    return fail(ALLOY_ERR_INVALID_ARG, "weight: dim 0 is %lld, expected C = %lld",
+                (long long)weight->shape[0], (long long)C);
+  if (K < 1 || K > 8) return fail(ALLOY_ERR_UNSUPPORTED, "weight: K must be in [1, 8]");
+  if (Lp < K - 1) return fail(ALLOY_ERR_INVALID_ARG, "x_padded: fewer than K-1 rows");
+  ALLOY_TRY(check_vec(bias, "bias", C, kAnyFloat, true));
+  const int64_t oshape[3] = {B, Lp - K + 1, C};
+  ALLOY_TRY(check_tensor(out, "out", 3, oshape, 1u << x_padded->dtype));
+  if (B * Lp * C >= (int64_t)1 << 40) return fail(ALLOY_ERR_UNSUPPORTED, "x_padded: too large");
+  ALLOY_TRY(current_device_checked(nullptr));
+  return conv1d_silu(x_padded, weight, bias, out, silu, as_stream(stream));
+}
+}  // namespace
+
+int alloy_conv1d_silu(const alloy_tensor_t* x_padded, const alloy_tensor_t* weight,
+                      const alloy_tensor_t* bias, alloy_tensor_t* out, void* stream) {
+  return conv_entry(x_padded, weight, bias, out, true, stream);
+}
+
+int alloy_depthwise_conv1d(const alloy_tensor_t* x_padded, const alloy_tensor_t* weight,
+                           const alloy_tensor_t* bias, alloy_tensor_t* out, void* stream) {
+  return conv_entry(x_padded, weight, bias, out, false, stream);
+}
+
+int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t* dt_raw,
+                       const alloy_tensor_t* conv_w, const alloy_tensor_t* conv_b,
+                       const alloy_tensor_t* dt_bias, const alloy_tensor_t* A_log,
+                       const alloy_tensor_t* D, const alloy_tensor_t* ssm_in,
+                       const alloy_tensor_t* conv_in, alloy_tensor_t* y,
+                       alloy_tensor_t* ssm_out, alloy_tensor_t* conv_out,
+                       const alloy_ssd_dims_t* dims, void* stream) {
+  last_error().clear();
+  int64_t h0 = 0, hc = 0;
+  ALLOY_TRY(check_dims(dims, &h0, &hc));
+  const int64_t H = dims->n_heads, P = dims->head_dim, N = dims->d_state, G = dims->n_groups,
+                K = dims->d_conv;
+  const int64_t conv_dim = H * P + 2 * G * N;
+  ALLOY_TRY(check_tensor(xBC, "xBC", 3, nullptr, kAnyFloat));
+  const int64_t B = xBC->shape[0], L = xBC->shape[1];
+  if (xBC->shape[2] != conv_dim)
+    return fail(ALLOY_ERR_INVALID_ARG, "xBC: dim 2 is %lld, expected H*P + 2*G*N = %lld",
+                (long long)xBC->shape[2], (long long)conv_dim);
+  if (xBC->stride[2] != 1) return fail(ALLOY_ERR_INVALID_ARG, "xBC: channel stride must be 1");
+  const unsigned act = 1u << xBC->dtype;
+  const int64_t dts[3] = {B, L, H};
+  ALLOY_TRY(check_tensor(dt_raw, "dt_raw", 3, dts, kAnyFloat));
+  const int64_t cws[2] = {conv_dim, K};
+  ALLOY_TRY(check_tensor(conv_w, "conv_w", 2, cws, kF32));
+  ALLOY_TRY(check_vec(conv_b, "conv_b", conv_dim, kF32, true));
+  ALLOY_TRY(check_vec(dt_bias, "dt_bias", H, kF32, false));
+  ALLOY_TRY(check_vec(A_log, "A_log", H, kF32, false));
+  ALLOY_TRY(check_vec(D, "D", H, kF32, true));
+  // states: [B, H, N, P] in any axis order given through strides
+  const int64_t ss[4] = {B, H, N, P};
+  if (present(ssm_in)) ALLOY_TRY(check_tensor(ssm_in, "ssm_in", 4, ss, kF32));
+  if (present(ssm_out)) ALLOY_TRY(check_tensor(ssm_out, "ssm_out", 4, ss, kF32));
+  const int64_t cs[3] = {B, K - 1, conv_dim};
+  if (present(conv_in)) ALLOY_TRY(check_tensor(conv_in, "conv_in", 3, cs, act));
+  if (present(conv_out)) ALLOY_TRY(check_tensor(conv_out, "conv_out", 3, cs, act));
+  const int64_t ys[4] = {B, L, H, P};
+  ALLOY_TRY(check_tensor(y, "y", 4, ys, act));
+  if (L == 0 && present(conv_out) == false && present(ssm_out) == false) return ALLOY_OK;
+  ALLOY_TRY(current_device_checked(nullptr));
+  const cudaStream_t s = as_stream(stream);
+
+  SsdArgs a;
+  memset(&a, 0, sizeof(a));
+  a.mode = 0;
+  a.B = (int)B; a.L = (int)L; a.H = (int)H; a.P = (int)P; a.N = (int)N; a.G = (int)G;
+  a.K = (int)K; a.head_begin = (int)h0; a.head_count = (int)hc;
+  a.xBC = xBC->data; a.xbc_bf16 = xBC->dtype == ALLOY_BF16;
+  a.xbc_sb = xBC->stride[0]; a.xbc_st = xBC->stride[1];
+  a.dt_raw = dt_raw->data; a.dt_bf16 = dt_raw->dtype == ALLOY_BF16;
+  a.dt_sb = dt_raw->stride[0]; a.dt_st = dt_raw->stride[1]; a.dt_sh = dt_raw->stride[2];
+  a.conv_w = static_cast<const float*>(conv_w->data);
+  a.cw_sc = conv_w->stride[0]; a.cw_sk = conv_w->stride[1];
+  if (present(conv_b)) { a.conv_b = static_cast<const float*>(conv_b->data); a.cb_s = conv_b->stride[0]; }
+  a.dt_bias = static_cast<const float*>(dt_bias->data); a.dtb_s = dt_bias->stride[0];
+  a.A_log = static_cast<const float*>(A_log->data); a.al_s = A_log->stride[0];
+  if (present(D)) { a.Dp = static_cast<const float*>(D->data); a.d_s = D->stride[0]; }
+  if (present(conv_in)) {
+    a.conv_in = conv_in->data; a.ci_bf16 = conv_in->dtype == ALLOY_BF16;
+    a.ci_sb = conv_in->stride[0]; a.ci_sk = conv_in->stride[1]; a.ci_sc = conv_in->stride[2];
+  }
+  if (present(ssm_in)) {
+    a.ssm_in = static_cast<const float*>(ssm_in->data);
+    a.si_sb = ssm_in->stride[0]; a.si_sh = ssm_in->stride[1];
+    a.si_sn = ssm_in->stride[2]; a.si_sp = ssm_in->stride[3];
+  }
+  if (present(ssm_out)) {
+    a.ssm_out = static_cast<float*>(ssm_out->data);
+    a.so_sb = ssm_out->stride[0]; a.so_sh = ssm_out->stride[1];
+    a.so_sn = ssm_out->stride[2]; a.so_sp = ssm_out->stride[3];
+  }
+  a.y = y->data; a.y_bf16 = y->dtype == ALLOY_BF16;
+  a.y_sb = y->stride[0]; a.y_st = y->stride[1]; a.y_sh = y->stride[2]; a.y_sp = y->stride[3];
+
+  if (L > 0) {
+    if (ssd_tc_supported(a)) {
+      ALLOY_TRY(ssd_tc(a, s));
+    } else {
+      ALLOY_TRY(ssd_simt(a, s));
+    }
+  } else if (present(ssm_out)) {
+    // zero tokens: the state passes through unchanged
+    return fail(ALLOY_ERR_UNSUPPORTED, "ssd_combined: L = 0 with ssm_out");
+  }
+  if (present(conv_out)) {
+    // must run after the scan: the scan reads conv_in, which conv_out may alias
+    ALLOY_TRY(conv_state_update(xBC, present(conv_in) ? conv_in : nullptr, conv_out, (int)H,
+                                (int)P, (int)N, (int)G, (int)K, (int)h0, (int)hc, s));
+  }
+  return ALLOY_OK;
+}
+
+int alloy_selective_scan(const alloy_tensor_t* x, const alloy_tensor_t* A_disc,
+                         const alloy_tensor_t* log_a, const alloy_tensor_t* Bm,
+                         const alloy_tensor_t* Cm, const alloy_tensor_t* ssm_in,
+                         alloy_tensor_t* y, alloy_tensor_t* ssm_out, void* stream) {
+  last_error().clear();
+  ALLOY_TRY(check_tensor(x, "x", 4, nullptr, kAnyFloat));
+  const int64_t B = x->shape[0], L = x->shape[1], H = x->shape[2], P = x->shape[3];
+  const int64_t bh[3] = {B, L, H};
+  if (present(log_a)) {
+    ALLOY_TRY(check_tensor(log_a, "log_a", 3, bh, kF32));
+  } else {
+    ALLOY_TRY(check_tensor(A_disc, "A_disc", 3, bh, kAnyFloat));
+  }
+  ALLOY_TRY(check_tensor(Bm, "B", 4, nullptr, kAnyFloat));
+  const int64_t Gb = Bm->shape[2], N = Bm->shape[3];
+  const int64_t bs[4] = {B, L, Gb, N};
+  ALLOY_TRY(check_tensor(Bm, "B", 4, bs, kAnyFloat));
+  ALLOY_TRY(check_tensor(Cm, "C", 4, bs, kAnyFloat));
+  if (Gb <= 0 || H % Gb != 0)
+    return fail(ALLOY_ERR_INVALID_ARG, "B/C: group dim %lld does not divide n_heads %lld",
+                (long long)Gb, (long long)H);
+  const int64_t ss[4] = {B, H, N, P};
+  if (present(ssm_in)) ALLOY_TRY(check_tensor(ssm_in, "ssm_in", 4, ss, kF32));
+  if (present(ssm_out)) ALLOY_TRY(check_tensor(ssm_out, "ssm_out", 4, ss, kF32));
+  const int64_t ys[4] = {B, L, H, P};
+  ALLOY_TRY(check_tensor(y, "y", 4, ys, kAnyFloat));
+  if (x->stride[3] != 1) return fail(ALLOY_ERR_INVALID_ARG, "x: head_dim stride must be 1");
+  if (B == 0 || H == 0) return ALLOY_OK;
+  if (L == 0) return fail(ALLOY_ERR_UNSUPPORTED, "selective_scan: L = 0");
+  ALLOY_TRY(current_device_checked(nullptr));
+
+  SsdArgs a;
+  memset(&a, 0, sizeof(a));
+  a.mode = 1;
+  a.B = (int)B; a.L = (int)L; a.H = (int)H; a.P = (int)P; a.N = (int)N; a.G = 1; a.K = 1;
+  a.head_begin = 0; a.head_count = (int)H; a.Gbc = (int)Gb;
+  a.x = x->data; a.x_bf16 = x->dtype == ALLOY_BF16;
+  a.x_sb = x->stride[0]; a.x_st = x->stride[1]; a.x_sh = x->stride[2];
+  if (present(log_a)) {
+    a.log_a = static_cast<const float*>(log_a->data);
+    a.la_sb = log_a->stride[0]; a.la_st = log_a->stride[1]; a.la_sh = log_a->stride[2];
+  } else {
+    a.A_disc = A_disc->data; a.ad_bf16 = A_disc->dtype == ALLOY_BF16;
+    a.ad_sb = A_disc->stride[0]; a.ad_st = A_disc->stride[1]; a.ad_sh = A_disc->stride[2];
+  }
+  a.Bm = Bm->data; a.bm_bf16 = Bm->dtype == ALLOY_BF16;
+  a.bm_sb = Bm->stride[0]; a.bm_st = Bm->stride[1]; a.bm_sg = Bm->stride[2]; a.bm_sn = Bm->stride[3];
+  a.Cm = Cm->data; a.cm_bf16 = Cm->dtype == ALLOY_BF16;
+  a.cm_sb = Cm->stride[0]; a.cm_st = Cm->stride[1]; a.cm_sg = Cm->stride[2]; a.cm_sn = Cm->stride[3];
+  if (present(ssm_in)) {
+    a.ssm_in = static_cast<const float*>(ssm_in->data);
+    a.si_sb = ssm_in->stride[0]; a.si_sh = ssm_in->stride[1];
+    a.si_sn = ssm_in->stride[2]; a.si_sp = ssm_in->stride[3];
+  }
+  if (present(ssm_out)) {
+    a.ssm_out = static_cast<float*>(ssm_out->data);
+    a.so_sb = ssm_out->stride[0]; a.so_sh = ssm_out->stride[1];
+    a.so_sn = ssm_out->stride[2]; a.so_sp = ssm_out->stride[3];
+  }
+  a.y = y->data; a.y_bf16 = y->dtype == ALLOY_BF16;
+  a.y_sb = y->stride[0]; a.y_st = y->stride[1]; a.y_sh = y->stride[2]; a.y_sp = y->stride[3];
+  return ssd_simt(a, as_stream(stream));
+}
+
+int alloy_ssd_decode_step(const alloy_tensor_t* xBC_tok, const alloy_tensor_t* dt_tok,
+                          const alloy_tensor_t* conv_w, const alloy_tensor_t* conv_b,
+                          const alloy_tensor_t* dt_bias, const alloy_tensor_t* A_log,
+                          const alloy_tensor_t* D, alloy_tensor_t* conv_state,
+                          alloy_tensor_t* ssm_state, alloy_tensor_t* y,
+                          const alloy_ssd_dims_t* dims, void* stream) {
+  last_error().clear();
+  int64_t h0 = 0, hc = 0;
+  ALLOY_TRY(check_dims(dims, &h0, &hc));
+  const int64_t H = dims->n_heads, P = dims->head_dim, N = dims->d_state, G = dims->n_groups,
+                K = dims->d_conv;
+  const int64_t conv_dim = H * P + 2 * G * N;
+  ALLOY_TRY(check_tensor(xBC_tok, "xBC_tok", 2, nullptr, kAnyFloat));
+  const int64_t B = xBC_tok->shape[0];
+  if (xBC_tok->shape[1] != conv_dim)
+    return fail(ALLOY_ERR_INVALID_ARG, "xBC_tok: dim 1 is %lld, expected %lld",
+                (long long)xBC_tok->shape[1], (long long)conv_dim);
+  if (xBC_tok->stride[1] != 1) return fail(ALLOY_ERR_INVALID_ARG, "xBC_tok: channel stride must be 1");
+  const unsigned act = 1u << xBC_tok->dtype;
+  const int64_t dts[2] = {B, H};
+  ALLOY_TRY(check_tensor(dt_tok, "dt_tok", 2, dts, kAnyFloat));
+  const int64_t cws[2] = {conv_dim, K};
+  ALLOY_TRY(check_tensor(conv_w, "conv_w", 2, cws, kF32));
+  ALLOY_TRY(check_vec(conv_b, "conv_b", conv_dim, kF32, true));
+  ALLOY_TRY(check_vec(dt_bias, "dt_bias", H, kF32, false));
+  ALLOY_TRY(check_vec(A_log, "A_log", H, kF32, false));
+  ALLOY_TRY(check_vec(D, "D", H, kF32, true));
+  const int64_t cs[3] = {B, K - 1, conv_dim};
+  ALLOY_TRY(check_tensor(conv_state, "conv_state", 3, cs, act));
+  const int64_t ss[4] = {B, H, N, P};
+  ALLOY_TRY(check_tensor(ssm_state, "ssm_state", 4, ss, kF32));
+  const int64_t ys[3] = {B, H, P};
+  ALLOY_TRY(check_tensor(y, "y", 3, ys, act));
+  if (y->stride[2] != 1) return fail(ALLOY_ERR_INVALID_ARG, "y: head_dim stride must be 1");
+  int state_pn;
+  int64_t row;
+  if (ssm_state->stride[2] == 1 && N > 1) {          // N contiguous: [.., P, N]
+    state_pn = 1; row = ssm_state->stride[3];
+  } else if (ssm_state->stride[3] == 1) {            // P contiguous: [.., N, P]
+    state_pn = 0; row = ssm_state->stride[2];
+  } else {
+    return fail(ALLOY_ERR_INVALID_ARG, "ssm_state: one of the d_state / head_dim strides must be 1");
+  }
+  if (B == 0) return ALLOY_OK;
+  ALLOY_TRY(current_device_checked(nullptr));
+
+  DecodeArgs a;
+  memset(&a, 0, sizeof(a));
+  a.B = (int)B; a.H = (int)H; a.P = (int)P; a.N = (int)N; a.G = (int)G; a.K = (int)K;
+  a.head_begin = (int)h0; a.head_count = (int)hc;
+  a.xbc = xBC_tok->data; a.x_bf16 = xBC_tok->dtype == ALLOY_BF16; a.x_sb = xBC_tok->stride[0];
+  a.dt = dt_tok->data; a.dt_bf16 = dt_tok->dtype == ALLOY_BF16;
+  a.dt_sb = dt_tok->stride[0]; a.dt_sh = dt_tok->stride[1];
+  a.conv_w = static_cast<const float*>(conv_w->data);
+  a.cw_sc = conv_w->stride[0]; a.cw_sk = conv_w->stride[1];
+  if (present(conv_b)) { a.conv_b = static_cast<const float*>(conv_b->data); a.cb_s = conv_b->stride[0]; }
+  a.dt_bias = static_cast<const float*>(dt_bias->data); a.dtb_s = dt_bias->stride[0];
+  a.A_log = static_cast<const float*>(A_log->data); a.al_s = A_log->stride[0];
+  if (present(D)) { a.Dp = static_cast<const float*>(D->data); a.d_s = D->stride[0]; }
+  a.conv_state = conv_state->data; a.cs_bf16 = conv_state->dtype == ALLOY_BF16;
+  a.cs_sb = conv_state->stride[0]; a.cs_sk = conv_state->stride[1]; a.cs_sc = conv_state->stride[2];
+  a.state = static_cast<float*>(ssm_state->data);
+  a.st_sb = ssm_state->stride[0]; a.st_sh = ssm_state->stride[1]; a.st_row = row;
+  a.state_pn = state_pn;
+  a.y = y->data; a.y_bf16 = y->dtype == ALLOY_BF16; a.y_sb = y->stride[0]; a.y_sh = y->stride[1];
+  return ssd_decode_step(a, as_stream(stream));
+}
+
+}  // extern "C"

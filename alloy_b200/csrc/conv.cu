@@ -1,0 +1,199 @@
+// Causal depthwise conv1d + SiLU (alloy/models/mamba_kernels.py:17-50,
+// alloy/models/mamba_block.py:144-158 + :455).
+//
+// Tiled kernel: a CTA owns TT timesteps x (32 x 16-byte) channel vectors of
+// one batch row.  It stages the TT + K - 1 input rows of its channel window
+// in shared memory with 128-bit channel-contiguous loads (the K-1 row halo is
+// shared by all outputs of the tile), then each thread produces 8 timesteps
+// of one 16-byte channel vector with an fp32 sliding window.  HBM traffic is
+// one read of the input and one write of the output; the halo re-read is
+// (K-1)/TT of the input and hits L2.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace alloy {
+
+namespace {
+
+constexpr int kConvThreads = 256;
+constexpr int kConvTT = 64;                     // timesteps per tile
+constexpr int kConvRowsPerThread = kConvTT / (kConvThreads / 32);  // 8
+
+template <typename T> struct Vec;
+template <> struct Vec<float> { static constexpr int N = 4; };
+template <> struct Vec<__nv_bfloat16> { static constexpr int N = 8; };
+
+__device__ __forceinline__ uint4 ldg_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack(const uint4& u, float* f);
+template <>
+__device__ __forceinline__ void unpack<float>(const uint4& u, float* f) {
+  f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+  f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+}
+template <>
+__device__ __forceinline__ void unpack<__nv_bfloat16>(const uint4& u, float* f) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack(const float* f);
+template <>
+__device__ __forceinline__ uint4 pack<float>(const float* f) {
+  return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                    __float_as_uint(f[3]));
+}
+template <>
+__device__ __forceinline__ uint4 pack<__nv_bfloat16>(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <typename T, int K, bool SILU>
+__global__ void __launch_bounds__(kConvThreads)
+conv1d_silu_tile_kernel(const T* __restrict__ xp, int64_t xp_sb, int64_t xp_st,
+                        const void* __restrict__ w, int w_bf16, int64_t w_sc, int64_t w_sk,
+                        const void* __restrict__ bias, int b_bf16, int64_t b_s,
+                        T* __restrict__ out, int64_t o_sb, int64_t o_st, int L, int C) {
+  constexpr int V = Vec<T>::N;
+  constexpr int CW = 32 * V;
+  __shared__ uint4 tile[(kConvTT + K - 1) * 32];
+
+  const int b = blockIdx.z;
+  const int t0 = blockIdx.y * kConvTT;
+  const int c0 = blockIdx.x * CW;
+  const int nt = min(kConvTT, L - t0);
+  const int rows = nt + K - 1;
+  const int nvec = min(CW, C - c0) / V;
+
+  const T* src = xp + (int64_t)b * xp_sb + (int64_t)t0 * xp_st + c0;
+  for (int i = threadIdx.x; i < rows * 32; i += kConvThreads) {
+    const int r = i >> 5, v = i & 31;
+    if (v < nvec) tile[i] = ldg_v4(src + (int64_t)r * xp_st + v * V);
+  }
+  __syncthreads();
+
+  const int v = threadIdx.x & 31;
+  const int r0 = (threadIdx.x >> 5) * kConvRowsPerThread;
+  if (v >= nvec || r0 >= nt) return;
+
+  const int c = c0 + v * V;
+  float wr[V][K], br[V];
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) wr[j][k] = load_any(w, (int64_t)(c + j) * w_sc + k * w_sk, w_bf16);
+    br[j] = bias ? load_any(bias, (int64_t)(c + j) * b_s, b_bf16) : 0.f;
+  }
+
+  float win[K][V];
+#pragma unroll
+  for (int k = 0; k < K - 1; ++k) unpack<T>(tile[(r0 + k) * 32 + v], win[k]);
+
+  T* dst = out + (int64_t)b * o_sb + (int64_t)(t0 + r0) * o_st + c;
+#pragma unroll
+  for (int i = 0; i < kConvRowsPerThread; ++i) {
+    if (r0 + i >= nt) break;
+    unpack<T>(tile[(r0 + i + K - 1) * 32 + v], win[K - 1]);
+    float o[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      float acc = br[j];
+#pragma unroll
+      for (int k = 0; k < K; ++k) acc = fmaf(win[k][j], wr[j][k], acc);
+      o[j] = SILU ? silu_f32(acc) : acc;
+    }
+    *reinterpret_cast<uint4*>(dst + (int64_t)i * o_st) = pack<T>(o);
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k)
+#pragma unroll
+      for (int j = 0; j < V; ++j) win[k][j] = win[k + 1][j];
+  }
+}
+
+// Any layout / alignment / K: one thread per output element.
+__global__ void conv1d_silu_scalar_kernel(const void* __restrict__ xp, int x_bf16, int64_t xp_sb,
+                                          int64_t xp_st, int64_t xp_sc,
+                                          const void* __restrict__ w, int w_bf16, int64_t w_sc,
+                                          int64_t w_sk, const void* __restrict__ bias, int b_bf16,
+                                          int64_t b_s, void* __restrict__ out, int o_bf16,
+                                          int64_t o_sb, int64_t o_st, int64_t o_sc, int B, int L,
+                                          int C, int K, int silu) {
+  const int64_t total = (int64_t)B * L * C;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const int t = (int)((i / C) % L);
+    const int b = (int)(i / ((int64_t)C * L));
+    float acc = bias ? load_any(bias, (int64_t)c * b_s, b_bf16) : 0.f;
+    for (int k = 0; k < K; ++k)
+      acc = fmaf(load_any(xp, b * xp_sb + (int64_t)(t + k) * xp_st + c * xp_sc, x_bf16),
+                 load_any(w, (int64_t)c * w_sc + k * w_sk, w_bf16), acc);
+    store_any(out, b * o_sb + (int64_t)t * o_st + c * o_sc, o_bf16, silu ? silu_f32(acc) : acc);
+  }
+}
+
+template <typename T, bool SILU>
+int launch_tile(const alloy_tensor_t* x, const alloy_tensor_t* w, const alloy_tensor_t* bias,
+                alloy_tensor_t* out, int B, int L, int C, cudaStream_t s) {
+  constexpr int V = Vec<T>::N;
+  dim3 grid((C + 32 * V - 1) / (32 * V), (L + kConvTT - 1) / kConvTT, B);
+  const void* bptr = present(bias) ? bias->data : nullptr;
+  conv1d_silu_tile_kernel<T, 4, SILU><<<grid, kConvThreads, 0, s>>>(
+      static_cast<const T*>(x->data), x->stride[0], x->stride[1], w->data,
+      w->dtype == ALLOY_BF16, w->stride[0], w->stride[1], bptr,
+      bptr ? bias->dtype == ALLOY_BF16 : 0, bptr ? bias->stride[0] : 0,
+      static_cast<T*>(out->data), out->stride[0], out->stride[1], L, C);
+  return check_launch("conv1d_silu_tile_kernel");
+}
+
+}  // namespace
+
+int conv1d_silu(const alloy_tensor_t* x, const alloy_tensor_t* w, const alloy_tensor_t* bias,
+                alloy_tensor_t* out, bool silu, cudaStream_t s) {
+  const int B = (int)x->shape[0], Lp = (int)x->shape[1], C = (int)x->shape[2];
+  const int K = (int)w->shape[1];
+  const int L = Lp - K + 1;
+  if (B == 0 || L == 0 || C == 0) return ALLOY_OK;
+  const int es = elem_size(x->dtype);
+  const int V = 16 / es;
+  const bool vec_ok = K == 4 && x->stride[2] == 1 && out->stride[2] == 1 && C % V == 0 &&
+                      aligned16(x->data) && aligned16(out->data) &&
+                      (x->stride[0] * es) % 16 == 0 && (x->stride[1] * es) % 16 == 0 &&
+                      (out->stride[0] * es) % 16 == 0 && (out->stride[1] * es) % 16 == 0;
+  if (vec_ok) {
+    if (silu)
+      return x->dtype == ALLOY_BF16 ? launch_tile<__nv_bfloat16, true>(x, w, bias, out, B, L, C, s)
+                                    : launch_tile<float, true>(x, w, bias, out, B, L, C, s);
+    return x->dtype == ALLOY_BF16 ? launch_tile<__nv_bfloat16, false>(x, w, bias, out, B, L, C, s)
+                                  : launch_tile<float, false>(x, w, bias, out, B, L, C, s);
+  }
+  const int64_t total = (int64_t)B * L * C;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
+  const void* bptr = present(bias) ? bias->data : nullptr;
+  conv1d_silu_scalar_kernel<<<blocks, 256, 0, s>>>(
+      x->data, x->dtype == ALLOY_BF16, x->stride[0], x->stride[1], x->stride[2], w->data,
+      w->dtype == ALLOY_BF16, w->stride[0], w->stride[1], bptr,
+      bptr ? bias->dtype == ALLOY_BF16 : 0, bptr ? bias->stride[0] : 0, out->data,
+      out->dtype == ALLOY_BF16, out->stride[0], out->stride[1], out->stride[2], B, L, C, K,
+      silu ? 1 : 0);
+  return check_launch("conv1d_silu_scalar_kernel");
+}
+
+}  // namespace alloy

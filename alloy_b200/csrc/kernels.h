@@ -1,0 +1,76 @@
+// Internal launch interfaces of liballoy_ssd (host side).  Arguments have been
+// validated by capi.cu before any of these is called.
+#pragma once
+
+#include "common.cuh"
+
+namespace alloy {
+
+// conv.cu
+int conv1d_silu(const alloy_tensor_t* x_padded, const alloy_tensor_t* w,
+                const alloy_tensor_t* bias, alloy_tensor_t* out, bool silu, cudaStream_t s);
+
+// Flattened view of one SSD call, shared by the SSD kernels.  Strides are in
+// elements.  mode 0: raw xBC (conv + discretisation fused); mode 1:
+// pre-discretised inputs (x, log decay, B, C).
+struct SsdArgs {
+  int mode;
+  int B, L, H, P, N, G, K;
+  int head_begin, head_count;
+  // mode 0 inputs
+  const void* xBC; int xbc_bf16; int64_t xbc_sb, xbc_st;
+  const void* dt_raw; int dt_bf16; int64_t dt_sb, dt_st, dt_sh;
+  const float* conv_w; int64_t cw_sc, cw_sk;
+  const float* conv_b; int64_t cb_s;
+  const float* dt_bias; int64_t dtb_s;
+  const float* A_log; int64_t al_s;
+  const float* Dp; int64_t d_s;
+  const void* conv_in; int ci_bf16; int64_t ci_sb, ci_sk, ci_sc;
+  // mode 1 inputs
+  const void* x; int x_bf16; int64_t x_sb, x_st, x_sh;
+  const void* A_disc; int ad_bf16; int64_t ad_sb, ad_st, ad_sh;
+  const float* log_a; int64_t la_sb, la_st, la_sh;
+  const void* Bm; int bm_bf16; int64_t bm_sb, bm_st, bm_sg, bm_sn;
+  const void* Cm; int cm_bf16; int64_t cm_sb, cm_st, cm_sg, cm_sn;
+  int Gbc;
+  // states and output
+  const float* ssm_in; int64_t si_sb, si_sh, si_sn, si_sp;
+  float* ssm_out; int64_t so_sb, so_sh, so_sn, so_sp;
+  void* y; int y_bf16; int64_t y_sb, y_st, y_sh, y_sp;
+};
+
+// ssd_simt.cu: fp32 CUDA-core SSD (any sizes that fit shared memory).
+int ssd_simt(const SsdArgs& a, cudaStream_t s);
+size_t ssd_simt_smem_bytes(int P, int N);
+
+// Rolls the conv cache after a prefill of L tokens: conv_out[b, j, c] =
+// x_padded[b, L + j, c] for the channels of heads [h0, h0+hc) and of their
+// groups' B and C columns.  Reads every source before writing, so conv_out
+// may alias conv_in.
+int conv_state_update(const alloy_tensor_t* xBC, const alloy_tensor_t* conv_in,
+                      alloy_tensor_t* conv_out, int H, int P, int N, int G, int K,
+                      int head_begin, int head_count, cudaStream_t s);
+
+// decode.cu
+struct DecodeArgs {
+  int B, H, P, N, G, K, head_begin, head_count;
+  const void* xbc; int x_bf16; int64_t x_sb;
+  const void* dt; int dt_bf16; int64_t dt_sb, dt_sh;
+  const float* conv_w; int64_t cw_sc, cw_sk;
+  const float* conv_b; int64_t cb_s;
+  const float* dt_bias; int64_t dtb_s;
+  const float* A_log; int64_t al_s;
+  const float* Dp; int64_t d_s;
+  void* conv_state; int cs_bf16; int64_t cs_sb, cs_sk, cs_sc;
+  float* state; int64_t st_sb, st_sh, st_row;   // row = the non-unit stride of (N, P)
+  int state_pn;                                 // 1: [.., P, N] (N contiguous); 0: [.., N, P]
+  void* y; int y_bf16; int64_t y_sb, y_sh;
+};
+int ssd_decode_step(const DecodeArgs& a, cudaStream_t s);
+
+// ssd_tc.cu: tcgen05 tensor-core SSD for bf16 inputs (mode 0 only).
+// Returns ALLOY_ERR_UNSUPPORTED (and launches nothing) for sizes it does not cover.
+int ssd_tc(const SsdArgs& a, cudaStream_t s);
+bool ssd_tc_supported(const SsdArgs& a);
+
+}  // namespace alloy

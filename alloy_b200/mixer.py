@@ -1,0 +1,194 @@
+"""Functional API of the Mamba-2 mixer hot path over torch CUDA tensors.
+
+Each function validates devices on the host and calls one liballoy_ssd entry
+point on torch's current CUDA stream.  Inputs must already be CUDA tensors:
+there is no CPU path and no fallback.
+
+Layouts follow gxcsoccer/alloy (alloy/models/mamba_block.py):
+``xBC [B, L, H*P + 2*G*N]`` = conv input ``[x | B | C]``; ``dt_raw [B, L, H]``;
+``ssm_state [B, H, N, P]`` fp32 and ``conv_state [B, K-1, conv_dim]``.
+State arguments may be any permutation of those axes (given by strides), so
+``[B, H, P, N]`` states are passed as ``state.transpose(2, 3)``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "conv1d_silu", "depthwise_conv1d", "ssd_combined", "selective_scan",
+    "ssd_decode_step",
+]
+
+
+def _cuda(name, t):
+    if t is None:
+        return None
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name}: expected a torch.Tensor, got {type(t).__name__}")
+    if not t.is_cuda:
+        raise ValueError(f"{name}: must be a CUDA tensor (liballoy_ssd has no CPU path)")
+    return t
+
+
+def _same_device(*named):
+    dev = None
+    for name, t in named:
+        if t is None:
+            continue
+        _cuda(name, t)
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"{name}: on {t.device}, expected {dev}")
+    return dev
+
+
+def _f32(t):
+    return None if t is None else (t if t.dtype == torch.float32 else t.float())
+
+
+def _dims(n_heads, head_dim, d_state, n_groups, d_conv, chunk_size, head_begin, head_count):
+    d = _lib.Dims()
+    d.n_heads, d.head_dim, d.d_state, d.n_groups = n_heads, head_dim, d_state, n_groups
+    d.d_conv, d.chunk_size = d_conv, chunk_size
+    d.head_begin, d.head_count = head_begin, head_count
+    return d
+
+
+def _conv(entry, x_padded, weight, bias, L, out):
+    dev = _same_device(("x_padded", x_padded), ("weight", weight), ("bias", bias), ("out", out))
+    Bsz, Lp, C = x_padded.shape
+    K = weight.shape[1]
+    if L is None:
+        L = Lp - K + 1
+    if L != Lp - K + 1:
+        x_padded = x_padded[:, :L + K - 1]
+    if out is None:
+        out = torch.empty((Bsz, L, C), dtype=x_padded.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call(entry, *(_lib.ref(_lib.desc(t, n)) for t, n in (
+            (x_padded, "x_padded"), (weight, "weight"), (bias, "bias"), (out, "out"))),
+            _lib.stream_handle(dev))
+    return out
+
+
+def conv1d_silu(x_padded, weight, bias=None, L=None, out=None):
+    """silu(causal depthwise conv) of a pre-padded input ``[B, L+K-1, C]``.
+
+    Mirrors ``fused_conv1d_silu(x_padded, weight, bias, L)``
+    (alloy/models/mamba_kernels.py:39-50).
+    """
+    return _conv("alloy_conv1d_silu", x_padded, weight, bias, L, out)
+
+
+def depthwise_conv1d(x_padded, weight, bias=None, L=None, out=None):
+    """Causal depthwise conv without activation, ``MambaBlock._depthwise_conv1d``
+    (alloy/models/mamba_block.py:144-158)."""
+    return _conv("alloy_depthwise_conv1d", x_padded, weight, bias, L, out)
+
+
+def ssd_combined(xBC, dt_raw, conv_weight, conv_bias, dt_bias, A_log, D, *, n_heads,
+                 head_dim, d_state, n_groups, d_conv=4, chunk_size=256, ssm_state=None,
+                 conv_state=None, out=None, ssm_state_out=None, conv_state_out=None,
+                 write_ssm_state=True, write_conv_state=True, head_begin=0, head_count=0):
+    """Fused conv + discretisation + chunked SSD scan + D skip (prefill).
+
+    The hot part of ``MambaBlock._forward_combined``
+    (alloy/models/mamba_block.py:446-493).  Returns
+    ``(y [B, L, H, P], ssm_state_out [B, H, N, P] fp32, conv_state_out
+    [B, K-1, conv_dim])``; the state outputs are new tensors unless given
+    (they may alias the inputs for an in-place cache update).  ``head_begin``
+    / ``head_count`` restrict the call to a head range (multi-GPU sharding):
+    only those heads of ``y`` and of the states are written.
+    """
+    dev = _same_device(("xBC", xBC), ("dt_raw", dt_raw), ("conv_weight", conv_weight),
+                       ("conv_bias", conv_bias), ("dt_bias", dt_bias), ("A_log", A_log),
+                       ("D", D), ("ssm_state", ssm_state), ("conv_state", conv_state),
+                       ("out", out), ("ssm_state_out", ssm_state_out),
+                       ("conv_state_out", conv_state_out))
+    Bsz, L, Cdim = xBC.shape
+    H, P, N = n_heads, head_dim, d_state
+    if out is None:
+        out = torch.empty((Bsz, L, H, P), dtype=xBC.dtype, device=dev)
+    if ssm_state_out is None and write_ssm_state:
+        ssm_state_out = torch.empty((Bsz, H, N, P), dtype=torch.float32, device=dev)
+    if conv_state_out is None and write_conv_state:
+        conv_state_out = torch.empty((Bsz, d_conv - 1, Cdim), dtype=xBC.dtype, device=dev)
+    if conv_state is not None and conv_state.dtype != xBC.dtype:
+        conv_state = conv_state.to(xBC.dtype)
+    dims = _dims(H, P, N, n_groups, d_conv, chunk_size, head_begin, head_count)
+    args = [(xBC, "xBC"), (dt_raw, "dt_raw"), (_f32(conv_weight), "conv_weight"),
+            (_f32(conv_bias), "conv_bias"), (_f32(dt_bias), "dt_bias"), (_f32(A_log), "A_log"),
+            (_f32(D), "D"), (ssm_state, "ssm_state"), (conv_state, "conv_state"), (out, "y"),
+            (ssm_state_out, "ssm_state_out"), (conv_state_out, "conv_state_out")]
+    descs = [_lib.desc(t, n) for t, n in args]
+    with torch.cuda.device(dev):
+        _lib.call("alloy_ssd_combined", *(_lib.ref(d) for d in descs), _lib.ref(dims),
+                  _lib.stream_handle(dev))
+    return out, ssm_state_out, conv_state_out
+
+
+def selective_scan(x, A_disc, B, C, ssm_state=None, log_a=None, out=None, out_dtype=None,
+                   ssm_state_out=None, write_ssm_state=True):
+    """Scan on pre-discretised inputs (``MambaBlock._selective_scan``,
+    alloy/models/mamba_block.py:287-366).
+
+    x [B, L, H, P] (dt-scaled), A_disc [B, L, H], B/C [B, L, G', N] with G'
+    dividing H (G' = H for the reference's per-head repeated B/C), ssm_state
+    [B, H, N, P] fp32 or None.  ``log_a`` (fp32), when given, is used in
+    place of log(A_disc).  Returns (y, ssm_state_out); y has ``out_dtype``
+    (default: x's dtype).
+    """
+    dev = _same_device(("x", x), ("A_disc", A_disc), ("B", B), ("C", C),
+                       ("ssm_state", ssm_state), ("log_a", log_a), ("out", out),
+                       ("ssm_state_out", ssm_state_out))
+    Bsz, L, H, P = x.shape
+    N = B.shape[-1]
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if out is None:
+        out = torch.empty((Bsz, L, H, P), dtype=out_dtype or x.dtype, device=dev)
+    if ssm_state_out is None and write_ssm_state:
+        ssm_state_out = torch.empty((Bsz, H, N, P), dtype=torch.float32, device=dev)
+    if ssm_state is not None and ssm_state.dtype != torch.float32:
+        ssm_state = ssm_state.float()
+    args = [(x, "x"), (A_disc, "A_disc"), (_f32(log_a), "log_a"), (B, "B"), (C, "C"),
+            (ssm_state, "ssm_state"), (out, "y"), (ssm_state_out, "ssm_state_out")]
+    descs = [_lib.desc(t, n) for t, n in args]
+    with torch.cuda.device(dev):
+        _lib.call("alloy_selective_scan", *(_lib.ref(d) for d in descs), _lib.stream_handle(dev))
+    return out, ssm_state_out
+
+
+def ssd_decode_step(xBC_tok, dt_tok, conv_weight, conv_bias, dt_bias, A_log, D, conv_state,
+                    ssm_state, *, n_heads, head_dim, d_state, n_groups, out=None, head_begin=0,
+                    head_count=0):
+    """One decode token, updating ``conv_state`` and ``ssm_state`` in place.
+
+    The L = 1 path of ``MambaBlock._forward_combined`` (conv-cache roll,
+    alloy/models/mamba_block.py:446-448; ``_selective_scan_sequential``
+    :160-204; D residual :492-493).  xBC_tok [B, conv_dim], dt_tok [B, H],
+    conv_state [B, K-1, conv_dim] (or its [B, conv_dim, K-1] transpose via
+    strides), ssm_state [B, H, N, P] (or [B, H, P, N] via strides), fp32.
+    Returns y [B, H, P].
+    """
+    dev = _same_device(("xBC_tok", xBC_tok), ("dt_tok", dt_tok), ("conv_weight", conv_weight),
+                       ("conv_bias", conv_bias), ("dt_bias", dt_bias), ("A_log", A_log),
+                       ("D", D), ("conv_state", conv_state), ("ssm_state", ssm_state),
+                       ("out", out))
+    Bsz = xBC_tok.shape[0]
+    if out is None:
+        out = torch.empty((Bsz, n_heads, head_dim), dtype=xBC_tok.dtype, device=dev)
+    d_conv = conv_state.shape[1] + 1
+    dims = _dims(n_heads, head_dim, d_state, n_groups, d_conv, 1, head_begin, head_count)
+    args = [(xBC_tok, "xBC_tok"), (dt_tok, "dt_tok"), (_f32(conv_weight), "conv_weight"),
+            (_f32(conv_bias), "conv_bias"), (_f32(dt_bias), "dt_bias"), (_f32(A_log), "A_log"),
+            (_f32(D), "D"), (conv_state, "conv_state"), (ssm_state, "ssm_state"), (out, "y")]
+    descs = [_lib.desc(t, n) for t, n in args]
+    with torch.cuda.device(dev):
+        _lib.call("alloy_ssd_decode_step", *(_lib.ref(d) for d in descs), _lib.ref(dims),
+                  _lib.stream_handle(dev))
+    return out

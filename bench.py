@@ -1,0 +1,514 @@
+#!/usr/bin/env python
+"""Mamba-2 SSD prefill benchmark on B200 (tokens/s, fraction of roofline).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
+                    [--workload nemotron|zamba2|long|decode]
+
+One step is one fused mixer-core prefill (conv1d+SiLU -> discretise ->
+chunked SSD scan -> D skip, plus the conv-cache roll) over one batch of
+synthetic inputs of the Nemotron-H-8B layer shape (B=4, L=8192, 128 heads x
+64, d_state 128, 8 groups), already resident in HBM.  With N GPUs (torchrun,
+one process per GPU) the 8 head-groups are split across ranks (8/N groups per
+GPU, no collective in the path): total work is fixed ("strong" scaling) and
+``value`` = B*L tokens / max-over-ranks step time.
+
+Rank 0 prints one JSON line.  ``e2e`` is the same metric through the public
+API (``alloy_b200.mixer.ssd_combined``) with host->device copies of the step's
+inputs from pinned memory and a device->host read of its outputs inside the
+timed region.  ``--impl reference`` times the reference algorithm on the host
+CPU (the numpy restatement in ``oracle/``; alloy's own MLX path cannot run on
+this machine) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "Mamba-2 SSD prefill tokens/s (Nemotron-H shape) at 1/2/4/8 B200; % roofline"
+
+WORKLOADS = {
+    "nemotron": dict(name="nemotron_h_8b_mamba2_layer_prefill", B=4, L=8192, H=128, P=64, N=128,
+                     G=8, K=4, Q=256),
+    "zamba2": dict(name="zamba2_1.2b_mamba2_layer_prefill", B=8, L=4096, H=64, P=64, N=64, G=1,
+                   K=4, Q=256),
+    "long": dict(name="zamba2_1.2b_mamba2_layer_prefill_131k", B=1, L=131072, H=64, P=64, N=64,
+                 G=1, K=4, Q=512),
+    "decode": dict(name="nemotron_h_8b_mamba2_decode_step", B=256, L=1, H=128, P=64, N=128, G=8,
+                   K=4, Q=256),
+}
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+# DRAM bytes per launch of the dominant kernel measured with ncu (read + write),
+# keyed by (workload, n_gpus); see profiles/ for the captures.  None = not yet
+# captured for that configuration.
+NCU_TRAFFIC_BYTES = {}
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x2: "applications_clocks_setting", 0x1: "gpu_idle", 0x10: "sync_boost"}
+
+    def __init__(self, torch_device):
+        self.samples = []
+        self.ok = False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            handle = None
+            try:
+                import torch
+                bus = torch.cuda.get_device_properties(torch_device).pci_bus_id
+                handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                handle = pynvml.nvmlDeviceGetHandleByIndex(torch_device)
+            self.h = handle
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # pragma: no cover - no NVML
+            self.err = str(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                try:
+                    rs = self.nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                except Exception:
+                    rs = 0
+            self.samples.append((time.perf_counter(), mhz, rs))
+            time.sleep(0.005)
+
+    def start(self):
+        if self.ok:
+            self.th = threading.Thread(target=self._run, daemon=True)
+            self.th.start()
+
+    def stop(self):
+        if self.ok:
+            self._stop.set()
+            self.th.join()
+
+    def summary(self, t0, t1):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "nvml unavailable"}
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not inside and self.samples:
+            mid = 0.5 * (t0 + t1)
+            inside = [min(self.samples, key=lambda s: abs(s[0] - mid))]
+        mhz = sorted(s[1] for s in inside)
+        bits = 0
+        for s in inside:
+            bits |= s[2]
+        reasons = sorted({name for b, name in self.REASONS.items() if bits & b} - {"gpu_idle"})
+        return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(inside)}
+
+
+# ------------------------------------------------------------------------ distributed
+def dist_setup(gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != gpus:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def dist_max(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def local_problem(w, world, rank):
+    """The shard of the layer this rank computes: (H_l, G_l) with heads split
+    by head-group (or by heads inside the single group when G < world)."""
+    H, G = w["H"], w["G"]
+    if H % world:
+        raise SystemExit(f"{H} heads do not split over {world} GPUs")
+    if G % world == 0:
+        return H // world, G // world
+    if G == 1:
+        return H // world, 1
+    raise SystemExit(f"{G} groups do not split over {world} GPUs")
+
+
+# ------------------------------------------------------------------------ our arm
+def make_prefill_inputs(B, L, H, P, N, G, K, seed, device):
+    """Synthetic inputs with the workload's distributions, generated on the GPU."""
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    conv_dim = H * P + 2 * G * N
+    xBC = torch.randn((B, L, conv_dim), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+    dt_raw = torch.randn((B, L, H), generator=gen, device=device).to(torch.bfloat16)
+    conv_w = torch.randn((conv_dim, K), generator=gen, device=device) * 0.5
+    conv_b = torch.zeros(conv_dim, device=device)
+    u = torch.exp(torch.empty(H, device=device).uniform_(math.log(1e-3), math.log(0.1), generator=gen))
+    dt_bias = torch.log(torch.expm1(u))
+    A_log = torch.empty(H, device=device).uniform_(0.0, math.log(16.0), generator=gen)
+    D = torch.randn(H, generator=gen, device=device)
+    return dict(xBC=xBC, dt_raw=dt_raw, conv_w=conv_w, conv_b=conv_b, dt_bias=dt_bias,
+                A_log=A_log, D=D)
+
+
+def run_ours(args, w):
+    import torch
+    from alloy_b200 import mixer
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    H_l, G_l = local_problem(w, world, rank)
+    B, L, P, N, K, Q = w["B"], w["L"], w["P"], w["N"], w["K"], w["Q"]
+    conv_dim = H_l * P + 2 * G_l * N
+    kw = dict(n_heads=H_l, head_dim=P, d_state=N, n_groups=G_l, d_conv=K, chunk_size=Q)
+
+    # one input/output set per rotation slot, so that every step reads and
+    # writes memory not touched in the previous steps (> 3x L2 in between)
+    step_bytes = B * L * (conv_dim + H_l) * 2 + B * L * H_l * P * 2
+    rot = max(1, math.ceil(3 * L2_BYTES / step_bytes))
+    sets = []
+    for r in range(rot):
+        inp = make_prefill_inputs(B, L, H_l, P, N, G_l, K, seed=1000 * rank + r, device=dev)
+        out = dict(y=torch.empty((B, L, H_l, P), dtype=torch.bfloat16, device=dev),
+                   h=torch.empty((B, H_l, N, P), dtype=torch.float32, device=dev),
+                   cs=torch.empty((B, K - 1, conv_dim), dtype=torch.bfloat16, device=dev))
+        sets.append((inp, out))
+
+    def step(i):
+        inp, out = sets[i % rot]
+        mixer.ssd_combined(inp["xBC"], inp["dt_raw"], inp["conv_w"], inp["conv_b"],
+                           inp["dt_bias"], inp["A_log"], inp["D"], out=out["y"],
+                           ssm_state_out=out["h"], conv_state_out=out["cs"], **kw)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream(dev)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ke = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    h0 = time.perf_counter()
+    ev0.record(stream)
+    for i in range(args.steps):
+        ks[i].record(stream)
+        step(i)
+        ke[i].record(stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    h1 = time.perf_counter()
+    barrier(world)
+    clocks.stop()
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    kernel_ms_local = sum(a.elapsed_time(b) for a, b in zip(ks, ke)) / args.steps
+    ms = dist_max(ms_local, world)
+    kernel_ms = dist_max(kernel_ms_local, world)
+    tokens = B * L
+    value = tokens / (ms * 1e-3)
+
+    # algorithmic bytes of one step of this rank (one pass over the data)
+    alg = (B * L * conv_dim * 2 + B * L * H_l * 2 + B * L * H_l * P * 2 + B * H_l * N * P * 4
+           + B * (K - 1) * conv_dim * 2)
+    peak, peak_kind = measured_peaks()
+    achieved = alg / (kernel_ms_local * 1e-3) / 1e9
+    achieved = dist_max(-achieved, world) * -1 if world > 1 else achieved  # slowest rank
+    traffic = NCU_TRAFFIC_BYTES.get((args.workload, world))
+
+    # ---- end to end through the public API, host buffers ----
+    inp, out = sets[0]
+    host_in = {k: torch.empty(inp[k].shape, dtype=inp[k].dtype, pin_memory=True)
+               for k in ("xBC", "dt_raw")}
+    for k in host_in:
+        host_in[k].copy_(inp[k])
+    host_y = torch.empty(out["y"].shape, dtype=out["y"].dtype, pin_memory=True)
+    host_h = torch.empty(out["h"].shape, dtype=out["h"].dtype, pin_memory=True)
+    dev_in = {k: torch.empty_like(inp[k]) for k in host_in}
+    e2e_steps = max(3, min(args.steps, 10))
+
+    def e2e_step():
+        for k in host_in:
+            dev_in[k].copy_(host_in[k], non_blocking=True)
+        y, h, _ = mixer.ssd_combined(dev_in["xBC"], dev_in["dt_raw"], inp["conv_w"],
+                                     inp["conv_b"], inp["dt_bias"], inp["A_log"], inp["D"],
+                                     out=out["y"], ssm_state_out=out["h"],
+                                     conv_state_out=out["cs"], **kw)
+        host_y.copy_(y, non_blocking=True)
+        host_h.copy_(h, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = dist_max(e0.elapsed_time(e1) / e2e_steps, world)
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = host_y.numel() * host_y.element_size() + host_h.numel() * host_h.element_size()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_sample(w, budget_s=20.0)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": w["name"], "batch": B, "seq_len": L, "n_heads": w["H"],
+                       "head_dim": P, "d_state": N, "n_groups": w["G"], "d_conv": K,
+                       "chunk_size": Q, "state_dtype": "f32",
+                       "shard": f"{H_l} heads / {G_l} groups per GPU",
+                       "l2": f"inputs larger than L2: {rot} rotating input/output sets, "
+                             f"{step_bytes * rot / 2**20:.0f} MiB touched per rotation"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{peak_kind} hbm_gbs",
+                         "kernel_ms": kernel_ms, "algorithmic_bytes_per_gpu": alg},
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                    "ms_per_step": e2e_ms, "steps": e2e_steps},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks.summary(h0, h1),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_decode(args, w):
+    """Decode-step workload: B sequences advance one token per step through
+    the conv cache and the fp32 SSM cache ([B, H, P, N] storage), 64
+    sequential tokens cycled; reported as achieved HBM GB/s (the state is
+    read and written once per token)."""
+    import torch
+    from alloy_b200 import mixer
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    H, P, N, G, K = w["H"], w["P"], w["N"], w["G"], w["K"]
+    if w["B"] % world:
+        raise SystemExit("batch does not split over the GPUs")
+    B = w["B"] // world
+    C = H * P + 2 * G * N
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7 + rank)
+    state_pn = torch.randn((B, H, P, N), generator=gen, device=dev) * math.sqrt(0.1)
+    conv_ck = torch.randn((B, C, K - 1), generator=gen, device=dev).to(torch.bfloat16)
+    T = 64
+    xtok = torch.randn((T, B, C), generator=gen, device=dev).to(torch.bfloat16)
+    dtok = torch.randn((T, B, H), generator=gen, device=dev).to(torch.bfloat16)
+    p = make_prefill_inputs(1, 1, H, P, N, G, K, seed=3, device=dev)
+    y = torch.empty((B, H, P), dtype=torch.bfloat16, device=dev)
+    ssm, conv = state_pn.transpose(2, 3), conv_ck.transpose(1, 2)
+    kw = dict(n_heads=H, head_dim=P, d_state=N, n_groups=G, out=y)
+
+    def step(i):
+        mixer.ssd_decode_step(xtok[i % T], dtok[i % T], p["conv_w"], p["conv_b"], p["dt_bias"],
+                              p["A_log"], p["D"], conv, ssm, **kw)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    h0 = time.perf_counter()
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    h1 = time.perf_counter()
+    barrier(world)
+    clocks.stop()
+    ms = dist_max(ev0.elapsed_time(ev1) / args.steps, world)
+    alg = (2 * B * H * P * N * 4 + 2 * B * C * (K - 1) * 2 + B * C * 2 + B * H * 2
+           + B * H * P * 2)
+    peak, peak_kind = measured_peaks()
+    gbs = alg * world / (ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Mamba-2 decode step (state update + conv-cache roll) HBM GB/s",
+            "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": w["name"], "batch": w["B"], "n_heads": H, "head_dim": P,
+                       "d_state": N, "n_groups": G, "state_layout": "[B,H,P,N] f32",
+                       "conv_state_layout": "[B,C,K-1] bf16", "tokens_cycled": T,
+                       "l2": "state of %.0f MiB per GPU > L2" % (B * H * P * N * 4 / 2**20)},
+            "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / world / peak, "traffic": None,
+                         "peak_source": f"{peak_kind} hbm_gbs"},
+            "gpu_launches": args.steps, "clocks": clocks.summary(h0, h1)}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ CPU reference
+def _blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def _cpu_sample(w, heads, tokens, seed=0):
+    """Time the reference algorithm (oracle.mixer_core: conv -> discretise ->
+    chunked state-space scan -> D) on one batch row, ``heads`` heads of one
+    group, ``tokens`` tokens.  Returns seconds."""
+    import oracle
+    inp = oracle.make_inputs(B=1, L=tokens, H=heads, P=w["P"], N=w["N"], G=1, dtype="bf16",
+                             seed=seed)
+    t0 = time.perf_counter()
+    oracle.mixer_core(inp["xBC"], inp["dt_raw"], inp["conv_weight"], inp["conv_bias"],
+                      inp["dt_bias"], inp["A_log"], inp["D"], n_heads=heads, headdim=w["P"],
+                      d_state=w["N"], n_groups=1, chunk_size=w["Q"])
+    return time.perf_counter() - t0
+
+
+def cpu_baseline_sample(w, budget_s=20.0):
+    heads = w["H"] // w["G"]           # one head-group
+    tokens = min(w["L"], 2 * w["Q"])   # the first chunks of one batch row
+    secs = _cpu_sample(w, heads, tokens)
+    reps = 1
+    while secs * (reps + 1) < budget_s and reps < 4:
+        secs = min(secs, _cpu_sample(w, heads, tokens, seed=reps))
+        reps += 1
+    per_layer_tokens_s = tokens / (secs * w["H"] / heads)
+    return {"value": per_layer_tokens_s, "unit": "tokens/s", "cores": _blas_threads(),
+            "kind": "port",
+            "sample": f"oracle.mixer_core (the reference's chunked state-space scan, numpy fp32) "
+                      f"on 1 batch row x {heads} heads (one group) x {tokens} tokens, "
+                      f"best of {reps}; extrapolated linearly to all {w['H']} heads"}
+
+
+def run_reference(args, w):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    heads = w["H"] // w["G"]
+    tokens = min(w["L"], w["Q"])
+    # size each step so that warmup + steps stay within about two minutes
+    probe = _cpu_sample(w, 1, tokens)
+    per_head = max(probe, 1e-3)
+    budget_per_step = 120.0 / max(1, args.steps + args.warmup)
+    heads = max(1, min(heads, int(budget_per_step / per_head)))
+    for i in range(args.warmup):
+        _cpu_sample(w, heads, tokens, seed=i)
+    total = 0.0
+    for i in range(args.steps):
+        total += _cpu_sample(w, heads, tokens, seed=100 + i)
+    secs = total / args.steps
+    value = tokens / (secs * w["H"] / heads)
+    cores = _blas_threads()
+    sample = (f"oracle.mixer_core (numpy restatement of alloy's mamba_block.py conv + "
+              f"discretise + chunked state-space scan + D; MLX is not installable here) on "
+              f"1 batch row x {heads} heads x {tokens} tokens per step, extrapolated "
+              f"linearly to {w['H']} heads")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": secs * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": w["name"], "batch": w["B"], "seq_len": w["L"],
+                       "n_heads": w["H"], "head_dim": w["P"], "d_state": w["N"],
+                       "n_groups": w["G"], "chunk_size": w["Q"]},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "gpu_launches": 0}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="nemotron")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, w)
+    elif args.workload == "decode":
+        run_decode(args, w)
+    else:
+        run_ours(args, w)
+
+
+if __name__ == "__main__":
+    main()

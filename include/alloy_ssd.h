@@ -1,0 +1,190 @@
+/*
+ * alloy_ssd.h -- C ABI of liballoy_ssd.so, the B200 (sm_100a) kernels of the
+ * Mamba-2 mixer hot path of gxcsoccer/alloy.
+ *
+ * The reference (alloy, Python + MLX) has no native library; its hot path is
+ * the set of Python functions cited beside each entry point below.  Each entry
+ * point is what a ctypes binding in the reference's kernel package
+ * (alloy/kernels/__init__.py, currently an empty placeholder) would call in
+ * place of those functions.
+ *
+ * Conventions
+ *   - Every tensor is passed as an alloy_tensor_t: a device pointer, a dtype,
+ *     a shape and element strides (like DLPack's DLTensor, without the device
+ *     field).  The caller owns every buffer; the library allocates nothing.
+ *   - Every call is asynchronous on the given cudaStream_t (passed as void*,
+ *     NULL = legacy default stream) and returns ALLOY_OK or a negative
+ *     status.  Argument errors are detected on the host before any launch.
+ *     alloy_get_last_error() returns the calling thread's last message.
+ *   - State tensors may be updated in place (state_in == state_out).
+ *   - No call traps, asserts or spins without bound on the device.
+ */
+#ifndef ALLOY_SSD_H
+#define ALLOY_SSD_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ALLOY_API __attribute__((visibility("default")))
+#else
+#define ALLOY_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ALLOY_SSD_ABI_VERSION 1
+
+/* status codes */
+#define ALLOY_OK                0
+#define ALLOY_ERR_INVALID_ARG  -1  /* null pointer, bad shape/stride/dtype      */
+#define ALLOY_ERR_UNSUPPORTED  -2  /* valid but not implemented for these sizes */
+#define ALLOY_ERR_ALIGNMENT    -3  /* pointer/stride alignment not met          */
+#define ALLOY_ERR_CUDA         -4  /* a CUDA runtime call failed                */
+#define ALLOY_ERR_DEVICE       -5  /* no usable sm_100 device                   */
+
+/* element types */
+#define ALLOY_F32   0
+#define ALLOY_BF16  1
+
+#define ALLOY_MAX_DIMS 5
+
+typedef struct alloy_tensor {
+    void*   data;                     /* device pointer (NULL = absent)  */
+    int32_t dtype;                    /* ALLOY_F32 / ALLOY_BF16          */
+    int32_t ndim;
+    int64_t shape[ALLOY_MAX_DIMS];
+    int64_t stride[ALLOY_MAX_DIMS];   /* in elements                     */
+} alloy_tensor_t;
+
+/* Sizes of one Mamba-2 mixer (MambaBlock constructor arguments,
+ * alloy/models/mamba_block.py:76-102), plus the head range this call
+ * computes (head_begin, head_count; head_count 0 = all heads).  The head
+ * range lets a multi-GPU caller shard a layer by (batch, head-group) without
+ * copying: tensors stay full-width and only the selected heads are read and
+ * written. */
+typedef struct alloy_ssd_dims {
+    int64_t n_heads;      /* H */
+    int64_t head_dim;     /* P */
+    int64_t d_state;      /* N */
+    int64_t n_groups;     /* G, H % G == 0; head h uses group h / (H/G) */
+    int64_t d_conv;       /* K (4) */
+    int64_t chunk_size;   /* the reference's scan chunk; results do not depend on it */
+    int64_t head_begin;
+    int64_t head_count;
+} alloy_ssd_dims_t;
+
+/* ABI version (ALLOY_SSD_ABI_VERSION) and a human-readable build string. */
+ALLOY_API int         alloy_abi_version(void);
+ALLOY_API const char* alloy_build_info(void);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len); returns its full length. */
+ALLOY_API size_t alloy_get_last_error(char* buf, size_t len);
+
+/*
+ * Causal depthwise conv1d + SiLU on a pre-padded input.
+ * Replaces fused_conv1d_silu (alloy/models/mamba_kernels.py:39-50, Metal
+ * kernel :17-36) and MambaBlock._depthwise_conv1d + nn.silu
+ * (alloy/models/mamba_block.py:144-158, :454-455).
+ *
+ *   x_padded [B, L+K-1, C]  F32|BF16, channel stride 1
+ *   weight   [C, K]         F32|BF16 (any strides)
+ *   bias     [C]            F32|BF16 (data NULL = zero bias)
+ *   out      [B, L, C]      dtype of x_padded, channel stride 1
+ *   out[b,t,c] = silu(bias[c] + sum_k x_padded[b,t+k,c] * weight[c,k]),
+ *   accumulated in fp32.
+ */
+ALLOY_API int alloy_conv1d_silu(const alloy_tensor_t* x_padded, const alloy_tensor_t* weight,
+                      const alloy_tensor_t* bias, alloy_tensor_t* out, void* stream);
+
+/*
+ * The same causal depthwise conv without the SiLU.
+ * Replaces MambaBlock._depthwise_conv1d (alloy/models/mamba_block.py:144-158).
+ * Arguments as for alloy_conv1d_silu; out[b,t,c] = bias[c] + sum_k x_padded[b,t+k,c] * weight[c,k].
+ */
+ALLOY_API int alloy_depthwise_conv1d(const alloy_tensor_t* x_padded, const alloy_tensor_t* weight,
+                                     const alloy_tensor_t* bias, alloy_tensor_t* out, void* stream);
+
+/*
+ * Fused Mamba-2 mixer core in combined (Zamba2 / Nemotron-H) mode, prefill of
+ * L >= 1 tokens: conv1d+SiLU with the conv-cache prefix, split into x|B|C,
+ * discretisation, chunked SSD scan with state carry, D skip.
+ * Replaces the hot part of MambaBlock._forward_combined
+ * (alloy/models/mamba_block.py:446-493): the conv-cache update (:446-452),
+ * _depthwise_conv1d + silu (:454-455), the group split/repeat (:458-468),
+ * discretisation (:471-486), _selective_scan (:287-366, with _scan_chunk
+ * :206-285) and the D residual (:481-482, :492-493).
+ *
+ *   xBC        [B, L, conv_dim]  F32|BF16, conv_dim = H*P + 2*G*N, channel stride 1
+ *   dt_raw     [B, L, H]         F32|BF16 (the in_proj dt slice, before softplus)
+ *   conv_w     [conv_dim, K]     F32;  conv_b [conv_dim] F32 (data NULL = 0)
+ *   dt_bias, A_log [H]           F32;  D [H] F32 (data NULL = no D skip)
+ *   ssm_in     [B, H, N, P] or any permutation via strides, F32 (data NULL = zeros)
+ *   conv_in    [B, K-1, conv_dim] (any strides), dtype of xBC (data NULL = zeros)
+ *   y          [B, L, H, P]      dtype of xBC (head/P strides free, P stride 1 for BF16)
+ *   ssm_out    like ssm_in, F32 (data NULL = not written); may alias ssm_in
+ *   conv_out   like conv_in (data NULL = not written); may alias conv_in
+ * y = scan(dt*x) + D*x, where x is the UNSCALED conv output.
+ */
+ALLOY_API int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t* dt_raw,
+                       const alloy_tensor_t* conv_w, const alloy_tensor_t* conv_b,
+                       const alloy_tensor_t* dt_bias, const alloy_tensor_t* A_log,
+                       const alloy_tensor_t* D,
+                       const alloy_tensor_t* ssm_in, const alloy_tensor_t* conv_in,
+                       alloy_tensor_t* y, alloy_tensor_t* ssm_out,
+                       alloy_tensor_t* conv_out,
+                       const alloy_ssd_dims_t* dims, void* stream);
+
+/*
+ * Selective scan on pre-discretised inputs.
+ * Replaces MambaBlock._selective_scan (alloy/models/mamba_block.py:287-366)
+ * -- and, through it, _scan_chunk (:206-285), _selective_scan_sequential
+ * (:160-204) and scan_chunk_metal / fused_parallel_scan_chunk
+ * (alloy/models/mamba_kernels.py:193-224, :333-396), which compute the same
+ * recurrence over one chunk.
+ *
+ *   x       [B, L, H, P]   F32|BF16 (already dt-scaled), P stride 1
+ *   A_disc  [B, L, H]      F32|BF16, used as log(max(A_disc, 1e-10)) when log_a is absent
+ *   log_a   [B, L, H]      F32 (data NULL = absent), mamba_block.py:246-249
+ *   Bm, Cm  [B, L, G', N]  F32|BF16, G' divides H (G' = H for per-head B/C)
+ *   ssm_in  [B, H, N, P]   F32 via strides (data NULL = zeros)
+ *   y       [B, L, H, P]   F32|BF16
+ *   ssm_out [B, H, N, P]   F32 via strides (data NULL = not written), may alias ssm_in
+ * h_t = a_t h_{t-1} + B_t x_t^T;  y_t = C_t h_t  (fp32 state and accumulation).
+ */
+ALLOY_API int alloy_selective_scan(const alloy_tensor_t* x, const alloy_tensor_t* A_disc,
+                         const alloy_tensor_t* log_a, const alloy_tensor_t* Bm,
+                         const alloy_tensor_t* Cm, const alloy_tensor_t* ssm_in,
+                         alloy_tensor_t* y, alloy_tensor_t* ssm_out, void* stream);
+
+/*
+ * One decode token through the conv cache and the SSM cache, in place.
+ * Replaces the L = 1 path of MambaBlock._forward_combined: the conv-cache roll
+ * (alloy/models/mamba_block.py:446-448), conv + silu (:454-455), split
+ * (:458-468), discretisation (:471-486), _selective_scan_sequential
+ * (:160-204) and the D residual (:492-493).
+ *
+ *   xBC_tok    [B, conv_dim]  F32|BF16, channel stride 1
+ *   dt_tok     [B, H]         F32|BF16
+ *   conv_w, conv_b, dt_bias, A_log, D   as in alloy_ssd_combined
+ *   conv_state [B, K-1, conv_dim] or [B, conv_dim, K-1] via strides, dtype of
+ *              xBC_tok; read and rolled in place
+ *   ssm_state  [B, H, N, P] or [B, H, P, N] (one of N, P with stride 1), F32,
+ *              updated in place
+ *   y          [B, H, P]      dtype of xBC_tok, P stride 1
+ */
+ALLOY_API int alloy_ssd_decode_step(const alloy_tensor_t* xBC_tok, const alloy_tensor_t* dt_tok,
+                          const alloy_tensor_t* conv_w, const alloy_tensor_t* conv_b,
+                          const alloy_tensor_t* dt_bias, const alloy_tensor_t* A_log,
+                          const alloy_tensor_t* D,
+                          alloy_tensor_t* conv_state, alloy_tensor_t* ssm_state,
+                          alloy_tensor_t* y, const alloy_ssd_dims_t* dims, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ALLOY_SSD_H */

@@ -1,0 +1,132 @@
+"""The C ABI without a GPU: the library loads, exports every entry point the
+header declares, and rejects bad arguments on the host before touching a
+device."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from alloy_b200 import _lib
+from conftest import REPO
+
+HEADER = os.path.join(REPO, "include", "alloy_ssd.h")
+
+
+def header_entry_points():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"ALLOY_API\s+[\w\s\*]+?\b(alloy_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_python_export_list():
+    assert header_entry_points() == sorted(_lib.EXPORTS)
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in header_entry_points():
+        assert hasattr(lib, name), name
+    assert lib.alloy_abi_version() == _lib.ABI_VERSION
+    assert b"sm_100a" in lib.alloy_build_info()
+
+
+def _t(shape, dtype=_lib.F32, ptr=0x1000, strides=None):
+    d = _lib.Tensor()
+    d.data = ptr
+    d.dtype = dtype
+    d.ndim = len(shape)
+    if strides is None:
+        strides, acc = [], 1
+        for s in reversed(shape):
+            strides.insert(0, acc)
+            acc *= s
+    for i, (s, st) in enumerate(zip(shape, strides)):
+        d.shape[i] = s
+        d.stride[i] = st
+    return d
+
+
+def _dims(H=8, P=32, N=16, G=1, K=4, Q=64, h0=0, hc=0):
+    d = _lib.Dims()
+    d.n_heads, d.head_dim, d.d_state, d.n_groups, d.d_conv, d.chunk_size = H, P, N, G, K, Q
+    d.head_begin, d.head_count = h0, hc
+    return d
+
+
+def _combined(**over):
+    B, L, H, P, N, G, K = 2, 16, 8, 32, 16, 1, 4
+    C = H * P + 2 * G * N
+    t = dict(xBC=_t([B, L, C]), dt=_t([B, L, H]), w=_t([C, K]), b=_t([C]), dtb=_t([H]),
+             alog=_t([H]), D=_t([H]), si=_lib.Tensor(), ci=_lib.Tensor(),
+             y=_t([B, L, H, P]), so=_lib.Tensor(), co=_lib.Tensor())
+    dims = over.pop("dims", _dims(H, P, N, G, K))
+    t.update(over)
+    lib = _lib.load()
+    order = ["xBC", "dt", "w", "b", "dtb", "alog", "D", "si", "ci", "y", "so", "co"]
+    st = lib.alloy_ssd_combined(*(ctypes.byref(t[k]) for k in order), ctypes.byref(dims), None)
+    return st, _lib.last_error()
+
+
+@pytest.mark.parametrize("over,needle", [
+    (dict(xBC=_lib.Tensor()), "xBC: null"),
+    (dict(xBC=_t([2, 16, 300])), "expected H*P + 2*G*N"),
+    (dict(dt=_t([2, 15, 8])), "dt_raw: dim 1"),
+    (dict(w=_t([288, 4], dtype=_lib.BF16)), "conv_w: unsupported dtype"),
+    (dict(y=_t([2, 16, 8, 32], dtype=_lib.BF16)), "y: unsupported dtype"),
+    (dict(dims=_dims(H=8, G=3)), "not divisible"),
+    (dict(dims=_dims(h0=6, hc=4)), "head range"),
+    (dict(dims=_dims(K=9)), "d_conv"),
+    (dict(so=_t([2, 8, 16, 31])), "ssm_out: dim 3"),
+    (dict(xBC=_t([2, 16, 288], strides=[16 * 288 * 2, 288 * 2, 2])), "channel stride"),
+])
+def test_combined_rejects_bad_arguments(over, needle):
+    st, msg = _combined(**over)
+    assert st in (-1, -2), (st, msg)
+    assert needle in msg, msg
+
+
+def test_conv_rejects_bad_arguments():
+    lib = _lib.load()
+    x, w, out = _t([2, 19, 64]), _t([64, 4]), _t([2, 15, 64])
+    st = lib.alloy_conv1d_silu(ctypes.byref(x), ctypes.byref(w), None, ctypes.byref(out), None)
+    assert st == -1 and "out: dim 1" in _lib.last_error()
+    w9 = _t([64, 9])
+    st = lib.alloy_depthwise_conv1d(ctypes.byref(x), ctypes.byref(w9), None, ctypes.byref(out), None)
+    assert st == -2 and "K must be" in _lib.last_error()
+
+
+def test_decode_rejects_bad_state_layout():
+    lib = _lib.load()
+    B, H, P, N, G, K = 2, 8, 32, 16, 1, 4
+    C = H * P + 2 * G * N
+    st_bad = _t([B, H, N, P], strides=[H * N * P * 2, N * P * 2, 2 * P, 2])
+    args = [_t([B, C]), _t([B, H]), _t([C, K]), _lib.Tensor(), _t([H]), _t([H]),
+            _lib.Tensor(), _t([B, K - 1, C]), st_bad, _t([B, H, P])]
+    st = lib.alloy_ssd_decode_step(*(ctypes.byref(a) for a in args),
+                                   ctypes.byref(_dims(H, P, N, G, K)), None)
+    assert st == -1 and "ssm_state" in _lib.last_error()
+
+
+def test_selective_scan_rejects_group_mismatch():
+    lib = _lib.load()
+    B, L, H, P, N = 1, 8, 6, 16, 8
+    args = [_t([B, L, H, P]), _t([B, L, H]), _lib.Tensor(), _t([B, L, 4, N]),
+            _t([B, L, 4, N]), _lib.Tensor(), _t([B, L, H, P]), _lib.Tensor()]
+    st = lib.alloy_selective_scan(*(ctypes.byref(a) for a in args), None)
+    assert st == -1 and "does not divide" in _lib.last_error()
+
+
+def test_error_message_is_per_thread():
+    import threading
+    _combined(xBC=_lib.Tensor())
+    seen = {}
+
+    def other():
+        seen["msg"] = _lib.last_error()
+
+    th = threading.Thread(target=other)
+    th.start()
+    th.join()
+    assert seen["msg"] == ""
+    assert "xBC" in _lib.last_error()

@@ -1,0 +1,273 @@
+"""CUDA kernels (through the C ABI) against the oracle and the reference's
+golden vectors.  Needs a B200."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from alloy_b200 import kernels, mixer
+from alloy_b200.mamba_block import MambaBlock, MambaCache
+from conftest import (TOL_BF16_MAX_REL, TOL_BF16_REL_L2, TOL_F32_REL_L2, load_golden)
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def cu(a, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV, dtype)
+
+
+def np_(t):
+    return t.detach().float().cpu().numpy()
+
+
+def assert_close(got, ref, bf16):
+    r = oracle.rel_l2(got, ref)
+    if bf16:
+        m = oracle.max_rel(got, ref)
+        assert r <= TOL_BF16_REL_L2 and m <= TOL_BF16_MAX_REL, (r, m)
+    else:
+        assert r <= TOL_F32_REL_L2, r
+
+
+def run_combined(g, dtype, *, with_state=True, state_layout="nP", conv_layout="kC", **kw):
+    B, L, H, P, N, G, Q = (int(v) for v in g["dims"])
+    ssm_in = conv_in = None
+    if with_state and "ssm_state" in g:
+        ssm_in = cu(g["ssm_state"])
+        if state_layout == "pN":   # [B, H, P, N] storage passed as a strided view
+            ssm_in = ssm_in.transpose(2, 3).contiguous().transpose(2, 3)
+        conv_in = cu(g["conv_state"], dtype)
+        if conv_layout == "Ck":    # [B, C, K-1] storage
+            conv_in = conv_in.transpose(1, 2).contiguous().transpose(1, 2)
+    y, h, cs = mixer.ssd_combined(
+        cu(g["xBC"], dtype), cu(g["dt_raw"], dtype), cu(g["conv_weight"]), cu(g["conv_bias"]),
+        cu(g["dt_bias"]), cu(g["A_log"]), cu(g["D"]), n_heads=H, head_dim=P, d_state=N,
+        n_groups=G, chunk_size=Q, ssm_state=ssm_in, conv_state=conv_in, **kw)
+    torch.cuda.synchronize()
+    return y, h, cs
+
+
+# --------------------------------------------------------------------------- conv
+def test_conv1d_silu_golden():
+    g = load_golden("conv1d_silu")
+    out = kernels.fused_conv1d_silu(cu(g["x_padded"]), cu(g["weight"]), cu(g["bias"]),
+                                    g["x_padded"].shape[1] - 3)
+    np.testing.assert_allclose(np_(out), g["out"], rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize("B,L,C,dtype", [(1, 64, 128, torch.float32), (4, 2048, 1024, torch.bfloat16),
+                                         (2, 512, 512, torch.float32), (3, 77, 4224, torch.bfloat16),
+                                         (2, 5, 100, torch.bfloat16), (1, 1, 24, torch.float32)])
+def test_conv1d_silu_sizes(B, L, C, dtype):
+    # shapes of the reference's tests/test_metal_kernels.py:37-47 plus ragged ones
+    rng = np.random.default_rng(B * 1000 + L)
+    xp = rng.standard_normal((B, L + 3, C), dtype=np.float32)
+    if dtype == torch.bfloat16:
+        xp = oracle.bf16_round(xp)
+    w = (rng.standard_normal((C, 4)) * 0.5).astype(np.float32)
+    b = rng.standard_normal(C).astype(np.float32)
+    ref = oracle.conv1d_silu(xp, w, b, L)
+    out = mixer.conv1d_silu(cu(xp, dtype), cu(w), cu(b), L)
+    assert out.shape == (B, L, C) and out.dtype == dtype
+    assert_close(np_(out), ref, dtype == torch.bfloat16)
+    out2 = mixer.depthwise_conv1d(cu(xp, dtype), cu(w), cu(b), L)
+    assert_close(np_(out2), oracle.depthwise_conv1d(xp, w, b, L), dtype == torch.bfloat16)
+
+
+def test_conv1d_strided_input_uses_generic_path():
+    rng = np.random.default_rng(7)
+    xp = rng.standard_normal((2, 40, 64), dtype=np.float32)
+    w = rng.standard_normal((32, 4), dtype=np.float32)
+    ref = oracle.conv1d_silu(xp[:, :, ::2].copy(), w, np.zeros(32, np.float32), 37)
+    out = mixer.conv1d_silu(cu(xp)[:, :, ::2], cu(w), None, 37)
+    assert_close(np_(out), ref, False)
+
+
+# --------------------------------------------------------------------- fused prefill
+@pytest.mark.parametrize("name", ["toy_prefill", "groups_ragged_state", "short_state"])
+def test_combined_fp32_golden(name):
+    g = load_golden(name)
+    y, h, cs = run_combined(g, torch.float32)
+    assert_close(np_(y), g["y"], False)
+    assert_close(np_(h), g["ssm_state_out"], False)
+    np.testing.assert_array_equal(np_(cs), g["conv_state_out"])
+
+
+@pytest.mark.parametrize("name", ["bf16_p64_n64", "bf16_p64_n128_g2"])
+def test_combined_bf16_golden(name):
+    g = load_golden(name)
+    y, h, cs = run_combined(g, torch.bfloat16)
+    assert y.dtype == torch.bfloat16
+    assert_close(np_(y), g["y"], True)
+    assert_close(np_(h), g["ssm_state_out"], True)
+    np.testing.assert_array_equal(np_(cs), g["conv_state_out"])
+
+
+def test_combined_state_layouts_and_in_place():
+    g = load_golden("groups_ragged_state")
+    y_ref, h_ref, cs_ref = run_combined(g, torch.float32)
+    # [B,H,P,N] ssm state and [B,C,K-1] conv state storage, updated in place
+    B, L, H, P, N, G, Q = (int(v) for v in g["dims"])
+    ssm = cu(g["ssm_state"]).transpose(2, 3).contiguous()            # [B,H,P,N]
+    conv = cu(g["conv_state"]).transpose(1, 2).contiguous()          # [B,C,K-1]
+    ssm_v, conv_v = ssm.transpose(2, 3), conv.transpose(1, 2)
+    y, _, _ = mixer.ssd_combined(
+        cu(g["xBC"]), cu(g["dt_raw"]), cu(g["conv_weight"]), cu(g["conv_bias"]),
+        cu(g["dt_bias"]), cu(g["A_log"]), cu(g["D"]), n_heads=H, head_dim=P, d_state=N,
+        n_groups=G, ssm_state=ssm_v, conv_state=conv_v, ssm_state_out=ssm_v,
+        conv_state_out=conv_v)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(np_(y), np_(y_ref))
+    np.testing.assert_array_equal(np_(ssm.transpose(2, 3)), np_(h_ref))
+    np.testing.assert_array_equal(np_(conv.transpose(1, 2)), np_(cs_ref))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_combined_head_ranges_partition_the_layer(dtype):
+    """Sharding by head range (multi-GPU partitioning) computes exactly the
+    heads of the full call."""
+    g = load_golden("bf16_p64_n128_g2")
+    B, L, H, P, N, G, Q = (int(v) for v in g["dims"])
+    y_full, h_full, _ = run_combined(g, dtype)
+    y = torch.zeros_like(y_full)
+    h = torch.zeros_like(h_full)
+    for h0, hc in ((0, 1), (1, 2), (3, 1)):
+        run_combined(g, dtype, out=y, ssm_state_out=h, head_begin=h0, head_count=hc,
+                     write_conv_state=False)
+    np.testing.assert_array_equal(np_(y), np_(y_full))
+    np.testing.assert_array_equal(np_(h), np_(h_full))
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(B=2, L=700, H=8, P=64, N=64, G=1),
+    dict(B=1, L=513, H=16, P=64, N=128, G=8),
+    dict(B=1, L=129, H=4, P=32, N=16, G=2),
+    dict(B=1, L=3, H=4, P=64, N=128, G=1),
+])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_combined_vs_fp64_recurrence(cfg, dtype):
+    inp = oracle.make_inputs(**cfg, dtype="bf16" if dtype == torch.bfloat16 else "fp32",
+                             seed=11, with_state=True)
+    H, P, N, G = cfg["H"], cfg["P"], cfg["N"], cfg["G"]
+    y64, h64, _ = oracle.mixer_core_fp64(
+        inp["xBC"], inp["dt_raw"], inp["conv_weight"], inp["conv_bias"], inp["dt_bias"],
+        inp["A_log"], inp["D"], n_heads=H, headdim=P, d_state=N, n_groups=G,
+        ssm_state=inp["ssm_state"], conv_state=inp["conv_state"])
+    y, h, _ = mixer.ssd_combined(
+        cu(inp["xBC"], dtype), cu(inp["dt_raw"], dtype), cu(inp["conv_weight"]),
+        cu(inp["conv_bias"]), cu(inp["dt_bias"]), cu(inp["A_log"]), cu(inp["D"]), n_heads=H,
+        head_dim=P, d_state=N, n_groups=G, ssm_state=cu(inp["ssm_state"]),
+        conv_state=cu(inp["conv_state"], dtype))
+    torch.cuda.synchronize()
+    assert_close(np_(y), y64, dtype == torch.bfloat16)
+    assert_close(np_(h), h64, dtype == torch.bfloat16)
+
+
+# ------------------------------------------------------------ pre-discretised scan
+def test_scan_chunk_golden():
+    g = load_golden("scan_chunk")
+    H, P, N = 8, 64, 16
+    y, h = kernels.scan_chunk_metal(cu(g["x"]), cu(g["a"]), cu(g["B"]), cu(g["C"]),
+                                    cu(g["h"]), H, P, N)
+    assert y.dtype == torch.float32
+    assert_close(np_(y), g["y"], False)
+    assert_close(np_(h), g["h_new"], False)
+    y2, _ = kernels.fused_parallel_scan_chunk(cu(g["x"]), cu(g["a"]), cu(g["B"]), cu(g["C"]),
+                                              cu(g["h"]) * 0, H, P, N)
+    assert_close(np_(y2), g["y_seq_zero_h"], False)
+
+
+def test_block_scan_methods_match_oracle():
+    rng = np.random.default_rng(3)
+    B, L, H, P, N = 2, 300, 4, 32, 16
+    x = rng.standard_normal((B, L, H, P), dtype=np.float32)
+    log_a = -rng.uniform(0.01, 0.5, size=(B, L, H)).astype(np.float32)
+    Bm = rng.standard_normal((B, L, H, N), dtype=np.float32)
+    Cm = rng.standard_normal((B, L, H, N), dtype=np.float32)
+    y_ref, h_ref = oracle.selective_scan(x, np.exp(log_a), Bm, Cm, None, log_a, 64)
+    blk = MambaBlock(d_model=H * P // 2, d_state=N, headdim=P, chunk_size=64, device=DEV)
+    cache = MambaCache()
+    y = blk._selective_scan(cu(x), cu(np.exp(log_a)), cu(Bm), cu(Cm), cache, cu(log_a))
+    assert_close(np_(y), y_ref, False)
+    assert_close(np_(cache.ssm_state), h_ref, False)
+    y1 = blk._selective_scan_sequential(cu(x[:, :1]), cu(np.exp(log_a[:, :1])), cu(Bm[:, :1]),
+                                        cu(Cm[:, :1]), None)
+    y1_ref, _ = oracle.selective_scan_sequential(x[:, :1], np.exp(log_a[:, :1]), Bm[:, :1],
+                                                 Cm[:, :1])
+    assert_close(np_(y1), y1_ref, False)
+
+
+# ---------------------------------------------------------------------- decode step
+def test_decode_steps_golden():
+    g = load_golden("decode_steps")
+    B, L0, steps, H, P, N, G, Q = (int(v) for v in g["dims"])
+    kw = dict(n_heads=H, head_dim=P, d_state=N, n_groups=G)
+    p = [cu(g[k]) for k in ("conv_weight", "conv_bias", "dt_bias", "A_log", "D")]
+    y0, h, cs = mixer.ssd_combined(cu(g["xBC"][:, :L0]), cu(g["dt_raw"][:, :L0]), *p,
+                                   chunk_size=Q, **kw)
+    assert_close(np_(y0), g["y_prefill"], False)
+    ys = []
+    for t in range(L0, L0 + steps):
+        ys.append(mixer.ssd_decode_step(cu(g["xBC"][:, t]), cu(g["dt_raw"][:, t]), *p, cs, h,
+                                        **kw))
+    torch.cuda.synchronize()
+    assert_close(np_(torch.stack(ys, 1)), g["y_steps"], False)
+    assert_close(np_(h), g["ssm_state_out"], False)
+    np.testing.assert_array_equal(np_(cs), g["conv_state_out"])
+
+
+@pytest.mark.parametrize("state_layout", ["NP", "PN"])
+@pytest.mark.parametrize("N,P,G,H", [(128, 64, 8, 32), (64, 64, 1, 8), (16, 32, 2, 4), (24, 20, 1, 2)])
+def test_decode_step_vs_fp64(state_layout, N, P, G, H):
+    B, K = 3, 4
+    inp = oracle.make_inputs(B=B, L=1, H=H, P=P, N=N, G=G, dtype="bf16", seed=5,
+                             with_state=True)
+    y64, h64, cs64 = oracle.decode_step_fp64(
+        inp["xBC"][:, 0], inp["dt_raw"][:, 0], inp["conv_weight"], inp["conv_bias"],
+        inp["dt_bias"], inp["A_log"], inp["D"], inp["ssm_state"], inp["conv_state"],
+        n_heads=H, headdim=P, d_state=N, n_groups=G)
+    ssm = cu(inp["ssm_state"])
+    if state_layout == "PN":
+        store = ssm.transpose(2, 3).contiguous()      # [B, H, P, N]
+        ssm = store.transpose(2, 3)
+    conv_store = cu(inp["conv_state"], torch.bfloat16).transpose(1, 2).contiguous()  # [B, C, K-1]
+    y = mixer.ssd_decode_step(
+        cu(inp["xBC"][:, 0], torch.bfloat16), cu(inp["dt_raw"][:, 0], torch.bfloat16),
+        cu(inp["conv_weight"]), cu(inp["conv_bias"]), cu(inp["dt_bias"]), cu(inp["A_log"]),
+        cu(inp["D"]), conv_store.transpose(1, 2), ssm, n_heads=H, head_dim=P, d_state=N,
+        n_groups=G)
+    torch.cuda.synchronize()
+    assert_close(np_(y), y64, True)
+    assert_close(np_(ssm), h64, True)
+    np.testing.assert_array_equal(np_(conv_store.transpose(1, 2)), cs64.astype(np.float32))
+
+
+# ------------------------------------------------------------------- block level
+@pytest.mark.parametrize("combined", [True, False])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_block_autoregressive_matches_parallel(combined, dtype):
+    """The reference's tests/test_mamba_block.py:39-60 invariant: step-by-step
+    generation through the cache equals one parallel pass."""
+    torch.manual_seed(42)
+    kw = dict(combined_proj=True, n_groups=2, use_D=True) if combined else {}
+    blk = MambaBlock(d_model=64, d_state=16, d_conv=4, expand=2, headdim=32, chunk_size=16,
+                     device=DEV, dtype=dtype, **kw)
+    with torch.no_grad():
+        blk.A_log.uniform_(0, 2)
+        blk.dt_bias.uniform_(-3, -1)
+        if blk.D is not None:
+            blk.D.normal_()
+        blk.conv_weight.normal_(0, 0.5)
+        x = torch.randn(2, 40, 64, device=DEV, dtype=dtype)
+        y_par = blk(x)
+        cache = MambaCache()
+        y0 = blk(x[:, :24], cache=cache)
+        outs = [y0] + [blk(x[:, t:t + 1], cache=cache) for t in range(24, 40)]
+        y_seq = torch.cat(outs, dim=1)
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-4
+    assert oracle.rel_l2(np_(y_seq), np_(y_par)) < tol
+    assert cache.ssm_state.shape == (2, 4, 16, 32)
+    conv_dim = 128 + (2 * 2 * 16 if combined else 0)
+    assert cache.conv_state.shape == (2, 3, conv_dim)
