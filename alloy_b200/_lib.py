@@ -29,6 +29,7 @@ STATUS = {
     -3: "alignment",
     -4: "cuda error",
     -5: "no usable device",
+    -6: "device wait timed out",
 }
 
 # every entry point include/alloy_ssd.h declares
@@ -41,6 +42,8 @@ EXPORTS = (
     "alloy_ssd_combined",
     "alloy_selective_scan",
     "alloy_ssd_decode_step",
+    "alloy_ssd_combined_workspace_size",
+    "alloy_check_device_status",
 )
 
 
@@ -108,10 +111,15 @@ def load():
         vp = ctypes.c_void_p
         lib.alloy_conv1d_silu.argtypes = [P, P, P, P, vp]
         lib.alloy_depthwise_conv1d.argtypes = [P, P, P, P, vp]
-        lib.alloy_ssd_combined.argtypes = [P] * 12 + [D, vp]
+        lib.alloy_ssd_combined.argtypes = [P] * 12 + [vp, ctypes.c_size_t, D, vp]
+        lib.alloy_ssd_combined_workspace_size.argtypes = [ctypes.c_int64, ctypes.c_int64,
+                                                          ctypes.c_int32, D]
+        lib.alloy_ssd_combined_workspace_size.restype = ctypes.c_size_t
+        lib.alloy_check_device_status.argtypes = [vp]
         lib.alloy_selective_scan.argtypes = [P] * 8 + [vp]
         lib.alloy_ssd_decode_step.argtypes = [P] * 10 + [D, vp]
-        for name in EXPORTS[3:]:
+        for name in ("alloy_conv1d_silu", "alloy_depthwise_conv1d", "alloy_ssd_combined",
+                     "alloy_selective_scan", "alloy_ssd_decode_step", "alloy_check_device_status"):
             getattr(lib, name).restype = ctypes.c_int
         if lib.alloy_abi_version() != ABI_VERSION:
             raise AlloyLibraryError(

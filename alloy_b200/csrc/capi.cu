@@ -14,13 +14,21 @@ std::string& last_error() {
 }
 
 int current_device_checked(int* dev) {
+  // 0 = unchecked, 1 = sm_100, 2 = other architecture (per device, checked once)
+  static int arch_ok[kMaxDevices] = {0};
   int d = 0;
   ALLOY_CUDA(cudaGetDevice(&d));
-  cudaDeviceProp prop;
-  ALLOY_CUDA(cudaGetDeviceProperties(&prop, d));
-  if (prop.major != 10)
-    return fail(ALLOY_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", d,
-                prop.major, prop.minor);
+  if (d < 0 || d >= kMaxDevices) return fail(ALLOY_ERR_DEVICE, "device index %d out of range", d);
+  if (arch_ok[d] == 0) {
+    int major = 0, minor = 0;
+    ALLOY_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d));
+    ALLOY_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, d));
+    arch_ok[d] = (major == 10 && minor == 0) ? 1 : 2;
+    if (arch_ok[d] == 2)
+      return fail(ALLOY_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", d,
+                  major, minor);
+  }
+  if (arch_ok[d] == 2) return fail(ALLOY_ERR_DEVICE, "device %d is not sm_100", d);
   if (dev) *dev = d;
   return ALLOY_OK;
 }
@@ -117,6 +125,7 @@ int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t* dt_raw,
                        const alloy_tensor_t* D, const alloy_tensor_t* ssm_in,
                        const alloy_tensor_t* conv_in, alloy_tensor_t* y,
                        alloy_tensor_t* ssm_out, alloy_tensor_t* conv_out,
+                       void* workspace, size_t workspace_bytes,
                        const alloy_ssd_dims_t* dims, void* stream) {
   last_error().clear();
   int64_t h0 = 0, hc = 0;
@@ -186,7 +195,7 @@ int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t* dt_raw,
 
   if (L > 0) {
     if (ssd_tc_supported(a)) {
-      ALLOY_TRY(ssd_tc(a, s));
+      ALLOY_TRY(ssd_tc(a, workspace, workspace_bytes, s));
     } else {
       ALLOY_TRY(ssd_simt(a, s));
     }
@@ -199,6 +208,35 @@ int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t* dt_raw,
     ALLOY_TRY(conv_state_update(xBC, present(conv_in) ? conv_in : nullptr, conv_out, (int)H,
                                 (int)P, (int)N, (int)G, (int)K, (int)h0, (int)hc, s));
   }
+  return ALLOY_OK;
+}
+
+size_t alloy_ssd_combined_workspace_size(int64_t batch, int64_t seqlen, int32_t dtype,
+                                         const alloy_ssd_dims_t* dims) {
+  int64_t h0 = 0, hc = 0;
+  if (check_dims(dims, &h0, &hc) != ALLOY_OK || batch < 0 || seqlen < 0) return 0;
+  SsdArgs a;
+  memset(&a, 0, sizeof(a));
+  a.mode = 0;
+  a.B = (int)batch; a.L = (int)seqlen; a.H = (int)dims->n_heads; a.P = (int)dims->head_dim;
+  a.N = (int)dims->d_state; a.G = (int)dims->n_groups; a.K = (int)dims->d_conv;
+  a.head_begin = (int)h0; a.head_count = (int)hc;
+  a.xbc_bf16 = a.y_bf16 = (dtype == ALLOY_BF16);
+  a.y_sp = 1;
+  // layout conditions are checked per call; size the workspace by dims alone
+  if (!a.xbc_bf16 || a.P != 64 || !(a.N == 64 || a.N == 128) || a.K != 4 ||
+      (a.H / a.G) % 2 != 0 || a.head_begin % 2 != 0 || a.head_count % 2 != 0)
+    return 0;
+  return ssd_tc_workspace_bytes(a);
+}
+
+int alloy_check_device_status(void* stream) {
+  last_error().clear();
+  unsigned int e[3] = {0, 0, 0};
+  ALLOY_TRY(ssd_tc_take_error(as_stream(stream), e));
+  if (e[0] != 0)
+    return fail(ALLOY_ERR_TIMEOUT, "ssd_tc_kernel: bounded wait at site %u ran out (block %u, %u)",
+                e[0] - 1, e[1], e[2]);
   return ALLOY_OK;
 }
 

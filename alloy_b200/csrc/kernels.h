@@ -70,7 +70,11 @@ int ssd_decode_step(const DecodeArgs& a, cudaStream_t s);
 
 // ssd_tc.cu: tcgen05 tensor-core SSD for bf16 inputs (mode 0 only).
 // Returns ALLOY_ERR_UNSUPPORTED (and launches nothing) for sizes it does not cover.
-int ssd_tc(const SsdArgs& a, cudaStream_t s);
 bool ssd_tc_supported(const SsdArgs& a);
+size_t ssd_tc_workspace_bytes(const SsdArgs& a);
+int ssd_tc(const SsdArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t s);
+// Synchronises the stream, then reads and clears the error word that a CTA
+// of the tensor-core SSD writes when one of its bounded waits runs out.
+int ssd_tc_take_error(cudaStream_t s, unsigned int out[3]);
 
 }  // namespace alloy

@@ -1,10 +1,807 @@
-// tcgen05 tensor-core SSD (bf16 inputs): placeholder until the kernel lands.
+// Tensor-core (tcgen05) chunked SSD for bf16 activations: the fused prefill
+// of alloy/models/mamba_block.py:446-493 (conv + SiLU, discretisation,
+// _selective_scan / _scan_chunk :206-366, D skip).
+//
+// Two launches per call:
+//  1. bc_conv_kernel: conv1d + SiLU of the B and C columns of the selected
+//     head groups -> bf16 workspace [B, L, groups, {B,C}, N].  Every head of a
+//     group reads the same B/C, so they are produced once instead of once per
+//     head pair.
+//  2. ssd_tc_kernel: one CTA per (batch row, pair of heads of one group),
+//     walking chunks of Q = 128 steps in order with the fp32 state resident in
+//     tensor memory.  Per chunk (t, s in [0, Q); p < P = 64; n < N):
+//        cum[t]  = sum_{u<=t} A dt_u                      (fp32, per head)
+//        CB      = C B^T                                  (tcgen05, TMEM)
+//        S[t,s]  = CB[t,s] exp(cum[t]-cum[s]) dt_s  (s<=t), + D on s==t
+//        Y       = S X                                    (tcgen05)
+//        Yi      = C H^T,  H = bf16(state) before this chunk
+//        y[t]    = Y[t] + exp(cum[t]) Yi[t]               (epilogue, bf16)
+//        state   = exp(cum[Q-1]) state + X'^T B,  X'[s] = X[s] dt_s exp(cum[Q-1]-cum[s])
+//     X is the unscaled conv+SiLU output of the pair's x channels (bf16,
+//     produced in the CTA); B/C tiles arrive by TMA (128-byte swizzle) into a
+//     two-stage ring of 64-column halves.  The state of both heads is one
+//     128 x N fp32 TMEM accumulator with rows (head, p): its update is a
+//     single M = 128 MMA per N-half.
+//
+// Warp roles (320 threads): warps 0-3 / 4-7 = warpgroup of head 0 / 1 (conv,
+// dt/cumsum, scores S, X', state copy, epilogue); warp 8 = TMA producer;
+// warp 9 = TMEM allocator and MMA issuer.  Every mbarrier wait is bounded:
+// on timeout the CTA records an error word, drains its in-flight copies and
+// MMAs, frees its tensor memory and exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_ptx.cuh"
 
 namespace alloy {
-bool ssd_tc_supported(const SsdArgs&) { return false; }
-int ssd_tc(const SsdArgs&, cudaStream_t) {
-  return fail(ALLOY_ERR_UNSUPPORTED, "ssd_tc: not available");
+
+// error word written by a CTA whose bounded wait ran out (0 = none):
+// [0] = 1 + site id, [1] = blockIdx.x, [2] = blockIdx.y
+__device__ unsigned int g_ssd_tc_error[3];
+
+namespace {
+
+using namespace tc;
+
+constexpr int Q = 128;                 // chunk length (UMMA M)
+constexpr int P = 64;                  // head dim
+constexpr int kThreads = 320;
+constexpr int kMmaWarp = 9;
+constexpr int kTmaWarp = 8;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
+
+// shared-memory map (bytes from the 1024-aligned base)
+constexpr uint32_t kStageBytes = 32768;             // B half [128][64] + C half [128][64] bf16
+constexpr uint32_t OFF_STAGE = 0;                   // 2 stages
+constexpr uint32_t OFF_X = 65536;                   // X_h [128 s][64 p] bf16, 16 KB each
+constexpr uint32_t OFF_S = 98304;                   // S_h [2][128 t][64 s] bf16, 32 KB each
+constexpr uint32_t OFF_HX = 163840;                 // H_h / X'_h, 16 KB each
+constexpr uint32_t OFF_MISC = 196608;
+// misc: floats
+constexpr uint32_t OFF_CUM = OFF_MISC;              // [2][128]
+constexpr uint32_t OFF_DT = OFF_CUM + 1024;         // [2][128]
+constexpr uint32_t OFF_CF = OFF_DT + 1024;          // [2][128] column factors
+constexpr uint32_t OFF_WSUM = OFF_CF + 1024;        // [2][4]
+constexpr uint32_t OFF_BAR = OFF_WSUM + 64;         // mbarriers (8 bytes each)
+constexpr int NBAR = 20;
+constexpr uint32_t OFF_TMEMPTR = OFF_BAR + NBAR * 8;
+constexpr uint32_t OFF_ABORT = OFF_TMEMPTR + 8;
+constexpr uint32_t kSmemBytes = OFF_ABORT + 16 + 1024;  // + alignment slack
+
+// barrier ids
+enum {
+  B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1, B_CB_FULL, B_CB_EMPTY, B_HBF_READY, B_YI_DONE,
+  B_XP_READY, B_ST_DONE, B_S_READY0, B_S_READY1, B_X_FREE0, B_X_FREE1, B_Y_FULL, B_Y_EMPTY,
+  B_DRAIN, B_WG0, B_WG1, B_XWG
+};
+
+// TMEM columns
+constexpr uint32_t T_CB = 0;      // [128 t][128 s] fp32
+constexpr uint32_t T_ST = 128;    // [128 (h,p)][N] fp32
+constexpr uint32_t T_Y = 256;     // + 64 h
+constexpr uint32_t T_YI = 384;    // + 64 h
+
+struct TcArgs {
+  int B, L, H, N, G, K;
+  int head_begin, group_begin;
+  const __nv_bfloat16* xbc; int64_t x_sb, x_st;
+  const void* dt; int dt_bf16; int64_t dt_sb, dt_st, dt_sh;
+  const float* conv_w; int64_t cw_sc, cw_sk;
+  const float* conv_b; int64_t cb_s;
+  const float* dt_bias; int64_t dtb_s;
+  const float* A_log; int64_t al_s;
+  const float* Dp; int64_t d_s;
+  const __nv_bfloat16* conv_in; int64_t ci_sb, ci_sk, ci_sc;
+  const float* ssm_in; int64_t si_sb, si_sh, si_sn, si_sp;
+  float* ssm_out; int64_t so_sb, so_sh, so_sn, so_sp;
+  __nv_bfloat16* y; int64_t y_sb, y_st, y_sh;
+};
+
+// ----------------------------------------------------------------------------
+// bounded waits
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void signal_abort(volatile int* abort_flag, int site) {
+  *abort_flag = 1;
+  if (atomicCAS(&g_ssd_tc_error[0], 0u, 1u + site) == 0u) {
+    g_ssd_tc_error[1] = blockIdx.x;
+    g_ssd_tc_error[2] = blockIdx.y;
+  }
 }
+
+// single-thread wait (TMA / MMA roles)
+__device__ __forceinline__ bool wait1(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                      int site) {
+  const long long t0 = clock64();
+  for (uint32_t it = 0; it < (1u << 30); ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) break;
+  }
+  signal_abort(abort_flag, site);
+  return false;
+}
+
+// warp-uniform wait (all 32 lanes poll; the outcome is the same on all lanes)
+__device__ __forceinline__ bool waitw(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                      int site) {
+  const long long t0 = clock64();
+  for (uint32_t it = 0; it < (1u << 30); ++it) {
+    const uint32_t ok = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, ok)) return true;
+    const int ab = *abort_flag;
+    const int late = clock64() - t0 > kWaitCycles;
+    if (__any_sync(0xffffffffu, ab || late)) {
+      if (!ab && late && (threadIdx.x & 31) == 0) signal_abort(abort_flag, site);
+      __syncwarp();
+      return false;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) signal_abort(abort_flag, site);
+  __syncwarp();
+  return false;
+}
+
+// Barrier among the warps of one or both warpgroups, built on an mbarrier so
+// that it is bounded like every other wait (a hardware bar.sync is not).
+// `uses` counts this warp's previous uses of the barrier (its phase).
+__device__ __forceinline__ bool warps_sync(uint32_t bar, uint32_t& uses, volatile int* abort_flag,
+                                           int site) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+  const bool ok = waitw(bar, uses & 1, abort_flag, site);
+  ++uses;
+  return ok;
+}
+
+// 16-byte chunk `chunk` (0..7) of row `row` in a 128-byte-swizzled tile
+__device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
+  return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// ----------------------------------------------------------------------------
+// B/C conv + SiLU pre-pass
+// ----------------------------------------------------------------------------
+// bc[b, t, j], j in [0, 2*Gs*N): group gl = j / (2N), part = (j / N) % 2 (0 = B,
+// 1 = C), n = j % N; source channel H*P + part*G*N + (group_begin + gl)*N + n.
+__global__ void __launch_bounds__(256)
+bc_conv_kernel(const TcArgs a, __nv_bfloat16* __restrict__ bc, int ncols) {
+  const int b = blockIdx.z;
+  const int v = threadIdx.x & 31;
+  const int rg = threadIdx.x >> 5;
+  const int j = (blockIdx.x * 32 + v) * 8;
+  if (j >= ncols) return;
+  const int t_first = blockIdx.y * 64 + rg * 8;
+  if (t_first >= a.L) return;
+  const int N = a.N;
+  const int gl = j / (2 * N), part = (j / N) & 1, n = j % N;
+  const int c = a.H * P + part * a.G * N + (a.group_begin + gl) * N + n;
+  float w[8][4], bias[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[i][k] = a.conv_w[(int64_t)(c + i) * a.cw_sc + k * a.cw_sk];
+    bias[i] = a.conv_b ? a.conv_b[(int64_t)(c + i) * a.cb_s] : 0.f;
+  }
+  float raw[11][8];
+#pragma unroll
+  for (int r = 0; r < 11; ++r) {
+    const int t = t_first - 3 + r;
+    if (t >= 0 && t < a.L) {
+      const uint4 u = ldg_nc_v4(a.xbc + (int64_t)b * a.x_sb + (int64_t)t * a.x_st + c);
+      const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        raw[r][2 * i] = bf16_lo(wd[i]);
+        raw[r][2 * i + 1] = bf16_hi(wd[i]);
+      }
+    } else if (t < 0 && a.conv_in) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        raw[r][i] = __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb + (int64_t)(a.K - 1 + t) * a.ci_sk +
+                                               (int64_t)(c + i) * a.ci_sc]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) raw[r][i] = 0.f;
+    }
+  }
+  __nv_bfloat16* dst = bc + ((int64_t)b * a.L + t_first) * ncols + j;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    if (t_first + r >= a.L) break;
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float f[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int ch = 2 * i + e;
+        float acc = bias[ch];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc = fmaf(raw[r + k][ch], w[ch][k], acc);
+        f[e] = silu_fast(acc);
+      }
+      o[i] = pack_bf16x2(f[0], f[1]);
+    }
+    *reinterpret_cast<uint4*>(dst + (int64_t)r * ncols) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// the SSD kernel
+// ----------------------------------------------------------------------------
+template <int N>
+__global__ void __launch_bounds__(kThreads, 1)
+ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
+  constexpr int NK = N / 64;            // 64-column halves of B/C per chunk
+  constexpr int NHALF = N / 2;          // state columns per warpgroup
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_base);
+
+  float* cum_s = reinterpret_cast<float*>(smem + OFF_CUM);
+  float* dt_s = reinterpret_cast<float*>(smem + OFF_DT);
+  float* cf_s = reinterpret_cast<float*>(smem + OFF_CF);
+  float* wsum = reinterpret_cast<float*>(smem + OFF_WSUM);
+  volatile uint32_t* tmem_ptr = reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEMPTR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_ABORT);
+  auto bar = [&](int i) { return base + OFF_BAR + 8u * i; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+  const int h0 = a.head_begin + 2 * blockIdx.x;   // first head of the pair
+  const int hpg = a.H / a.G;
+  const int gl = h0 / hpg - a.group_begin;        // group index inside the workspace
+  const int L = a.L;
+  const int nchunks = (L + Q - 1) / Q;
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    mbar_init(bar(B_FULL0), 1);
+    mbar_init(bar(B_FULL1), 1);
+    mbar_init(bar(B_EMPTY0), 1);
+    mbar_init(bar(B_EMPTY1), 1);
+    mbar_init(bar(B_CB_FULL), 1);
+    mbar_init(bar(B_CB_EMPTY), 8);
+    mbar_init(bar(B_HBF_READY), 8);
+    mbar_init(bar(B_YI_DONE), 1);
+    mbar_init(bar(B_XP_READY), 8);
+    mbar_init(bar(B_ST_DONE), 1);
+    mbar_init(bar(B_S_READY0), 4);
+    mbar_init(bar(B_S_READY1), 4);
+    mbar_init(bar(B_X_FREE0), 1);
+    mbar_init(bar(B_X_FREE1), 1);
+    mbar_init(bar(B_Y_FULL), 1);
+    mbar_init(bar(B_Y_EMPTY), 8);
+    mbar_init(bar(B_DRAIN), 1);
+    mbar_init(bar(B_WG0), 4);
+    mbar_init(bar(B_WG1), 4);
+    mbar_init(bar(B_XWG), 8);
+    mbar_fence_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(base + OFF_TMEMPTR, 512);
+    tmem_relinquish();
+  }
+  if (warp == kTmaWarp && lane == 0) prefetch_tmap(&bc_map);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_ptr;
+
+  if (warp == kTmaWarp) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int c = 0; c < nchunks; ++c) {
+        for (int k = 0; k < NK; ++k) {
+          const int i = c * NK + k, slot = i & 1;
+          if (i >= 2 && !wait1(bar(B_EMPTY0 + slot), ((i >> 1) - 1) & 1, abort_flag, 1)) goto tma_done;
+          mbar_arrive_expect_tx(bar(B_FULL0 + slot), kStageBytes);
+          const uint32_t dst = base + OFF_STAGE + slot * kStageBytes;
+          tma_load_3d(dst, &bc_map, bar(B_FULL0 + slot), (gl * 2 + 0) * N + 64 * k, c * Q, b);
+          tma_load_3d(dst + 16384, &bc_map, bar(B_FULL0 + slot), (gl * 2 + 1) * N + 64 * k, c * Q, b);
+          ++issued;
+        }
+      }
+    tma_done:
+      // the copies of the last two fills must land before the CTA exits
+      for (int i = max(0, issued - 2); i < issued; ++i) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(bar(B_FULL0 + (i & 1)), (i >> 1) & 1) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_CB = idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t ID_YI = idesc_bf16(128, 64, 0, 0);
+      constexpr uint32_t ID_ST = idesc_bf16(128, 64, 1, 1);
+      constexpr uint32_t ID_Y = idesc_bf16(128, 64, 0, 1);
+      for (int c = 0; c < nchunks; ++c) {
+        const uint32_t ph = c & 1, pph = (c - 1) & 1;
+        // CB = C B^T over the N halves
+        for (int k = 0; k < NK; ++k) {
+          const int i = c * NK + k, slot = i & 1;
+          if (!wait1(bar(B_FULL0 + slot), (i >> 1) & 1, abort_flag, 2)) goto mma_done;
+          if (k == 0 && c > 0 && !wait1(bar(B_CB_EMPTY), pph, abort_flag, 3)) goto mma_done;
+          tc_fence_after();
+          const uint32_t sB = base + OFF_STAGE + slot * kStageBytes, sC = sB + 16384;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + T_CB, sw128_desc(sC + 32 * kk, 16, 1024),
+                      sw128_desc(sB + 32 * kk, 16, 1024), ID_CB, (k | kk) != 0);
+        }
+        umma_commit(bar(B_CB_FULL));
+        // Yi_h = C H_h^T
+        if (!wait1(bar(B_HBF_READY), ph, abort_flag, 4)) goto mma_done;
+        if (c > 0 && !wait1(bar(B_Y_EMPTY), pph, abort_flag, 5)) goto mma_done;
+        tc_fence_after();
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t sH = base + OFF_HX + h * 16384;
+          for (int k = 0; k < NK; ++k) {
+            const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(tmem + T_YI + 64 * h, sw128_desc(sC + 32 * kk, 16, 1024),
+                        sw128_desc(sH + k * 8192 + 32 * kk, 16, 1024), ID_YI, (k | kk) != 0);
+          }
+        }
+        umma_commit(bar(B_YI_DONE));
+        // state: ST[(h,p), n] += X'^T B over s, per N half; releases the stages
+        if (!wait1(bar(B_XP_READY), ph, abort_flag, 6)) goto mma_done;
+        tc_fence_after();
+        for (int k = 0; k < NK; ++k) {
+          const int slot = (c * NK + k) & 1;
+          const uint32_t sB = base + OFF_STAGE + slot * kStageBytes;
+          const uint32_t sX = base + OFF_HX;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tmem + T_ST + 64 * k, sw128_desc(sX + 2048 * kk, 16384, 1024),
+                      sw128_desc(sB + 2048 * kk, 16384, 1024), ID_ST, 1);
+          umma_commit(bar(B_EMPTY0 + slot));
+        }
+        umma_commit(bar(B_ST_DONE));
+        // Y_h = S_h X_h
+        for (int h = 0; h < 2; ++h) {
+          if (!wait1(bar(B_S_READY0 + h), ph, abort_flag, 7)) goto mma_done;
+          tc_fence_after();
+          const uint32_t sS = base + OFF_S + h * 32768, sX = base + OFF_X + h * 16384;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tmem + T_Y + 64 * h, sw128_desc(sS + (kk >> 2) * 16384 + 32 * (kk & 3), 16, 1024),
+                      sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
+          umma_commit(bar(B_X_FREE0 + h));
+        }
+        umma_commit(bar(B_Y_FULL));
+      }
+    mma_done:
+      // wait (bounded) for every MMA this thread issued
+      umma_commit(bar(B_DRAIN));
+      {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(bar(B_DRAIN), 0) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ warpgroups
+    const int wg = warp >> 2;           // head of the pair handled by this warpgroup
+    const int q = warp & 3;             // TMEM lane quadrant
+    const int t = q * 32 + lane;        // row of this thread (t, s or (h,p))
+    const int tid = threadIdx.x & 127;
+    const int head = h0 + wg;
+    const float A = -expf(a.A_log[(int64_t)head * a.al_s]);
+    const float dtb = a.dt_bias[(int64_t)head * a.dtb_s];
+    const float Dh = a.Dp ? a.Dp[(int64_t)head * a.d_s] : 0.f;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    // state rows: r = t -> head hr = t / 64, p = t % 64; this warpgroup owns
+    // state columns [wg * N/2, (wg+1) * N/2)
+    const int hr = t >> 6, pr = t & 63;
+
+    // conv weights of this thread's 8 x channels
+    const int vc = tid & 7, strip = tid >> 3;
+    const int xch = head * P + vc * 8;
+    float w[8][4], cbias[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) w[i][k] = a.conv_w[(int64_t)(xch + i) * a.cw_sc + k * a.cw_sk];
+      cbias[i] = a.conv_b ? a.conv_b[(int64_t)(xch + i) * a.cb_s] : 0.f;
+    }
+
+    // initial state -> TMEM
+    for (int cc = 0; cc < NHALF / 32; ++cc) {
+      uint32_t r[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int n = wg * NHALF + cc * 32 + i;
+        const float v = a.ssm_in ? a.ssm_in[(int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh +
+                                            (int64_t)n * a.si_sn + (int64_t)pr * a.si_sp]
+                                 : 0.f;
+        r[i] = __float_as_uint(v);
+      }
+      tmem_st32(lane_base + T_ST + wg * NHALF + cc * 32, r);
+    }
+    tmem_st_wait();
+
+    uint32_t wg_uses = 0, x_uses = 0;
+    for (int c = 0; c < nchunks; ++c) {
+      const uint32_t ph = c & 1, pph = (c - 1) & 1;
+      const int t0 = c * Q;
+      if (c > 0 && !waitw(bar(B_X_FREE0 + wg), pph, abort_flag, 10)) break;
+      // ---- dt, cumulative log decay (this head) ----
+      {
+        const int tt = t0 + tid;
+        float dt = 0.f;
+        if (tt < L) {
+          const float raw = load_any(a.dt, (int64_t)b * a.dt_sb + (int64_t)tt * a.dt_st +
+                                               (int64_t)head * a.dt_sh, a.dt_bf16);
+          dt = softplus_f32(raw + dtb);
+        }
+        float v = A * dt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float u = __shfl_up_sync(0xffffffffu, v, o);
+          if (lane >= o) v += u;
+        }
+        if (lane == 31) wsum[wg * 4 + q] = v;
+        if (!warps_sync(bar(B_WG0 + wg), wg_uses, abort_flag, 16)) break;
+        for (int i = 0; i < q; ++i) v += wsum[wg * 4 + i];
+        cum_s[wg * 128 + tid] = v;
+        dt_s[wg * 128 + tid] = dt;
+      }
+      // ---- conv + SiLU of this head's x channels -> X_h (bf16, unscaled) ----
+      {
+        float raw[11][8];
+#pragma unroll
+        for (int r = 0; r < 11; ++r) {
+          const int tt = t0 + strip * 8 - 3 + r;
+          if (tt >= 0 && tt < L) {
+            const uint4 u = ldg_nc_v4(a.xbc + (int64_t)b * a.x_sb + (int64_t)tt * a.x_st + xch);
+            const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              raw[r][2 * i] = bf16_lo(wd[i]);
+              raw[r][2 * i + 1] = bf16_hi(wd[i]);
+            }
+          } else if (tt < 0 && a.conv_in) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              raw[r][i] = __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
+                                                     (int64_t)(a.K - 1 + tt) * a.ci_sk +
+                                                     (int64_t)(xch + i) * a.ci_sc]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) raw[r][i] = 0.f;
+          }
+        }
+        const uint32_t sX = base + OFF_X + wg * 16384;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const int s = strip * 8 + r;
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float f[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int ch = 2 * i + e;
+              float acc = cbias[ch];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) acc = fmaf(raw[r + k][ch], w[ch][k], acc);
+              f[e] = (t0 + s < L) ? silu_fast(acc) : 0.f;
+            }
+            o[i] = pack_bf16x2(f[0], f[1]);
+          }
+          st_shared_v4(sX + sw_off(s, vc), o[0], o[1], o[2], o[3]);
+        }
+      }
+      if (!warps_sync(bar(B_WG0 + wg), wg_uses, abort_flag, 17)) break;
+      // ---- column factors cf[s] = exp(cum[end of s's 32-block] - cum[s]) dt[s] ----
+      {
+        const float* cm = cum_s + wg * 128;
+        cf_s[wg * 128 + tid] = ex2_approx((cm[(tid | 31)] - cm[tid]) * kLog2e) * dt_s[wg * 128 + tid];
+      }
+      fence_async_smem();
+      // both heads' cum / dt / cf visible
+      if (!warps_sync(bar(B_XWG), x_uses, abort_flag, 18)) break;
+      // ---- state: H = bf16(state) -> HX_hr; state *= exp(cum[Q-1]) ----
+      if (c > 0 && !waitw(bar(B_ST_DONE), pph, abort_flag, 11)) break;
+      tc_fence_after();
+      {
+        const float e_end = ex2_approx(cum_s[hr * 128 + 127] * kLog2e);
+        const uint32_t sH = base + OFF_HX + hr * 16384;
+#pragma unroll
+        for (int cc = 0; cc < NHALF / 32; ++cc) {
+          const int n0 = wg * NHALF + cc * 32;
+          uint32_t r[32];
+          tmem_ld32(lane_base + T_ST + n0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int g4 = 0; g4 < 4; ++g4) {
+            const int n = n0 + g4 * 8;
+            uint32_t o[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              o[i] = pack_bf16x2(__uint_as_float(r[g4 * 8 + 2 * i]), __uint_as_float(r[g4 * 8 + 2 * i + 1]));
+            st_shared_v4(sH + (n >> 6) * 8192 + sw_off(pr, (n & 63) >> 3), o[0], o[1], o[2], o[3]);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * e_end);
+          tmem_st32(lane_base + T_ST + n0, r);
+        }
+        tmem_st_wait();
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_HBF_READY));
+      // ---- scores S_h = CB * decay * dt (+ D on the diagonal) ----
+      if (!waitw(bar(B_CB_FULL), ph, abort_flag, 12)) break;
+      tc_fence_after();
+      {
+        const float* cm = cum_s + wg * 128;
+        const float* dtv = dt_s + wg * 128;
+        const float* cfv = cf_s + wg * 128;
+        const float cum_t = cm[t];
+        const uint32_t sS = base + OFF_S + wg * 32768;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float f[32];
+          if (j > q) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) f[i] = 0.f;
+          } else {
+            uint32_t r[32];
+            tmem_ld32(lane_base + T_CB + 32 * j, r);
+            tmem_ld_wait();
+            if (j < q) {
+              const float R = ex2_approx((cum_t - cm[32 * j + 31]) * kLog2e);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(r[i]) * R * cfv[32 * j + i];
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int s = 32 * j + i;
+                float v = 0.f;
+                if (s <= t) v = __uint_as_float(r[i]) * ex2_approx((cum_t - cm[s]) * kLog2e) * dtv[s];
+                if (s == t) v += Dh;
+                f[i] = v;
+              }
+            }
+          }
+          // 32 columns = 4 chunks of 8 in the (j/2)-th 64-column block
+#pragma unroll
+          for (int g4 = 0; g4 < 4; ++g4) {
+            const int chunk = (j & 1) * 4 + g4;
+            st_shared_v4(sS + (j >> 1) * 16384 + sw_off(t, chunk),
+                         pack_bf16x2(f[g4 * 8 + 0], f[g4 * 8 + 1]),
+                         pack_bf16x2(f[g4 * 8 + 2], f[g4 * 8 + 3]),
+                         pack_bf16x2(f[g4 * 8 + 4], f[g4 * 8 + 5]),
+                         pack_bf16x2(f[g4 * 8 + 6], f[g4 * 8 + 7]));
+          }
+        }
+      }
+      tc_fence_before();
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(bar(B_CB_EMPTY));
+        mbar_arrive(bar(B_S_READY0 + wg));
+      }
+      // ---- X'_h = X_h * dt * exp(cum[Q-1] - cum[s]) -> HX_h ----
+      if (!waitw(bar(B_YI_DONE), ph, abort_flag, 13)) break;
+      {
+        const float* cm = cum_s + wg * 128;
+        const float e = dt_s[wg * 128 + t] * ex2_approx((cm[127] - cm[t]) * kLog2e);
+        const uint32_t sX = base + OFF_X + wg * 16384, sXp = base + OFF_HX + wg * 16384;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const uint4 u = ld_shared_v4(sX + sw_off(t, ch));
+          const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) o[i] = pack_bf16x2(bf16_lo(wd[i]) * e, bf16_hi(wd[i]) * e);
+          st_shared_v4(sXp + sw_off(t, ch), o[0], o[1], o[2], o[3]);
+        }
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_XP_READY));
+      // ---- epilogue: y = Y + exp(cum[t]) Yi -> global (bf16) ----
+      if (!waitw(bar(B_Y_FULL), ph, abort_flag, 14)) break;
+      tc_fence_after();
+      {
+        const float e = ex2_approx(cum_s[wg * 128 + t] * kLog2e);
+        const bool valid = t0 + t < L;
+        __nv_bfloat16* yrow = a.y + (int64_t)b * a.y_sb + (int64_t)(t0 + t) * a.y_st +
+                              (int64_t)head * a.y_sh;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t ry[32], ri[32];
+          tmem_ld32(lane_base + T_Y + 64 * wg + 32 * half, ry);
+          tmem_ld32(lane_base + T_YI + 64 * wg + 32 * half, ri);
+          tmem_ld_wait();
+          if (valid) {
+#pragma unroll
+            for (int g4 = 0; g4 < 4; ++g4) {
+              uint32_t o[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int k0 = g4 * 8 + 2 * i;
+                o[i] = pack_bf16x2(fmaf(e, __uint_as_float(ri[k0]), __uint_as_float(ry[k0])),
+                                   fmaf(e, __uint_as_float(ri[k0 + 1]), __uint_as_float(ry[k0 + 1])));
+              }
+              *reinterpret_cast<uint4*>(yrow + half * 32 + g4 * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_Y_EMPTY));
+    }
+    // ---- final state -> ssm_out ----
+    if (!*abort_flag && a.ssm_out && waitw(bar(B_ST_DONE), (nchunks - 1) & 1, abort_flag, 15)) {
+      tc_fence_after();
+      for (int cc = 0; cc < NHALF / 32; ++cc) {
+        const int n0 = wg * NHALF + cc * 32;
+        uint32_t r[32];
+        tmem_ld32(lane_base + T_ST + n0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          a.ssm_out[(int64_t)b * a.so_sb + (int64_t)(h0 + hr) * a.so_sh + (int64_t)(n0 + i) * a.so_sn +
+                    (int64_t)pr * a.so_sp] = __uint_as_float(r[i]);
+      }
+    }
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// host side
+// ----------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int group_range(const SsdArgs& a, int* g0, int* gs) {
+  const int hpg = a.H / a.G;
+  *g0 = a.head_begin / hpg;
+  *gs = (a.head_begin + a.head_count - 1) / hpg - *g0 + 1;
+  return ALLOY_OK;
+}
+
+}  // namespace
+
+bool ssd_tc_supported(const SsdArgs& a) {
+  if (a.mode != 0 || !a.xbc_bf16 || !a.y_bf16) return false;
+  if (a.P != 64 || !(a.N == 64 || a.N == 128) || a.K != 4) return false;
+  if ((a.H / a.G) % 2 != 0 || a.head_begin % 2 != 0 || a.head_count % 2 != 0) return false;
+  if (a.conv_in && !a.ci_bf16) return false;
+  if ((reinterpret_cast<uintptr_t>(a.xBC) & 15) || (a.xbc_sb & 7) || (a.xbc_st & 7)) return false;
+  if ((reinterpret_cast<uintptr_t>(a.y) & 15) || a.y_sp != 1 || (a.y_sb & 7) || (a.y_st & 7) ||
+      (a.y_sh & 7))
+    return false;
+  if (a.L < 1 || a.B < 1 || a.B > 65535) return false;
+  return true;
+}
+
+size_t ssd_tc_workspace_bytes(const SsdArgs& a) {
+  int g0, gs;
+  group_range(a, &g0, &gs);
+  return (size_t)a.B * a.L * 2 * gs * a.N * sizeof(__nv_bfloat16);
+}
+
+int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!ssd_tc_supported(s)) return fail(ALLOY_ERR_UNSUPPORTED, "ssd_tc: unsupported sizes/layout");
+  const size_t need = ssd_tc_workspace_bytes(s);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(ALLOY_ERR_INVALID_ARG, "ssd_tc: workspace of %zu bytes required, got %zu", need,
+                workspace_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) & 15)
+    return fail(ALLOY_ERR_ALIGNMENT, "ssd_tc: workspace must be 16-byte aligned");
+  int g0, gs;
+  group_range(s, &g0, &gs);
+
+  TcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.B = s.B; a.L = s.L; a.H = s.H; a.N = s.N; a.G = s.G; a.K = s.K;
+  a.head_begin = s.head_begin; a.group_begin = g0;
+  a.xbc = static_cast<const __nv_bfloat16*>(s.xBC); a.x_sb = s.xbc_sb; a.x_st = s.xbc_st;
+  a.dt = s.dt_raw; a.dt_bf16 = s.dt_bf16; a.dt_sb = s.dt_sb; a.dt_st = s.dt_st; a.dt_sh = s.dt_sh;
+  a.conv_w = s.conv_w; a.cw_sc = s.cw_sc; a.cw_sk = s.cw_sk;
+  a.conv_b = s.conv_b; a.cb_s = s.cb_s;
+  a.dt_bias = s.dt_bias; a.dtb_s = s.dtb_s;
+  a.A_log = s.A_log; a.al_s = s.al_s;
+  a.Dp = s.Dp; a.d_s = s.d_s;
+  a.conv_in = static_cast<const __nv_bfloat16*>(s.conv_in);
+  a.ci_sb = s.ci_sb; a.ci_sk = s.ci_sk; a.ci_sc = s.ci_sc;
+  a.ssm_in = s.ssm_in; a.si_sb = s.si_sb; a.si_sh = s.si_sh; a.si_sn = s.si_sn; a.si_sp = s.si_sp;
+  a.ssm_out = s.ssm_out; a.so_sb = s.so_sb; a.so_sh = s.so_sh; a.so_sn = s.so_sn; a.so_sp = s.so_sp;
+  a.y = static_cast<__nv_bfloat16*>(s.y); a.y_sb = s.y_sb; a.y_st = s.y_st; a.y_sh = s.y_sh;
+
+  // 1. B/C conv pre-pass into the workspace
+  const int ncols = 2 * gs * s.N;
+  __nv_bfloat16* bc = static_cast<__nv_bfloat16*>(workspace);
+  {
+    dim3 grid((ncols / 8 + 31) / 32, (s.L + 63) / 64, s.B);
+    bc_conv_kernel<<<grid, 256, 0, stream>>>(a, bc, ncols);
+    ALLOY_TRY(check_launch("bc_conv_kernel"));
+  }
+  // 2. tensor map over the workspace [B][L][ncols], box 64 columns x 128 rows
+  PFN_cuTensorMapEncodeTiled_v12000 encode = get_encode_fn();
+  if (!encode) return fail(ALLOY_ERR_CUDA, "ssd_tc: cuTensorMapEncodeTiled unavailable");
+  CUtensorMap map;
+  const cuuint64_t gdim[3] = {(cuuint64_t)ncols, (cuuint64_t)s.L, (cuuint64_t)s.B};
+  const cuuint64_t gstride[2] = {(cuuint64_t)ncols * 2, (cuuint64_t)ncols * 2 * s.L};
+  const cuuint32_t box[3] = {64, (cuuint32_t)Q, 1};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, bc, gdim, gstride, box, estride,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ALLOY_ERR_CUDA, "ssd_tc: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  // 3. the SSD kernel
+  dim3 grid(s.head_count / 2, s.B);
+  if (s.N == 128) {
+    ALLOY_CUDA(cudaFuncSetAttribute(ssd_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)kSmemBytes));
+    ssd_tc_kernel<128><<<grid, kThreads, kSmemBytes, stream>>>(map, a);
+  } else {
+    ALLOY_CUDA(cudaFuncSetAttribute(ssd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)kSmemBytes));
+    ssd_tc_kernel<64><<<grid, kThreads, kSmemBytes, stream>>>(map, a);
+  }
+  return check_launch("ssd_tc_kernel");
+}
+
+int ssd_tc_take_error(cudaStream_t stream, unsigned int out[3]) {
+  ALLOY_CUDA(cudaStreamSynchronize(stream));
+  unsigned int zero[3] = {0, 0, 0};
+  ALLOY_CUDA(cudaMemcpyFromSymbol(out, g_ssd_tc_error, sizeof(zero)));
+  if (out[0] != 0) ALLOY_CUDA(cudaMemcpyToSymbol(g_ssd_tc_error, zero, sizeof(zero)));
+  return ALLOY_OK;
+}
+
 }  // namespace alloy

@@ -120,15 +120,35 @@ def ssd_combined(xBC, dt_raw, conv_weight, conv_bias, dt_bias, A_log, D, *, n_he
     if conv_state is not None and conv_state.dtype != xBC.dtype:
         conv_state = conv_state.to(xBC.dtype)
     dims = _dims(H, P, N, n_groups, d_conv, chunk_size, head_begin, head_count)
+    ws_bytes = _lib.load().alloy_ssd_combined_workspace_size(
+        Bsz, L, _lib.BF16 if xBC.dtype == torch.bfloat16 else _lib.F32, _lib.ref(dims))
+    ws = _workspace(dev, ws_bytes)
     args = [(xBC, "xBC"), (dt_raw, "dt_raw"), (_f32(conv_weight), "conv_weight"),
             (_f32(conv_bias), "conv_bias"), (_f32(dt_bias), "dt_bias"), (_f32(A_log), "A_log"),
             (_f32(D), "D"), (ssm_state, "ssm_state"), (conv_state, "conv_state"), (out, "y"),
             (ssm_state_out, "ssm_state_out"), (conv_state_out, "conv_state_out")]
     descs = [_lib.desc(t, n) for t, n in args]
     with torch.cuda.device(dev):
-        _lib.call("alloy_ssd_combined", *(_lib.ref(d) for d in descs), _lib.ref(dims),
+        _lib.call("alloy_ssd_combined", *(_lib.ref(d) for d in descs),
+                  ws.data_ptr() if ws is not None else None, ws_bytes, _lib.ref(dims),
                   _lib.stream_handle(dev))
     return out, ssm_state_out, conv_state_out
+
+
+def _workspace(dev, nbytes):
+    """Device scratch for one call, from torch's caching allocator (freed when
+    the last reference goes; the allocator orders reuse on the stream)."""
+    if nbytes == 0:
+        return None
+    return torch.empty(nbytes, dtype=torch.uint8, device=dev)
+
+
+def check_device_status(device=None):
+    """Synchronise torch's current stream and raise AlloyError if a kernel gave
+    up on a bounded device-side wait since the last check."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    with torch.cuda.device(dev):
+        _lib.call("alloy_check_device_status", _lib.stream_handle(dev))
 
 
 def selective_scan(x, A_disc, B, C, ssm_state=None, log_a=None, out=None, out_dtype=None,

@@ -23,6 +23,7 @@ this machine) on a bounded sample of the same workload.
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import json
 import math
 import os
@@ -82,11 +83,19 @@ class ClockSampler:
             pynvml.nvmlInit()
             self.nv = pynvml
             handle = None
-            try:
-                import torch
-                bus = torch.cuda.get_device_properties(torch_device).pci_bus_id
-                handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-            except Exception:
+            import torch
+            pr = torch.cuda.get_device_properties(torch_device)
+            want = (int(getattr(pr, "pci_domain_id", 0)), int(getattr(pr, "pci_bus_id", -1)),
+                    int(getattr(pr, "pci_device_id", 0)))
+            # match the CUDA device to its NVML handle by PCI location (CUDA and
+            # NVML enumerate devices differently under CUDA_VISIBLE_DEVICES)
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                hi = pynvml.nvmlDeviceGetHandleByIndex(i)
+                pci = pynvml.nvmlDeviceGetPciInfo(hi)
+                if (int(pci.domain), int(pci.bus), int(pci.device)) == want:
+                    handle = hi
+                    break
+            if handle is None:
                 handle = pynvml.nvmlDeviceGetHandleByIndex(torch_device)
             self.h = handle
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
@@ -491,6 +500,7 @@ def run_reference(args, w):
 
 
 def main():
+    faulthandler.enable()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)

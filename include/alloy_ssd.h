@@ -44,6 +44,7 @@ extern "C" {
 #define ALLOY_ERR_ALIGNMENT    -3  /* pointer/stride alignment not met          */
 #define ALLOY_ERR_CUDA         -4  /* a CUDA runtime call failed                */
 #define ALLOY_ERR_DEVICE       -5  /* no usable sm_100 device                   */
+#define ALLOY_ERR_TIMEOUT      -6  /* a bounded device-side wait ran out        */
 
 /* element types */
 #define ALLOY_F32   0
@@ -127,6 +128,8 @@ ALLOY_API int alloy_depthwise_conv1d(const alloy_tensor_t* x_padded, const alloy
  *   y          [B, L, H, P]      dtype of xBC (head/P strides free, P stride 1 for BF16)
  *   ssm_out    like ssm_in, F32 (data NULL = not written); may alias ssm_in
  *   conv_out   like conv_in (data NULL = not written); may alias conv_in
+ *   workspace  device scratch of alloy_ssd_combined_workspace_size() bytes
+ *              (may be NULL when that size is 0)
  * y = scan(dt*x) + D*x, where x is the UNSCALED conv output.
  */
 ALLOY_API int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t* dt_raw,
@@ -136,7 +139,27 @@ ALLOY_API int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t
                        const alloy_tensor_t* ssm_in, const alloy_tensor_t* conv_in,
                        alloy_tensor_t* y, alloy_tensor_t* ssm_out,
                        alloy_tensor_t* conv_out,
+                       void* workspace, size_t workspace_bytes,
                        const alloy_ssd_dims_t* dims, void* stream);
+
+/*
+ * Bytes of device workspace alloy_ssd_combined needs for a call with this
+ * batch, sequence length, activation dtype and dims (0 = none).  The
+ * workspace holds the conv + SiLU of the B and C columns (bf16), shared by
+ * all heads of a group; it must be 16-byte aligned and may be reused across
+ * calls that do not overlap on the device.  No counterpart in the reference
+ * (its kernels allocate their outputs through MLX).
+ */
+ALLOY_API size_t alloy_ssd_combined_workspace_size(int64_t batch, int64_t seqlen, int32_t dtype,
+                                                   const alloy_ssd_dims_t* dims);
+
+/*
+ * Synchronises `stream` and reports whether a kernel launched since the last
+ * check gave up on a bounded device-side wait (ALLOY_ERR_TIMEOUT, with the
+ * site in the last-error message); clears the record.  No counterpart in the
+ * reference (MLX kernels have no device-side waits).
+ */
+ALLOY_API int alloy_check_device_status(void* stream);
 
 /*
  * Selective scan on pre-discretised inputs.

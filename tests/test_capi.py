@@ -64,7 +64,8 @@ def _combined(**over):
     t.update(over)
     lib = _lib.load()
     order = ["xBC", "dt", "w", "b", "dtb", "alog", "D", "si", "ci", "y", "so", "co"]
-    st = lib.alloy_ssd_combined(*(ctypes.byref(t[k]) for k in order), ctypes.byref(dims), None)
+    st = lib.alloy_ssd_combined(*(ctypes.byref(t[k]) for k in order), None, 0,
+                                ctypes.byref(dims), None)
     return st, _lib.last_error()
 
 
