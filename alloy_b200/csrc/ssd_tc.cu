@@ -35,6 +35,11 @@
 #include "kernels.h"
 #include "tc_ptx.cuh"
 
+// Phase markers: no code unless a timing build defines ALLOY_TRACE_POINT.
+#ifndef ALLOY_TRACE_POINT
+#define ALLOY_TRACE_POINT(role, chunk, id)
+#endif
+
 namespace alloy {
 
 // error word written by a CTA whose bounded wait ran out (0 = none):
@@ -61,11 +66,12 @@ constexpr uint32_t OFF_S = 98304;                   // S_h [2][128 t][64 s] bf16
 constexpr uint32_t OFF_HX = 163840;                 // H_h / X'_h, 16 KB each
 constexpr uint32_t OFF_MISC = 196608;
 // misc: floats
-constexpr uint32_t OFF_CUM = OFF_MISC;              // [2][128]
-constexpr uint32_t OFF_DT = OFF_CUM + 1024;         // [2][128]
-constexpr uint32_t OFF_CF = OFF_DT + 1024;          // [2][128] column factors
-constexpr uint32_t OFF_WSUM = OFF_CF + 1024;        // [2][4]
-constexpr uint32_t OFF_BAR = OFF_WSUM + 64;         // mbarriers (8 bytes each)
+constexpr uint32_t OFF_CUM = OFF_MISC;              // [2 buffers][2 heads][128]
+constexpr uint32_t OFF_DT = OFF_CUM + 2048;         // [2][2][128]
+constexpr uint32_t OFF_CF = OFF_DT + 2048;          // [2][2][128] column factors
+constexpr uint32_t OFF_WSUM = OFF_CF + 2048;        // [2][4]
+constexpr uint32_t OFF_CW = OFF_WSUM + 64;          // x conv weights [2 heads][64 ch][4] + bias [2][64]
+constexpr uint32_t OFF_BAR = OFF_CW + 2560;         // mbarriers (8 bytes each)
 constexpr int NBAR = 20;
 constexpr uint32_t OFF_TMEMPTR = OFF_BAR + NBAR * 8;
 constexpr uint32_t OFF_ABORT = OFF_TMEMPTR + 8;
@@ -206,26 +212,34 @@ bc_conv_kernel(const TcArgs a, __nv_bfloat16* __restrict__ bc, int ncols) {
     for (int k = 0; k < 4; ++k) w[i][k] = a.conv_w[(int64_t)(c + i) * a.cw_sc + k * a.cw_sk];
     bias[i] = a.conv_b ? a.conv_b[(int64_t)(c + i) * a.cb_s] : 0.f;
   }
+  // all 11 row loads in flight at once (addresses clamped, rows masked below)
+  uint4 u[11];
+  const __nv_bfloat16* src = a.xbc + (int64_t)b * a.x_sb + c;
+#pragma unroll
+  for (int r = 0; r < 11; ++r) {
+    const int t = min(max(t_first - 3 + r, 0), a.L - 1);
+    u[r] = ldg_nc_v4(src + (int64_t)t * a.x_st);
+  }
   float raw[11][8];
 #pragma unroll
   for (int r = 0; r < 11; ++r) {
     const int t = t_first - 3 + r;
-    if (t >= 0 && t < a.L) {
-      const uint4 u = ldg_nc_v4(a.xbc + (int64_t)b * a.x_sb + (int64_t)t * a.x_st + c);
-      const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+    const uint32_t wd[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        raw[r][2 * i] = bf16_lo(wd[i]);
-        raw[r][2 * i + 1] = bf16_hi(wd[i]);
-      }
-    } else if (t < 0 && a.conv_in) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        raw[r][i] = __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb + (int64_t)(a.K - 1 + t) * a.ci_sk +
-                                               (int64_t)(c + i) * a.ci_sc]);
-    } else {
+    for (int i = 0; i < 4; ++i) {
+      raw[r][2 * i] = bf16_lo(wd[i]);
+      raw[r][2 * i + 1] = bf16_hi(wd[i]);
+    }
+    if (t >= a.L) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) raw[r][i] = 0.f;
+    } else if (t < 0) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        raw[r][i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
+                                                          (int64_t)(a.K - 1 + t) * a.ci_sk +
+                                                          (int64_t)(c + i) * a.ci_sc])
+                              : 0.f;
     }
   }
   __nv_bfloat16* dst = bc + ((int64_t)b * a.L + t_first) * ncols + j;
@@ -321,6 +335,7 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
         for (int k = 0; k < NK; ++k) {
           const int i = c * NK + k, slot = i & 1;
           if (i >= 2 && !wait1(bar(B_EMPTY0 + slot), ((i >> 1) - 1) & 1, abort_flag, 1)) goto tma_done;
+          ALLOY_TRACE_POINT(2, c, k);
           mbar_arrive_expect_tx(bar(B_FULL0 + slot), kStageBytes);
           const uint32_t dst = base + OFF_STAGE + slot * kStageBytes;
           tma_load_3d(dst, &bc_map, bar(B_FULL0 + slot), (gl * 2 + 0) * N + 64 * k, c * Q, b);
@@ -338,6 +353,7 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
+    // per chunk: CB -> Yi (after the state copy) -> Y (after the scores) -> state update
     if (lane == 0) {
       constexpr uint32_t ID_CB = idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t ID_YI = idesc_bf16(128, 64, 0, 0);
@@ -349,6 +365,7 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
         for (int k = 0; k < NK; ++k) {
           const int i = c * NK + k, slot = i & 1;
           if (!wait1(bar(B_FULL0 + slot), (i >> 1) & 1, abort_flag, 2)) goto mma_done;
+          ALLOY_TRACE_POINT(3, c, 5 + k);
           if (k == 0 && c > 0 && !wait1(bar(B_CB_EMPTY), pph, abort_flag, 3)) goto mma_done;
           tc_fence_after();
           const uint32_t sB = base + OFF_STAGE + slot * kStageBytes, sC = sB + 16384;
@@ -358,9 +375,10 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
                       sw128_desc(sB + 32 * kk, 16, 1024), ID_CB, (k | kk) != 0);
         }
         umma_commit(bar(B_CB_FULL));
-        // Yi_h = C H_h^T
-        if (!wait1(bar(B_HBF_READY), ph, abort_flag, 4)) goto mma_done;
+        ALLOY_TRACE_POINT(3, c, 0);
+        // Yi_h = C H_h^T (the accumulators are free once the previous epilogue read them)
         if (c > 0 && !wait1(bar(B_Y_EMPTY), pph, abort_flag, 5)) goto mma_done;
+        if (!wait1(bar(B_HBF_READY), ph, abort_flag, 4)) goto mma_done;
         tc_fence_after();
         for (int h = 0; h < 2; ++h) {
           const uint32_t sH = base + OFF_HX + h * 16384;
@@ -373,6 +391,19 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
           }
         }
         umma_commit(bar(B_YI_DONE));
+        ALLOY_TRACE_POINT(3, c, 1);
+        // Y_h = S_h X_h; x_free[h] also marks Y_h and Yi_h complete for the epilogue
+        for (int h = 0; h < 2; ++h) {
+          if (!wait1(bar(B_S_READY0 + h), ph, abort_flag, 7)) goto mma_done;
+          tc_fence_after();
+          const uint32_t sS = base + OFF_S + h * 32768, sX = base + OFF_X + h * 16384;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tmem + T_Y + 64 * h, sw128_desc(sS + (kk >> 2) * 16384 + 32 * (kk & 3), 16, 1024),
+                      sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
+          umma_commit(bar(B_X_FREE0 + h));
+        }
+        ALLOY_TRACE_POINT(3, c, 2);
         // state: ST[(h,p), n] += X'^T B over s, per N half; releases the stages
         if (!wait1(bar(B_XP_READY), ph, abort_flag, 6)) goto mma_done;
         tc_fence_after();
@@ -387,18 +418,7 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
           umma_commit(bar(B_EMPTY0 + slot));
         }
         umma_commit(bar(B_ST_DONE));
-        // Y_h = S_h X_h
-        for (int h = 0; h < 2; ++h) {
-          if (!wait1(bar(B_S_READY0 + h), ph, abort_flag, 7)) goto mma_done;
-          tc_fence_after();
-          const uint32_t sS = base + OFF_S + h * 32768, sX = base + OFF_X + h * 16384;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_bf16(tmem + T_Y + 64 * h, sw128_desc(sS + (kk >> 2) * 16384 + 32 * (kk & 3), 16, 1024),
-                      sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
-          umma_commit(bar(B_X_FREE0 + h));
-        }
-        umma_commit(bar(B_Y_FULL));
+        ALLOY_TRACE_POINT(3, c, 3);
       }
     mma_done:
       // wait (bounded) for every MMA this thread issued
@@ -411,10 +431,12 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
     }
   } else {
     // ------------------------------------------------------------ warpgroups
+    // Iteration c: scores S(c), state copy (c), X'(c), then the inputs of
+    // chunk c+1 (dt, cumsum, conv) while the tensor cores run chunk c, then
+    // the epilogue of chunk c.  cum/dt/cf are double-buffered by chunk parity.
     const int wg = warp >> 2;           // head of the pair handled by this warpgroup
     const int q = warp & 3;             // TMEM lane quadrant
     const int t = q * 32 + lane;        // row of this thread (t, s or (h,p))
-    const int tid = threadIdx.x & 127;
     const int head = h0 + wg;
     const float A = -expf(a.A_log[(int64_t)head * a.al_s]);
     const float dtb = a.dt_bias[(int64_t)head * a.dtb_s];
@@ -424,16 +446,140 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
     // state columns [wg * N/2, (wg+1) * N/2)
     const int hr = t >> 6, pr = t & 63;
 
-    // conv weights of this thread's 8 x channels
-    const int vc = tid & 7, strip = tid >> 3;
-    const int xch = head * P + vc * 8;
-    float w[8][4], cbias[8];
+    // conv weights of this head's 64 x channels -> shared memory (read per chunk)
+    float* cw_s = reinterpret_cast<float*>(smem + OFF_CW) + wg * 256;     // [64 ch][4]
+    float* cb_s = reinterpret_cast<float*>(smem + OFF_CW) + 512 + wg * 64;
+    if (t < 64) {
+      const int ch = head * P + t;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) w[i][k] = a.conv_w[(int64_t)(xch + i) * a.cw_sc + k * a.cw_sk];
-      cbias[i] = a.conv_b ? a.conv_b[(int64_t)(xch + i) * a.cb_s] : 0.f;
+      for (int k = 0; k < 4; ++k) cw_s[t * 4 + k] = a.conv_w[(int64_t)ch * a.cw_sc + k * a.cw_sk];
+      cb_s[t] = a.conv_b ? a.conv_b[(int64_t)ch * a.cb_s] : 0.f;
     }
+    // this thread's conv work: 8 channels (vector vc) x rows strip*8 .. strip*8+7
+    const int vc = t & 7, strip = t >> 3;
+    const int xch = head * P + vc * 8;
+    const __nv_bfloat16* xsrc = a.xbc + (int64_t)b * a.x_sb + xch;
+
+    // raw rows (strip*8 - 3 ... strip*8 + 7) of chunk cc: all 11 loads in
+    // flight at once (addresses clamped into the sequence, masked on use)
+    uint4 raw[11];
+    // raw dt of the next chunk for this head [0] and the pair's other head [1]
+    // (bf16 bits zero-extended; converted only when used, so the loads stay in flight)
+    uint32_t dt_bits[2] = {0u, 0u};
+    const int other = h0 + (wg ^ 1);
+    const float A_o = -expf(a.A_log[(int64_t)other * a.al_s]);
+    const float dtb_o = a.dt_bias[(int64_t)other * a.dtb_s];
+    float cum_end_other = 0.f;   // the other head's sum of A dt over the chunk being produced
+    auto load_chunk = [&](int cc) {
+      const int tb = cc * Q + strip * 8 - 3;
+#pragma unroll
+      for (int r = 0; r < 11; ++r) {
+        const int tt = min(max(tb + r, 0), L - 1);
+        raw[r] = ldg_nc_v4(xsrc + (int64_t)tt * a.x_st);
+      }
+      const int td = min(cc * Q + t, L - 1);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int64_t di = (int64_t)b * a.dt_sb + (int64_t)td * a.dt_st +
+                           (int64_t)(hh ? other : head) * a.dt_sh;
+        if (a.dt_bf16)
+          asm volatile("ld.global.nc.u16 %0, [%1];" : "=r"(dt_bits[hh])
+                       : "l"(static_cast<const __nv_bfloat16*>(a.dt) + di));
+        else
+          asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(dt_bits[hh])
+                       : "l"(static_cast<const float*>(a.dt) + di));
+      }
+    };
+    auto dt_value = [&](uint32_t bits) {
+      return a.dt_bf16 ? __uint_as_float(bits << 16) : __uint_as_float(bits);
+    };
+
+    uint32_t wg_uses = 0;
+    float* wsum_o = wsum + 8;   // [2 wg][4 warps] partial sums of the other head
+    // dt, cumsum, column factors and conv of chunk cc into buffer cc & 1
+    auto produce = [&](int cc) -> bool {
+      const int buf = cc & 1;
+      float* cm = cum_s + (buf * 2 + wg) * 128;
+      float* dtv = dt_s + (buf * 2 + wg) * 128;
+      float* cfv = cf_s + (buf * 2 + wg) * 128;
+      const int t0 = cc * Q;
+      const bool in_seq = t0 + t < L;
+      const float dt = in_seq ? softplus_f32(dt_value(dt_bits[0]) + dtb) : 0.f;
+      float v = A * dt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      // column factor exp(cum[end of the 32-block] - cum[t]) dt[t] needs only this warp's scan
+      cfv[t] = ex2_approx((__shfl_sync(0xffffffffu, v, 31) - v) * kLog2e) * dt;
+      float vo = in_seq ? A_o * softplus_f32(dt_value(dt_bits[1]) + dtb_o) : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) vo += __shfl_xor_sync(0xffffffffu, vo, o);
+      if (lane == 31) wsum[wg * 4 + q] = v;
+      if (lane == 0) wsum_o[wg * 4 + q] = vo;
+      ALLOY_TRACE_POINT(wg, cc - 1, 10);
+      // conv + SiLU of this head's x channels -> X_h (bf16, unscaled)
+      {
+        float xr[11][8];
+        const int tb = t0 + strip * 8 - 3;
+#pragma unroll
+        for (int r = 0; r < 11; ++r) {
+          const int tt = tb + r;
+          const uint32_t wd[4] = {raw[r].x, raw[r].y, raw[r].z, raw[r].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            xr[r][2 * i] = bf16_lo(wd[i]);
+            xr[r][2 * i + 1] = bf16_hi(wd[i]);
+          }
+          if (tt >= L) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xr[r][i] = 0.f;
+          } else if (tt < 0) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              xr[r][i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
+                                                               (int64_t)(a.K - 1 + tt) * a.ci_sk +
+                                                               (int64_t)(xch + i) * a.ci_sc])
+                                   : 0.f;
+          }
+        }
+        ALLOY_TRACE_POINT(wg, cc - 1, 11);
+        const uint32_t sX = base + OFF_X + wg * 16384;
+        float y8[8][8];
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const float4 wv = reinterpret_cast<const float4*>(cw_s)[vc * 8 + ch];
+          const float bv = cb_s[vc * 8 + ch];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            float acc = bv;
+            acc = fmaf(xr[r][ch], wv.x, acc);
+            acc = fmaf(xr[r + 1][ch], wv.y, acc);
+            acc = fmaf(xr[r + 2][ch], wv.z, acc);
+            acc = fmaf(xr[r + 3][ch], wv.w, acc);
+            y8[r][ch] = (t0 + strip * 8 + r < L) ? silu_fast(acc) : 0.f;
+          }
+        }
+        ALLOY_TRACE_POINT(wg, cc - 1, 12);
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+          st_shared_v4(sX + sw_off(strip * 8 + r, vc), pack_bf16x2(y8[r][0], y8[r][1]),
+                       pack_bf16x2(y8[r][2], y8[r][3]), pack_bf16x2(y8[r][4], y8[r][5]),
+                       pack_bf16x2(y8[r][6], y8[r][7]));
+      }
+      ALLOY_TRACE_POINT(wg, cc - 1, 13);
+      fence_async_smem();
+      if (!warps_sync(bar(B_WG0 + wg), wg_uses, abort_flag, 16)) return false;
+      ALLOY_TRACE_POINT(wg, cc - 1, 14);
+      for (int i = 0; i < q; ++i) v += wsum[wg * 4 + i];
+      cum_end_other = wsum_o[wg * 4 + 0] + wsum_o[wg * 4 + 1] + wsum_o[wg * 4 + 2] +
+                      wsum_o[wg * 4 + 3];
+      cm[t] = v;
+      dtv[t] = dt;
+      // cum / dt visible to the whole warpgroup
+      return warps_sync(bar(B_WG0 + wg), wg_uses, abort_flag, 17);
+    };
 
     // initial state -> TMEM
     for (int cc = 0; cc < NHALF / 32; ++cc) {
@@ -450,92 +596,24 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
     }
     tmem_st_wait();
 
-    uint32_t wg_uses = 0, x_uses = 0;
-    for (int c = 0; c < nchunks; ++c) {
+    load_chunk(0);
+    // conv weights in shared memory are visible to the whole warpgroup
+    bool ok = warps_sync(bar(B_WG0 + wg), wg_uses, abort_flag, 19) && produce(0);
+    for (int c = 0; ok && c < nchunks; ++c) {
       const uint32_t ph = c & 1, pph = (c - 1) & 1;
-      const int t0 = c * Q;
-      if (c > 0 && !waitw(bar(B_X_FREE0 + wg), pph, abort_flag, 10)) break;
-      // ---- dt, cumulative log decay (this head) ----
-      {
-        const int tt = t0 + tid;
-        float dt = 0.f;
-        if (tt < L) {
-          const float raw = load_any(a.dt, (int64_t)b * a.dt_sb + (int64_t)tt * a.dt_st +
-                                               (int64_t)head * a.dt_sh, a.dt_bf16);
-          dt = softplus_f32(raw + dtb);
-        }
-        float v = A * dt;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float u = __shfl_up_sync(0xffffffffu, v, o);
-          if (lane >= o) v += u;
-        }
-        if (lane == 31) wsum[wg * 4 + q] = v;
-        if (!warps_sync(bar(B_WG0 + wg), wg_uses, abort_flag, 16)) break;
-        for (int i = 0; i < q; ++i) v += wsum[wg * 4 + i];
-        cum_s[wg * 128 + tid] = v;
-        dt_s[wg * 128 + tid] = dt;
-      }
-      // ---- conv + SiLU of this head's x channels -> X_h (bf16, unscaled) ----
-      {
-        float raw[11][8];
-#pragma unroll
-        for (int r = 0; r < 11; ++r) {
-          const int tt = t0 + strip * 8 - 3 + r;
-          if (tt >= 0 && tt < L) {
-            const uint4 u = ldg_nc_v4(a.xbc + (int64_t)b * a.x_sb + (int64_t)tt * a.x_st + xch);
-            const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              raw[r][2 * i] = bf16_lo(wd[i]);
-              raw[r][2 * i + 1] = bf16_hi(wd[i]);
-            }
-          } else if (tt < 0 && a.conv_in) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              raw[r][i] = __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
-                                                     (int64_t)(a.K - 1 + tt) * a.ci_sk +
-                                                     (int64_t)(xch + i) * a.ci_sc]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) raw[r][i] = 0.f;
-          }
-        }
-        const uint32_t sX = base + OFF_X + wg * 16384;
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const int s = strip * 8 + r;
-          uint32_t o[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float f[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int ch = 2 * i + e;
-              float acc = cbias[ch];
-#pragma unroll
-              for (int k = 0; k < 4; ++k) acc = fmaf(raw[r + k][ch], w[ch][k], acc);
-              f[e] = (t0 + s < L) ? silu_fast(acc) : 0.f;
-            }
-            o[i] = pack_bf16x2(f[0], f[1]);
-          }
-          st_shared_v4(sX + sw_off(s, vc), o[0], o[1], o[2], o[3]);
-        }
-      }
-      if (!warps_sync(bar(B_WG0 + wg), wg_uses, abort_flag, 17)) break;
-      // ---- column factors cf[s] = exp(cum[end of s's 32-block] - cum[s]) dt[s] ----
-      {
-        const float* cm = cum_s + wg * 128;
-        cf_s[wg * 128 + tid] = ex2_approx((cm[(tid | 31)] - cm[tid]) * kLog2e) * dt_s[wg * 128 + tid];
-      }
-      fence_async_smem();
-      // both heads' cum / dt / cf visible
-      if (!warps_sync(bar(B_XWG), x_uses, abort_flag, 18)) break;
+      const int buf = c & 1;
+      const float* cm = cum_s + (buf * 2 + wg) * 128;
+      const float* dtv = dt_s + (buf * 2 + wg) * 128;
+      const float* cfv = cf_s + (buf * 2 + wg) * 128;
+      const bool more = c + 1 < nchunks;
+      if (more) load_chunk(c + 1);
+      ALLOY_TRACE_POINT(wg, c, 0);
       // ---- state: H = bf16(state) -> HX_hr; state *= exp(cum[Q-1]) ----
       if (c > 0 && !waitw(bar(B_ST_DONE), pph, abort_flag, 11)) break;
+      ALLOY_TRACE_POINT(wg, c, 3);
       tc_fence_after();
       {
-        const float e_end = ex2_approx(cum_s[hr * 128 + 127] * kLog2e);
+        const float e_end = ex2_approx((hr == wg ? cm[127] : cum_end_other) * kLog2e);
         const uint32_t sH = base + OFF_HX + hr * 16384;
 #pragma unroll
         for (int cc = 0; cc < NHALF / 32; ++cc) {
@@ -562,29 +640,34 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_HBF_READY));
+      ALLOY_TRACE_POINT(wg, c, 4);
       // ---- scores S_h = CB * decay * dt (+ D on the diagonal) ----
       if (!waitw(bar(B_CB_FULL), ph, abort_flag, 12)) break;
+      ALLOY_TRACE_POINT(wg, c, 1);
       tc_fence_after();
       {
-        const float* cm = cum_s + wg * 128;
-        const float* dtv = dt_s + wg * 128;
-        const float* cfv = cf_s + wg * 128;
         const float cum_t = cm[t];
         const uint32_t sS = base + OFF_S + wg * 32768;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          float f[32];
+          uint32_t r[32];   // CB row segment, overwritten in place by the scores
           if (j > q) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) f[i] = 0.f;
+            for (int i = 0; i < 32; ++i) r[i] = 0u;
           } else {
-            uint32_t r[32];
             tmem_ld32(lane_base + T_CB + 32 * j, r);
             tmem_ld_wait();
             if (j < q) {
               const float R = ex2_approx((cum_t - cm[32 * j + 31]) * kLog2e);
+              const float4* cf4 = reinterpret_cast<const float4*>(cfv + 32 * j);
 #pragma unroll
-              for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(r[i]) * R * cfv[32 * j + i];
+              for (int i4 = 0; i4 < 8; ++i4) {
+                const float4 f = cf4[i4];
+                r[4 * i4 + 0] = __float_as_uint(__uint_as_float(r[4 * i4 + 0]) * R * f.x);
+                r[4 * i4 + 1] = __float_as_uint(__uint_as_float(r[4 * i4 + 1]) * R * f.y);
+                r[4 * i4 + 2] = __float_as_uint(__uint_as_float(r[4 * i4 + 2]) * R * f.z);
+                r[4 * i4 + 3] = __float_as_uint(__uint_as_float(r[4 * i4 + 3]) * R * f.w);
+              }
             } else {
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
@@ -592,19 +675,17 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
                 float v = 0.f;
                 if (s <= t) v = __uint_as_float(r[i]) * ex2_approx((cum_t - cm[s]) * kLog2e) * dtv[s];
                 if (s == t) v += Dh;
-                f[i] = v;
+                r[i] = __float_as_uint(v);
               }
             }
           }
-          // 32 columns = 4 chunks of 8 in the (j/2)-th 64-column block
 #pragma unroll
           for (int g4 = 0; g4 < 4; ++g4) {
             const int chunk = (j & 1) * 4 + g4;
-            st_shared_v4(sS + (j >> 1) * 16384 + sw_off(t, chunk),
-                         pack_bf16x2(f[g4 * 8 + 0], f[g4 * 8 + 1]),
-                         pack_bf16x2(f[g4 * 8 + 2], f[g4 * 8 + 3]),
-                         pack_bf16x2(f[g4 * 8 + 4], f[g4 * 8 + 5]),
-                         pack_bf16x2(f[g4 * 8 + 6], f[g4 * 8 + 7]));
+            const float* f = reinterpret_cast<const float*>(r) + g4 * 8;
+            st_shared_v4(sS + (j >> 1) * 16384 + sw_off(t, chunk), pack_bf16x2(f[0], f[1]),
+                         pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                         pack_bf16x2(f[6], f[7]));
           }
         }
       }
@@ -615,11 +696,12 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
         mbar_arrive(bar(B_CB_EMPTY));
         mbar_arrive(bar(B_S_READY0 + wg));
       }
+      ALLOY_TRACE_POINT(wg, c, 2);
       // ---- X'_h = X_h * dt * exp(cum[Q-1] - cum[s]) -> HX_h ----
       if (!waitw(bar(B_YI_DONE), ph, abort_flag, 13)) break;
+      ALLOY_TRACE_POINT(wg, c, 5);
       {
-        const float* cm = cum_s + wg * 128;
-        const float e = dt_s[wg * 128 + t] * ex2_approx((cm[127] - cm[t]) * kLog2e);
+        const float e = dtv[t] * ex2_approx((cm[127] - cm[t]) * kLog2e);
         const uint32_t sX = base + OFF_X + wg * 16384, sXp = base + OFF_HX + wg * 16384;
 #pragma unroll
         for (int ch = 0; ch < 8; ++ch) {
@@ -634,38 +716,56 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_XP_READY));
+      ALLOY_TRACE_POINT(wg, c, 6);
+      // ---- inputs of the next chunk (X_h is free once Y(c) has read it) ----
+      if (more) {
+        if (!waitw(bar(B_X_FREE0 + wg), ph, abort_flag, 10)) break;
+        ALLOY_TRACE_POINT(wg, c, 7);
+        if (!produce(c + 1)) break;
+      }
+      ALLOY_TRACE_POINT(wg, c, 8);
       // ---- epilogue: y = Y + exp(cum[t]) Yi -> global (bf16) ----
-      if (!waitw(bar(B_Y_FULL), ph, abort_flag, 14)) break;
+      // Each warp stages its 32 rows in its own rows of S_h (free: Y(c) has
+      // read it), then stores 4 full 128-byte rows per instruction.
+      if (!more && !waitw(bar(B_X_FREE0 + wg), ph, abort_flag, 14)) break;
       tc_fence_after();
       {
-        const float e = ex2_approx(cum_s[wg * 128 + t] * kLog2e);
-        const bool valid = t0 + t < L;
-        __nv_bfloat16* yrow = a.y + (int64_t)b * a.y_sb + (int64_t)(t0 + t) * a.y_st +
-                              (int64_t)head * a.y_sh;
+        const int t0 = c * Q;
+        const float e = ex2_approx(cm[t] * kLog2e);
+        const uint32_t stage = base + OFF_S + wg * 32768 + q * 4096;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t ry[32], ri[32];
           tmem_ld32(lane_base + T_Y + 64 * wg + 32 * half, ry);
           tmem_ld32(lane_base + T_YI + 64 * wg + 32 * half, ri);
           tmem_ld_wait();
-          if (valid) {
 #pragma unroll
-            for (int g4 = 0; g4 < 4; ++g4) {
-              uint32_t o[4];
+          for (int g4 = 0; g4 < 4; ++g4) {
+            uint32_t o[4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int k0 = g4 * 8 + 2 * i;
-                o[i] = pack_bf16x2(fmaf(e, __uint_as_float(ri[k0]), __uint_as_float(ry[k0])),
-                                   fmaf(e, __uint_as_float(ri[k0 + 1]), __uint_as_float(ry[k0 + 1])));
-              }
-              *reinterpret_cast<uint4*>(yrow + half * 32 + g4 * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+            for (int i = 0; i < 4; ++i) {
+              const int k0 = g4 * 8 + 2 * i;
+              o[i] = pack_bf16x2(fmaf(e, __uint_as_float(ri[k0]), __uint_as_float(ry[k0])),
+                                 fmaf(e, __uint_as_float(ri[k0 + 1]), __uint_as_float(ry[k0 + 1])));
             }
+            st_shared_v4(stage + sw_off(lane, half * 4 + g4), o[0], o[1], o[2], o[3]);
           }
         }
+        __syncwarp();
+        __nv_bfloat16* ybase = a.y + (int64_t)b * a.y_sb + (int64_t)head * a.y_sh + (lane & 7) * 8;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int row = 4 * k + (lane >> 3);
+          const uint4 v = ld_shared_v4(stage + sw_off(row, lane & 7));
+          const int tt = t0 + q * 32 + row;
+          if (tt < L) *reinterpret_cast<uint4*>(ybase + (int64_t)tt * a.y_st) = v;
+        }
+        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_Y_EMPTY));
+      ALLOY_TRACE_POINT(wg, c, 9);
     }
     // ---- final state -> ssm_out ----
     if (!*abort_flag && a.ssm_out && waitw(bar(B_ST_DONE), (nchunks - 1) & 1, abort_flag, 15)) {

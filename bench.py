@@ -48,6 +48,8 @@ WORKLOADS = {
 }
 
 L2_BYTES = 126 * 1024 * 1024
+# kernels one prefill step launches: B/C conv pre-pass, SSD, conv-cache roll
+LAUNCHES_PER_STEP = 3
 FALLBACK_HBM_GBS = 6650.0
 
 # DRAM bytes per launch of the dominant kernel measured with ncu (read + write),
@@ -278,7 +280,47 @@ def run_ours(args, w):
     traffic = NCU_TRAFFIC_BYTES.get((args.workload, world))
 
     # ---- end to end through the public API, host buffers ----
-    inp, out = sets[0]
+    e2e = None if args.no_e2e else run_e2e(args, sets[0], kw, world, stream, B * L)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_sample(w, budget_s=20.0)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": w["name"], "batch": B, "seq_len": L, "n_heads": w["H"],
+                       "head_dim": P, "d_state": N, "n_groups": w["G"], "d_conv": K,
+                       "chunk_size": Q, "state_dtype": "f32",
+                       "shard": f"{H_l} heads / {G_l} groups per GPU",
+                       "l2": f"inputs larger than L2: {rot} rotating input/output sets, "
+                             f"{step_bytes * rot / 2**20:.0f} MiB touched per rotation"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{peak_kind} hbm_gbs",
+                         "kernel_ms": kernel_ms, "algorithmic_bytes_per_gpu": alg},
+            "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+            "clocks": clocks.summary(h0, h1),
+        }
+        if e2e is not None:
+            line["e2e"] = e2e
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_e2e(args, set0, kw, world, stream, tokens):
+    """The same step through the public API with host buffers: H2D of the
+    step's activations from pinned memory, the call, D2H of y and the state."""
+    import torch
+    from alloy_b200 import mixer
+    inp, out = set0
     host_in = {k: torch.empty(inp[k].shape, dtype=inp[k].dtype, pin_memory=True)
                for k in ("xBC", "dt_raw")}
     for k in host_in:
@@ -312,39 +354,9 @@ def run_ours(args, w):
     e2e_ms = dist_max(e0.elapsed_time(e1) / e2e_steps, world)
     h2d = sum(t.numel() * t.element_size() for t in host_in.values())
     d2h = host_y.numel() * host_y.element_size() + host_h.numel() * host_h.element_size()
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_sample(w, budget_s=20.0)
-
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": w["name"], "batch": B, "seq_len": L, "n_heads": w["H"],
-                       "head_dim": P, "d_state": N, "n_groups": w["G"], "d_conv": K,
-                       "chunk_size": Q, "state_dtype": "f32",
-                       "shard": f"{H_l} heads / {G_l} groups per GPU",
-                       "l2": f"inputs larger than L2: {rot} rotating input/output sets, "
-                             f"{step_bytes * rot / 2**20:.0f} MiB touched per rotation"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": f"{peak_kind} hbm_gbs",
-                         "kernel_ms": kernel_ms, "algorithmic_bytes_per_gpu": alg},
-            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
-                    "ms_per_step": e2e_ms, "steps": e2e_steps},
-            "gpu_launches": 2 * args.steps,
-            "clocks": clocks.summary(h0, h1),
-        }
-        if cpu is not None:
-            line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    return {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+            "ms_per_step": e2e_ms, "steps": e2e_steps}
 
 
 def run_decode(args, w):
@@ -508,10 +520,21 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="nemotron")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the workload's batch (smaller cases for profiling)")
+    ap.add_argument("--seqlen", type=int, default=None,
+                    help="override the workload's sequence length")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.batch is not None:
+        w["B"] = args.batch
+    if args.seqlen is not None:
+        w["L"] = args.seqlen
+    if args.batch is not None or args.seqlen is not None:
+        w["name"] += f"_b{w['B']}_l{w['L']}"
     if args.impl == "reference":
         run_reference(args, w)
     elif args.workload == "decode":
