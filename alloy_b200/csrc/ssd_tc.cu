@@ -52,41 +52,54 @@ using namespace tc;
 
 constexpr int Q = 128;                 // chunk length (UMMA M)
 constexpr int P = 64;                  // head dim
-constexpr int kThreads = 320;
-constexpr int kMmaWarp = 9;
-constexpr int kTmaWarp = 8;
+constexpr int kThreads = 576;          // 18 warps
+constexpr int kTmaWarp = 16;
+constexpr int kMmaWarp = 17;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 // shared-memory map (bytes from the 1024-aligned base)
 constexpr uint32_t kStageBytes = 32768;             // B half [128][64] + C half [128][64] bf16
 constexpr uint32_t OFF_STAGE = 0;                   // 2 stages
-constexpr uint32_t OFF_X = 65536;                   // X_h [128 s][64 p] bf16, 16 KB each
-constexpr uint32_t OFF_S = 98304;                   // S_h [2][128 t][64 s] bf16, 32 KB each
-constexpr uint32_t OFF_HX = 163840;                 // H_h / X'_h, 16 KB each
-constexpr uint32_t OFF_MISC = 196608;
-// misc: floats
-constexpr uint32_t OFF_CUM = OFF_MISC;              // [2 buffers][2 heads][128]
+constexpr uint32_t OFF_X = 65536;                   // X [2 buffers][2 heads][128 s][64 p] bf16
+constexpr uint32_t OFF_HX = 131072;                 // H_h / X'_h [2 heads], 16 KB each
+constexpr uint32_t OFF_RAW = 163840;                // raw x rows [2 heads][131][64] bf16
+constexpr uint32_t kRawRows = Q + 3;
+constexpr uint32_t kRawBytes = kRawRows * 128;      // 16768 per head
+constexpr uint32_t kRawStride = 17408;              // 1024-aligned per-head stride
+constexpr uint32_t OFF_MISC = OFF_RAW + 2 * kRawStride;
+constexpr uint32_t OFF_CUM = OFF_MISC;              // [2 buffers][2 heads][128] f32
 constexpr uint32_t OFF_DT = OFF_CUM + 2048;         // [2][2][128]
 constexpr uint32_t OFF_CF = OFF_DT + 2048;          // [2][2][128] column factors
-constexpr uint32_t OFF_WSUM = OFF_CF + 2048;        // [2][4]
-constexpr uint32_t OFF_CW = OFF_WSUM + 64;          // x conv weights [2 heads][64 ch][4] + bias [2][64]
+constexpr uint32_t OFF_WSUM = OFF_CF + 2048;        // [2 buffers][2 heads][4 warps]
+constexpr uint32_t OFF_CW = OFF_WSUM + 64;          // x conv weights [2][64][4] + bias [2][64]
 constexpr uint32_t OFF_BAR = OFF_CW + 2560;         // mbarriers (8 bytes each)
-constexpr int NBAR = 20;
+constexpr int NBAR = 24;
 constexpr uint32_t OFF_TMEMPTR = OFF_BAR + NBAR * 8;
 constexpr uint32_t OFF_ABORT = OFF_TMEMPTR + 8;
 constexpr uint32_t kSmemBytes = OFF_ABORT + 16 + 1024;  // + alignment slack
 
-// barrier ids
+// barrier ids (counts in the kernel's init table)
 enum {
-  B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1, B_CB_FULL, B_CB_EMPTY, B_HBF_READY, B_YI_DONE,
-  B_XP_READY, B_ST_DONE, B_S_READY0, B_S_READY1, B_X_FREE0, B_X_FREE1, B_Y_FULL, B_Y_EMPTY,
-  B_DRAIN, B_WG0, B_WG1, B_XWG
+  B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1,   // B/C half-tile ring (TMA <-> MMA)
+  B_RAW_FULL,                                 // TMA -> producers: raw x rows of a chunk
+  B_RAW_EMPTY,                                // producers -> TMA (8 warps)
+  B_X_READY0, B_X_READY1,                     // producers -> consumers: X, cum, dt, cf (per buffer)
+  B_CB_FULL,                                  // MMA -> consumers: CB in TMEM
+  B_HBF_READY,                                // consumers -> MMA: H copies written, state scaled
+  B_YI_DONE,                                  // MMA -> consumers: Yi done (H buffer reusable)
+  B_S_READY,                                  // consumers -> MMA: scores in TMEM
+  B_Y_FULL,                                   // MMA -> consumers: Y and Yi complete
+  B_XP_READY,                                 // consumers -> MMA: X' written
+  B_ST_DONE,                                  // MMA -> consumers: state update done
+  B_Y_EMPTY0, B_Y_EMPTY1,                     // consumers -> producers/MMA: y read out (per buffer)
+  B_PWG0, B_PWG1, B_CWG0, B_CWG1,             // per-warpgroup syncs
+  B_DRAIN
 };
 
 // TMEM columns
-constexpr uint32_t T_CB = 0;      // [128 t][128 s] fp32
-constexpr uint32_t T_ST = 128;    // [128 (h,p)][N] fp32
+constexpr uint32_t T_CB = 0;      // CB [128 t][128 s] f32, overwritten in place by the scores
+constexpr uint32_t T_ST = 128;    // state [128 (h,p)][N] f32
 constexpr uint32_t T_Y = 256;     // + 64 h
 constexpr uint32_t T_YI = 384;    // + 64 h
 
@@ -267,20 +280,35 @@ bc_conv_kernel(const TcArgs a, __nv_bfloat16* __restrict__ bc, int ncols) {
 // ----------------------------------------------------------------------------
 // the SSD kernel
 // ----------------------------------------------------------------------------
+// Roles (18 warps):
+//   warps 0-7   consumers: warpgroup cw = 0/1.  Per chunk: copy of the state to
+//               bf16 (H) and its decay (state columns split by warpgroup), the
+//               scores S of both heads for the 32-column blocks j = cw, cw + 2
+//               written in place over CB in tensor memory, X' of head cw, and
+//               the epilogue of head cw.
+//   warps 8-15  producers: warpgroup ph = 0/1 for head ph of the pair.  Per
+//               chunk: dt, cumulative log decay and column factors, and the
+//               conv + SiLU of the head's x channels from the TMA-staged raw
+//               rows into the double-buffered X.  They run up to one chunk
+//               ahead of the consumers.
+//   warp 16     TMA: lane 0 loads the raw x rows, lane 1 the B/C half tiles.
+//   warp 17     TMEM allocation and the MMA issue (one thread).
 template <int N>
 __global__ void __launch_bounds__(kThreads, 1)
-ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
+ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant__ CUtensorMap x_map,
+              const TcArgs a) {
   constexpr int NK = N / 64;            // 64-column halves of B/C per chunk
-  constexpr int NHALF = N / 2;          // state columns per warpgroup
+  constexpr int NHALF = N / 2;          // state columns per consumer warpgroup
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_base);
 
-  float* cum_s = reinterpret_cast<float*>(smem + OFF_CUM);
+  float* cum_s = reinterpret_cast<float*>(smem + OFF_CUM);   // [buf][head][128]
   float* dt_s = reinterpret_cast<float*>(smem + OFF_DT);
   float* cf_s = reinterpret_cast<float*>(smem + OFF_CF);
   float* wsum = reinterpret_cast<float*>(smem + OFF_WSUM);
+  float* cw_all = reinterpret_cast<float*>(smem + OFF_CW);   // [2][64][4], then bias [2][64]
   volatile uint32_t* tmem_ptr = reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEMPTR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_ABORT);
   auto bar = [&](int i) { return base + OFF_BAR + 8u * i; };
@@ -295,46 +323,61 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    mbar_init(bar(B_FULL0), 1);
-    mbar_init(bar(B_FULL1), 1);
-    mbar_init(bar(B_EMPTY0), 1);
-    mbar_init(bar(B_EMPTY1), 1);
-    mbar_init(bar(B_CB_FULL), 1);
-    mbar_init(bar(B_CB_EMPTY), 8);
-    mbar_init(bar(B_HBF_READY), 8);
-    mbar_init(bar(B_YI_DONE), 1);
-    mbar_init(bar(B_XP_READY), 8);
-    mbar_init(bar(B_ST_DONE), 1);
-    mbar_init(bar(B_S_READY0), 4);
-    mbar_init(bar(B_S_READY1), 4);
-    mbar_init(bar(B_X_FREE0), 1);
-    mbar_init(bar(B_X_FREE1), 1);
-    mbar_init(bar(B_Y_FULL), 1);
-    mbar_init(bar(B_Y_EMPTY), 8);
-    mbar_init(bar(B_DRAIN), 1);
-    mbar_init(bar(B_WG0), 4);
-    mbar_init(bar(B_WG1), 4);
-    mbar_init(bar(B_XWG), 8);
+    const int counts[NBAR] = {1, 1, 1, 1, 1, 8, 8, 8, 1, 8, 1, 8, 1, 8, 1, 8, 8, 4, 4, 4, 4, 1, 0, 0};
+    for (int i = 0; i < NBAR; ++i)
+      if (counts[i]) mbar_init(bar(i), counts[i]);
     mbar_fence_init();
   }
   if (warp == kMmaWarp) {
     tmem_alloc(base + OFF_TMEMPTR, 512);
     tmem_relinquish();
   }
-  if (warp == kTmaWarp && lane == 0) prefetch_tmap(&bc_map);
+  if (warp == kTmaWarp && lane == 0) {
+    prefetch_tmap(&bc_map);
+    prefetch_tmap(&x_map);
+  }
+  // x conv weights of both heads (producers read them per output row), laid
+  // out [head][channel within vector][vector][tap] so that the 8 vectors a
+  // warp reads at once are contiguous (no bank conflicts)
+  if (threadIdx.x < 128) {
+    const int hh = threadIdx.x >> 6, ch = threadIdx.x & 63;
+    const int vec = ch >> 3, e = ch & 7;
+    const int64_t c = (int64_t)(h0 + hh) * P + ch;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      cw_all[hh * 256 + (e * 8 + vec) * 4 + k] = a.conv_w[c * a.cw_sc + k * a.cw_sk];
+    cw_all[512 + hh * 64 + e * 8 + vec] = a.conv_b ? a.conv_b[c * a.cb_s] : 0.f;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_ptr;
 
   if (warp == kTmaWarp) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA
     if (lane == 0) {
+      // raw x rows [c*Q - 3, c*Q + Q) of both heads' channels (rows outside
+      // [0, L) arrive as zeros)
+      int issued = 0;
+      for (int c = 0; c < nchunks; ++c) {
+        if (c > 0 && !wait1(bar(B_RAW_EMPTY), (c - 1) & 1, abort_flag, 1)) break;
+        mbar_arrive_expect_tx(bar(B_RAW_FULL), 2 * kRawBytes);
+        tma_load_3d(base + OFF_RAW, &x_map, bar(B_RAW_FULL), h0 * P, c * Q - 3, b);
+        tma_load_3d(base + OFF_RAW + kRawStride, &x_map, bar(B_RAW_FULL), (h0 + 1) * P, c * Q - 3, b);
+        ++issued;
+      }
+      if (issued > 0) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(bar(B_RAW_FULL), (issued - 1) & 1) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    } else if (lane == 1) {
+      // B/C half tiles into the two-stage ring
       int issued = 0;
       for (int c = 0; c < nchunks; ++c) {
         for (int k = 0; k < NK; ++k) {
           const int i = c * NK + k, slot = i & 1;
-          if (i >= 2 && !wait1(bar(B_EMPTY0 + slot), ((i >> 1) - 1) & 1, abort_flag, 1)) goto tma_done;
+          if (i >= 2 && !wait1(bar(B_EMPTY0 + slot), ((i >> 1) - 1) & 1, abort_flag, 2)) goto bc_done;
           ALLOY_TRACE_POINT(2, c, k);
           mbar_arrive_expect_tx(bar(B_FULL0 + slot), kStageBytes);
           const uint32_t dst = base + OFF_STAGE + slot * kStageBytes;
@@ -343,8 +386,7 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
           ++issued;
         }
       }
-    tma_done:
-      // the copies of the last two fills must land before the CTA exits
+    bc_done:
       for (int i = max(0, issued - 2); i < issued; ++i) {
         const long long t0 = clock64();
         while (!mbar_try_wait(bar(B_FULL0 + (i & 1)), (i >> 1) & 1) && clock64() - t0 < kWaitCycles) {
@@ -353,7 +395,7 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    // per chunk: CB -> Yi (after the state copy) -> Y (after the scores) -> state update
+    // per chunk: CB -> Yi (after the state copy) -> Y (scores from TMEM) -> state update
     if (lane == 0) {
       constexpr uint32_t ID_CB = idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t ID_YI = idesc_bf16(128, 64, 0, 0);
@@ -361,12 +403,14 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
       constexpr uint32_t ID_Y = idesc_bf16(128, 64, 0, 1);
       for (int c = 0; c < nchunks; ++c) {
         const uint32_t ph = c & 1, pph = (c - 1) & 1;
-        // CB = C B^T over the N halves
+        const int buf = c & 1;
+        // CB = C B^T over the N halves; the region held the previous scores,
+        // so Y(c-1) must have completed
         for (int k = 0; k < NK; ++k) {
           const int i = c * NK + k, slot = i & 1;
-          if (!wait1(bar(B_FULL0 + slot), (i >> 1) & 1, abort_flag, 2)) goto mma_done;
+          if (!wait1(bar(B_FULL0 + slot), (i >> 1) & 1, abort_flag, 3)) goto mma_done;
           ALLOY_TRACE_POINT(3, c, 5 + k);
-          if (k == 0 && c > 0 && !wait1(bar(B_CB_EMPTY), pph, abort_flag, 3)) goto mma_done;
+          if (k == 0 && c > 0 && !wait1(bar(B_Y_FULL), pph, abort_flag, 4)) goto mma_done;
           tc_fence_after();
           const uint32_t sB = base + OFF_STAGE + slot * kStageBytes, sC = sB + 16384;
 #pragma unroll
@@ -376,9 +420,9 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
         }
         umma_commit(bar(B_CB_FULL));
         ALLOY_TRACE_POINT(3, c, 0);
-        // Yi_h = C H_h^T (the accumulators are free once the previous epilogue read them)
-        if (c > 0 && !wait1(bar(B_Y_EMPTY), pph, abort_flag, 5)) goto mma_done;
-        if (!wait1(bar(B_HBF_READY), ph, abort_flag, 4)) goto mma_done;
+        // Yi_h = C H_h^T
+        if (c > 0 && !wait1(bar(B_Y_EMPTY0 + (buf ^ 1)), ((c - 1) >> 1) & 1, abort_flag, 5)) goto mma_done;
+        if (!wait1(bar(B_HBF_READY), ph, abort_flag, 6)) goto mma_done;
         tc_fence_after();
         for (int h = 0; h < 2; ++h) {
           const uint32_t sH = base + OFF_HX + h * 16384;
@@ -392,28 +436,28 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
         }
         umma_commit(bar(B_YI_DONE));
         ALLOY_TRACE_POINT(3, c, 1);
-        // Y_h = S_h X_h; x_free[h] also marks Y_h and Yi_h complete for the epilogue
+        // Y_h = S_h X_h, S_h (bf16 pairs) read from tensor memory
+        if (!wait1(bar(B_S_READY), ph, abort_flag, 7)) goto mma_done;
+        tc_fence_after();
         for (int h = 0; h < 2; ++h) {
-          if (!wait1(bar(B_S_READY0 + h), ph, abort_flag, 7)) goto mma_done;
-          tc_fence_after();
-          const uint32_t sS = base + OFF_S + h * 32768, sX = base + OFF_X + h * 16384;
+          const uint32_t sX = base + OFF_X + (buf * 2 + h) * 16384;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_bf16(tmem + T_Y + 64 * h, sw128_desc(sS + (kk >> 2) * 16384 + 32 * (kk & 3), 16, 1024),
-                      sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
-          umma_commit(bar(B_X_FREE0 + h));
+            umma_bf16_ta(tmem + T_Y + 64 * h, tmem + T_CB + 32 * (kk >> 1) + 16 * h + 8 * (kk & 1),
+                         sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
         }
+        umma_commit(bar(B_Y_FULL));
         ALLOY_TRACE_POINT(3, c, 2);
         // state: ST[(h,p), n] += X'^T B over s, per N half; releases the stages
-        if (!wait1(bar(B_XP_READY), ph, abort_flag, 6)) goto mma_done;
+        if (!wait1(bar(B_XP_READY), ph, abort_flag, 8)) goto mma_done;
         tc_fence_after();
         for (int k = 0; k < NK; ++k) {
           const int slot = (c * NK + k) & 1;
           const uint32_t sB = base + OFF_STAGE + slot * kStageBytes;
-          const uint32_t sX = base + OFF_HX;
+          const uint32_t sXp = base + OFF_HX;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_bf16(tmem + T_ST + 64 * k, sw128_desc(sX + 2048 * kk, 16384, 1024),
+            umma_bf16(tmem + T_ST + 64 * k, sw128_desc(sXp + 2048 * kk, 16384, 1024),
                       sw128_desc(sB + 2048 * kk, 16384, 1024), ID_ST, 1);
           umma_commit(bar(B_EMPTY0 + slot));
         }
@@ -429,206 +473,170 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
         }
       }
     }
-  } else {
-    // ------------------------------------------------------------ warpgroups
-    // Iteration c: scores S(c), state copy (c), X'(c), then the inputs of
-    // chunk c+1 (dt, cumsum, conv) while the tensor cores run chunk c, then
-    // the epilogue of chunk c.  cum/dt/cf are double-buffered by chunk parity.
-    const int wg = warp >> 2;           // head of the pair handled by this warpgroup
-    const int q = warp & 3;             // TMEM lane quadrant
-    const int t = q * 32 + lane;        // row of this thread (t, s or (h,p))
-    const int head = h0 + wg;
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ producers
+    const int hh = (warp - 8) >> 2;     // head of the pair
+    const int q = warp & 3;
+    const int t = q * 32 + lane;
+    const int head = h0 + hh;
     const float A = -expf(a.A_log[(int64_t)head * a.al_s]);
     const float dtb = a.dt_bias[(int64_t)head * a.dtb_s];
-    const float Dh = a.Dp ? a.Dp[(int64_t)head * a.d_s] : 0.f;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    // state rows: r = t -> head hr = t / 64, p = t % 64; this warpgroup owns
-    // state columns [wg * N/2, (wg+1) * N/2)
-    const int hr = t >> 6, pr = t & 63;
-
-    // conv weights of this head's 64 x channels -> shared memory (read per chunk)
-    float* cw_s = reinterpret_cast<float*>(smem + OFF_CW) + wg * 256;     // [64 ch][4]
-    float* cb_s = reinterpret_cast<float*>(smem + OFF_CW) + 512 + wg * 64;
-    if (t < 64) {
-      const int ch = head * P + t;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) cw_s[t * 4 + k] = a.conv_w[(int64_t)ch * a.cw_sc + k * a.cw_sk];
-      cb_s[t] = a.conv_b ? a.conv_b[(int64_t)ch * a.cb_s] : 0.f;
-    }
-    // this thread's conv work: 8 channels (vector vc) x rows strip*8 .. strip*8+7
-    const int vc = t & 7, strip = t >> 3;
+    const float* wv_s = cw_all + hh * 256;
+    const float* bv_s = cw_all + 512 + hh * 64;
+    const int vc = t & 7, strip = t >> 3;   // 8 channels x rows strip*8 .. strip*8+7
     const int xch = head * P + vc * 8;
-    const __nv_bfloat16* xsrc = a.xbc + (int64_t)b * a.x_sb + xch;
-
-    // raw rows (strip*8 - 3 ... strip*8 + 7) of chunk cc: all 11 loads in
-    // flight at once (addresses clamped into the sequence, masked on use)
-    uint4 raw[11];
-    // raw dt of the next chunk for this head [0] and the pair's other head [1]
-    // (bf16 bits zero-extended; converted only when used, so the loads stay in flight)
-    uint32_t dt_bits[2] = {0u, 0u};
-    const int other = h0 + (wg ^ 1);
-    const float A_o = -expf(a.A_log[(int64_t)other * a.al_s]);
-    const float dtb_o = a.dt_bias[(int64_t)other * a.dtb_s];
-    float cum_end_other = 0.f;   // the other head's sum of A dt over the chunk being produced
-    auto load_chunk = [&](int cc) {
-      const int tb = cc * Q + strip * 8 - 3;
-#pragma unroll
-      for (int r = 0; r < 11; ++r) {
-        const int tt = min(max(tb + r, 0), L - 1);
-        raw[r] = ldg_nc_v4(xsrc + (int64_t)tt * a.x_st);
-      }
-      const int td = min(cc * Q + t, L - 1);
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int64_t di = (int64_t)b * a.dt_sb + (int64_t)td * a.dt_st +
-                           (int64_t)(hh ? other : head) * a.dt_sh;
-        if (a.dt_bf16)
-          asm volatile("ld.global.nc.u16 %0, [%1];" : "=r"(dt_bits[hh])
-                       : "l"(static_cast<const __nv_bfloat16*>(a.dt) + di));
-        else
-          asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(dt_bits[hh])
-                       : "l"(static_cast<const float*>(a.dt) + di));
-      }
+    const uint32_t raw_row0 = base + OFF_RAW + hh * kRawStride + (uint32_t)(strip * 8) * 128 + vc * 16;
+    const int64_t dt_row = (int64_t)b * a.dt_sb + (int64_t)head * a.dt_sh;
+    uint32_t dt_bits = 0;   // raw dt of the chunk about to be produced (converted when used)
+    auto load_dt = [&](int cc) {
+      const int64_t di = dt_row + (int64_t)min(cc * Q + t, L - 1) * a.dt_st;
+      if (a.dt_bf16)
+        asm volatile("ld.global.nc.u16 %0, [%1];" : "=r"(dt_bits)
+                     : "l"(static_cast<const __nv_bfloat16*>(a.dt) + di));
+      else
+        asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(dt_bits)
+                     : "l"(static_cast<const float*>(a.dt) + di));
     };
-    auto dt_value = [&](uint32_t bits) {
-      return a.dt_bf16 ? __uint_as_float(bits << 16) : __uint_as_float(bits);
-    };
-
     uint32_t wg_uses = 0;
-    float* wsum_o = wsum + 8;   // [2 wg][4 warps] partial sums of the other head
-    // dt, cumsum, column factors and conv of chunk cc into buffer cc & 1
-    auto produce = [&](int cc) -> bool {
-      const int buf = cc & 1;
-      float* cm = cum_s + (buf * 2 + wg) * 128;
-      float* dtv = dt_s + (buf * 2 + wg) * 128;
-      float* cfv = cf_s + (buf * 2 + wg) * 128;
-      const int t0 = cc * Q;
-      const bool in_seq = t0 + t < L;
-      const float dt = in_seq ? softplus_f32(dt_value(dt_bits[0]) + dtb) : 0.f;
+    load_dt(0);
+    for (int c = 0; c < nchunks; ++c) {
+      const int buf = c & 1;
+      const int t0 = c * Q;
+      // X[buf] and cum/dt/cf[buf] are free once the epilogue of chunk c-2 is done
+      if (c >= 2 && !waitw(bar(B_Y_EMPTY0 + buf), ((c - 2) >> 1) & 1, abort_flag, 20)) break;
+      ALLOY_TRACE_POINT(4 + hh, c, 0);
+      // ---- dt, warp-local scan, column factors ----
+      const float dt = t0 + t < L
+          ? softplus_f32((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
+          : 0.f;
+      if (c + 1 < nchunks) load_dt(c + 1);
       float v = A * dt;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const float u = __shfl_up_sync(0xffffffffu, v, o);
         if (lane >= o) v += u;
       }
-      // column factor exp(cum[end of the 32-block] - cum[t]) dt[t] needs only this warp's scan
-      cfv[t] = ex2_approx((__shfl_sync(0xffffffffu, v, 31) - v) * kLog2e) * dt;
-      float vo = in_seq ? A_o * softplus_f32(dt_value(dt_bits[1]) + dtb_o) : 0.f;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) vo += __shfl_xor_sync(0xffffffffu, vo, o);
-      if (lane == 31) wsum[wg * 4 + q] = v;
-      if (lane == 0) wsum_o[wg * 4 + q] = vo;
-      ALLOY_TRACE_POINT(wg, cc - 1, 10);
-      // conv + SiLU of this head's x channels -> X_h (bf16, unscaled)
+      float* cm = cum_s + (buf * 2 + hh) * 128;
+      cf_s[(buf * 2 + hh) * 128 + t] = ex2_approx((__shfl_sync(0xffffffffu, v, 31) - v) * kLog2e) * dt;
+      dt_s[(buf * 2 + hh) * 128 + t] = dt;
+      if (lane == 31) wsum[(buf * 2 + hh) * 4 + q] = v;
+      // ---- conv + SiLU of this head's x channels -> X[buf][hh] (bf16, unscaled) ----
+      if (!waitw(bar(B_RAW_FULL), c & 1, abort_flag, 21)) break;
+      ALLOY_TRACE_POINT(4 + hh, c, 1);
       {
-        float xr[11][8];
-        const int tb = t0 + strip * 8 - 3;
+        const uint32_t sX = base + OFF_X + (buf * 2 + hh) * 16384;
+        float win[4][8];
 #pragma unroll
         for (int r = 0; r < 11; ++r) {
-          const int tt = tb + r;
-          const uint32_t wd[4] = {raw[r].x, raw[r].y, raw[r].z, raw[r].w};
+          const int tt = t0 + strip * 8 - 3 + r;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            xr[r][2 * i] = bf16_lo(wd[i]);
-            xr[r][2 * i + 1] = bf16_hi(wd[i]);
-          }
-          if (tt >= L) {
+          for (int k = 0; k < 3; ++k)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) xr[r][i] = 0.f;
-          } else if (tt < 0) {
+            for (int i = 0; i < 8; ++i) win[k][i] = win[k + 1][i];
+          if (tt < 0) {
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-              xr[r][i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
-                                                               (int64_t)(a.K - 1 + tt) * a.ci_sk +
-                                                               (int64_t)(xch + i) * a.ci_sc])
-                                   : 0.f;
+              win[3][i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
+                                                                (int64_t)(a.K - 1 + tt) * a.ci_sk +
+                                                                (int64_t)(xch + i) * a.ci_sc])
+                                    : 0.f;
+          } else {
+            const uint4 u = ld_shared_v4(raw_row0 + r * 128);
+            const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              win[3][2 * i] = bf16_lo(wd[i]);
+              win[3][2 * i + 1] = bf16_hi(wd[i]);
+            }
+          }
+          if (r >= 3) {
+            const int s = strip * 8 + r - 3;
+            float y8[8];
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+              const float4 w = reinterpret_cast<const float4*>(wv_s)[ch * 8 + vc];
+              float acc = bv_s[ch * 8 + vc];
+              acc = fmaf(win[0][ch], w.x, acc);
+              acc = fmaf(win[1][ch], w.y, acc);
+              acc = fmaf(win[2][ch], w.z, acc);
+              acc = fmaf(win[3][ch], w.w, acc);
+              y8[ch] = (t0 + s < L) ? silu_fast(acc) : 0.f;
+            }
+            st_shared_v4(sX + sw_off(s, vc), pack_bf16x2(y8[0], y8[1]), pack_bf16x2(y8[2], y8[3]),
+                         pack_bf16x2(y8[4], y8[5]), pack_bf16x2(y8[6], y8[7]));
           }
         }
-        ALLOY_TRACE_POINT(wg, cc - 1, 11);
-        const uint32_t sX = base + OFF_X + wg * 16384;
-        float y8[8][8];
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const float4 wv = reinterpret_cast<const float4*>(cw_s)[vc * 8 + ch];
-          const float bv = cb_s[vc * 8 + ch];
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            float acc = bv;
-            acc = fmaf(xr[r][ch], wv.x, acc);
-            acc = fmaf(xr[r + 1][ch], wv.y, acc);
-            acc = fmaf(xr[r + 2][ch], wv.z, acc);
-            acc = fmaf(xr[r + 3][ch], wv.w, acc);
-            y8[r][ch] = (t0 + strip * 8 + r < L) ? silu_fast(acc) : 0.f;
-          }
-        }
-        ALLOY_TRACE_POINT(wg, cc - 1, 12);
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-          st_shared_v4(sX + sw_off(strip * 8 + r, vc), pack_bf16x2(y8[r][0], y8[r][1]),
-                       pack_bf16x2(y8[r][2], y8[r][3]), pack_bf16x2(y8[r][4], y8[r][5]),
-                       pack_bf16x2(y8[r][6], y8[r][7]));
       }
-      ALLOY_TRACE_POINT(wg, cc - 1, 13);
       fence_async_smem();
-      if (!warps_sync(bar(B_WG0 + wg), wg_uses, abort_flag, 16)) return false;
-      ALLOY_TRACE_POINT(wg, cc - 1, 14);
-      for (int i = 0; i < q; ++i) v += wsum[wg * 4 + i];
-      cum_end_other = wsum_o[wg * 4 + 0] + wsum_o[wg * 4 + 1] + wsum_o[wg * 4 + 2] +
-                      wsum_o[wg * 4 + 3];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_RAW_EMPTY));
+      ALLOY_TRACE_POINT(4 + hh, c, 2);
+      // ---- prefix over the warps -> cumulative log decay ----
+      // (wsum is double-buffered by chunk parity: its next write, two chunks
+      // on, comes after every warp has passed the next chunk's sync)
+      if (!warps_sync(bar(B_PWG0 + hh), wg_uses, abort_flag, 22)) break;
+      for (int i = 0; i < q; ++i) v += wsum[(buf * 2 + hh) * 4 + i];
       cm[t] = v;
-      dtv[t] = dt;
-      // cum / dt visible to the whole warpgroup
-      return warps_sync(bar(B_WG0 + wg), wg_uses, abort_flag, 17);
-    };
+      // X, cum, dt, cf of chunk c are ready
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_X_READY0 + buf));
+      ALLOY_TRACE_POINT(4 + hh, c, 3);
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int cw = warp >> 2;           // consumer warpgroup
+    const int q = warp & 3;             // TMEM lane quadrant
+    const int t = q * 32 + lane;        // row of this thread (t, s or (h,p))
+    const int head = h0 + cw;           // head whose X' and epilogue this warpgroup does
+    const float D0 = a.Dp ? a.Dp[(int64_t)h0 * a.d_s] : 0.f;
+    const float D1 = a.Dp ? a.Dp[(int64_t)(h0 + 1) * a.d_s] : 0.f;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    // state rows: r = t -> head hr = t / 64, p = t % 64; this warpgroup owns
+    // state columns [cw * N/2, (cw+1) * N/2)
+    const int hr = t >> 6, pr = t & 63;
 
     // initial state -> TMEM
     for (int cc = 0; cc < NHALF / 32; ++cc) {
       uint32_t r[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const int n = wg * NHALF + cc * 32 + i;
+        const int n = cw * NHALF + cc * 32 + i;
         const float v = a.ssm_in ? a.ssm_in[(int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh +
                                             (int64_t)n * a.si_sn + (int64_t)pr * a.si_sp]
                                  : 0.f;
         r[i] = __float_as_uint(v);
       }
-      tmem_st32(lane_base + T_ST + wg * NHALF + cc * 32, r);
+      tmem_st32(lane_base + T_ST + cw * NHALF + cc * 32, r);
     }
     tmem_st_wait();
 
-    load_chunk(0);
-    // conv weights in shared memory are visible to the whole warpgroup
-    bool ok = warps_sync(bar(B_WG0 + wg), wg_uses, abort_flag, 19) && produce(0);
-    for (int c = 0; ok && c < nchunks; ++c) {
+    for (int c = 0; c < nchunks; ++c) {
       const uint32_t ph = c & 1, pph = (c - 1) & 1;
       const int buf = c & 1;
-      const float* cm = cum_s + (buf * 2 + wg) * 128;
-      const float* dtv = dt_s + (buf * 2 + wg) * 128;
-      const float* cfv = cf_s + (buf * 2 + wg) * 128;
-      const bool more = c + 1 < nchunks;
-      if (more) load_chunk(c + 1);
-      ALLOY_TRACE_POINT(wg, c, 0);
+      const float* cm0 = cum_s + (buf * 2 + 0) * 128;
+      const float* cm1 = cum_s + (buf * 2 + 1) * 128;
+      if (!waitw(bar(B_X_READY0 + buf), (c >> 1) & 1, abort_flag, 30)) break;
+      ALLOY_TRACE_POINT(cw, c, 0);
       // ---- state: H = bf16(state) -> HX_hr; state *= exp(cum[Q-1]) ----
-      if (c > 0 && !waitw(bar(B_ST_DONE), pph, abort_flag, 11)) break;
-      ALLOY_TRACE_POINT(wg, c, 3);
+      if (c > 0 && !waitw(bar(B_ST_DONE), pph, abort_flag, 31)) break;
       tc_fence_after();
       {
-        const float e_end = ex2_approx((hr == wg ? cm[127] : cum_end_other) * kLog2e);
+        const float e_end = ex2_approx((hr ? cm1[127] : cm0[127]) * kLog2e);
         const uint32_t sH = base + OFF_HX + hr * 16384;
 #pragma unroll
         for (int cc = 0; cc < NHALF / 32; ++cc) {
-          const int n0 = wg * NHALF + cc * 32;
+          const int n0 = cw * NHALF + cc * 32;
           uint32_t r[32];
           tmem_ld32(lane_base + T_ST + n0, r);
           tmem_ld_wait();
 #pragma unroll
           for (int g4 = 0; g4 < 4; ++g4) {
             const int n = n0 + g4 * 8;
-            uint32_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              o[i] = pack_bf16x2(__uint_as_float(r[g4 * 8 + 2 * i]), __uint_as_float(r[g4 * 8 + 2 * i + 1]));
-            st_shared_v4(sH + (n >> 6) * 8192 + sw_off(pr, (n & 63) >> 3), o[0], o[1], o[2], o[3]);
+            st_shared_v4(sH + (n >> 6) * 8192 + sw_off(pr, (n & 63) >> 3),
+                         pack_bf16x2(__uint_as_float(r[g4 * 8 + 0]), __uint_as_float(r[g4 * 8 + 1])),
+                         pack_bf16x2(__uint_as_float(r[g4 * 8 + 2]), __uint_as_float(r[g4 * 8 + 3])),
+                         pack_bf16x2(__uint_as_float(r[g4 * 8 + 4]), __uint_as_float(r[g4 * 8 + 5])),
+                         pack_bf16x2(__uint_as_float(r[g4 * 8 + 6]), __uint_as_float(r[g4 * 8 + 7])));
           }
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * e_end);
@@ -640,115 +648,113 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_HBF_READY));
-      ALLOY_TRACE_POINT(wg, c, 4);
-      // ---- scores S_h = CB * decay * dt (+ D on the diagonal) ----
-      if (!waitw(bar(B_CB_FULL), ph, abort_flag, 12)) break;
-      ALLOY_TRACE_POINT(wg, c, 1);
+      ALLOY_TRACE_POINT(cw, c, 1);
+      // ---- scores of both heads, blocks j = cw, cw + 2, in place over CB ----
+      // S_h[t, s] = CB[t, s] exp(cum_h[t] - cum_h[s]) dt_h[s] for s <= t (+ D_h on s == t),
+      // block j of S_h stored as bf16 pairs in columns [32j + 16h, 32j + 16h + 16)
+      if (!waitw(bar(B_CB_FULL), ph, abort_flag, 32)) break;
+      ALLOY_TRACE_POINT(cw, c, 2);
       tc_fence_after();
-      {
-        const float cum_t = cm[t];
-        const uint32_t sS = base + OFF_S + wg * 32768;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t r[32];   // CB row segment, overwritten in place by the scores
-          if (j > q) {
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = cw + 2 * jj;
+        uint32_t o[32];
+        if (j > q) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = 0u;
-          } else {
-            tmem_ld32(lane_base + T_CB + 32 * j, r);
-            tmem_ld_wait();
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        } else {
+          uint32_t r[32];
+          tmem_ld32(lane_base + T_CB + 32 * j, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float* cm = h ? cm1 : cm0;
+            const float cum_t = cm[t];
             if (j < q) {
               const float R = ex2_approx((cum_t - cm[32 * j + 31]) * kLog2e);
-              const float4* cf4 = reinterpret_cast<const float4*>(cfv + 32 * j);
+              const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + 32 * j);
 #pragma unroll
               for (int i4 = 0; i4 < 8; ++i4) {
                 const float4 f = cf4[i4];
-                r[4 * i4 + 0] = __float_as_uint(__uint_as_float(r[4 * i4 + 0]) * R * f.x);
-                r[4 * i4 + 1] = __float_as_uint(__uint_as_float(r[4 * i4 + 1]) * R * f.y);
-                r[4 * i4 + 2] = __float_as_uint(__uint_as_float(r[4 * i4 + 2]) * R * f.z);
-                r[4 * i4 + 3] = __float_as_uint(__uint_as_float(r[4 * i4 + 3]) * R * f.w);
+                o[16 * h + 2 * i4] = pack_bf16x2(__uint_as_float(r[4 * i4 + 0]) * R * f.x,
+                                                 __uint_as_float(r[4 * i4 + 1]) * R * f.y);
+                o[16 * h + 2 * i4 + 1] = pack_bf16x2(__uint_as_float(r[4 * i4 + 2]) * R * f.z,
+                                                     __uint_as_float(r[4 * i4 + 3]) * R * f.w);
               }
             } else {
+              const float* dtv = dt_s + (buf * 2 + h) * 128;
+              const float Dh = h ? D1 : D0;
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const int s = 32 * j + i;
-                float v = 0.f;
-                if (s <= t) v = __uint_as_float(r[i]) * ex2_approx((cum_t - cm[s]) * kLog2e) * dtv[s];
-                if (s == t) v += Dh;
-                r[i] = __float_as_uint(v);
+              for (int i2 = 0; i2 < 16; ++i2) {
+                float v2[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const int s = 32 * j + 2 * i2 + e;
+                  float v = 0.f;
+                  if (s <= t) v = __uint_as_float(r[2 * i2 + e]) * ex2_approx((cum_t - cm[s]) * kLog2e) * dtv[s];
+                  if (s == t) v += Dh;
+                  v2[e] = v;
+                }
+                o[16 * h + i2] = pack_bf16x2(v2[0], v2[1]);
               }
             }
           }
-#pragma unroll
-          for (int g4 = 0; g4 < 4; ++g4) {
-            const int chunk = (j & 1) * 4 + g4;
-            const float* f = reinterpret_cast<const float*>(r) + g4 * 8;
-            st_shared_v4(sS + (j >> 1) * 16384 + sw_off(t, chunk), pack_bf16x2(f[0], f[1]),
-                         pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
-                         pack_bf16x2(f[6], f[7]));
-          }
         }
+        tmem_st32(lane_base + T_CB + 32 * j, o);
       }
+      tmem_st_wait();
       tc_fence_before();
-      fence_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(bar(B_CB_EMPTY));
-        mbar_arrive(bar(B_S_READY0 + wg));
-      }
-      ALLOY_TRACE_POINT(wg, c, 2);
-      // ---- X'_h = X_h * dt * exp(cum[Q-1] - cum[s]) -> HX_h ----
-      if (!waitw(bar(B_YI_DONE), ph, abort_flag, 13)) break;
-      ALLOY_TRACE_POINT(wg, c, 5);
+      if (lane == 0) mbar_arrive(bar(B_S_READY));
+      ALLOY_TRACE_POINT(cw, c, 3);
+      // ---- X'_cw = X * dt * exp(cum[Q-1] - cum[s]) -> HX_cw ----
+      if (!waitw(bar(B_YI_DONE), ph, abort_flag, 33)) break;
+      ALLOY_TRACE_POINT(cw, c, 4);
       {
-        const float e = dtv[t] * ex2_approx((cm[127] - cm[t]) * kLog2e);
-        const uint32_t sX = base + OFF_X + wg * 16384, sXp = base + OFF_HX + wg * 16384;
+        const float* cm = cw ? cm1 : cm0;
+        const float e = dt_s[(buf * 2 + cw) * 128 + t] * ex2_approx((cm[127] - cm[t]) * kLog2e);
+        const uint32_t sX = base + OFF_X + (buf * 2 + cw) * 16384, sXp = base + OFF_HX + cw * 16384;
 #pragma unroll
         for (int ch = 0; ch < 8; ++ch) {
           const uint4 u = ld_shared_v4(sX + sw_off(t, ch));
           const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
-          uint32_t o[4];
+          uint32_t o4[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) o[i] = pack_bf16x2(bf16_lo(wd[i]) * e, bf16_hi(wd[i]) * e);
-          st_shared_v4(sXp + sw_off(t, ch), o[0], o[1], o[2], o[3]);
+          for (int i = 0; i < 4; ++i) o4[i] = pack_bf16x2(bf16_lo(wd[i]) * e, bf16_hi(wd[i]) * e);
+          st_shared_v4(sXp + sw_off(t, ch), o4[0], o4[1], o4[2], o4[3]);
         }
       }
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_XP_READY));
-      ALLOY_TRACE_POINT(wg, c, 6);
-      // ---- inputs of the next chunk (X_h is free once Y(c) has read it) ----
-      if (more) {
-        if (!waitw(bar(B_X_FREE0 + wg), ph, abort_flag, 10)) break;
-        ALLOY_TRACE_POINT(wg, c, 7);
-        if (!produce(c + 1)) break;
-      }
-      ALLOY_TRACE_POINT(wg, c, 8);
+      ALLOY_TRACE_POINT(cw, c, 5);
       // ---- epilogue: y = Y + exp(cum[t]) Yi -> global (bf16) ----
-      // Each warp stages its 32 rows in its own rows of S_h (free: Y(c) has
-      // read it), then stores 4 full 128-byte rows per instruction.
-      if (!more && !waitw(bar(B_X_FREE0 + wg), ph, abort_flag, 14)) break;
+      // Each warp stages its 32 rows in its own rows of X[buf][cw] (read by
+      // Y(c) and X'(c), both done), then stores 4 full 128-byte rows per
+      // instruction.
+      if (!waitw(bar(B_Y_FULL), ph, abort_flag, 34)) break;
+      ALLOY_TRACE_POINT(cw, c, 6);
       tc_fence_after();
       {
         const int t0 = c * Q;
-        const float e = ex2_approx(cm[t] * kLog2e);
-        const uint32_t stage = base + OFF_S + wg * 32768 + q * 4096;
+        const float e = ex2_approx((cw ? cm1[t] : cm0[t]) * kLog2e);
+        const uint32_t stage = base + OFF_X + (buf * 2 + cw) * 16384 + q * 4096;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t ry[32], ri[32];
-          tmem_ld32(lane_base + T_Y + 64 * wg + 32 * half, ry);
-          tmem_ld32(lane_base + T_YI + 64 * wg + 32 * half, ri);
+          tmem_ld32(lane_base + T_Y + 64 * cw + 32 * half, ry);
+          tmem_ld32(lane_base + T_YI + 64 * cw + 32 * half, ri);
           tmem_ld_wait();
 #pragma unroll
           for (int g4 = 0; g4 < 4; ++g4) {
-            uint32_t o[4];
+            uint32_t o4[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int k0 = g4 * 8 + 2 * i;
-              o[i] = pack_bf16x2(fmaf(e, __uint_as_float(ri[k0]), __uint_as_float(ry[k0])),
-                                 fmaf(e, __uint_as_float(ri[k0 + 1]), __uint_as_float(ry[k0 + 1])));
+              o4[i] = pack_bf16x2(fmaf(e, __uint_as_float(ri[k0]), __uint_as_float(ry[k0])),
+                                  fmaf(e, __uint_as_float(ri[k0 + 1]), __uint_as_float(ry[k0 + 1])));
             }
-            st_shared_v4(stage + sw_off(lane, half * 4 + g4), o[0], o[1], o[2], o[3]);
+            st_shared_v4(stage + sw_off(lane, half * 4 + g4), o4[0], o4[1], o4[2], o4[3]);
           }
         }
         __syncwarp();
@@ -763,15 +769,14 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const TcArgs a) {
         __syncwarp();
       }
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_Y_EMPTY));
-      ALLOY_TRACE_POINT(wg, c, 9);
+      if (lane == 0) mbar_arrive(bar(B_Y_EMPTY0 + buf));
+      ALLOY_TRACE_POINT(cw, c, 7);
     }
     // ---- final state -> ssm_out ----
-    if (!*abort_flag && a.ssm_out && waitw(bar(B_ST_DONE), (nchunks - 1) & 1, abort_flag, 15)) {
+    if (!*abort_flag && a.ssm_out && waitw(bar(B_ST_DONE), (nchunks - 1) & 1, abort_flag, 35)) {
       tc_fence_after();
       for (int cc = 0; cc < NHALF / 32; ++cc) {
-        const int n0 = wg * NHALF + cc * 32;
+        const int n0 = cw * NHALF + cc * 32;
         uint32_t r[32];
         tmem_ld32(lane_base + T_ST + n0, r);
         tmem_ld_wait();
@@ -882,16 +887,28 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(ALLOY_ERR_CUDA, "ssd_tc: cuTensorMapEncodeTiled failed (%d)", (int)r);
-  // 3. the SSD kernel
+  // 3. tensor map over xBC for the raw x rows: box 64 channels x (Q + 3) rows
+  CUtensorMap xmap;
+  {
+    const cuuint64_t xd[3] = {(cuuint64_t)(s.H * 64 + 2 * s.G * s.N), (cuuint64_t)s.L, (cuuint64_t)s.B};
+    const cuuint64_t xs[2] = {(cuuint64_t)s.xbc_st * 2, (cuuint64_t)s.xbc_sb * 2};
+    const cuuint32_t xbox[3] = {64, (cuuint32_t)kRawRows, 1};
+    r = encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(s.xBC), xd, xs, xbox,
+               estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(ALLOY_ERR_CUDA, "ssd_tc: cuTensorMapEncodeTiled (xBC) failed (%d)", (int)r);
+  }
+  // 4. the SSD kernel
   dim3 grid(s.head_count / 2, s.B);
   if (s.N == 128) {
     ALLOY_CUDA(cudaFuncSetAttribute(ssd_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemBytes));
-    ssd_tc_kernel<128><<<grid, kThreads, kSmemBytes, stream>>>(map, a);
+    ssd_tc_kernel<128><<<grid, kThreads, kSmemBytes, stream>>>(map, xmap, a);
   } else {
     ALLOY_CUDA(cudaFuncSetAttribute(ssd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemBytes));
-    ssd_tc_kernel<64><<<grid, kThreads, kSmemBytes, stream>>>(map, a);
+    ssd_tc_kernel<64><<<grid, kThreads, kSmemBytes, stream>>>(map, xmap, a);
   }
   return check_launch("ssd_tc_kernel");
 }
