@@ -44,6 +44,7 @@ EXPORTS = (
     "alloy_ssd_decode_step",
     "alloy_ssd_combined_workspace_size",
     "alloy_check_device_status",
+    "alloy_ssd_combined_noalloc",
 )
 
 
@@ -116,10 +117,12 @@ def load():
                                                           ctypes.c_int32, D]
         lib.alloy_ssd_combined_workspace_size.restype = ctypes.c_size_t
         lib.alloy_check_device_status.argtypes = [vp]
+        lib.alloy_ssd_combined_noalloc.argtypes = [P] * 12 + [D, vp]
         lib.alloy_selective_scan.argtypes = [P] * 8 + [vp]
         lib.alloy_ssd_decode_step.argtypes = [P] * 10 + [D, vp]
         for name in ("alloy_conv1d_silu", "alloy_depthwise_conv1d", "alloy_ssd_combined",
-                     "alloy_selective_scan", "alloy_ssd_decode_step", "alloy_check_device_status"):
+                     "alloy_selective_scan", "alloy_ssd_decode_step", "alloy_check_device_status",
+                     "alloy_ssd_combined_noalloc"):
             getattr(lib, name).restype = ctypes.c_int
         if lib.alloy_abi_version() != ABI_VERSION:
             raise AlloyLibraryError(

@@ -154,6 +154,38 @@ ALLOY_API size_t alloy_ssd_combined_workspace_size(int64_t batch, int64_t seqlen
                                                    const alloy_ssd_dims_t* dims);
 
 /*
+ * alloy_ssd_combined for callers that cannot allocate device memory.
+ * No counterpart in the reference (MLX allocates every buffer itself).
+ *
+ * Who needs it: a process that gives all device memory to its own pool at
+ * start-up and forbids allocation afterwards, or a host runtime that only has
+ * raw device pointers from another framework and no CUDA allocator of its own
+ * (for instance a Go or Java service calling in through FFI).
+ * Same arguments and results as alloy_ssd_combined, without the workspace:
+ * the scratch comes from one fixed 8 MiB array compiled into the library,
+ * held by every device that loads it until the process exits.  Calls whose
+ * scratch (alloy_ssd_combined_workspace_size) would exceed 8 MiB are rejected
+ * with ALLOY_ERR_UNSUPPORTED before anything is launched.  The call allocates
+ * and frees nothing.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture begins.
+ *  - All calls on a device share the array, and it keeps the last call's
+ *    contents: calls that may overlap on the device (different streams, or
+ *    other host threads) race and must be serialised by the caller.  Nothing
+ *    needs clearing between calls: the scan reads only what the same call's
+ *    B/C pre-pass wrote.
+ */
+ALLOY_API int alloy_ssd_combined_noalloc(const alloy_tensor_t* xBC, const alloy_tensor_t* dt_raw,
+                       const alloy_tensor_t* conv_w, const alloy_tensor_t* conv_b,
+                       const alloy_tensor_t* dt_bias, const alloy_tensor_t* A_log,
+                       const alloy_tensor_t* D,
+                       const alloy_tensor_t* ssm_in, const alloy_tensor_t* conv_in,
+                       alloy_tensor_t* y, alloy_tensor_t* ssm_out,
+                       alloy_tensor_t* conv_out,
+                       const alloy_ssd_dims_t* dims, void* stream);
+
+/*
  * Synchronises `stream` and reports whether a kernel launched since the last
  * check gave up on a bounded device-side wait (ALLOY_ERR_TIMEOUT, with the
  * site in the last-error message); clears the record.  No counterpart in the
