@@ -52,9 +52,10 @@ using namespace tc;
 
 constexpr int Q = 128;                 // chunk length (UMMA M)
 constexpr int P = 64;                  // head dim
-constexpr int kThreads = 576;          // 18 warps
-constexpr int kTmaWarp = 16;
+constexpr int kThreads = 608;          // 19 warps
+constexpr int kTmaWarp = 16;           // B/C half tiles
 constexpr int kMmaWarp = 17;
+constexpr int kRawWarp = 18;           // raw x rows
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
@@ -280,19 +281,20 @@ bc_conv_kernel(const TcArgs a, __nv_bfloat16* __restrict__ bc, int ncols) {
 // ----------------------------------------------------------------------------
 // the SSD kernel
 // ----------------------------------------------------------------------------
-// Roles (18 warps):
-//   warps 0-7   consumers: warpgroup cw = 0/1.  Per chunk: copy of the state to
-//               bf16 (H) and its decay (state columns split by warpgroup), the
-//               scores S of both heads for the 32-column blocks j = cw, cw + 2
-//               written in place over CB in tensor memory, X' of head cw, and
-//               the epilogue of head cw.
+// Roles (19 warps):
+//   warps 0-7   consumers: warpgroup cw = 0/1.  Per chunk: the bf16 copy of
+//               the state and its decay (state columns split by warpgroup),
+//               X' of head cw, and the scores S of both heads for the
+//               32-column blocks j = cw, cw + 2, written in place over CB in
+//               tensor memory.
 //   warps 8-15  producers: warpgroup ph = 0/1 for head ph of the pair.  Per
-//               chunk: dt, cumulative log decay and column factors, and the
-//               conv + SiLU of the head's x channels from the TMA-staged raw
-//               rows into the double-buffered X.  They run up to one chunk
-//               ahead of the consumers.
-//   warp 16     TMA: lane 0 loads the raw x rows, lane 1 the B/C half tiles.
+//               chunk: dt, cumulative log decay and column factors, the conv +
+//               SiLU of the head's x channels from the TMA-staged raw rows into
+//               the double-buffered X, then the epilogue (y) of the previous
+//               chunk.  They run up to one chunk ahead of the consumers.
+//   warp 16     TMA of the B/C half tiles.
 //   warp 17     TMEM allocation and the MMA issue (one thread).
+//   warp 18     TMA of the raw x rows.
 template <int N>
 __global__ void __launch_bounds__(kThreads, 1)
 ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant__ CUtensorMap x_map,
@@ -332,29 +334,24 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
     tmem_alloc(base + OFF_TMEMPTR, 512);
     tmem_relinquish();
   }
-  if (warp == kTmaWarp && lane == 0) {
-    prefetch_tmap(&bc_map);
-    prefetch_tmap(&x_map);
-  }
-  // x conv weights of both heads (producers read them per output row), laid
-  // out [head][channel within vector][vector][tap] so that the 8 vectors a
-  // warp reads at once are contiguous (no bank conflicts)
+  if (warp == kTmaWarp && lane == 0) prefetch_tmap(&bc_map);
+  if (warp == kRawWarp && lane == 0) prefetch_tmap(&x_map);
+  // x conv weights of both heads, [head][channel][tap] and bias [head][channel]
+  // (each producer thread copies its 4 channels' taps into registers once)
   if (threadIdx.x < 128) {
     const int hh = threadIdx.x >> 6, ch = threadIdx.x & 63;
-    const int vec = ch >> 3, e = ch & 7;
     const int64_t c = (int64_t)(h0 + hh) * P + ch;
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-      cw_all[hh * 256 + (e * 8 + vec) * 4 + k] = a.conv_w[c * a.cw_sc + k * a.cw_sk];
-    cw_all[512 + hh * 64 + e * 8 + vec] = a.conv_b ? a.conv_b[c * a.cb_s] : 0.f;
+    for (int k = 0; k < 4; ++k) cw_all[(hh * 64 + ch) * 4 + k] = a.conv_w[c * a.cw_sc + k * a.cw_sk];
+    cw_all[512 + hh * 64 + ch] = a.conv_b ? a.conv_b[c * a.cb_s] : 0.f;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_ptr;
 
-  if (warp == kTmaWarp) {
-    // ------------------------------------------------------------ TMA
+  if (warp == kRawWarp) {
+    // ------------------------------------------------------------ TMA: raw x
     if (lane == 0) {
       // raw x rows [c*Q - 3, c*Q + Q) of both heads' channels (rows outside
       // [0, L) arrive as zeros)
@@ -371,7 +368,11 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
         while (!mbar_try_wait(bar(B_RAW_FULL), (issued - 1) & 1) && clock64() - t0 < kWaitCycles) {
         }
       }
-    } else if (lane == 1) {
+    }
+  } else if (warp == kTmaWarp) {
+    // ------------------------------------------------------------ TMA: B/C
+    // (its own warp: a sleeping wait in one lane would hold up a role in another)
+    if (lane == 0) {
       // B/C half tiles into the two-stage ring
       int issued = 0;
       for (int c = 0; c < nchunks; ++c) {
@@ -395,11 +396,11 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    // per chunk: CB -> Yi (after the state copy) -> Y (scores from TMEM) -> state update
+    // per chunk: CB -> Yi (after the state copy) -> state update (after X') -> Y (scores from TMEM)
     if (lane == 0) {
       constexpr uint32_t ID_CB = idesc_bf16(128, 128, 0, 0);
-      constexpr uint32_t ID_YI = idesc_bf16(128, 64, 0, 0);
-      constexpr uint32_t ID_ST = idesc_bf16(128, 64, 1, 1);
+      constexpr uint32_t ID_YI = idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t ID_ST = idesc_bf16(128, N, 1, 1);
       constexpr uint32_t ID_Y = idesc_bf16(128, 64, 0, 1);
       for (int c = 0; c < nchunks; ++c) {
         const uint32_t ph = c & 1, pph = (c - 1) & 1;
@@ -420,48 +421,51 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
         }
         umma_commit(bar(B_CB_FULL));
         ALLOY_TRACE_POINT(3, c, 0);
-        // Yi_h = C H_h^T
+        // Yi = C [H_0; H_1]^T for both heads at once (N = 128 rows (h, p))
         if (c > 0 && !wait1(bar(B_Y_EMPTY0 + (buf ^ 1)), ((c - 1) >> 1) & 1, abort_flag, 5)) goto mma_done;
         if (!wait1(bar(B_HBF_READY), ph, abort_flag, 6)) goto mma_done;
         tc_fence_after();
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t sH = base + OFF_HX + h * 16384;
-          for (int k = 0; k < NK; ++k) {
-            const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
+        for (int k = 0; k < NK; ++k) {
+          const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
+          const uint32_t sH = base + OFF_HX + k * 16384;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16(tmem + T_YI + 64 * h, sw128_desc(sC + 32 * kk, 16, 1024),
-                        sw128_desc(sH + k * 8192 + 32 * kk, 16, 1024), ID_YI, (k | kk) != 0);
-          }
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + T_YI, sw128_desc(sC + 32 * kk, 16, 1024),
+                      sw128_desc(sH + 32 * kk, 16, 1024), ID_YI, (k | kk) != 0);
         }
         umma_commit(bar(B_YI_DONE));
         ALLOY_TRACE_POINT(3, c, 1);
+        // state: ST[(h,p), n] += X'^T B over s, per N half; releases the stages
+        if (!wait1(bar(B_XP_READY), ph, abort_flag, 8)) goto mma_done;
+        ALLOY_TRACE_POINT(3, c, 9);
+        tc_fence_after();
+        {
+          // N = d_state in one chain: for d_state 128 the two 64-column halves of B
+          // sit in the two stage slots, 32 KB apart (the MN-atom stride)
+          const int slot0 = (c * NK) & 1;
+          const uint32_t sB = base + OFF_STAGE + slot0 * kStageBytes;
+          const uint32_t sXp = base + OFF_HX;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tmem + T_ST, sw128_desc(sXp + 2048 * kk, 16384, 1024),
+                      sw128_desc(sB + 2048 * kk, kStageBytes, 1024), ID_ST, 1);
+          for (int k = 0; k < NK; ++k) umma_commit(bar(B_EMPTY0 + ((c * NK + k) & 1)));
+        }
+        umma_commit(bar(B_ST_DONE));
+        ALLOY_TRACE_POINT(3, c, 10);
         // Y_h = S_h X_h, S_h (bf16 pairs) read from tensor memory
         if (!wait1(bar(B_S_READY), ph, abort_flag, 7)) goto mma_done;
+        ALLOY_TRACE_POINT(3, c, 8);
         tc_fence_after();
         for (int h = 0; h < 2; ++h) {
           const uint32_t sX = base + OFF_X + (buf * 2 + h) * 16384;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_bf16_ta(tmem + T_Y + 64 * h, tmem + T_CB + 32 * (kk >> 1) + 16 * h + 8 * (kk & 1),
+            umma_bf16_ta(tmem + T_Y + 64 * h, tmem + T_CB + 16 * kk + 8 * h,
                          sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
         }
         umma_commit(bar(B_Y_FULL));
         ALLOY_TRACE_POINT(3, c, 2);
-        // state: ST[(h,p), n] += X'^T B over s, per N half; releases the stages
-        if (!wait1(bar(B_XP_READY), ph, abort_flag, 8)) goto mma_done;
-        tc_fence_after();
-        for (int k = 0; k < NK; ++k) {
-          const int slot = (c * NK + k) & 1;
-          const uint32_t sB = base + OFF_STAGE + slot * kStageBytes;
-          const uint32_t sXp = base + OFF_HX;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_bf16(tmem + T_ST + 64 * k, sw128_desc(sXp + 2048 * kk, 16384, 1024),
-                      sw128_desc(sB + 2048 * kk, 16384, 1024), ID_ST, 1);
-          umma_commit(bar(B_EMPTY0 + slot));
-        }
-        umma_commit(bar(B_ST_DONE));
         ALLOY_TRACE_POINT(3, c, 3);
       }
     mma_done:
@@ -474,18 +478,17 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
       }
     }
   } else if (warp >= 8) {
-    // ------------------------------------------------------------ producers
+    // ------------------------------------------------------------ producers (warps 8-15)
     const int hh = (warp - 8) >> 2;     // head of the pair
     const int q = warp & 3;
     const int t = q * 32 + lane;
     const int head = h0 + hh;
     const float A = -expf(a.A_log[(int64_t)head * a.al_s]);
     const float dtb = a.dt_bias[(int64_t)head * a.dtb_s];
-    const float* wv_s = cw_all + hh * 256;
-    const float* bv_s = cw_all + 512 + hh * 64;
-    const int vc = t & 7, strip = t >> 3;   // 8 channels x rows strip*8 .. strip*8+7
-    const int xch = head * P + vc * 8;
-    const uint32_t raw_row0 = base + OFF_RAW + hh * kRawStride + (uint32_t)(strip * 8) * 128 + vc * 16;
+    // this thread's conv work: 4 channels (4*vc4 .. 4*vc4+3) x 16 rows (16*strip ..)
+    const int vc4 = t & 15, strip = t >> 4;
+    const int xch = head * P + vc4 * 4;
+    const uint32_t raw_row0 = base + OFF_RAW + hh * kRawStride + (uint32_t)(strip * 16) * 128 + vc4 * 8;
     const int64_t dt_row = (int64_t)b * a.dt_sb + (int64_t)head * a.dt_sh;
     uint32_t dt_bits = 0;   // raw dt of the chunk about to be produced (converted when used)
     auto load_dt = [&](int cc) {
@@ -497,13 +500,59 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
         asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(dt_bits)
                      : "l"(static_cast<const float*>(a.dt) + di));
     };
+    // ---- epilogue of chunk cc (head hh): y = Y + exp(cum[t]) Yi -> global ----
+    // Each warp stages its 32 rows in its own rows of X[cc&1][hh] (read by
+    // Y(cc) and X'(cc), both complete once Y_FULL(cc) is), then stores 4
+    // full 128-byte rows per instruction.
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    auto epilogue = [&](int cc) -> bool {
+      const int ebuf = cc & 1;
+      if (!waitw(bar(B_Y_FULL), cc & 1, abort_flag, 34)) return false;
+      tc_fence_after();
+      const int t0 = cc * Q;
+      const float e = ex2_approx(cum_s[(ebuf * 2 + hh) * 128 + t] * kLog2e);
+      const uint32_t stage = base + OFF_X + (ebuf * 2 + hh) * 16384 + q * 4096;
+      const uint64_t e2 = f2_splat(e);
+#pragma unroll
+      for (int qq = 0; qq < 4; ++qq) {
+        uint32_t ry[16], ri[16];
+        tmem_ld16(lane_base + T_Y + 64 * hh + 16 * qq, ry);
+        tmem_ld16(lane_base + T_YI + 64 * hh + 16 * qq, ri);
+        tmem_ld_wait();
+#pragma unroll
+        for (int g2 = 0; g2 < 2; ++g2) {
+          uint32_t o4[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int k0 = g2 * 8 + 2 * i;
+            o4[i] = f2_to_bf2(f2_fma(f2_pack(__uint_as_float(ri[k0]), __uint_as_float(ri[k0 + 1])), e2,
+                                     f2_pack(__uint_as_float(ry[k0]), __uint_as_float(ry[k0 + 1]))));
+          }
+          st_shared_v4(stage + sw_off(lane, qq * 2 + g2), o4[0], o4[1], o4[2], o4[3]);
+        }
+      }
+      __syncwarp();
+      __nv_bfloat16* ybase = a.y + (int64_t)b * a.y_sb + (int64_t)head * a.y_sh + (lane & 7) * 8;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int row = 4 * k + (lane >> 3);
+        const uint4 v = ld_shared_v4(stage + sw_off(row, lane & 7));
+        const int tt = t0 + q * 32 + row;
+        if (tt < L) *reinterpret_cast<uint4*>(ybase + (int64_t)tt * a.y_st) = v;
+      }
+      __syncwarp();
+      tc_fence_before();
+      if (lane == 0) mbar_arrive(bar(B_Y_EMPTY0 + ebuf));
+      return true;
+    };
     uint32_t wg_uses = 0;
     load_dt(0);
-    for (int c = 0; c < nchunks; ++c) {
+    bool ok = true;
+    for (int c = 0; ok && c < nchunks; ++c) {
       const int buf = c & 1;
       const int t0 = c * Q;
-      // X[buf] and cum/dt/cf[buf] are free once the epilogue of chunk c-2 is done
-      if (c >= 2 && !waitw(bar(B_Y_EMPTY0 + buf), ((c - 2) >> 1) & 1, abort_flag, 20)) break;
+      // X[buf] and cum/dt/cf[buf] held chunk c-2, whose epilogue this warpgroup
+      // finished last iteration (after Y(c-2), and so after X'(c-2) and S(c-2))
       ALLOY_TRACE_POINT(4 + hh, c, 0);
       // ---- dt, warp-local scan, column factors ----
       const float dt = t0 + t < L
@@ -524,46 +573,55 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
       if (!waitw(bar(B_RAW_FULL), c & 1, abort_flag, 21)) break;
       ALLOY_TRACE_POINT(4 + hh, c, 1);
       {
+        // taps and bias of this thread's channel pairs (0,1), (2,3), reloaded
+        // per chunk so they are not live across the epilogue
+        uint64_t w2[4][2], b2[2];
+#pragma unroll
+        for (int pp = 0; pp < 2; ++pp) {
+          const float* w0 = cw_all + (hh * 64 + vc4 * 4 + 2 * pp) * 4;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) w2[k][pp] = f2_pack(w0[k], w0[4 + k]);
+          b2[pp] = f2_pack(cw_all[512 + hh * 64 + vc4 * 4 + 2 * pp],
+                           cw_all[512 + hh * 64 + vc4 * 4 + 2 * pp + 1]);
+        }
         const uint32_t sX = base + OFF_X + (buf * 2 + hh) * 16384;
-        float win[4][8];
+        uint64_t win[4][2];   // the last 4 rows, as channel pairs
 #pragma unroll
-        for (int r = 0; r < 11; ++r) {
-          const int tt = t0 + strip * 8 - 3 + r;
+        for (int r = 0; r < 19; ++r) {
+          const int tt = t0 + strip * 16 - 3 + r;
 #pragma unroll
-          for (int k = 0; k < 3; ++k)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) win[k][i] = win[k + 1][i];
+          for (int k = 0; k < 3; ++k) {
+            win[k][0] = win[k + 1][0];
+            win[k][1] = win[k + 1][1];
+          }
           if (tt < 0) {
+            float f[4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              win[3][i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
-                                                                (int64_t)(a.K - 1 + tt) * a.ci_sk +
-                                                                (int64_t)(xch + i) * a.ci_sc])
-                                    : 0.f;
+            for (int i = 0; i < 4; ++i)
+              f[i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
+                                                           (int64_t)(a.K - 1 + tt) * a.ci_sk +
+                                                           (int64_t)(xch + i) * a.ci_sc])
+                               : 0.f;
+            win[3][0] = f2_pack(f[0], f[1]);
+            win[3][1] = f2_pack(f[2], f[3]);
           } else {
-            const uint4 u = ld_shared_v4(raw_row0 + r * 128);
-            const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              win[3][2 * i] = bf16_lo(wd[i]);
-              win[3][2 * i + 1] = bf16_hi(wd[i]);
-            }
+            uint32_t w0, w1;
+            asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(w0), "=r"(w1) : "r"(raw_row0 + r * 128));
+            win[3][0] = f2_from_bf2(w0);
+            win[3][1] = f2_from_bf2(w1);
           }
           if (r >= 3) {
-            const int s = strip * 8 + r - 3;
-            float y8[8];
+            const int srow = strip * 16 + r - 3;
+            uint32_t o[2];
 #pragma unroll
-            for (int ch = 0; ch < 8; ++ch) {
-              const float4 w = reinterpret_cast<const float4*>(wv_s)[ch * 8 + vc];
-              float acc = bv_s[ch * 8 + vc];
-              acc = fmaf(win[0][ch], w.x, acc);
-              acc = fmaf(win[1][ch], w.y, acc);
-              acc = fmaf(win[2][ch], w.z, acc);
-              acc = fmaf(win[3][ch], w.w, acc);
-              y8[ch] = (t0 + s < L) ? silu_fast(acc) : 0.f;
+            for (int pp = 0; pp < 2; ++pp) {
+              uint64_t acc = b2[pp];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) acc = f2_fma(win[k][pp], w2[k][pp], acc);
+              o[pp] = (t0 + srow < L) ? f2_to_bf2(f2_silu(acc)) : 0u;
             }
-            st_shared_v4(sX + sw_off(s, vc), pack_bf16x2(y8[0], y8[1]), pack_bf16x2(y8[2], y8[3]),
-                         pack_bf16x2(y8[4], y8[5]), pack_bf16x2(y8[6], y8[7]));
+            const uint32_t addr = sX + srow * 128 + ((((vc4 >> 1) ^ (srow & 7))) << 4) + ((vc4 & 1) << 3);
+            asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(addr), "r"(o[0]), "r"(o[1]) : "memory");
           }
         }
       }
@@ -581,13 +639,16 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_X_READY0 + buf));
       ALLOY_TRACE_POINT(4 + hh, c, 3);
+      // the previous chunk's output, while the tensor cores and consumers work on this one
+      if (c > 0 && !epilogue(c - 1)) break;
+      ALLOY_TRACE_POINT(4 + hh, c, 4);
     }
+    if (!*abort_flag && nchunks > 0) epilogue(nchunks - 1);
   } else {
     // ------------------------------------------------------------ consumers
     const int cw = warp >> 2;           // consumer warpgroup
     const int q = warp & 3;             // TMEM lane quadrant
     const int t = q * 32 + lane;        // row of this thread (t, s or (h,p))
-    const int head = h0 + cw;           // head whose X' and epilogue this warpgroup does
     const float D0 = a.Dp ? a.Dp[(int64_t)h0 * a.d_s] : 0.f;
     const float D1 = a.Dp ? a.Dp[(int64_t)(h0 + 1) * a.d_s] : 0.f;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
@@ -622,7 +683,7 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
       tc_fence_after();
       {
         const float e_end = ex2_approx((hr ? cm1[127] : cm0[127]) * kLog2e);
-        const uint32_t sH = base + OFF_HX + hr * 16384;
+        const uint32_t sH = base + OFF_HX + hr * 8192;   // [n block][head][64 p][64 n]
 #pragma unroll
         for (int cc = 0; cc < NHALF / 32; ++cc) {
           const int n0 = cw * NHALF + cc * 32;
@@ -632,14 +693,20 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
 #pragma unroll
           for (int g4 = 0; g4 < 4; ++g4) {
             const int n = n0 + g4 * 8;
-            st_shared_v4(sH + (n >> 6) * 8192 + sw_off(pr, (n & 63) >> 3),
+            st_shared_v4(sH + (n >> 6) * 16384 + sw_off(pr, (n & 63) >> 3),
                          pack_bf16x2(__uint_as_float(r[g4 * 8 + 0]), __uint_as_float(r[g4 * 8 + 1])),
                          pack_bf16x2(__uint_as_float(r[g4 * 8 + 2]), __uint_as_float(r[g4 * 8 + 3])),
                          pack_bf16x2(__uint_as_float(r[g4 * 8 + 4]), __uint_as_float(r[g4 * 8 + 5])),
                          pack_bf16x2(__uint_as_float(r[g4 * 8 + 6]), __uint_as_float(r[g4 * 8 + 7])));
           }
+          const uint64_t e2 = f2_splat(e_end);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * e_end);
+          for (int i = 0; i < 16; ++i) {
+            float lo, hi;
+            f2_unpack(f2_mul(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), e2), lo, hi);
+            r[2 * i] = __float_as_uint(lo);
+            r[2 * i + 1] = __float_as_uint(hi);
+          }
           tmem_st32(lane_base + T_ST + n0, r);
         }
         tmem_st_wait();
@@ -649,64 +716,6 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_HBF_READY));
       ALLOY_TRACE_POINT(cw, c, 1);
-      // ---- scores of both heads, blocks j = cw, cw + 2, in place over CB ----
-      // S_h[t, s] = CB[t, s] exp(cum_h[t] - cum_h[s]) dt_h[s] for s <= t (+ D_h on s == t),
-      // block j of S_h stored as bf16 pairs in columns [32j + 16h, 32j + 16h + 16)
-      if (!waitw(bar(B_CB_FULL), ph, abort_flag, 32)) break;
-      ALLOY_TRACE_POINT(cw, c, 2);
-      tc_fence_after();
-#pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const int j = cw + 2 * jj;
-        uint32_t o[32];
-        if (j > q) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = 0u;
-        } else {
-          uint32_t r[32];
-          tmem_ld32(lane_base + T_CB + 32 * j, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float* cm = h ? cm1 : cm0;
-            const float cum_t = cm[t];
-            if (j < q) {
-              const float R = ex2_approx((cum_t - cm[32 * j + 31]) * kLog2e);
-              const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + 32 * j);
-#pragma unroll
-              for (int i4 = 0; i4 < 8; ++i4) {
-                const float4 f = cf4[i4];
-                o[16 * h + 2 * i4] = pack_bf16x2(__uint_as_float(r[4 * i4 + 0]) * R * f.x,
-                                                 __uint_as_float(r[4 * i4 + 1]) * R * f.y);
-                o[16 * h + 2 * i4 + 1] = pack_bf16x2(__uint_as_float(r[4 * i4 + 2]) * R * f.z,
-                                                     __uint_as_float(r[4 * i4 + 3]) * R * f.w);
-              }
-            } else {
-              const float* dtv = dt_s + (buf * 2 + h) * 128;
-              const float Dh = h ? D1 : D0;
-#pragma unroll
-              for (int i2 = 0; i2 < 16; ++i2) {
-                float v2[2];
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                  const int s = 32 * j + 2 * i2 + e;
-                  float v = 0.f;
-                  if (s <= t) v = __uint_as_float(r[2 * i2 + e]) * ex2_approx((cum_t - cm[s]) * kLog2e) * dtv[s];
-                  if (s == t) v += Dh;
-                  v2[e] = v;
-                }
-                o[16 * h + i2] = pack_bf16x2(v2[0], v2[1]);
-              }
-            }
-          }
-        }
-        tmem_st32(lane_base + T_CB + 32 * j, o);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_S_READY));
-      ALLOY_TRACE_POINT(cw, c, 3);
       // ---- X'_cw = X * dt * exp(cum[Q-1] - cum[s]) -> HX_cw ----
       if (!waitw(bar(B_YI_DONE), ph, abort_flag, 33)) break;
       ALLOY_TRACE_POINT(cw, c, 4);
@@ -714,62 +723,106 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
         const float* cm = cw ? cm1 : cm0;
         const float e = dt_s[(buf * 2 + cw) * 128 + t] * ex2_approx((cm[127] - cm[t]) * kLog2e);
         const uint32_t sX = base + OFF_X + (buf * 2 + cw) * 16384, sXp = base + OFF_HX + cw * 16384;
+        const uint64_t e2 = f2_splat(e);
 #pragma unroll
         for (int ch = 0; ch < 8; ++ch) {
           const uint4 u = ld_shared_v4(sX + sw_off(t, ch));
-          const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
-          uint32_t o4[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) o4[i] = pack_bf16x2(bf16_lo(wd[i]) * e, bf16_hi(wd[i]) * e);
-          st_shared_v4(sXp + sw_off(t, ch), o4[0], o4[1], o4[2], o4[3]);
+          st_shared_v4(sXp + sw_off(t, ch), f2_to_bf2(f2_mul(f2_from_bf2(u.x), e2)),
+                       f2_to_bf2(f2_mul(f2_from_bf2(u.y), e2)), f2_to_bf2(f2_mul(f2_from_bf2(u.z), e2)),
+                       f2_to_bf2(f2_mul(f2_from_bf2(u.w), e2)));
         }
       }
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_XP_READY));
       ALLOY_TRACE_POINT(cw, c, 5);
-      // ---- epilogue: y = Y + exp(cum[t]) Yi -> global (bf16) ----
-      // Each warp stages its 32 rows in its own rows of X[buf][cw] (read by
-      // Y(c) and X'(c), both done), then stores 4 full 128-byte rows per
-      // instruction.
-      if (!waitw(bar(B_Y_FULL), ph, abort_flag, 34)) break;
-      ALLOY_TRACE_POINT(cw, c, 6);
+      // ---- scores of both heads, blocks j = cw, cw + 2, in place over CB ----
+      // S_h[t, s] = CB[t, s] exp(cum_h[t] - cum_h[s]) dt_h[s] for s <= t (+ D_h on s == t),
+      // K-step k (sources 16k .. 16k+15) of S_h stored as bf16 pairs in columns [16k + 8h, 16k + 8h + 8)
+      if (!waitw(bar(B_CB_FULL), ph, abort_flag, 32)) break;
+      ALLOY_TRACE_POINT(cw, c, 2);
       tc_fence_after();
-      {
-        const int t0 = c * Q;
-        const float e = ex2_approx((cw ? cm1[t] : cm0[t]) * kLog2e);
-        const uint32_t stage = base + OFF_X + (buf * 2 + cw) * 16384 + q * 4096;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t ry[32], ri[32];
-          tmem_ld32(lane_base + T_Y + 64 * cw + 32 * half, ry);
-          tmem_ld32(lane_base + T_YI + 64 * cw + 32 * half, ri);
-          tmem_ld_wait();
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = cw + 2 * jj;
+        // block j in two 16-column halves (K-steps k = 2j + g): CB[t, 16k + i]
+        // becomes the bf16 pairs of S_h in columns 16k + 8h .. +8, inside the
+        // half just read, so no half overwrites CB values still to be read
 #pragma unroll
-          for (int g4 = 0; g4 < 4; ++g4) {
-            uint32_t o4[4];
+        for (int g = 0; g < 2; ++g) {
+          uint32_t o0[8], o1[8];
+          if (j > q) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int k0 = g4 * 8 + 2 * i;
-              o4[i] = pack_bf16x2(fmaf(e, __uint_as_float(ri[k0]), __uint_as_float(ry[k0])),
-                                  fmaf(e, __uint_as_float(ri[k0 + 1]), __uint_as_float(ry[k0 + 1])));
+            for (int i = 0; i < 8; ++i) o0[i] = o1[i] = 0u;
+          } else {
+            uint32_t r[16];
+            tmem_ld16(lane_base + T_CB + 32 * j + 16 * g, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint32_t* o = h ? o1 : o0;
+              const float* cm = h ? cm1 : cm0;
+              const float cum_t = cm[t];
+              const float cend = cm[32 * j + 31];
+              // exp(cum_t - cum_s) dt_s = R * cf[s] with R = exp(cum_t - cum[end of block j])
+              // and cf[s] = exp(cum[end] - cum[s]) dt_s.  Off the diagonal R <= 1;
+              // on the diagonal R <= exp(block range), safe when the range is <= 80.
+              const bool fact = j < q || (cm[32 * j] - cend) <= 80.f;
+              if (fact) {
+                const uint64_t R2 = f2_splat(ex2_approx((cum_t - cend) * kLog2e));
+                const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + 32 * j + 16 * g);
+#pragma unroll
+                for (int i4 = 0; i4 < 4; ++i4) {
+                  const float4 f = cf4[i4];
+                  uint64_t v0 = f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4]), __uint_as_float(r[4 * i4 + 1])), R2),
+                                       f2_pack(f.x, f.y));
+                  uint64_t v1 = f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4 + 2]), __uint_as_float(r[4 * i4 + 3])), R2),
+                                       f2_pack(f.z, f.w));
+                  if (j == q) {   // causal mask and D on the diagonal
+                    const float Dh = h ? D1 : D0;
+                    float e[4];
+                    f2_unpack(v0, e[0], e[1]);
+                    f2_unpack(v1, e[2], e[3]);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                      const int s = 32 * j + 16 * g + 4 * i4 + u;
+                      e[u] = s < t ? e[u] : (s == t ? e[u] + Dh : 0.f);
+                    }
+                    v0 = f2_pack(e[0], e[1]);
+                    v1 = f2_pack(e[2], e[3]);
+                  }
+                  o[2 * i4] = f2_to_bf2(v0);
+                  o[2 * i4 + 1] = f2_to_bf2(v1);
+                }
+              } else {
+                // wide decay range inside the block: exact exps per element
+                const float* dtv = dt_s + (buf * 2 + h) * 128;
+                const float Dh = h ? D1 : D0;
+#pragma unroll
+                for (int i2 = 0; i2 < 8; ++i2) {
+                  float v2[2];
+#pragma unroll
+                  for (int e = 0; e < 2; ++e) {
+                    const int s = 32 * j + 16 * g + 2 * i2 + e;
+                    float v = 0.f;
+                    if (s <= t) v = __uint_as_float(r[2 * i2 + e]) * ex2_approx((cum_t - cm[s]) * kLog2e) * dtv[s];
+                    if (s == t) v += Dh;
+                    v2[e] = v;
+                  }
+                  o[i2] = pack_bf16x2(v2[0], v2[1]);
+                }
+              }
             }
-            st_shared_v4(stage + sw_off(lane, half * 4 + g4), o4[0], o4[1], o4[2], o4[3]);
           }
+          tmem_st8(lane_base + T_CB + 32 * j + 16 * g, o0);
+          tmem_st8(lane_base + T_CB + 32 * j + 16 * g + 8, o1);
         }
-        __syncwarp();
-        __nv_bfloat16* ybase = a.y + (int64_t)b * a.y_sb + (int64_t)head * a.y_sh + (lane & 7) * 8;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int row = 4 * k + (lane >> 3);
-          const uint4 v = ld_shared_v4(stage + sw_off(row, lane & 7));
-          const int tt = t0 + q * 32 + row;
-          if (tt < L) *reinterpret_cast<uint4*>(ybase + (int64_t)tt * a.y_st) = v;
-        }
-        __syncwarp();
       }
+      tmem_st_wait();
       tc_fence_before();
-      if (lane == 0) mbar_arrive(bar(B_Y_EMPTY0 + buf));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_S_READY));
+      ALLOY_TRACE_POINT(cw, c, 3);
       ALLOY_TRACE_POINT(cw, c, 7);
     }
     // ---- final state -> ssm_out ----
