@@ -57,6 +57,7 @@ constexpr int kTmaWarp = 16;           // B/C half tiles
 constexpr int kMmaWarp = 17;
 constexpr int kRawWarp = 18;           // raw x rows
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kL2Ahead = 2;            // chunks of x and B/C prefetched into L2
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 // shared-memory map (bytes from the 1024-aligned base)
@@ -106,7 +107,7 @@ constexpr uint32_t T_YI = 384;    // + 64 h
 
 struct TcArgs {
   int B, L, H, N, G, K;
-  int head_begin, group_begin;
+  int head_begin, group_begin, group_count;
   const __nv_bfloat16* xbc; int64_t x_sb, x_st;
   const void* dt; int dt_bf16; int64_t dt_sb, dt_st, dt_sh;
   const float* conv_w; int64_t cw_sc, cw_sk;
@@ -194,85 +195,126 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
                : "r"(addr));
   return v;
 }
-__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
-}
 
 // ----------------------------------------------------------------------------
 // B/C conv + SiLU pre-pass
 // ----------------------------------------------------------------------------
-// bc[b, t, j], j in [0, 2*Gs*N): group gl = j / (2N), part = (j / N) % 2 (0 = B,
-// 1 = C), n = j % N; source channel H*P + part*G*N + (group_begin + gl)*N + n.
+// bc[b, t, j], j in [0, 2*Gs*N): part = j / (Gs*N) (0 = B, 1 = C), then group
+// gl and state index n of j % (Gs*N) = gl*N + n; source channel
+// H*P + part*G*N + group_begin*N + j % (Gs*N), i.e. the same column order as
+// xBC's B and C blocks, restricted to the selected groups.
+//
+// One CTA per (128-row tile, kBcW-column tile, batch row): a single tensor
+// copy brings rows [t0 - 3, t0 + 128) of the tile's columns into shared
+// memory (rows outside [0, L) arrive as zeros; rows before 0 are then taken
+// from the conv cache), and each thread convolves 8 adjacent columns over a
+// strip of rows with the last 3 inputs kept in registers.
+constexpr int kBcTileRows = 128;
+
+template <int W>   // tile width in columns: 256, 128 or 64
 __global__ void __launch_bounds__(256)
-bc_conv_kernel(const TcArgs a, __nv_bfloat16* __restrict__ bc, int ncols) {
+bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv_bfloat16* __restrict__ bc,
+               int ncols) {
+  constexpr int CG = W / 8;            // column groups of 8
+  constexpr int R = kBcTileRows * CG / 256;   // rows per thread
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar;
+  const uint32_t tile = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
+  const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&full_bar));
   const int b = blockIdx.z;
-  const int v = threadIdx.x & 31;
-  const int rg = threadIdx.x >> 5;
-  const int j = (blockIdx.x * 32 + v) * 8;
-  if (j >= ncols) return;
-  const int t_first = blockIdx.y * 64 + rg * 8;
-  if (t_first >= a.L) return;
-  const int N = a.N;
-  const int gl = j / (2 * N), part = (j / N) & 1, n = j % N;
-  const int c = a.H * P + part * a.G * N + (a.group_begin + gl) * N + n;
-  float w[8][4], bias[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) w[i][k] = a.conv_w[(int64_t)(c + i) * a.cw_sc + k * a.cw_sk];
-    bias[i] = a.conv_b ? a.conv_b[(int64_t)(c + i) * a.cb_s] : 0.f;
+  const int t0 = blockIdx.x * kBcTileRows;
+  const int j0 = blockIdx.y * W;
+  const int span = a.group_count * a.N;
+  const int part = j0 / span;
+  const int src0 = a.H * P + part * a.G * a.N + a.group_begin * a.N + (j0 - part * span);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    mbar_fence_init();
   }
-  // all 11 row loads in flight at once (addresses clamped, rows masked below)
-  uint4 u[11];
-  const __nv_bfloat16* src = a.xbc + (int64_t)b * a.x_sb + c;
-#pragma unroll
-  for (int r = 0; r < 11; ++r) {
-    const int t = min(max(t_first - 3 + r, 0), a.L - 1);
-    u[r] = ldg_nc_v4(src + (int64_t)t * a.x_st);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(bar, (kBcTileRows + 3) * W * 2);
+    tma_load_3d(tile, &src_map, bar, src0, t0 - 3, b);
   }
-  float raw[11][8];
+  const int cg = threadIdx.x % CG, strip = threadIdx.x / CG;
+  const int c = src0 + cg * 8;
+  // taps and bias as channel pairs (loaded while the copy is in flight)
+  uint64_t w2[4][4], b2[4];
 #pragma unroll
-  for (int r = 0; r < 11; ++r) {
-    const int t = t_first - 3 + r;
-    const uint32_t wd[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
+  for (int i = 0; i < 4; ++i) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      raw[r][2 * i] = bf16_lo(wd[i]);
-      raw[r][2 * i + 1] = bf16_hi(wd[i]);
+    for (int k = 0; k < 4; ++k)
+      w2[k][i] = f2_pack(a.conv_w[(int64_t)(c + 2 * i) * a.cw_sc + k * a.cw_sk],
+                         a.conv_w[(int64_t)(c + 2 * i + 1) * a.cw_sc + k * a.cw_sk]);
+    b2[i] = a.conv_b ? f2_pack(a.conv_b[(int64_t)(c + 2 * i) * a.cb_s], a.conv_b[(int64_t)(c + 2 * i + 1) * a.cb_s])
+                     : f2_splat(0.f);
+  }
+  // bounded wait for the tile; on timeout record the error and give the copy
+  // a second bounded period before the CTA leaves
+  {
+    const long long start = clock64();
+    bool ok = false;
+    while (!(ok = mbar_try_wait(bar, 0)) && clock64() - start < kWaitCycles) {
     }
-    if (t >= a.L) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) raw[r][i] = 0.f;
-    } else if (t < 0) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        raw[r][i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
-                                                          (int64_t)(a.K - 1 + t) * a.ci_sk +
-                                                          (int64_t)(c + i) * a.ci_sc])
-                              : 0.f;
+    if (!__syncthreads_and(ok)) {
+      if (threadIdx.x == 0) {
+        if (atomicCAS(&g_ssd_tc_error[0], 0u, 1u + 40u) == 0u) {
+          g_ssd_tc_error[1] = blockIdx.x;
+          g_ssd_tc_error[2] = blockIdx.y;
+        }
+        const long long again = clock64();
+        while (!mbar_try_wait(bar, 0) && clock64() - again < kWaitCycles) {
+        }
+      }
+      __syncthreads();
+      return;
     }
   }
-  __nv_bfloat16* dst = bc + ((int64_t)b * a.L + t_first) * ncols + j;
+  const int r0 = strip * R;            // first output row of this thread (tile-relative)
+  const uint32_t col = tile + cg * 16;
+  uint64_t win[3][4];
 #pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    if (t_first + r >= a.L) break;
+  for (int r = 0; r < 3; ++r) {
+    const int t = t0 + r0 - 3 + r;
+    if (t >= 0) {
+      uint32_t w0, w1, w2v, w3;
+      asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(w0), "=r"(w1), "=r"(w2v), "=r"(w3) : "r"(col + (r0 + r) * (W * 2)));
+      win[r][0] = f2_from_bf2(w0); win[r][1] = f2_from_bf2(w1);
+      win[r][2] = f2_from_bf2(w2v); win[r][3] = f2_from_bf2(w3);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float f[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          f[e] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb + (int64_t)(a.K - 1 + t) * a.ci_sk +
+                                                       (int64_t)(c + 2 * i + e) * a.ci_sc])
+                           : 0.f;
+        win[r][i] = f2_pack(f[0], f[1]);
+      }
+    }
+  }
+  __nv_bfloat16* dst = bc + ((int64_t)b * a.L + t0 + r0) * ncols + j0 + cg * 8;
+  const int nrows = min(R, a.L - (t0 + r0));
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (r >= nrows) break;
+    uint32_t u0, u1, u2, u3;
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(u0), "=r"(u1), "=r"(u2), "=r"(u3) : "r"(col + (r0 + r + 3) * (W * 2)));
+    const uint64_t x[4] = {f2_from_bf2(u0), f2_from_bf2(u1), f2_from_bf2(u2), f2_from_bf2(u3)};
     uint32_t o[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      float f[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int ch = 2 * i + e;
-        float acc = bias[ch];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) acc = fmaf(raw[r + k][ch], w[ch][k], acc);
-        f[e] = silu_fast(acc);
-      }
-      o[i] = pack_bf16x2(f[0], f[1]);
+      uint64_t acc = f2_fma(win[0][i], w2[0][i], b2[i]);
+      acc = f2_fma(win[1][i], w2[1][i], acc);
+      acc = f2_fma(win[2][i], w2[2][i], acc);
+      acc = f2_fma(x[i], w2[3][i], acc);
+      o[i] = f2_to_bf2(f2_silu(acc));
+      win[0][i] = win[1][i];
+      win[1][i] = win[2][i];
+      win[2][i] = x[i];
     }
     *reinterpret_cast<uint4*>(dst + (int64_t)r * ncols) = make_uint4(o[0], o[1], o[2], o[3]);
   }
@@ -355,9 +397,19 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
     if (lane == 0) {
       // raw x rows [c*Q - 3, c*Q + Q) of both heads' channels (rows outside
       // [0, L) arrive as zeros)
+      // the rows of the next kL2Ahead chunks are pulled into L2 ahead of
+      // their loads, so a load waits on L2 rather than on DRAM
+      for (int c = 1; c <= kL2Ahead && c < nchunks; ++c) {
+        tma_prefetch_3d(&x_map, h0 * P, c * Q - 3, b);
+        tma_prefetch_3d(&x_map, (h0 + 1) * P, c * Q - 3, b);
+      }
       int issued = 0;
       for (int c = 0; c < nchunks; ++c) {
         if (c > 0 && !wait1(bar(B_RAW_EMPTY), (c - 1) & 1, abort_flag, 1)) break;
+        if (c + kL2Ahead < nchunks) {
+          tma_prefetch_3d(&x_map, h0 * P, (c + kL2Ahead) * Q - 3, b);
+          tma_prefetch_3d(&x_map, (h0 + 1) * P, (c + kL2Ahead) * Q - 3, b);
+        }
         mbar_arrive_expect_tx(bar(B_RAW_FULL), 2 * kRawBytes);
         tma_load_3d(base + OFF_RAW, &x_map, bar(B_RAW_FULL), h0 * P, c * Q - 3, b);
         tma_load_3d(base + OFF_RAW + kRawStride, &x_map, bar(B_RAW_FULL), (h0 + 1) * P, c * Q - 3, b);
@@ -373,17 +425,28 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
     // ------------------------------------------------------------ TMA: B/C
     // (its own warp: a sleeping wait in one lane would hold up a role in another)
     if (lane == 0) {
+      const int gs = a.group_count;   // groups in the workspace: B blocks, then C blocks
       // B/C half tiles into the two-stage ring
+      for (int c = 1; c <= kL2Ahead && c < nchunks; ++c)
+        for (int k = 0; k < NK; ++k) {
+          tma_prefetch_3d(&bc_map, gl * N + 64 * k, c * Q, b);
+          tma_prefetch_3d(&bc_map, (gs + gl) * N + 64 * k, c * Q, b);
+        }
       int issued = 0;
       for (int c = 0; c < nchunks; ++c) {
+        if (c + kL2Ahead < nchunks)
+          for (int k = 0; k < NK; ++k) {
+            tma_prefetch_3d(&bc_map, gl * N + 64 * k, (c + kL2Ahead) * Q, b);
+            tma_prefetch_3d(&bc_map, (gs + gl) * N + 64 * k, (c + kL2Ahead) * Q, b);
+          }
         for (int k = 0; k < NK; ++k) {
           const int i = c * NK + k, slot = i & 1;
           if (i >= 2 && !wait1(bar(B_EMPTY0 + slot), ((i >> 1) - 1) & 1, abort_flag, 2)) goto bc_done;
           ALLOY_TRACE_POINT(2, c, k);
           mbar_arrive_expect_tx(bar(B_FULL0 + slot), kStageBytes);
           const uint32_t dst = base + OFF_STAGE + slot * kStageBytes;
-          tma_load_3d(dst, &bc_map, bar(B_FULL0 + slot), (gl * 2 + 0) * N + 64 * k, c * Q, b);
-          tma_load_3d(dst + 16384, &bc_map, bar(B_FULL0 + slot), (gl * 2 + 1) * N + 64 * k, c * Q, b);
+          tma_load_3d(dst, &bc_map, bar(B_FULL0 + slot), gl * N + 64 * k, c * Q, b);
+          tma_load_3d(dst + 16384, &bc_map, bar(B_FULL0 + slot), (gs + gl) * N + 64 * k, c * Q, b);
           ++issued;
         }
       }
@@ -585,44 +648,38 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
                            cw_all[512 + hh * 64 + vc4 * 4 + 2 * pp + 1]);
         }
         const uint32_t sX = base + OFF_X + (buf * 2 + hh) * 16384;
-        uint64_t win[4][2];   // the last 4 rows, as channel pairs
+        // all 19 input rows of this thread's strip in flight at once
+        uint32_t rw[19][2];
 #pragma unroll
-        for (int r = 0; r < 19; ++r) {
-          const int tt = t0 + strip * 16 - 3 + r;
+        for (int r = 0; r < 19; ++r)
+          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(rw[r][0]), "=r"(rw[r][1]) : "r"(raw_row0 + r * 128));
+        if (c == 0 && strip == 0) {
+          // rows before t = 0 come from the conv cache (zeros without one)
 #pragma unroll
-          for (int k = 0; k < 3; ++k) {
-            win[k][0] = win[k + 1][0];
-            win[k][1] = win[k + 1][1];
-          }
-          if (tt < 0) {
+          for (int r = 0; r < 3; ++r) {
             float f[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-              f[i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
-                                                           (int64_t)(a.K - 1 + tt) * a.ci_sk +
+              f[i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb + (int64_t)(a.K - 1 + r - 3) * a.ci_sk +
                                                            (int64_t)(xch + i) * a.ci_sc])
                                : 0.f;
-            win[3][0] = f2_pack(f[0], f[1]);
-            win[3][1] = f2_pack(f[2], f[3]);
-          } else {
-            uint32_t w0, w1;
-            asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(w0), "=r"(w1) : "r"(raw_row0 + r * 128));
-            win[3][0] = f2_from_bf2(w0);
-            win[3][1] = f2_from_bf2(w1);
+            rw[r][0] = pack_bf16x2(f[0], f[1]);
+            rw[r][1] = pack_bf16x2(f[2], f[3]);
           }
-          if (r >= 3) {
-            const int srow = strip * 16 + r - 3;
-            uint32_t o[2];
+        }
 #pragma unroll
-            for (int pp = 0; pp < 2; ++pp) {
-              uint64_t acc = b2[pp];
+        for (int r = 3; r < 19; ++r) {
+          const int srow = strip * 16 + r - 3;
+          uint32_t o[2];
 #pragma unroll
-              for (int k = 0; k < 4; ++k) acc = f2_fma(win[k][pp], w2[k][pp], acc);
-              o[pp] = (t0 + srow < L) ? f2_to_bf2(f2_silu(acc)) : 0u;
-            }
-            const uint32_t addr = sX + srow * 128 + ((((vc4 >> 1) ^ (srow & 7))) << 4) + ((vc4 & 1) << 3);
-            asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(addr), "r"(o[0]), "r"(o[1]) : "memory");
+          for (int pp = 0; pp < 2; ++pp) {
+            uint64_t acc = b2[pp];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc = f2_fma(f2_from_bf2(rw[r - 3 + k][pp]), w2[k][pp], acc);
+            o[pp] = (t0 + srow < L) ? f2_to_bf2(f2_silu(acc)) : 0u;
           }
+          const uint32_t addr = sX + srow * 128 + ((((vc4 >> 1) ^ (srow & 7))) << 4) + ((vc4 & 1) << 3);
+          asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(addr), "r"(o[0]), "r"(o[1]) : "memory");
         }
       }
       fence_async_smem();
@@ -906,7 +963,7 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
   TcArgs a;
   memset(&a, 0, sizeof(a));
   a.B = s.B; a.L = s.L; a.H = s.H; a.N = s.N; a.G = s.G; a.K = s.K;
-  a.head_begin = s.head_begin; a.group_begin = g0;
+  a.head_begin = s.head_begin; a.group_begin = g0; a.group_count = gs;
   a.xbc = static_cast<const __nv_bfloat16*>(s.xBC); a.x_sb = s.xbc_sb; a.x_st = s.xbc_st;
   a.dt = s.dt_raw; a.dt_bf16 = s.dt_bf16; a.dt_sb = s.dt_sb; a.dt_st = s.dt_st; a.dt_sh = s.dt_sh;
   a.conv_w = s.conv_w; a.cw_sc = s.cw_sc; a.cw_sk = s.cw_sk;
@@ -921,21 +978,41 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
   a.y = static_cast<__nv_bfloat16*>(s.y); a.y_sb = s.y_sb; a.y_st = s.y_st; a.y_sh = s.y_sh;
 
   // 1. B/C conv pre-pass into the workspace
+  PFN_cuTensorMapEncodeTiled_v12000 encode = get_encode_fn();
+  if (!encode) return fail(ALLOY_ERR_CUDA, "ssd_tc: cuTensorMapEncodeTiled unavailable");
+  const cuuint32_t estride[3] = {1, 1, 1};
+  const cuuint64_t xd[3] = {(cuuint64_t)(s.H * 64 + 2 * s.G * s.N), (cuuint64_t)s.L, (cuuint64_t)s.B};
+  const cuuint64_t xs[2] = {(cuuint64_t)s.xbc_st * 2, (cuuint64_t)s.xbc_sb * 2};
   const int ncols = 2 * gs * s.N;
   __nv_bfloat16* bc = static_cast<__nv_bfloat16*>(workspace);
   {
-    dim3 grid((ncols / 8 + 31) / 32, (s.L + 63) / 64, s.B);
-    bc_conv_kernel<<<grid, 256, 0, stream>>>(a, bc, ncols);
+    // widest tile dividing one of the B / C blocks (gs * N is a multiple of 64)
+    const int span = gs * s.N;
+    const int W = span % 256 == 0 ? 256 : span % 128 == 0 ? 128 : 64;
+    CUtensorMap smap;
+    const cuuint32_t sbox[3] = {(cuuint32_t)W, (cuuint32_t)(kBcTileRows + 3), 1};
+    CUresult r = encode(&smap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(s.xBC), xd, xs, sbox,
+                        estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(ALLOY_ERR_CUDA, "ssd_tc: cuTensorMapEncodeTiled (B/C tile) failed (%d)", (int)r);
+    dim3 grid((s.L + kBcTileRows - 1) / kBcTileRows, ncols / W, s.B);
+    const int smem = (kBcTileRows + 3) * W * 2;
+    if (W == 256) {
+      ALLOY_CUDA(cudaFuncSetAttribute(bc_conv_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      bc_conv_kernel<256><<<grid, 256, smem, stream>>>(smap, a, bc, ncols);
+    } else if (W == 128) {
+      bc_conv_kernel<128><<<grid, 256, smem, stream>>>(smap, a, bc, ncols);
+    } else {
+      bc_conv_kernel<64><<<grid, 256, smem, stream>>>(smap, a, bc, ncols);
+    }
     ALLOY_TRY(check_launch("bc_conv_kernel"));
   }
   // 2. tensor map over the workspace [B][L][ncols], box 64 columns x 128 rows
-  PFN_cuTensorMapEncodeTiled_v12000 encode = get_encode_fn();
-  if (!encode) return fail(ALLOY_ERR_CUDA, "ssd_tc: cuTensorMapEncodeTiled unavailable");
   CUtensorMap map;
   const cuuint64_t gdim[3] = {(cuuint64_t)ncols, (cuuint64_t)s.L, (cuuint64_t)s.B};
   const cuuint64_t gstride[2] = {(cuuint64_t)ncols * 2, (cuuint64_t)ncols * 2 * s.L};
   const cuuint32_t box[3] = {64, (cuuint32_t)Q, 1};
-  const cuuint32_t estride[3] = {1, 1, 1};
   CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, bc, gdim, gstride, box, estride,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -943,8 +1020,6 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
   // 3. tensor map over xBC for the raw x rows: box 64 channels x (Q + 3) rows
   CUtensorMap xmap;
   {
-    const cuuint64_t xd[3] = {(cuuint64_t)(s.H * 64 + 2 * s.G * s.N), (cuuint64_t)s.L, (cuuint64_t)s.B};
-    const cuuint64_t xs[2] = {(cuuint64_t)s.xbc_st * 2, (cuuint64_t)s.xbc_sb * 2};
     const cuuint32_t xbox[3] = {64, (cuuint32_t)kRawRows, 1};
     r = encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(s.xBC), xd, xs, xbox,
                estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
