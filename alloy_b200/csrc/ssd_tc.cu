@@ -4,7 +4,7 @@
 //
 // Two launches per call:
 //  1. bc_conv_kernel: conv1d + SiLU of the B and C columns of the selected
-//     head groups -> bf16 workspace [B, L, groups, {B,C}, N].  Every head of a
+//     head groups -> bf16 workspace [B, L, {B,C}, groups, N].  Every head of a
 //     group reads the same B/C, so they are produced once instead of once per
 //     head pair.
 //  2. ssd_tc_kernel: one CTA per (batch row, pair of heads of one group),
@@ -19,15 +19,16 @@
 //        state   = exp(cum[Q-1]) state + X'^T B,  X'[s] = X[s] dt_s exp(cum[Q-1]-cum[s])
 //     X is the unscaled conv+SiLU output of the pair's x channels (bf16,
 //     produced in the CTA); B/C tiles arrive by TMA (128-byte swizzle) into a
-//     two-stage ring of 64-column halves.  The state of both heads is one
-//     128 x N fp32 TMEM accumulator with rows (head, p): its update is a
-//     single M = 128 MMA per N-half.
+//     two-stage ring of 64-column halves; raw x rows (with the 3-row conv
+//     halo) arrive by TMA per head.  The state of both heads is one 128 x N
+//     fp32 TMEM accumulator with rows (head, p): its update is a single
+//     M = 128, N = d_state MMA chain.
 //
-// Warp roles (320 threads): warps 0-3 / 4-7 = warpgroup of head 0 / 1 (conv,
-// dt/cumsum, scores S, X', state copy, epilogue); warp 8 = TMA producer;
-// warp 9 = TMEM allocator and MMA issuer.  Every mbarrier wait is bounded:
-// on timeout the CTA records an error word, drains its in-flight copies and
-// MMAs, frees its tensor memory and exits.
+// Warp roles: two consumer warpgroups (state copy, X', scores), two producer
+// warpgroups (dt/cumsum, x conv, epilogue), a B/C TMA warp and an MMA warp;
+// see the kernel.  Every mbarrier wait is bounded: on timeout the CTA records
+// an error word, drains its in-flight copies and MMAs, frees its tensor memory
+// and exits.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -52,10 +53,11 @@ using namespace tc;
 
 constexpr int Q = 128;                 // chunk length (UMMA M)
 constexpr int P = 64;                  // head dim
-constexpr int kThreads = 608;          // 19 warps
+constexpr int kThreads = 640;          // 20 warps: 4 compute warpgroups + 1 role warpgroup
+constexpr int kRoleRegs = 64;          // registers per thread after the split: role warpgroup
+constexpr int kComputeRegs = 104;      // compute warpgroups (4 x 128 x 112 + 128 x 24 <= 640 x 96)
 constexpr int kTmaWarp = 16;           // B/C half tiles
 constexpr int kMmaWarp = 17;
-constexpr int kRawWarp = 18;           // raw x rows
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kL2Ahead = 2;            // chunks of x and B/C prefetched into L2
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
@@ -84,8 +86,7 @@ constexpr uint32_t kSmemBytes = OFF_ABORT + 16 + 1024;  // + alignment slack
 // barrier ids (counts in the kernel's init table)
 enum {
   B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1,   // B/C half-tile ring (TMA <-> MMA)
-  B_RAW_FULL,                                 // TMA -> producers: raw x rows of a chunk
-  B_RAW_EMPTY,                                // producers -> TMA (8 warps)
+  B_RAW_FULL0, B_RAW_FULL1,                   // raw x rows of a chunk, per head (TMA issued by the producers)
   B_X_READY0, B_X_READY1,                     // producers -> consumers: X, cum, dt, cf (per buffer)
   B_CB_FULL,                                  // MMA -> consumers: CB in TMEM
   B_HBF_READY,                                // consumers -> MMA: H copies written, state scaled
@@ -323,7 +324,8 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
 // ----------------------------------------------------------------------------
 // the SSD kernel
 // ----------------------------------------------------------------------------
-// Roles (19 warps):
+// Roles (20 warps, launched with 96 registers a thread; the role warpgroup
+// hands registers to the compute warpgroups with setmaxnreg):
 //   warps 0-7   consumers: warpgroup cw = 0/1.  Per chunk: the bf16 copy of
 //               the state and its decay (state columns split by warpgroup),
 //               X' of head cw, and the scores S of both heads for the
@@ -332,11 +334,13 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
 //   warps 8-15  producers: warpgroup ph = 0/1 for head ph of the pair.  Per
 //               chunk: dt, cumulative log decay and column factors, the conv +
 //               SiLU of the head's x channels from the TMA-staged raw rows into
-//               the double-buffered X, then the epilogue (y) of the previous
-//               chunk.  They run up to one chunk ahead of the consumers.
+//               the double-buffered X (one thread of the group issues the raw
+//               rows' copy for the next chunk once the group is done with
+//               them), then the epilogue (y) of the previous chunk.  They run
+//               up to one chunk ahead of the consumers.
 //   warp 16     TMA of the B/C half tiles.
 //   warp 17     TMEM allocation and the MMA issue (one thread).
-//   warp 18     TMA of the raw x rows.
+//   warps 18-19 no work (they complete the role warpgroup).
 template <int N>
 __global__ void __launch_bounds__(kThreads, 1)
 ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant__ CUtensorMap x_map,
@@ -367,7 +371,7 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    const int counts[NBAR] = {1, 1, 1, 1, 1, 8, 8, 8, 1, 8, 1, 8, 1, 8, 1, 8, 8, 4, 4, 4, 4, 1, 0, 0};
+    const int counts[NBAR] = {1, 1, 1, 1, 1, 1, 8, 8, 1, 8, 1, 8, 1, 8, 1, 8, 8, 4, 4, 4, 4, 1, 0, 0};
     for (int i = 0; i < NBAR; ++i)
       if (counts[i]) mbar_init(bar(i), counts[i]);
     mbar_fence_init();
@@ -377,7 +381,7 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
     tmem_relinquish();
   }
   if (warp == kTmaWarp && lane == 0) prefetch_tmap(&bc_map);
-  if (warp == kRawWarp && lane == 0) prefetch_tmap(&x_map);
+  if (warp == 8 && lane == 0) prefetch_tmap(&x_map);
   // x conv weights of both heads, [head][channel][tap] and bias [head][channel]
   // (each producer thread copies its 4 channels' taps into registers once)
   if (threadIdx.x < 128) {
@@ -392,511 +396,525 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
   tc_fence_after();
   const uint32_t tmem = *tmem_ptr;
 
-  if (warp == kRawWarp) {
-    // ------------------------------------------------------------ TMA: raw x
-    if (lane == 0) {
-      // raw x rows [c*Q - 3, c*Q + Q) of both heads' channels (rows outside
-      // [0, L) arrive as zeros)
-      // the rows of the next kL2Ahead chunks are pulled into L2 ahead of
-      // their loads, so a load waits on L2 rather than on DRAM
-      for (int c = 1; c <= kL2Ahead && c < nchunks; ++c) {
-        tma_prefetch_3d(&x_map, h0 * P, c * Q - 3, b);
-        tma_prefetch_3d(&x_map, (h0 + 1) * P, c * Q - 3, b);
-      }
-      int issued = 0;
-      for (int c = 0; c < nchunks; ++c) {
-        if (c > 0 && !wait1(bar(B_RAW_EMPTY), (c - 1) & 1, abort_flag, 1)) break;
-        if (c + kL2Ahead < nchunks) {
-          tma_prefetch_3d(&x_map, h0 * P, (c + kL2Ahead) * Q - 3, b);
-          tma_prefetch_3d(&x_map, (h0 + 1) * P, (c + kL2Ahead) * Q - 3, b);
-        }
-        mbar_arrive_expect_tx(bar(B_RAW_FULL), 2 * kRawBytes);
-        tma_load_3d(base + OFF_RAW, &x_map, bar(B_RAW_FULL), h0 * P, c * Q - 3, b);
-        tma_load_3d(base + OFF_RAW + kRawStride, &x_map, bar(B_RAW_FULL), (h0 + 1) * P, c * Q - 3, b);
-        ++issued;
-      }
-      if (issued > 0) {
-        const long long t0 = clock64();
-        while (!mbar_try_wait(bar(B_RAW_FULL), (issued - 1) & 1) && clock64() - t0 < kWaitCycles) {
-        }
-      }
-    }
-  } else if (warp == kTmaWarp) {
-    // ------------------------------------------------------------ TMA: B/C
-    // (its own warp: a sleeping wait in one lane would hold up a role in another)
-    if (lane == 0) {
-      const int gs = a.group_count;   // groups in the workspace: B blocks, then C blocks
-      // B/C half tiles into the two-stage ring
-      for (int c = 1; c <= kL2Ahead && c < nchunks; ++c)
-        for (int k = 0; k < NK; ++k) {
-          tma_prefetch_3d(&bc_map, gl * N + 64 * k, c * Q, b);
-          tma_prefetch_3d(&bc_map, (gs + gl) * N + 64 * k, c * Q, b);
-        }
-      int issued = 0;
-      for (int c = 0; c < nchunks; ++c) {
-        if (c + kL2Ahead < nchunks)
+  if (warp >= 16) {
+    // role warpgroup: hand registers to the compute warpgroups
+    reg_dealloc<kRoleRegs>();
+    if (warp == kTmaWarp) {
+      // ------------------------------------------------------------ TMA: B/C
+      // (its own warp: a sleeping wait in one lane would hold up a role in another)
+      if (lane == 0) {
+        const int gs = a.group_count;   // groups in the workspace: B blocks, then C blocks
+        // B/C half tiles into the two-stage ring
+        for (int c = 1; c <= kL2Ahead && c < nchunks; ++c)
           for (int k = 0; k < NK; ++k) {
-            tma_prefetch_3d(&bc_map, gl * N + 64 * k, (c + kL2Ahead) * Q, b);
-            tma_prefetch_3d(&bc_map, (gs + gl) * N + 64 * k, (c + kL2Ahead) * Q, b);
+            tma_prefetch_3d(&bc_map, gl * N + 64 * k, c * Q, b);
+            tma_prefetch_3d(&bc_map, (gs + gl) * N + 64 * k, c * Q, b);
           }
-        for (int k = 0; k < NK; ++k) {
-          const int i = c * NK + k, slot = i & 1;
-          if (i >= 2 && !wait1(bar(B_EMPTY0 + slot), ((i >> 1) - 1) & 1, abort_flag, 2)) goto bc_done;
-          ALLOY_TRACE_POINT(2, c, k);
-          mbar_arrive_expect_tx(bar(B_FULL0 + slot), kStageBytes);
-          const uint32_t dst = base + OFF_STAGE + slot * kStageBytes;
-          tma_load_3d(dst, &bc_map, bar(B_FULL0 + slot), gl * N + 64 * k, c * Q, b);
-          tma_load_3d(dst + 16384, &bc_map, bar(B_FULL0 + slot), (gs + gl) * N + 64 * k, c * Q, b);
-          ++issued;
+        int issued = 0;
+        for (int c = 0; c < nchunks; ++c) {
+          if (c + kL2Ahead < nchunks)
+            for (int k = 0; k < NK; ++k) {
+              tma_prefetch_3d(&bc_map, gl * N + 64 * k, (c + kL2Ahead) * Q, b);
+              tma_prefetch_3d(&bc_map, (gs + gl) * N + 64 * k, (c + kL2Ahead) * Q, b);
+            }
+          for (int k = 0; k < NK; ++k) {
+            const int i = c * NK + k, slot = i & 1;
+            if (i >= 2 && !wait1(bar(B_EMPTY0 + slot), ((i >> 1) - 1) & 1, abort_flag, 2)) goto bc_done;
+            ALLOY_TRACE_POINT(2, c, k);
+            mbar_arrive_expect_tx(bar(B_FULL0 + slot), kStageBytes);
+            const uint32_t dst = base + OFF_STAGE + slot * kStageBytes;
+            tma_load_3d(dst, &bc_map, bar(B_FULL0 + slot), gl * N + 64 * k, c * Q, b);
+            tma_load_3d(dst + 16384, &bc_map, bar(B_FULL0 + slot), (gs + gl) * N + 64 * k, c * Q, b);
+            ++issued;
+          }
+        }
+      bc_done:
+        for (int i = max(0, issued - 2); i < issued; ++i) {
+          const long long t0 = clock64();
+          while (!mbar_try_wait(bar(B_FULL0 + (i & 1)), (i >> 1) & 1) && clock64() - t0 < kWaitCycles) {
+          }
         }
       }
-    bc_done:
-      for (int i = max(0, issued - 2); i < issued; ++i) {
-        const long long t0 = clock64();
-        while (!mbar_try_wait(bar(B_FULL0 + (i & 1)), (i >> 1) & 1) && clock64() - t0 < kWaitCycles) {
+    } else if (warp == kMmaWarp) {
+      // ------------------------------------------------------------ MMA issuer
+      // per chunk: CB -> Yi (after the state copy) -> state update (after X') -> Y (scores from TMEM)
+      if (lane == 0) {
+        constexpr uint32_t ID_CB = idesc_bf16(128, 128, 0, 0);
+        constexpr uint32_t ID_YI = idesc_bf16(128, 128, 0, 0);
+        constexpr uint32_t ID_ST = idesc_bf16(128, N, 1, 1);
+        constexpr uint32_t ID_Y = idesc_bf16(128, 64, 0, 1);
+        for (int c = 0; c < nchunks; ++c) {
+          const uint32_t ph = c & 1, pph = (c - 1) & 1;
+          const int buf = c & 1;
+          // CB = C B^T over the N halves; the region held the previous scores,
+          // so Y(c-1) must have completed
+          for (int k = 0; k < NK; ++k) {
+            const int i = c * NK + k, slot = i & 1;
+            if (!wait1(bar(B_FULL0 + slot), (i >> 1) & 1, abort_flag, 3)) goto mma_done;
+            ALLOY_TRACE_POINT(3, c, 5 + k);
+            if (k == 0 && c > 0 && !wait1(bar(B_Y_FULL), pph, abort_flag, 4)) goto mma_done;
+            tc_fence_after();
+            const uint32_t sB = base + OFF_STAGE + slot * kStageBytes, sC = sB + 16384;
+  #pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(tmem + T_CB, sw128_desc(sC + 32 * kk, 16, 1024),
+                        sw128_desc(sB + 32 * kk, 16, 1024), ID_CB, (k | kk) != 0);
+          }
+          umma_commit(bar(B_CB_FULL));
+          ALLOY_TRACE_POINT(3, c, 0);
+          // Yi = C [H_0; H_1]^T for both heads at once (N = 128 rows (h, p))
+          if (c > 0 && !wait1(bar(B_Y_EMPTY0 + (buf ^ 1)), ((c - 1) >> 1) & 1, abort_flag, 5)) goto mma_done;
+          if (!wait1(bar(B_HBF_READY), ph, abort_flag, 6)) goto mma_done;
+          tc_fence_after();
+          for (int k = 0; k < NK; ++k) {
+            const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
+            const uint32_t sH = base + OFF_HX + k * 16384;
+  #pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(tmem + T_YI, sw128_desc(sC + 32 * kk, 16, 1024),
+                        sw128_desc(sH + 32 * kk, 16, 1024), ID_YI, (k | kk) != 0);
+          }
+          umma_commit(bar(B_YI_DONE));
+          ALLOY_TRACE_POINT(3, c, 1);
+          // state: ST[(h,p), n] += X'^T B over s, per N half; releases the stages
+          if (!wait1(bar(B_XP_READY), ph, abort_flag, 8)) goto mma_done;
+          ALLOY_TRACE_POINT(3, c, 9);
+          tc_fence_after();
+          {
+            // N = d_state in one chain: for d_state 128 the two 64-column halves of B
+            // sit in the two stage slots, 32 KB apart (the MN-atom stride)
+            const int slot0 = (c * NK) & 1;
+            const uint32_t sB = base + OFF_STAGE + slot0 * kStageBytes;
+            const uint32_t sXp = base + OFF_HX;
+  #pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_bf16(tmem + T_ST, sw128_desc(sXp + 2048 * kk, 16384, 1024),
+                        sw128_desc(sB + 2048 * kk, kStageBytes, 1024), ID_ST, 1);
+            for (int k = 0; k < NK; ++k) umma_commit(bar(B_EMPTY0 + ((c * NK + k) & 1)));
+          }
+          umma_commit(bar(B_ST_DONE));
+          ALLOY_TRACE_POINT(3, c, 10);
+          // Y_h = S_h X_h, S_h (bf16 pairs) read from tensor memory
+          if (!wait1(bar(B_S_READY), ph, abort_flag, 7)) goto mma_done;
+          ALLOY_TRACE_POINT(3, c, 8);
+          tc_fence_after();
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t sX = base + OFF_X + (buf * 2 + h) * 16384;
+  #pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_bf16_ta(tmem + T_Y + 64 * h, tmem + T_CB + 16 * kk + 8 * h,
+                           sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
+          }
+          umma_commit(bar(B_Y_FULL));
+          ALLOY_TRACE_POINT(3, c, 2);
+          ALLOY_TRACE_POINT(3, c, 3);
+        }
+      mma_done:
+        // wait (bounded) for every MMA this thread issued
+        umma_commit(bar(B_DRAIN));
+        {
+          const long long t0 = clock64();
+          while (!mbar_try_wait(bar(B_DRAIN), 0) && clock64() - t0 < kWaitCycles) {
+          }
         }
       }
     }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
-    // per chunk: CB -> Yi (after the state copy) -> state update (after X') -> Y (scores from TMEM)
-    if (lane == 0) {
-      constexpr uint32_t ID_CB = idesc_bf16(128, 128, 0, 0);
-      constexpr uint32_t ID_YI = idesc_bf16(128, 128, 0, 0);
-      constexpr uint32_t ID_ST = idesc_bf16(128, N, 1, 1);
-      constexpr uint32_t ID_Y = idesc_bf16(128, 64, 0, 1);
+  } else {
+    reg_alloc<kComputeRegs>();
+    if (warp >= 8) {
+      // ------------------------------------------------------------ producers (warps 8-15)
+      const int hh = (warp - 8) >> 2;     // head of the pair
+      const int q = warp & 3;
+      const int t = q * 32 + lane;
+      const int head = h0 + hh;
+      const float A = -expf(a.A_log[(int64_t)head * a.al_s]);
+      const float dtb = a.dt_bias[(int64_t)head * a.dtb_s];
+      // this thread's conv work: 4 channels (4*vc4 .. 4*vc4+3) x 16 rows (16*strip ..)
+      const int vc4 = t & 15, strip = t >> 4;
+      const int xch = head * P + vc4 * 4;
+      const uint32_t raw_row0 = base + OFF_RAW + hh * kRawStride + (uint32_t)(strip * 16) * 128 + vc4 * 8;
+      const int64_t dt_row = (int64_t)b * a.dt_sb + (int64_t)head * a.dt_sh;
+      uint32_t dt_bits = 0;   // raw dt of the chunk about to be produced (converted when used)
+      auto load_dt = [&](int cc) {
+        const int64_t di = dt_row + (int64_t)min(cc * Q + t, L - 1) * a.dt_st;
+        if (a.dt_bf16)
+          asm volatile("ld.global.nc.u16 %0, [%1];" : "=r"(dt_bits)
+                       : "l"(static_cast<const __nv_bfloat16*>(a.dt) + di));
+        else
+          asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(dt_bits)
+                       : "l"(static_cast<const float*>(a.dt) + di));
+      };
+      // ---- epilogue of chunk cc (head hh): y = Y + exp(cum[t]) Yi -> global ----
+      // Each warp stages its 32 rows in its own rows of X[cc&1][hh] (read by
+      // Y(cc) and X'(cc), both complete once Y_FULL(cc) is), then stores 4
+      // full 128-byte rows per instruction.
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+      auto epilogue = [&](int cc) -> bool {
+        const int ebuf = cc & 1;
+        if (!waitw(bar(B_Y_FULL), cc & 1, abort_flag, 34)) return false;
+        tc_fence_after();
+        const int t0 = cc * Q;
+        const float e = ex2_approx(cum_s[(ebuf * 2 + hh) * 128 + t] * kLog2e);
+        const uint32_t stage = base + OFF_X + (ebuf * 2 + hh) * 16384 + q * 4096;
+        const uint64_t e2 = f2_splat(e);
+  #pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          uint32_t ry[16], ri[16];
+          tmem_ld16(lane_base + T_Y + 64 * hh + 16 * qq, ry);
+          tmem_ld16(lane_base + T_YI + 64 * hh + 16 * qq, ri);
+          tmem_ld_wait();
+  #pragma unroll
+          for (int g2 = 0; g2 < 2; ++g2) {
+            uint32_t o4[4];
+  #pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int k0 = g2 * 8 + 2 * i;
+              o4[i] = f2_to_bf2(f2_fma(f2_pack(__uint_as_float(ri[k0]), __uint_as_float(ri[k0 + 1])), e2,
+                                       f2_pack(__uint_as_float(ry[k0]), __uint_as_float(ry[k0 + 1]))));
+            }
+            st_shared_v4(stage + sw_off(lane, qq * 2 + g2), o4[0], o4[1], o4[2], o4[3]);
+          }
+        }
+        __syncwarp();
+        __nv_bfloat16* ybase = a.y + (int64_t)b * a.y_sb + (int64_t)head * a.y_sh + (lane & 7) * 8;
+  #pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int row = 4 * k + (lane >> 3);
+          const uint4 v = ld_shared_v4(stage + sw_off(row, lane & 7));
+          const int tt = t0 + q * 32 + row;
+          if (tt < L) *reinterpret_cast<uint4*>(ybase + (int64_t)tt * a.y_st) = v;
+        }
+        __syncwarp();
+        tc_fence_before();
+        if (lane == 0) mbar_arrive(bar(B_Y_EMPTY0 + ebuf));
+        return true;
+      };
+      // raw x rows [c*Q - 3, c*Q + Q) of this head's channels (rows outside
+      // [0, L) arrive as zeros), issued by one thread of the warpgroup once its
+      // four warps are done with the previous chunk's rows; the rows of the
+      // next kL2Ahead chunks are pulled into L2 ahead of their loads
+      const bool raw_issuer = q == 0 && lane == 0;
+      const uint32_t raw_bar = bar(B_RAW_FULL0 + hh), raw_dst = base + OFF_RAW + hh * kRawStride;
+      int raw_issued = 0;
+      auto issue_raw = [&](int cc) {
+        if (cc + kL2Ahead < nchunks) tma_prefetch_3d(&x_map, head * P, (cc + kL2Ahead) * Q - 3, b);
+        mbar_arrive_expect_tx(raw_bar, kRawBytes);
+        tma_load_3d(raw_dst, &x_map, raw_bar, head * P, cc * Q - 3, b);
+        ++raw_issued;
+      };
+      if (raw_issuer) {
+        for (int cc = 1; cc < kL2Ahead && cc < nchunks; ++cc) tma_prefetch_3d(&x_map, head * P, cc * Q - 3, b);
+        issue_raw(0);
+      }
+      uint32_t wg_uses = 0;
+      load_dt(0);
+      bool ok = true;
+      for (int c = 0; ok && c < nchunks; ++c) {
+        const int buf = c & 1;
+        const int t0 = c * Q;
+        // X[buf] and cum/dt/cf[buf] held chunk c-2, whose epilogue this warpgroup
+        // finished last iteration (after Y(c-2), and so after X'(c-2) and S(c-2))
+        ALLOY_TRACE_POINT(4 + hh, c, 0);
+        // ---- dt, warp-local scan, column factors ----
+        const float dt = t0 + t < L
+            ? softplus_f32((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
+            : 0.f;
+        if (c + 1 < nchunks) load_dt(c + 1);
+        float v = A * dt;
+  #pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float u = __shfl_up_sync(0xffffffffu, v, o);
+          if (lane >= o) v += u;
+        }
+        float* cm = cum_s + (buf * 2 + hh) * 128;
+        cf_s[(buf * 2 + hh) * 128 + t] = ex2_approx((__shfl_sync(0xffffffffu, v, 31) - v) * kLog2e) * dt;
+        dt_s[(buf * 2 + hh) * 128 + t] = dt;
+        if (lane == 31) wsum[(buf * 2 + hh) * 4 + q] = v;
+        // ---- conv + SiLU of this head's x channels -> X[buf][hh] (bf16, unscaled) ----
+        if (!waitw(raw_bar, c & 1, abort_flag, 21)) break;
+        ALLOY_TRACE_POINT(4 + hh, c, 1);
+        {
+          // taps and bias of this thread's channel pairs (0,1), (2,3), reloaded
+          // per chunk so they are not live across the epilogue
+          uint64_t w2[4][2], b2[2];
+  #pragma unroll
+          for (int pp = 0; pp < 2; ++pp) {
+            const float* w0 = cw_all + (hh * 64 + vc4 * 4 + 2 * pp) * 4;
+  #pragma unroll
+            for (int k = 0; k < 4; ++k) w2[k][pp] = f2_pack(w0[k], w0[4 + k]);
+            b2[pp] = f2_pack(cw_all[512 + hh * 64 + vc4 * 4 + 2 * pp],
+                             cw_all[512 + hh * 64 + vc4 * 4 + 2 * pp + 1]);
+          }
+          const uint32_t sX = base + OFF_X + (buf * 2 + hh) * 16384;
+          // all 19 input rows of this thread's strip in flight at once
+          uint32_t rw[19][2];
+  #pragma unroll
+          for (int r = 0; r < 19; ++r)
+            asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(rw[r][0]), "=r"(rw[r][1]) : "r"(raw_row0 + r * 128));
+          if (c == 0 && strip == 0) {
+            // rows before t = 0 come from the conv cache (zeros without one)
+  #pragma unroll
+            for (int r = 0; r < 3; ++r) {
+              float f[4];
+  #pragma unroll
+              for (int i = 0; i < 4; ++i)
+                f[i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb + (int64_t)(a.K - 1 + r - 3) * a.ci_sk +
+                                                             (int64_t)(xch + i) * a.ci_sc])
+                                 : 0.f;
+              rw[r][0] = pack_bf16x2(f[0], f[1]);
+              rw[r][1] = pack_bf16x2(f[2], f[3]);
+            }
+          }
+  #pragma unroll
+          for (int r = 3; r < 19; ++r) {
+            const int srow = strip * 16 + r - 3;
+            uint32_t o[2];
+  #pragma unroll
+            for (int pp = 0; pp < 2; ++pp) {
+              uint64_t acc = b2[pp];
+  #pragma unroll
+              for (int k = 0; k < 4; ++k) acc = f2_fma(f2_from_bf2(rw[r - 3 + k][pp]), w2[k][pp], acc);
+              o[pp] = (t0 + srow < L) ? f2_to_bf2(f2_silu(acc)) : 0u;
+            }
+            const uint32_t addr = sX + srow * 128 + ((((vc4 >> 1) ^ (srow & 7))) << 4) + ((vc4 & 1) << 3);
+            asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(addr), "r"(o[0]), "r"(o[1]) : "memory");
+          }
+        }
+        fence_async_smem();
+        ALLOY_TRACE_POINT(4 + hh, c, 2);
+        // ---- prefix over the warps -> cumulative log decay ----
+        // (wsum is double-buffered by chunk parity: its next write, two chunks
+        // on, comes after every warp has passed the next chunk's sync)
+        if (!warps_sync(bar(B_PWG0 + hh), wg_uses, abort_flag, 22)) break;
+        // every warp of the group has read this chunk's raw rows
+        if (raw_issuer && c + 1 < nchunks) issue_raw(c + 1);
+        for (int i = 0; i < q; ++i) v += wsum[(buf * 2 + hh) * 4 + i];
+        cm[t] = v;
+        // X, cum, dt, cf of chunk c are ready
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_X_READY0 + buf));
+        ALLOY_TRACE_POINT(4 + hh, c, 3);
+        // the previous chunk's output, while the tensor cores and consumers work on this one
+        if (c > 0 && !epilogue(c - 1)) break;
+        ALLOY_TRACE_POINT(4 + hh, c, 4);
+      }
+      if (!*abort_flag && nchunks > 0) epilogue(nchunks - 1);
+      if (raw_issuer && raw_issued > 0) {
+        // the last raw copy has landed (at once unless a wait above gave up)
+        const long long t0 = clock64();
+        while (!mbar_try_wait(raw_bar, (raw_issued - 1) & 1) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    } else {
+      // ------------------------------------------------------------ consumers
+      const int cw = warp >> 2;           // consumer warpgroup
+      const int q = warp & 3;             // TMEM lane quadrant
+      const int t = q * 32 + lane;        // row of this thread (t, s or (h,p))
+      const float D0 = a.Dp ? a.Dp[(int64_t)h0 * a.d_s] : 0.f;
+      const float D1 = a.Dp ? a.Dp[(int64_t)(h0 + 1) * a.d_s] : 0.f;
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+      // state rows: r = t -> head hr = t / 64, p = t % 64; this warpgroup owns
+      // state columns [cw * N/2, (cw+1) * N/2)
+      const int hr = t >> 6, pr = t & 63;
+
+      // initial state -> TMEM
+  #pragma unroll 1
+      for (int cc = 0; cc < NHALF / 32; ++cc) {
+        uint32_t r[32];
+  #pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int n = cw * NHALF + cc * 32 + i;
+          const float v = a.ssm_in ? a.ssm_in[(int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh +
+                                              (int64_t)n * a.si_sn + (int64_t)pr * a.si_sp]
+                                   : 0.f;
+          r[i] = __float_as_uint(v);
+        }
+        tmem_st32(lane_base + T_ST + cw * NHALF + cc * 32, r);
+      }
+      tmem_st_wait();
+
       for (int c = 0; c < nchunks; ++c) {
         const uint32_t ph = c & 1, pph = (c - 1) & 1;
         const int buf = c & 1;
-        // CB = C B^T over the N halves; the region held the previous scores,
-        // so Y(c-1) must have completed
-        for (int k = 0; k < NK; ++k) {
-          const int i = c * NK + k, slot = i & 1;
-          if (!wait1(bar(B_FULL0 + slot), (i >> 1) & 1, abort_flag, 3)) goto mma_done;
-          ALLOY_TRACE_POINT(3, c, 5 + k);
-          if (k == 0 && c > 0 && !wait1(bar(B_Y_FULL), pph, abort_flag, 4)) goto mma_done;
-          tc_fence_after();
-          const uint32_t sB = base + OFF_STAGE + slot * kStageBytes, sC = sB + 16384;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem + T_CB, sw128_desc(sC + 32 * kk, 16, 1024),
-                      sw128_desc(sB + 32 * kk, 16, 1024), ID_CB, (k | kk) != 0);
-        }
-        umma_commit(bar(B_CB_FULL));
-        ALLOY_TRACE_POINT(3, c, 0);
-        // Yi = C [H_0; H_1]^T for both heads at once (N = 128 rows (h, p))
-        if (c > 0 && !wait1(bar(B_Y_EMPTY0 + (buf ^ 1)), ((c - 1) >> 1) & 1, abort_flag, 5)) goto mma_done;
-        if (!wait1(bar(B_HBF_READY), ph, abort_flag, 6)) goto mma_done;
-        tc_fence_after();
-        for (int k = 0; k < NK; ++k) {
-          const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
-          const uint32_t sH = base + OFF_HX + k * 16384;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem + T_YI, sw128_desc(sC + 32 * kk, 16, 1024),
-                      sw128_desc(sH + 32 * kk, 16, 1024), ID_YI, (k | kk) != 0);
-        }
-        umma_commit(bar(B_YI_DONE));
-        ALLOY_TRACE_POINT(3, c, 1);
-        // state: ST[(h,p), n] += X'^T B over s, per N half; releases the stages
-        if (!wait1(bar(B_XP_READY), ph, abort_flag, 8)) goto mma_done;
-        ALLOY_TRACE_POINT(3, c, 9);
+        const float* cm0 = cum_s + (buf * 2 + 0) * 128;
+        const float* cm1 = cum_s + (buf * 2 + 1) * 128;
+        if (!waitw(bar(B_X_READY0 + buf), (c >> 1) & 1, abort_flag, 30)) break;
+        ALLOY_TRACE_POINT(cw, c, 0);
+        // ---- state: H = bf16(state) -> HX_hr; state *= exp(cum[Q-1]) ----
+        if (c > 0 && !waitw(bar(B_ST_DONE), pph, abort_flag, 31)) break;
         tc_fence_after();
         {
-          // N = d_state in one chain: for d_state 128 the two 64-column halves of B
-          // sit in the two stage slots, 32 KB apart (the MN-atom stride)
-          const int slot0 = (c * NK) & 1;
-          const uint32_t sB = base + OFF_STAGE + slot0 * kStageBytes;
-          const uint32_t sXp = base + OFF_HX;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_bf16(tmem + T_ST, sw128_desc(sXp + 2048 * kk, 16384, 1024),
-                      sw128_desc(sB + 2048 * kk, kStageBytes, 1024), ID_ST, 1);
-          for (int k = 0; k < NK; ++k) umma_commit(bar(B_EMPTY0 + ((c * NK + k) & 1)));
+          const float e_end = ex2_approx((hr ? cm1[127] : cm0[127]) * kLog2e);
+          const uint32_t sH = base + OFF_HX + hr * 8192;   // [n block][head][64 p][64 n]
+          const uint64_t e2 = f2_splat(e_end);
+          // 16-column pieces of this warpgroup's state columns, the next piece
+          // read from tensor memory while this one is copied and scaled
+          constexpr int NPIECE = NHALF / 16;
+          uint32_t rb[2][16];
+          tmem_ld16(lane_base + T_ST + cw * NHALF, rb[0]);
+  #pragma unroll
+          for (int i = 0; i < NPIECE; ++i) {
+            uint32_t (&r)[16] = rb[i & 1];
+            tmem_ld_wait_regs(r);
+            if (i + 1 < NPIECE) tmem_ld16(lane_base + T_ST + cw * NHALF + 16 * (i + 1), rb[(i + 1) & 1]);
+            const int n0 = cw * NHALF + 16 * i;
+  #pragma unroll
+            for (int g4 = 0; g4 < 2; ++g4) {
+              const int n = n0 + g4 * 8;
+              st_shared_v4(sH + (n >> 6) * 16384 + sw_off(pr, (n & 63) >> 3),
+                           pack_bf16x2(__uint_as_float(r[g4 * 8 + 0]), __uint_as_float(r[g4 * 8 + 1])),
+                           pack_bf16x2(__uint_as_float(r[g4 * 8 + 2]), __uint_as_float(r[g4 * 8 + 3])),
+                           pack_bf16x2(__uint_as_float(r[g4 * 8 + 4]), __uint_as_float(r[g4 * 8 + 5])),
+                           pack_bf16x2(__uint_as_float(r[g4 * 8 + 6]), __uint_as_float(r[g4 * 8 + 7])));
+            }
+  #pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              float lo, hi;
+              f2_unpack(f2_mul(f2_pack(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1])), e2), lo, hi);
+              r[2 * k] = __float_as_uint(lo);
+              r[2 * k + 1] = __float_as_uint(hi);
+            }
+            tmem_st16(lane_base + T_ST + n0, r);
+          }
+          tmem_st_wait();
         }
-        umma_commit(bar(B_ST_DONE));
-        ALLOY_TRACE_POINT(3, c, 10);
-        // Y_h = S_h X_h, S_h (bf16 pairs) read from tensor memory
-        if (!wait1(bar(B_S_READY), ph, abort_flag, 7)) goto mma_done;
-        ALLOY_TRACE_POINT(3, c, 8);
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_HBF_READY));
+        ALLOY_TRACE_POINT(cw, c, 1);
+        // ---- X'_cw = X * dt * exp(cum[Q-1] - cum[s]) -> HX_cw ----
+        if (!waitw(bar(B_YI_DONE), ph, abort_flag, 33)) break;
+        ALLOY_TRACE_POINT(cw, c, 4);
+        {
+          const float* cm = cw ? cm1 : cm0;
+          const float e = dt_s[(buf * 2 + cw) * 128 + t] * ex2_approx((cm[127] - cm[t]) * kLog2e);
+          const uint32_t sX = base + OFF_X + (buf * 2 + cw) * 16384, sXp = base + OFF_HX + cw * 16384;
+          const uint64_t e2 = f2_splat(e);
+          uint4 u[8];
+  #pragma unroll
+          for (int ch = 0; ch < 8; ++ch) u[ch] = ld_shared_v4(sX + sw_off(t, ch));
+  #pragma unroll
+          for (int ch = 0; ch < 8; ++ch)
+            st_shared_v4(sXp + sw_off(t, ch), f2_to_bf2(f2_mul(f2_from_bf2(u[ch].x), e2)),
+                         f2_to_bf2(f2_mul(f2_from_bf2(u[ch].y), e2)), f2_to_bf2(f2_mul(f2_from_bf2(u[ch].z), e2)),
+                         f2_to_bf2(f2_mul(f2_from_bf2(u[ch].w), e2)));
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_XP_READY));
+        ALLOY_TRACE_POINT(cw, c, 5);
+        // ---- scores of both heads, blocks j = cw, cw + 2, in place over CB ----
+        // S_h[t, s] = CB[t, s] exp(cum_h[t] - cum_h[s]) dt_h[s] for s <= t (+ D_h on s == t),
+        // K-step k (sources 16k .. 16k+15) of S_h stored as bf16 pairs in columns [16k + 8h, 16k + 8h + 8)
+        if (!waitw(bar(B_CB_FULL), ph, abort_flag, 32)) break;
+        ALLOY_TRACE_POINT(cw, c, 2);
         tc_fence_after();
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t sX = base + OFF_X + (buf * 2 + h) * 16384;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_bf16_ta(tmem + T_Y + 64 * h, tmem + T_CB + 16 * kk + 8 * h,
-                         sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
-        }
-        umma_commit(bar(B_Y_FULL));
-        ALLOY_TRACE_POINT(3, c, 2);
-        ALLOY_TRACE_POINT(3, c, 3);
-      }
-    mma_done:
-      // wait (bounded) for every MMA this thread issued
-      umma_commit(bar(B_DRAIN));
-      {
-        const long long t0 = clock64();
-        while (!mbar_try_wait(bar(B_DRAIN), 0) && clock64() - t0 < kWaitCycles) {
-        }
-      }
-    }
-  } else if (warp >= 8) {
-    // ------------------------------------------------------------ producers (warps 8-15)
-    const int hh = (warp - 8) >> 2;     // head of the pair
-    const int q = warp & 3;
-    const int t = q * 32 + lane;
-    const int head = h0 + hh;
-    const float A = -expf(a.A_log[(int64_t)head * a.al_s]);
-    const float dtb = a.dt_bias[(int64_t)head * a.dtb_s];
-    // this thread's conv work: 4 channels (4*vc4 .. 4*vc4+3) x 16 rows (16*strip ..)
-    const int vc4 = t & 15, strip = t >> 4;
-    const int xch = head * P + vc4 * 4;
-    const uint32_t raw_row0 = base + OFF_RAW + hh * kRawStride + (uint32_t)(strip * 16) * 128 + vc4 * 8;
-    const int64_t dt_row = (int64_t)b * a.dt_sb + (int64_t)head * a.dt_sh;
-    uint32_t dt_bits = 0;   // raw dt of the chunk about to be produced (converted when used)
-    auto load_dt = [&](int cc) {
-      const int64_t di = dt_row + (int64_t)min(cc * Q + t, L - 1) * a.dt_st;
-      if (a.dt_bf16)
-        asm volatile("ld.global.nc.u16 %0, [%1];" : "=r"(dt_bits)
-                     : "l"(static_cast<const __nv_bfloat16*>(a.dt) + di));
-      else
-        asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(dt_bits)
-                     : "l"(static_cast<const float*>(a.dt) + di));
-    };
-    // ---- epilogue of chunk cc (head hh): y = Y + exp(cum[t]) Yi -> global ----
-    // Each warp stages its 32 rows in its own rows of X[cc&1][hh] (read by
-    // Y(cc) and X'(cc), both complete once Y_FULL(cc) is), then stores 4
-    // full 128-byte rows per instruction.
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    auto epilogue = [&](int cc) -> bool {
-      const int ebuf = cc & 1;
-      if (!waitw(bar(B_Y_FULL), cc & 1, abort_flag, 34)) return false;
-      tc_fence_after();
-      const int t0 = cc * Q;
-      const float e = ex2_approx(cum_s[(ebuf * 2 + hh) * 128 + t] * kLog2e);
-      const uint32_t stage = base + OFF_X + (ebuf * 2 + hh) * 16384 + q * 4096;
-      const uint64_t e2 = f2_splat(e);
-#pragma unroll
-      for (int qq = 0; qq < 4; ++qq) {
-        uint32_t ry[16], ri[16];
-        tmem_ld16(lane_base + T_Y + 64 * hh + 16 * qq, ry);
-        tmem_ld16(lane_base + T_YI + 64 * hh + 16 * qq, ri);
-        tmem_ld_wait();
-#pragma unroll
-        for (int g2 = 0; g2 < 2; ++g2) {
-          uint32_t o4[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int k0 = g2 * 8 + 2 * i;
-            o4[i] = f2_to_bf2(f2_fma(f2_pack(__uint_as_float(ri[k0]), __uint_as_float(ri[k0 + 1])), e2,
-                                     f2_pack(__uint_as_float(ry[k0]), __uint_as_float(ry[k0 + 1]))));
-          }
-          st_shared_v4(stage + sw_off(lane, qq * 2 + g2), o4[0], o4[1], o4[2], o4[3]);
-        }
-      }
-      __syncwarp();
-      __nv_bfloat16* ybase = a.y + (int64_t)b * a.y_sb + (int64_t)head * a.y_sh + (lane & 7) * 8;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int row = 4 * k + (lane >> 3);
-        const uint4 v = ld_shared_v4(stage + sw_off(row, lane & 7));
-        const int tt = t0 + q * 32 + row;
-        if (tt < L) *reinterpret_cast<uint4*>(ybase + (int64_t)tt * a.y_st) = v;
-      }
-      __syncwarp();
-      tc_fence_before();
-      if (lane == 0) mbar_arrive(bar(B_Y_EMPTY0 + ebuf));
-      return true;
-    };
-    uint32_t wg_uses = 0;
-    load_dt(0);
-    bool ok = true;
-    for (int c = 0; ok && c < nchunks; ++c) {
-      const int buf = c & 1;
-      const int t0 = c * Q;
-      // X[buf] and cum/dt/cf[buf] held chunk c-2, whose epilogue this warpgroup
-      // finished last iteration (after Y(c-2), and so after X'(c-2) and S(c-2))
-      ALLOY_TRACE_POINT(4 + hh, c, 0);
-      // ---- dt, warp-local scan, column factors ----
-      const float dt = t0 + t < L
-          ? softplus_f32((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
-          : 0.f;
-      if (c + 1 < nchunks) load_dt(c + 1);
-      float v = A * dt;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float u = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += u;
-      }
-      float* cm = cum_s + (buf * 2 + hh) * 128;
-      cf_s[(buf * 2 + hh) * 128 + t] = ex2_approx((__shfl_sync(0xffffffffu, v, 31) - v) * kLog2e) * dt;
-      dt_s[(buf * 2 + hh) * 128 + t] = dt;
-      if (lane == 31) wsum[(buf * 2 + hh) * 4 + q] = v;
-      // ---- conv + SiLU of this head's x channels -> X[buf][hh] (bf16, unscaled) ----
-      if (!waitw(bar(B_RAW_FULL), c & 1, abort_flag, 21)) break;
-      ALLOY_TRACE_POINT(4 + hh, c, 1);
-      {
-        // taps and bias of this thread's channel pairs (0,1), (2,3), reloaded
-        // per chunk so they are not live across the epilogue
-        uint64_t w2[4][2], b2[2];
-#pragma unroll
-        for (int pp = 0; pp < 2; ++pp) {
-          const float* w0 = cw_all + (hh * 64 + vc4 * 4 + 2 * pp) * 4;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) w2[k][pp] = f2_pack(w0[k], w0[4 + k]);
-          b2[pp] = f2_pack(cw_all[512 + hh * 64 + vc4 * 4 + 2 * pp],
-                           cw_all[512 + hh * 64 + vc4 * 4 + 2 * pp + 1]);
-        }
-        const uint32_t sX = base + OFF_X + (buf * 2 + hh) * 16384;
-        // all 19 input rows of this thread's strip in flight at once
-        uint32_t rw[19][2];
-#pragma unroll
-        for (int r = 0; r < 19; ++r)
-          asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(rw[r][0]), "=r"(rw[r][1]) : "r"(raw_row0 + r * 128));
-        if (c == 0 && strip == 0) {
-          // rows before t = 0 come from the conv cache (zeros without one)
-#pragma unroll
-          for (int r = 0; r < 3; ++r) {
-            float f[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              f[i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb + (int64_t)(a.K - 1 + r - 3) * a.ci_sk +
-                                                           (int64_t)(xch + i) * a.ci_sc])
-                               : 0.f;
-            rw[r][0] = pack_bf16x2(f[0], f[1]);
-            rw[r][1] = pack_bf16x2(f[2], f[3]);
+        // Four 16-column pieces i = (block jj, half g), j = cw + 2 jj: piece i+1 is
+        // read from tensor memory while piece i is scaled.  Block j covers
+        // K-steps k = 2j + g: CB[t, 16k + i] becomes the bf16 pairs of S_h in
+        // columns 16k + 8h .. +8, inside the piece just read, so no piece
+        // overwrites CB values still to be read.  Blocks above the diagonal
+        // (j > q) are zero.
+        uint32_t rb[2][16];
+        if (cw <= q) tmem_ld16(lane_base + T_CB + 32 * cw, rb[0]);
+  #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int j = cw + 2 * (i >> 1), g = i & 1;
+          {
+            uint32_t o0[8], o1[8];
+            if (j > q) {
+  #pragma unroll
+              for (int k = 0; k < 8; ++k) o0[k] = o1[k] = 0u;
+            } else {
+              uint32_t (&r)[16] = rb[i & 1];
+              tmem_ld_wait_regs(r);
+              if (i < 3 && cw + 2 * ((i + 1) >> 1) <= q)
+                tmem_ld16(lane_base + T_CB + 32 * (cw + 2 * ((i + 1) >> 1)) + 16 * ((i + 1) & 1), rb[(i + 1) & 1]);
+  #pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                uint32_t* o = h ? o1 : o0;
+                const float* cm = h ? cm1 : cm0;
+                const float cum_t = cm[t];
+                const float cend = cm[32 * j + 31];
+                // exp(cum_t - cum_s) dt_s = R * cf[s] with R = exp(cum_t - cum[end of block j])
+                // and cf[s] = exp(cum[end] - cum[s]) dt_s.  Off the diagonal R <= 1;
+                // on the diagonal R <= exp(block range), safe when the range is <= 80.
+                const bool fact = j < q || (cm[32 * j] - cend) <= 80.f;
+                if (fact) {
+                  const uint64_t R2 = f2_splat(ex2_approx((cum_t - cend) * kLog2e));
+                  const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + 32 * j + 16 * g);
+  #pragma unroll
+                  for (int i4 = 0; i4 < 4; ++i4) {
+                    const float4 f = cf4[i4];
+                    uint64_t v0 = f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4]), __uint_as_float(r[4 * i4 + 1])), R2),
+                                         f2_pack(f.x, f.y));
+                    uint64_t v1 = f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4 + 2]), __uint_as_float(r[4 * i4 + 3])), R2),
+                                         f2_pack(f.z, f.w));
+                    if (j == q) {   // causal mask and D on the diagonal
+                      const float Dh = h ? D1 : D0;
+                      float e[4];
+                      f2_unpack(v0, e[0], e[1]);
+                      f2_unpack(v1, e[2], e[3]);
+  #pragma unroll
+                      for (int u = 0; u < 4; ++u) {
+                        const int s = 32 * j + 16 * g + 4 * i4 + u;
+                        e[u] = s < t ? e[u] : (s == t ? e[u] + Dh : 0.f);
+                      }
+                      v0 = f2_pack(e[0], e[1]);
+                      v1 = f2_pack(e[2], e[3]);
+                    }
+                    o[2 * i4] = f2_to_bf2(v0);
+                    o[2 * i4 + 1] = f2_to_bf2(v1);
+                  }
+                } else {
+                  // wide decay range inside the block: exact exps per element
+                  const float* dtv = dt_s + (buf * 2 + h) * 128;
+                  const float Dh = h ? D1 : D0;
+  #pragma unroll
+                  for (int i2 = 0; i2 < 8; ++i2) {
+                    float v2[2];
+  #pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                      const int s = 32 * j + 16 * g + 2 * i2 + e;
+                      float v = 0.f;
+                      if (s <= t) v = __uint_as_float(r[2 * i2 + e]) * ex2_approx((cum_t - cm[s]) * kLog2e) * dtv[s];
+                      if (s == t) v += Dh;
+                      v2[e] = v;
+                    }
+                    o[i2] = pack_bf16x2(v2[0], v2[1]);
+                  }
+                }
+              }
+            }
+            tmem_st8(lane_base + T_CB + 32 * j + 16 * g, o0);
+            tmem_st8(lane_base + T_CB + 32 * j + 16 * g + 8, o1);
           }
         }
-#pragma unroll
-        for (int r = 3; r < 19; ++r) {
-          const int srow = strip * 16 + r - 3;
-          uint32_t o[2];
-#pragma unroll
-          for (int pp = 0; pp < 2; ++pp) {
-            uint64_t acc = b2[pp];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) acc = f2_fma(f2_from_bf2(rw[r - 3 + k][pp]), w2[k][pp], acc);
-            o[pp] = (t0 + srow < L) ? f2_to_bf2(f2_silu(acc)) : 0u;
-          }
-          const uint32_t addr = sX + srow * 128 + ((((vc4 >> 1) ^ (srow & 7))) << 4) + ((vc4 & 1) << 3);
-          asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(addr), "r"(o[0]), "r"(o[1]) : "memory");
-        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_S_READY));
+        ALLOY_TRACE_POINT(cw, c, 3);
+        ALLOY_TRACE_POINT(cw, c, 7);
       }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_RAW_EMPTY));
-      ALLOY_TRACE_POINT(4 + hh, c, 2);
-      // ---- prefix over the warps -> cumulative log decay ----
-      // (wsum is double-buffered by chunk parity: its next write, two chunks
-      // on, comes after every warp has passed the next chunk's sync)
-      if (!warps_sync(bar(B_PWG0 + hh), wg_uses, abort_flag, 22)) break;
-      for (int i = 0; i < q; ++i) v += wsum[(buf * 2 + hh) * 4 + i];
-      cm[t] = v;
-      // X, cum, dt, cf of chunk c are ready
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_X_READY0 + buf));
-      ALLOY_TRACE_POINT(4 + hh, c, 3);
-      // the previous chunk's output, while the tensor cores and consumers work on this one
-      if (c > 0 && !epilogue(c - 1)) break;
-      ALLOY_TRACE_POINT(4 + hh, c, 4);
-    }
-    if (!*abort_flag && nchunks > 0) epilogue(nchunks - 1);
-  } else {
-    // ------------------------------------------------------------ consumers
-    const int cw = warp >> 2;           // consumer warpgroup
-    const int q = warp & 3;             // TMEM lane quadrant
-    const int t = q * 32 + lane;        // row of this thread (t, s or (h,p))
-    const float D0 = a.Dp ? a.Dp[(int64_t)h0 * a.d_s] : 0.f;
-    const float D1 = a.Dp ? a.Dp[(int64_t)(h0 + 1) * a.d_s] : 0.f;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    // state rows: r = t -> head hr = t / 64, p = t % 64; this warpgroup owns
-    // state columns [cw * N/2, (cw+1) * N/2)
-    const int hr = t >> 6, pr = t & 63;
-
-    // initial state -> TMEM
-    for (int cc = 0; cc < NHALF / 32; ++cc) {
-      uint32_t r[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int n = cw * NHALF + cc * 32 + i;
-        const float v = a.ssm_in ? a.ssm_in[(int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh +
-                                            (int64_t)n * a.si_sn + (int64_t)pr * a.si_sp]
-                                 : 0.f;
-        r[i] = __float_as_uint(v);
-      }
-      tmem_st32(lane_base + T_ST + cw * NHALF + cc * 32, r);
-    }
-    tmem_st_wait();
-
-    for (int c = 0; c < nchunks; ++c) {
-      const uint32_t ph = c & 1, pph = (c - 1) & 1;
-      const int buf = c & 1;
-      const float* cm0 = cum_s + (buf * 2 + 0) * 128;
-      const float* cm1 = cum_s + (buf * 2 + 1) * 128;
-      if (!waitw(bar(B_X_READY0 + buf), (c >> 1) & 1, abort_flag, 30)) break;
-      ALLOY_TRACE_POINT(cw, c, 0);
-      // ---- state: H = bf16(state) -> HX_hr; state *= exp(cum[Q-1]) ----
-      if (c > 0 && !waitw(bar(B_ST_DONE), pph, abort_flag, 31)) break;
-      tc_fence_after();
-      {
-        const float e_end = ex2_approx((hr ? cm1[127] : cm0[127]) * kLog2e);
-        const uint32_t sH = base + OFF_HX + hr * 8192;   // [n block][head][64 p][64 n]
-#pragma unroll
+      // ---- final state -> ssm_out ----
+      if (!*abort_flag && a.ssm_out && waitw(bar(B_ST_DONE), (nchunks - 1) & 1, abort_flag, 35)) {
+        tc_fence_after();
+  #pragma unroll 1
         for (int cc = 0; cc < NHALF / 32; ++cc) {
           const int n0 = cw * NHALF + cc * 32;
           uint32_t r[32];
           tmem_ld32(lane_base + T_ST + n0, r);
           tmem_ld_wait();
-#pragma unroll
-          for (int g4 = 0; g4 < 4; ++g4) {
-            const int n = n0 + g4 * 8;
-            st_shared_v4(sH + (n >> 6) * 16384 + sw_off(pr, (n & 63) >> 3),
-                         pack_bf16x2(__uint_as_float(r[g4 * 8 + 0]), __uint_as_float(r[g4 * 8 + 1])),
-                         pack_bf16x2(__uint_as_float(r[g4 * 8 + 2]), __uint_as_float(r[g4 * 8 + 3])),
-                         pack_bf16x2(__uint_as_float(r[g4 * 8 + 4]), __uint_as_float(r[g4 * 8 + 5])),
-                         pack_bf16x2(__uint_as_float(r[g4 * 8 + 6]), __uint_as_float(r[g4 * 8 + 7])));
-          }
-          const uint64_t e2 = f2_splat(e_end);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float lo, hi;
-            f2_unpack(f2_mul(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), e2), lo, hi);
-            r[2 * i] = __float_as_uint(lo);
-            r[2 * i + 1] = __float_as_uint(hi);
-          }
-          tmem_st32(lane_base + T_ST + n0, r);
+  #pragma unroll
+          for (int i = 0; i < 32; ++i)
+            a.ssm_out[(int64_t)b * a.so_sb + (int64_t)(h0 + hr) * a.so_sh + (int64_t)(n0 + i) * a.so_sn +
+                      (int64_t)pr * a.so_sp] = __uint_as_float(r[i]);
         }
-        tmem_st_wait();
       }
-      fence_async_smem();
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_HBF_READY));
-      ALLOY_TRACE_POINT(cw, c, 1);
-      // ---- X'_cw = X * dt * exp(cum[Q-1] - cum[s]) -> HX_cw ----
-      if (!waitw(bar(B_YI_DONE), ph, abort_flag, 33)) break;
-      ALLOY_TRACE_POINT(cw, c, 4);
-      {
-        const float* cm = cw ? cm1 : cm0;
-        const float e = dt_s[(buf * 2 + cw) * 128 + t] * ex2_approx((cm[127] - cm[t]) * kLog2e);
-        const uint32_t sX = base + OFF_X + (buf * 2 + cw) * 16384, sXp = base + OFF_HX + cw * 16384;
-        const uint64_t e2 = f2_splat(e);
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const uint4 u = ld_shared_v4(sX + sw_off(t, ch));
-          st_shared_v4(sXp + sw_off(t, ch), f2_to_bf2(f2_mul(f2_from_bf2(u.x), e2)),
-                       f2_to_bf2(f2_mul(f2_from_bf2(u.y), e2)), f2_to_bf2(f2_mul(f2_from_bf2(u.z), e2)),
-                       f2_to_bf2(f2_mul(f2_from_bf2(u.w), e2)));
-        }
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_XP_READY));
-      ALLOY_TRACE_POINT(cw, c, 5);
-      // ---- scores of both heads, blocks j = cw, cw + 2, in place over CB ----
-      // S_h[t, s] = CB[t, s] exp(cum_h[t] - cum_h[s]) dt_h[s] for s <= t (+ D_h on s == t),
-      // K-step k (sources 16k .. 16k+15) of S_h stored as bf16 pairs in columns [16k + 8h, 16k + 8h + 8)
-      if (!waitw(bar(B_CB_FULL), ph, abort_flag, 32)) break;
-      ALLOY_TRACE_POINT(cw, c, 2);
-      tc_fence_after();
-#pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const int j = cw + 2 * jj;
-        // block j in two 16-column halves (K-steps k = 2j + g): CB[t, 16k + i]
-        // becomes the bf16 pairs of S_h in columns 16k + 8h .. +8, inside the
-        // half just read, so no half overwrites CB values still to be read
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          uint32_t o0[8], o1[8];
-          if (j > q) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o0[i] = o1[i] = 0u;
-          } else {
-            uint32_t r[16];
-            tmem_ld16(lane_base + T_CB + 32 * j + 16 * g, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              uint32_t* o = h ? o1 : o0;
-              const float* cm = h ? cm1 : cm0;
-              const float cum_t = cm[t];
-              const float cend = cm[32 * j + 31];
-              // exp(cum_t - cum_s) dt_s = R * cf[s] with R = exp(cum_t - cum[end of block j])
-              // and cf[s] = exp(cum[end] - cum[s]) dt_s.  Off the diagonal R <= 1;
-              // on the diagonal R <= exp(block range), safe when the range is <= 80.
-              const bool fact = j < q || (cm[32 * j] - cend) <= 80.f;
-              if (fact) {
-                const uint64_t R2 = f2_splat(ex2_approx((cum_t - cend) * kLog2e));
-                const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + 32 * j + 16 * g);
-#pragma unroll
-                for (int i4 = 0; i4 < 4; ++i4) {
-                  const float4 f = cf4[i4];
-                  uint64_t v0 = f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4]), __uint_as_float(r[4 * i4 + 1])), R2),
-                                       f2_pack(f.x, f.y));
-                  uint64_t v1 = f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4 + 2]), __uint_as_float(r[4 * i4 + 3])), R2),
-                                       f2_pack(f.z, f.w));
-                  if (j == q) {   // causal mask and D on the diagonal
-                    const float Dh = h ? D1 : D0;
-                    float e[4];
-                    f2_unpack(v0, e[0], e[1]);
-                    f2_unpack(v1, e[2], e[3]);
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                      const int s = 32 * j + 16 * g + 4 * i4 + u;
-                      e[u] = s < t ? e[u] : (s == t ? e[u] + Dh : 0.f);
-                    }
-                    v0 = f2_pack(e[0], e[1]);
-                    v1 = f2_pack(e[2], e[3]);
-                  }
-                  o[2 * i4] = f2_to_bf2(v0);
-                  o[2 * i4 + 1] = f2_to_bf2(v1);
-                }
-              } else {
-                // wide decay range inside the block: exact exps per element
-                const float* dtv = dt_s + (buf * 2 + h) * 128;
-                const float Dh = h ? D1 : D0;
-#pragma unroll
-                for (int i2 = 0; i2 < 8; ++i2) {
-                  float v2[2];
-#pragma unroll
-                  for (int e = 0; e < 2; ++e) {
-                    const int s = 32 * j + 16 * g + 2 * i2 + e;
-                    float v = 0.f;
-                    if (s <= t) v = __uint_as_float(r[2 * i2 + e]) * ex2_approx((cum_t - cm[s]) * kLog2e) * dtv[s];
-                    if (s == t) v += Dh;
-                    v2[e] = v;
-                  }
-                  o[i2] = pack_bf16x2(v2[0], v2[1]);
-                }
-              }
-            }
-          }
-          tmem_st8(lane_base + T_CB + 32 * j + 16 * g, o0);
-          tmem_st8(lane_base + T_CB + 32 * j + 16 * g + 8, o1);
-        }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_S_READY));
-      ALLOY_TRACE_POINT(cw, c, 3);
-      ALLOY_TRACE_POINT(cw, c, 7);
     }
-    // ---- final state -> ssm_out ----
-    if (!*abort_flag && a.ssm_out && waitw(bar(B_ST_DONE), (nchunks - 1) & 1, abort_flag, 35)) {
-      tc_fence_after();
-      for (int cc = 0; cc < NHALF / 32; ++cc) {
-        const int n0 = cw * NHALF + cc * 32;
-        uint32_t r[32];
-        tmem_ld32(lane_base + T_ST + n0, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          a.ssm_out[(int64_t)b * a.so_sb + (int64_t)(h0 + hr) * a.so_sh + (int64_t)(n0 + i) * a.so_sn +
-                    (int64_t)pr * a.so_sp] = __uint_as_float(r[i]);
-      }
-    }
-    tc_fence_before();
   }
 
   __syncthreads();
