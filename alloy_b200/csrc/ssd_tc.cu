@@ -4,9 +4,12 @@
 //
 // Two launches per call:
 //  1. bc_conv_kernel: conv1d + SiLU of the B and C columns of the selected
-//     head groups -> bf16 workspace [B, L, {B,C}, groups, N].  Every head of a
-//     group reads the same B/C, so they are produced once instead of once per
-//     head pair.
+//     head groups -> bf16 workspace of 16 KB tiles, each a [128 rows][64
+//     columns] half of B or C of one (batch row, chunk, group) laid out as the
+//     SSD kernel's shared memory holds it (128-byte swizzle), so the kernel
+//     fetches a chunk's B/C with plain bulk copies.  Every head of a group
+//     reads the same B/C, so they are produced once instead of once per head
+//     pair.
 //  2. ssd_tc_kernel: one CTA per (batch row, pair of heads of one group),
 //     walking chunks of Q = 128 steps in order with the fp32 state resident in
 //     tensor memory.  Per chunk (t, s in [0, Q); p < P = 64; n < N):
@@ -18,7 +21,7 @@
 //        y[t]    = Y[t] + exp(cum[t]) Yi[t]               (epilogue, bf16)
 //        state   = exp(cum[Q-1]) state + X'^T B,  X'[s] = X[s] dt_s exp(cum[Q-1]-cum[s])
 //     X is the unscaled conv+SiLU output of the pair's x channels (bf16,
-//     produced in the CTA); B/C tiles arrive by TMA (128-byte swizzle) into a
+//     produced in the CTA); B/C tiles arrive by bulk copy into a
 //     two-stage ring of 64-column halves; raw x rows (with the 3-row conv
 //     halo) arrive by TMA per head.  The state of both heads is one 128 x N
 //     fp32 TMEM accumulator with rows (head, p): its update is a single
@@ -39,6 +42,9 @@
 // Phase markers: no code unless a timing build defines ALLOY_TRACE_POINT.
 #ifndef ALLOY_TRACE_POINT
 #define ALLOY_TRACE_POINT(role, chunk, id)
+#endif
+#ifndef ALLOY_TRACE_COPY_DONE
+#define ALLOY_TRACE_COPY_DONE(bar, parity, role, chunk, id)
 #endif
 
 namespace alloy {
@@ -66,39 +72,35 @@ constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 constexpr uint32_t kStageBytes = 32768;             // B half [128][64] + C half [128][64] bf16
 constexpr uint32_t OFF_STAGE = 0;                   // 2 stages
 constexpr uint32_t OFF_X = 65536;                   // X [2 buffers][2 heads][128 s][64 p] bf16
-constexpr uint32_t OFF_HX = 131072;                 // H_h / X'_h [2 heads], 16 KB each
-constexpr uint32_t OFF_RAW = 163840;                // raw x rows [2 heads][131][64] bf16
-constexpr uint32_t kRawRows = Q + 3;
-constexpr uint32_t kRawBytes = kRawRows * 128;      // 16768 per head
-constexpr uint32_t kRawStride = 17408;              // 1024-aligned per-head stride
-constexpr uint32_t OFF_MISC = OFF_RAW + 2 * kRawStride;
+constexpr uint32_t OFF_H = 131072;                  // H [N/64 blocks][2 heads][64 p][64 n] bf16
+constexpr uint32_t OFF_XP = 163840;                 // X' [2 heads][128 s][64 p] bf16
+constexpr uint32_t OFF_MISC = 196608;
 constexpr uint32_t OFF_CUM = OFF_MISC;              // [2 buffers][2 heads][128] f32
 constexpr uint32_t OFF_DT = OFF_CUM + 2048;         // [2][2][128]
 constexpr uint32_t OFF_CF = OFF_DT + 2048;          // [2][2][128] column factors
 constexpr uint32_t OFF_WSUM = OFF_CF + 2048;        // [2 buffers][2 heads][4 warps]
 constexpr uint32_t OFF_CW = OFF_WSUM + 64;          // x conv weights [2][64][4] + bias [2][64]
-constexpr uint32_t OFF_BAR = OFF_CW + 2560;         // mbarriers (8 bytes each)
-constexpr int NBAR = 24;
+constexpr uint32_t OFF_XF = OFF_CW + 2560;          // X' row factors [2 heads][128]
+constexpr uint32_t OFF_BAR = OFF_XF + 1024;         // mbarriers (8 bytes each)
+constexpr int NBAR = 16;
 constexpr uint32_t OFF_TMEMPTR = OFF_BAR + NBAR * 8;
 constexpr uint32_t OFF_ABORT = OFF_TMEMPTR + 8;
 constexpr uint32_t kSmemBytes = OFF_ABORT + 16 + 1024;  // + alignment slack
 
 // barrier ids (counts in the kernel's init table)
 enum {
-  B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1,   // B/C half-tile ring (TMA <-> MMA)
-  B_RAW_FULL0, B_RAW_FULL1,                   // raw x rows of a chunk, per head (TMA issued by the producers)
-  B_X_READY0, B_X_READY1,                     // producers -> consumers: X, cum, dt, cf (per buffer)
+  B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1,   // B/C stage ring (copies <-> MMA)
+  B_X_READY0, B_X_READY1,                     // producers -> consumers, MMA: X, X', cum, dt, cf (per buffer)
   B_CB_FULL,                                  // MMA -> consumers: CB in TMEM
-  B_HBF_READY,                                // consumers -> MMA: H copies written, state scaled
-  B_YI_DONE,                                  // MMA -> consumers: Yi done (H buffer reusable)
+  B_HBF_READY,                                // consumers -> MMA: H written, state scaled
   B_S_READY,                                  // consumers -> MMA: scores in TMEM
-  B_Y_FULL,                                   // MMA -> consumers: Y and Yi complete
-  B_XP_READY,                                 // consumers -> MMA: X' written
-  B_ST_DONE,                                  // MMA -> consumers: state update done
-  B_Y_EMPTY0, B_Y_EMPTY1,                     // consumers -> producers/MMA: y read out (per buffer)
-  B_PWG0, B_PWG1, B_CWG0, B_CWG1,             // per-warpgroup syncs
+  B_Y_FULL,                                   // MMA -> producers: Y and Yi complete
+  B_ST_DONE,                                  // MMA -> consumers, producers: state update done
+  B_Y_EMPTY0, B_Y_EMPTY1,                     // producers -> MMA: y read out (per buffer)
+  B_PWG0, B_PWG1,                             // producer warpgroup syncs
   B_DRAIN
 };
+static_assert(B_DRAIN + 1 == NBAR, "barrier table");
 
 // TMEM columns
 constexpr uint32_t T_CB = 0;      // CB [128 t][128 s] f32, overwritten in place by the scores
@@ -120,6 +122,7 @@ struct TcArgs {
   const float* ssm_in; int64_t si_sb, si_sh, si_sn, si_sp;
   float* ssm_out; int64_t so_sb, so_sh, so_sn, so_sp;
   __nv_bfloat16* y; int64_t y_sb, y_st, y_sh;
+  const __nv_bfloat16* bc;   // B/C tile workspace
 };
 
 // ----------------------------------------------------------------------------
@@ -146,24 +149,19 @@ __device__ __forceinline__ bool wait1(uint32_t bar, uint32_t parity, volatile in
   return false;
 }
 
-// warp-uniform wait (all 32 lanes poll; the outcome is the same on all lanes)
+// warp-uniform wait: every lane polls (bounded by the clock limit and the
+// CTA's abort flag), then one vote makes the outcome the same on all lanes
 __device__ __forceinline__ bool waitw(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                       int site) {
   const long long t0 = clock64();
-  for (uint32_t it = 0; it < (1u << 30); ++it) {
-    const uint32_t ok = mbar_try_wait(bar, parity);
-    if (__all_sync(0xffffffffu, ok)) return true;
-    const int ab = *abort_flag;
-    const int late = clock64() - t0 > kWaitCycles;
-    if (__any_sync(0xffffffffu, ab || late)) {
-      if (!ab && late && (threadIdx.x & 31) == 0) signal_abort(abort_flag, site);
-      __syncwarp();
-      return false;
-    }
+  bool ok;
+  while (!(ok = mbar_try_wait(bar, parity) != 0)) {
+    if (*abort_flag || clock64() - t0 > kWaitCycles) break;
   }
-  if ((threadIdx.x & 31) == 0) signal_abort(abort_flag, site);
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok && (threadIdx.x & 31) == 0 && !*abort_flag) signal_abort(abort_flag, site);
   __syncwarp();
-  return false;
+  return ok;
 }
 
 // Barrier among the warps of one or both warpgroups, built on an mbarrier so
@@ -200,10 +198,11 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
 // ----------------------------------------------------------------------------
 // B/C conv + SiLU pre-pass
 // ----------------------------------------------------------------------------
-// bc[b, t, j], j in [0, 2*Gs*N): part = j / (Gs*N) (0 = B, 1 = C), then group
-// gl and state index n of j % (Gs*N) = gl*N + n; source channel
-// H*P + part*G*N + group_begin*N + j % (Gs*N), i.e. the same column order as
-// xBC's B and C blocks, restricted to the selected groups.
+// Workspace: tiles bc[b][chunk][gl][k][part] of [128 rows][64 columns] bf16
+// (16 KB), part 0 = B, 1 = C, k = 64-column half of the state index n,
+// element (r, j) at byte r*128 + ((j/8 ^ r%8) * 16) + (j%8)*2 (the 128-byte
+// swizzle of a K-major UMMA operand tile).  Rows past L are zeros.  Source
+// column of (part, gl, n): H*P + part*G*N + (group_begin + gl)*N + n.
 //
 // One CTA per (128-row tile, kBcW-column tile, batch row): a single tensor
 // copy brings rows [t0 - 3, t0 + 128) of the tile's columns into shared
@@ -220,7 +219,7 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
   constexpr int R = kBcTileRows * CG / 256;   // rows per thread
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t full_bar;
-  const uint32_t tile = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
+  const uint32_t stile = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
   const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&full_bar));
   const int b = blockIdx.z;
   const int t0 = blockIdx.x * kBcTileRows;
@@ -235,10 +234,15 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
   __syncthreads();
   if (threadIdx.x == 0) {
     mbar_arrive_expect_tx(bar, (kBcTileRows + 3) * W * 2);
-    tma_load_3d(tile, &src_map, bar, src0, t0 - 3, b);
+    tma_load_3d(stile, &src_map, bar, src0, t0 - 3, b);
   }
   const int cg = threadIdx.x % CG, strip = threadIdx.x / CG;
   const int c = src0 + cg * 8;
+  // this thread's 8 columns in the tile layout
+  const int rem = j0 - part * span + cg * 8;   // gl * N + n
+  const int gl = rem / a.N, n = rem % a.N;
+  const int nchunks = (a.L + kBcTileRows - 1) / kBcTileRows;
+  const int64_t tile = ((((int64_t)b * nchunks + blockIdx.x) * a.group_count + gl) * (a.N / 64) + n / 64) * 2 + part;
   // taps and bias as channel pairs (loaded while the copy is in flight)
   uint64_t w2[4][4], b2[4];
 #pragma unroll
@@ -272,7 +276,7 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
     }
   }
   const int r0 = strip * R;            // first output row of this thread (tile-relative)
-  const uint32_t col = tile + cg * 16;
+  const uint32_t col = stile + cg * 16;
   uint64_t win[3][4];
 #pragma unroll
   for (int r = 0; r < 3; ++r) {
@@ -296,11 +300,10 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
       }
     }
   }
-  __nv_bfloat16* dst = bc + ((int64_t)b * a.L + t0 + r0) * ncols + j0 + cg * 8;
-  const int nrows = min(R, a.L - (t0 + r0));
+  unsigned char* dst = reinterpret_cast<unsigned char*>(bc) + tile * 16384;
+  const int nn8 = (n % 64) / 8;   // 16-byte chunk of the row
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    if (r >= nrows) break;
     uint32_t u0, u1, u2, u3;
     asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(u0), "=r"(u1), "=r"(u2), "=r"(u3) : "r"(col + (r0 + r + 3) * (W * 2)));
@@ -312,12 +315,13 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
       acc = f2_fma(win[1][i], w2[1][i], acc);
       acc = f2_fma(win[2][i], w2[2][i], acc);
       acc = f2_fma(x[i], w2[3][i], acc);
-      o[i] = f2_to_bf2(f2_silu(acc));
+      o[i] = t0 + r0 + r < a.L ? f2_to_bf2(f2_silu(acc)) : 0u;
       win[0][i] = win[1][i];
       win[1][i] = win[2][i];
       win[2][i] = x[i];
     }
-    *reinterpret_cast<uint4*>(dst + (int64_t)r * ncols) = make_uint4(o[0], o[1], o[2], o[3]);
+    const int row = r0 + r;
+    *reinterpret_cast<uint4*>(dst + row * 128 + ((nn8 ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -326,25 +330,24 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
 // ----------------------------------------------------------------------------
 // Roles (20 warps, launched with 96 registers a thread; the role warpgroup
 // hands registers to the compute warpgroups with setmaxnreg):
-//   warps 0-7   consumers: warpgroup cw = 0/1.  Per chunk: the bf16 copy of
+//   warps 0-7   consumers, warpgroup cw = 0/1.  Per chunk: the bf16 copy H of
 //               the state and its decay (state columns split by warpgroup),
-//               X' of head cw, and the scores S of both heads for the
-//               32-column blocks j = cw, cw + 2, written in place over CB in
-//               tensor memory.
-//   warps 8-15  producers: warpgroup ph = 0/1 for head ph of the pair.  Per
-//               chunk: dt, cumulative log decay and column factors, the conv +
-//               SiLU of the head's x channels from the TMA-staged raw rows into
-//               the double-buffered X (one thread of the group issues the raw
-//               rows' copy for the next chunk once the group is done with
-//               them), then the epilogue (y) of the previous chunk.  They run
-//               up to one chunk ahead of the consumers.
-//   warp 16     TMA of the B/C half tiles.
+//               then the scores S of both heads for the 32-column blocks
+//               j = cw, cw + 2, written in place over CB in tensor memory.
+//   warps 8-15  producers, warpgroup hh = 0/1 for head hh of the pair.  Per
+//               chunk: dt, cumulative log decay and column factors; the conv +
+//               SiLU of the head's x channels from x rows loaded into
+//               registers (a chunk ahead), written as X (double-buffered) and
+//               X' = X dt exp(cum[Q-1] - cum[s]); then the epilogue (y) of the
+//               previous chunk.  They run up to one chunk ahead of the
+//               consumers.
+//   warp 16     bulk copies of the B/C tiles.
 //   warp 17     TMEM allocation and the MMA issue (one thread).
 //   warps 18-19 no work (they complete the role warpgroup).
+// Per chunk the MMA thread issues CB, Yi (after the state copy), the state
+// update (after X'), then Y (after the scores).
 template <int N>
-__global__ void __launch_bounds__(kThreads, 1)
-ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant__ CUtensorMap x_map,
-              const TcArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
   constexpr int NK = N / 64;            // 64-column halves of B/C per chunk
   constexpr int NHALF = N / 2;          // state columns per consumer warpgroup
   extern __shared__ uint8_t smem_raw[];
@@ -357,6 +360,7 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
   float* cf_s = reinterpret_cast<float*>(smem + OFF_CF);
   float* wsum = reinterpret_cast<float*>(smem + OFF_WSUM);
   float* cw_all = reinterpret_cast<float*>(smem + OFF_CW);   // [2][64][4], then bias [2][64]
+  float* xf_s = reinterpret_cast<float*>(smem + OFF_XF);     // [head][128]
   volatile uint32_t* tmem_ptr = reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEMPTR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_ABORT);
   auto bar = [&](int i) { return base + OFF_BAR + 8u * i; };
@@ -371,19 +375,16 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    const int counts[NBAR] = {1, 1, 1, 1, 1, 1, 8, 8, 1, 8, 1, 8, 1, 8, 1, 8, 8, 4, 4, 4, 4, 1, 0, 0};
-    for (int i = 0; i < NBAR; ++i)
-      if (counts[i]) mbar_init(bar(i), counts[i]);
+    // FULL0/1 EMPTY0/1 X_READY0/1 CB_FULL HBF_READY S_READY Y_FULL ST_DONE Y_EMPTY0/1 PWG0/1 DRAIN
+    const int counts[NBAR] = {1, 1, 1, 1, 8, 8, 1, 8, 8, 1, 1, 8, 8, 4, 4, 1};
+    for (int i = 0; i < NBAR; ++i) mbar_init(bar(i), counts[i]);
     mbar_fence_init();
   }
   if (warp == kMmaWarp) {
     tmem_alloc(base + OFF_TMEMPTR, 512);
     tmem_relinquish();
   }
-  if (warp == kTmaWarp && lane == 0) prefetch_tmap(&bc_map);
-  if (warp == 8 && lane == 0) prefetch_tmap(&x_map);
   // x conv weights of both heads, [head][channel][tap] and bias [head][channel]
-  // (each producer thread copies its 4 channels' taps into registers once)
   if (threadIdx.x < 128) {
     const int hh = threadIdx.x >> 6, ch = threadIdx.x & 63;
     const int64_t c = (int64_t)(h0 + hh) * P + ch;
@@ -400,35 +401,30 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
     // role warpgroup: hand registers to the compute warpgroups
     reg_dealloc<kRoleRegs>();
     if (warp == kTmaWarp) {
-      // ------------------------------------------------------------ TMA: B/C
-      // (its own warp: a sleeping wait in one lane would hold up a role in another)
+      // ------------------------------------------------------------ B/C copies
       if (lane == 0) {
-        const int gs = a.group_count;   // groups in the workspace: B blocks, then C blocks
-        // B/C half tiles into the two-stage ring
-        for (int c = 1; c <= kL2Ahead && c < nchunks; ++c)
-          for (int k = 0; k < NK; ++k) {
-            tma_prefetch_3d(&bc_map, gl * N + 64 * k, c * Q, b);
-            tma_prefetch_3d(&bc_map, (gs + gl) * N + 64 * k, c * Q, b);
-          }
+        // this pair's group: chunk c's B/C halves are NK consecutive 32 KB
+        // stage images [B half k | C half k]
+        const int64_t chunk_stride = (int64_t)a.group_count * NK * kStageBytes;
+        const unsigned char* src0 = reinterpret_cast<const unsigned char*>(a.bc) +
+                                    ((int64_t)b * nchunks * a.group_count + gl) * NK * kStageBytes;
+        for (int c = 1; c <= kL2Ahead && c < nchunks; ++c) bulk_prefetch_l2(src0 + c * chunk_stride, NK * kStageBytes);
         int issued = 0;
         for (int c = 0; c < nchunks; ++c) {
-          if (c + kL2Ahead < nchunks)
-            for (int k = 0; k < NK; ++k) {
-              tma_prefetch_3d(&bc_map, gl * N + 64 * k, (c + kL2Ahead) * Q, b);
-              tma_prefetch_3d(&bc_map, (gs + gl) * N + 64 * k, (c + kL2Ahead) * Q, b);
-            }
+          if (c + kL2Ahead < nchunks) bulk_prefetch_l2(src0 + (c + kL2Ahead) * chunk_stride, NK * kStageBytes);
           for (int k = 0; k < NK; ++k) {
             const int i = c * NK + k, slot = i & 1;
             if (i >= 2 && !wait1(bar(B_EMPTY0 + slot), ((i >> 1) - 1) & 1, abort_flag, 2)) goto bc_done;
             ALLOY_TRACE_POINT(2, c, k);
             mbar_arrive_expect_tx(bar(B_FULL0 + slot), kStageBytes);
-            const uint32_t dst = base + OFF_STAGE + slot * kStageBytes;
-            tma_load_3d(dst, &bc_map, bar(B_FULL0 + slot), gl * N + 64 * k, c * Q, b);
-            tma_load_3d(dst + 16384, &bc_map, bar(B_FULL0 + slot), (gs + gl) * N + 64 * k, c * Q, b);
+            bulk_load(base + OFF_STAGE + slot * kStageBytes, src0 + c * chunk_stride + k * kStageBytes, kStageBytes,
+                      bar(B_FULL0 + slot));
+            ALLOY_TRACE_COPY_DONE(bar(B_FULL0 + slot), (i >> 1) & 1, 2, c, 2 + k);
             ++issued;
           }
         }
       bc_done:
+        // the copies in flight land before the CTA leaves
         for (int i = max(0, issued - 2); i < issued; ++i) {
           const long long t0 = clock64();
           while (!mbar_try_wait(bar(B_FULL0 + (i & 1)), (i >> 1) & 1) && clock64() - t0 < kWaitCycles) {
@@ -437,7 +433,6 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
       }
     } else if (warp == kMmaWarp) {
       // ------------------------------------------------------------ MMA issuer
-      // per chunk: CB -> Yi (after the state copy) -> state update (after X') -> Y (scores from TMEM)
       if (lane == 0) {
         constexpr uint32_t ID_CB = idesc_bf16(128, 128, 0, 0);
         constexpr uint32_t ID_YI = idesc_bf16(128, 128, 0, 0);
@@ -455,38 +450,37 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
             if (k == 0 && c > 0 && !wait1(bar(B_Y_FULL), pph, abort_flag, 4)) goto mma_done;
             tc_fence_after();
             const uint32_t sB = base + OFF_STAGE + slot * kStageBytes, sC = sB + 16384;
-  #pragma unroll
+#pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              umma_bf16(tmem + T_CB, sw128_desc(sC + 32 * kk, 16, 1024),
-                        sw128_desc(sB + 32 * kk, 16, 1024), ID_CB, (k | kk) != 0);
+              umma_bf16(tmem + T_CB, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sB + 32 * kk, 16, 1024), ID_CB,
+                        (k | kk) != 0);
           }
           umma_commit(bar(B_CB_FULL));
           ALLOY_TRACE_POINT(3, c, 0);
-          // Yi = C [H_0; H_1]^T for both heads at once (N = 128 rows (h, p))
+          // Yi = C [H_0; H_1]^T for both heads at once (N = 128 rows (h, p));
+          // its columns and Y's held chunk c-1's output until its epilogue
           if (c > 0 && !wait1(bar(B_Y_EMPTY0 + (buf ^ 1)), ((c - 1) >> 1) & 1, abort_flag, 5)) goto mma_done;
           if (!wait1(bar(B_HBF_READY), ph, abort_flag, 6)) goto mma_done;
           tc_fence_after();
           for (int k = 0; k < NK; ++k) {
             const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
-            const uint32_t sH = base + OFF_HX + k * 16384;
-  #pragma unroll
+            const uint32_t sH = base + OFF_H + k * 16384;
+#pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              umma_bf16(tmem + T_YI, sw128_desc(sC + 32 * kk, 16, 1024),
-                        sw128_desc(sH + 32 * kk, 16, 1024), ID_YI, (k | kk) != 0);
+              umma_bf16(tmem + T_YI, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sH + 32 * kk, 16, 1024), ID_YI,
+                        (k | kk) != 0);
           }
-          umma_commit(bar(B_YI_DONE));
           ALLOY_TRACE_POINT(3, c, 1);
-          // state: ST[(h,p), n] += X'^T B over s, per N half; releases the stages
-          if (!wait1(bar(B_XP_READY), ph, abort_flag, 8)) goto mma_done;
+          // state[(h,p), n] += X'^T B over s (X' arrives with X); releases the stages
+          if (!wait1(bar(B_X_READY0 + buf), (c >> 1) & 1, abort_flag, 8)) goto mma_done;
           ALLOY_TRACE_POINT(3, c, 9);
           tc_fence_after();
           {
             // N = d_state in one chain: for d_state 128 the two 64-column halves of B
             // sit in the two stage slots, 32 KB apart (the MN-atom stride)
-            const int slot0 = (c * NK) & 1;
-            const uint32_t sB = base + OFF_STAGE + slot0 * kStageBytes;
-            const uint32_t sXp = base + OFF_HX;
-  #pragma unroll
+            const uint32_t sB = base + OFF_STAGE + ((c * NK) & 1) * kStageBytes;
+            const uint32_t sXp = base + OFF_XP;
+#pragma unroll
             for (int kk = 0; kk < 8; ++kk)
               umma_bf16(tmem + T_ST, sw128_desc(sXp + 2048 * kk, 16384, 1024),
                         sw128_desc(sB + 2048 * kk, kStageBytes, 1024), ID_ST, 1);
@@ -498,16 +492,16 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
           if (!wait1(bar(B_S_READY), ph, abort_flag, 7)) goto mma_done;
           ALLOY_TRACE_POINT(3, c, 8);
           tc_fence_after();
+#pragma unroll
           for (int h = 0; h < 2; ++h) {
             const uint32_t sX = base + OFF_X + (buf * 2 + h) * 16384;
-  #pragma unroll
+#pragma unroll
             for (int kk = 0; kk < 8; ++kk)
-              umma_bf16_ta(tmem + T_Y + 64 * h, tmem + T_CB + 16 * kk + 8 * h,
-                           sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
+              umma_bf16_ta(tmem + T_Y + 64 * h, tmem + T_CB + 16 * kk + 8 * h, sw128_desc(sX + 2048 * kk, 16, 1024),
+                           ID_Y, kk != 0);
           }
           umma_commit(bar(B_Y_FULL));
           ALLOY_TRACE_POINT(3, c, 2);
-          ALLOY_TRACE_POINT(3, c, 3);
         }
       mma_done:
         // wait (bounded) for every MMA this thread issued
@@ -521,18 +515,20 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
     }
   } else {
     reg_alloc<kComputeRegs>();
+    const int q = warp & 3;               // TMEM lane quadrant
+    const int t = q * 32 + lane;          // row of this thread (t, s or (h,p))
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     if (warp >= 8) {
       // ------------------------------------------------------------ producers (warps 8-15)
       const int hh = (warp - 8) >> 2;     // head of the pair
-      const int q = warp & 3;
-      const int t = q * 32 + lane;
       const int head = h0 + hh;
       const float A = -expf(a.A_log[(int64_t)head * a.al_s]);
       const float dtb = a.dt_bias[(int64_t)head * a.dtb_s];
-      // this thread's conv work: 4 channels (4*vc4 .. 4*vc4+3) x 16 rows (16*strip ..)
+      // this thread's conv work: 4 channels (4*vc4 .. 4*vc4+3) x 16 rows
+      // [16 strip, 16 strip + 16), inside the warp's rows [32q, 32q + 32)
       const int vc4 = t & 15, strip = t >> 4;
       const int xch = head * P + vc4 * 4;
-      const uint32_t raw_row0 = base + OFF_RAW + hh * kRawStride + (uint32_t)(strip * 16) * 128 + vc4 * 8;
+      const __nv_bfloat16* xsrc = a.xbc + (int64_t)b * a.x_sb + xch;
       const int64_t dt_row = (int64_t)b * a.dt_sb + (int64_t)head * a.dt_sh;
       uint32_t dt_bits = 0;   // raw dt of the chunk about to be produced (converted when used)
       auto load_dt = [&](int cc) {
@@ -544,40 +540,69 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
           asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(dt_bits)
                        : "l"(static_cast<const float*>(a.dt) + di));
       };
+      // x rows [cc*Q + 16 strip - 3, cc*Q + 16 strip + 16) of this thread's
+      // channels (clamped into [0, L); rows before 0 are replaced from the
+      // conv cache, rows past L only feed masked outputs)
+      uint32_t rw[19][2];
+      auto load_rows = [&](int cc) {
+        const int r0 = cc * Q + strip * 16 - 3;
+#pragma unroll
+        for (int r = 0; r < 19; ++r) {
+          const int tt = min(max(r0 + r, 0), L - 1);
+          asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];"
+                       : "=r"(rw[r][0]), "=r"(rw[r][1])
+                       : "l"(xsrc + (int64_t)tt * a.x_st));
+        }
+      };
+      // the x rows of chunk cc into L2, one row a thread (128 threads, 131 rows)
+      const __nv_bfloat16* xhead = a.xbc + (int64_t)b * a.x_sb + head * P;
+      auto prefetch_rows = [&](int cc) {
+        if (cc >= nchunks) return;
+        const int r0 = cc * Q - 3 + t;
+        if (r0 >= 0 && r0 < L) prefetch_l2(xhead + (int64_t)r0 * a.x_st);
+        if (t < 3 && r0 + Q < L) prefetch_l2(xhead + (int64_t)(r0 + Q) * a.x_st);
+      };
       // ---- epilogue of chunk cc (head hh): y = Y + exp(cum[t]) Yi -> global ----
       // Each warp stages its 32 rows in its own rows of X[cc&1][hh] (read by
-      // Y(cc) and X'(cc), both complete once Y_FULL(cc) is), then stores 4
-      // full 128-byte rows per instruction.
-      const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+      // Y(cc), complete once Y_FULL(cc) is), then stores 4 full 128-byte rows
+      // per instruction.
       auto epilogue = [&](int cc) -> bool {
         const int ebuf = cc & 1;
         if (!waitw(bar(B_Y_FULL), cc & 1, abort_flag, 34)) return false;
+        ALLOY_TRACE_POINT(4 + hh, cc + 1, 5);
         tc_fence_after();
-        const int t0 = cc * Q;
-        const float e = ex2_approx(cum_s[(ebuf * 2 + hh) * 128 + t] * kLog2e);
+        const uint64_t e2 = f2_splat(ex2_approx(cum_s[(ebuf * 2 + hh) * 128 + t] * kLog2e));
         const uint32_t stage = base + OFF_X + (ebuf * 2 + hh) * 16384 + q * 4096;
-        const uint64_t e2 = f2_splat(e);
-  #pragma unroll
-        for (int qq = 0; qq < 4; ++qq) {
-          uint32_t ry[16], ri[16];
-          tmem_ld16(lane_base + T_Y + 64 * hh + 16 * qq, ry);
-          tmem_ld16(lane_base + T_YI + 64 * hh + 16 * qq, ri);
-          tmem_ld_wait();
-  #pragma unroll
-          for (int g2 = 0; g2 < 2; ++g2) {
-            uint32_t o4[4];
-  #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int k0 = g2 * 8 + 2 * i;
-              o4[i] = f2_to_bf2(f2_fma(f2_pack(__uint_as_float(ri[k0]), __uint_as_float(ri[k0 + 1])), e2,
-                                       f2_pack(__uint_as_float(ry[k0]), __uint_as_float(ry[k0 + 1]))));
-            }
-            st_shared_v4(stage + sw_off(lane, qq * 2 + g2), o4[0], o4[1], o4[2], o4[3]);
+        const uint32_t ty = lane_base + T_Y + 64 * hh, ti = lane_base + T_YI + 64 * hh;
+        // 16-column pieces, the next pair read while this one is combined
+        uint32_t ya[8], ia[8], yb[8], ib[8];
+        auto combine = [&](int piece, uint32_t (&ry)[8], uint32_t (&ri)[8]) {
+          uint32_t o4[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o4[i] = f2_to_bf2(f2_fma(f2_pack(__uint_as_float(ri[2 * i]), __uint_as_float(ri[2 * i + 1])), e2,
+                                     f2_pack(__uint_as_float(ry[2 * i]), __uint_as_float(ry[2 * i + 1]))));
+          st_shared_v4(stage + sw_off(lane, piece), o4[0], o4[1], o4[2], o4[3]);
+        };
+        tmem_ld8(ty, ya);
+        tmem_ld8(ti, ia);
+#pragma unroll 1
+        for (int pc = 0; pc < 8; pc += 2) {
+          tmem_ld_wait_regs(ya, ia);
+          tmem_ld8(ty + 8 * (pc + 1), yb);
+          tmem_ld8(ti + 8 * (pc + 1), ib);
+          combine(pc, ya, ia);
+          tmem_ld_wait_regs(yb, ib);
+          if (pc + 2 < 8) {
+            tmem_ld8(ty + 8 * (pc + 2), ya);
+            tmem_ld8(ti + 8 * (pc + 2), ia);
           }
+          combine(pc + 1, yb, ib);
         }
         __syncwarp();
+        const int t0 = cc * Q;
         __nv_bfloat16* ybase = a.y + (int64_t)b * a.y_sb + (int64_t)head * a.y_sh + (lane & 7) * 8;
-  #pragma unroll
+#pragma unroll
         for (int k = 0; k < 8; ++k) {
           const int row = 4 * k + (lane >> 3);
           const uint4 v = ld_shared_v4(stage + sw_off(row, lane & 7));
@@ -589,176 +614,168 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
         if (lane == 0) mbar_arrive(bar(B_Y_EMPTY0 + ebuf));
         return true;
       };
-      // raw x rows [c*Q - 3, c*Q + Q) of this head's channels (rows outside
-      // [0, L) arrive as zeros), issued by one thread of the warpgroup once its
-      // four warps are done with the previous chunk's rows; the rows of the
-      // next kL2Ahead chunks are pulled into L2 ahead of their loads
-      const bool raw_issuer = q == 0 && lane == 0;
-      const uint32_t raw_bar = bar(B_RAW_FULL0 + hh), raw_dst = base + OFF_RAW + hh * kRawStride;
-      int raw_issued = 0;
-      auto issue_raw = [&](int cc) {
-        if (cc + kL2Ahead < nchunks) tma_prefetch_3d(&x_map, head * P, (cc + kL2Ahead) * Q - 3, b);
-        mbar_arrive_expect_tx(raw_bar, kRawBytes);
-        tma_load_3d(raw_dst, &x_map, raw_bar, head * P, cc * Q - 3, b);
-        ++raw_issued;
-      };
-      if (raw_issuer) {
-        for (int cc = 1; cc < kL2Ahead && cc < nchunks; ++cc) tma_prefetch_3d(&x_map, head * P, cc * Q - 3, b);
-        issue_raw(0);
-      }
-      uint32_t wg_uses = 0;
+      for (int cc = 1; cc <= kL2Ahead; ++cc) prefetch_rows(cc);
       load_dt(0);
-      bool ok = true;
-      for (int c = 0; ok && c < nchunks; ++c) {
-        const int buf = c & 1;
-        const int t0 = c * Q;
-        // X[buf] and cum/dt/cf[buf] held chunk c-2, whose epilogue this warpgroup
-        // finished last iteration (after Y(c-2), and so after X'(c-2) and S(c-2))
-        ALLOY_TRACE_POINT(4 + hh, c, 0);
-        // ---- dt, warp-local scan, column factors ----
-        const float dt = t0 + t < L
-            ? softplus_f32((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
-            : 0.f;
-        if (c + 1 < nchunks) load_dt(c + 1);
-        float v = A * dt;
-  #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float u = __shfl_up_sync(0xffffffffu, v, o);
-          if (lane >= o) v += u;
-        }
-        float* cm = cum_s + (buf * 2 + hh) * 128;
-        cf_s[(buf * 2 + hh) * 128 + t] = ex2_approx((__shfl_sync(0xffffffffu, v, 31) - v) * kLog2e) * dt;
-        dt_s[(buf * 2 + hh) * 128 + t] = dt;
-        if (lane == 31) wsum[(buf * 2 + hh) * 4 + q] = v;
-        // ---- conv + SiLU of this head's x channels -> X[buf][hh] (bf16, unscaled) ----
-        if (!waitw(raw_bar, c & 1, abort_flag, 21)) break;
-        ALLOY_TRACE_POINT(4 + hh, c, 1);
-        {
-          // taps and bias of this thread's channel pairs (0,1), (2,3), reloaded
-          // per chunk so they are not live across the epilogue
-          uint64_t w2[4][2], b2[2];
-  #pragma unroll
-          for (int pp = 0; pp < 2; ++pp) {
-            const float* w0 = cw_all + (hh * 64 + vc4 * 4 + 2 * pp) * 4;
-  #pragma unroll
-            for (int k = 0; k < 4; ++k) w2[k][pp] = f2_pack(w0[k], w0[4 + k]);
-            b2[pp] = f2_pack(cw_all[512 + hh * 64 + vc4 * 4 + 2 * pp],
-                             cw_all[512 + hh * 64 + vc4 * 4 + 2 * pp + 1]);
+      uint32_t wg_uses = 0;
+      // iteration c: chunk c (c >= 0), the rows of chunk c+1, the epilogue of c-1
+      for (int c = -1; c <= nchunks; ++c) {
+        if (c >= 0 && c < nchunks) {
+          const int buf = c & 1;
+          const int t0 = c * Q;
+          // X[buf] and cum/dt/cf[buf] held chunk c-2, whose epilogue this
+          // warpgroup finished last iteration (after Y(c-2), and so after the
+          // scores and the state copy of c-2)
+          ALLOY_TRACE_POINT(4 + hh, c, 0);
+          // ---- dt, warp-local scan, column factors ----
+          const float dt = t0 + t < L
+              ? softplus_f32((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
+              : 0.f;
+          if (c + 1 < nchunks) load_dt(c + 1);
+          float v = A * dt;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const float u = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += u;
           }
-          const uint32_t sX = base + OFF_X + (buf * 2 + hh) * 16384;
-          // all 19 input rows of this thread's strip in flight at once
-          uint32_t rw[19][2];
-  #pragma unroll
-          for (int r = 0; r < 19; ++r)
-            asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(rw[r][0]), "=r"(rw[r][1]) : "r"(raw_row0 + r * 128));
-          if (c == 0 && strip == 0) {
-            // rows before t = 0 come from the conv cache (zeros without one)
-  #pragma unroll
-            for (int r = 0; r < 3; ++r) {
-              float f[4];
-  #pragma unroll
-              for (int i = 0; i < 4; ++i)
-                f[i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb + (int64_t)(a.K - 1 + r - 3) * a.ci_sk +
-                                                             (int64_t)(xch + i) * a.ci_sc])
-                                 : 0.f;
-              rw[r][0] = pack_bf16x2(f[0], f[1]);
-              rw[r][1] = pack_bf16x2(f[2], f[3]);
+          // column factor relative to the end of this row's 16-step piece
+          const float vend = __shfl_sync(0xffffffffu, v, lane | 15);
+          const float cf = ex2_approx((vend - v) * kLog2e) * dt;
+          if (lane == 31) wsum[(buf * 2 + hh) * 4 + q] = v;
+          // ---- prefix over the warps -> cumulative log decay ----
+          // (wsum is double-buffered by chunk parity: its next write, two
+          // chunks on, comes after every warp has passed the next chunk's sync)
+          if (!warps_sync(bar(B_PWG0 + hh), wg_uses, abort_flag, 22)) break;
+          float pre = 0.f, tot = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float w = wsum[(buf * 2 + hh) * 4 + i];
+            pre += i < q ? w : 0.f;
+            tot += w;
+          }
+          const float cum = v + pre;
+          cum_s[(buf * 2 + hh) * 128 + t] = cum;
+          dt_s[(buf * 2 + hh) * 128 + t] = dt;
+          cf_s[(buf * 2 + hh) * 128 + t] = cf;
+          // X' factor of row t, read back below by the lanes of this warp that convolve the row
+          xf_s[hh * 128 + t] = ex2_approx((tot - cum) * kLog2e) * dt;
+          __syncwarp();
+          ALLOY_TRACE_POINT(4 + hh, c, 1);
+          // X' is single-buffered: the state update of chunk c-1 read it
+          if (c > 0 && !waitw(bar(B_ST_DONE), (c - 1) & 1, abort_flag, 23)) break;
+          // ---- conv + SiLU -> X[buf][hh] (bf16) and X'[hh] = X * xf ----
+          {
+            float w[4][4], bias[4];   // [tap][channel]
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float* w0 = cw_all + (hh * 64 + vc4 * 4 + i) * 4;
+#pragma unroll
+              for (int k = 0; k < 4; ++k) w[k][i] = w0[k];
+              bias[i] = cw_all[512 + hh * 64 + vc4 * 4 + i];
+            }
+            if (c == 0 && strip == 0) {
+              // rows before t = 0 come from the conv cache (zeros without one)
+#pragma unroll
+              for (int r = 0; r < 3; ++r) {
+                float f[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  f[i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
+                                                               (int64_t)(a.K - 4 + r) * a.ci_sk +
+                                                               (int64_t)(xch + i) * a.ci_sc])
+                                   : 0.f;
+                rw[r][0] = pack_bf16x2(f[0], f[1]);
+                rw[r][1] = pack_bf16x2(f[2], f[3]);
+              }
+            }
+            const uint32_t sX = base + OFF_X + (buf * 2 + hh) * 16384, sXp = base + OFF_XP + hh * 16384;
+            const float4* xf4 = reinterpret_cast<const float4*>(xf_s + hh * 128 + strip * 16);
+            float4 fq;
+#pragma unroll
+            for (int r = 3; r < 19; ++r) {
+              const int srow = strip * 16 + r - 3;
+              if (((r - 3) & 3) == 0) fq = xf4[(r - 3) >> 2];
+              const float fx = ((r - 3) & 3) == 0 ? fq.x : ((r - 3) & 3) == 1 ? fq.y : ((r - 3) & 3) == 2 ? fq.z : fq.w;
+              const bool valid = t0 + srow < L;
+              float y4[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                float acc = bias[i];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const uint32_t wd = rw[r - 3 + k][i >> 1];
+                  acc = fmaf((i & 1) ? bf16_hi(wd) : bf16_lo(wd), w[k][i], acc);
+                }
+                y4[i] = valid ? silu_fast(acc) : 0.f;
+              }
+              uint32_t o[2], ox[2];
+              o[0] = pack_bf16x2(y4[0], y4[1]);
+              o[1] = pack_bf16x2(y4[2], y4[3]);
+              ox[0] = pack_bf16x2(y4[0] * fx, y4[1] * fx);
+              ox[1] = pack_bf16x2(y4[2] * fx, y4[3] * fx);
+              const uint32_t off = srow * 128 + (((vc4 >> 1) ^ (srow & 7)) << 4) + ((vc4 & 1) << 3);
+              asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(sX + off), "r"(o[0]), "r"(o[1]) : "memory");
+              asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(sXp + off), "r"(ox[0]), "r"(ox[1]) : "memory");
             }
           }
-  #pragma unroll
-          for (int r = 3; r < 19; ++r) {
-            const int srow = strip * 16 + r - 3;
-            uint32_t o[2];
-  #pragma unroll
-            for (int pp = 0; pp < 2; ++pp) {
-              uint64_t acc = b2[pp];
-  #pragma unroll
-              for (int k = 0; k < 4; ++k) acc = f2_fma(f2_from_bf2(rw[r - 3 + k][pp]), w2[k][pp], acc);
-              o[pp] = (t0 + srow < L) ? f2_to_bf2(f2_silu(acc)) : 0u;
-            }
-            const uint32_t addr = sX + srow * 128 + ((((vc4 >> 1) ^ (srow & 7))) << 4) + ((vc4 & 1) << 3);
-            asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(addr), "r"(o[0]), "r"(o[1]) : "memory");
-          }
+          prefetch_rows(c + 1 + kL2Ahead);
+          // X, X', cum, dt, cf of chunk c are ready
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_X_READY0 + buf));
+          ALLOY_TRACE_POINT(4 + hh, c, 3);
         }
-        fence_async_smem();
-        ALLOY_TRACE_POINT(4 + hh, c, 2);
-        // ---- prefix over the warps -> cumulative log decay ----
-        // (wsum is double-buffered by chunk parity: its next write, two chunks
-        // on, comes after every warp has passed the next chunk's sync)
-        if (!warps_sync(bar(B_PWG0 + hh), wg_uses, abort_flag, 22)) break;
-        // every warp of the group has read this chunk's raw rows
-        if (raw_issuer && c + 1 < nchunks) issue_raw(c + 1);
-        for (int i = 0; i < q; ++i) v += wsum[(buf * 2 + hh) * 4 + i];
-        cm[t] = v;
-        // X, cum, dt, cf of chunk c are ready
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_X_READY0 + buf));
-        ALLOY_TRACE_POINT(4 + hh, c, 3);
+        // the next chunk's rows, in flight during the epilogue below
+        if (c + 1 < nchunks) load_rows(c + 1);
         // the previous chunk's output, while the tensor cores and consumers work on this one
         if (c > 0 && !epilogue(c - 1)) break;
         ALLOY_TRACE_POINT(4 + hh, c, 4);
       }
-      if (!*abort_flag && nchunks > 0) epilogue(nchunks - 1);
-      if (raw_issuer && raw_issued > 0) {
-        // the last raw copy has landed (at once unless a wait above gave up)
-        const long long t0 = clock64();
-        while (!mbar_try_wait(raw_bar, (raw_issued - 1) & 1) && clock64() - t0 < kWaitCycles) {
-        }
-      }
     } else {
       // ------------------------------------------------------------ consumers
       const int cw = warp >> 2;           // consumer warpgroup
-      const int q = warp & 3;             // TMEM lane quadrant
-      const int t = q * 32 + lane;        // row of this thread (t, s or (h,p))
       const float D0 = a.Dp ? a.Dp[(int64_t)h0 * a.d_s] : 0.f;
       const float D1 = a.Dp ? a.Dp[(int64_t)(h0 + 1) * a.d_s] : 0.f;
-      const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
       // state rows: r = t -> head hr = t / 64, p = t % 64; this warpgroup owns
       // state columns [cw * N/2, (cw+1) * N/2)
       const int hr = t >> 6, pr = t & 63;
 
       // initial state -> TMEM
-  #pragma unroll 1
-      for (int cc = 0; cc < NHALF / 32; ++cc) {
-        uint32_t r[32];
-  #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int n = cw * NHALF + cc * 32 + i;
-          const float v = a.ssm_in ? a.ssm_in[(int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh +
-                                              (int64_t)n * a.si_sn + (int64_t)pr * a.si_sp]
-                                   : 0.f;
-          r[i] = __float_as_uint(v);
+#pragma unroll 1
+      for (int n8 = 0; n8 < NHALF / 8; ++n8) {
+        uint32_t r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int n = cw * NHALF + n8 * 8 + i;
+          r[i] = __float_as_uint(a.ssm_in ? a.ssm_in[(int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh +
+                                                     (int64_t)n * a.si_sn + (int64_t)pr * a.si_sp]
+                                          : 0.f);
         }
-        tmem_st32(lane_base + T_ST + cw * NHALF + cc * 32, r);
+        tmem_st8(lane_base + T_ST + cw * NHALF + n8 * 8, r);
       }
       tmem_st_wait();
 
+      // score pieces of this warp: 16-column halves g of the 32-column blocks
+      // j = cw, cw + 2 (K-steps 2j + g of the Y MMA); blocks right of the
+      // warp's rows (j > q) are zero
+      const int npieces = q >= cw + 2 ? 4 : (q >= cw ? 2 : 0);
+      auto piece_col = [&](int i) { return 32 * (cw + 2 * (i >> 1)) + 16 * (i & 1); };
+
       for (int c = 0; c < nchunks; ++c) {
-        const uint32_t ph = c & 1, pph = (c - 1) & 1;
         const int buf = c & 1;
-        const float* cm0 = cum_s + (buf * 2 + 0) * 128;
-        const float* cm1 = cum_s + (buf * 2 + 1) * 128;
         if (!waitw(bar(B_X_READY0 + buf), (c >> 1) & 1, abort_flag, 30)) break;
         ALLOY_TRACE_POINT(cw, c, 0);
-        // ---- state: H = bf16(state) -> HX_hr; state *= exp(cum[Q-1]) ----
-        if (c > 0 && !waitw(bar(B_ST_DONE), pph, abort_flag, 31)) break;
+        // ---- state: H = bf16(state) -> smem; state *= exp(cum[Q-1]) ----
+        if (c > 0 && !waitw(bar(B_ST_DONE), (c - 1) & 1, abort_flag, 31)) break;
         tc_fence_after();
         {
-          const float e_end = ex2_approx((hr ? cm1[127] : cm0[127]) * kLog2e);
-          const uint32_t sH = base + OFF_HX + hr * 8192;   // [n block][head][64 p][64 n]
+          const float e_end = ex2_approx(cum_s[(buf * 2 + hr) * 128 + 127] * kLog2e);
+          const uint32_t sH = base + OFF_H + hr * 8192;   // [n block][head][64 p][64 n]
           const uint64_t e2 = f2_splat(e_end);
           // 16-column pieces of this warpgroup's state columns, the next piece
           // read from tensor memory while this one is copied and scaled
-          constexpr int NPIECE = NHALF / 16;
-          uint32_t rb[2][16];
-          tmem_ld16(lane_base + T_ST + cw * NHALF, rb[0]);
-  #pragma unroll
-          for (int i = 0; i < NPIECE; ++i) {
-            uint32_t (&r)[16] = rb[i & 1];
-            tmem_ld_wait_regs(r);
-            if (i + 1 < NPIECE) tmem_ld16(lane_base + T_ST + cw * NHALF + 16 * (i + 1), rb[(i + 1) & 1]);
+          auto copy_piece = [&](int i, uint32_t (&r)[16]) {
             const int n0 = cw * NHALF + 16 * i;
-  #pragma unroll
+#pragma unroll
             for (int g4 = 0; g4 < 2; ++g4) {
               const int n = n0 + g4 * 8;
               st_shared_v4(sH + (n >> 6) * 16384 + sw_off(pr, (n & 63) >> 3),
@@ -767,7 +784,7 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
                            pack_bf16x2(__uint_as_float(r[g4 * 8 + 4]), __uint_as_float(r[g4 * 8 + 5])),
                            pack_bf16x2(__uint_as_float(r[g4 * 8 + 6]), __uint_as_float(r[g4 * 8 + 7])));
             }
-  #pragma unroll
+#pragma unroll
             for (int k = 0; k < 8; ++k) {
               float lo, hi;
               f2_unpack(f2_mul(f2_pack(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1])), e2), lo, hi);
@@ -775,6 +792,17 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
               r[2 * k + 1] = __float_as_uint(hi);
             }
             tmem_st16(lane_base + T_ST + n0, r);
+          };
+          uint32_t ra[16], rb[16];
+          tmem_ld16(lane_base + T_ST + cw * NHALF, ra);
+#pragma unroll 1
+          for (int i = 0; i < NHALF / 16; i += 2) {
+            tmem_ld_wait_regs(ra);
+            tmem_ld16(lane_base + T_ST + cw * NHALF + 16 * (i + 1), rb);
+            copy_piece(i, ra);
+            tmem_ld_wait_regs(rb);
+            if (i + 2 < NHALF / 16) tmem_ld16(lane_base + T_ST + cw * NHALF + 16 * (i + 2), ra);
+            copy_piece(i + 1, rb);
           }
           tmem_st_wait();
         }
@@ -783,112 +811,76 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_HBF_READY));
         ALLOY_TRACE_POINT(cw, c, 1);
-        // ---- X'_cw = X * dt * exp(cum[Q-1] - cum[s]) -> HX_cw ----
-        if (!waitw(bar(B_YI_DONE), ph, abort_flag, 33)) break;
-        ALLOY_TRACE_POINT(cw, c, 4);
-        {
-          const float* cm = cw ? cm1 : cm0;
-          const float e = dt_s[(buf * 2 + cw) * 128 + t] * ex2_approx((cm[127] - cm[t]) * kLog2e);
-          const uint32_t sX = base + OFF_X + (buf * 2 + cw) * 16384, sXp = base + OFF_HX + cw * 16384;
-          const uint64_t e2 = f2_splat(e);
-          uint4 u[8];
-  #pragma unroll
-          for (int ch = 0; ch < 8; ++ch) u[ch] = ld_shared_v4(sX + sw_off(t, ch));
-  #pragma unroll
-          for (int ch = 0; ch < 8; ++ch)
-            st_shared_v4(sXp + sw_off(t, ch), f2_to_bf2(f2_mul(f2_from_bf2(u[ch].x), e2)),
-                         f2_to_bf2(f2_mul(f2_from_bf2(u[ch].y), e2)), f2_to_bf2(f2_mul(f2_from_bf2(u[ch].z), e2)),
-                         f2_to_bf2(f2_mul(f2_from_bf2(u[ch].w), e2)));
-        }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_XP_READY));
-        ALLOY_TRACE_POINT(cw, c, 5);
-        // ---- scores of both heads, blocks j = cw, cw + 2, in place over CB ----
-        // S_h[t, s] = CB[t, s] exp(cum_h[t] - cum_h[s]) dt_h[s] for s <= t (+ D_h on s == t),
-        // K-step k (sources 16k .. 16k+15) of S_h stored as bf16 pairs in columns [16k + 8h, 16k + 8h + 8)
-        if (!waitw(bar(B_CB_FULL), ph, abort_flag, 32)) break;
+        // ---- scores of both heads, in place over CB ----
+        // S_h[t, s] = CB[t, s] exp(cum_h[t] - cum_h[s]) dt_h[s] for s <= t (+ D_h on
+        // s == t); K-step k (sources 16k .. 16k+15) of S_h stored as bf16 pairs
+        // in columns [16k + 8h, 16k + 8h + 8), inside the piece it was read from
+        if (!waitw(bar(B_CB_FULL), c & 1, abort_flag, 32)) break;
         ALLOY_TRACE_POINT(cw, c, 2);
         tc_fence_after();
-        // Four 16-column pieces i = (block jj, half g), j = cw + 2 jj: piece i+1 is
-        // read from tensor memory while piece i is scaled.  Block j covers
-        // K-steps k = 2j + g: CB[t, 16k + i] becomes the bf16 pairs of S_h in
-        // columns 16k + 8h .. +8, inside the piece just read, so no piece
-        // overwrites CB values still to be read.  Blocks above the diagonal
-        // (j > q) are zero.
-        uint32_t rb[2][16];
-        if (cw <= q) tmem_ld16(lane_base + T_CB + 32 * cw, rb[0]);
-  #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int j = cw + 2 * (i >> 1), g = i & 1;
-          {
-            uint32_t o0[8], o1[8];
-            if (j > q) {
-  #pragma unroll
-              for (int k = 0; k < 8; ++k) o0[k] = o1[k] = 0u;
+        auto score_piece = [&](int i, const uint32_t (&r)[16]) {
+          const int j = cw + 2 * (i >> 1);
+          const int s0 = piece_col(i);
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            const float* cm = cum_s + (buf * 2 + h) * 128;
+            const float cum_t = cm[t];
+            uint32_t o[8];
+            if (j < q) {
+              // left of the diagonal block: exp(cum_t - cum_s) dt_s = R cf[s] with
+              // R = exp(cum_t - cum[s0+15]) <= 1 and cf[s] = exp(cum[s0+15] - cum_s) dt_s <= dt_s
+              const uint64_t R2 = f2_splat(ex2_approx((cum_t - cm[s0 + 15]) * kLog2e));
+              const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + s0);
+#pragma unroll
+              for (int i4 = 0; i4 < 4; ++i4) {
+                const float4 f = cf4[i4];
+                o[2 * i4] = f2_to_bf2(
+                    f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4]), __uint_as_float(r[4 * i4 + 1])), R2),
+                           f2_pack(f.x, f.y)));
+                o[2 * i4 + 1] = f2_to_bf2(
+                    f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4 + 2]), __uint_as_float(r[4 * i4 + 3])), R2),
+                           f2_pack(f.z, f.w)));
+              }
             } else {
-              uint32_t (&r)[16] = rb[i & 1];
-              tmem_ld_wait_regs(r);
-              if (i < 3 && cw + 2 * ((i + 1) >> 1) <= q)
-                tmem_ld16(lane_base + T_CB + 32 * (cw + 2 * ((i + 1) >> 1)) + 16 * ((i + 1) & 1), rb[(i + 1) & 1]);
-  #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                uint32_t* o = h ? o1 : o0;
-                const float* cm = h ? cm1 : cm0;
-                const float cum_t = cm[t];
-                const float cend = cm[32 * j + 31];
-                // exp(cum_t - cum_s) dt_s = R * cf[s] with R = exp(cum_t - cum[end of block j])
-                // and cf[s] = exp(cum[end] - cum[s]) dt_s.  Off the diagonal R <= 1;
-                // on the diagonal R <= exp(block range), safe when the range is <= 80.
-                const bool fact = j < q || (cm[32 * j] - cend) <= 80.f;
-                if (fact) {
-                  const uint64_t R2 = f2_splat(ex2_approx((cum_t - cend) * kLog2e));
-                  const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + 32 * j + 16 * g);
-  #pragma unroll
-                  for (int i4 = 0; i4 < 4; ++i4) {
-                    const float4 f = cf4[i4];
-                    uint64_t v0 = f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4]), __uint_as_float(r[4 * i4 + 1])), R2),
-                                         f2_pack(f.x, f.y));
-                    uint64_t v1 = f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4 + 2]), __uint_as_float(r[4 * i4 + 3])), R2),
-                                         f2_pack(f.z, f.w));
-                    if (j == q) {   // causal mask and D on the diagonal
-                      const float Dh = h ? D1 : D0;
-                      float e[4];
-                      f2_unpack(v0, e[0], e[1]);
-                      f2_unpack(v1, e[2], e[3]);
-  #pragma unroll
-                      for (int u = 0; u < 4; ++u) {
-                        const int s = 32 * j + 16 * g + 4 * i4 + u;
-                        e[u] = s < t ? e[u] : (s == t ? e[u] + Dh : 0.f);
-                      }
-                      v0 = f2_pack(e[0], e[1]);
-                      v1 = f2_pack(e[2], e[3]);
-                    }
-                    o[2 * i4] = f2_to_bf2(v0);
-                    o[2 * i4 + 1] = f2_to_bf2(v1);
-                  }
-                } else {
-                  // wide decay range inside the block: exact exps per element
-                  const float* dtv = dt_s + (buf * 2 + h) * 128;
-                  const float Dh = h ? D1 : D0;
-  #pragma unroll
-                  for (int i2 = 0; i2 < 8; ++i2) {
-                    float v2[2];
-  #pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                      const int s = 32 * j + 16 * g + 2 * i2 + e;
-                      float v = 0.f;
-                      if (s <= t) v = __uint_as_float(r[2 * i2 + e]) * ex2_approx((cum_t - cm[s]) * kLog2e) * dtv[s];
-                      if (s == t) v += Dh;
-                      v2[e] = v;
-                    }
-                    o[i2] = pack_bf16x2(v2[0], v2[1]);
-                  }
+              // the diagonal block: exact factors (<= 1 for s <= t), zero right
+              // of the diagonal, D on it
+              const float* dv = dt_s + (buf * 2 + h) * 128;
+              const float Dh = h ? D1 : D0;
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                float x[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  const int s = s0 + 2 * e + u;
+                  const float w = ex2_approx((cum_t - cm[s]) * kLog2e) * dv[s];
+                  const float xv = __uint_as_float(r[2 * e + u]) * w;
+                  x[u] = s < t ? xv : (s == t ? xv + Dh : 0.f);
                 }
+                o[e] = pack_bf16x2(x[0], x[1]);
               }
             }
-            tmem_st8(lane_base + T_CB + 32 * j + 16 * g, o0);
-            tmem_st8(lane_base + T_CB + 32 * j + 16 * g + 8, o1);
+            tmem_st8(lane_base + T_CB + s0 + 8 * h, o);
+          }
+        };
+        {
+          uint32_t ra[16], rb[16];
+          if (npieces > 0) tmem_ld16(lane_base + T_CB + piece_col(0), ra);
+#pragma unroll 1
+          for (int i = 0; i < npieces; i += 2) {
+            tmem_ld_wait_regs(ra);
+            tmem_ld16(lane_base + T_CB + piece_col(i + 1), rb);
+            score_piece(i, ra);
+            tmem_ld_wait_regs(rb);
+            if (i + 2 < npieces) tmem_ld16(lane_base + T_CB + piece_col(i + 2), ra);
+            score_piece(i + 1, rb);
+          }
+          uint32_t z[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) z[k] = 0u;
+#pragma unroll 1
+          for (int i = npieces; i < 4; ++i) {
+            tmem_st8(lane_base + T_CB + piece_col(i), z);
+            tmem_st8(lane_base + T_CB + piece_col(i) + 8, z);
           }
         }
         tmem_st_wait();
@@ -896,25 +888,24 @@ ssd_tc_kernel(const __grid_constant__ CUtensorMap bc_map, const __grid_constant_
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_S_READY));
         ALLOY_TRACE_POINT(cw, c, 3);
-        ALLOY_TRACE_POINT(cw, c, 7);
       }
       // ---- final state -> ssm_out ----
       if (!*abort_flag && a.ssm_out && waitw(bar(B_ST_DONE), (nchunks - 1) & 1, abort_flag, 35)) {
         tc_fence_after();
-  #pragma unroll 1
-        for (int cc = 0; cc < NHALF / 32; ++cc) {
-          const int n0 = cw * NHALF + cc * 32;
-          uint32_t r[32];
-          tmem_ld32(lane_base + T_ST + n0, r);
+#pragma unroll 1
+        for (int n8 = 0; n8 < NHALF / 8; ++n8) {
+          const int n0 = cw * NHALF + n8 * 8;
+          uint32_t r[8];
+          tmem_ld8(lane_base + T_ST + n0, r);
           tmem_ld_wait();
-  #pragma unroll
-          for (int i = 0; i < 32; ++i)
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
             a.ssm_out[(int64_t)b * a.so_sb + (int64_t)(h0 + hr) * a.so_sh + (int64_t)(n0 + i) * a.so_sn +
                       (int64_t)pr * a.so_sp] = __uint_as_float(r[i]);
         }
       }
-      tc_fence_before();
     }
+    tc_fence_before();
   }
 
   __syncthreads();
@@ -964,7 +955,9 @@ bool ssd_tc_supported(const SsdArgs& a) {
 size_t ssd_tc_workspace_bytes(const SsdArgs& a) {
   int g0, gs;
   group_range(a, &g0, &gs);
-  return (size_t)a.B * a.L * 2 * gs * a.N * sizeof(__nv_bfloat16);
+  // B/C tiles of every chunk, the last one padded to Q rows
+  const size_t rows = (size_t)((a.L + Q - 1) / Q) * Q;
+  return (size_t)a.B * rows * 2 * gs * a.N * sizeof(__nv_bfloat16);
 }
 
 int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
@@ -1026,35 +1019,17 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
     }
     ALLOY_TRY(check_launch("bc_conv_kernel"));
   }
-  // 2. tensor map over the workspace [B][L][ncols], box 64 columns x 128 rows
-  CUtensorMap map;
-  const cuuint64_t gdim[3] = {(cuuint64_t)ncols, (cuuint64_t)s.L, (cuuint64_t)s.B};
-  const cuuint64_t gstride[2] = {(cuuint64_t)ncols * 2, (cuuint64_t)ncols * 2 * s.L};
-  const cuuint32_t box[3] = {64, (cuuint32_t)Q, 1};
-  CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, bc, gdim, gstride, box, estride,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(ALLOY_ERR_CUDA, "ssd_tc: cuTensorMapEncodeTiled failed (%d)", (int)r);
-  // 3. tensor map over xBC for the raw x rows: box 64 channels x (Q + 3) rows
-  CUtensorMap xmap;
-  {
-    const cuuint32_t xbox[3] = {64, (cuuint32_t)kRawRows, 1};
-    r = encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(s.xBC), xd, xs, xbox,
-               estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS)
-      return fail(ALLOY_ERR_CUDA, "ssd_tc: cuTensorMapEncodeTiled (xBC) failed (%d)", (int)r);
-  }
+  a.bc = bc;
   // 4. the SSD kernel
   dim3 grid(s.head_count / 2, s.B);
   if (s.N == 128) {
     ALLOY_CUDA(cudaFuncSetAttribute(ssd_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemBytes));
-    ssd_tc_kernel<128><<<grid, kThreads, kSmemBytes, stream>>>(map, xmap, a);
+    ssd_tc_kernel<128><<<grid, kThreads, kSmemBytes, stream>>>(a);
   } else {
     ALLOY_CUDA(cudaFuncSetAttribute(ssd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemBytes));
-    ssd_tc_kernel<64><<<grid, kThreads, kSmemBytes, stream>>>(map, xmap, a);
+    ssd_tc_kernel<64><<<grid, kThreads, kSmemBytes, stream>>>(a);
   }
   return check_launch("ssd_tc_kernel");
 }
