@@ -60,8 +60,12 @@ using namespace tc;
 constexpr int Q = 128;                 // chunk length (UMMA M)
 constexpr int P = 64;                  // head dim
 constexpr int kThreads = 640;          // 20 warps: 4 compute warpgroups + 1 role warpgroup
-constexpr int kRoleRegs = 64;          // registers per thread after the split: role warpgroup
-constexpr int kComputeRegs = 104;      // compute warpgroups (4 x 128 x 112 + 128 x 24 <= 640 x 96)
+// registers per thread after the split (launch: 640 x 96): the role and
+// consumer warpgroups give registers to the two producer warpgroups
+// (128 x 64 + 256 x 88 + 256 x 120 = 640 x 96)
+constexpr int kRoleRegs = 64;
+constexpr int kConsumerRegs = 88;
+constexpr int kProducerRegs = 120;
 constexpr int kTmaWarp = 16;           // B/C half tiles
 constexpr int kMmaWarp = 17;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -161,18 +165,6 @@ __device__ __forceinline__ bool waitw(uint32_t bar, uint32_t parity, volatile in
   ok = __all_sync(0xffffffffu, ok);
   if (!ok && (threadIdx.x & 31) == 0 && !*abort_flag) signal_abort(abort_flag, site);
   __syncwarp();
-  return ok;
-}
-
-// Barrier among the warps of one or both warpgroups, built on an mbarrier so
-// that it is bounded like every other wait (a hardware bar.sync is not).
-// `uses` counts this warp's previous uses of the barrier (its phase).
-__device__ __forceinline__ bool warps_sync(uint32_t bar, uint32_t& uses, volatile int* abort_flag,
-                                           int site) {
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
-  const bool ok = waitw(bar, uses & 1, abort_flag, site);
-  ++uses;
   return ok;
 }
 
@@ -328,8 +320,8 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
 // ----------------------------------------------------------------------------
 // the SSD kernel
 // ----------------------------------------------------------------------------
-// Roles (20 warps, launched with 96 registers a thread; the role warpgroup
-// hands registers to the compute warpgroups with setmaxnreg):
+// Roles (20 warps, launched with 96 registers a thread; the role and consumer
+// warpgroups hand registers to the producers with setmaxnreg):
 //   warps 0-7   consumers, warpgroup cw = 0/1.  Per chunk: the bf16 copy H of
 //               the state and its decay (state columns split by warpgroup),
 //               then the scores S of both heads for the 32-column blocks
@@ -384,13 +376,14 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
     tmem_alloc(base + OFF_TMEMPTR, 512);
     tmem_relinquish();
   }
-  // x conv weights of both heads, [head][channel][tap] and bias [head][channel]
+  // x conv weights of both heads, [head][channel][tap] and bias [head][channel],
+  // halved: the conv then gives h = x/2 and silu(x) = h + h tanh(h)
   if (threadIdx.x < 128) {
     const int hh = threadIdx.x >> 6, ch = threadIdx.x & 63;
     const int64_t c = (int64_t)(h0 + hh) * P + ch;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) cw_all[(hh * 64 + ch) * 4 + k] = a.conv_w[c * a.cw_sc + k * a.cw_sk];
-    cw_all[512 + hh * 64 + ch] = a.conv_b ? a.conv_b[c * a.cb_s] : 0.f;
+    for (int k = 0; k < 4; ++k) cw_all[(hh * 64 + ch) * 4 + k] = 0.5f * a.conv_w[c * a.cw_sc + k * a.cw_sk];
+    cw_all[512 + hh * 64 + ch] = a.conv_b ? 0.5f * a.conv_b[c * a.cb_s] : 0.f;
   }
   tc_fence_before();
   __syncthreads();
@@ -514,12 +507,12 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       }
     }
   } else {
-    reg_alloc<kComputeRegs>();
     const int q = warp & 3;               // TMEM lane quadrant
     const int t = q * 32 + lane;          // row of this thread (t, s or (h,p))
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     if (warp >= 8) {
       // ------------------------------------------------------------ producers (warps 8-15)
+      reg_alloc<kProducerRegs>();
       const int hh = (warp - 8) >> 2;     // head of the pair
       const int head = h0 + hh;
       const float A = -expf(a.A_log[(int64_t)head * a.al_s]);
@@ -616,35 +609,44 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       };
       for (int cc = 1; cc <= kL2Ahead; ++cc) prefetch_rows(cc);
       load_dt(0);
-      uint32_t wg_uses = 0;
-      // iteration c: chunk c (c >= 0), the rows of chunk c+1, the epilogue of c-1
+      // ---- dt, warp-local scan and column factors of chunk cc; the warp's
+      // total goes to wsum and the warp arrives on the group barrier, whose
+      // wait (for the prefix over the warps) comes when the chunk is produced
+      float v_c = 0.f, dt_c = 0.f, cf_c = 0.f;
+      auto scan_chunk = [&](int cc) {
+        const int cbuf = cc & 1;
+        const float dt = cc * Q + t < L
+            ? softplus_f32((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
+            : 0.f;
+        if (cc + 1 < nchunks) load_dt(cc + 1);
+        float v = A * dt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float u = __shfl_up_sync(0xffffffffu, v, o);
+          if (lane >= o) v += u;
+        }
+        // column factor relative to the end of this row's 16-step piece
+        const float vend = __shfl_sync(0xffffffffu, v, lane | 15);
+        cf_c = ex2_approx((vend - v) * kLog2e) * dt;
+        v_c = v;
+        dt_c = dt;
+        // (wsum is double-buffered by chunk parity: a warp writes it for chunk
+        // cc+2 only after the wait for cc+1, which every warp's arrival for
+        // cc+1 precedes, and each warp reads wsum(cc) before that arrival)
+        if (lane == 31) wsum[(cbuf * 2 + hh) * 4 + q] = v;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_PWG0 + hh));
+      };
+      // iteration c: chunk c (c >= 0); the rows and the scan of chunk c+1; the epilogue of c-1
       for (int c = -1; c <= nchunks; ++c) {
         if (c >= 0 && c < nchunks) {
           const int buf = c & 1;
-          const int t0 = c * Q;
           // X[buf] and cum/dt/cf[buf] held chunk c-2, whose epilogue this
           // warpgroup finished last iteration (after Y(c-2), and so after the
           // scores and the state copy of c-2)
           ALLOY_TRACE_POINT(4 + hh, c, 0);
-          // ---- dt, warp-local scan, column factors ----
-          const float dt = t0 + t < L
-              ? softplus_f32((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
-              : 0.f;
-          if (c + 1 < nchunks) load_dt(c + 1);
-          float v = A * dt;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const float u = __shfl_up_sync(0xffffffffu, v, o);
-            if (lane >= o) v += u;
-          }
-          // column factor relative to the end of this row's 16-step piece
-          const float vend = __shfl_sync(0xffffffffu, v, lane | 15);
-          const float cf = ex2_approx((vend - v) * kLog2e) * dt;
-          if (lane == 31) wsum[(buf * 2 + hh) * 4 + q] = v;
           // ---- prefix over the warps -> cumulative log decay ----
-          // (wsum is double-buffered by chunk parity: its next write, two
-          // chunks on, comes after every warp has passed the next chunk's sync)
-          if (!warps_sync(bar(B_PWG0 + hh), wg_uses, abort_flag, 22)) break;
+          if (!waitw(bar(B_PWG0 + hh), c & 1, abort_flag, 22)) break;
           float pre = 0.f, tot = 0.f;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -652,12 +654,12 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
             pre += i < q ? w : 0.f;
             tot += w;
           }
-          const float cum = v + pre;
+          const float cum = v_c + pre;
           cum_s[(buf * 2 + hh) * 128 + t] = cum;
-          dt_s[(buf * 2 + hh) * 128 + t] = dt;
-          cf_s[(buf * 2 + hh) * 128 + t] = cf;
+          dt_s[(buf * 2 + hh) * 128 + t] = dt_c;
+          cf_s[(buf * 2 + hh) * 128 + t] = cf_c;
           // X' factor of row t, read back below by the lanes of this warp that convolve the row
-          xf_s[hh * 128 + t] = ex2_approx((tot - cum) * kLog2e) * dt;
+          xf_s[hh * 128 + t] = ex2_approx((tot - cum) * kLog2e) * dt_c;
           __syncwarp();
           ALLOY_TRACE_POINT(4 + hh, c, 1);
           // X' is single-buffered: the state update of chunk c-1 read it
@@ -695,7 +697,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
               const int srow = strip * 16 + r - 3;
               if (((r - 3) & 3) == 0) fq = xf4[(r - 3) >> 2];
               const float fx = ((r - 3) & 3) == 0 ? fq.x : ((r - 3) & 3) == 1 ? fq.y : ((r - 3) & 3) == 2 ? fq.z : fq.w;
-              const bool valid = t0 + srow < L;
+              // (rows past L need no masking: X and X' there only meet dt = 0
+              // or outputs that are not stored)
               float y4[4];
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
@@ -705,7 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
                   const uint32_t wd = rw[r - 3 + k][i >> 1];
                   acc = fmaf((i & 1) ? bf16_hi(wd) : bf16_lo(wd), w[k][i], acc);
                 }
-                y4[i] = valid ? silu_fast(acc) : 0.f;
+                y4[i] = fmaf(acc, tanh_approx(acc), acc);   // silu of 2 acc
               }
               uint32_t o[2], ox[2];
               o[0] = pack_bf16x2(y4[0], y4[1]);
@@ -724,14 +727,18 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           if (lane == 0) mbar_arrive(bar(B_X_READY0 + buf));
           ALLOY_TRACE_POINT(4 + hh, c, 3);
         }
-        // the next chunk's rows, in flight during the epilogue below
-        if (c + 1 < nchunks) load_rows(c + 1);
+        // the next chunk's rows (in flight during the epilogue below) and its scan
+        if (c + 1 < nchunks) {
+          load_rows(c + 1);
+          scan_chunk(c + 1);
+        }
         // the previous chunk's output, while the tensor cores and consumers work on this one
         if (c > 0 && !epilogue(c - 1)) break;
         ALLOY_TRACE_POINT(4 + hh, c, 4);
       }
     } else {
       // ------------------------------------------------------------ consumers
+      reg_dealloc<kConsumerRegs>();
       const int cw = warp >> 2;           // consumer warpgroup
       const float D0 = a.Dp ? a.Dp[(int64_t)h0 * a.d_s] : 0.f;
       const float D1 = a.Dp ? a.Dp[(int64_t)(h0 + 1) * a.d_s] : 0.f;
