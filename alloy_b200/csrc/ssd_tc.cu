@@ -43,6 +43,9 @@
 #ifndef ALLOY_TRACE_POINT
 #define ALLOY_TRACE_POINT(role, chunk, id)
 #endif
+#ifndef ALLOY_TRACE_SPIN
+#define ALLOY_TRACE_SPIN()
+#endif
 #ifndef ALLOY_TRACE_COPY_DONE
 #define ALLOY_TRACE_COPY_DONE(bar, parity, role, chunk, id)
 #endif
@@ -86,7 +89,7 @@ constexpr uint32_t OFF_WSUM = OFF_CF + 2048;        // [2 buffers][2 heads][4 wa
 constexpr uint32_t OFF_CW = OFF_WSUM + 64;          // x conv weights [2][64][4] + bias [2][64]
 constexpr uint32_t OFF_XF = OFF_CW + 2560;          // X' row factors [2 heads][128]
 constexpr uint32_t OFF_BAR = OFF_XF + 1024;         // mbarriers (8 bytes each)
-constexpr int NBAR = 16;
+constexpr int NBAR = 17;
 constexpr uint32_t OFF_TMEMPTR = OFF_BAR + NBAR * 8;
 constexpr uint32_t OFF_ABORT = OFF_TMEMPTR + 8;
 constexpr uint32_t kSmemBytes = OFF_ABORT + 16 + 1024;  // + alignment slack
@@ -99,7 +102,8 @@ enum {
   B_HBF_READY,                                // consumers -> MMA: H written, state scaled
   B_S_READY,                                  // consumers -> MMA: scores in TMEM
   B_Y_FULL,                                   // MMA -> producers: Y and Yi complete
-  B_ST_DONE,                                  // MMA -> consumers, producers: state update done
+  B_ST_DONE,                                  // MMA -> producers: state update done (X' reusable)
+  B_YI_DONE,                                  // MMA -> consumers: Yi done (H reusable; state update done)
   B_Y_EMPTY0, B_Y_EMPTY1,                     // producers -> MMA: y read out (per buffer)
   B_PWG0, B_PWG1,                             // producer warpgroup syncs
   B_DRAIN
@@ -146,6 +150,7 @@ __device__ __forceinline__ bool wait1(uint32_t bar, uint32_t parity, volatile in
   const long long t0 = clock64();
   for (uint32_t it = 0; it < (1u << 30); ++it) {
     if (mbar_try_wait(bar, parity)) return true;
+    ALLOY_TRACE_SPIN();
     if (*abort_flag) return false;
     if (clock64() - t0 > kWaitCycles) break;
   }
@@ -160,6 +165,7 @@ __device__ __forceinline__ bool waitw(uint32_t bar, uint32_t parity, volatile in
   const long long t0 = clock64();
   bool ok;
   while (!(ok = mbar_try_wait(bar, parity) != 0)) {
+    ALLOY_TRACE_SPIN();
     if (*abort_flag || clock64() - t0 > kWaitCycles) break;
   }
   ok = __all_sync(0xffffffffu, ok);
@@ -336,8 +342,8 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
 //   warp 16     bulk copies of the B/C tiles.
 //   warp 17     TMEM allocation and the MMA issue (one thread).
 //   warps 18-19 no work (they complete the role warpgroup).
-// Per chunk the MMA thread issues CB, Yi (after the state copy), the state
-// update (after X'), then Y (after the scores).
+// Per chunk the MMA thread issues CB, the state update (after the state copy
+// and X'), Yi (after the previous epilogue), then Y (after the scores).
 template <int N>
 __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
   constexpr int NK = N / 64;            // 64-column halves of B/C per chunk
@@ -367,8 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    // FULL0/1 EMPTY0/1 X_READY0/1 CB_FULL HBF_READY S_READY Y_FULL ST_DONE Y_EMPTY0/1 PWG0/1 DRAIN
-    const int counts[NBAR] = {1, 1, 1, 1, 8, 8, 1, 8, 8, 1, 1, 8, 8, 4, 4, 1};
+    // FULL0/1 EMPTY0/1 X_READY0/1 CB_FULL HBF_READY S_READY Y_FULL ST_DONE YI_DONE Y_EMPTY0/1 PWG0/1 DRAIN
+    const int counts[NBAR] = {1, 1, 1, 1, 8, 8, 1, 8, 8, 1, 1, 1, 8, 8, 4, 4, 1};
     for (int i = 0; i < NBAR; ++i) mbar_init(bar(i), counts[i]);
     mbar_fence_init();
   }
@@ -450,21 +456,9 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           }
           umma_commit(bar(B_CB_FULL));
           ALLOY_TRACE_POINT(3, c, 0);
-          // Yi = C [H_0; H_1]^T for both heads at once (N = 128 rows (h, p));
-          // its columns and Y's held chunk c-1's output until its epilogue
-          if (c > 0 && !wait1(bar(B_Y_EMPTY0 + (buf ^ 1)), ((c - 1) >> 1) & 1, abort_flag, 5)) goto mma_done;
+          // state[(h,p), n] += X'^T B over s, once the state is scaled and
+          // copied (HBF) and X' has arrived with X
           if (!wait1(bar(B_HBF_READY), ph, abort_flag, 6)) goto mma_done;
-          tc_fence_after();
-          for (int k = 0; k < NK; ++k) {
-            const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
-            const uint32_t sH = base + OFF_H + k * 16384;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16(tmem + T_YI, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sH + 32 * kk, 16, 1024), ID_YI,
-                        (k | kk) != 0);
-          }
-          ALLOY_TRACE_POINT(3, c, 1);
-          // state[(h,p), n] += X'^T B over s (X' arrives with X); releases the stages
           if (!wait1(bar(B_X_READY0 + buf), (c >> 1) & 1, abort_flag, 8)) goto mma_done;
           ALLOY_TRACE_POINT(3, c, 9);
           tc_fence_after();
@@ -477,10 +471,26 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
             for (int kk = 0; kk < 8; ++kk)
               umma_bf16(tmem + T_ST, sw128_desc(sXp + 2048 * kk, 16384, 1024),
                         sw128_desc(sB + 2048 * kk, kStageBytes, 1024), ID_ST, 1);
-            for (int k = 0; k < NK; ++k) umma_commit(bar(B_EMPTY0 + ((c * NK + k) & 1)));
           }
           umma_commit(bar(B_ST_DONE));
           ALLOY_TRACE_POINT(3, c, 10);
+          // Yi = C [H_0; H_1]^T for both heads at once (N = 128 rows (h, p));
+          // its columns and Y's held chunk c-1's output until its epilogue.
+          // H is a copy, so the state update above does not disturb it.
+          if (c > 0 && !wait1(bar(B_Y_EMPTY0 + (buf ^ 1)), ((c - 1) >> 1) & 1, abort_flag, 5)) goto mma_done;
+          tc_fence_after();
+          for (int k = 0; k < NK; ++k) {
+            const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
+            const uint32_t sH = base + OFF_H + k * 16384;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(tmem + T_YI, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sH + 32 * kk, 16, 1024), ID_YI,
+                        (k | kk) != 0);
+          }
+          // the last reads of this chunk's B/C stages and of H
+          for (int k = 0; k < NK; ++k) umma_commit(bar(B_EMPTY0 + ((c * NK + k) & 1)));
+          umma_commit(bar(B_YI_DONE));
+          ALLOY_TRACE_POINT(3, c, 1);
           // Y_h = S_h X_h, S_h (bf16 pairs) read from tensor memory
           if (!wait1(bar(B_S_READY), ph, abort_flag, 7)) goto mma_done;
           ALLOY_TRACE_POINT(3, c, 8);
@@ -730,7 +740,9 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         // the next chunk's rows (in flight during the epilogue below) and its scan
         if (c + 1 < nchunks) {
           load_rows(c + 1);
+          ALLOY_TRACE_POINT(4 + hh, c + 1, 6);
           scan_chunk(c + 1);
+          ALLOY_TRACE_POINT(4 + hh, c + 1, 7);
         }
         // the previous chunk's output, while the tensor cores and consumers work on this one
         if (c > 0 && !epilogue(c - 1)) break;
@@ -772,7 +784,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         if (!waitw(bar(B_X_READY0 + buf), (c >> 1) & 1, abort_flag, 30)) break;
         ALLOY_TRACE_POINT(cw, c, 0);
         // ---- state: H = bf16(state) -> smem; state *= exp(cum[Q-1]) ----
-        if (c > 0 && !waitw(bar(B_ST_DONE), (c - 1) & 1, abort_flag, 31)) break;
+        // (Yi(c-1), the last reader of H, follows the state update of c-1)
+        if (c > 0 && !waitw(bar(B_YI_DONE), (c - 1) & 1, abort_flag, 31)) break;
         tc_fence_after();
         {
           const float e_end = ex2_approx(cum_s[(buf * 2 + hr) * 128 + 127] * kLog2e);
@@ -849,21 +862,24 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
                            f2_pack(f.z, f.w)));
               }
             } else {
-              // the diagonal block: exact factors (<= 1 for s <= t), zero right
-              // of the diagonal, D on it
-              const float* dv = dt_s + (buf * 2 + h) * 128;
+              // the diagonal block: exact factors (<= 1 for s <= t, at any decay
+              // range), zero right of the diagonal, D on it
+              const float4* cm4 = reinterpret_cast<const float4*>(cm + s0);
+              const float4* dv4 = reinterpret_cast<const float4*>(dt_s + (buf * 2 + h) * 128 + s0);
               const float Dh = h ? D1 : D0;
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                float x[2];
+              for (int i4 = 0; i4 < 4; ++i4) {
+                const float4 c4 = cm4[i4], d4 = dv4[i4];
+                const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, ds[4] = {d4.x, d4.y, d4.z, d4.w};
+                float x[4];
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                  const int s = s0 + 2 * e + u;
-                  const float w = ex2_approx((cum_t - cm[s]) * kLog2e) * dv[s];
-                  const float xv = __uint_as_float(r[2 * e + u]) * w;
+                for (int u = 0; u < 4; ++u) {
+                  const int s = s0 + 4 * i4 + u;
+                  const float xv = __uint_as_float(r[4 * i4 + u]) * (ex2_approx((cum_t - cs[u]) * kLog2e) * ds[u]);
                   x[u] = s < t ? xv : (s == t ? xv + Dh : 0.f);
                 }
-                o[e] = pack_bf16x2(x[0], x[1]);
+                o[2 * i4] = pack_bf16x2(x[0], x[1]);
+                o[2 * i4 + 1] = pack_bf16x2(x[2], x[3]);
               }
             }
             tmem_st8(lane_base + T_CB + s0 + 8 * h, o);
@@ -875,11 +891,14 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
 #pragma unroll 1
           for (int i = 0; i < npieces; i += 2) {
             tmem_ld_wait_regs(ra);
+            if (i == 0) ALLOY_TRACE_POINT(cw, c, 8);
             tmem_ld16(lane_base + T_CB + piece_col(i + 1), rb);
             score_piece(i, ra);
+            if (i == 0) ALLOY_TRACE_POINT(cw, c, 9);
             tmem_ld_wait_regs(rb);
             if (i + 2 < npieces) tmem_ld16(lane_base + T_CB + piece_col(i + 2), ra);
             score_piece(i + 1, rb);
+            if (i == 0) ALLOY_TRACE_POINT(cw, c, 10);
           }
           uint32_t z[8];
 #pragma unroll
@@ -890,14 +909,16 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
             tmem_st8(lane_base + T_CB + piece_col(i) + 8, z);
           }
         }
+        ALLOY_TRACE_POINT(cw, c, 11);
         tmem_st_wait();
+        ALLOY_TRACE_POINT(cw, c, 12);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_S_READY));
         ALLOY_TRACE_POINT(cw, c, 3);
       }
       // ---- final state -> ssm_out ----
-      if (!*abort_flag && a.ssm_out && waitw(bar(B_ST_DONE), (nchunks - 1) & 1, abort_flag, 35)) {
+      if (!*abort_flag && a.ssm_out && waitw(bar(B_YI_DONE), (nchunks - 1) & 1, abort_flag, 35)) {
         tc_fence_after();
 #pragma unroll 1
         for (int n8 = 0; n8 < NHALF / 8; ++n8) {

@@ -316,6 +316,32 @@ def test_tensor_core_ssd_vs_oracle(cfg):
     np.testing.assert_array_equal(np_(cs), cs_ref)
 
 
+@pytest.mark.parametrize("dt_bias", [
+    [8.0, 8.0, 8.0, 8.0],          # |A dt| of 8 to 128 a step: every 16-step piece spans > e^80
+    [-3.0, 0.0, 1.5, 3.0],         # per-head ranges on both sides of that bound
+])
+def test_tensor_core_ssd_strong_decay(dt_bias):
+    """Fast-decaying heads take the exact-exponent path on the diagonal pieces
+    of the scores (a decay range over 16 steps beyond e^80); parity with the
+    oracle holds there too."""
+    cfg = dict(B=2, L=700, H=4, P=64, N=128, G=1)
+    inp = oracle.make_inputs(**cfg, dtype="bf16", seed=23, with_state=True)
+    inp["dt_bias"] = np.asarray(dt_bias, np.float32)
+    y_ref, h_ref, _ = oracle.mixer_core(
+        inp["xBC"], inp["dt_raw"], inp["conv_weight"], inp["conv_bias"], inp["dt_bias"],
+        inp["A_log"], inp["D"], n_heads=4, headdim=64, d_state=128, n_groups=1, chunk_size=256,
+        ssm_state=inp["ssm_state"], conv_state=inp["conv_state"])
+    y, h, _ = mixer.ssd_combined(
+        cu(inp["xBC"], torch.bfloat16), cu(inp["dt_raw"], torch.bfloat16),
+        cu(inp["conv_weight"]), cu(inp["conv_bias"]), cu(inp["dt_bias"]), cu(inp["A_log"]),
+        cu(inp["D"]), n_heads=4, head_dim=64, d_state=128, n_groups=1,
+        ssm_state=cu(inp["ssm_state"]), conv_state=cu(inp["conv_state"], torch.bfloat16))
+    mixer.check_device_status()
+    assert np.isfinite(np_(y)).all() and np.isfinite(np_(h)).all()
+    assert_close(np_(y), y_ref, True)
+    assert_close(np_(h), h_ref, True)
+
+
 def test_tensor_core_ssd_is_deterministic_and_chunk_independent():
     cfg = dict(B=1, L=600, H=4, P=64, N=128, G=1)
     inp = oracle.make_inputs(**cfg, dtype="bf16", seed=22)
