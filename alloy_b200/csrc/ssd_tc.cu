@@ -202,12 +202,12 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
 // swizzle of a K-major UMMA operand tile).  Rows past L are zeros.  Source
 // column of (part, gl, n): H*P + part*G*N + (group_begin + gl)*N + n.
 //
-// One CTA per (128-row tile, kBcW-column tile, batch row): a single tensor
-// copy brings rows [t0 - 3, t0 + 128) of the tile's columns into shared
+// One CTA per (kBcTileRows-row tile, W-column tile, batch row): a single tensor
+// copy brings rows [t0 - 3, t0 + kBcTileRows) of the tile's columns into shared
 // memory (rows outside [0, L) arrive as zeros; rows before 0 are then taken
 // from the conv cache), and each thread convolves 8 adjacent columns over a
 // strip of rows with the last 3 inputs kept in registers.
-constexpr int kBcTileRows = 128;
+constexpr int kBcTileRows = 128;   // one chunk (64-row tiles measured slower: per-CTA setup dominates)
 
 template <int W>   // tile width in columns: 256, 128 or 64
 __global__ void __launch_bounds__(256)
@@ -239,8 +239,11 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
   // this thread's 8 columns in the tile layout
   const int rem = j0 - part * span + cg * 8;   // gl * N + n
   const int gl = rem / a.N, n = rem % a.N;
-  const int nchunks = (a.L + kBcTileRows - 1) / kBcTileRows;
-  const int64_t tile = ((((int64_t)b * nchunks + blockIdx.x) * a.group_count + gl) * (a.N / 64) + n / 64) * 2 + part;
+  const int nchunks = (a.L + Q - 1) / Q;
+  constexpr int kTilesPerChunk = Q / kBcTileRows;
+  const int chunk = blockIdx.x / kTilesPerChunk;
+  const int row0 = (blockIdx.x % kTilesPerChunk) * kBcTileRows;   // first row of the tile inside its chunk
+  const int64_t tile = ((((int64_t)b * nchunks + chunk) * a.group_count + gl) * (a.N / 64) + n / 64) * 2 + part;
   // taps and bias as channel pairs (loaded while the copy is in flight)
   uint64_t w2[4][4], b2[4];
 #pragma unroll
@@ -318,7 +321,7 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
       win[1][i] = win[2][i];
       win[2][i] = x[i];
     }
-    const int row = r0 + r;
+    const int row = row0 + r0 + r;
     *reinterpret_cast<uint4*>(dst + row * 128 + ((nn8 ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
@@ -1035,7 +1038,8 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
       return fail(ALLOY_ERR_CUDA, "ssd_tc: cuTensorMapEncodeTiled (B/C tile) failed (%d)", (int)r);
-    dim3 grid((s.L + kBcTileRows - 1) / kBcTileRows, ncols / W, s.B);
+    // every row of every chunk, the padded rows past L included (written as zeros)
+    dim3 grid(((s.L + Q - 1) / Q) * (Q / kBcTileRows), ncols / W, s.B);
     const int smem = (kBcTileRows + 3) * W * 2;
     if (W == 256) {
       ALLOY_CUDA(cudaFuncSetAttribute(bc_conv_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));

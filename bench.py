@@ -52,10 +52,11 @@ L2_BYTES = 126 * 1024 * 1024
 LAUNCHES_PER_STEP = 3
 FALLBACK_HBM_GBS = 6650.0
 
-# DRAM bytes per launch of the dominant kernel measured with ncu (read + write),
-# keyed by (workload, n_gpus); see profiles/ for the captures.  None = not yet
-# captured for that configuration.
-NCU_TRAFFIC_BYTES = {}
+# DRAM bytes (read + write) of one prefill step on one GPU, measured with ncu
+# over the step's three launches (B/C pre-pass, SSD, conv-cache roll), keyed by
+# (workload, n_gpus); profiles/prefill_nemotron_b4_launch_list.md has the
+# capture.  Configurations not captured report None.
+NCU_TRAFFIC_BYTES = {("nemotron", 1): (134.3 + 82.0 + 685.4 + 507.3 + 0.4) * 1e6}
 
 
 def measured_peaks():
