@@ -54,8 +54,8 @@ FALLBACK_HBM_GBS = 6650.0
 
 # DRAM bytes (read + write) of one prefill step on one GPU, measured with ncu
 # over the step's three launches (B/C pre-pass, SSD, conv-cache roll), keyed by
-# (workload, n_gpus); profiles/prefill_nemotron_b4_launch_list.md has the
-# capture.  Configurations not captured report None.
+# (workload, n_gpus); the capture's summary is kept under profiles/.
+# Configurations not captured report None.
 NCU_TRAFFIC_BYTES = {("nemotron", 1): (134.3 + 82.0 + 685.4 + 507.3 + 0.4) * 1e6}
 
 
