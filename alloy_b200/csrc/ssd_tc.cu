@@ -217,6 +217,8 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
   constexpr int R = kBcTileRows * CG / 256;   // rows per thread
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t full_bar;
+  __shared__ float4 taps_s[W];     // the tile's conv taps and bias, halved (silu(2h) = h + h tanh h)
+  __shared__ float bias_s[W];
   const uint32_t stile = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
   const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&full_bar));
   const int b = blockIdx.z;
@@ -228,6 +230,13 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
   if (threadIdx.x == 0) {
     mbar_init(bar, 1);
     mbar_fence_init();
+  }
+  if (threadIdx.x < W) {   // one column each, consecutive threads on consecutive columns
+    const int64_t ch = src0 + threadIdx.x;
+    taps_s[threadIdx.x] = make_float4(0.5f * a.conv_w[ch * a.cw_sc], 0.5f * a.conv_w[ch * a.cw_sc + a.cw_sk],
+                                      0.5f * a.conv_w[ch * a.cw_sc + 2 * a.cw_sk],
+                                      0.5f * a.conv_w[ch * a.cw_sc + 3 * a.cw_sk]);
+    bias_s[threadIdx.x] = a.conv_b ? 0.5f * a.conv_b[ch * a.cb_s] : 0.f;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -244,16 +253,16 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
   const int chunk = blockIdx.x / kTilesPerChunk;
   const int row0 = (blockIdx.x % kTilesPerChunk) * kBcTileRows;   // first row of the tile inside its chunk
   const int64_t tile = ((((int64_t)b * nchunks + chunk) * a.group_count + gl) * (a.N / 64) + n / 64) * 2 + part;
-  // taps and bias as channel pairs (loaded while the copy is in flight)
+  // halved taps and bias of this thread's 8 columns, as channel pairs
   uint64_t w2[4][4], b2[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      w2[k][i] = f2_pack(a.conv_w[(int64_t)(c + 2 * i) * a.cw_sc + k * a.cw_sk],
-                         a.conv_w[(int64_t)(c + 2 * i + 1) * a.cw_sc + k * a.cw_sk]);
-    b2[i] = a.conv_b ? f2_pack(a.conv_b[(int64_t)(c + 2 * i) * a.cb_s], a.conv_b[(int64_t)(c + 2 * i + 1) * a.cb_s])
-                     : f2_splat(0.f);
+    const float4 t0v = taps_s[cg * 8 + 2 * i], t1v = taps_s[cg * 8 + 2 * i + 1];
+    w2[0][i] = f2_pack(t0v.x, t1v.x);
+    w2[1][i] = f2_pack(t0v.y, t1v.y);
+    w2[2][i] = f2_pack(t0v.z, t1v.z);
+    w2[3][i] = f2_pack(t0v.w, t1v.w);
+    b2[i] = f2_pack(bias_s[cg * 8 + 2 * i], bias_s[cg * 8 + 2 * i + 1]);
   }
   // bounded wait for the tile; on timeout record the error and give the copy
   // a second bounded period before the CTA leaves
@@ -316,7 +325,10 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
       acc = f2_fma(win[1][i], w2[1][i], acc);
       acc = f2_fma(win[2][i], w2[2][i], acc);
       acc = f2_fma(x[i], w2[3][i], acc);
-      o[i] = t0 + r0 + r < a.L ? f2_to_bf2(f2_silu(acc)) : 0u;
+      // acc = h = x/2: silu(x) = h + h tanh(h)
+      float hl, hh;
+      f2_unpack(acc, hl, hh);
+      o[i] = t0 + r0 + r < a.L ? pack_bf16x2(fmaf(hl, tanh_approx(hl), hl), fmaf(hh, tanh_approx(hh), hh)) : 0u;
       win[0][i] = win[1][i];
       win[1][i] = win[2][i];
       win[2][i] = x[i];
