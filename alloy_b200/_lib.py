@@ -43,8 +43,10 @@ EXPORTS = (
     "alloy_selective_scan",
     "alloy_ssd_decode_step",
     "alloy_ssd_combined_workspace_size",
+    "alloy_ssd_combined_min_workspace_size",
     "alloy_check_device_status",
     "alloy_ssd_combined_noalloc",
+    "alloy_kernel_launch_count",
 )
 
 
@@ -116,7 +118,12 @@ def load():
         lib.alloy_ssd_combined_workspace_size.argtypes = [ctypes.c_int64, ctypes.c_int64,
                                                           ctypes.c_int32, D]
         lib.alloy_ssd_combined_workspace_size.restype = ctypes.c_size_t
+        lib.alloy_ssd_combined_min_workspace_size.argtypes = [ctypes.c_int64, ctypes.c_int64,
+                                                          ctypes.c_int32, D]
+        lib.alloy_ssd_combined_min_workspace_size.restype = ctypes.c_size_t
         lib.alloy_check_device_status.argtypes = [vp]
+        lib.alloy_kernel_launch_count.argtypes = []
+        lib.alloy_kernel_launch_count.restype = ctypes.c_uint64
         lib.alloy_ssd_combined_noalloc.argtypes = [P] * 12 + [D, vp]
         lib.alloy_selective_scan.argtypes = [P] * 8 + [vp]
         lib.alloy_ssd_decode_step.argtypes = [P] * 10 + [D, vp]

@@ -13,6 +13,11 @@ std::string& last_error() {
   return msg;
 }
 
+std::atomic<uint64_t>& launch_counter() {
+  static std::atomic<uint64_t> n{0};
+  return n;
+}
+
 int current_device_checked(int* dev) {
   // 0 = unchecked, 1 = sm_100, 2 = other architecture (per device, checked once)
   static int arch_ok[kMaxDevices] = {0};
@@ -65,6 +70,26 @@ int check_dims(const alloy_ssd_dims_t* d, int64_t* h0, int64_t* hc) {
 }
 
 }  // namespace
+
+size_t ssd_combined_workspace(int64_t batch, int64_t seqlen, int32_t dtype, const alloy_ssd_dims_t* dims,
+                              bool full) {
+  int64_t h0 = 0, hc = 0;
+  if (check_dims(dims, &h0, &hc) != ALLOY_OK || batch < 0 || seqlen < 0) return 0;
+  SsdArgs a;
+  memset(&a, 0, sizeof(a));
+  a.mode = 0;
+  a.B = (int)batch; a.L = (int)seqlen; a.H = (int)dims->n_heads; a.P = (int)dims->head_dim;
+  a.N = (int)dims->d_state; a.G = (int)dims->n_groups; a.K = (int)dims->d_conv;
+  a.head_begin = (int)h0; a.head_count = (int)hc;
+  a.xbc_bf16 = a.y_bf16 = (dtype == ALLOY_BF16);
+  a.y_sp = 1;
+  // layout conditions are checked per call; size the workspace by dims alone
+  if (!a.xbc_bf16 || a.P != 64 || !(a.N == 64 || a.N == 128) || a.K != 4 ||
+      (a.H / a.G) % 2 != 0 || a.head_begin % 2 != 0 || a.head_count % 2 != 0)
+    return 0;
+  return full ? ssd_tc_workspace_bytes(a) : ssd_tc_workspace_min_bytes(a);
+}
+
 }  // namespace alloy
 
 using namespace alloy;
@@ -211,24 +236,18 @@ int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t* dt_raw,
   return ALLOY_OK;
 }
 
+
 size_t alloy_ssd_combined_workspace_size(int64_t batch, int64_t seqlen, int32_t dtype,
                                          const alloy_ssd_dims_t* dims) {
-  int64_t h0 = 0, hc = 0;
-  if (check_dims(dims, &h0, &hc) != ALLOY_OK || batch < 0 || seqlen < 0) return 0;
-  SsdArgs a;
-  memset(&a, 0, sizeof(a));
-  a.mode = 0;
-  a.B = (int)batch; a.L = (int)seqlen; a.H = (int)dims->n_heads; a.P = (int)dims->head_dim;
-  a.N = (int)dims->d_state; a.G = (int)dims->n_groups; a.K = (int)dims->d_conv;
-  a.head_begin = (int)h0; a.head_count = (int)hc;
-  a.xbc_bf16 = a.y_bf16 = (dtype == ALLOY_BF16);
-  a.y_sp = 1;
-  // layout conditions are checked per call; size the workspace by dims alone
-  if (!a.xbc_bf16 || a.P != 64 || !(a.N == 64 || a.N == 128) || a.K != 4 ||
-      (a.H / a.G) % 2 != 0 || a.head_begin % 2 != 0 || a.head_count % 2 != 0)
-    return 0;
-  return ssd_tc_workspace_bytes(a);
+  return ssd_combined_workspace(batch, seqlen, dtype, dims, true);
 }
+
+size_t alloy_ssd_combined_min_workspace_size(int64_t batch, int64_t seqlen, int32_t dtype,
+                                             const alloy_ssd_dims_t* dims) {
+  return ssd_combined_workspace(batch, seqlen, dtype, dims, false);
+}
+
+uint64_t alloy_kernel_launch_count(void) { return launch_counter().load(std::memory_order_relaxed); }
 
 int alloy_check_device_status(void* stream) {
   last_error().clear();

@@ -7,6 +7,7 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <stdarg.h>
+#include <atomic>
 #include <string>
 
 #include "alloy_ssd.h"
@@ -41,13 +42,19 @@ inline int cuda_status(cudaError_t e, const char* what) {
 
 #define ALLOY_CUDA(expr) ALLOY_TRY(::alloy::cuda_status((expr), #expr))
 
-// Reports a failed launch (bad configuration, missing device code, ...).
+// kernels this library launched in this process (alloy_kernel_launch_count)
+std::atomic<uint64_t>& launch_counter();
+
+// Reports a failed launch (bad configuration, missing device code, ...) and
+// counts the ones that went out.  Every kernel launch of the library is
+// followed by this check.
 inline int check_launch(const char* name) {
   cudaError_t e = cudaPeekAtLastError();
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(ALLOY_ERR_CUDA, "launch of %s failed: %s", name, cudaGetErrorString(e));
   }
+  launch_counter().fetch_add(1, std::memory_order_relaxed);
   return ALLOY_OK;
 }
 

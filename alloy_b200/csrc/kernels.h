@@ -71,7 +71,12 @@ int ssd_decode_step(const DecodeArgs& a, cudaStream_t s);
 // ssd_tc.cu: tcgen05 tensor-core SSD for bf16 inputs (mode 0 only).
 // Returns ALLOY_ERR_UNSUPPORTED (and launches nothing) for sizes it does not cover.
 bool ssd_tc_supported(const SsdArgs& a);
-size_t ssd_tc_workspace_bytes(const SsdArgs& a);
+size_t ssd_tc_workspace_bytes(const SsdArgs& a);       // with the sequence-segment states (fastest)
+size_t ssd_tc_workspace_min_bytes(const SsdArgs& a);   // the B/C tiles alone (one CTA per head pair)
+// workspace of alloy_ssd_combined for a layer: full size, or the smallest that
+// runs (full == false); 0 when none is needed
+size_t ssd_combined_workspace(int64_t batch, int64_t seqlen, int32_t dtype, const alloy_ssd_dims_t* dims,
+                              bool full);
 int ssd_tc(const SsdArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t s);
 // Synchronises the stream, then reads and clears the error word that a CTA
 // of the tensor-core SSD writes when one of its bounded waits runs out.

@@ -57,7 +57,7 @@ extern "C" int alloy_ssd_combined_noalloc(
     const alloy_ssd_dims_t* dims, void* stream) {
   size_t need = 0;
   if (xBC != nullptr && xBC->ndim == 3 && dims != nullptr)
-    need = alloy_ssd_combined_workspace_size(xBC->shape[0], xBC->shape[1], xBC->dtype, dims);
+    need = ssd_combined_workspace(xBC->shape[0], xBC->shape[1], xBC->dtype, dims, false);
   if (need > kNoAllocScratchBytes) {
     last_error().clear();
     return fail(ALLOY_ERR_UNSUPPORTED,
@@ -70,8 +70,9 @@ extern "C" int alloy_ssd_combined_noalloc(
     const int st = scratch_of_current_device(&ws);
     if (st != ALLOY_OK) return st;
   }
-  // Every element of the scratch that the scan reads is written by the B/C
-  // pre-pass of the same call, so nothing needs clearing between calls.
+  // Every element of the scratch that the scan reads is written earlier in
+  // the same call (by the B/C pre-pass, or by the state-only pass of a
+  // segmented call), so nothing needs clearing between calls.
   return alloy_ssd_combined(xBC, dt_raw, conv_w, conv_b, dt_bias, A_log, D, ssm_in, conv_in, y,
                             ssm_out, conv_out, ws, need > 0 ? kNoAllocScratchBytes : 0, dims,
                             stream);

@@ -35,6 +35,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tc_ptx.cuh"
@@ -63,12 +65,16 @@ using namespace tc;
 constexpr int Q = 128;                 // chunk length (UMMA M)
 constexpr int P = 64;                  // head dim
 constexpr int kThreads = 640;          // 20 warps: 4 compute warpgroups + 1 role warpgroup
-// registers per thread after the split (launch: 640 x 96): the role and
-// consumer warpgroups give registers to the two producer warpgroups
-// (128 x 64 + 256 x 88 + 256 x 120 = 640 x 96)
-constexpr int kRoleRegs = 64;
-constexpr int kConsumerRegs = 88;
+// registers per thread after the split (launch: 640 x 96, i.e. 480 a thread
+// summed over one thread of each of the five warpgroups): the full pass gives
+// 2 x 120 to the producers, 2 x 80 to the consumers, 80 to the role warps; the
+// state-only pass (no scores, the conv dominant) 2 x 136, 2 x 72 and 56
 constexpr int kProducerRegs = 120;
+constexpr int kConsumerRegs = 88;
+constexpr int kRoleRegs = 64;
+constexpr int kProducerRegsS = 136;
+constexpr int kConsumerRegsS = 72;
+constexpr int kRoleRegsS = 56;
 constexpr int kTmaWarp = 16;           // B/C half tiles
 constexpr int kMmaWarp = 17;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -131,6 +137,14 @@ struct TcArgs {
   float* ssm_out; int64_t so_sb, so_sh, so_sn, so_sp;
   __nv_bfloat16* y; int64_t y_sb, y_st, y_sh;
   const __nv_bfloat16* bc;   // B/C tile workspace
+  // sequence segments (gridDim.z of the full kernel): segment s of a (batch
+  // row, head pair) covers chunks [s nchunks / nseg, (s+1) nchunks / nseg)
+  int nseg;
+  // [B][head pairs][nseg][128 (h,p)][N]: record 0 the call's initial state,
+  // record s + 1 the end state of segment s (segment 0 from the initial state,
+  // later segments from zero), written by the state-only pass
+  float* seg_state;
+  float* seg_logdecay;       // [B][head pairs][nseg][2]: sum of A dt over segment s, per head
 };
 
 // ----------------------------------------------------------------------------
@@ -359,7 +373,7 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
 //   warps 18-19 no work (they complete the role warpgroup).
 // Per chunk the MMA thread issues CB, the state update (after the state copy
 // and X'), Yi (after the previous epilogue), then Y (after the scores).
-template <int N>
+template <int N, bool kStateOnly>
 __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
   constexpr int NK = N / 64;            // 64-column halves of B/C per chunk
   constexpr int NHALF = N / 2;          // state columns per consumer warpgroup
@@ -385,6 +399,11 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
   const int gl = h0 / hpg - a.group_begin;        // group index inside the workspace
   const int L = a.L;
   const int nchunks = (L + Q - 1) / Q;
+  // this CTA's segment: chunks [c_lo, c_lo + nk); the loops below count c from 0
+  // (32-bit unsigned: nseg <= the SM count and nchunks < 2^24 keep the products in range)
+  const int seg = blockIdx.z;
+  const int c_lo = (int)((unsigned)seg * (unsigned)nchunks / (unsigned)a.nseg);
+  const int nk = (int)((unsigned)(seg + 1) * (unsigned)nchunks / (unsigned)a.nseg) - c_lo;
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
@@ -413,19 +432,20 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
 
   if (warp >= 16) {
     // role warpgroup: hand registers to the compute warpgroups
-    reg_dealloc<kRoleRegs>();
+    reg_dealloc<kStateOnly ? kRoleRegsS : kRoleRegs>();
     if (warp == kTmaWarp) {
       // ------------------------------------------------------------ B/C copies
       if (lane == 0) {
         // this pair's group: chunk c's B/C halves are NK consecutive 32 KB
         // stage images [B half k | C half k]
         const int64_t chunk_stride = (int64_t)a.group_count * NK * kStageBytes;
+        // (src0: this segment's first chunk)
         const unsigned char* src0 = reinterpret_cast<const unsigned char*>(a.bc) +
-                                    ((int64_t)b * nchunks * a.group_count + gl) * NK * kStageBytes;
-        for (int c = 1; c <= kL2Ahead && c < nchunks; ++c) bulk_prefetch_l2(src0 + c * chunk_stride, NK * kStageBytes);
+                                    (((int64_t)b * nchunks + c_lo) * a.group_count + gl) * NK * kStageBytes;
+        for (int c = 1; c <= kL2Ahead && c < nk; ++c) bulk_prefetch_l2(src0 + c * chunk_stride, NK * kStageBytes);
         int issued = 0;
-        for (int c = 0; c < nchunks; ++c) {
-          if (c + kL2Ahead < nchunks) bulk_prefetch_l2(src0 + (c + kL2Ahead) * chunk_stride, NK * kStageBytes);
+        for (int c = 0; c < nk; ++c) {
+          if (c + kL2Ahead < nk) bulk_prefetch_l2(src0 + (c + kL2Ahead) * chunk_stride, NK * kStageBytes);
           for (int k = 0; k < NK; ++k) {
             const int i = c * NK + k, slot = i & 1;
             if (i >= 2 && !wait1(bar(B_EMPTY0 + slot), ((i >> 1) - 1) & 1, abort_flag, 2)) goto bc_done;
@@ -452,24 +472,27 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         constexpr uint32_t ID_YI = idesc_bf16(128, 128, 0, 0);
         constexpr uint32_t ID_ST = idesc_bf16(128, N, 1, 1);
         constexpr uint32_t ID_Y = idesc_bf16(128, 64, 0, 1);
-        for (int c = 0; c < nchunks; ++c) {
+        for (int c = 0; c < nk; ++c) {
           const uint32_t ph = c & 1, pph = (c - 1) & 1;
           const int buf = c & 1;
           // CB = C B^T over the N halves; the region held the previous scores,
-          // so Y(c-1) must have completed
+          // so Y(c-1) must have completed (the state-only pass just waits for
+          // the stages)
           for (int k = 0; k < NK; ++k) {
             const int i = c * NK + k, slot = i & 1;
             if (!wait1(bar(B_FULL0 + slot), (i >> 1) & 1, abort_flag, 3)) goto mma_done;
             ALLOY_TRACE_POINT(3, c, 5 + k);
-            if (k == 0 && c > 0 && !wait1(bar(B_Y_FULL), pph, abort_flag, 4)) goto mma_done;
-            tc_fence_after();
-            const uint32_t sB = base + OFF_STAGE + slot * kStageBytes, sC = sB + 16384;
+            if constexpr (!kStateOnly) {
+              if (k == 0 && c > 0 && !wait1(bar(B_Y_FULL), pph, abort_flag, 4)) goto mma_done;
+              tc_fence_after();
+              const uint32_t sB = base + OFF_STAGE + slot * kStageBytes, sC = sB + 16384;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16(tmem + T_CB, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sB + 32 * kk, 16, 1024), ID_CB,
-                        (k | kk) != 0);
+              for (int kk = 0; kk < 4; ++kk)
+                umma_bf16(tmem + T_CB, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sB + 32 * kk, 16, 1024), ID_CB,
+                          (k | kk) != 0);
+            }
           }
-          umma_commit(bar(B_CB_FULL));
+          if constexpr (!kStateOnly) umma_commit(bar(B_CB_FULL));
           ALLOY_TRACE_POINT(3, c, 0);
           // state[(h,p), n] += X'^T B over s, once the state is scaled and
           // copied (HBF) and X' has arrived with X
@@ -492,33 +515,37 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           // Yi = C [H_0; H_1]^T for both heads at once (N = 128 rows (h, p));
           // its columns and Y's held chunk c-1's output until its epilogue.
           // H is a copy, so the state update above does not disturb it.
-          if (c > 0 && !wait1(bar(B_Y_EMPTY0 + (buf ^ 1)), ((c - 1) >> 1) & 1, abort_flag, 5)) goto mma_done;
-          tc_fence_after();
-          for (int k = 0; k < NK; ++k) {
-            const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
-            const uint32_t sH = base + OFF_H + k * 16384;
+          if constexpr (!kStateOnly) {
+            if (c > 0 && !wait1(bar(B_Y_EMPTY0 + (buf ^ 1)), ((c - 1) >> 1) & 1, abort_flag, 5)) goto mma_done;
+            tc_fence_after();
+            for (int k = 0; k < NK; ++k) {
+              const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
+              const uint32_t sH = base + OFF_H + k * 16384;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16(tmem + T_YI, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sH + 32 * kk, 16, 1024), ID_YI,
-                        (k | kk) != 0);
+              for (int kk = 0; kk < 4; ++kk)
+                umma_bf16(tmem + T_YI, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sH + 32 * kk, 16, 1024),
+                          ID_YI, (k | kk) != 0);
+            }
           }
           // the last reads of this chunk's B/C stages and of H
           for (int k = 0; k < NK; ++k) umma_commit(bar(B_EMPTY0 + ((c * NK + k) & 1)));
           umma_commit(bar(B_YI_DONE));
           ALLOY_TRACE_POINT(3, c, 1);
           // Y_h = S_h X_h, S_h (bf16 pairs) read from tensor memory
-          if (!wait1(bar(B_S_READY), ph, abort_flag, 7)) goto mma_done;
-          ALLOY_TRACE_POINT(3, c, 8);
-          tc_fence_after();
+          if constexpr (!kStateOnly) {
+            if (!wait1(bar(B_S_READY), ph, abort_flag, 7)) goto mma_done;
+            ALLOY_TRACE_POINT(3, c, 8);
+            tc_fence_after();
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t sX = base + OFF_X + (buf * 2 + h) * 16384;
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t sX = base + OFF_X + (buf * 2 + h) * 16384;
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma_bf16_ta(tmem + T_Y + 64 * h, tmem + T_CB + 16 * kk + 8 * h, sw128_desc(sX + 2048 * kk, 16, 1024),
-                           ID_Y, kk != 0);
+              for (int kk = 0; kk < 8; ++kk)
+                umma_bf16_ta(tmem + T_Y + 64 * h, tmem + T_CB + 16 * kk + 8 * h,
+                             sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
+            }
+            umma_commit(bar(B_Y_FULL));
           }
-          umma_commit(bar(B_Y_FULL));
           ALLOY_TRACE_POINT(3, c, 2);
         }
       mma_done:
@@ -537,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     if (warp >= 8) {
       // ------------------------------------------------------------ producers (warps 8-15)
-      reg_alloc<kProducerRegs>();
+      reg_alloc<kStateOnly ? kProducerRegsS : kProducerRegs>();
       const int hh = (warp - 8) >> 2;     // head of the pair
       const int head = h0 + hh;
       const float A = -expf(a.A_log[(int64_t)head * a.al_s]);
@@ -550,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       const int64_t dt_row = (int64_t)b * a.dt_sb + (int64_t)head * a.dt_sh;
       uint32_t dt_bits = 0;   // raw dt of the chunk about to be produced (converted when used)
       auto load_dt = [&](int cc) {
-        const int64_t di = dt_row + (int64_t)min(cc * Q + t, L - 1) * a.dt_st;
+        const int64_t di = dt_row + (int64_t)min((c_lo + cc) * Q + t, L - 1) * a.dt_st;
         if (a.dt_bf16)
           asm volatile("ld.global.nc.u16 %0, [%1];" : "=r"(dt_bits)
                        : "l"(static_cast<const __nv_bfloat16*>(a.dt) + di));
@@ -563,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       // conv cache, rows past L only feed masked outputs)
       uint32_t rw[19][2];
       auto load_rows = [&](int cc) {
-        const int r0 = cc * Q + strip * 16 - 3;
+        const int r0 = (c_lo + cc) * Q + strip * 16 - 3;
 #pragma unroll
         for (int r = 0; r < 19; ++r) {
           const int tt = min(max(r0 + r, 0), L - 1);
@@ -575,8 +602,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       // the x rows of chunk cc into L2, one row a thread (128 threads, 131 rows)
       const __nv_bfloat16* xhead = a.xbc + (int64_t)b * a.x_sb + head * P;
       auto prefetch_rows = [&](int cc) {
-        if (cc >= nchunks) return;
-        const int r0 = cc * Q - 3 + t;
+        if (cc >= nk) return;
+        const int r0 = (c_lo + cc) * Q - 3 + t;
         if (r0 >= 0 && r0 < L) prefetch_l2(xhead + (int64_t)r0 * a.x_st);
         if (t < 3 && r0 + Q < L) prefetch_l2(xhead + (int64_t)(r0 + Q) * a.x_st);
       };
@@ -618,7 +645,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           combine(pc + 1, yb, ib);
         }
         __syncwarp();
-        const int t0 = cc * Q;
+        const int t0 = (c_lo + cc) * Q;
         __nv_bfloat16* ybase = a.y + (int64_t)b * a.y_sb + (int64_t)head * a.y_sh + (lane & 7) * 8;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -640,10 +667,10 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       float v_c = 0.f, dt_c = 0.f, cf_c = 0.f;
       auto scan_chunk = [&](int cc) {
         const int cbuf = cc & 1;
-        const float dt = cc * Q + t < L
+        const float dt = (c_lo + cc) * Q + t < L
             ? softplus_f32((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
             : 0.f;
-        if (cc + 1 < nchunks) load_dt(cc + 1);
+        if (cc + 1 < nk) load_dt(cc + 1);
         float v = A * dt;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -663,8 +690,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         if (lane == 0) mbar_arrive(bar(B_PWG0 + hh));
       };
       // iteration c: chunk c (c >= 0); the rows and the scan of chunk c+1; the epilogue of c-1
-      for (int c = -1; c <= nchunks; ++c) {
-        if (c >= 0 && c < nchunks) {
+      for (int c = -1; c <= nk; ++c) {
+        if (c >= 0 && c < nk) {
           const int buf = c & 1;
           // X[buf] and cum/dt/cf[buf] held chunk c-2, whose epilogue this
           // warpgroup finished last iteration (after Y(c-2), and so after the
@@ -699,7 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
               for (int k = 0; k < 4; ++k) w[k][i] = w0[k];
               bias[i] = cw_all[512 + hh * 64 + vc4 * 4 + i];
             }
-            if (c == 0 && strip == 0) {
+            if (c_lo + c == 0 && strip == 0) {
               // rows before t = 0 come from the conv cache (zeros without one)
 #pragma unroll
               for (int r = 0; r < 3; ++r) {
@@ -741,7 +768,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
               ox[0] = pack_bf16x2(y4[0] * fx, y4[1] * fx);
               ox[1] = pack_bf16x2(y4[2] * fx, y4[3] * fx);
               const uint32_t off = srow * 128 + (((vc4 >> 1) ^ (srow & 7)) << 4) + ((vc4 & 1) << 3);
-              asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(sX + off), "r"(o[0]), "r"(o[1]) : "memory");
+              if constexpr (!kStateOnly)   // (the state-only pass needs X' alone)
+                asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(sX + off), "r"(o[0]), "r"(o[1]) : "memory");
               asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(sXp + off), "r"(ox[0]), "r"(ox[1]) : "memory");
             }
           }
@@ -753,19 +781,21 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           ALLOY_TRACE_POINT(4 + hh, c, 3);
         }
         // the next chunk's rows (in flight during the epilogue below) and its scan
-        if (c + 1 < nchunks) {
+        if (c + 1 < nk) {
           load_rows(c + 1);
           ALLOY_TRACE_POINT(4 + hh, c + 1, 6);
           scan_chunk(c + 1);
           ALLOY_TRACE_POINT(4 + hh, c + 1, 7);
         }
         // the previous chunk's output, while the tensor cores and consumers work on this one
-        if (c > 0 && !epilogue(c - 1)) break;
+        if constexpr (!kStateOnly) {
+          if (c > 0 && !epilogue(c - 1)) break;
+        }
         ALLOY_TRACE_POINT(4 + hh, c, 4);
       }
     } else {
       // ------------------------------------------------------------ consumers
-      reg_dealloc<kConsumerRegs>();
+      reg_dealloc<kStateOnly ? kConsumerRegsS : kConsumerRegs>();
       const int cw = warp >> 2;           // consumer warpgroup
       const float D0 = a.Dp ? a.Dp[(int64_t)h0 * a.d_s] : 0.f;
       const float D1 = a.Dp ? a.Dp[(int64_t)(h0 + 1) * a.d_s] : 0.f;
@@ -773,20 +803,59 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       // state columns [cw * N/2, (cw+1) * N/2)
       const int hr = t >> 6, pr = t & 63;
 
-      // initial state -> TMEM
+      // first segment record of this (batch row, head pair)
+      const size_t seg_slot = ((size_t)b * gridDim.x + blockIdx.x) * a.nseg;
+      auto record = [&](int j, int n8) {
+        return reinterpret_cast<float4*>(a.seg_state + ((seg_slot + j) * 128 + t) * N + cw * NHALF + n8 * 8);
+      };
+      // initial state -> TMEM.  Unsegmented, the call's initial state.  The
+      // state-only pass starts segment 0 from it (and keeps a copy as record
+      // 0), later segments from zero.  The full pass of a segmented call reads
+      // the call's initial state only through those records, so an in-place
+      // update (ssm_out aliasing ssm_in) is safe: segment 0 starts from record
+      // 0, segment s > 0 from the true end state of segment 0 carried over
+      // segments 1 .. s-1 as state = exp(sum of A dt over segment j) state +
+      // (end state of segment j from zero).  sp: a strided view of the
+      // call's initial state or a record (n stride 1), or none (zero).
+      const float* sp = nullptr;
+      int64_t sn = 1;
+      if (kStateOnly || a.nseg == 1) {
+        if (a.ssm_in && (!kStateOnly || seg == 0)) {
+          sp = a.ssm_in + (int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh + (int64_t)pr * a.si_sp +
+               (int64_t)(cw * NHALF) * a.si_sn;
+          sn = a.si_sn;
+        }
+      } else {
+        sp = reinterpret_cast<const float*>(record(seg == 0 ? 0 : 1, 0));
+      }
 #pragma unroll 1
       for (int n8 = 0; n8 < NHALF / 8; ++n8) {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = sp ? sp[(int64_t)(n8 * 8 + i) * sn] : 0.f;
+        if constexpr (kStateOnly) {
+          if (seg == 0) {
+            record(0, n8)[0] = make_float4(v[0], v[1], v[2], v[3]);
+            record(0, n8)[1] = make_float4(v[4], v[5], v[6], v[7]);
+          }
+        } else {
+#pragma unroll 1
+          for (int j = 1; j < seg; ++j) {
+            const float dj = ex2_approx(a.seg_logdecay[(seg_slot + j) * 2 + hr] * kLog2e);
+            const float4* sj = record(j + 1, n8);
+            const float4 w0 = sj[0], w1 = sj[1];
+            const float add[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = fmaf(dj, v[i], add[i]);
+          }
+        }
         uint32_t r[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int n = cw * NHALF + n8 * 8 + i;
-          r[i] = __float_as_uint(a.ssm_in ? a.ssm_in[(int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh +
-                                                     (int64_t)n * a.si_sn + (int64_t)pr * a.si_sp]
-                                          : 0.f);
-        }
+        for (int i = 0; i < 8; ++i) r[i] = __float_as_uint(v[i]);
         tmem_st8(lane_base + T_ST + cw * NHALF + n8 * 8, r);
       }
       tmem_st_wait();
+      float logdecay = 0.f;   // sum of A dt over this segment (head hr), for the state-only pass
 
       // score pieces of this warp: 16-column halves g of the 32-column blocks
       // j = cw, cw + 2 (K-steps 2j + g of the Y MMA); blocks right of the
@@ -794,7 +863,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       const int npieces = q >= cw + 2 ? 4 : (q >= cw ? 2 : 0);
       auto piece_col = [&](int i) { return 32 * (cw + 2 * (i >> 1)) + 16 * (i & 1); };
 
-      for (int c = 0; c < nchunks; ++c) {
+      for (int c = 0; c < nk; ++c) {
         const int buf = c & 1;
         if (!waitw(bar(B_X_READY0 + buf), (c >> 1) & 1, abort_flag, 30)) break;
         ALLOY_TRACE_POINT(cw, c, 0);
@@ -803,7 +872,9 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         if (c > 0 && !waitw(bar(B_YI_DONE), (c - 1) & 1, abort_flag, 31)) break;
         tc_fence_after();
         {
-          const float e_end = ex2_approx(cum_s[(buf * 2 + hr) * 128 + 127] * kLog2e);
+          const float lg_end = cum_s[(buf * 2 + hr) * 128 + 127];
+          const float e_end = ex2_approx(lg_end * kLog2e);
+          logdecay += lg_end;
           const uint32_t sH = base + OFF_H + hr * 8192;   // [n block][head][64 p][64 n]
           const uint64_t e2 = f2_splat(e_end);
           // 16-column pieces of this warpgroup's state columns, the next piece
@@ -811,7 +882,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           auto copy_piece = [&](int i, uint32_t (&r)[16]) {
             const int n0 = cw * NHALF + 16 * i;
 #pragma unroll
-            for (int g4 = 0; g4 < 2; ++g4) {
+            for (int g4 = 0; g4 < 2 && !kStateOnly; ++g4) {   // (no H in the state-only pass)
               const int n = n0 + g4 * 8;
               st_shared_v4(sH + (n >> 6) * 16384 + sw_off(pr, (n & 63) >> 3),
                            pack_bf16x2(__uint_as_float(r[g4 * 8 + 0]), __uint_as_float(r[g4 * 8 + 1])),
@@ -846,105 +917,119 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_HBF_READY));
         ALLOY_TRACE_POINT(cw, c, 1);
-        // ---- scores of both heads, in place over CB ----
-        // S_h[t, s] = CB[t, s] exp(cum_h[t] - cum_h[s]) dt_h[s] for s <= t (+ D_h on
-        // s == t); K-step k (sources 16k .. 16k+15) of S_h stored as bf16 pairs
-        // in columns [16k + 8h, 16k + 8h + 8), inside the piece it was read from
-        if (!waitw(bar(B_CB_FULL), c & 1, abort_flag, 32)) break;
-        ALLOY_TRACE_POINT(cw, c, 2);
-        tc_fence_after();
-        auto score_piece = [&](int i, const uint32_t (&r)[16]) {
-          const int j = cw + 2 * (i >> 1);
-          const int s0 = piece_col(i);
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            const float* cm = cum_s + (buf * 2 + h) * 128;
-            const float cum_t = cm[t];
-            uint32_t o[8];
-            if (j < q) {
-              // left of the diagonal block: exp(cum_t - cum_s) dt_s = R cf[s] with
-              // R = exp(cum_t - cum[s0+15]) <= 1 and cf[s] = exp(cum[s0+15] - cum_s) dt_s <= dt_s
-              const uint64_t R2 = f2_splat(ex2_approx((cum_t - cm[s0 + 15]) * kLog2e));
-              const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + s0);
-#pragma unroll
-              for (int i4 = 0; i4 < 4; ++i4) {
-                const float4 f = cf4[i4];
-                o[2 * i4] = f2_to_bf2(
-                    f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4]), __uint_as_float(r[4 * i4 + 1])), R2),
-                           f2_pack(f.x, f.y)));
-                o[2 * i4 + 1] = f2_to_bf2(
-                    f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4 + 2]), __uint_as_float(r[4 * i4 + 3])), R2),
-                           f2_pack(f.z, f.w)));
-              }
-            } else {
-              // the diagonal block: exact factors (<= 1 for s <= t, at any decay
-              // range), zero right of the diagonal, D on it
-              const float4* cm4 = reinterpret_cast<const float4*>(cm + s0);
-              const float4* dv4 = reinterpret_cast<const float4*>(dt_s + (buf * 2 + h) * 128 + s0);
-              const float Dh = h ? D1 : D0;
-#pragma unroll
-              for (int i4 = 0; i4 < 4; ++i4) {
-                const float4 c4 = cm4[i4], d4 = dv4[i4];
-                const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, ds[4] = {d4.x, d4.y, d4.z, d4.w};
-                float x[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                  const int s = s0 + 4 * i4 + u;
-                  const float xv = __uint_as_float(r[4 * i4 + u]) * (ex2_approx((cum_t - cs[u]) * kLog2e) * ds[u]);
-                  x[u] = s < t ? xv : (s == t ? xv + Dh : 0.f);
+        if constexpr (!kStateOnly) {
+          // ---- scores of both heads, in place over CB ----
+          // S_h[t, s] = CB[t, s] exp(cum_h[t] - cum_h[s]) dt_h[s] for s <= t (+ D_h on
+          // s == t); K-step k (sources 16k .. 16k+15) of S_h stored as bf16 pairs
+          // in columns [16k + 8h, 16k + 8h + 8), inside the piece it was read from
+          if (!waitw(bar(B_CB_FULL), c & 1, abort_flag, 32)) break;
+          ALLOY_TRACE_POINT(cw, c, 2);
+          tc_fence_after();
+          auto score_piece = [&](int i, const uint32_t (&r)[16]) {
+            const int j = cw + 2 * (i >> 1);
+            const int s0 = piece_col(i);
+  #pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              const float* cm = cum_s + (buf * 2 + h) * 128;
+              const float cum_t = cm[t];
+              uint32_t o[8];
+              if (j < q) {
+                // left of the diagonal block: exp(cum_t - cum_s) dt_s = R cf[s] with
+                // R = exp(cum_t - cum[s0+15]) <= 1 and cf[s] = exp(cum[s0+15] - cum_s) dt_s <= dt_s
+                const uint64_t R2 = f2_splat(ex2_approx((cum_t - cm[s0 + 15]) * kLog2e));
+                const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + s0);
+  #pragma unroll
+                for (int i4 = 0; i4 < 4; ++i4) {
+                  const float4 f = cf4[i4];
+                  o[2 * i4] = f2_to_bf2(
+                      f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4]), __uint_as_float(r[4 * i4 + 1])), R2),
+                             f2_pack(f.x, f.y)));
+                  o[2 * i4 + 1] = f2_to_bf2(
+                      f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4 + 2]), __uint_as_float(r[4 * i4 + 3])), R2),
+                             f2_pack(f.z, f.w)));
                 }
-                o[2 * i4] = pack_bf16x2(x[0], x[1]);
-                o[2 * i4 + 1] = pack_bf16x2(x[2], x[3]);
+              } else {
+                // the diagonal block: exact factors (<= 1 for s <= t, at any decay
+                // range), zero right of the diagonal, D on it
+                const float4* cm4 = reinterpret_cast<const float4*>(cm + s0);
+                const float4* dv4 = reinterpret_cast<const float4*>(dt_s + (buf * 2 + h) * 128 + s0);
+                const float Dh = h ? D1 : D0;
+  #pragma unroll
+                for (int i4 = 0; i4 < 4; ++i4) {
+                  const float4 c4 = cm4[i4], d4 = dv4[i4];
+                  const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, ds[4] = {d4.x, d4.y, d4.z, d4.w};
+                  float x[4];
+  #pragma unroll
+                  for (int u = 0; u < 4; ++u) {
+                    const int s = s0 + 4 * i4 + u;
+                    const float xv = __uint_as_float(r[4 * i4 + u]) * (ex2_approx((cum_t - cs[u]) * kLog2e) * ds[u]);
+                    x[u] = s < t ? xv : (s == t ? xv + Dh : 0.f);
+                  }
+                  o[2 * i4] = pack_bf16x2(x[0], x[1]);
+                  o[2 * i4 + 1] = pack_bf16x2(x[2], x[3]);
+                }
               }
+              tmem_st8(lane_base + T_CB + s0 + 8 * h, o);
             }
-            tmem_st8(lane_base + T_CB + s0 + 8 * h, o);
+          };
+          {
+            uint32_t ra[16], rb[16];
+            if (npieces > 0) tmem_ld16(lane_base + T_CB + piece_col(0), ra);
+  #pragma unroll 1
+            for (int i = 0; i < npieces; i += 2) {
+              tmem_ld_wait_regs(ra);
+              if (i == 0) ALLOY_TRACE_POINT(cw, c, 8);
+              tmem_ld16(lane_base + T_CB + piece_col(i + 1), rb);
+              score_piece(i, ra);
+              if (i == 0) ALLOY_TRACE_POINT(cw, c, 9);
+              tmem_ld_wait_regs(rb);
+              if (i + 2 < npieces) tmem_ld16(lane_base + T_CB + piece_col(i + 2), ra);
+              score_piece(i + 1, rb);
+              if (i == 0) ALLOY_TRACE_POINT(cw, c, 10);
+            }
+            uint32_t z[8];
+  #pragma unroll
+            for (int k = 0; k < 8; ++k) z[k] = 0u;
+  #pragma unroll 1
+            for (int i = npieces; i < 4; ++i) {
+              tmem_st8(lane_base + T_CB + piece_col(i), z);
+              tmem_st8(lane_base + T_CB + piece_col(i) + 8, z);
+            }
           }
-        };
-        {
-          uint32_t ra[16], rb[16];
-          if (npieces > 0) tmem_ld16(lane_base + T_CB + piece_col(0), ra);
-#pragma unroll 1
-          for (int i = 0; i < npieces; i += 2) {
-            tmem_ld_wait_regs(ra);
-            if (i == 0) ALLOY_TRACE_POINT(cw, c, 8);
-            tmem_ld16(lane_base + T_CB + piece_col(i + 1), rb);
-            score_piece(i, ra);
-            if (i == 0) ALLOY_TRACE_POINT(cw, c, 9);
-            tmem_ld_wait_regs(rb);
-            if (i + 2 < npieces) tmem_ld16(lane_base + T_CB + piece_col(i + 2), ra);
-            score_piece(i + 1, rb);
-            if (i == 0) ALLOY_TRACE_POINT(cw, c, 10);
-          }
-          uint32_t z[8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) z[k] = 0u;
-#pragma unroll 1
-          for (int i = npieces; i < 4; ++i) {
-            tmem_st8(lane_base + T_CB + piece_col(i), z);
-            tmem_st8(lane_base + T_CB + piece_col(i) + 8, z);
-          }
+          ALLOY_TRACE_POINT(cw, c, 11);
+          tmem_st_wait();
+          ALLOY_TRACE_POINT(cw, c, 12);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_S_READY));
+          ALLOY_TRACE_POINT(cw, c, 3);
         }
-        ALLOY_TRACE_POINT(cw, c, 11);
-        tmem_st_wait();
-        ALLOY_TRACE_POINT(cw, c, 12);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_S_READY));
-        ALLOY_TRACE_POINT(cw, c, 3);
       }
-      // ---- final state -> ssm_out ----
-      if (!*abort_flag && a.ssm_out && waitw(bar(B_YI_DONE), (nchunks - 1) & 1, abort_flag, 35)) {
+      // ---- the state at the segment's end: the state-only pass stores it
+      // (with the segment's log decay) for the later segments; the full pass
+      // of the last segment stores the final state to ssm_out ----
+      const bool store = kStateOnly || (a.ssm_out && seg == a.nseg - 1);
+      if (!*abort_flag && store && waitw(bar(B_YI_DONE), (nk - 1) & 1, abort_flag, 35)) {
         tc_fence_after();
+        float* sig = reinterpret_cast<float*>(record(seg + 1, 0));
+        if (kStateOnly && cw == 0 && pr == 0) a.seg_logdecay[(seg_slot + seg) * 2 + hr] = logdecay;
 #pragma unroll 1
         for (int n8 = 0; n8 < NHALF / 8; ++n8) {
           const int n0 = cw * NHALF + n8 * 8;
           uint32_t r[8];
           tmem_ld8(lane_base + T_ST + n0, r);
           tmem_ld_wait();
+          if constexpr (kStateOnly) {
+            reinterpret_cast<float4*>(sig)[2 * n8] =
+                make_float4(__uint_as_float(r[0]), __uint_as_float(r[1]), __uint_as_float(r[2]), __uint_as_float(r[3]));
+            reinterpret_cast<float4*>(sig)[2 * n8 + 1] =
+                make_float4(__uint_as_float(r[4]), __uint_as_float(r[5]), __uint_as_float(r[6]), __uint_as_float(r[7]));
+          } else {
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            a.ssm_out[(int64_t)b * a.so_sb + (int64_t)(h0 + hr) * a.so_sh + (int64_t)(n0 + i) * a.so_sn +
-                      (int64_t)pr * a.so_sp] = __uint_as_float(r[i]);
+            for (int i = 0; i < 8; ++i)
+              a.ssm_out[(int64_t)b * a.so_sb + (int64_t)(h0 + hr) * a.so_sh + (int64_t)(n0 + i) * a.so_sn +
+                        (int64_t)pr * a.so_sp] = __uint_as_float(r[i]);
+          }
         }
       }
     }
@@ -995,17 +1080,57 @@ bool ssd_tc_supported(const SsdArgs& a) {
   return true;
 }
 
-size_t ssd_tc_workspace_bytes(const SsdArgs& a) {
+// A (batch row, head pair) is walked chunk after chunk by one CTA.  When the
+// call has fewer pairs than the GPU has SMs, each pair's chunks are cut into
+// nseg segments walked by nseg CTAs at once: a state-only pass first gives
+// every segment but the last its end state (conv, X' and the state update
+// alone; segment 0 from the call's initial state, the others from zero), and
+// the full pass then starts segment s from the state carried over segments
+// 0..s-1.  Segments keep at least kMinSegChunks chunks.
+constexpr int kMinSegChunks = 4;
+
+int sm_count_of_current_device() {
+  static int counts[kMaxDevices] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+  if (counts[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    counts[dev] = n;
+  }
+  return counts[dev];
+}
+
+struct TcLayout {
+  int nseg;
+  size_t tiles, seg_state, seg_logdecay, total;   // byte offsets / sizes in the workspace
+};
+
+TcLayout tc_layout(const SsdArgs& a) {
   int g0, gs;
   group_range(a, &g0, &gs);
+  TcLayout l;
+  const int nchunks = (a.L + Q - 1) / Q;
+  const int units = a.B * (a.head_count / 2);
+  const int sms = sm_count_of_current_device();
+  l.nseg = 1;
+  if (units > 0 && sms > units) l.nseg = std::max(1, std::min(sms / units, nchunks / kMinSegChunks));
   // B/C tiles of every chunk, the last one padded to Q rows
-  const size_t rows = (size_t)((a.L + Q - 1) / Q) * Q;
-  return (size_t)a.B * rows * 2 * gs * a.N * sizeof(__nv_bfloat16);
+  l.tiles = (size_t)a.B * nchunks * Q * 2 * gs * a.N * sizeof(__nv_bfloat16);
+  const size_t nslots = (size_t)units * l.nseg;
+  l.seg_state = (l.tiles + 255) & ~size_t(255);
+  l.seg_logdecay = l.seg_state + nslots * 128 * a.N * sizeof(float);
+  l.total = l.nseg > 1 ? l.seg_logdecay + nslots * 2 * sizeof(float) : l.tiles;
+  return l;
 }
+
+size_t ssd_tc_workspace_bytes(const SsdArgs& a) { return tc_layout(a).total; }
+size_t ssd_tc_workspace_min_bytes(const SsdArgs& a) { return tc_layout(a).tiles; }
 
 int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (!ssd_tc_supported(s)) return fail(ALLOY_ERR_UNSUPPORTED, "ssd_tc: unsupported sizes/layout");
-  const size_t need = ssd_tc_workspace_bytes(s);
+  const TcLayout lay = tc_layout(s);
+  const size_t need = lay.tiles;
   if (workspace == nullptr || workspace_bytes < need)
     return fail(ALLOY_ERR_INVALID_ARG, "ssd_tc: workspace of %zu bytes required, got %zu", need,
                 workspace_bytes);
@@ -1064,18 +1189,24 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
     ALLOY_TRY(check_launch("bc_conv_kernel"));
   }
   a.bc = bc;
-  // 4. the SSD kernel
-  dim3 grid(s.head_count / 2, s.B);
+  // segments: only with the workspace for their states (a workspace of the
+  // B/C tiles alone runs one CTA per head pair)
+  a.nseg = workspace_bytes >= lay.total ? lay.nseg : 1;
+  a.seg_state = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + lay.seg_state);
+  a.seg_logdecay = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + lay.seg_logdecay);
+  // 4. the SSD kernel: the state-only pass over all segments but the last,
+  // then the full pass over all
+  auto launch = [&](auto kernel, int nz) -> int {
+    ALLOY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    kernel<<<dim3(s.head_count / 2, s.B, nz), kThreads, kSmemBytes, stream>>>(a);
+    return check_launch("ssd_tc_kernel");
+  };
   if (s.N == 128) {
-    ALLOY_CUDA(cudaFuncSetAttribute(ssd_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)kSmemBytes));
-    ssd_tc_kernel<128><<<grid, kThreads, kSmemBytes, stream>>>(a);
-  } else {
-    ALLOY_CUDA(cudaFuncSetAttribute(ssd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)kSmemBytes));
-    ssd_tc_kernel<64><<<grid, kThreads, kSmemBytes, stream>>>(a);
+    if (a.nseg > 1) ALLOY_TRY(launch(ssd_tc_kernel<128, true>, a.nseg - 1));
+    return launch(ssd_tc_kernel<128, false>, a.nseg);
   }
-  return check_launch("ssd_tc_kernel");
+  if (a.nseg > 1) ALLOY_TRY(launch(ssd_tc_kernel<64, true>, a.nseg - 1));
+  return launch(ssd_tc_kernel<64, false>, a.nseg);
 }
 
 int ssd_tc_take_error(cudaStream_t stream, unsigned int out[3]) {

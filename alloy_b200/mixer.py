@@ -93,7 +93,8 @@ def depthwise_conv1d(x_padded, weight, bias=None, L=None, out=None):
 def ssd_combined(xBC, dt_raw, conv_weight, conv_bias, dt_bias, A_log, D, *, n_heads,
                  head_dim, d_state, n_groups, d_conv=4, chunk_size=256, ssm_state=None,
                  conv_state=None, out=None, ssm_state_out=None, conv_state_out=None,
-                 write_ssm_state=True, write_conv_state=True, head_begin=0, head_count=0):
+                 write_ssm_state=True, write_conv_state=True, head_begin=0, head_count=0,
+                 workspace="full"):
     """Fused conv + discretisation + chunked SSD scan + D skip (prefill).
 
     The hot part of ``MambaBlock._forward_combined``
@@ -102,7 +103,9 @@ def ssd_combined(xBC, dt_raw, conv_weight, conv_bias, dt_bias, A_log, D, *, n_he
     [B, K-1, conv_dim])``; the state outputs are new tensors unless given
     (they may alias the inputs for an in-place cache update).  ``head_begin``
     / ``head_count`` restrict the call to a head range (multi-GPU sharding):
-    only those heads of ``y`` and of the states are written.
+    only those heads of ``y`` and of the states are written.  ``workspace``
+    "full" sizes the scratch for the fastest schedule; "min" gives the
+    library the smallest it accepts (each head pair walked by one CTA).
     """
     dev = _same_device(("xBC", xBC), ("dt_raw", dt_raw), ("conv_weight", conv_weight),
                        ("conv_bias", conv_bias), ("dt_bias", dt_bias), ("A_log", A_log),
@@ -120,8 +123,11 @@ def ssd_combined(xBC, dt_raw, conv_weight, conv_bias, dt_bias, A_log, D, *, n_he
     if conv_state is not None and conv_state.dtype != xBC.dtype:
         conv_state = conv_state.to(xBC.dtype)
     dims = _dims(H, P, N, n_groups, d_conv, chunk_size, head_begin, head_count)
-    ws_bytes = _lib.load().alloy_ssd_combined_workspace_size(
-        Bsz, L, _lib.BF16 if xBC.dtype == torch.bfloat16 else _lib.F32, _lib.ref(dims))
+    if workspace not in ("full", "min"):
+        raise ValueError(f"workspace must be 'full' or 'min', got {workspace!r}")
+    size_fn = (_lib.load().alloy_ssd_combined_workspace_size if workspace == "full"
+               else _lib.load().alloy_ssd_combined_min_workspace_size)
+    ws_bytes = size_fn(Bsz, L, _lib.BF16 if xBC.dtype == torch.bfloat16 else _lib.F32, _lib.ref(dims))
     ws = _workspace(dev, ws_bytes)
     args = [(xBC, "xBC"), (dt_raw, "dt_raw"), (_f32(conv_weight), "conv_weight"),
             (_f32(conv_bias), "conv_bias"), (_f32(dt_bias), "dt_bias"), (_f32(A_log), "A_log"),

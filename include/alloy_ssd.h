@@ -128,8 +128,9 @@ ALLOY_API int alloy_depthwise_conv1d(const alloy_tensor_t* x_padded, const alloy
  *   y          [B, L, H, P]      dtype of xBC (head/P strides free, P stride 1 for BF16)
  *   ssm_out    like ssm_in, F32 (data NULL = not written); may alias ssm_in
  *   conv_out   like conv_in (data NULL = not written); may alias conv_in
- *   workspace  device scratch of alloy_ssd_combined_workspace_size() bytes
- *              (may be NULL when that size is 0)
+ *   workspace  device scratch of alloy_ssd_combined_workspace_size() bytes, or
+ *              of at least alloy_ssd_combined_min_workspace_size() (may be
+ *              NULL when that size is 0)
  * y = scan(dt*x) + D*x, where x is the UNSCALED conv output.
  */
 ALLOY_API int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t* dt_raw,
@@ -144,14 +145,26 @@ ALLOY_API int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t
 
 /*
  * Bytes of device workspace alloy_ssd_combined needs for a call with this
- * batch, sequence length, activation dtype and dims (0 = none).  The
- * workspace holds the conv + SiLU of the B and C columns (bf16), shared by
- * all heads of a group; it must be 16-byte aligned and may be reused across
- * calls that do not overlap on the device.  No counterpart in the reference
- * (its kernels allocate their outputs through MLX).
+ * batch, sequence length, activation dtype and dims (0 = none), on the
+ * current device.  The workspace holds the conv + SiLU of the B and C columns
+ * (bf16), shared by all heads of a group, and, when the call has fewer
+ * (batch row, head pair) units than the GPU has SMs, the end states of the
+ * sequence segments the kernel then walks in parallel.  It must be 16-byte
+ * aligned and may be reused across calls that do not overlap on the device.
+ * No counterpart in the reference (its kernels allocate their outputs through
+ * MLX).
  */
 ALLOY_API size_t alloy_ssd_combined_workspace_size(int64_t batch, int64_t seqlen, int32_t dtype,
                                                    const alloy_ssd_dims_t* dims);
+
+/*
+ * The smallest workspace alloy_ssd_combined accepts for the same call: the B/C
+ * tiles alone.  With it each (batch row, head pair) is walked by one CTA from
+ * its first chunk to its last (results equal up to the fp32 rounding of the
+ * state carried between segments).  No counterpart in the reference.
+ */
+ALLOY_API size_t alloy_ssd_combined_min_workspace_size(int64_t batch, int64_t seqlen, int32_t dtype,
+                                                       const alloy_ssd_dims_t* dims);
 
 /*
  * alloy_ssd_combined for callers that cannot allocate device memory.
@@ -164,9 +177,10 @@ ALLOY_API size_t alloy_ssd_combined_workspace_size(int64_t batch, int64_t seqlen
  * Same arguments and results as alloy_ssd_combined, without the workspace:
  * the scratch comes from one fixed 8 MiB array compiled into the library,
  * held by every device that loads it until the process exits.  Calls whose
- * scratch (alloy_ssd_combined_workspace_size) would exceed 8 MiB are rejected
- * with ALLOY_ERR_UNSUPPORTED before anything is launched.  The call allocates
- * and frees nothing.
+ * smallest scratch (alloy_ssd_combined_min_workspace_size) would exceed 8 MiB
+ * are rejected with ALLOY_ERR_UNSUPPORTED before anything is launched (the
+ * array then holds the B/C tiles alone).  The call allocates and frees
+ * nothing.
  *  - The first call on a device looks up the array's device address
  *    (cudaGetSymbolAddress) with that device current; make that first call
  *    before any stream capture begins.
@@ -192,6 +206,15 @@ ALLOY_API int alloy_ssd_combined_noalloc(const alloy_tensor_t* xBC, const alloy_
  * reference (MLX kernels have no device-side waits).
  */
 ALLOY_API int alloy_check_device_status(void* stream);
+
+/*
+ * Number of kernels this library has launched in this process (every thread
+ * and device), for counting the launches of a timed region: a segmented
+ * prefill (alloy_ssd_combined with fewer (batch row, head pair) units than
+ * SMs) launches one more than an unsegmented one.  No counterpart in the
+ * reference.
+ */
+ALLOY_API uint64_t alloy_kernel_launch_count(void);
 
 /*
  * Selective scan on pre-discretised inputs.

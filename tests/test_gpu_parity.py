@@ -342,6 +342,48 @@ def test_tensor_core_ssd_strong_decay(dt_bias):
     assert_close(np_(h), h_ref, True)
 
 
+@pytest.mark.parametrize("cfg", [
+    dict(B=1, L=4096, H=4, P=64, N=128, G=1),      # 2 head pairs, 32 chunks: 8 segments each
+    dict(B=2, L=2999, H=2, P=64, N=64, G=1),       # ragged last chunk, 24 chunks: 6 segments
+])
+def test_tensor_core_ssd_sequence_segments(cfg):
+    """With fewer (batch row, head pair) units than SMs the chunks of a unit
+    are cut into segments walked by several CTAs (a state-only pass, then the
+    full pass from the carried state).  Parity with the oracle, agreement with
+    the one-CTA-a-unit walk of the smallest workspace, and an in-place update
+    of the state cache (ssm_state_out aliasing ssm_state)."""
+    from alloy_b200 import _lib
+    H, P, N, G, L = cfg["H"], cfg["P"], cfg["N"], cfg["G"], cfg["L"]
+    lib = _lib.load()
+    d = mixer._dims(H, P, N, G, 4, 256, 0, 0)
+    full = lib.alloy_ssd_combined_workspace_size(cfg["B"], L, _lib.BF16, _lib.ref(d))
+    small = lib.alloy_ssd_combined_min_workspace_size(cfg["B"], L, _lib.BF16, _lib.ref(d))
+    assert full > small > 0       # the segment records only come with the full size
+    inp = oracle.make_inputs(**cfg, dtype="bf16", seed=24, with_state=True)
+    y_ref, h_ref, _ = oracle.mixer_core(
+        inp["xBC"], inp["dt_raw"], inp["conv_weight"], inp["conv_bias"], inp["dt_bias"],
+        inp["A_log"], inp["D"], n_heads=H, headdim=P, d_state=N, n_groups=G, chunk_size=256,
+        ssm_state=inp["ssm_state"], conv_state=inp["conv_state"])
+    args = (cu(inp["xBC"], torch.bfloat16), cu(inp["dt_raw"], torch.bfloat16),
+            cu(inp["conv_weight"]), cu(inp["conv_bias"]), cu(inp["dt_bias"]),
+            cu(inp["A_log"]), cu(inp["D"]))
+    kw = dict(n_heads=H, head_dim=P, d_state=N, n_groups=G,
+              conv_state=cu(inp["conv_state"], torch.bfloat16))
+    state = cu(inp["ssm_state"])
+    y_seg, h_seg, _ = mixer.ssd_combined(*args, ssm_state=state, ssm_state_out=state, **kw)
+    y_one, h_one, _ = mixer.ssd_combined(*args, ssm_state=cu(inp["ssm_state"]), workspace="min",
+                                         **kw)
+    mixer.check_device_status()
+    assert h_seg.data_ptr() == state.data_ptr()
+    assert_close(np_(y_seg), y_ref, True)
+    assert_close(np_(h_seg), h_ref, True)
+    assert_close(np_(y_one), y_ref, True)
+    assert_close(np_(h_one), h_ref, True)
+    # the two walks differ only in the fp32 rounding of the carried state
+    assert oracle.rel_l2(np_(y_seg), np_(y_one)) < 3e-3
+    assert oracle.rel_l2(np_(h_seg), np_(h_one)) < 1e-4
+
+
 def test_tensor_core_ssd_is_deterministic_and_chunk_independent():
     cfg = dict(B=1, L=600, H=4, P=64, N=128, G=1)
     inp = oracle.make_inputs(**cfg, dtype="bf16", seed=22)
