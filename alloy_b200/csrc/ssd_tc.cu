@@ -67,13 +67,14 @@ constexpr int P = 64;                  // head dim
 constexpr int kThreads = 640;          // 20 warps: 4 compute warpgroups + 1 role warpgroup
 // registers per thread after the split (launch: 640 x 96, i.e. 480 a thread
 // summed over one thread of each of the five warpgroups): the full pass gives
-// 2 x 120 to the producers, 2 x 80 to the consumers, 80 to the role warps; the
-// state-only pass (no scores, the conv dominant) 2 x 136, 2 x 72 and 56
+// 2 x 120 to the producers, 2 x 88 to the consumers, 64 to the role warps; the
+// state-only pass (producers: the conv alone, two chunks of x rows in
+// registers; consumers: the dt scan) 2 x 144, 2 x 64 and 56
 constexpr int kProducerRegs = 120;
 constexpr int kConsumerRegs = 88;
 constexpr int kRoleRegs = 64;
-constexpr int kProducerRegsS = 136;
-constexpr int kConsumerRegsS = 72;
+constexpr int kProducerRegsS = 144;
+constexpr int kConsumerRegsS = 64;
 constexpr int kRoleRegsS = 56;
 constexpr int kTmaWarp = 16;           // B/C half tiles
 constexpr int kMmaWarp = 17;
@@ -115,6 +116,13 @@ enum {
   B_DRAIN
 };
 static_assert(B_DRAIN + 1 == NBAR, "barrier table");
+// the state-only pass reuses barriers only the full pass needs otherwise
+constexpr int B_XF_FULL0 = B_HBF_READY;   // consumers -> producers: X' row factors of a chunk (per buffer)
+constexpr int B_XF_EMPTY0 = B_ST_DONE;    // producers -> consumers: row factors read (per buffer)
+constexpr int B_XP_FREE0 = B_Y_EMPTY0;    // MMA -> producers: X' buffer read (per buffer)
+constexpr int B_ST_FINAL = B_Y_FULL;      // MMA -> consumers: the segment's end state complete
+static_assert(B_XF_FULL0 + 1 == B_S_READY && B_XF_EMPTY0 + 1 == B_YI_DONE && B_XP_FREE0 + 1 == B_Y_EMPTY1,
+              "paired barriers");
 
 // TMEM columns
 constexpr uint32_t T_CB = 0;      // CB [128 t][128 s] f32, overwritten in place by the scores
@@ -404,11 +412,19 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
   const int seg = blockIdx.z;
   const int c_lo = (int)((unsigned)seg * (unsigned)nchunks / (unsigned)a.nseg);
   const int nk = (int)((unsigned)(seg + 1) * (unsigned)nchunks / (unsigned)a.nseg) - c_lo;
+  // the chunk of walk step c: the full pass walks its segment forward, the
+  // state-only pass backward, so that each chunk's contribution to the
+  // segment's end state carries its decay to that end (the sum of A dt over
+  // the chunks already walked) and nothing rescales the state per chunk
+  auto chunk_at = [&](int c) { return kStateOnly ? c_lo + nk - 1 - c : c_lo + c; };
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     // FULL0/1 EMPTY0/1 X_READY0/1 CB_FULL HBF_READY S_READY Y_FULL ST_DONE YI_DONE Y_EMPTY0/1 PWG0/1 DRAIN
-    const int counts[NBAR] = {1, 1, 1, 1, 8, 8, 1, 8, 8, 1, 1, 1, 8, 8, 4, 4, 1};
+    // (the state-only pass: XF_EMPTY0/1 in place of ST_DONE / YI_DONE,
+    // XP_FREE0/1 in place of Y_EMPTY0/1)
+    const int s8 = kStateOnly ? 8 : 1, s1 = kStateOnly ? 1 : 8;
+    const int counts[NBAR] = {1, 1, 1, 1, 8, 8, 1, 8, 8, 1, s8, s8, s1, s1, 4, 4, 1};
     for (int i = 0; i < NBAR; ++i) mbar_init(bar(i), counts[i]);
     mbar_fence_init();
   }
@@ -439,22 +455,41 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         // this pair's group: chunk c's B/C halves are NK consecutive 32 KB
         // stage images [B half k | C half k]
         const int64_t chunk_stride = (int64_t)a.group_count * NK * kStageBytes;
-        // (src0: this segment's first chunk)
         const unsigned char* src0 = reinterpret_cast<const unsigned char*>(a.bc) +
-                                    (((int64_t)b * nchunks + c_lo) * a.group_count + gl) * NK * kStageBytes;
-        for (int c = 1; c <= kL2Ahead && c < nk; ++c) bulk_prefetch_l2(src0 + c * chunk_stride, NK * kStageBytes);
-        int issued = 0;
-        for (int c = 0; c < nk; ++c) {
-          if (c + kL2Ahead < nk) bulk_prefetch_l2(src0 + (c + kL2Ahead) * chunk_stride, NK * kStageBytes);
-          for (int k = 0; k < NK; ++k) {
-            const int i = c * NK + k, slot = i & 1;
-            if (i >= 2 && !wait1(bar(B_EMPTY0 + slot), ((i >> 1) - 1) & 1, abort_flag, 2)) goto bc_done;
-            ALLOY_TRACE_POINT(2, c, k);
-            mbar_arrive_expect_tx(bar(B_FULL0 + slot), kStageBytes);
-            bulk_load(base + OFF_STAGE + slot * kStageBytes, src0 + c * chunk_stride + k * kStageBytes, kStageBytes,
-                      bar(B_FULL0 + slot));
-            ALLOY_TRACE_COPY_DONE(bar(B_FULL0 + slot), (i >> 1) & 1, 2, c, 2 + k);
+                                    ((int64_t)b * nchunks * a.group_count + gl) * NK * kStageBytes;
+        int issued = 0;   // stages (full pass) or chunks (state-only pass) sent
+        if constexpr (kStateOnly) {
+          // B halves alone (16 KB each), two chunks in flight: chunk buffer cb
+          // holds half k at stage offset 32 KB k + 16 KB cb, so a chunk's
+          // halves sit 32 KB apart as in the full pass
+          auto prefetch = [&](int c) {
+            for (int k = 0; k < NK; ++k) bulk_prefetch_l2(src0 + chunk_at(c) * chunk_stride + k * kStageBytes, 16384);
+          };
+          for (int c = 1; c <= kL2Ahead && c < nk; ++c) prefetch(c);
+          for (int c = 0; c < nk; ++c) {
+            if (c + kL2Ahead < nk) prefetch(c + kL2Ahead);
+            const int cb = c & 1;
+            if (c >= 2 && !wait1(bar(B_EMPTY0 + cb), ((c >> 1) - 1) & 1, abort_flag, 2)) goto bc_done;
+            mbar_arrive_expect_tx(bar(B_FULL0 + cb), NK * 16384);
+            for (int k = 0; k < NK; ++k)
+              bulk_load(base + OFF_STAGE + k * 32768 + cb * 16384,
+                        src0 + chunk_at(c) * chunk_stride + k * kStageBytes, 16384, bar(B_FULL0 + cb));
             ++issued;
+          }
+        } else {
+          for (int c = 1; c <= kL2Ahead && c < nk; ++c) bulk_prefetch_l2(src0 + chunk_at(c) * chunk_stride, NK * kStageBytes);
+          for (int c = 0; c < nk; ++c) {
+            if (c + kL2Ahead < nk) bulk_prefetch_l2(src0 + chunk_at(c + kL2Ahead) * chunk_stride, NK * kStageBytes);
+            for (int k = 0; k < NK; ++k) {
+              const int i = c * NK + k, slot = i & 1;
+              if (i >= 2 && !wait1(bar(B_EMPTY0 + slot), ((i >> 1) - 1) & 1, abort_flag, 2)) goto bc_done;
+              ALLOY_TRACE_POINT(2, c, k);
+              mbar_arrive_expect_tx(bar(B_FULL0 + slot), kStageBytes);
+              bulk_load(base + OFF_STAGE + slot * kStageBytes, src0 + chunk_at(c) * chunk_stride + k * kStageBytes,
+                        kStageBytes, bar(B_FULL0 + slot));
+              ALLOY_TRACE_COPY_DONE(bar(B_FULL0 + slot), (i >> 1) & 1, 2, c, 2 + k);
+              ++issued;
+            }
           }
         }
       bc_done:
@@ -472,27 +507,45 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         constexpr uint32_t ID_YI = idesc_bf16(128, 128, 0, 0);
         constexpr uint32_t ID_ST = idesc_bf16(128, N, 1, 1);
         constexpr uint32_t ID_Y = idesc_bf16(128, 64, 0, 1);
+        if constexpr (kStateOnly) {
+          // state[(h,p), n] = sum over the walk of X'^T B, X' carrying the
+          // decay to the segment's end (the first MMA overwrites tensor memory)
+          for (int c = 0; c < nk; ++c) {
+            const int cb = c & 1;
+            if (!wait1(bar(B_FULL0 + cb), (c >> 1) & 1, abort_flag, 3)) goto mma_done;
+            ALLOY_TRACE_POINT(3, c, 5);
+            if (!wait1(bar(B_X_READY0 + cb), (c >> 1) & 1, abort_flag, 8)) goto mma_done;
+            ALLOY_TRACE_POINT(3, c, 9);
+            tc_fence_after();
+            const uint32_t sB = base + OFF_STAGE + cb * 16384;
+            const uint32_t sXp = base + (cb ? OFF_X : OFF_XP);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_bf16(tmem + T_ST, sw128_desc(sXp + 2048 * kk, 16384, 1024),
+                        sw128_desc(sB + 2048 * kk, kStageBytes, 1024), ID_ST, (c | kk) != 0);
+            umma_commit(bar(B_EMPTY0 + cb));     // B halves of buffer cb free
+            umma_commit(bar(B_XP_FREE0 + cb));   // X'[cb] free
+          }
+          umma_commit(bar(B_ST_FINAL));
+        } else
         for (int c = 0; c < nk; ++c) {
           const uint32_t ph = c & 1, pph = (c - 1) & 1;
           const int buf = c & 1;
           // CB = C B^T over the N halves; the region held the previous scores,
-          // so Y(c-1) must have completed (the state-only pass just waits for
-          // the stages)
+          // so Y(c-1) must have completed
           for (int k = 0; k < NK; ++k) {
             const int i = c * NK + k, slot = i & 1;
             if (!wait1(bar(B_FULL0 + slot), (i >> 1) & 1, abort_flag, 3)) goto mma_done;
             ALLOY_TRACE_POINT(3, c, 5 + k);
-            if constexpr (!kStateOnly) {
-              if (k == 0 && c > 0 && !wait1(bar(B_Y_FULL), pph, abort_flag, 4)) goto mma_done;
-              tc_fence_after();
-              const uint32_t sB = base + OFF_STAGE + slot * kStageBytes, sC = sB + 16384;
+            if (k == 0 && c > 0 && !wait1(bar(B_Y_FULL), pph, abort_flag, 4)) goto mma_done;
+            tc_fence_after();
+            const uint32_t sB = base + OFF_STAGE + slot * kStageBytes, sC = sB + 16384;
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                umma_bf16(tmem + T_CB, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sB + 32 * kk, 16, 1024), ID_CB,
-                          (k | kk) != 0);
-            }
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(tmem + T_CB, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sB + 32 * kk, 16, 1024), ID_CB,
+                        (k | kk) != 0);
           }
-          if constexpr (!kStateOnly) umma_commit(bar(B_CB_FULL));
+          umma_commit(bar(B_CB_FULL));
           ALLOY_TRACE_POINT(3, c, 0);
           // state[(h,p), n] += X'^T B over s, once the state is scaled and
           // copied (HBF) and X' has arrived with X
@@ -515,37 +568,33 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           // Yi = C [H_0; H_1]^T for both heads at once (N = 128 rows (h, p));
           // its columns and Y's held chunk c-1's output until its epilogue.
           // H is a copy, so the state update above does not disturb it.
-          if constexpr (!kStateOnly) {
-            if (c > 0 && !wait1(bar(B_Y_EMPTY0 + (buf ^ 1)), ((c - 1) >> 1) & 1, abort_flag, 5)) goto mma_done;
-            tc_fence_after();
-            for (int k = 0; k < NK; ++k) {
-              const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
-              const uint32_t sH = base + OFF_H + k * 16384;
+          if (c > 0 && !wait1(bar(B_Y_EMPTY0 + (buf ^ 1)), ((c - 1) >> 1) & 1, abort_flag, 5)) goto mma_done;
+          tc_fence_after();
+          for (int k = 0; k < NK; ++k) {
+            const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
+            const uint32_t sH = base + OFF_H + k * 16384;
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                umma_bf16(tmem + T_YI, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sH + 32 * kk, 16, 1024),
-                          ID_YI, (k | kk) != 0);
-            }
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(tmem + T_YI, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sH + 32 * kk, 16, 1024),
+                        ID_YI, (k | kk) != 0);
           }
           // the last reads of this chunk's B/C stages and of H
           for (int k = 0; k < NK; ++k) umma_commit(bar(B_EMPTY0 + ((c * NK + k) & 1)));
           umma_commit(bar(B_YI_DONE));
           ALLOY_TRACE_POINT(3, c, 1);
           // Y_h = S_h X_h, S_h (bf16 pairs) read from tensor memory
-          if constexpr (!kStateOnly) {
-            if (!wait1(bar(B_S_READY), ph, abort_flag, 7)) goto mma_done;
-            ALLOY_TRACE_POINT(3, c, 8);
-            tc_fence_after();
+          if (!wait1(bar(B_S_READY), ph, abort_flag, 7)) goto mma_done;
+          ALLOY_TRACE_POINT(3, c, 8);
+          tc_fence_after();
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const uint32_t sX = base + OFF_X + (buf * 2 + h) * 16384;
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t sX = base + OFF_X + (buf * 2 + h) * 16384;
 #pragma unroll
-              for (int kk = 0; kk < 8; ++kk)
-                umma_bf16_ta(tmem + T_Y + 64 * h, tmem + T_CB + 16 * kk + 8 * h,
-                             sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
-            }
-            umma_commit(bar(B_Y_FULL));
+            for (int kk = 0; kk < 8; ++kk)
+              umma_bf16_ta(tmem + T_Y + 64 * h, tmem + T_CB + 16 * kk + 8 * h,
+                           sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
           }
+          umma_commit(bar(B_Y_FULL));
           ALLOY_TRACE_POINT(3, c, 2);
         }
       mma_done:
@@ -577,7 +626,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       const int64_t dt_row = (int64_t)b * a.dt_sb + (int64_t)head * a.dt_sh;
       uint32_t dt_bits = 0;   // raw dt of the chunk about to be produced (converted when used)
       auto load_dt = [&](int cc) {
-        const int64_t di = dt_row + (int64_t)min((c_lo + cc) * Q + t, L - 1) * a.dt_st;
+        const int64_t di = dt_row + (int64_t)min(chunk_at(cc) * Q + t, L - 1) * a.dt_st;
         if (a.dt_bf16)
           asm volatile("ld.global.nc.u16 %0, [%1];" : "=r"(dt_bits)
                        : "l"(static_cast<const __nv_bfloat16*>(a.dt) + di));
@@ -589,13 +638,13 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       // channels (clamped into [0, L); rows before 0 are replaced from the
       // conv cache, rows past L only feed masked outputs)
       uint32_t rw[19][2];
-      auto load_rows = [&](int cc) {
-        const int r0 = (c_lo + cc) * Q + strip * 16 - 3;
+      auto load_rows = [&](int cc, uint32_t (&rr)[19][2]) {
+        const int r0 = chunk_at(cc) * Q + strip * 16 - 3;
 #pragma unroll
         for (int r = 0; r < 19; ++r) {
           const int tt = min(max(r0 + r, 0), L - 1);
           asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];"
-                       : "=r"(rw[r][0]), "=r"(rw[r][1])
+                       : "=r"(rr[r][0]), "=r"(rr[r][1])
                        : "l"(xsrc + (int64_t)tt * a.x_st));
         }
       };
@@ -603,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       const __nv_bfloat16* xhead = a.xbc + (int64_t)b * a.x_sb + head * P;
       auto prefetch_rows = [&](int cc) {
         if (cc >= nk) return;
-        const int r0 = (c_lo + cc) * Q - 3 + t;
+        const int r0 = chunk_at(cc) * Q - 3 + t;
         if (r0 >= 0 && r0 < L) prefetch_l2(xhead + (int64_t)r0 * a.x_st);
         if (t < 3 && r0 + Q < L) prefetch_l2(xhead + (int64_t)(r0 + Q) * a.x_st);
       };
@@ -645,7 +694,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           combine(pc + 1, yb, ib);
         }
         __syncwarp();
-        const int t0 = (c_lo + cc) * Q;
+        const int t0 = chunk_at(cc) * Q;
         __nv_bfloat16* ybase = a.y + (int64_t)b * a.y_sb + (int64_t)head * a.y_sh + (lane & 7) * 8;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -660,14 +709,14 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         return true;
       };
       for (int cc = 1; cc <= kL2Ahead; ++cc) prefetch_rows(cc);
-      load_dt(0);
+      if constexpr (!kStateOnly) load_dt(0);
       // ---- dt, warp-local scan and column factors of chunk cc; the warp's
       // total goes to wsum and the warp arrives on the group barrier, whose
       // wait (for the prefix over the warps) comes when the chunk is produced
       float v_c = 0.f, dt_c = 0.f, cf_c = 0.f;
       auto scan_chunk = [&](int cc) {
         const int cbuf = cc & 1;
-        const float dt = (c_lo + cc) * Q + t < L
+        const float dt = chunk_at(cc) * Q + t < L
             ? softplus_f32((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
             : 0.f;
         if (cc + 1 < nk) load_dt(cc + 1);
@@ -689,16 +738,24 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_PWG0 + hh));
       };
-      // iteration c: chunk c (c >= 0); the rows and the scan of chunk c+1; the epilogue of c-1
-      for (int c = -1; c <= nk; ++c) {
-        if (c >= 0 && c < nk) {
-          const int buf = c & 1;
+      // ---- chunk c from its rows rr: prefix over the warps, X (full pass) and X' ----
+      auto produce = [&](int c, uint32_t (&rr)[19][2]) -> bool {
+        const int buf = c & 1;
+        const float* xfp;   // X' row factors of this chunk (head hh)
+        if constexpr (kStateOnly) {
+          // the row factors (decay to the segment's end) come from the consumer
+          // warps; X' is double-buffered
+          if (!waitw(bar(B_XF_FULL0 + buf), (c >> 1) & 1, abort_flag, 22)) return false;
+          ALLOY_TRACE_POINT(4 + hh, c, 1);
+          if (c >= 2 && !waitw(bar(B_XP_FREE0 + buf), ((c >> 1) - 1) & 1, abort_flag, 23)) return false;
+          xfp = cum_s + (buf * 2 + hh) * 128;
+        } else {
           // X[buf] and cum/dt/cf[buf] held chunk c-2, whose epilogue this
           // warpgroup finished last iteration (after Y(c-2), and so after the
           // scores and the state copy of c-2)
           ALLOY_TRACE_POINT(4 + hh, c, 0);
           // ---- prefix over the warps -> cumulative log decay ----
-          if (!waitw(bar(B_PWG0 + hh), c & 1, abort_flag, 22)) break;
+          if (!waitw(bar(B_PWG0 + hh), c & 1, abort_flag, 22)) return false;
           float pre = 0.f, tot = 0.f;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -715,83 +772,105 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           __syncwarp();
           ALLOY_TRACE_POINT(4 + hh, c, 1);
           // X' is single-buffered: the state update of chunk c-1 read it
-          if (c > 0 && !waitw(bar(B_ST_DONE), (c - 1) & 1, abort_flag, 23)) break;
-          // ---- conv + SiLU -> X[buf][hh] (bf16) and X'[hh] = X * xf ----
-          {
-            float w[4][4], bias[4];   // [tap][channel]
+          if (c > 0 && !waitw(bar(B_ST_DONE), (c - 1) & 1, abort_flag, 23)) return false;
+          xfp = xf_s + hh * 128;
+        }
+        // ---- conv + SiLU -> X[buf][hh] (bf16) and X'[hh] = X * xf ----
+        {
+          float w[4][4], bias[4];   // [tap][channel]
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float* w0 = cw_all + (hh * 64 + vc4 * 4 + i) * 4;
+          for (int i = 0; i < 4; ++i) {
+            const float* w0 = cw_all + (hh * 64 + vc4 * 4 + i) * 4;
 #pragma unroll
-              for (int k = 0; k < 4; ++k) w[k][i] = w0[k];
-              bias[i] = cw_all[512 + hh * 64 + vc4 * 4 + i];
-            }
-            if (c_lo + c == 0 && strip == 0) {
-              // rows before t = 0 come from the conv cache (zeros without one)
+            for (int k = 0; k < 4; ++k) w[k][i] = w0[k];
+            bias[i] = cw_all[512 + hh * 64 + vc4 * 4 + i];
+          }
+          if (chunk_at(c) == 0 && strip == 0) {
+            // rows before t = 0 come from the conv cache (zeros without one)
 #pragma unroll
-              for (int r = 0; r < 3; ++r) {
-                float f[4];
+            for (int r = 0; r < 3; ++r) {
+              float f[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                  f[i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
-                                                               (int64_t)(a.K - 4 + r) * a.ci_sk +
-                                                               (int64_t)(xch + i) * a.ci_sc])
-                                   : 0.f;
-                rw[r][0] = pack_bf16x2(f[0], f[1]);
-                rw[r][1] = pack_bf16x2(f[2], f[3]);
-              }
-            }
-            const uint32_t sX = base + OFF_X + (buf * 2 + hh) * 16384, sXp = base + OFF_XP + hh * 16384;
-            const float4* xf4 = reinterpret_cast<const float4*>(xf_s + hh * 128 + strip * 16);
-            float4 fq;
-#pragma unroll
-            for (int r = 3; r < 19; ++r) {
-              const int srow = strip * 16 + r - 3;
-              if (((r - 3) & 3) == 0) fq = xf4[(r - 3) >> 2];
-              const float fx = ((r - 3) & 3) == 0 ? fq.x : ((r - 3) & 3) == 1 ? fq.y : ((r - 3) & 3) == 2 ? fq.z : fq.w;
-              // (rows past L need no masking: X and X' there only meet dt = 0
-              // or outputs that are not stored)
-              float y4[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                float acc = bias[i];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  const uint32_t wd = rw[r - 3 + k][i >> 1];
-                  acc = fmaf((i & 1) ? bf16_hi(wd) : bf16_lo(wd), w[k][i], acc);
-                }
-                y4[i] = fmaf(acc, tanh_approx(acc), acc);   // silu of 2 acc
-              }
-              uint32_t o[2], ox[2];
-              o[0] = pack_bf16x2(y4[0], y4[1]);
-              o[1] = pack_bf16x2(y4[2], y4[3]);
-              ox[0] = pack_bf16x2(y4[0] * fx, y4[1] * fx);
-              ox[1] = pack_bf16x2(y4[2] * fx, y4[3] * fx);
-              const uint32_t off = srow * 128 + (((vc4 >> 1) ^ (srow & 7)) << 4) + ((vc4 & 1) << 3);
-              if constexpr (!kStateOnly)   // (the state-only pass needs X' alone)
-                asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(sX + off), "r"(o[0]), "r"(o[1]) : "memory");
-              asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(sXp + off), "r"(ox[0]), "r"(ox[1]) : "memory");
+              for (int i = 0; i < 4; ++i)
+                f[i] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb +
+                                                             (int64_t)(a.K - 4 + r) * a.ci_sk +
+                                                             (int64_t)(xch + i) * a.ci_sc])
+                                 : 0.f;
+              rr[r][0] = pack_bf16x2(f[0], f[1]);
+              rr[r][1] = pack_bf16x2(f[2], f[3]);
             }
           }
-          prefetch_rows(c + 1 + kL2Ahead);
-          // X, X', cum, dt, cf of chunk c are ready
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(B_X_READY0 + buf));
-          ALLOY_TRACE_POINT(4 + hh, c, 3);
+          const uint32_t sX = base + OFF_X + (buf * 2 + hh) * 16384;
+          const uint32_t sXp = base + (kStateOnly && buf ? OFF_X : OFF_XP) + hh * 16384;
+          const float4* xf4 = reinterpret_cast<const float4*>(xfp + strip * 16);
+          float4 fq;
+#pragma unroll
+          for (int r = 3; r < 19; ++r) {
+            const int srow = strip * 16 + r - 3;
+            if (((r - 3) & 3) == 0) fq = xf4[(r - 3) >> 2];
+            const float fx = ((r - 3) & 3) == 0 ? fq.x : ((r - 3) & 3) == 1 ? fq.y : ((r - 3) & 3) == 2 ? fq.z : fq.w;
+            // (rows past L need no masking: X and X' there only meet dt = 0
+            // or outputs that are not stored)
+            float y4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              float acc = bias[i];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const uint32_t wd = rr[r - 3 + k][i >> 1];
+                acc = fmaf((i & 1) ? bf16_hi(wd) : bf16_lo(wd), w[k][i], acc);
+              }
+              y4[i] = fmaf(acc, tanh_approx(acc), acc);   // silu of 2 acc
+            }
+            uint32_t o[2], ox[2];
+            o[0] = pack_bf16x2(y4[0], y4[1]);
+            o[1] = pack_bf16x2(y4[2], y4[3]);
+            ox[0] = pack_bf16x2(y4[0] * fx, y4[1] * fx);
+            ox[1] = pack_bf16x2(y4[2] * fx, y4[3] * fx);
+            const uint32_t off = srow * 128 + (((vc4 >> 1) ^ (srow & 7)) << 4) + ((vc4 & 1) << 3);
+            if constexpr (!kStateOnly)   // (the state-only pass needs X' alone)
+              asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(sX + off), "r"(o[0]), "r"(o[1]) : "memory");
+            asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(sXp + off), "r"(ox[0]), "r"(ox[1]) : "memory");
+          }
         }
-        // the next chunk's rows (in flight during the epilogue below) and its scan
-        if (c + 1 < nk) {
-          load_rows(c + 1);
-          ALLOY_TRACE_POINT(4 + hh, c + 1, 6);
-          scan_chunk(c + 1);
-          ALLOY_TRACE_POINT(4 + hh, c + 1, 7);
+        prefetch_rows(c + 1 + kL2Ahead);
+        // X, X', cum, dt, cf of chunk c are ready
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(bar(B_X_READY0 + buf));
+          if (kStateOnly) mbar_arrive(bar(B_XF_EMPTY0 + buf));
         }
-        // the previous chunk's output, while the tensor cores and consumers work on this one
-        if constexpr (!kStateOnly) {
+        ALLOY_TRACE_POINT(4 + hh, c, 3);
+        return true;
+      };
+      if constexpr (!kStateOnly) {
+        // iteration c: chunk c (c >= 0); the rows and the scan of chunk c+1; the epilogue of c-1
+        for (int c = -1; c <= nk; ++c) {
+          if (c >= 0 && c < nk && !produce(c, rw)) break;
+          // the next chunk's rows (in flight during the epilogue below) and its scan
+          if (c + 1 < nk) {
+            load_rows(c + 1, rw);
+            ALLOY_TRACE_POINT(4 + hh, c + 1, 6);
+            scan_chunk(c + 1);
+            ALLOY_TRACE_POINT(4 + hh, c + 1, 7);
+          }
+          // the previous chunk's output, while the tensor cores and consumers work on this one
           if (c > 0 && !epilogue(c - 1)) break;
+          ALLOY_TRACE_POINT(4 + hh, c, 4);
         }
-        ALLOY_TRACE_POINT(4 + hh, c, 4);
+      } else {
+        // the conv alone (the consumer warps scan dt): the rows of chunk c+2
+        // are in flight while chunk c+1 is produced (two register sets)
+        uint32_t rw2[19][2];
+        load_rows(0, rw);
+        if (nk > 1) load_rows(1, rw2);
+        for (int c = 0; c < nk; c += 2) {
+          if (!produce(c, rw)) break;
+          if (c + 2 < nk) load_rows(c + 2, rw);
+          if (c + 1 >= nk || !produce(c + 1, rw2)) break;
+          if (c + 3 < nk) load_rows(c + 3, rw2);
+        }
       }
     } else {
       // ------------------------------------------------------------ consumers
@@ -803,51 +882,132 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       // state columns [cw * N/2, (cw+1) * N/2)
       const int hr = t >> 6, pr = t & 63;
 
-      // first segment record of this (batch row, head pair)
+      // segment records of this (batch row, head pair): record 0 the call's
+      // initial state, record j + 1 the end state of segment j from zero
       const size_t seg_slot = ((size_t)b * gridDim.x + blockIdx.x) * a.nseg;
       auto record = [&](int j, int n8) {
         return reinterpret_cast<float4*>(a.seg_state + ((seg_slot + j) * 128 + t) * N + cw * NHALF + n8 * 8);
       };
-      // initial state -> TMEM.  Unsegmented, the call's initial state.  The
-      // state-only pass starts segment 0 from it (and keeps a copy as record
-      // 0), later segments from zero.  The full pass of a segmented call reads
-      // the call's initial state only through those records, so an in-place
-      // update (ssm_out aliasing ssm_in) is safe: segment 0 starts from record
-      // 0, segment s > 0 from the true end state of segment 0 carried over
-      // segments 1 .. s-1 as state = exp(sum of A dt over segment j) state +
-      // (end state of segment j from zero).  sp: a strided view of the
-      // call's initial state or a record (n stride 1), or none (zero).
-      const float* sp = nullptr;
-      int64_t sn = 1;
-      if (kStateOnly || a.nseg == 1) {
-        if (a.ssm_in && (!kStateOnly || seg == 0)) {
-          sp = a.ssm_in + (int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh + (int64_t)pr * a.si_sp +
-               (int64_t)(cw * NHALF) * a.si_sn;
-          sn = a.si_sn;
+      if constexpr (kStateOnly) {
+        // segment 0 keeps the call's initial state (zeros without one) as
+        // record 0, so that the full pass never reads ssm_in of a segmented
+        // call and an in-place update (ssm_out aliasing ssm_in) is safe
+        if (seg == 0) {
+#pragma unroll 1
+          for (int n8 = 0; n8 < NHALF / 8; ++n8) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int n = cw * NHALF + n8 * 8 + i;
+              v[i] = a.ssm_in ? a.ssm_in[(int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh +
+                                         (int64_t)n * a.si_sn + (int64_t)pr * a.si_sp]
+                              : 0.f;
+            }
+            record(0, n8)[0] = make_float4(v[0], v[1], v[2], v[3]);
+            record(0, n8)[1] = make_float4(v[4], v[5], v[6], v[7]);
+          }
+        }
+        // ---- per chunk of the walk: dt, its scan and the X' row factors ----
+        // Warpgroup cw scans head h0 + cw, warp q rows [32q, 32q + 32).  The
+        // factor of row t is exp(the sum of A dt after row t to the segment's
+        // end) dt_t: the rest of its chunk (tot - cum_t) and the chunks walked
+        // before it (suffix).  Double-buffered in the cum region, which the
+        // state-only pass does not use otherwise.
+        {
+          const int head = h0 + cw;
+          const float A = -expf(a.A_log[(int64_t)head * a.al_s]);
+          const float dtb = a.dt_bias[(int64_t)head * a.dtb_s];
+          const int64_t dt_row = (int64_t)b * a.dt_sb + (int64_t)head * a.dt_sh;
+          auto load_dt = [&](int cc) {
+            uint32_t bits;
+            const int64_t di = dt_row + (int64_t)min(chunk_at(cc) * Q + t, L - 1) * a.dt_st;
+            if (a.dt_bf16)
+              asm volatile("ld.global.nc.u16 %0, [%1];" : "=r"(bits)
+                           : "l"(static_cast<const __nv_bfloat16*>(a.dt) + di));
+            else
+              asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(bits)
+                           : "l"(static_cast<const float*>(a.dt) + di));
+            return bits;
+          };
+          uint32_t dt_bits = load_dt(0);
+          float suffix = 0.f;
+          for (int c = 0; c < nk; ++c) {
+            const int buf = c & 1;
+            const float dt = chunk_at(c) * Q + t < L
+                ? softplus_f32((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
+                : 0.f;
+            if (c + 1 < nk) dt_bits = load_dt(c + 1);
+            float v = A * dt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const float u = __shfl_up_sync(0xffffffffu, v, o);
+              if (lane >= o) v += u;
+            }
+            // warp totals -> wsum[buf]: a warp writes it for chunk c+2 only after
+            // the wait for c+1, which every warp's arrival for c+1 precedes, and
+            // each warp reads wsum(c) before that arrival
+            if (lane == 31) wsum[(buf * 2 + cw) * 4 + q] = v;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_PWG0 + cw));
+            if (!waitw(bar(B_PWG0 + cw), c & 1, abort_flag, 24)) break;
+            float pre = 0.f, tot = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float w = wsum[(buf * 2 + cw) * 4 + i];
+              pre += i < q ? w : 0.f;
+              tot += w;
+            }
+            // the producers have read the factors of chunk c-2
+            if (c >= 2 && !waitw(bar(B_XF_EMPTY0 + buf), ((c >> 1) - 1) & 1, abort_flag, 25)) break;
+            cum_s[(buf * 2 + cw) * 128 + t] = ex2_approx((suffix + tot - (v + pre)) * kLog2e) * dt;
+            suffix += tot;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_XF_FULL0 + buf));
+          }
+          // the segment's log decay (head h0 + cw), for the full pass's carry
+          if (t == 0) a.seg_logdecay[(seg_slot + seg) * 2 + cw] = suffix;
+        }
+        // the segment's end state from zero -> record seg + 1
+        if (waitw(bar(B_ST_FINAL), 0, abort_flag, 36)) {
+          tc_fence_after();
+#pragma unroll 1
+          for (int n8 = 0; n8 < NHALF / 8; ++n8) {
+            uint32_t r[8];
+            tmem_ld8(lane_base + T_ST + cw * NHALF + n8 * 8, r);
+            tmem_ld_wait();
+            record(seg + 1, n8)[0] = make_float4(__uint_as_float(r[0]), __uint_as_float(r[1]),
+                                                 __uint_as_float(r[2]), __uint_as_float(r[3]));
+            record(seg + 1, n8)[1] = make_float4(__uint_as_float(r[4]), __uint_as_float(r[5]),
+                                                 __uint_as_float(r[6]), __uint_as_float(r[7]));
+          }
         }
       } else {
-        sp = reinterpret_cast<const float*>(record(seg == 0 ? 0 : 1, 0));
+      // initial state -> TMEM: the call's initial state (unsegmented), else
+      // record 0 carried over segments 0 .. seg-1 as state = exp(sum of A dt
+      // over segment j) state + (end state of segment j from zero).  sp: a
+      // strided view of ssm_in or record 0 (n stride 1), or none (zero).
+      const float* sp = nullptr;
+      int64_t sn = 1;
+      if (a.nseg > 1) {
+        sp = reinterpret_cast<const float*>(record(0, 0));
+      } else if (a.ssm_in) {
+        sp = a.ssm_in + (int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh + (int64_t)pr * a.si_sp +
+             (int64_t)(cw * NHALF) * a.si_sn;
+        sn = a.si_sn;
       }
 #pragma unroll 1
       for (int n8 = 0; n8 < NHALF / 8; ++n8) {
         float v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = sp ? sp[(int64_t)(n8 * 8 + i) * sn] : 0.f;
-        if constexpr (kStateOnly) {
-          if (seg == 0) {
-            record(0, n8)[0] = make_float4(v[0], v[1], v[2], v[3]);
-            record(0, n8)[1] = make_float4(v[4], v[5], v[6], v[7]);
-          }
-        } else {
 #pragma unroll 1
-          for (int j = 1; j < seg; ++j) {
-            const float dj = ex2_approx(a.seg_logdecay[(seg_slot + j) * 2 + hr] * kLog2e);
-            const float4* sj = record(j + 1, n8);
-            const float4 w0 = sj[0], w1 = sj[1];
-            const float add[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        for (int j = 0; j < seg; ++j) {
+          const float dj = ex2_approx(a.seg_logdecay[(seg_slot + j) * 2 + hr] * kLog2e);
+          const float4* sj = record(j + 1, n8);
+          const float4 w0 = sj[0], w1 = sj[1];
+          const float add[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = fmaf(dj, v[i], add[i]);
-          }
+          for (int i = 0; i < 8; ++i) v[i] = fmaf(dj, v[i], add[i]);
         }
         uint32_t r[8];
 #pragma unroll
@@ -855,7 +1015,6 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         tmem_st8(lane_base + T_ST + cw * NHALF + n8 * 8, r);
       }
       tmem_st_wait();
-      float logdecay = 0.f;   // sum of A dt over this segment (head hr), for the state-only pass
 
       // score pieces of this warp: 16-column halves g of the 32-column blocks
       // j = cw, cw + 2 (K-steps 2j + g of the Y MMA); blocks right of the
@@ -874,7 +1033,6 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         {
           const float lg_end = cum_s[(buf * 2 + hr) * 128 + 127];
           const float e_end = ex2_approx(lg_end * kLog2e);
-          logdecay += lg_end;
           const uint32_t sH = base + OFF_H + hr * 8192;   // [n block][head][64 p][64 n]
           const uint64_t e2 = f2_splat(e_end);
           // 16-column pieces of this warpgroup's state columns, the next piece
@@ -882,7 +1040,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           auto copy_piece = [&](int i, uint32_t (&r)[16]) {
             const int n0 = cw * NHALF + 16 * i;
 #pragma unroll
-            for (int g4 = 0; g4 < 2 && !kStateOnly; ++g4) {   // (no H in the state-only pass)
+            for (int g4 = 0; g4 < 2; ++g4) {
               const int n = n0 + g4 * 8;
               st_shared_v4(sH + (n >> 6) * 16384 + sw_off(pr, (n & 63) >> 3),
                            pack_bf16x2(__uint_as_float(r[g4 * 8 + 0]), __uint_as_float(r[g4 * 8 + 1])),
@@ -917,121 +1075,108 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_HBF_READY));
         ALLOY_TRACE_POINT(cw, c, 1);
-        if constexpr (!kStateOnly) {
-          // ---- scores of both heads, in place over CB ----
-          // S_h[t, s] = CB[t, s] exp(cum_h[t] - cum_h[s]) dt_h[s] for s <= t (+ D_h on
-          // s == t); K-step k (sources 16k .. 16k+15) of S_h stored as bf16 pairs
-          // in columns [16k + 8h, 16k + 8h + 8), inside the piece it was read from
-          if (!waitw(bar(B_CB_FULL), c & 1, abort_flag, 32)) break;
-          ALLOY_TRACE_POINT(cw, c, 2);
-          tc_fence_after();
-          auto score_piece = [&](int i, const uint32_t (&r)[16]) {
-            const int j = cw + 2 * (i >> 1);
-            const int s0 = piece_col(i);
-  #pragma unroll 1
-            for (int h = 0; h < 2; ++h) {
-              const float* cm = cum_s + (buf * 2 + h) * 128;
-              const float cum_t = cm[t];
-              uint32_t o[8];
-              if (j < q) {
-                // left of the diagonal block: exp(cum_t - cum_s) dt_s = R cf[s] with
-                // R = exp(cum_t - cum[s0+15]) <= 1 and cf[s] = exp(cum[s0+15] - cum_s) dt_s <= dt_s
-                const uint64_t R2 = f2_splat(ex2_approx((cum_t - cm[s0 + 15]) * kLog2e));
-                const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + s0);
-  #pragma unroll
-                for (int i4 = 0; i4 < 4; ++i4) {
-                  const float4 f = cf4[i4];
-                  o[2 * i4] = f2_to_bf2(
-                      f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4]), __uint_as_float(r[4 * i4 + 1])), R2),
-                             f2_pack(f.x, f.y)));
-                  o[2 * i4 + 1] = f2_to_bf2(
-                      f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4 + 2]), __uint_as_float(r[4 * i4 + 3])), R2),
-                             f2_pack(f.z, f.w)));
-                }
-              } else {
-                // the diagonal block: exact factors (<= 1 for s <= t, at any decay
-                // range), zero right of the diagonal, D on it
-                const float4* cm4 = reinterpret_cast<const float4*>(cm + s0);
-                const float4* dv4 = reinterpret_cast<const float4*>(dt_s + (buf * 2 + h) * 128 + s0);
-                const float Dh = h ? D1 : D0;
-  #pragma unroll
-                for (int i4 = 0; i4 < 4; ++i4) {
-                  const float4 c4 = cm4[i4], d4 = dv4[i4];
-                  const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, ds[4] = {d4.x, d4.y, d4.z, d4.w};
-                  float x[4];
-  #pragma unroll
-                  for (int u = 0; u < 4; ++u) {
-                    const int s = s0 + 4 * i4 + u;
-                    const float xv = __uint_as_float(r[4 * i4 + u]) * (ex2_approx((cum_t - cs[u]) * kLog2e) * ds[u]);
-                    x[u] = s < t ? xv : (s == t ? xv + Dh : 0.f);
-                  }
-                  o[2 * i4] = pack_bf16x2(x[0], x[1]);
-                  o[2 * i4 + 1] = pack_bf16x2(x[2], x[3]);
-                }
-              }
-              tmem_st8(lane_base + T_CB + s0 + 8 * h, o);
-            }
-          };
-          {
-            uint32_t ra[16], rb[16];
-            if (npieces > 0) tmem_ld16(lane_base + T_CB + piece_col(0), ra);
-  #pragma unroll 1
-            for (int i = 0; i < npieces; i += 2) {
-              tmem_ld_wait_regs(ra);
-              if (i == 0) ALLOY_TRACE_POINT(cw, c, 8);
-              tmem_ld16(lane_base + T_CB + piece_col(i + 1), rb);
-              score_piece(i, ra);
-              if (i == 0) ALLOY_TRACE_POINT(cw, c, 9);
-              tmem_ld_wait_regs(rb);
-              if (i + 2 < npieces) tmem_ld16(lane_base + T_CB + piece_col(i + 2), ra);
-              score_piece(i + 1, rb);
-              if (i == 0) ALLOY_TRACE_POINT(cw, c, 10);
-            }
-            uint32_t z[8];
-  #pragma unroll
-            for (int k = 0; k < 8; ++k) z[k] = 0u;
-  #pragma unroll 1
-            for (int i = npieces; i < 4; ++i) {
-              tmem_st8(lane_base + T_CB + piece_col(i), z);
-              tmem_st8(lane_base + T_CB + piece_col(i) + 8, z);
-            }
-          }
-          ALLOY_TRACE_POINT(cw, c, 11);
-          tmem_st_wait();
-          ALLOY_TRACE_POINT(cw, c, 12);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(B_S_READY));
-          ALLOY_TRACE_POINT(cw, c, 3);
-        }
-      }
-      // ---- the state at the segment's end: the state-only pass stores it
-      // (with the segment's log decay) for the later segments; the full pass
-      // of the last segment stores the final state to ssm_out ----
-      const bool store = kStateOnly || (a.ssm_out && seg == a.nseg - 1);
-      if (!*abort_flag && store && waitw(bar(B_YI_DONE), (nk - 1) & 1, abort_flag, 35)) {
+        // ---- scores of both heads, in place over CB ----
+        // S_h[t, s] = CB[t, s] exp(cum_h[t] - cum_h[s]) dt_h[s] for s <= t (+ D_h on
+        // s == t); K-step k (sources 16k .. 16k+15) of S_h stored as bf16 pairs
+        // in columns [16k + 8h, 16k + 8h + 8), inside the piece it was read from
+        if (!waitw(bar(B_CB_FULL), c & 1, abort_flag, 32)) break;
+        ALLOY_TRACE_POINT(cw, c, 2);
         tc_fence_after();
-        float* sig = reinterpret_cast<float*>(record(seg + 1, 0));
-        if (kStateOnly && cw == 0 && pr == 0) a.seg_logdecay[(seg_slot + seg) * 2 + hr] = logdecay;
+        auto score_piece = [&](int i, const uint32_t (&r)[16]) {
+          const int j = cw + 2 * (i >> 1);
+          const int s0 = piece_col(i);
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            const float* cm = cum_s + (buf * 2 + h) * 128;
+            const float cum_t = cm[t];
+            uint32_t o[8];
+            if (j < q) {
+              // left of the diagonal block: exp(cum_t - cum_s) dt_s = R cf[s] with
+              // R = exp(cum_t - cum[s0+15]) <= 1 and cf[s] = exp(cum[s0+15] - cum_s) dt_s <= dt_s
+              const uint64_t R2 = f2_splat(ex2_approx((cum_t - cm[s0 + 15]) * kLog2e));
+              const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + s0);
+#pragma unroll
+              for (int i4 = 0; i4 < 4; ++i4) {
+                const float4 f = cf4[i4];
+                o[2 * i4] = f2_to_bf2(
+                    f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4]), __uint_as_float(r[4 * i4 + 1])), R2),
+                           f2_pack(f.x, f.y)));
+                o[2 * i4 + 1] = f2_to_bf2(
+                    f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4 + 2]), __uint_as_float(r[4 * i4 + 3])), R2),
+                           f2_pack(f.z, f.w)));
+              }
+            } else {
+              // the diagonal block: exact factors (<= 1 for s <= t, at any decay
+              // range), zero right of the diagonal, D on it
+              const float4* cm4 = reinterpret_cast<const float4*>(cm + s0);
+              const float4* dv4 = reinterpret_cast<const float4*>(dt_s + (buf * 2 + h) * 128 + s0);
+              const float Dh = h ? D1 : D0;
+#pragma unroll
+              for (int i4 = 0; i4 < 4; ++i4) {
+                const float4 c4 = cm4[i4], d4 = dv4[i4];
+                const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, ds[4] = {d4.x, d4.y, d4.z, d4.w};
+                float x[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const int s = s0 + 4 * i4 + u;
+                  const float xv = __uint_as_float(r[4 * i4 + u]) * (ex2_approx((cum_t - cs[u]) * kLog2e) * ds[u]);
+                  x[u] = s < t ? xv : (s == t ? xv + Dh : 0.f);
+                }
+                o[2 * i4] = pack_bf16x2(x[0], x[1]);
+                o[2 * i4 + 1] = pack_bf16x2(x[2], x[3]);
+              }
+            }
+            tmem_st8(lane_base + T_CB + s0 + 8 * h, o);
+          }
+        };
+        {
+          uint32_t ra[16], rb[16];
+          if (npieces > 0) tmem_ld16(lane_base + T_CB + piece_col(0), ra);
+#pragma unroll 1
+          for (int i = 0; i < npieces; i += 2) {
+            tmem_ld_wait_regs(ra);
+            if (i == 0) ALLOY_TRACE_POINT(cw, c, 8);
+            tmem_ld16(lane_base + T_CB + piece_col(i + 1), rb);
+            score_piece(i, ra);
+            if (i == 0) ALLOY_TRACE_POINT(cw, c, 9);
+            tmem_ld_wait_regs(rb);
+            if (i + 2 < npieces) tmem_ld16(lane_base + T_CB + piece_col(i + 2), ra);
+            score_piece(i + 1, rb);
+            if (i == 0) ALLOY_TRACE_POINT(cw, c, 10);
+          }
+          uint32_t z[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) z[k] = 0u;
+#pragma unroll 1
+          for (int i = npieces; i < 4; ++i) {
+            tmem_st8(lane_base + T_CB + piece_col(i), z);
+            tmem_st8(lane_base + T_CB + piece_col(i) + 8, z);
+          }
+        }
+        ALLOY_TRACE_POINT(cw, c, 11);
+        tmem_st_wait();
+        ALLOY_TRACE_POINT(cw, c, 12);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_S_READY));
+        ALLOY_TRACE_POINT(cw, c, 3);
+      }
+      // ---- the final state: the last segment's end state -> ssm_out ----
+      if (!*abort_flag && a.ssm_out && seg == a.nseg - 1 && waitw(bar(B_YI_DONE), (nk - 1) & 1, abort_flag, 35)) {
+        tc_fence_after();
 #pragma unroll 1
         for (int n8 = 0; n8 < NHALF / 8; ++n8) {
           const int n0 = cw * NHALF + n8 * 8;
           uint32_t r[8];
           tmem_ld8(lane_base + T_ST + n0, r);
           tmem_ld_wait();
-          if constexpr (kStateOnly) {
-            reinterpret_cast<float4*>(sig)[2 * n8] =
-                make_float4(__uint_as_float(r[0]), __uint_as_float(r[1]), __uint_as_float(r[2]), __uint_as_float(r[3]));
-            reinterpret_cast<float4*>(sig)[2 * n8 + 1] =
-                make_float4(__uint_as_float(r[4]), __uint_as_float(r[5]), __uint_as_float(r[6]), __uint_as_float(r[7]));
-          } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              a.ssm_out[(int64_t)b * a.so_sb + (int64_t)(h0 + hr) * a.so_sh + (int64_t)(n0 + i) * a.so_sn +
-                        (int64_t)pr * a.so_sp] = __uint_as_float(r[i]);
-          }
+          for (int i = 0; i < 8; ++i)
+            a.ssm_out[(int64_t)b * a.so_sb + (int64_t)(h0 + hr) * a.so_sh + (int64_t)(n0 + i) * a.so_sn +
+                      (int64_t)pr * a.so_sp] = __uint_as_float(r[i]);
         }
       }
+      }   // full pass
     }
     tc_fence_before();
   }
