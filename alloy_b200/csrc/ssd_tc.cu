@@ -93,7 +93,7 @@ constexpr uint32_t OFF_CUM = OFF_MISC;              // [2 buffers][2 heads][128]
 constexpr uint32_t OFF_DT = OFF_CUM + 2048;         // [2][2][128]
 constexpr uint32_t OFF_CF = OFF_DT + 2048;          // [2][2][128] column factors
 constexpr uint32_t OFF_WSUM = OFF_CF + 2048;        // [2 buffers][2 heads][4 warps]
-constexpr uint32_t OFF_CW = OFF_WSUM + 64;          // x conv weights [2][64][4] + bias [2][64]
+constexpr uint32_t OFF_CW = OFF_WSUM + 64;          // x conv weights [2][4][16][4] + bias [2][16][4]
 constexpr uint32_t OFF_XF = OFF_CW + 2560;          // X' row factors [2 heads][128]
 constexpr uint32_t OFF_BAR = OFF_XF + 1024;         // mbarriers (8 bytes each)
 constexpr int NBAR = 17;
@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
   float* dt_s = reinterpret_cast<float*>(smem + OFF_DT);
   float* cf_s = reinterpret_cast<float*>(smem + OFF_CF);
   float* wsum = reinterpret_cast<float*>(smem + OFF_WSUM);
-  float* cw_all = reinterpret_cast<float*>(smem + OFF_CW);   // [2][64][4], then bias [2][64]
+  float* cw_all = reinterpret_cast<float*>(smem + OFF_CW);   // [2][4][16][4], then bias [2][16][4]
   float* xf_s = reinterpret_cast<float*>(smem + OFF_XF);     // [head][128]
   volatile uint32_t* tmem_ptr = reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEMPTR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_ABORT);
@@ -432,13 +432,15 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
     tmem_alloc(base + OFF_TMEMPTR, 512);
     tmem_relinquish();
   }
-  // x conv weights of both heads, [head][channel][tap] and bias [head][channel],
-  // halved: the conv then gives h = x/2 and silu(x) = h + h tanh(h)
+  // x conv weights of both heads, [head][tap][channel], and bias
+  // [head][channel], halved: the conv then gives h = x/2 and silu(x) = h +
+  // h tanh(h).  A producer thread reads its 4 channels of a tap as one float4,
+  // the 16 channel groups of a warp in consecutive banks.
   if (threadIdx.x < 128) {
     const int hh = threadIdx.x >> 6, ch = threadIdx.x & 63;
     const int64_t c = (int64_t)(h0 + hh) * P + ch;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) cw_all[(hh * 64 + ch) * 4 + k] = 0.5f * a.conv_w[c * a.cw_sc + k * a.cw_sk];
+    for (int k = 0; k < 4; ++k) cw_all[(hh * 4 + k) * 64 + ch] = 0.5f * a.conv_w[c * a.cw_sc + k * a.cw_sk];
     cw_all[512 + hh * 64 + ch] = a.conv_b ? 0.5f * a.conv_b[c * a.cb_s] : 0.f;
   }
   tc_fence_before();
@@ -779,11 +781,13 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         {
           float w[4][4], bias[4];   // [tap][channel]
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float* w0 = cw_all + (hh * 64 + vc4 * 4 + i) * 4;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) w[k][i] = w0[k];
-            bias[i] = cw_all[512 + hh * 64 + vc4 * 4 + i];
+          for (int k = 0; k < 4; ++k) {
+            const float4 wk = *reinterpret_cast<const float4*>(cw_all + (hh * 4 + k) * 64 + vc4 * 4);
+            w[k][0] = wk.x; w[k][1] = wk.y; w[k][2] = wk.z; w[k][3] = wk.w;
+          }
+          {
+            const float4 bk = *reinterpret_cast<const float4*>(cw_all + 512 + hh * 64 + vc4 * 4);
+            bias[0] = bk.x; bias[1] = bk.y; bias[2] = bk.z; bias[3] = bk.w;
           }
           if (chunk_at(c) == 0 && strip == 0) {
             // rows before t = 0 come from the conv cache (zeros without one)
@@ -1105,9 +1109,33 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
                     f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4 + 2]), __uint_as_float(r[4 * i4 + 3])), R2),
                            f2_pack(f.z, f.w)));
               }
+            } else if (cm[32 * q] - cm[32 * q + 31] < 64.f) {
+              // the diagonal block with a decay range below e^64 over its 32
+              // rows (uniform across the warp): factored like the pieces left of
+              // it, R = exp(cum_t - cum[s0+15]) <= e^64; zero right of the
+              // diagonal, D on it
+              const uint64_t R2 = f2_splat(ex2_approx((cum_t - cm[s0 + 15]) * kLog2e));
+              const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + s0);
+              const float Dh = h ? D1 : D0;
+#pragma unroll
+              for (int i4 = 0; i4 < 4; ++i4) {
+                const float4 f = cf4[i4];
+                float x[4];
+                f2_unpack(f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4]), __uint_as_float(r[4 * i4 + 1])), R2),
+                                 f2_pack(f.x, f.y)), x[0], x[1]);
+                f2_unpack(f2_mul(f2_mul(f2_pack(__uint_as_float(r[4 * i4 + 2]), __uint_as_float(r[4 * i4 + 3])), R2),
+                                 f2_pack(f.z, f.w)), x[2], x[3]);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const int s = s0 + 4 * i4 + u;
+                  x[u] = s < t ? x[u] : (s == t ? x[u] + Dh : 0.f);
+                }
+                o[2 * i4] = pack_bf16x2(x[0], x[1]);
+                o[2 * i4 + 1] = pack_bf16x2(x[2], x[3]);
+              }
             } else {
-              // the diagonal block: exact factors (<= 1 for s <= t, at any decay
-              // range), zero right of the diagonal, D on it
+              // the diagonal block at a larger decay range: exact factors (<= 1
+              // for s <= t, at any range), zero right of the diagonal, D on it
               const float4* cm4 = reinterpret_cast<const float4*>(cm + s0);
               const float4* dv4 = reinterpret_cast<const float4*>(dt_s + (buf * 2 + h) * 128 + s0);
               const float Dh = h ? D1 : D0;
