@@ -47,6 +47,7 @@ EXPORTS = (
     "alloy_check_device_status",
     "alloy_ssd_combined_noalloc",
     "alloy_kernel_launch_count",
+    "alloy_gated_rmsnorm",
 )
 
 
@@ -122,6 +123,8 @@ def load():
                                                           ctypes.c_int32, D]
         lib.alloy_ssd_combined_min_workspace_size.restype = ctypes.c_size_t
         lib.alloy_check_device_status.argtypes = [vp]
+        lib.alloy_gated_rmsnorm.argtypes = [P, P, P, P, ctypes.c_float, ctypes.c_int64, vp]
+        lib.alloy_gated_rmsnorm.restype = ctypes.c_int
         lib.alloy_kernel_launch_count.argtypes = []
         lib.alloy_kernel_launch_count.restype = ctypes.c_uint64
         lib.alloy_ssd_combined_noalloc.argtypes = [P] * 12 + [D, vp]

@@ -247,6 +247,33 @@ size_t alloy_ssd_combined_min_workspace_size(int64_t batch, int64_t seqlen, int3
   return ssd_combined_workspace(batch, seqlen, dtype, dims, false);
 }
 
+int alloy_gated_rmsnorm(const alloy_tensor_t* y, const alloy_tensor_t* gate,
+                        const alloy_tensor_t* weight, alloy_tensor_t* out, float eps,
+                        int64_t group_size, void* stream) {
+  last_error().clear();
+  ALLOY_TRY(check_tensor(y, "y", 2, nullptr, kAnyFloat));
+  const int64_t rows = y->shape[0], D = y->shape[1];
+  const int64_t s2[2] = {rows, D};
+  const unsigned act = 1u << y->dtype;
+  ALLOY_TRY(check_tensor(gate, "gate", 2, s2, act));
+  ALLOY_TRY(check_tensor(out, "out", 2, s2, act));
+  if (y->stride[1] != 1 || gate->stride[1] != 1 || out->stride[1] != 1)
+    return fail(ALLOY_ERR_INVALID_ARG, "gated_rmsnorm: channel stride must be 1");
+  ALLOY_TRY(check_vec(weight, "weight", D, kF32, true));
+  const int64_t grp = group_size == 0 ? D : group_size;
+  if (grp <= 0 || (D > 0 && D % grp != 0))
+    return fail(ALLOY_ERR_INVALID_ARG, "gated_rmsnorm: group_size %lld does not divide %lld channels",
+                (long long)group_size, (long long)D);
+  if (!(eps >= 0.f)) return fail(ALLOY_ERR_INVALID_ARG, "gated_rmsnorm: eps must be >= 0");
+  if (D > (1 << 24) || rows >= ((int64_t)1 << 31))
+    return fail(ALLOY_ERR_UNSUPPORTED, "gated_rmsnorm: %lld rows x %lld channels too large",
+                (long long)rows, (long long)D);
+  if (rows == 0 || D == 0) return ALLOY_OK;
+  ALLOY_TRY(current_device_checked(nullptr));
+  return gated_rmsnorm(y, gate, present(weight) ? weight : nullptr, out, eps, (int)grp,
+                       as_stream(stream));
+}
+
 uint64_t alloy_kernel_launch_count(void) { return launch_counter().load(std::memory_order_relaxed); }
 
 int alloy_check_device_status(void* stream) {

@@ -68,6 +68,11 @@ struct DecodeArgs {
 };
 int ssd_decode_step(const DecodeArgs& a, cudaStream_t s);
 
+// norm.cu: out = rmsnorm(y * silu(gate)) * w over groups of `group` channels
+// (w null: out = y * silu(gate)); y, gate, out [rows, D] with channel stride 1.
+int gated_rmsnorm(const alloy_tensor_t* y, const alloy_tensor_t* gate, const alloy_tensor_t* w,
+                  alloy_tensor_t* out, float eps, int group, cudaStream_t s);
+
 // ssd_tc.cu: tcgen05 tensor-core SSD for bf16 inputs (mode 0 only).
 // Returns ALLOY_ERR_UNSUPPORTED (and launches nothing) for sizes it does not cover.
 bool ssd_tc_supported(const SsdArgs& a);

@@ -83,7 +83,8 @@ class MambaBlock(torch.nn.Module):
         self.A_log = torch.nn.Parameter(torch.zeros(self.n_heads, **p32))
         self.dt_bias = torch.nn.Parameter(torch.zeros(self.n_heads, **p32))
         self.D = torch.nn.Parameter(torch.zeros(self.n_heads, **p32)) if use_D else None
-        self.norm = torch.nn.RMSNorm(d_inner, **fk) if use_inner_norm else None
+        # eps of the reference's nn.RMSNorm (MLX default 1e-5)
+        self.norm = torch.nn.RMSNorm(d_inner, eps=1e-5, **fk) if use_inner_norm else None
         self.out_proj = torch.nn.Linear(d_inner, d_model, bias=False, **fk)
 
     # ------------------------------------------------------------------ hot path
@@ -172,7 +173,7 @@ class MambaBlock(torch.nn.Module):
             if cache is not None:
                 cache.ssm_state, cache.conv_state = h, cs
             y = y.reshape(Bsz, L, self.d_inner)
-        y = y * F.silu(gate)
-        if self.norm is not None:
-            y = self.norm(y)
+        # gate first, then the inner norm (:495-499), fused in one kernel
+        y = mixer.gated_rmsnorm(y, gate, self.norm.weight if self.norm is not None else None,
+                                eps=self.norm.eps if self.norm is not None else 1e-5)
         return self.out_proj(y)

@@ -19,7 +19,7 @@ from . import _lib
 
 __all__ = [
     "conv1d_silu", "depthwise_conv1d", "ssd_combined", "selective_scan",
-    "ssd_decode_step",
+    "ssd_decode_step", "gated_rmsnorm",
 ]
 
 
@@ -216,5 +216,33 @@ def ssd_decode_step(xBC_tok, dt_tok, conv_weight, conv_bias, dt_bias, A_log, D, 
     descs = [_lib.desc(t, n) for t, n in args]
     with torch.cuda.device(dev):
         _lib.call("alloy_ssd_decode_step", *(_lib.ref(d) for d in descs), _lib.ref(dims),
+                  _lib.stream_handle(dev))
+    return out
+
+
+def gated_rmsnorm(y, gate, weight=None, *, eps=1e-5, group_size=0, out=None):
+    """The gate and inner norm after the scan, ``MambaBlock._forward_combined``
+    step 7 (alloy/models/mamba_block.py:495-499): ``g = y * silu(gate)``, then
+    (when ``weight`` is given) ``g * rsqrt(mean(g^2) + eps) * weight`` over the
+    last dimension (``nn.RMSNorm(d_inner)``, :137) or over runs of
+    ``group_size`` channels of it.  ``y`` and ``gate`` [..., D] of one dtype
+    (bf16 or fp32); fp32 math; returns ``out`` (y's shape and dtype; may be
+    ``y`` itself).
+    """
+    dev = _same_device(("y", y), ("gate", gate), ("weight", weight), ("out", out))
+    if gate.shape != y.shape:
+        raise ValueError(f"gate shape {tuple(gate.shape)} != y shape {tuple(y.shape)}")
+    D = y.shape[-1]
+    if out is None:
+        out = torch.empty(y.shape, dtype=y.dtype, device=dev)
+    rows = lambda t: t.reshape(-1, D)   # a view for the usual layouts; a copy only for inputs
+    try:
+        out2 = out.view(-1, D)
+    except RuntimeError as e:
+        raise ValueError("out: its leading dimensions must flatten without a copy") from e
+    args = [(rows(y), "y"), (rows(gate), "gate"), (_f32(weight), "weight"), (out2, "out")]
+    descs = [_lib.desc(t, n) for t, n in args]
+    with torch.cuda.device(dev):
+        _lib.call("alloy_gated_rmsnorm", *(_lib.ref(d) for d in descs), float(eps), int(group_size),
                   _lib.stream_handle(dev))
     return out

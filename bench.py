@@ -45,6 +45,9 @@ WORKLOADS = {
                  G=1, K=4, Q=512),
     "decode": dict(name="nemotron_h_8b_mamba2_decode_step", B=256, L=1, H=128, P=64, N=128, G=8,
                    K=4, Q=256),
+    # the gate and inner RMS norm after the scan (d_inner = H * P), full-width norm
+    "gated_norm": dict(name="nemotron_h_8b_mamba2_gated_rmsnorm", B=4, L=8192, H=128, P=64,
+                       N=128, G=8, K=4, Q=256),
 }
 
 L2_BYTES = 126 * 1024 * 1024
@@ -283,6 +286,11 @@ def run_ours(args, w):
 
     # ---- end to end through the public API, host buffers ----
     e2e = None if args.no_e2e else run_e2e(args, sets[0], kw, world, stream, B * L)
+    # ---- the same steps followed by the all-gather of y (a caller that needs
+    # every head of y on every GPU; head shards only, so N > 1) ----
+    gather = None
+    if world > 1 and (args.gather or args.workload == "long"):
+        gather = run_with_gather(args, step, sets, world, stream, B * L)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -309,12 +317,45 @@ def run_ours(args, w):
         }
         if e2e is not None:
             line["e2e"] = e2e
+        if gather is not None:
+            line["with_gather"] = gather
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def run_with_gather(args, step, sets, world, stream, tokens):
+    """Device-timed steps, each one prefill followed by the all-gather of y
+    over the ranks (`sharding.allgather_heads`: one NCCL all-gather into a
+    head-major buffer, then a permute to [B, L, H, P]); max over ranks."""
+    import torch
+    from alloy_b200 import sharding
+    rot = len(sets)
+    y_bytes = sets[0][1]["y"].numel() * sets[0][1]["y"].element_size()
+
+    def gstep(i):
+        step(i)
+        sharding.allgather_heads(sets[i % rot][1]["y"], world)
+
+    for i in range(args.warmup):
+        gstep(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        gstep(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = dist_max(ev0.elapsed_time(ev1) / args.steps, world)
+    return {"value": tokens / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "collective": "NCCL all_gather of y (head-major) + permute to [B, L, H, P]",
+            "bytes_received_per_gpu": y_bytes * (world - 1)}
 
 
 def run_e2e(args, set0, kw, world, stream, tokens):
@@ -359,6 +400,76 @@ def run_e2e(args, set0, kw, world, stream, tokens):
     return {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
             "ms_per_step": e2e_ms, "steps": e2e_steps}
+
+
+def run_gated_norm(args, w):
+    """Gate + inner RMS norm of the mixer output (y * silu(gate), then the
+    full-width RMS norm with a weight): the rows of the workload's tokens split
+    over the GPUs; reported as achieved HBM GB/s (y and gate read once, out
+    written once).  Inputs rotate through enough sets to exceed 3x L2."""
+    import torch
+    from alloy_b200 import _lib, mixer
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    D = w["H"] * w["P"]
+    rows_total = w["B"] * w["L"]
+    if rows_total % world:
+        raise SystemExit("rows do not split over the GPUs")
+    rows = rows_total // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11 + rank)
+    set_bytes = 3 * rows * D * 2
+    rot = max(1, math.ceil(3 * L2_BYTES / set_bytes))
+    sets = [(torch.randn((rows, D), generator=gen, device=dev).to(torch.bfloat16),
+             torch.randn((rows, D), generator=gen, device=dev).to(torch.bfloat16),
+             torch.empty((rows, D), dtype=torch.bfloat16, device=dev)) for _ in range(rot)]
+    weight = torch.rand(D, generator=gen, device=dev) + 0.5
+
+    def step(i):
+        y, g, o = sets[i % rot]
+        mixer.gated_rmsnorm(y, g, weight, eps=1e-5, out=o)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    h0 = time.perf_counter()
+    launches0 = _lib.load().alloy_kernel_launch_count()
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    launches = _lib.load().alloy_kernel_launch_count() - launches0
+    torch.cuda.synchronize()
+    h1 = time.perf_counter()
+    barrier(world)
+    clocks.stop()
+    ms = dist_max(ev0.elapsed_time(ev1) / args.steps, world)
+    alg = 3 * rows * D * 2 + D * 4
+    peak, peak_kind = measured_peaks()
+    gbs = alg * world / (ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Mamba-2 gated RMS norm (y * silu(gate), RMSNorm(d_inner)) HBM GB/s",
+            "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": w["name"], "rows": rows_total, "channels": D,
+                       "norm": "full width, eps 1e-5, fp32 weight",
+                       "l2": f"{rot} rotating input/output sets of {set_bytes / 2**20:.0f} MiB"},
+            "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / world / peak, "traffic": None,
+                         "peak_source": f"{peak_kind} hbm_gbs"},
+            "gpu_launches": launches, "clocks": clocks.summary(h0, h1)}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
 
 
 def run_decode(args, w):
@@ -525,6 +636,9 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="nemotron")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    ap.add_argument("--gather", action="store_true",
+                    help="also time each step followed by the all-gather of y (N > 1; "
+                         "always on for the long workload)")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the workload's batch (smaller cases for profiling)")
     ap.add_argument("--seqlen", type=int, default=None,
@@ -543,6 +657,8 @@ def main():
         run_reference(args, w)
     elif args.workload == "decode":
         run_decode(args, w)
+    elif args.workload == "gated_norm":
+        run_gated_norm(args, w)
     else:
         run_ours(args, w)
 

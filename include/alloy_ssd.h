@@ -208,6 +208,27 @@ ALLOY_API int alloy_ssd_combined_noalloc(const alloy_tensor_t* xBC, const alloy_
 ALLOY_API int alloy_check_device_status(void* stream);
 
 /*
+ * Gated RMS norm of the mixer output:
+ *   g = y * silu(gate);  out = g * rsqrt(mean of g^2 over the group + eps) * weight
+ * with the group the whole row (group_size 0) or consecutive runs of
+ * group_size channels; math in fp32, out in the activation dtype.  With
+ * weight NULL (data NULL) only the gate is applied: out = y * silu(gate).
+ * Replaces step 7 of MambaBlock._forward_combined
+ * (alloy/models/mamba_block.py:495-499: `y = y * nn.silu(gate)`, then
+ * `self.norm(y)` with the nn.RMSNorm(d_inner) of :137, eps 1e-5).
+ *   y, gate, out  [rows, D] BF16 or F32 (one dtype), channel stride 1, any row
+ *                 stride; out may alias y (same element layout)
+ *   weight        [D] F32, or NULL
+ *   eps           >= 0, added to the mean of squares
+ *   group_size    channels per norm group, dividing D (0 = D)
+ * No counterpart kernel in the reference (MLX element-wise ops and
+ * mx.fast.rms_norm).
+ */
+ALLOY_API int alloy_gated_rmsnorm(const alloy_tensor_t* y, const alloy_tensor_t* gate,
+                                  const alloy_tensor_t* weight, alloy_tensor_t* out, float eps,
+                                  int64_t group_size, void* stream);
+
+/*
  * Number of kernels this library has launched in this process (every thread
  * and device), for counting the launches of a timed region: a segmented
  * prefill (alloy_ssd_combined with fewer (batch row, head pair) units than

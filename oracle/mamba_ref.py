@@ -25,8 +25,8 @@ __all__ = [
     "softplus", "sigmoid", "silu", "depthwise_conv1d", "conv1d_silu",
     "pad_conv_input", "discretize", "scan_chunk", "selective_scan",
     "selective_scan_sequential", "mixer_core", "mixer_core_fp64",
-    "decode_step_fp64", "make_inputs", "bf16_round", "rel_l2", "max_rel",
-    "CONFIGS",
+    "decode_step_fp64", "gated_rmsnorm", "make_inputs", "bf16_round", "rel_l2",
+    "max_rel", "CONFIGS",
 ]
 
 
@@ -268,6 +268,29 @@ def decode_step_fp64(xBC_tok, dt_tok, conv_weight, conv_bias, dt_bias, A_log, D,
                                headdim=headdim, d_state=d_state, n_groups=n_groups,
                                ssm_state=ssm_state, conv_state=conv_state)
     return y[:, 0], h, cs
+
+
+# ---------------------------------------------------------------------------
+# gate and inner norm after the scan
+# ---------------------------------------------------------------------------
+
+def gated_rmsnorm(y, gate, weight=None, eps=1e-5, group_size=0):
+    """Step 7 of ``_forward_combined`` (mamba_block.py:495-499): the gate first,
+    ``y * nn.silu(gate)``, then ``nn.RMSNorm(d_inner)`` (:137; MLX's
+    ``x * rsqrt(mean(x^2, -1) + eps) * weight``, eps 1e-5) when a weight is
+    given.  ``group_size`` > 0 normalises runs of that many channels instead of
+    the whole row (the group-wise form of the same norm).  float32 on the given
+    values."""
+    y = np.asarray(y, F32)
+    g = np.asarray(gate, F32)
+    v = y * silu(g)
+    if weight is None:
+        return v
+    D = v.shape[-1]
+    gs = group_size or D
+    vg = v.reshape(*v.shape[:-1], D // gs, gs)
+    r = F32(1) / np.sqrt(np.mean(vg * vg, axis=-1, keepdims=True, dtype=F32) + F32(eps))
+    return (vg * r).reshape(v.shape) * np.asarray(weight, F32)
 
 
 # ---------------------------------------------------------------------------

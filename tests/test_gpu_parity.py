@@ -253,14 +253,55 @@ def test_decode_step_vs_fp64(state_layout, N, P, G, H):
     np.testing.assert_array_equal(np_(conv_store.transpose(1, 2)), cs64.astype(np.float32))
 
 
+# ------------------------------------------------------------ gate + inner norm
+@pytest.mark.parametrize("rows,D,group,dtype,with_w", [
+    (64, 8192, 0, torch.bfloat16, True),      # Nemotron-H d_inner, full-width norm
+    (33, 4096, 0, torch.bfloat16, True),      # Zamba2 d_inner
+    (16, 8192, 1024, torch.bfloat16, True),   # group-wise: 8 groups of 1024 channels
+    (40, 4096, 0, torch.float32, True),       # fp32 (4-wide vectors)
+    (8, 8192, 0, torch.bfloat16, False),      # the gate alone
+    (7, 100, 0, torch.bfloat16, True),        # 100 channels: the scalar kernel
+    (5, 20000, 0, torch.float32, True),       # more than 8 vectors a thread: the scalar kernel
+])
+def test_gated_rmsnorm_vs_oracle(rows, D, group, dtype, with_w):
+    rng = np.random.default_rng(rows + D)
+    y = rng.standard_normal((rows, D)).astype(np.float32)
+    g = rng.standard_normal((rows, D)).astype(np.float32)
+    w = rng.uniform(0.5, 1.5, D).astype(np.float32) if with_w else None
+    yt, gt = cu(y, dtype), cu(g, dtype)
+    out = mixer.gated_rmsnorm(yt, gt, cu(w) if with_w else None, eps=1e-5, group_size=group)
+    torch.cuda.synchronize()
+    assert out.dtype == dtype and out.shape == yt.shape
+    ref = oracle.gated_rmsnorm(np_(yt), np_(gt), w, eps=1e-5, group_size=group)
+    assert_close(np_(out), ref, dtype == torch.bfloat16)
+
+
+@pytest.mark.parametrize("extra", [1280, 1283])   # row stride a multiple of 8 or not
+def test_gated_rmsnorm_strided_gate_in_place(extra):
+    """The gate as a column slice of the in-projection's output (row stride >
+    D), y normalised in place."""
+    proj = torch.randn(2, 50, 8192 + extra, device=DEV).to(torch.bfloat16)
+    gate = proj[..., :8192]
+    y = torch.randn(2, 50, 8192, device=DEV).to(torch.bfloat16)
+    w = torch.rand(8192, device=DEV) + 0.5
+    ref = oracle.gated_rmsnorm(np_(y), np_(gate), np_(w))
+    out = mixer.gated_rmsnorm(y, gate, w, out=y)
+    torch.cuda.synchronize()
+    assert out.data_ptr() == y.data_ptr()
+    assert_close(np_(out), ref, True)
+
+
 # ------------------------------------------------------------------- block level
-@pytest.mark.parametrize("combined", [True, False])
+@pytest.mark.parametrize("combined", [True, False, "norm"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_block_autoregressive_matches_parallel(combined, dtype):
     """The reference's tests/test_mamba_block.py:39-60 invariant: step-by-step
-    generation through the cache equals one parallel pass."""
+    generation through the cache equals one parallel pass ("norm": the
+    combined projection with the inner RMS norm, Zamba2's configuration)."""
     torch.manual_seed(42)
     kw = dict(combined_proj=True, n_groups=2, use_D=True) if combined else {}
+    if combined == "norm":
+        kw["use_inner_norm"] = True
     blk = MambaBlock(d_model=64, d_state=16, d_conv=4, expand=2, headdim=32, chunk_size=16,
                      device=DEV, dtype=dtype, **kw)
     with torch.no_grad():

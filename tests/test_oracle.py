@@ -117,3 +117,23 @@ def test_make_inputs_distributions():
     assert (A >= 1).all() and (A <= 16).all()
     assert abs(inp["conv_weight"].std() - 0.5) < 0.1
     assert inp["xBC"].shape == (2, 64, 32 * 8 + 2 * 2 * 4)
+
+
+def test_gated_rmsnorm_matches_fp64():
+    """Gate first, then RMS norm over the row or over channel groups
+    (mamba_block.py:495-499), against a float64 restatement."""
+    rng = np.random.default_rng(5)
+    y = rng.standard_normal((4, 96)).astype(np.float32)
+    g = rng.standard_normal((4, 96)).astype(np.float32)
+    w = rng.uniform(0.5, 1.5, 96).astype(np.float32)
+    v = y.astype(np.float64) * g / (1 + np.exp(-g.astype(np.float64)))
+    for gs in (0, 32):
+        n = gs or 96
+        vv = v.reshape(4, 96 // n, n)
+        ref = (vv / np.sqrt((vv ** 2).mean(-1, keepdims=True) + 1e-5)).reshape(4, 96) * w
+        got = oracle.gated_rmsnorm(y, g, w, eps=1e-5, group_size=gs)
+        assert got.dtype == np.float32
+        assert oracle.rel_l2(got, ref) < 1e-6
+    # no weight: the gate alone
+    assert oracle.rel_l2(oracle.gated_rmsnorm(y, g), v) < 1e-6
+
