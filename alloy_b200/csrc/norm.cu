@@ -19,6 +19,19 @@ constexpr int kNormThreads = 256;
 // silu(x) = x / (1 + e^-x) with the hardware exponential and reciprocal (a few
 // ulp; the accurate library forms would make this memory-bound kernel issue-bound)
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
+// bf16 outputs: silu(x) = h + h tanh(h) with h = x/2, one hardware tanh
+// (relative error ~2^-11, below the 2^-9 rounding of the bf16 result)
+__device__ __forceinline__ float silu_tanh(float x) {
+  float t;
+  const float h = 0.5f * x;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+  return fmaf(h, t, h);
+}
+template <typename T>
+__device__ __forceinline__ float silu_for(float x) {
+  if constexpr (sizeof(T) == 2) return silu_tanh(x);
+  else return silu_fast(x);
+}
 constexpr int kMaxVecPerThread = 8;   // the vector kernel holds up to 8 x 16 bytes of g a thread
 
 template <typename T>
@@ -62,6 +75,7 @@ struct NormArgs {
   const void* gate; int64_t g_s;
   void* out; int64_t o_s;
   const float* w; int64_t w_s;   // null: gate only
+  int w_vec;                     // w contiguous and 16-byte aligned
   int D, group;                  // channels per row, per norm group
   float eps;
 };
@@ -98,7 +112,7 @@ __global__ void __launch_bounds__(kNormThreads) gated_rmsnorm_vec_kernel(NormArg
       float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < V; ++i) {
-        g[j][i] = yv[i] * silu_fast(gv[i]);
+        g[j][i] = yv[i] * silu_for<T>(gv[i]);
         ss = fmaf(g[j][i], g[j][i], ss);
       }
       if (a.w) sh[v] = ss;
@@ -125,8 +139,16 @@ __global__ void __launch_bounds__(kNormThreads) gated_rmsnorm_vec_kernel(NormArg
     if (v < nvec) {
       if (a.w) {
         const float r = scale[(v * V) / a.group];
+        if (a.w_vec) {   // contiguous, 16-byte aligned weights
 #pragma unroll
-        for (int i = 0; i < V; ++i) g[j][i] *= r * a.w[(int64_t)(v * V + i) * a.w_s];
+          for (int i = 0; i < V; i += 4) {
+            const float4 w4 = __ldg(reinterpret_cast<const float4*>(a.w + v * V + i));
+            g[j][i] *= r * w4.x; g[j][i + 1] *= r * w4.y; g[j][i + 2] *= r * w4.z; g[j][i + 3] *= r * w4.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < V; ++i) g[j][i] *= r * a.w[(int64_t)(v * V + i) * a.w_s];
+        }
       }
       Vec<T>::store(out + (int64_t)v * V, g[j]);
     }
@@ -143,7 +165,7 @@ __global__ void __launch_bounds__(kNormThreads) gated_rmsnorm_scalar_kernel(Norm
   const T* gt = static_cast<const T*>(a.gate) + row * a.g_s;
   T* out = static_cast<T*>(a.out) + row * a.o_s;
   const int ngroups = a.D / a.group;
-  auto gated = [&](int c) { return to_f32(y[c]) * silu_fast(to_f32(gt[c])); };
+  auto gated = [&](int c) { return to_f32(y[c]) * silu_for<T>(to_f32(gt[c])); };
   if (a.w) {
     for (int i = threadIdx.x; i < ngroups; i += kNormThreads) gs[i] = 0.f;
     __syncthreads();
@@ -198,6 +220,7 @@ int gated_rmsnorm(const alloy_tensor_t* y, const alloy_tensor_t* gate, const all
   a.out = out->data; a.o_s = out->stride[0];
   a.w = w ? static_cast<const float*>(w->data) : nullptr;
   a.w_s = w ? w->stride[0] : 0;
+  a.w_vec = a.w && a.w_s == 1 && (reinterpret_cast<uintptr_t>(a.w) & 15) == 0;
   a.D = (int)y->shape[1];
   a.group = group;
   a.eps = eps;
