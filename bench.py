@@ -48,6 +48,9 @@ WORKLOADS = {
     # the gate and inner RMS norm after the scan (d_inner = H * P), full-width norm
     "gated_norm": dict(name="nemotron_h_8b_mamba2_gated_rmsnorm", B=4, L=8192, H=128, P=64,
                        N=128, G=8, K=4, Q=256),
+    # one whole Mamba layer (projections, cached step, gate + norm) decoding at batch 1
+    "decode_block": dict(name="nemotron_h_8b_mamba2_layer_decode_b1", B=1, L=64, H=128, P=64,
+                         N=128, G=8, K=4, Q=256),
 }
 
 L2_BYTES = 126 * 1024 * 1024
@@ -472,6 +475,88 @@ def run_gated_norm(args, w):
         dist.destroy_process_group()
 
 
+def run_decode_block(args, w):
+    """One Nemotron-H Mamba layer (d_model 4096, in-projection, cached step,
+    gate + inner norm, out-projection; random bf16 weights) decoding B
+    sequences after an L-token prefill: tokens/s with the step replayed from a
+    CUDA graph (`MambaDecodeGraph`), and eagerly.  Batch 1 is weight-bound: the
+    projections' 219 MB of weights are read once per token."""
+    import torch
+    from alloy_b200 import _lib
+    from alloy_b200.decode_graph import MambaDecodeGraph
+    from alloy_b200.mamba_block import MambaBlock, MambaCache
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    H, P, N, G, K = w["H"], w["P"], w["N"], w["G"], w["K"]
+    B = w["B"]
+    torch.manual_seed(5 + rank)
+    blk = MambaBlock(d_model=H * P // 2, d_state=N, d_conv=K, expand=2, headdim=P, n_groups=G,
+                     use_D=True, use_inner_norm=True, combined_proj=True, device=dev,
+                     dtype=torch.bfloat16)
+    with torch.no_grad():
+        blk.A_log.uniform_(0.0, math.log(16.0))
+        blk.dt_bias.uniform_(-6.0, -2.0)
+        blk.D.normal_()
+        blk.conv_weight.normal_(0, 0.5)
+    T = 64
+    xs = torch.randn((T, B, 1, blk.d_model), device=dev, dtype=torch.bfloat16)
+    cache = MambaCache()
+    with torch.no_grad():
+        blk(torch.randn((B, w["L"], blk.d_model), device=dev, dtype=torch.bfloat16), cache=cache)
+    graph = MambaDecodeGraph(blk, cache, batch=B)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        barrier(world)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0 = _lib.load().alloy_kernel_launch_count()
+        ev0.record(stream)
+        for i in range(args.steps):
+            fn(i)
+        ev1.record(stream)
+        n = _lib.load().alloy_kernel_launch_count() - n0
+        torch.cuda.synchronize()
+        barrier(world)
+        return dist_max(ev0.elapsed_time(ev1) / args.steps, world), n
+
+    with torch.no_grad():
+        ms_eager, n_eager = timed(lambda i: blk(xs[i % T], cache=cache))
+        clocks = ClockSampler(dev.index)
+        clocks.start()
+        h0 = time.perf_counter()
+        ms_graph, _ = timed(lambda i: graph.step(xs[i % T]))
+        h1 = time.perf_counter()
+        clocks.stop()
+    weights = sum(p.numel() * p.element_size() for p in (blk.in_proj.weight, blk.out_proj.weight))
+    alg = weights + 2 * cache.ssm_state.numel() * 4 + 2 * cache.conv_state.numel() * 2
+    peak, peak_kind = measured_peaks()
+    gbs = alg / (ms_graph * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Mamba-2 layer decode tokens/s (Nemotron-H layer, batch 1, CUDA graph)",
+            "value": B * world / (ms_graph * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_graph,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random weights)",
+            "config": {"workload": w["name"], "batch": B, "prefill": w["L"], "d_model": blk.d_model,
+                       "n_heads": H, "head_dim": P, "d_state": N, "n_groups": G,
+                       "weights_mb": round(weights / 1e6, 1)},
+            "eager": {"value": B * world / (ms_eager * 1e-3), "unit": "tokens/s",
+                      "ms_per_step": ms_eager, "alloy_launches_per_step": n_eager / args.steps},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / peak, "traffic": None, "peak_source": f"{peak_kind} hbm_gbs",
+                         "note": "bytes per step = projection weights + state and conv cache read and written"},
+            "gpu_launches": "graph replays: " + str(args.steps),
+            "clocks": clocks.summary(h0, h1)}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def run_decode(args, w):
     """Decode-step workload: B sequences advance one token per step through
     the conv cache and the fp32 SSM cache ([B, H, P, N] storage), 64
@@ -659,6 +744,8 @@ def main():
         run_decode(args, w)
     elif args.workload == "gated_norm":
         run_gated_norm(args, w)
+    elif args.workload == "decode_block":
+        run_decode_block(args, w)
     else:
         run_ours(args, w)
 

@@ -323,6 +323,35 @@ def test_block_autoregressive_matches_parallel(combined, dtype):
     assert cache.conv_state.shape == (2, 3, conv_dim)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_decode_graph_matches_eager(dtype):
+    """Decode steps replayed from one captured CUDA graph (in-projection,
+    in-place cache step, gate + inner norm, out-projection) equal the same
+    steps run eagerly, outputs and cache."""
+    from alloy_b200.decode_graph import MambaDecodeGraph
+    torch.manual_seed(7)
+    blk = MambaBlock(d_model=256, d_state=64, d_conv=4, expand=2, headdim=64, n_groups=2,
+                     use_D=True, use_inner_norm=True, combined_proj=True, chunk_size=64,
+                     device=DEV, dtype=dtype)
+    with torch.no_grad():
+        blk.A_log.uniform_(0, 2)
+        blk.dt_bias.uniform_(-3, -1)
+        blk.D.normal_()
+        blk.conv_weight.normal_(0, 0.5)
+        x = torch.randn(3, 20, 256, device=DEV, dtype=dtype)
+        eager = MambaCache()
+        blk(x[:, :12], cache=eager)
+        graphed = MambaCache(ssm_state=eager.ssm_state.clone(), conv_state=eager.conv_state.clone())
+        g = MambaDecodeGraph(blk, graphed, batch=3)
+        assert torch.equal(graphed.ssm_state, eager.ssm_state)   # capture leaves the cache as it was
+        for t in range(12, 20):
+            ye = blk(x[:, t:t + 1], cache=eager)
+            yg = g.step(x[:, t:t + 1]).clone()
+            torch.testing.assert_close(yg, ye)
+        torch.testing.assert_close(graphed.ssm_state, eager.ssm_state)
+        torch.testing.assert_close(graphed.conv_state, eager.conv_state)
+
+
 # ------------------------------------------------------- tensor-core path checks
 def test_tensor_core_path_is_selected_for_bf16_layer_shapes():
     from alloy_b200 import _lib
