@@ -1,8 +1,10 @@
 """Functional API of the Mamba-2 mixer hot path over torch CUDA tensors.
 
 Each function validates devices on the host and calls one liballoy_ssd entry
-point on torch's current CUDA stream.  Inputs must already be CUDA tensors:
-there is no CPU path and no fallback.
+point on torch's current CUDA stream.  Inputs must already be CUDA tensors,
+except for ``ssd_combined_streamed``, which copies host activations in and
+its results out around the same kernels; there is no CPU compute path and no
+fallback.
 
 Layouts follow gxcsoccer/alloy (alloy/models/mamba_block.py):
 ``xBC [B, L, H*P + 2*G*N]`` = conv input ``[x | B | C]``; ``dt_raw [B, L, H]``;
@@ -19,7 +21,7 @@ from . import _lib
 
 __all__ = [
     "conv1d_silu", "depthwise_conv1d", "ssd_combined", "selective_scan",
-    "ssd_decode_step", "gated_rmsnorm",
+    "ssd_decode_step", "gated_rmsnorm", "ssd_combined_streamed",
 ]
 
 
@@ -138,6 +140,120 @@ def ssd_combined(xBC, dt_raw, conv_weight, conv_bias, dt_bias, A_log, D, *, n_he
         _lib.call("alloy_ssd_combined", *(_lib.ref(d) for d in descs),
                   ws.data_ptr() if ws is not None else None, ws_bytes, _lib.ref(dims),
                   _lib.stream_handle(dev))
+    return out, ssm_state_out, conv_state_out
+
+
+def ssd_combined_streamed(xBC, dt_raw, conv_weight, conv_bias, dt_bias, A_log, D, *, n_heads,
+                          head_dim, d_state, n_groups, d_conv=4, chunk_size=256, ssm_state=None,
+                          conv_state=None, out=None, ssm_state_out=None, conv_state_out=None,
+                          piece_tokens=2048, slots=3):
+    """``ssd_combined`` for activations that live in host memory.
+
+    For a caller whose activations are host arrays: an MLX caller (unified
+    memory, reached through ``mlx_bridge``'s numpy path), or a service that
+    receives them over the network.  ``xBC`` [B, L, conv_dim] and ``dt_raw``
+    [B, L, H] are pinned CPU tensors; the parameters are CUDA tensors and
+    choose the device; ``ssm_state`` / ``conv_state`` (optional) are CPU
+    tensors in the layouts ``ssd_combined`` takes.  Returns pinned CPU
+    ``(y [B, L, H, P], ssm_state_out [B, H, N, P] fp32, conv_state_out
+    [B, K-1, conv_dim])``, valid when the call returns.
+
+    The sequence of each batch row is cut into pieces of ``piece_tokens``
+    tokens.  Each piece is copied in on one stream, computed on a second and
+    its y copied out on a third, through ``slots`` device buffers, so that the
+    host->device copy of piece i+1, the kernels of piece i and the
+    device->host copy of piece i-1 overlap; a row's states carry from piece
+    to piece in device memory, in fp32 as inside one call.  Pieces start on
+    multiples of ``chunk_size`` tokens when ``piece_tokens`` is one.
+    """
+    for name, t in (("xBC", xBC), ("dt_raw", dt_raw)):
+        if not isinstance(t, torch.Tensor) or t.is_cuda:
+            raise ValueError(f"{name}: expected a CPU tensor (use ssd_combined for CUDA tensors)")
+        if not t.is_pinned():
+            raise ValueError(f"{name}: must be in pinned host memory (torch.Tensor.pin_memory())")
+        if not t.is_contiguous():
+            raise ValueError(f"{name}: must be contiguous")
+    dev = _same_device(("conv_weight", conv_weight), ("conv_bias", conv_bias),
+                       ("dt_bias", dt_bias), ("A_log", A_log), ("D", D))
+    if piece_tokens < 1 or slots < 2:
+        raise ValueError("piece_tokens must be >= 1 and slots >= 2")
+    Bsz, L, Cdim = xBC.shape
+    H, P, N, K = n_heads, head_dim, d_state, d_conv
+    if out is None:
+        out = torch.empty((Bsz, L, H, P), dtype=xBC.dtype, pin_memory=True)
+    if ssm_state_out is None:
+        ssm_state_out = torch.empty((Bsz, H, N, P), dtype=torch.float32, pin_memory=True)
+    if conv_state_out is None:
+        conv_state_out = torch.empty((Bsz, K - 1, Cdim), dtype=xBC.dtype, pin_memory=True)
+    kw = dict(n_heads=H, head_dim=P, d_state=N, n_groups=n_groups, d_conv=K,
+              chunk_size=chunk_size)
+    pieces = [(b, l0, min(L, l0 + piece_tokens)) for b in range(Bsz)
+              for l0 in range(0, L, piece_tokens)]
+    T = min(piece_tokens, L)
+    main = torch.cuda.current_stream(dev)
+    s_in, s_cmp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+    with torch.cuda.device(dev):
+        # every device buffer exists before the side streams start
+        d_x = [torch.empty((1, T, Cdim), dtype=xBC.dtype, device=dev) for _ in range(slots)]
+        d_dt = [torch.empty((1, T, H), dtype=dt_raw.dtype, device=dev) for _ in range(slots)]
+        d_y = [torch.empty((1, T, H, P), dtype=xBC.dtype, device=dev) for _ in range(slots)]
+        # the carried states, one set per row parity (a row's final states are
+        # copied out while the next row runs on the other set)
+        d_h = [torch.empty((1, H, N, P), dtype=torch.float32, device=dev) for _ in range(2)]
+        d_cs = [torch.empty((1, K - 1, Cdim), dtype=xBC.dtype, device=dev) for _ in range(2)]
+        states_out = [None, None]
+        d_h0 = d_cs0 = None
+        if ssm_state is not None:
+            d_h0 = ssm_state.to(dev, torch.float32)
+        if conv_state is not None:
+            d_cs0 = conv_state.to(dev, xBC.dtype)
+        ev = lambda: torch.cuda.Event()
+        in_ready = [ev() for _ in range(slots)]
+        consumed = [ev() for _ in range(slots)]
+        copied_out = [ev() for _ in range(slots)]
+        used = [False] * slots
+        start = ev()
+        start.record(main)
+        for s in (s_in, s_cmp, s_out):
+            s.wait_event(start)
+        for i, (b, l0, l1) in enumerate(pieces):
+            k, n = i % slots, l1 - l0
+            # copy in: the slot's inputs were read by the piece that used it last
+            if used[k]:
+                s_in.wait_event(consumed[k])
+            with torch.cuda.stream(s_in):
+                d_x[k][:, :n].copy_(xBC[b:b + 1, l0:l1], non_blocking=True)
+                d_dt[k][:, :n].copy_(dt_raw[b:b + 1, l0:l1], non_blocking=True)
+                in_ready[k].record(s_in)
+            # compute: inputs in, and the slot's previous y copied out
+            s_cmp.wait_event(in_ready[k])
+            if used[k]:
+                s_cmp.wait_event(copied_out[k])
+            st = b & 1
+            first = l0 == 0
+            if first and states_out[st] is not None:
+                # this state set's previous row has been copied out
+                s_cmp.wait_event(states_out[st])
+            with torch.cuda.stream(s_cmp):
+                h_in = (d_h0[b:b + 1] if d_h0 is not None else None) if first else d_h[st]
+                cs_in = (d_cs0[b:b + 1] if d_cs0 is not None else None) if first else d_cs[st]
+                ssd_combined(d_x[k][:, :n], d_dt[k][:, :n], conv_weight, conv_bias, dt_bias,
+                             A_log, D, ssm_state=h_in, conv_state=cs_in, out=d_y[k][:, :n],
+                             ssm_state_out=d_h[st], conv_state_out=d_cs[st], **kw)
+                consumed[k].record(s_cmp)
+            # copy out (the row's final states after its last piece)
+            s_out.wait_event(consumed[k])
+            with torch.cuda.stream(s_out):
+                out[b:b + 1, l0:l1].copy_(d_y[k][:, :n], non_blocking=True)
+                copied_out[k].record(s_out)
+                if l1 == L:
+                    ssm_state_out[b:b + 1].copy_(d_h[st], non_blocking=True)
+                    conv_state_out[b:b + 1].copy_(d_cs[st], non_blocking=True)
+                    states_out[st] = ev()
+                    states_out[st].record(s_out)
+            used[k] = True
+        s_out.synchronize()
+        main.wait_stream(s_out)
     return out, ssm_state_out, conv_state_out
 
 

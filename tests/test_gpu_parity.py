@@ -174,6 +174,45 @@ def test_combined_vs_fp64_recurrence(cfg, dtype):
     assert_close(np_(h), h64, dtype == torch.bfloat16)
 
 
+@pytest.mark.parametrize("cfg,piece", [
+    (dict(B=2, L=700, H=8, P=64, N=128, G=2), 256),     # ragged last piece, tensor cores
+    (dict(B=3, L=300, H=4, P=32, N=16, G=1), 128),      # CUDA-core path, odd row count
+    (dict(B=1, L=1000, H=8, P=64, N=64, G=1), 4096),    # one piece per row
+])
+@pytest.mark.parametrize("with_state", [False, True])
+def test_streamed_prefill_from_host_memory(cfg, piece, with_state):
+    inp = oracle.make_inputs(**cfg, dtype="bf16", seed=17, with_state=True)
+    H, P, N, G = cfg["H"], cfg["P"], cfg["N"], cfg["G"]
+    ssm0 = inp["ssm_state"] if with_state else None
+    cs0 = inp["conv_state"] if with_state else None
+    y64, h64, cs64 = oracle.mixer_core_fp64(
+        inp["xBC"], inp["dt_raw"], inp["conv_weight"], inp["conv_bias"], inp["dt_bias"],
+        inp["A_log"], inp["D"], n_heads=H, headdim=P, d_state=N, n_groups=G,
+        ssm_state=ssm0, conv_state=cs0)
+
+    def host(a, dt=torch.float32):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(dt).pin_memory()
+
+    params = [cu(inp[k]) for k in ("conv_weight", "conv_bias", "dt_bias", "A_log", "D")]
+    kw = dict(n_heads=H, head_dim=P, d_state=N, n_groups=G)
+    y, h, cs = mixer.ssd_combined_streamed(
+        host(inp["xBC"], torch.bfloat16), host(inp["dt_raw"], torch.bfloat16), *params,
+        ssm_state=None if ssm0 is None else host(ssm0),
+        conv_state=None if cs0 is None else host(cs0, torch.bfloat16), piece_tokens=piece, **kw)
+    assert not y.is_cuda and y.shape == (cfg["B"], cfg["L"], H, P) and y.dtype == torch.bfloat16
+    assert_close(y.float().numpy(), y64, True)
+    assert_close(h.numpy(), h64, True)
+    assert np.array_equal(cs.float().numpy(), cs64.astype(np.float32))
+    # the same layer through the device API
+    yd, hd, csd = mixer.ssd_combined(
+        cu(inp["xBC"], torch.bfloat16), cu(inp["dt_raw"], torch.bfloat16), *params,
+        ssm_state=None if ssm0 is None else cu(ssm0),
+        conv_state=None if cs0 is None else cu(cs0, torch.bfloat16), **kw)
+    torch.cuda.synchronize()
+    assert_close(y.float().numpy(), np_(yd), True)
+    assert torch.equal(cs, csd.cpu())
+
+
 # ------------------------------------------------------------ pre-discretised scan
 def test_scan_chunk_golden():
     g = load_golden("scan_chunk")

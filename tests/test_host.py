@@ -108,3 +108,15 @@ def test_patch_mamba_block_swaps_and_restores_methods():
     for name, fn in saved.items():
         setattr(FakeBlock, name, fn)
     assert FakeBlock()._selective_scan() == "ref"
+
+
+def test_streamed_prefill_rejects_unpinned_or_device_activations():
+    from alloy_b200 import mixer
+    x = torch.zeros((1, 8, 288), dtype=torch.bfloat16)
+    dt = torch.zeros((1, 8, 8), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="pinned"):
+        mixer.ssd_combined_streamed(x, dt, None, None, None, None, None, n_heads=8,
+                                    head_dim=32, d_state=16, n_groups=1)
+    with pytest.raises(ValueError, match="CPU tensor"):
+        mixer.ssd_combined_streamed(None, dt, None, None, None, None, None, n_heads=8,
+                                    head_dim=32, d_state=16, n_groups=1)
