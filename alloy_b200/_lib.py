@@ -48,6 +48,8 @@ EXPORTS = (
     "alloy_ssd_combined_noalloc",
     "alloy_kernel_launch_count",
     "alloy_gated_rmsnorm",
+    "alloy_conv1d_silu_backward",
+    "alloy_conv1d_silu_backward_workspace_size",
 )
 
 
@@ -115,6 +117,9 @@ def load():
         vp = ctypes.c_void_p
         lib.alloy_conv1d_silu.argtypes = [P, P, P, P, vp]
         lib.alloy_depthwise_conv1d.argtypes = [P, P, P, P, vp]
+        lib.alloy_conv1d_silu_backward.argtypes = [P] * 7 + [vp, ctypes.c_size_t, vp]
+        lib.alloy_conv1d_silu_backward_workspace_size.argtypes = [ctypes.c_int64] * 4
+        lib.alloy_conv1d_silu_backward_workspace_size.restype = ctypes.c_size_t
         lib.alloy_ssd_combined.argtypes = [P] * 12 + [vp, ctypes.c_size_t, D, vp]
         lib.alloy_ssd_combined_workspace_size.argtypes = [ctypes.c_int64, ctypes.c_int64,
                                                           ctypes.c_int32, D]
@@ -130,7 +135,8 @@ def load():
         lib.alloy_ssd_combined_noalloc.argtypes = [P] * 12 + [D, vp]
         lib.alloy_selective_scan.argtypes = [P] * 8 + [vp]
         lib.alloy_ssd_decode_step.argtypes = [P] * 10 + [D, vp]
-        for name in ("alloy_conv1d_silu", "alloy_depthwise_conv1d", "alloy_ssd_combined",
+        for name in ("alloy_conv1d_silu", "alloy_depthwise_conv1d", "alloy_conv1d_silu_backward",
+                     "alloy_ssd_combined",
                      "alloy_selective_scan", "alloy_ssd_decode_step", "alloy_check_device_status",
                      "alloy_ssd_combined_noalloc"):
             getattr(lib, name).restype = ctypes.c_int
@@ -169,10 +175,9 @@ def desc(t: torch.Tensor | None, name: str = "tensor") -> Tensor:
         raise TypeError(f"{name}: dtype {t.dtype} is not supported (float32 or bfloat16)")
     if t.dim() > MAX_DIMS:
         raise ValueError(f"{name}: at most {MAX_DIMS} dims")
-    d.data = t.data_ptr() if t.numel() > 0 else 0
-    if d.data == 0 and t.numel() == 0:
-        # empty tensors still need a non-null pointer to be "present"
-        d.data = 16
+    # empty tensors still need a non-null pointer to be "present" (nothing
+    # dereferences it: every extent that indexes it is zero)
+    d.data = t.data_ptr() if t.numel() > 0 else 16
     d.dtype = _DTYPES[t.dtype]
     d.ndim = t.dim()
     for i, (s, st) in enumerate(zip(t.shape, t.stride())):

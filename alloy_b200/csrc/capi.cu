@@ -144,6 +144,48 @@ int alloy_depthwise_conv1d(const alloy_tensor_t* x_padded, const alloy_tensor_t*
   return conv_entry(x_padded, weight, bias, out, false, stream);
 }
 
+size_t alloy_conv1d_silu_backward_workspace_size(int64_t batch, int64_t padded_len, int64_t channels,
+                                                 int64_t d_conv) {
+  if (batch < 0 || channels < 0 || d_conv < 1 || d_conv > 8 || padded_len < d_conv - 1) return 0;
+  return conv1d_silu_backward_workspace(batch, padded_len, channels, d_conv);
+}
+
+int alloy_conv1d_silu_backward(const alloy_tensor_t* x_padded, const alloy_tensor_t* weight,
+                               const alloy_tensor_t* bias, const alloy_tensor_t* dy,
+                               alloy_tensor_t* dx_padded, alloy_tensor_t* dweight,
+                               alloy_tensor_t* dbias, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  last_error().clear();
+  ALLOY_TRY(check_tensor(x_padded, "x_padded", 3, nullptr, kAnyFloat));
+  ALLOY_TRY(check_tensor(weight, "weight", 2, nullptr, kAnyFloat));
+  const int64_t B = x_padded->shape[0], Lp = x_padded->shape[1], C = x_padded->shape[2];
+  const int64_t K = weight->shape[1];
+  if (weight->shape[0] != C)
+    return fail(ALLOY_ERR_INVALID_ARG, "weight: dim 0 is %lld, expected C = %lld",
+                (long long)weight->shape[0], (long long)C);
+  if (K < 1 || K > 8) return fail(ALLOY_ERR_UNSUPPORTED, "weight: K must be in [1, 8]");
+  if (Lp < K - 1) return fail(ALLOY_ERR_INVALID_ARG, "x_padded: fewer than K-1 rows");
+  ALLOY_TRY(check_vec(bias, "bias", C, kAnyFloat, true));
+  const unsigned act = 1u << x_padded->dtype;
+  const int64_t yshape[3] = {B, Lp - K + 1, C};
+  ALLOY_TRY(check_tensor(dy, "dy", 3, yshape, act));
+  ALLOY_TRY(check_tensor(dx_padded, "dx_padded", 3, x_padded->shape, act));
+  const int64_t wshape[2] = {C, K};
+  ALLOY_TRY(check_tensor(dweight, "dweight", 2, wshape, kAnyFloat));
+  ALLOY_TRY(check_vec(dbias, "dbias", C, kAnyFloat, true));
+  if (B > 65535) return fail(ALLOY_ERR_UNSUPPORTED, "x_padded: batch above 65535");
+  if (B * Lp * C >= (int64_t)1 << 40) return fail(ALLOY_ERR_UNSUPPORTED, "x_padded: too large");
+  const size_t need = conv1d_silu_backward_workspace(B, Lp, C, K);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return fail(ALLOY_ERR_INVALID_ARG, "conv1d_silu_backward: workspace of %zu bytes required, got %zu",
+                need, workspace_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) & 3)
+    return fail(ALLOY_ERR_ALIGNMENT, "conv1d_silu_backward: workspace must be 4-byte aligned");
+  ALLOY_TRY(current_device_checked(nullptr));
+  return conv1d_silu_backward(x_padded, weight, bias, dy, dx_padded, dweight, dbias, workspace, (int)B,
+                              (int)(Lp - K + 1), (int)C, (int)K, as_stream(stream));
+}
+
 int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t* dt_raw,
                        const alloy_tensor_t* conv_w, const alloy_tensor_t* conv_b,
                        const alloy_tensor_t* dt_bias, const alloy_tensor_t* A_log,

@@ -10,6 +10,14 @@ namespace alloy {
 int conv1d_silu(const alloy_tensor_t* x_padded, const alloy_tensor_t* w,
                 const alloy_tensor_t* bias, alloy_tensor_t* out, bool silu, cudaStream_t s);
 
+// conv_bwd.cu: VJP of conv1d + SiLU (dx_padded, dweight, dbias from dy);
+// the workspace holds per-CTA partial sums of dweight / dbias
+size_t conv1d_silu_backward_workspace(int64_t B, int64_t Lp, int64_t C, int64_t K);
+int conv1d_silu_backward(const alloy_tensor_t* x_padded, const alloy_tensor_t* w,
+                         const alloy_tensor_t* bias, const alloy_tensor_t* dy, alloy_tensor_t* dx,
+                         alloy_tensor_t* dw, alloy_tensor_t* db, void* workspace, int B, int L, int C,
+                         int K, cudaStream_t s);
+
 // Flattened view of one SSD call, shared by the SSD kernels.  Strides are in
 // elements.  mode 0: raw xBC (conv + discretisation fused); mode 1:
 // pre-discretised inputs (x, log decay, B, C).

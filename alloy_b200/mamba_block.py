@@ -32,6 +32,13 @@ from . import mixer
 __all__ = ["MambaCache", "MambaBlock"]
 
 
+def _metal_conv1d_silu(x_padded, weight, bias, L):
+    """conv1d + SiLU that autograd differentiates with the library's backward
+    kernel, as alloy's ``@mx.custom_function _metal_conv1d_silu`` with its
+    ``.vjp`` (alloy/models/mamba_block.py:19-47)."""
+    return mixer.Conv1dSilu.apply(x_padded, weight, bias, L)
+
+
 @dataclass
 class MambaCache:
     """Decode cache of one Mamba layer (alloy/models/cache.py:13-25).
@@ -139,7 +146,11 @@ class MambaBlock(torch.nn.Module):
         xz = self.in_proj(x)
         x_branch, z = xz[..., :self.d_inner], xz[..., self.d_inner:]
         x_padded = self._conv_input_padded(x_branch, cache)
-        x_conv = mixer.conv1d_silu(x_padded, self.conv_weight, self.conv_bias, L)
+        # (:399-404: the differentiable kernel without a cache, the plain one with)
+        if cache is None:
+            x_conv = _metal_conv1d_silu(x_padded, self.conv_weight, self.conv_bias, L)
+        else:
+            x_conv = mixer.conv1d_silu(x_padded, self.conv_weight, self.conv_bias, L)
         ssm = self.x_proj(x_conv).reshape(Bsz, L, self.n_heads, 2 * self.d_state + 1)
         B_param = ssm[..., :self.d_state]
         C_param = ssm[..., self.d_state:2 * self.d_state]

@@ -21,7 +21,8 @@ from . import _lib
 
 __all__ = [
     "conv1d_silu", "depthwise_conv1d", "ssd_combined", "selective_scan",
-    "ssd_decode_step", "gated_rmsnorm", "ssd_combined_streamed",
+    "ssd_decode_step", "gated_rmsnorm", "ssd_combined_streamed", "conv1d_silu_backward",
+    "Conv1dSilu",
 ]
 
 
@@ -90,6 +91,59 @@ def depthwise_conv1d(x_padded, weight, bias=None, L=None, out=None):
     """Causal depthwise conv without activation, ``MambaBlock._depthwise_conv1d``
     (alloy/models/mamba_block.py:144-158)."""
     return _conv("alloy_depthwise_conv1d", x_padded, weight, bias, L, out)
+
+
+def conv1d_silu_backward(x_padded, weight, bias, dy, L=None, dx_out=None):
+    """Backward of ``conv1d_silu``: ``(dx_padded, dweight, dbias)`` from the
+    output cotangent ``dy [B, L, C]``, as ``_metal_conv1d_silu_vjp``
+    (alloy/models/mamba_block.py:25-47) computes them.  ``dx_padded`` has
+    x_padded's shape (rows past L+K-1 get zero); ``dweight`` / ``dbias`` have
+    the dtypes of weight / bias (``dbias`` is None without a bias).  Summed in
+    fp32 in a fixed order: repeated calls give identical results.
+    """
+    dev = _same_device(("x_padded", x_padded), ("weight", weight), ("bias", bias), ("dy", dy),
+                       ("dx_out", dx_out))
+    Bsz, Lp, C = x_padded.shape
+    K = weight.shape[1]
+    if L is None:
+        L = Lp - K + 1
+    if dy.shape != (Bsz, L, C):
+        raise ValueError(f"dy shape {tuple(dy.shape)} != {(Bsz, L, C)}")
+    if dy.dtype != x_padded.dtype:
+        dy = dy.to(x_padded.dtype)
+    if dx_out is None:
+        dx_out = (torch.empty_like(x_padded) if L + K - 1 == Lp
+                  else torch.zeros_like(x_padded))
+    x_used, dx_used = x_padded[:, :L + K - 1], dx_out[:, :L + K - 1]
+    dweight = torch.empty(weight.shape, dtype=weight.dtype, device=dev)
+    dbias = None if bias is None else torch.empty(bias.shape, dtype=bias.dtype, device=dev)
+    ws_bytes = _lib.load().alloy_conv1d_silu_backward_workspace_size(Bsz, L + K - 1, C, K)
+    ws = _workspace(dev, ws_bytes)
+    descs = [_lib.desc(t, n) for t, n in ((x_used, "x_padded"), (weight, "weight"), (bias, "bias"),
+                                          (dy, "dy"), (dx_used, "dx_padded"),
+                                          (dweight, "dweight"), (dbias, "dbias"))]
+    with torch.cuda.device(dev):
+        _lib.call("alloy_conv1d_silu_backward", *(_lib.ref(d) for d in descs),
+                  ws.data_ptr() if ws is not None else None, ws_bytes, _lib.stream_handle(dev))
+    return dx_out, dweight, dbias
+
+
+class Conv1dSilu(torch.autograd.Function):
+    """``conv1d_silu`` with its VJP, the counterpart of alloy's
+    ``@mx.custom_function _metal_conv1d_silu`` and its ``.vjp``
+    (alloy/models/mamba_block.py:19-47)."""
+
+    @staticmethod
+    def forward(ctx, x_padded, weight, bias, L):
+        ctx.save_for_backward(x_padded, weight, bias)
+        ctx.L = L
+        return conv1d_silu(x_padded, weight, bias, L)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x_padded, weight, bias = ctx.saved_tensors
+        dx, dw, db = conv1d_silu_backward(x_padded, weight, bias, dy.contiguous(), ctx.L)
+        return dx, dw, db, None
 
 
 def ssd_combined(xBC, dt_raw, conv_weight, conv_bias, dt_bias, A_log, D, *, n_heads,

@@ -49,6 +49,9 @@ WORKLOADS = {
     # the gate and inner RMS norm after the scan (d_inner = H * P), full-width norm
     "gated_norm": dict(name="nemotron_h_8b_mamba2_gated_rmsnorm", B=4, L=8192, H=128, P=64,
                        N=128, G=8, K=4, Q=256),
+    # backward of conv1d + SiLU over the layer's xBC (training: the reference's custom VJP)
+    "conv_bwd": dict(name="nemotron_h_8b_mamba2_conv1d_silu_backward", B=4, L=8192, H=128, P=64,
+                     N=128, G=8, K=4, Q=256),
     # one whole Mamba layer (projections, cached step, gate + norm) decoding at batch 1
     "decode_block": dict(name="nemotron_h_8b_mamba2_layer_decode_b1", B=1, L=64, H=128, P=64,
                          N=128, G=8, K=4, Q=256),
@@ -477,6 +480,76 @@ def run_gated_norm(args, w):
         dist.destroy_process_group()
 
 
+def run_conv_bwd(args, w):
+    """Backward of conv1d + SiLU over the layer's xBC (conv_dim = H P + 2 G N
+    channels): dx_padded, dweight, dbias from dy.  Batch rows split over the
+    GPUs; reported as achieved HBM GB/s (x_padded and dy read once, dx_padded
+    written once).  Inputs rotate through enough sets to exceed 3x L2."""
+    import torch
+    from alloy_b200 import _lib, mixer
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    B, L, K = w["B"], w["L"], w["K"]
+    C = w["H"] * w["P"] + 2 * w["G"] * w["N"]
+    if B % world:
+        raise SystemExit("batch rows do not split over the GPUs")
+    Bl = B // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(21 + rank)
+    set_bytes = Bl * (2 * (L + K - 1) + L) * C * 2
+    rot = max(1, math.ceil(3 * L2_BYTES / set_bytes))
+    sets = [(torch.randn((Bl, L + K - 1, C), generator=gen, device=dev).to(torch.bfloat16),
+             torch.randn((Bl, L, C), generator=gen, device=dev).to(torch.bfloat16),
+             torch.empty((Bl, L + K - 1, C), dtype=torch.bfloat16, device=dev)) for _ in range(rot)]
+    weight = torch.randn((C, K), generator=gen, device=dev) * 0.5
+    bias = torch.zeros(C, device=dev)
+
+    def step(i):
+        x, dy, dx = sets[i % rot]
+        mixer.conv1d_silu_backward(x, weight, bias, dy, dx_out=dx)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    h0 = time.perf_counter()
+    launches0 = _lib.load().alloy_kernel_launch_count()
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    launches = _lib.load().alloy_kernel_launch_count() - launches0
+    torch.cuda.synchronize()
+    h1 = time.perf_counter()
+    barrier(world)
+    clocks.stop()
+    ms = dist_max(ev0.elapsed_time(ev1) / args.steps, world)
+    alg = set_bytes + 2 * C * (K + 1) * 4
+    peak, peak_kind = measured_peaks()
+    gbs = alg * world / (ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Mamba-2 conv1d+SiLU backward (dx, dweight, dbias) HBM GB/s",
+            "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": w["name"], "batch": B, "seq_len": L, "channels": C, "d_conv": K,
+                       "l2": f"{rot} rotating input/output sets of {set_bytes / 2**20:.0f} MiB"},
+            "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / world / peak, "traffic": None,
+                         "peak_source": f"{peak_kind} hbm_gbs"},
+            "gpu_launches": launches, "clocks": clocks.summary(h0, h1)}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def run_decode_block(args, w):
     """One Nemotron-H Mamba layer (d_model 4096, in-projection, cached step,
     gate + inner norm, out-projection; random bf16 weights) decoding B
@@ -750,6 +823,8 @@ def main():
         run_gated_norm(args, w)
     elif args.workload == "decode_block":
         run_decode_block(args, w)
+    elif args.workload == "conv_bwd":
+        run_conv_bwd(args, w)
     else:
         run_ours(args, w)
 

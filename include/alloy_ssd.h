@@ -110,6 +110,34 @@ ALLOY_API int alloy_depthwise_conv1d(const alloy_tensor_t* x_padded, const alloy
                                      const alloy_tensor_t* bias, alloy_tensor_t* out, void* stream);
 
 /*
+ * Backward of conv1d + SiLU (the VJP of alloy_conv1d_silu).
+ * Replaces _metal_conv1d_silu_vjp (alloy/models/mamba_block.py:25-47), the
+ * VJP alloy registers for its Metal conv kernel (used by _forward_split
+ * :401 when training).
+ *
+ *   x_padded  [B, L+K-1, C]  F32|BF16 (the forward's input)
+ *   weight    [C, K], bias [C] (data NULL = zero bias), F32|BF16
+ *   dy        [B, L, C]      dtype of x_padded (cotangent of the output)
+ *   dx_padded [B, L+K-1, C]  dtype of x_padded; must not overlap x_padded or dy
+ *   dweight   [C, K]         F32|BF16;  dbias [C] F32|BF16 (data NULL = not wanted)
+ *   pre = bias + sum_k x_padded[t+k] weight[:,k];  sig = sigmoid(pre)
+ *   g = dy * sig * (1 + pre * (1 - sig))
+ *   dx_padded[t'] = sum_k g[t'-k] weight[:,k];  dweight[:,k] = sum_{b,t} g[t] x_padded[t+k];
+ *   dbias = sum_{b,t} g[t]
+ * fp32 arithmetic; dweight / dbias are summed in a fixed order (the same
+ * result on every call).  workspace: device memory of at least
+ * alloy_conv1d_silu_backward_workspace_size(B, L+K-1, C, K) bytes, 4-byte
+ * aligned, holding the per-CTA partial sums of dweight and dbias.
+ */
+ALLOY_API int alloy_conv1d_silu_backward(const alloy_tensor_t* x_padded, const alloy_tensor_t* weight,
+                               const alloy_tensor_t* bias, const alloy_tensor_t* dy,
+                               alloy_tensor_t* dx_padded, alloy_tensor_t* dweight,
+                               alloy_tensor_t* dbias, void* workspace, size_t workspace_bytes,
+                               void* stream);
+ALLOY_API size_t alloy_conv1d_silu_backward_workspace_size(int64_t batch, int64_t padded_len,
+                                                 int64_t channels, int64_t d_conv);
+
+/*
  * Fused Mamba-2 mixer core in combined (Zamba2 / Nemotron-H) mode, prefill of
  * L >= 1 tokens: conv1d+SiLU with the conv-cache prefix, split into x|B|C,
  * discretisation, chunked SSD scan with state carry, D skip.

@@ -22,7 +22,7 @@ import numpy as np
 F32 = np.float32
 
 __all__ = [
-    "softplus", "sigmoid", "silu", "depthwise_conv1d", "conv1d_silu",
+    "softplus", "sigmoid", "silu", "depthwise_conv1d", "conv1d_silu", "conv1d_silu_vjp",
     "pad_conv_input", "discretize", "scan_chunk", "selective_scan",
     "selective_scan_sequential", "mixer_core", "mixer_core_fp64",
     "decode_step_fp64", "gated_rmsnorm", "make_inputs", "bf16_round", "rel_l2",
@@ -68,6 +68,31 @@ def depthwise_conv1d(x_padded, weight, bias, L):
 def conv1d_silu(x_padded, weight, bias, L):
     """Fused conv1d + SiLU, mamba_kernels.py:17-50 (K1) == mamba_block.py:454-455."""
     return silu(depthwise_conv1d(x_padded, weight, bias, L))
+
+
+def conv1d_silu_vjp(x_padded, weight, bias, L, dy):
+    """Backward of conv1d + SiLU, the VJP alloy attaches to its Metal kernel
+    (``_metal_conv1d_silu_vjp``, mamba_block.py:25-47): the pre-activation is
+    recomputed (:32-35), ``dsilu = sig (1 + pre (1 - sig))`` (:36-37),
+    ``dconv = dy dsilu`` (:38), then per tap k ``dx_padded[k:k+L] += dconv w_k``
+    and ``dweight[:, k] = sum(dconv x_padded[k:k+L])`` over batch and time
+    (:39-45), ``dbias = sum(dconv)`` (:46).
+
+    Returns (dx_padded [B, L+K-1, C], dweight [C, K], dbias [C]), fp32.
+    """
+    x_padded = np.asarray(x_padded, F32)
+    weight = np.asarray(weight, F32)
+    dy = np.asarray(dy, F32)
+    K = weight.shape[1]
+    pre = depthwise_conv1d(x_padded, weight, np.asarray(bias, F32), L)
+    sig = sigmoid(pre)
+    dconv = dy * (sig * (1 + pre * (1 - sig)))
+    dx = np.zeros_like(x_padded)
+    dw = np.zeros_like(weight)
+    for k in range(K):
+        dx[:, k:k + L, :] += dconv * weight[:, k]
+        dw[:, k] += (dconv * x_padded[:, k:k + L, :]).sum(axis=(0, 1))
+    return dx, dw, dconv.sum(axis=(0, 1))
 
 
 def pad_conv_input(conv_input, K, conv_state=None):

@@ -23,6 +23,7 @@ in the .npz next to the outputs, so the fixtures are self-contained.
 from __future__ import annotations
 
 import importlib.util
+import types
 import os
 import sys
 
@@ -54,6 +55,30 @@ def load_reference(root):
         mods[name] = mod
     assert mods["mamba_block"].USE_METAL_KERNELS is False
     return mods["mamba_block"], mods["cache"]
+
+
+def load_reference_conv_vjp(root):
+    """mamba_block.py loaded with a stand-in for its Metal kernels module, so
+    that its try-block (:17-50) defines ``_metal_conv1d_silu_vjp``; only the
+    VJP body, which uses elementary MLX ops alone, is executed."""
+    mlx_numpy_standin.install()
+    kern = types.ModuleType("alloy.models.mamba_kernels")
+    for fn in ("fused_conv1d_silu", "scan_chunk_metal", "fused_parallel_scan_chunk"):
+        setattr(kern, fn, None)
+    saved = sys.modules.get("alloy.models.mamba_kernels", "absent")
+    sys.modules["alloy.models.mamba_kernels"] = kern
+    try:
+        path = os.path.join(root, "alloy", "models", "mamba_block.py")
+        spec = importlib.util.spec_from_file_location("alloy_ref_mamba_block_vjp", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    finally:
+        if saved == "absent":
+            del sys.modules["alloy.models.mamba_kernels"]
+        else:
+            sys.modules["alloy.models.mamba_kernels"] = saved
+    assert mod.USE_METAL_KERNELS is True
+    return mod
 
 
 class _Proj:
@@ -171,10 +196,29 @@ def case_conv(mb, name, seed=42):
     print(f"{name}: out {out.shape}")
 
 
+def case_conv_vjp(root, name, seed=43):
+    """The reference's own ``_metal_conv1d_silu_vjp`` (mamba_block.py:25-47)
+    on the conv shapes of tests/test_metal_kernels.py:18-35 with a non-zero
+    bias and a random cotangent."""
+    mod = load_reference_conv_vjp(root)
+    rng = np.random.default_rng(seed)
+    B, L, D, K = 2, 128, 256, 4
+    xp = rng.standard_normal((B, L + K - 1, D), dtype=np.float32).view(mlx_numpy_standin.AtArray)
+    w = (rng.standard_normal((D, K)) * 0.5).astype(np.float32).view(mlx_numpy_standin.AtArray)
+    b = (rng.standard_normal(D) * 0.1).astype(np.float32).view(mlx_numpy_standin.AtArray)
+    dy = rng.standard_normal((B, L, D), dtype=np.float32).view(mlx_numpy_standin.AtArray)
+    dx, dw, db, _ = mod._metal_conv1d_silu_vjp((xp, w, b, np.array(L)), dy, None)
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), x_padded=np.asarray(xp), weight=np.asarray(w),
+                        bias=np.asarray(b), dy=np.asarray(dy), dx_padded=np.asarray(dx, np.float32),
+                        dweight=np.asarray(dw, np.float32), dbias=np.asarray(db, np.float32))
+    print(f"{name}: dx {dx.shape}, dweight {dw.shape}")
+
+
 def main():
     root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     mb, cache_mod = load_reference(root)
     case_conv(mb, "conv1d_silu")
+    case_conv_vjp(root, "conv1d_silu_vjp")
     case_scan_chunk(mb, "scan_chunk")
     # the toy fp32 mixer configuration, full size
     case_prefill(mb, cache_mod, "toy_prefill", B=2, L=512, H=8, P=32, N=16, G=1, Q=64)

@@ -149,6 +149,49 @@ def softplus(a):
     return np.logaddexp(a, a.dtype.type(0)).astype(a.dtype, copy=False)
 
 
+class AtArray(np.ndarray):
+    """An ndarray with MLX's functional scatter, ``a.at[idx].add(v)`` (a new
+    array with v added at idx), for the code paths that use it."""
+
+    @property
+    def at(self):
+        return _At(self)
+
+
+class _At:
+    def __init__(self, a):
+        self._a = a
+
+    def __getitem__(self, idx):
+        a = self._a
+
+        class _Idx:
+            @staticmethod
+            def add(v):
+                r = a.copy()
+                r[idx] += v
+                return r
+
+        return _Idx()
+
+
+def custom_function(f):
+    """``mx.custom_function``: calls f; ``.vjp`` registers and returns the VJP."""
+
+    class _Custom:
+        def __init__(self):
+            self.vjp_fn = None
+
+        def __call__(self, *args):
+            return f(*args)
+
+        def vjp(self, g):
+            self.vjp_fn = g
+            return g
+
+    return _Custom()
+
+
 def install():
     """Register this module as ``mlx``, ``mlx.core`` and ``mlx.nn``."""
     me = sys.modules[__name__]

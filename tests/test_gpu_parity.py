@@ -76,6 +76,82 @@ def test_conv1d_silu_sizes(B, L, C, dtype):
     assert_close(np_(out2), oracle.depthwise_conv1d(xp, w, b, L), dtype == torch.bfloat16)
 
 
+def test_conv1d_silu_backward_golden():
+    # the reference's own _metal_conv1d_silu_vjp (mamba_block.py:25-47) on fp32 inputs
+    g = load_golden("conv1d_silu_vjp")
+    dx, dw, db = mixer.conv1d_silu_backward(cu(g["x_padded"]), cu(g["weight"]), cu(g["bias"]),
+                                            cu(g["dy"]))
+    torch.cuda.synchronize()
+    for got, ref in ((dx, "dx_padded"), (dw, "dweight"), (db, "dbias")):
+        assert_close(np_(got), g[ref], False)
+
+
+@pytest.mark.parametrize("B,L,C,K,dtype", [
+    (4, 2048, 1024, 4, torch.bfloat16), (3, 77, 4224, 4, torch.bfloat16),
+    (2, 600, 256, 4, torch.float32), (2, 5, 100, 4, torch.bfloat16),   # 4 does not divide C
+    (1, 1, 24, 4, torch.float32), (2, 300, 64, 2, torch.float32), (1, 700, 128, 3, torch.bfloat16),
+    (2, 0, 32, 4, torch.float32)])
+def test_conv1d_silu_backward_vs_oracle(B, L, C, K, dtype):
+    rng = np.random.default_rng(B * 1000 + L + K)
+    xp = rng.standard_normal((B, L + K - 1, C), dtype=np.float32)
+    dy = rng.standard_normal((B, L, C), dtype=np.float32)
+    if dtype == torch.bfloat16:
+        xp, dy = oracle.bf16_round(xp), oracle.bf16_round(dy)
+    w = (rng.standard_normal((C, K)) * 0.5).astype(np.float32)
+    b = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    ref = oracle.conv1d_silu_vjp(xp, w, b, L, dy)
+    got = mixer.conv1d_silu_backward(cu(xp, dtype), cu(w), cu(b), cu(dy, dtype))
+    torch.cuda.synchronize()
+    assert got[0].dtype == dtype and got[0].shape == xp.shape
+    for gt, rf in zip(got, ref):
+        if np.abs(rf).max() == 0:
+            assert np.abs(np_(gt)).max() == 0
+        else:
+            assert_close(np_(gt), rf, dtype == torch.bfloat16)
+
+
+def test_conv1d_silu_backward_strided_deterministic_and_long_input():
+    rng = np.random.default_rng(5)
+    B, L, C = 2, 200, 512
+    xp = rng.standard_normal((B, L + 3 + 10, C), dtype=np.float32)   # 10 rows past L+K-1
+    w = (rng.standard_normal((C, 4)) * 0.5).astype(np.float32)
+    dy = rng.standard_normal((B, L, C), dtype=np.float32)
+    ref = oracle.conv1d_silu_vjp(xp[:, :L + 3], w, np.zeros(C, np.float32), L, dy)
+    x_t = cu(xp)
+    a = mixer.conv1d_silu_backward(x_t, cu(w), None, cu(dy), L=L)
+    b2 = mixer.conv1d_silu_backward(x_t, cu(w), None, cu(dy), L=L)
+    # channel-strided input (generic path)
+    xs = cu(xp).transpose(1, 2).contiguous().transpose(1, 2)
+    c = mixer.conv1d_silu_backward(xs, cu(w), None, cu(dy), L=L)
+    torch.cuda.synchronize()
+    assert a[2] is None
+    assert torch.equal(a[0], b2[0]) and torch.equal(a[1], b2[1])   # fixed-order sums
+    assert np.abs(np_(a[0])[:, L + 3:]).max() == 0                   # rows the conv never read
+    for got in (a, c):
+        assert_close(np_(got[0])[:, :L + 3], ref[0], False)
+        assert_close(np_(got[1]), ref[1], False)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_conv1d_silu_autograd(dtype):
+    # _metal_conv1d_silu's custom VJP (mamba_block.py:19-47) against float64 autograd
+    from alloy_b200.mamba_block import _metal_conv1d_silu
+    rng = np.random.default_rng(9)
+    B, L, C = 2, 130, 192
+    xp = oracle.bf16_round(rng.standard_normal((B, L + 3, C), dtype=np.float32))
+    w = (rng.standard_normal((C, 4)) * 0.5).astype(np.float32)
+    b = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    up = oracle.bf16_round(rng.standard_normal((B, L, C), dtype=np.float32))
+    x_t = cu(xp, dtype).requires_grad_()
+    w_t, b_t = cu(w).requires_grad_(), cu(b).requires_grad_()
+    (_metal_conv1d_silu(x_t, w_t, b_t, L).float() * cu(up)).sum().backward()
+    x64, w64, b64 = (torch.tensor(a, dtype=torch.float64, requires_grad=True) for a in (xp, w, b))
+    pre = sum(x64[:, k:k + L, :] * w64[:, k] for k in range(4)) + b64
+    (torch.nn.functional.silu(pre) * torch.tensor(up, dtype=torch.float64)).sum().backward()
+    for got, ref in ((x_t.grad, x64.grad), (w_t.grad, w64.grad), (b_t.grad, b64.grad)):
+        assert_close(np_(got), ref.numpy(), dtype == torch.bfloat16)
+
+
 def test_conv1d_strided_input_uses_generic_path():
     rng = np.random.default_rng(7)
     xp = rng.standard_normal((2, 40, 64), dtype=np.float32)

@@ -34,6 +34,34 @@ def test_conv1d_silu_matches_reference():
     np.testing.assert_allclose(out, g["out"], rtol=0, atol=1e-6)
 
 
+def test_conv1d_silu_vjp_matches_reference():
+    # the reference's own _metal_conv1d_silu_vjp (mamba_block.py:25-47), executed
+    g = load_golden("conv1d_silu_vjp")
+    L = g["dy"].shape[1]
+    dx, dw, db = oracle.conv1d_silu_vjp(g["x_padded"], g["weight"], g["bias"], L, g["dy"])
+    np.testing.assert_allclose(dx, g["dx_padded"], rtol=0, atol=1e-6)
+    np.testing.assert_allclose(dw, g["dweight"], rtol=1e-6, atol=1e-5)
+    np.testing.assert_allclose(db, g["dbias"], rtol=1e-6, atol=1e-5)
+
+
+@pytest.mark.parametrize("K,L", [(4, 37), (2, 1), (3, 5)])
+def test_conv1d_silu_vjp_is_the_gradient(K, L):
+    # independent check: float64 autograd of conv + silu
+    import torch
+    rng = np.random.default_rng(K * 100 + L)
+    B, C = 2, 24
+    xp = rng.standard_normal((B, L + K - 1, C)).astype(np.float32)
+    w = (rng.standard_normal((C, K)) * 0.5).astype(np.float32)
+    b = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    dy = rng.standard_normal((B, L, C)).astype(np.float32)
+    dx, dw, db = oracle.conv1d_silu_vjp(xp, w, b, L, dy)
+    x_t, w_t, b_t = (torch.tensor(a, dtype=torch.float64, requires_grad=True) for a in (xp, w, b))
+    pre = sum(x_t[:, k:k + L, :] * w_t[:, k] for k in range(K)) + b_t
+    torch.nn.functional.silu(pre).backward(torch.tensor(dy, dtype=torch.float64))
+    for got, ref in ((dx, x_t.grad), (dw, w_t.grad), (db, b_t.grad)):
+        assert oracle.rel_l2(got, ref.numpy()) < 1e-6
+
+
 def test_scan_chunk_matches_reference():
     # reference tests/test_metal_kernels.py:75-89 (chunk kernels == pure ops)
     g = load_golden("scan_chunk")
