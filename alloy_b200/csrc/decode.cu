@@ -18,6 +18,15 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
 
+// the state is read and written once per token: streaming (evict-first)
+// cache policy for both, so it does not displace the rest of L2
+__device__ __forceinline__ float4 ld_state(const float* p) {
+  return __ldcs(reinterpret_cast<const float4*>(p));
+}
+__device__ __forceinline__ void st_state(float* p, const float4& v) {
+  __stcs(reinterpret_cast<float4*>(p), v);
+}
+
 // Phase 2 for the [.., P, N] layout (N contiguous): a row p is NV float4s,
 // handled by NV lanes (NV a power of two <= 32); y[p] is a segmented
 // shuffle reduction.  NV == 0 selects the generic loop (a warp per row).
@@ -39,7 +48,7 @@ __device__ __forceinline__ void state_rows_pn(const DecodeArgs& a, float* st, co
       for (int u = 0; u < kUnroll; ++u) {
         s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         const int p = p0 + u * RPW + sub;
-        if (p < P) s[u] = *reinterpret_cast<const float4*>(st + (int64_t)p * a.st_row + 4 * j);
+        if (p < P) s[u] = ld_state(st + (int64_t)p * a.st_row + 4 * j);
       }
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
@@ -54,7 +63,7 @@ __device__ __forceinline__ void state_rows_pn(const DecodeArgs& a, float* st, co
 #pragma unroll
         for (int o = NV / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
         if (p < P) {
-          *reinterpret_cast<float4*>(st + (int64_t)p * a.st_row + 4 * j) = v;
+          st_state(st + (int64_t)p * a.st_row + 4 * j, v);
           if (j == 0) store_any(yrow, y_off + p, a.y_bf16, fmaf(Dh, xs[p], part));
         }
       }
@@ -95,7 +104,7 @@ __device__ __forceinline__ void state_rows_np(const DecodeArgs& a, float* st, co
       for (int u = 0; u < kUnroll; ++u) {
         s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         const int n = n0 + u;
-        if (n < N) s[u] = *reinterpret_cast<const float4*>(st + (int64_t)n * a.st_row + 4 * j);
+        if (n < N) s[u] = ld_state(st + (int64_t)n * a.st_row + 4 * j);
       }
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
@@ -107,7 +116,7 @@ __device__ __forceinline__ void state_rows_np(const DecodeArgs& a, float* st, co
           v.y = fmaf(dA, v.y, bd * xv.y);
           v.z = fmaf(dA, v.z, bd * xv.z);
           v.w = fmaf(dA, v.w, bd * xv.w);
-          *reinterpret_cast<float4*>(st + (int64_t)n * a.st_row + 4 * j) = v;
+          st_state(st + (int64_t)n * a.st_row + 4 * j, v);
           acc.x = fmaf(c, v.x, acc.x);
           acc.y = fmaf(c, v.y, acc.y);
           acc.z = fmaf(c, v.z, acc.z);

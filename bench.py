@@ -49,6 +49,9 @@ WORKLOADS = {
     # the gate and inner RMS norm after the scan (d_inner = H * P), full-width norm
     "gated_norm": dict(name="nemotron_h_8b_mamba2_gated_rmsnorm", B=4, L=8192, H=128, P=64,
                        N=128, G=8, K=4, Q=256),
+    # the standalone conv1d + SiLU (split mode, alloy_conv1d_silu) over the layer's xBC
+    "conv": dict(name="nemotron_h_8b_mamba2_conv1d_silu", B=4, L=8192, H=128, P=64, N=128, G=8,
+                 K=4, Q=256),
     # backward of conv1d + SiLU over the layer's xBC (training: the reference's custom VJP)
     "conv_bwd": dict(name="nemotron_h_8b_mamba2_conv1d_silu_backward", B=4, L=8192, H=128, P=64,
                      N=128, G=8, K=4, Q=256),
@@ -227,7 +230,8 @@ def run_ours(args, w):
 
     world, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local if world > 1 else 0)
-    H_l, G_l = local_problem(w, world, rank)
+    # --shard-of N on one GPU: the share of one rank of an N-GPU run (profiling)
+    H_l, G_l = local_problem(w, args.shard_of if world == 1 and args.shard_of else world, rank)
     B, L, P, N, K, Q = w["B"], w["L"], w["P"], w["N"], w["K"], w["Q"]
     conv_dim = H_l * P + 2 * G_l * N
     kw = dict(n_heads=H_l, head_dim=P, d_state=N, n_groups=G_l, d_conv=K, chunk_size=Q)
@@ -470,6 +474,76 @@ def run_gated_norm(args, w):
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": w["name"], "rows": rows_total, "channels": D,
                        "norm": "full width, eps 1e-5, fp32 weight",
+                       "l2": f"{rot} rotating input/output sets of {set_bytes / 2**20:.0f} MiB"},
+            "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / world / peak, "traffic": None,
+                         "peak_source": f"{peak_kind} hbm_gbs"},
+            "gpu_launches": launches, "clocks": clocks.summary(h0, h1)}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_conv(args, w):
+    """The standalone causal depthwise conv1d + SiLU (``mixer.conv1d_silu``, the
+    split-mode kernel of the reference's ``fused_conv1d_silu``) over the layer's
+    xBC (conv_dim = H P + 2 G N channels).  Batch rows split over the GPUs;
+    reported as achieved HBM GB/s (x_padded read once, out written once).
+    Inputs rotate through enough sets to exceed 3x L2."""
+    import torch
+    from alloy_b200 import _lib, mixer
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    B, L, K = w["B"], w["L"], w["K"]
+    C = w["H"] * w["P"] + 2 * w["G"] * w["N"]
+    if B % world:
+        raise SystemExit("batch rows do not split over the GPUs")
+    Bl = B // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(31 + rank)
+    set_bytes = Bl * (2 * L + K - 1) * C * 2
+    rot = max(1, math.ceil(3 * L2_BYTES / set_bytes))
+    sets = [(torch.randn((Bl, L + K - 1, C), generator=gen, device=dev).to(torch.bfloat16),
+             torch.empty((Bl, L, C), dtype=torch.bfloat16, device=dev)) for _ in range(rot)]
+    weight = torch.randn((C, K), generator=gen, device=dev) * 0.5
+    bias = torch.zeros(C, device=dev)
+
+    def step(i):
+        x, out = sets[i % rot]
+        mixer.conv1d_silu(x, weight, bias, L, out=out)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    h0 = time.perf_counter()
+    launches0 = _lib.load().alloy_kernel_launch_count()
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    launches = _lib.load().alloy_kernel_launch_count() - launches0
+    torch.cuda.synchronize()
+    h1 = time.perf_counter()
+    barrier(world)
+    clocks.stop()
+    ms = dist_max(ev0.elapsed_time(ev1) / args.steps, world)
+    alg = set_bytes + C * (K + 1) * 4
+    peak, peak_kind = measured_peaks()
+    gbs = alg * world / (ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Mamba-2 causal depthwise conv1d+SiLU HBM GB/s",
+            "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": w["name"], "batch": B, "seq_len": L, "channels": C, "d_conv": K,
                        "l2": f"{rot} rotating input/output sets of {set_bytes / 2**20:.0f} MiB"},
             "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
                          "frac": gbs / world / peak, "traffic": None,
@@ -796,6 +870,9 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="nemotron")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    ap.add_argument("--shard-of", type=int, default=None,
+                    help="on one GPU, run the share of one rank of an N-GPU prefill (for profiling "
+                         "the per-GPU work of a multi-GPU run; the line reports that shard's tokens)")
     ap.add_argument("--piece-tokens", type=int, default=2048,
                     help="tokens per piece of the end-to-end leg's host-streamed prefill")
     ap.add_argument("--gather", action="store_true",
@@ -813,6 +890,8 @@ def main():
         w["B"] = args.batch
     if args.seqlen is not None:
         w["L"] = args.seqlen
+    if args.shard_of:
+        w["name"] += f"_shard_of_{args.shard_of}"
     if args.batch is not None or args.seqlen is not None:
         w["name"] += f"_b{w['B']}_l{w['L']}"
     if args.impl == "reference":
@@ -825,6 +904,8 @@ def main():
         run_decode_block(args, w)
     elif args.workload == "conv_bwd":
         run_conv_bwd(args, w)
+    elif args.workload == "conv":
+        run_conv(args, w)
     else:
         run_ours(args, w)
 
