@@ -128,19 +128,23 @@ conv1d_silu_tile_kernel(const T* __restrict__ xp, int64_t xp_sb, int64_t xp_st,
   }
 }
 
-// bf16 activations, K = 4 (the layer case): a CTA owns 128 output rows x 256
-// channels of one batch row.  Its 131 input rows arrive in shared memory by
-// cp.async 16-byte copies, all issued before the first wait, so a CTA has its
-// whole tile (67 KB) in flight and three CTAs share an SM.  Each thread then
-// convolves 8 channels over 16 rows in packed f32x2 FMAs with the taps and
-// bias halved, which gives h = x / 2 and silu(x) = h + h tanh(h) from one
-// hardware tanh (its error is below the bf16 rounding of the output).
-constexpr int kBfRows = 128;                       // output rows per CTA
+// bf16 activations, K = 4 (the layer case): a CTA owns kBfTiles consecutive
+// tiles of 64 output rows x 256 channels of one batch row.  The 67 input rows of
+// a tile (the K-1-row halo shared by its outputs) arrive in shared memory by
+// cp.async 16-byte copies into one of two buffers: the copies of tile i + 1 are
+// in flight while tile i is computed, and two CTAs share an SM (at three a CTA
+// the registers spill, which cost more than the third CTA gained).  Each thread
+// convolves 8 channels over 8 rows in packed f32x2 FMAs with the taps and bias
+// halved, which gives h = x / 2 and silu(x) = h + h tanh(h) from one hardware
+// tanh (its error is below the bf16 rounding of the output).
+constexpr int kBfRows = 64;                        // output rows per tile
+constexpr int kBfTiles = 8;                        // tiles per CTA
 constexpr int kBfCols = 256;                       // channels per CTA
-constexpr int kBfSmem = (kBfRows + 3) * kBfCols * 2;
+constexpr int kBfBuf = (kBfRows + 3) * kBfCols * 2;
+constexpr int kBfSmem = 2 * kBfBuf;
 
 template <bool SILU>
-__global__ void __launch_bounds__(256, 3)
+__global__ void __launch_bounds__(256, 2)
 conv1d_silu_bf16_kernel(const __nv_bfloat16* __restrict__ xp, int64_t xp_sb, int64_t xp_st,
                         const void* __restrict__ w, int w_bf16, int64_t w_sc, int64_t w_sk,
                         const void* __restrict__ bias, int b_bf16, int64_t b_s,
@@ -149,23 +153,29 @@ conv1d_silu_bf16_kernel(const __nv_bfloat16* __restrict__ xp, int64_t xp_sb, int
   extern __shared__ __align__(16) unsigned char tile_raw[];
   __shared__ float4 taps_s[kBfCols];
   __shared__ float bias_s[kBfCols];
-  const uint32_t tile = static_cast<uint32_t>(__cvta_generic_to_shared(tile_raw));
+  const uint32_t tiles = static_cast<uint32_t>(__cvta_generic_to_shared(tile_raw));
   const int b = blockIdx.z;
-  const int t0 = blockIdx.x * kBfRows;
   const int c0 = blockIdx.y * kBfCols;
   const int Lp = L + 3;
-  const int nvec = min(kBfCols, C - c0) / 8;        // 16-byte channel vectors of this tile
-  // the tile: input rows [t0, t0 + 131) x vectors [0, nvec); rows past the
-  // input are zero-filled (they only feed rows past L, which are not stored)
+  const int nvec = min(kBfCols, C - c0) / 8;        // 16-byte channel vectors of this CTA
+  const int tile0 = blockIdx.x * kBfTiles;
+  const int ntiles = min(kBfTiles, (L + kBfRows - 1) / kBfRows - tile0);
   const __nv_bfloat16* src = xp + (int64_t)b * xp_sb + c0;
-  for (int i = threadIdx.x; i < (kBfRows + 3) * 32; i += 256) {
-    const int r = i >> 5, v = i & 31;
-    const bool ok = v < nvec && t0 + r < Lp;
-    const void* g = ok ? (const void*)(src + (int64_t)(t0 + r) * xp_st + v * 8) : (const void*)src;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tile + i * 16), "l"(g), "r"(ok ? 16 : 0)
-                 : "memory");
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
+  // input rows [t0, t0 + 67) x vectors [0, nvec) of tile i into buffer i & 1;
+  // rows past the input are zero-filled (they only feed rows past L)
+  auto load_tile = [&](int i) {
+    const int t0 = (tile0 + i) * kBfRows;
+    const uint32_t buf = tiles + (i & 1) * kBfBuf;
+    for (int k = threadIdx.x; k < (kBfRows + 3) * 32; k += 256) {
+      const int r = k >> 5, v = k & 31;
+      const bool ok = v < nvec && t0 + r < Lp;
+      const void* g = ok ? (const void*)(src + (int64_t)(t0 + r) * xp_st + v * 8) : (const void*)src;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(buf + k * 16), "l"(g), "r"(ok ? 16 : 0)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  load_tile(0);
   if (threadIdx.x < kBfCols) {
     const int ch = min(c0 + (int)threadIdx.x, C - 1);
     const float f = SILU ? 0.5f : 1.f;   // halved for the tanh form of silu
@@ -175,58 +185,69 @@ conv1d_silu_bf16_kernel(const __nv_bfloat16* __restrict__ xp, int64_t xp_sb, int
                                       f * load_any(w, (int64_t)ch * w_sc + 3 * w_sk, w_bf16));
     bias_s[threadIdx.x] = bias ? f * load_any(bias, (int64_t)ch * b_s, b_bf16) : 0.f;
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-
-  const int cg = threadIdx.x & 31, strip = threadIdx.x >> 5;   // 8 channels x 16 rows
-  if (cg >= nvec) return;
+  const int cg = threadIdx.x & 31, strip = threadIdx.x >> 5;   // 8 channels x 8 rows
   uint64_t w2[4][4], b2[4];   // [tap][channel pair]
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float4 ta = taps_s[cg * 8 + 2 * i], tb = taps_s[cg * 8 + 2 * i + 1];
+    const int cc = min(cg, max(nvec - 1, 0)) * 8;
+    const float4 ta = taps_s[cc + 2 * i], tb = taps_s[cc + 2 * i + 1];
     w2[0][i] = f2_pack(ta.x, tb.x);
     w2[1][i] = f2_pack(ta.y, tb.y);
     w2[2][i] = f2_pack(ta.z, tb.z);
     w2[3][i] = f2_pack(ta.w, tb.w);
-    b2[i] = f2_pack(bias_s[cg * 8 + 2 * i], bias_s[cg * 8 + 2 * i + 1]);
+    b2[i] = f2_pack(bias_s[cc + 2 * i], bias_s[cc + 2 * i + 1]);
   }
-  const int r0 = strip * 16;
-  const uint32_t col = tile + cg * 16;
-  uint64_t win[3][4];
+  const int r0 = strip * 8;
+#pragma unroll 1
+  for (int i = 0; i < ntiles; ++i) {
+    // tile i + 1 in flight while tile i is computed (its buffer was last read
+    // by tile i - 1, which every thread finished before the barrier below)
+    if (i + 1 < ntiles) load_tile(i + 1);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncthreads();
+    const int t0 = (tile0 + i) * kBfRows;
+    if (cg < nvec) {
+      const uint32_t col = tiles + (i & 1) * kBfBuf + cg * 16;
+      uint64_t win[3][4];
 #pragma unroll
-  for (int r = 0; r < 3; ++r) {
-    uint32_t u0, u1, u2, u3;
-    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(u0), "=r"(u1), "=r"(u2), "=r"(u3)
-                 : "r"(col + (r0 + r) * 512));
-    win[r][0] = f2_from_bf2(u0); win[r][1] = f2_from_bf2(u1);
-    win[r][2] = f2_from_bf2(u2); win[r][3] = f2_from_bf2(u3);
-  }
-  __nv_bfloat16* dst = out + (int64_t)b * o_sb + (int64_t)(t0 + r0) * o_st + c0 + cg * 8;
-#pragma unroll
-  for (int r = 0; r < 16; ++r) {
-    uint32_t u0, u1, u2, u3;
-    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(u0), "=r"(u1), "=r"(u2), "=r"(u3)
-                 : "r"(col + (r0 + r + 3) * 512));
-    const uint64_t x[4] = {f2_from_bf2(u0), f2_from_bf2(u1), f2_from_bf2(u2), f2_from_bf2(u3)};
-    uint32_t o[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint64_t acc = f2_fma(win[0][i], w2[0][i], b2[i]);
-      acc = f2_fma(win[1][i], w2[1][i], acc);
-      acc = f2_fma(win[2][i], w2[2][i], acc);
-      acc = f2_fma(x[i], w2[3][i], acc);
-      if (SILU) {
-        float hl, hh;
-        f2_unpack(acc, hl, hh);
-        acc = f2_fma(acc, f2_pack(tanh_approx(hl), tanh_approx(hh)), acc);
+      for (int r = 0; r < 3; ++r) {
+        uint32_t u0, u1, u2, u3;
+        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(u0), "=r"(u1), "=r"(u2), "=r"(u3)
+                     : "r"(col + (r0 + r) * 512));
+        win[r][0] = f2_from_bf2(u0); win[r][1] = f2_from_bf2(u1);
+        win[r][2] = f2_from_bf2(u2); win[r][3] = f2_from_bf2(u3);
       }
-      o[i] = f2_to_bf2(acc);
-      win[0][i] = win[1][i];
-      win[1][i] = win[2][i];
-      win[2][i] = x[i];
+      __nv_bfloat16* dst = out + (int64_t)b * o_sb + (int64_t)(t0 + r0) * o_st + c0 + cg * 8;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        uint32_t u0, u1, u2, u3;
+        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(u0), "=r"(u1), "=r"(u2), "=r"(u3)
+                     : "r"(col + (r0 + r + 3) * 512));
+        const uint64_t x[4] = {f2_from_bf2(u0), f2_from_bf2(u1), f2_from_bf2(u2), f2_from_bf2(u3)};
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint64_t acc = f2_fma(win[0][q], w2[0][q], b2[q]);
+          acc = f2_fma(win[1][q], w2[1][q], acc);
+          acc = f2_fma(win[2][q], w2[2][q], acc);
+          acc = f2_fma(x[q], w2[3][q], acc);
+          if (SILU) {
+            float hl, hh;
+            f2_unpack(acc, hl, hh);
+            acc = f2_fma(acc, f2_pack(tanh_approx(hl), tanh_approx(hh)), acc);
+          }
+          o[q] = f2_to_bf2(acc);
+          win[0][q] = win[1][q];
+          win[1][q] = win[2][q];
+          win[2][q] = x[q];
+        }
+        if (t0 + r0 + r < L)
+          *reinterpret_cast<uint4*>(dst + (int64_t)r * o_st) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
     }
-    if (t0 + r0 + r < L)
-      *reinterpret_cast<uint4*>(dst + (int64_t)r * o_st) = make_uint4(o[0], o[1], o[2], o[3]);
+    __syncthreads();   // buffer i & 1 is free for tile i + 2
   }
 }
 
@@ -281,7 +302,7 @@ int conv1d_silu(const alloy_tensor_t* x, const alloy_tensor_t* w, const alloy_te
                       (x->stride[0] * es) % 16 == 0 && (x->stride[1] * es) % 16 == 0 &&
                       (out->stride[0] * es) % 16 == 0 && (out->stride[1] * es) % 16 == 0;
   if (vec_ok && x->dtype == ALLOY_BF16) {
-    dim3 grid((L + kBfRows - 1) / kBfRows, (C + kBfCols - 1) / kBfCols, B);
+    dim3 grid(((L + kBfRows - 1) / kBfRows + kBfTiles - 1) / kBfTiles, (C + kBfCols - 1) / kBfCols, B);
     const void* bptr = present(bias) ? bias->data : nullptr;
     auto launch = [&](auto kernel) {
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBfSmem);
