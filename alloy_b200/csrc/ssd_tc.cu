@@ -224,34 +224,45 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
 // swizzle of a K-major UMMA operand tile).  Rows past L are zeros.  Source
 // column of (part, gl, n): H*P + part*G*N + (group_begin + gl)*N + n.
 //
-// One CTA per (kBcTileRows-row tile, W-column tile, batch row): a single tensor
-// copy brings rows [t0 - 3, t0 + kBcTileRows) of the tile's columns into shared
-// memory (rows outside [0, L) arrive as zeros; rows before 0 are then taken
-// from the conv cache), and each thread convolves 8 adjacent columns over a
-// strip of rows with the last 3 inputs kept in registers.
-constexpr int kBcTileRows = 128;   // one chunk (64-row tiles measured slower: per-CTA setup dominates)
+// One CTA per (run of a.bc_chunks consecutive chunks, W-column tile, batch row).
+// Chunk i's rows [t0 - 3, t0 + kBcTileRows) of the tile's columns arrive by one
+// tensor copy into one of two shared-memory buffers (rows outside [0, L) as
+// zeros; rows before 0 are then taken from the conv cache): the copy of chunk
+// i + 1 is in flight while chunk i is convolved.  Each thread convolves 8
+// adjacent columns over a strip of rows with the last 3 inputs kept in
+// registers.
+constexpr int kBcTileRows = 128;   // one chunk
 
-template <int W>   // tile width in columns: 256, 128 or 64
-__global__ void __launch_bounds__(256)
+template <int W>   // tile width in columns: 128 or 64
+__global__ void __launch_bounds__(256, 2)
 bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv_bfloat16* __restrict__ bc,
-               int ncols) {
+               int ncols, int run) {
   constexpr int CG = W / 8;            // column groups of 8
   constexpr int R = kBcTileRows * CG / 256;   // rows per thread
+  constexpr uint32_t kBuf = ((kBcTileRows + 3) * W * 2 + 1023) & ~1023u;   // buffers 1 KB aligned
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ __align__(8) uint64_t full_bar;
+  __shared__ __align__(8) uint64_t full_bar[2];
   __shared__ float4 taps_s[W];     // the tile's conv taps and bias, halved (silu(2h) = h + h tanh h)
   __shared__ float bias_s[W];
   const uint32_t stile = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
-  const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&full_bar));
   const int b = blockIdx.z;
-  const int t0 = blockIdx.x * kBcTileRows;
   const int j0 = blockIdx.y * W;
   const int span = a.group_count * a.N;
   const int part = j0 / span;
   const int src0 = a.H * P + part * a.G * a.N + a.group_begin * a.N + (j0 - part * span);
+  const int nchunks = (a.L + Q - 1) / Q;
+  const int chunk0 = blockIdx.x * run;
+  const int nck = min(run, nchunks - chunk0);
+  auto bar = [&](int i) { return static_cast<uint32_t>(__cvta_generic_to_shared(&full_bar[i])); };
+  auto issue = [&](int i) {   // chunk chunk0 + i into buffer i & 1
+    mbar_arrive_expect_tx(bar(i & 1), (kBcTileRows + 3) * W * 2);
+    tma_load_3d(stile + (i & 1) * kBuf, &src_map, bar(i & 1), src0, (chunk0 + i) * kBcTileRows - 3, b);
+  };
   if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
+    mbar_init(bar(0), 1);
+    mbar_init(bar(1), 1);
     mbar_fence_init();
+    issue(0);
   }
   if (threadIdx.x < W) {   // one column each, consecutive threads on consecutive columns
     const int64_t ch = src0 + threadIdx.x;
@@ -261,20 +272,12 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
     bias_s[threadIdx.x] = a.conv_b ? 0.5f * a.conv_b[ch * a.cb_s] : 0.f;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(bar, (kBcTileRows + 3) * W * 2);
-    tma_load_3d(stile, &src_map, bar, src0, t0 - 3, b);
-  }
   const int cg = threadIdx.x % CG, strip = threadIdx.x / CG;
   const int c = src0 + cg * 8;
   // this thread's 8 columns in the tile layout
   const int rem = j0 - part * span + cg * 8;   // gl * N + n
   const int gl = rem / a.N, n = rem % a.N;
-  const int nchunks = (a.L + Q - 1) / Q;
-  constexpr int kTilesPerChunk = Q / kBcTileRows;
-  const int chunk = blockIdx.x / kTilesPerChunk;
-  const int row0 = (blockIdx.x % kTilesPerChunk) * kBcTileRows;   // first row of the tile inside its chunk
-  const int64_t tile = ((((int64_t)b * nchunks + chunk) * a.group_count + gl) * (a.N / 64) + n / 64) * 2 + part;
+  const int nn8 = (n % 64) / 8;   // 16-byte chunk of the row
   // halved taps and bias of this thread's 8 columns, as channel pairs
   uint64_t w2[4][4], b2[4];
 #pragma unroll
@@ -286,77 +289,91 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
     w2[3][i] = f2_pack(t0v.w, t1v.w);
     b2[i] = f2_pack(bias_s[cg * 8 + 2 * i], bias_s[cg * 8 + 2 * i + 1]);
   }
-  // bounded wait for the tile; on timeout record the error and give the copy
-  // a second bounded period before the CTA leaves
-  {
-    const long long start = clock64();
-    bool ok = false;
-    while (!(ok = mbar_try_wait(bar, 0)) && clock64() - start < kWaitCycles) {
-    }
-    if (!__syncthreads_and(ok)) {
-      if (threadIdx.x == 0) {
-        if (atomicCAS(&g_ssd_tc_error[0], 0u, 1u + 40u) == 0u) {
-          g_ssd_tc_error[1] = blockIdx.x;
-          g_ssd_tc_error[2] = blockIdx.y;
-        }
-        const long long again = clock64();
-        while (!mbar_try_wait(bar, 0) && clock64() - again < kWaitCycles) {
-        }
-      }
-      __syncthreads();
-      return;
-    }
-  }
   const int r0 = strip * R;            // first output row of this thread (tile-relative)
-  const uint32_t col = stile + cg * 16;
-  uint64_t win[3][4];
-#pragma unroll
-  for (int r = 0; r < 3; ++r) {
-    const int t = t0 + r0 - 3 + r;
-    if (t >= 0) {
-      uint32_t w0, w1, w2v, w3;
-      asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(w0), "=r"(w1), "=r"(w2v), "=r"(w3) : "r"(col + (r0 + r) * (W * 2)));
-      win[r][0] = f2_from_bf2(w0); win[r][1] = f2_from_bf2(w1);
-      win[r][2] = f2_from_bf2(w2v); win[r][3] = f2_from_bf2(w3);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float f[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e)
-          f[e] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb + (int64_t)(a.K - 1 + t) * a.ci_sk +
-                                                       (int64_t)(c + 2 * i + e) * a.ci_sc])
-                           : 0.f;
-        win[r][i] = f2_pack(f[0], f[1]);
+#pragma unroll 1
+  for (int i = 0; i < nck; ++i) {
+    const int chunk = chunk0 + i;
+    const int t0 = chunk * kBcTileRows;
+    // the next chunk's copy, into the buffer every thread finished reading
+    // before the barrier that ended the previous iteration
+    if (threadIdx.x == 0 && i + 1 < nck) {
+      fence_async_smem();
+      issue(i + 1);
+    }
+    // bounded wait for this chunk's tile; on timeout record the error and give
+    // the copies in flight a second bounded period before the CTA leaves
+    {
+      const long long start = clock64();
+      bool ok = false;
+      while (!(ok = mbar_try_wait(bar(i & 1), (i >> 1) & 1)) && clock64() - start < kWaitCycles) {
+      }
+      if (!__syncthreads_and(ok)) {
+        if (threadIdx.x == 0) {
+          if (atomicCAS(&g_ssd_tc_error[0], 0u, 1u + 40u) == 0u) {
+            g_ssd_tc_error[1] = blockIdx.x;
+            g_ssd_tc_error[2] = blockIdx.y;
+          }
+          for (int k = i; k < min(i + 2, nck); ++k) {
+            const long long again = clock64();
+            while (!mbar_try_wait(bar(k & 1), (k >> 1) & 1) && clock64() - again < kWaitCycles) {
+            }
+          }
+        }
+        __syncthreads();
+        return;
       }
     }
-  }
-  unsigned char* dst = reinterpret_cast<unsigned char*>(bc) + tile * 16384;
-  const int nn8 = (n % 64) / 8;   // 16-byte chunk of the row
+    const uint32_t col = stile + (i & 1) * kBuf + cg * 16;
+    uint64_t win[3][4];
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    uint32_t u0, u1, u2, u3;
-    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(u0), "=r"(u1), "=r"(u2), "=r"(u3) : "r"(col + (r0 + r + 3) * (W * 2)));
-    const uint64_t x[4] = {f2_from_bf2(u0), f2_from_bf2(u1), f2_from_bf2(u2), f2_from_bf2(u3)};
-    uint32_t o[4];
+    for (int r = 0; r < 3; ++r) {
+      const int t = t0 + r0 - 3 + r;
+      if (t >= 0) {
+        uint32_t w0, w1, w2v, w3;
+        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(w0), "=r"(w1), "=r"(w2v), "=r"(w3) : "r"(col + (r0 + r) * (W * 2)));
+        win[r][0] = f2_from_bf2(w0); win[r][1] = f2_from_bf2(w1);
+        win[r][2] = f2_from_bf2(w2v); win[r][3] = f2_from_bf2(w3);
+      } else {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint64_t acc = f2_fma(win[0][i], w2[0][i], b2[i]);
-      acc = f2_fma(win[1][i], w2[1][i], acc);
-      acc = f2_fma(win[2][i], w2[2][i], acc);
-      acc = f2_fma(x[i], w2[3][i], acc);
-      // acc = h = x/2: silu(x) = h + h tanh(h)
-      float hl, hh;
-      f2_unpack(acc, hl, hh);
-      o[i] = t0 + r0 + r < a.L ? pack_bf16x2(fmaf(hl, tanh_approx(hl), hl), fmaf(hh, tanh_approx(hh), hh)) : 0u;
-      win[0][i] = win[1][i];
-      win[1][i] = win[2][i];
-      win[2][i] = x[i];
+        for (int q = 0; q < 4; ++q) {
+          float f[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+            f[e] = a.conv_in ? __bfloat162float(a.conv_in[(int64_t)b * a.ci_sb + (int64_t)(a.K - 1 + t) * a.ci_sk +
+                                                         (int64_t)(c + 2 * q + e) * a.ci_sc])
+                             : 0.f;
+          win[r][q] = f2_pack(f[0], f[1]);
+        }
+      }
     }
-    const int row = row0 + r0 + r;
-    *reinterpret_cast<uint4*>(dst + row * 128 + ((nn8 ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    const int64_t tile = ((((int64_t)b * nchunks + chunk) * a.group_count + gl) * (a.N / 64) + n / 64) * 2 + part;
+    unsigned char* dst = reinterpret_cast<unsigned char*>(bc) + tile * 16384;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      uint32_t u0, u1, u2, u3;
+      asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(u0), "=r"(u1), "=r"(u2), "=r"(u3) : "r"(col + (r0 + r + 3) * (W * 2)));
+      const uint64_t x[4] = {f2_from_bf2(u0), f2_from_bf2(u1), f2_from_bf2(u2), f2_from_bf2(u3)};
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint64_t acc = f2_fma(win[0][q], w2[0][q], b2[q]);
+        acc = f2_fma(win[1][q], w2[1][q], acc);
+        acc = f2_fma(win[2][q], w2[2][q], acc);
+        acc = f2_fma(x[q], w2[3][q], acc);
+        // acc = h = x/2: silu(x) = h + h tanh(h)
+        float hl, hh;
+        f2_unpack(acc, hl, hh);
+        o[q] = t0 + r0 + r < a.L ? pack_bf16x2(fmaf(hl, tanh_approx(hl), hl), fmaf(hh, tanh_approx(hh), hh)) : 0u;
+        win[0][q] = win[1][q];
+        win[1][q] = win[2][q];
+        win[2][q] = x[q];
+      }
+      const int row = r0 + r;
+      *reinterpret_cast<uint4*>(dst + row * 128 + ((nn8 ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    __syncthreads();   // buffer i & 1 is free for chunk i + 2
   }
 }
 
@@ -1338,9 +1355,9 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
   const int ncols = 2 * gs * s.N;
   __nv_bfloat16* bc = static_cast<__nv_bfloat16*>(workspace);
   {
-    // widest tile dividing one of the B / C blocks (gs * N is a multiple of 64)
+    // 128-column tiles where they divide a B / C block (gs * N is a multiple of 64)
     const int span = gs * s.N;
-    const int W = span % 256 == 0 ? 256 : span % 128 == 0 ? 128 : 64;
+    const int W = span % 128 == 0 ? 128 : 64;
     CUtensorMap smap;
     const cuuint32_t sbox[3] = {(cuuint32_t)W, (cuuint32_t)(kBcTileRows + 3), 1};
     CUresult r = encode(&smap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(s.xBC), xd, xs, sbox,
@@ -1348,16 +1365,20 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
       return fail(ALLOY_ERR_CUDA, "ssd_tc: cuTensorMapEncodeTiled (B/C tile) failed (%d)", (int)r);
-    // every row of every chunk, the padded rows past L included (written as zeros)
-    dim3 grid(((s.L + Q - 1) / Q) * (Q / kBcTileRows), ncols / W, s.B);
-    const int smem = (kBcTileRows + 3) * W * 2;
-    if (W == 256) {
-      ALLOY_CUDA(cudaFuncSetAttribute(bc_conv_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      bc_conv_kernel<256><<<grid, 256, smem, stream>>>(smap, a, bc, ncols);
-    } else if (W == 128) {
-      bc_conv_kernel<128><<<grid, 256, smem, stream>>>(smap, a, bc, ncols);
+    // every row of every chunk, the padded rows past L included (written as
+    // zeros); runs of chunks per CTA long enough to double-buffer, short enough
+    // to leave about four CTAs per SM
+    const int nchunks = (s.L + Q - 1) / Q;
+    const int tiles = nchunks * (ncols / W) * s.B;
+    const int run = std::max(1, std::min(8, tiles / (4 * std::max(1, sm_count_of_current_device()))));
+    dim3 grid((nchunks + run - 1) / run, ncols / W, s.B);
+    const int smem = 2 * (((kBcTileRows + 3) * W * 2 + 1023) & ~1023);
+    if (W == 128) {
+      ALLOY_CUDA(cudaFuncSetAttribute(bc_conv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      bc_conv_kernel<128><<<grid, 256, smem, stream>>>(smap, a, bc, ncols, run);
     } else {
-      bc_conv_kernel<64><<<grid, 256, smem, stream>>>(smap, a, bc, ncols);
+      ALLOY_CUDA(cudaFuncSetAttribute(bc_conv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      bc_conv_kernel<64><<<grid, 256, smem, stream>>>(smap, a, bc, ncols, run);
     }
     ALLOY_TRY(check_launch("bc_conv_kernel"));
   }

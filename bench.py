@@ -67,7 +67,7 @@ FALLBACK_HBM_GBS = 6650.0
 # over the step's three launches (B/C pre-pass, SSD, conv-cache roll), keyed by
 # (workload, n_gpus); the capture's summary is kept under profiles/.
 # Configurations not captured report None.
-NCU_TRAFFIC_BYTES = {("nemotron", 1): (134.3 + 81.8 + 685.7 + 508.3 + 0.4) * 1e6,
+NCU_TRAFFIC_BYTES = {("nemotron", 1): (134.6 + 80.7 + 685.6 + 507.7 + 0.4) * 1e6,
                      ("long", 1): (33.6 + 0.3 + 830.7 + 1.3 + 1143.2 + 1028.0 + 0.1) * 1e6}
 
 
