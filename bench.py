@@ -782,6 +782,17 @@ def run_decode(args, w):
 
 
 # ------------------------------------------------------------------ CPU reference
+def _all_blas_threads():
+    """Every host core for the numpy BLAS of the CPU samples (torchrun sets
+    OMP_NUM_THREADS=1 for its ranks; the reference arm runs on rank 0 alone)."""
+    import contextlib
+    try:
+        from threadpoolctl import threadpool_limits
+        return threadpool_limits(limits=os.cpu_count() or 1, user_api="blas")
+    except Exception:
+        return contextlib.nullcontext()
+
+
 def _blas_threads():
     try:
         from threadpoolctl import threadpool_info
@@ -806,6 +817,11 @@ def _cpu_sample(w, heads, tokens, seed=0):
 
 
 def cpu_baseline_sample(w, budget_s=20.0):
+    with _all_blas_threads():
+        return _cpu_baseline_sample(w, budget_s)
+
+
+def _cpu_baseline_sample(w, budget_s):
     heads = w["H"] // w["G"]           # one head-group
     tokens = min(w["L"], 2 * w["Q"])   # the first chunks of one batch row
     secs = _cpu_sample(w, heads, tokens)
@@ -826,6 +842,11 @@ def run_reference(args, w):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    with _all_blas_threads():
+        _run_reference(args, w, world)
+
+
+def _run_reference(args, w, world):
     heads = w["H"] // w["G"]
     tokens = min(w["L"], w["Q"])
     # size each step so that warmup + steps stay within about two minutes
@@ -883,6 +904,11 @@ def main():
     ap.add_argument("--seqlen", type=int, default=None,
                     help="override the workload's sequence length")
     args = ap.parse_args()
+    if args.impl == "reference":
+        # the CPU arm uses every host core: torchrun sets OMP_NUM_THREADS=1 for
+        # its ranks, and numpy's BLAS sizes its thread pool when it loads
+        for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+            os.environ[var] = str(os.cpu_count() or 1)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     w = dict(WORKLOADS[args.workload])
