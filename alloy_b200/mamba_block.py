@@ -32,6 +32,10 @@ from . import mixer
 __all__ = ["MambaCache", "MambaBlock"]
 
 
+def _needs_grad(*ts):
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts)
+
+
 def _metal_conv1d_silu(x_padded, weight, bias, L):
     """conv1d + SiLU that autograd differentiates with the library's backward
     kernel, as alloy's ``@mx.custom_function _metal_conv1d_silu`` with its
@@ -114,15 +118,45 @@ class MambaBlock(torch.nn.Module):
                                     out_dtype=torch.float32)
 
     def _selective_scan(self, x, A_disc, B, C, cache=None, log_a=None):
-        """Chunked scan with the cache's state; y in x's dtype (:364-365)."""
+        """Chunked scan with the cache's state; y in x's dtype (:364-365).
+        Differentiable (``mixer.SelectiveScan``) when autograd needs it."""
+        h0 = cache.ssm_state if cache is not None else None
+        if _needs_grad(x, A_disc, B, C, log_a, h0):
+            y, h = mixer.SelectiveScan.apply(x, A_disc if log_a is None else None, B, C, h0, log_a)
+            if cache is not None:
+                cache.ssm_state = h
+            return y
         if x.shape[1] <= 1:
             return self._selective_scan_sequential(x, A_disc, B, C, cache)
-        h0 = cache.ssm_state if cache is not None else None
         y, h = mixer.selective_scan(x, A_disc, B, C, ssm_state=h0, log_a=log_a,
                                     write_ssm_state=cache is not None)
         if cache is not None:
             cache.ssm_state = h
         return y
+
+    def _forward_combined_train(self, gate, xBC, dt, Bsz, L):
+        """Combined mode under autograd (training, no cache): the fused prefill has
+        no backward, so the same steps run as differentiable pieces: the conv with
+        its VJP (``_metal_conv1d_silu``), the split and discretisation of
+        :458-486, the scan with its VJP (``mixer.SelectiveScan``), D on the
+        unscaled x (:481-482), then the gate and the inner norm (:495-499)."""
+        H, P, N, G, K = self.n_heads, self.headdim, self.d_state, self.n_groups, self.d_conv
+        x_padded = F.pad(xBC, (0, 0, K - 1, 0))
+        conv = _metal_conv1d_silu(x_padded, self.conv_weight, self.conv_bias, L)
+        xs, Bm, Cm = conv.split([H * P, G * N, G * N], dim=-1)
+        xh = xs.reshape(Bsz, L, H, P).float()
+        dtv = F.softplus(dt.float() + self.dt_bias)
+        log_a = dtv * -torch.exp(self.A_log.float())
+        y, _ = mixer.SelectiveScan.apply(xh * dtv[..., None], None,
+                                         Bm.reshape(Bsz, L, G, N).float(),
+                                         Cm.reshape(Bsz, L, G, N).float(), None, log_a)
+        if self.D is not None:
+            y = y + self.D.float()[:, None] * xh
+        y = y.to(xBC.dtype).reshape(Bsz, L, self.d_inner)
+        y = y * F.silu(gate)
+        if self.norm is not None:
+            y = self.norm(y)
+        return self.out_proj(y)
 
     # ------------------------------------------------------------------ forward
     def forward(self, x: torch.Tensor, cache: Optional[MambaCache] = None) -> torch.Tensor:
@@ -168,6 +202,8 @@ class MambaBlock(torch.nn.Module):
         xBC = proj[..., self.d_inner:self.d_inner + self.conv_dim]
         dt = proj[..., self.d_inner + self.conv_dim:]
         kw = dict(n_heads=self.n_heads, head_dim=self.headdim, d_state=N, n_groups=ng)
+        if cache is None and _needs_grad(xBC, dt, self.conv_weight, self.A_log, self.D):
+            return self._forward_combined_train(gate, xBC, dt, Bsz, L)
         if (L == 1 and cache is not None and cache.ssm_state is not None
                 and cache.conv_state is not None):
             y = mixer.ssd_decode_step(xBC[:, 0], dt[:, 0], self.conv_weight, self.conv_bias,

@@ -22,7 +22,7 @@ from . import _lib
 __all__ = [
     "conv1d_silu", "depthwise_conv1d", "ssd_combined", "selective_scan",
     "ssd_decode_step", "gated_rmsnorm", "ssd_combined_streamed", "conv1d_silu_backward",
-    "Conv1dSilu",
+    "Conv1dSilu", "selective_scan_backward", "SelectiveScan",
 ]
 
 
@@ -357,6 +357,103 @@ def selective_scan(x, A_disc, B, C, ssm_state=None, log_a=None, out=None, out_dt
     with torch.cuda.device(dev):
         _lib.call("alloy_selective_scan", *(_lib.ref(d) for d in descs), _lib.stream_handle(dev))
     return out, ssm_state_out
+
+
+def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dssm_state_out=None):
+    """Gradients of ``selective_scan``: ``(dx, dA_disc, dB, dC, dssm_state, dlog_a)``
+    for the output cotangent ``dy [B, L, H, P]`` and (optional) the cotangent of
+    the final state ``dssm_state_out [B, H, N, P]``.  What the reference gets
+    from MLX autograd through ``_selective_scan`` (alloy/models/mamba_block.py:
+    287-366); the reference has no custom kernel for it.
+
+    The scan h_t = a_t h_{t-1} + B_t x_t^T, y_t = C_t h_t has the adjoint state
+    g_t = a_{t+1} g_{t+1} + C_t dy_t^T (g_{L-1} also receives dssm_state_out),
+    and every gradient is the output of a scan of the same form, run by the
+    library's fp32 scan kernel on rearranged inputs:
+      dx_t = g_t^T B_t   : time-reversed scan, x' = dy, B' = C, C' = B,
+                           decay a'_u = a_{L-u} (a'_0 = 1), initial state dssm_state_out
+      dB_t = g_t x_t     : the same reversed scan with x' = C, B' = dy, C' = x
+      dC_t = h_t dy_t    : forward scan with x' = B, B' = x, C' = dy, initial state h0^T
+      dssm_state = a_0 g_0
+    and the log-decay gradient dla_t = <g_t, a_t h_{t-1}> telescopes (with
+    <g_t, h_t> = <g_{t+1}, a_{t+1} h_t> + dy_t . y_t) into a reverse cumulative sum:
+      dla_t = <dssm_state_out, h_{L-1}> + sum_{u >= t} (dy_u . y_u - B_u . dB_u).
+    ``dlog_a`` is returned when ``log_a`` was given (the decay came from it),
+    else ``dA_disc`` = dla / A_disc.  All arithmetic in fp32; the gradients have
+    the dtypes of their inputs.
+    """
+    dev = _same_device(("x", x), ("A_disc", A_disc), ("B", B), ("C", C), ("dy", dy),
+                       ("ssm_state", ssm_state), ("log_a", log_a),
+                       ("dssm_state_out", dssm_state_out))
+
+    def scan(xs, Bs, Cs, h0, la, want_state):
+        return selective_scan(xs, None, Bs, Cs, ssm_state=h0, log_a=la, out_dtype=torch.float32,
+                              write_ssm_state=want_state)
+
+    la = log_a.float() if log_a is not None else torch.log(torch.clamp(A_disc.float(), min=1e-10))
+    dx, dla, dB, dC, dh0 = _scan_backward(
+        scan, x.float().contiguous(), la, B.float(), C.float(), dy.float().contiguous(),
+        None if ssm_state is None else ssm_state.float(),
+        None if dssm_state_out is None else dssm_state_out.float(), dev)
+    dA = dla_out = None
+    if log_a is not None:
+        dla_out = dla.to(log_a.dtype)
+    else:
+        a = A_disc.float()
+        dA = torch.where(a > 1e-10, dla / a, torch.zeros_like(dla)).to(A_disc.dtype)
+    return (dx.to(x.dtype), dA, dB.to(B.dtype), dC.to(C.dtype),
+            None if ssm_state is None else dh0.to(ssm_state.dtype), dla_out)
+
+
+def _scan_backward(scan, x, la, B, C, dy, h0, dhT, device):
+    """The gradient algebra of ``selective_scan_backward`` over a scan callable
+    ``scan(x, B, C, h0, log_a, want_state) -> (y, final state or None)``
+    (B/C per head or per group, states [B, H, N, P] in any axis order)."""
+    Bsz, L, H, P = x.shape
+    G, N = B.shape[2], B.shape[3]
+    r = H // G
+    Bh = B.repeat_interleave(r, dim=2)          # per head [B, L, H, N]
+    Ch = C.repeat_interleave(r, dim=2)
+    if dhT is None:
+        dhT = torch.zeros((Bsz, H, N, P), dtype=x.dtype, device=device)
+    # the forward's outputs (y without D, and the final state)
+    y, hT = scan(x, Bh, Ch, h0, la, True)
+    # the reversed scans: step u is step L-1-u, its decay the one of step L-u
+    la_rev = torch.zeros_like(la)
+    la_rev[:, 1:] = la.flip(1)[:, :-1]
+    dy_r, B_r, C_r, x_r = dy.flip(1), Bh.flip(1), Ch.flip(1), x.flip(1)
+    dx_r, g0 = scan(dy_r, C_r, B_r, dhT, la_rev, True)
+    dB_r, _ = scan(C_r, dy_r, x_r, dhT.transpose(2, 3), la_rev, False)
+    dx, dBh = dx_r.flip(1), dB_r.flip(1)
+    dCh, _ = scan(Bh, x, dy, None if h0 is None else h0.transpose(2, 3), la, False)
+    # log-decay gradient: a reverse cumulative sum
+    s = (dy * y).sum(-1) - (Bh * dBh).sum(-1)           # [B, L, H]
+    dla = s.flip(1).cumsum(1).flip(1) + (dhT * hT).sum((-1, -2))[:, None, :]
+    dh0 = torch.exp(la[:, 0])[:, :, None, None] * g0
+    return (dx, dla, dBh.view(Bsz, L, G, r, N).sum(3), dCh.view(Bsz, L, G, r, N).sum(3), dh0)
+
+
+class SelectiveScan(torch.autograd.Function):
+    """``selective_scan`` with its gradient (``selective_scan_backward``), so
+    that training differentiates the scan as the reference's MLX autograd
+    differentiates ``_selective_scan`` (alloy/models/mamba_block.py:287-366).
+    Returns (y in x's dtype, final state fp32)."""
+
+    @staticmethod
+    def forward(ctx, x, A_disc, B, C, ssm_state, log_a):
+        y, h = selective_scan(x, A_disc, B, C, ssm_state=ssm_state, log_a=log_a)
+        ctx.save_for_backward(x, A_disc, B, C, ssm_state, log_a)
+        return y, h
+
+    @staticmethod
+    def backward(ctx, dy, dh):
+        x, A_disc, B, C, ssm_state, log_a = ctx.saved_tensors
+        if dy is None:
+            dy = torch.zeros(x.shape, dtype=x.dtype, device=x.device)
+        dx, dA, dB, dC, dh0, dla = selective_scan_backward(
+            x, A_disc if log_a is None else None, B, C, dy.contiguous(), ssm_state=ssm_state,
+            log_a=log_a, dssm_state_out=dh)
+        return dx, dA, dB, dC, dh0, dla
 
 
 def ssd_decode_step(xBC_tok, dt_tok, conv_weight, conv_bias, dt_bias, A_log, D, conv_state,

@@ -55,6 +55,9 @@ WORKLOADS = {
     # backward of conv1d + SiLU over the layer's xBC (training: the reference's custom VJP)
     "conv_bwd": dict(name="nemotron_h_8b_mamba2_conv1d_silu_backward", B=4, L=8192, H=128, P=64,
                      N=128, G=8, K=4, Q=256),
+    # the scan's backward (training) at the Zamba2 layer shape, fp32
+    "scan_bwd": dict(name="zamba2_1.2b_mamba2_selective_scan_backward", B=8, L=4096, H=64, P=64,
+                     N=64, G=1, K=4, Q=256),
     # one whole Mamba layer (projections, cached step, gate + norm) decoding at batch 1
     "decode_block": dict(name="nemotron_h_8b_mamba2_layer_decode_b1", B=1, L=64, H=128, P=64,
                          N=128, G=8, K=4, Q=256),
@@ -554,6 +557,69 @@ def run_conv(args, w):
         dist.destroy_process_group()
 
 
+def run_scan_bwd(args, w):
+    """Backward of the selective scan (``mixer.selective_scan_backward``: the
+    forward recomputed, two time-reversed scans and one forward scan on the fp32
+    CUDA-core scan kernel, the log-decay gradient as a reverse cumulative sum)
+    on fp32 inputs of the workload's shape; tokens/s of the backward.  Batch
+    rows split over the GPUs."""
+    import torch
+    from alloy_b200 import _lib, mixer
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    B, L, H, P, N, G = w["B"], w["L"], w["H"], w["P"], w["N"], w["G"]
+    if B % world:
+        raise SystemExit("batch rows do not split over the GPUs")
+    Bl = B // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(41 + rank)
+    x = torch.randn((Bl, L, H, P), generator=gen, device=dev) * 0.5
+    Bm = torch.randn((Bl, L, G, N), generator=gen, device=dev)
+    Cm = torch.randn((Bl, L, G, N), generator=gen, device=dev)
+    la = -torch.rand((Bl, L, H), generator=gen, device=dev) * 0.1
+    dy = torch.randn((Bl, L, H, P), generator=gen, device=dev)
+
+    def step(i):
+        mixer.selective_scan_backward(x, None, Bm, Cm, dy, log_a=la)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    h0 = time.perf_counter()
+    launches0 = _lib.load().alloy_kernel_launch_count()
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    launches = _lib.load().alloy_kernel_launch_count() - launches0
+    torch.cuda.synchronize()
+    h1 = time.perf_counter()
+    barrier(world)
+    clocks.stop()
+    ms = dist_max(ev0.elapsed_time(ev1) / args.steps, world)
+    tokens = B * L
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Mamba-2 selective scan backward tokens/s (fp32)",
+            "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": w["name"], "batch": B, "seq_len": L, "n_heads": H,
+                       "head_dim": P, "d_state": N, "n_groups": G,
+                       "path": "4 fp32 CUDA-core scans + reverse cumulative sum"},
+            "gpu_launches": launches, "clocks": clocks.summary(h0, h1)}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def run_conv_bwd(args, w):
     """Backward of conv1d + SiLU over the layer's xBC (conv_dim = H P + 2 G N
     channels): dx_padded, dweight, dbias from dy.  Batch rows split over the
@@ -932,6 +998,8 @@ def main():
         run_conv_bwd(args, w)
     elif args.workload == "conv":
         run_conv(args, w)
+    elif args.workload == "scan_bwd":
+        run_scan_bwd(args, w)
     else:
         run_ours(args, w)
 

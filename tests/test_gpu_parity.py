@@ -588,3 +588,95 @@ def test_tensor_core_ssd_is_deterministic_and_chunk_independent():
     y_cat = torch.cat([ya, yb], dim=1)
     assert oracle.rel_l2(np_(y_cat), np_(y1)) < 2e-3
     assert oracle.rel_l2(np_(hb), np_(h1)) < 2e-3
+
+
+# ------------------------------------------------------------- training (backward)
+def _scan64(x, A_log_decay, B, C, h0):
+    """float64 per-step recurrence (mamba_block.py:160-204) with autograd."""
+    b, L, H, _ = x.shape
+    r = H // B.shape[2]
+    Bh, Ch = B.repeat_interleave(r, 2), C.repeat_interleave(r, 2)
+    h = h0
+    ys = []
+    for t in range(L):
+        h = torch.exp(A_log_decay[:, t])[:, :, None, None] * h + Bh[:, t, :, :, None] * x[:, t, :, None, :]
+        ys.append((Ch[:, t, :, :, None] * h).sum(2))
+    return torch.stack(ys, 1), h
+
+
+@pytest.mark.parametrize("cfg", [dict(b=2, L=70, H=4, P=16, N=8, G=2, log=False),
+                                 dict(b=1, L=129, H=2, P=32, N=16, G=1, log=True)])
+def test_selective_scan_backward_vs_fp64_autograd(cfg):
+    g = torch.Generator().manual_seed(5)
+    b, L, H, P, N, G = (cfg[k] for k in ("b", "L", "H", "P", "N", "G"))
+    x = torch.randn(b, L, H, P, generator=g) * 0.5
+    Bm, Cm = torch.randn(b, L, G, N, generator=g), torch.randn(b, L, G, N, generator=g)
+    la = -torch.rand(b, L, H, generator=g) * 0.3
+    h0 = torch.randn(b, H, N, P, generator=g) * 0.3
+    U, V = torch.randn(b, L, H, P, generator=g), torch.randn(b, H, N, P, generator=g)
+    # float64 reference
+    leaves = [t.double().requires_grad_() for t in (x, la, Bm, Cm, h0)]
+    y64, h64 = _scan64(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4])
+    ((y64 * U.double()).sum() + (h64 * V.double()).sum()).backward()
+    # the library: A_disc or log_a input
+    xs = [t.to(DEV).requires_grad_() for t in (x, la.exp() if not cfg["log"] else la, Bm, Cm, h0)]
+    if cfg["log"]:
+        y, h = mixer.SelectiveScan.apply(xs[0], None, xs[2], xs[3], xs[4], xs[1])
+    else:
+        y, h = mixer.SelectiveScan.apply(xs[0], xs[1], xs[2], xs[3], xs[4], None)
+    ((y * U.to(DEV)).sum() + (h * V.to(DEV)).sum()).backward()
+    assert_close(np_(y), y64.detach().numpy(), False)
+    dla = xs[1].grad * (1.0 if cfg["log"] else xs[1].detach())   # d/dla = A d/dA
+    for got, ref in ((xs[0].grad, leaves[0].grad), (dla, leaves[1].grad), (xs[2].grad, leaves[2].grad),
+                     (xs[3].grad, leaves[3].grad), (xs[4].grad, leaves[4].grad)):
+        assert_close(np_(got), ref.numpy(), False)
+
+
+def test_combined_block_training_gradients_vs_fp64():
+    """MambaBlock (combined projection, inner norm) under autograd: the forward
+    equals the fused inference path, and every parameter's gradient matches a
+    float64 torch restatement of the layer (conv, split, discretisation,
+    per-step scan, D, gate, RMSNorm, projections)."""
+    torch.manual_seed(7)
+    blk = MambaBlock(d_model=64, d_state=16, d_conv=4, expand=2, headdim=32, chunk_size=16,
+                     combined_proj=True, n_groups=2, use_D=True, use_inner_norm=True,
+                     device=DEV, dtype=torch.float32)
+    with torch.no_grad():
+        blk.A_log.uniform_(0, 2)
+        blk.dt_bias.uniform_(-3, -1)
+        blk.D.normal_()
+        blk.conv_weight.normal_(0, 0.5)
+        blk.conv_bias.normal_(0, 0.1)
+    x = torch.randn(2, 45, 64, device=DEV)
+    U = torch.randn(2, 45, 64, device=DEV)
+    with torch.no_grad():
+        y_inf = blk(x)
+    x_t = x.clone().requires_grad_()
+    y = blk(x_t)
+    assert_close(np_(y), np_(y_inf), False)
+    (y * U).sum().backward()
+
+    # float64 restatement
+    p = {n: t.detach().double().cpu().requires_grad_() for n, t in blk.named_parameters()}
+    x64 = x.detach().double().cpu().requires_grad_()
+    H, P, N, G, K, Di = blk.n_heads, blk.headdim, blk.d_state, blk.n_groups, blk.d_conv, blk.d_inner
+    proj = x64 @ p["in_proj.weight"].T
+    gate, xBC, dt = proj[..., :Di], proj[..., Di:Di + blk.conv_dim], proj[..., Di + blk.conv_dim:]
+    xp = torch.nn.functional.pad(xBC, (0, 0, K - 1, 0))
+    L = x.shape[1]
+    conv = sum(xp[:, k:k + L] * p["conv_weight"][:, k] for k in range(K)) + p["conv_bias"]
+    conv = torch.nn.functional.silu(conv)
+    xs, Bm, Cm = conv.split([H * P, G * N, G * N], dim=-1)
+    xh = xs.reshape(2, L, H, P)
+    dtv = torch.nn.functional.softplus(dt + p["dt_bias"])
+    la = dtv * -torch.exp(p["A_log"])
+    ys, _ = _scan64(xh * dtv[..., None], la, Bm.reshape(2, L, G, N), Cm.reshape(2, L, G, N),
+                    torch.zeros(2, H, N, P, dtype=torch.float64))
+    yy = (ys + p["D"][:, None] * xh).reshape(2, L, Di) * torch.nn.functional.silu(gate)
+    yy = yy * torch.rsqrt((yy * yy).mean(-1, keepdim=True) + 1e-5) * p["norm.weight"]
+    out = yy @ p["out_proj.weight"].T
+    (out * U.double().cpu()).sum().backward()
+    assert_close(np_(y), out.detach().numpy(), False)
+    assert_close(np_(x_t.grad), x64.grad.numpy(), False)
+    for n, t in blk.named_parameters():
+        assert_close(np_(t.grad), p[n].grad.numpy(), False), n

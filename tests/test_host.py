@@ -120,3 +120,42 @@ def test_streamed_prefill_rejects_unpinned_or_device_activations():
     with pytest.raises(ValueError, match="CPU tensor"):
         mixer.ssd_combined_streamed(None, dt, None, None, None, None, None, n_heads=8,
                                     head_dim=32, d_state=16, n_groups=1)
+
+
+def _torch_scan(x, B, C, h0, la, want_state):
+    """The per-step recurrence h_t = exp(la_t) h_{t-1} + B_t x_t^T, y_t = C_t h_t
+    (alloy/models/mamba_block.py:160-204), float64 on the CPU."""
+    b, L, H, _ = x.shape
+    G = B.shape[2]
+    Bh, Ch = B.repeat_interleave(H // G, 2), C.repeat_interleave(H // G, 2)
+    h = torch.zeros(b, H, B.shape[3], x.shape[3], dtype=x.dtype) if h0 is None else h0.clone()
+    ys = []
+    for t in range(L):
+        h = torch.exp(la[:, t])[:, :, None, None] * h + Bh[:, t, :, :, None] * x[:, t, :, None, :]
+        ys.append((Ch[:, t, :, :, None] * h).sum(2))
+    return torch.stack(ys, 1), (h if want_state else None)
+
+
+@pytest.mark.parametrize("with_state", [False, True])
+def test_scan_gradient_algebra_matches_autograd(with_state):
+    # the decomposition selective_scan_backward runs on the GPU (three
+    # rearranged scans and a reverse cumulative sum), here over a float64 scan
+    from alloy_b200 import mixer
+    g = torch.Generator().manual_seed(3)
+    b, L, H, P, N, G = 2, 23, 4, 5, 3, 2
+    r = lambda *s: torch.randn(*s, generator=g, dtype=torch.float64)
+    x, B, C = r(b, L, H, P), r(b, L, G, N), r(b, L, G, N)
+    la = -torch.rand(b, L, H, generator=g, dtype=torch.float64)
+    h0 = r(b, H, N, P) if with_state else None
+    U, V = r(b, L, H, P), r(b, H, N, P)
+    leaves = [t.clone().requires_grad_() for t in (x, B, C, la)] + (
+        [h0.clone().requires_grad_()] if with_state else [])
+    y, hT = _torch_scan(leaves[0], leaves[1], leaves[2], leaves[4] if with_state else None,
+                        leaves[3], True)
+    ((y * U).sum() + (hT * V).sum()).backward()
+    dx, dla, dB, dC, dh0 = mixer._scan_backward(_torch_scan, x, la, B, C, U, h0, V, "cpu")
+    got = [dx, dB, dC, dla] + ([dh0] if with_state else [])
+    want = [leaves[0].grad, leaves[1].grad, leaves[2].grad, leaves[3].grad] + (
+        [leaves[4].grad] if with_state else [])
+    for gt, wt in zip(got, want):
+        assert torch.allclose(gt, wt, rtol=1e-9, atol=1e-9), (gt - wt).abs().max()
