@@ -154,6 +154,50 @@ __global__ void __launch_bounds__(kThreads) ssd_simt_kernel(const SsdArgs a) {
     __syncthreads();
     if (tid < QS) av[tid] = tid < qn ? expf(cl - cum[tid]) : 0.f;
     // ---- outputs -----------------------------------------------------------
+    if ((P & 3) == 0 && (N & 3) == 0) {
+      // register tiles of 4 steps x 2 columns: per reduction index one float2
+      // of x (or h) and 4 broadcast scalars of W (or C) feed 8 FMAs
+      const int ntile = (QS / 4) * (P / 2);
+      for (int tile = tid; tile < ntile; tile += kThreads) {
+        const int pp = (tile % (P / 2)) * 2, t0r = (tile / (P / 2)) * 4;
+        if (t0r >= qn) continue;
+        float intra[4][2], inter[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) intra[i][0] = intra[i][1] = inter[i][0] = inter[i][1] = 0.f;
+        const int smax = min(t0r + 4, qn);
+        for (int s2 = 0; s2 < smax; ++s2) {   // W is zero above the diagonal
+          const float2 xv = *reinterpret_cast<const float2*>(xs + s2 * P + pp);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float wv = W[(t0r + i) * QS + s2];
+            intra[i][0] = fmaf(wv, xv.x, intra[i][0]);
+            intra[i][1] = fmaf(wv, xv.y, intra[i][1]);
+          }
+        }
+        for (int n = 0; n < N; ++n) {
+          const float2 hv = *reinterpret_cast<const float2*>(hs + n * P + pp);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float cv = Cs[(t0r + i) * N + n];
+            inter[i][0] = fmaf(cv, hv.x, inter[i][0]);
+            inter[i][1] = fmaf(cv, hv.y, inter[i][1]);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int t = t0r + i;
+          if (t >= qn) break;
+          const float e = expf(cum[t]);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            float yv = fmaf(e, inter[i][j], intra[i][j]);
+            if (a.mode == 0) yv = fmaf(Dh, xu[t * P + pp + j], yv);
+            store_any(a.y, b * a.y_sb + (int64_t)(t0 + t) * a.y_st + h * a.y_sh + (pp + j) * a.y_sp,
+                      a.y_bf16, yv);
+          }
+        }
+      }
+    } else
     for (int i = tid; i < qn * P; i += kThreads) {
       const int t = i / P, p = i % P;
       float intra = 0.f;
@@ -168,6 +212,42 @@ __global__ void __launch_bounds__(kThreads) ssd_simt_kernel(const SsdArgs a) {
     __syncthreads();
     // ---- state update --------------------------------------------------------
     const float dl = expf(cl);
+    if ((P & 3) == 0 && (N & 3) == 0) {
+      // B_s decayed to the chunk end, transposed to [s][n] in the C buffer (read
+      // by the outputs above, complete at the barrier), then register tiles of
+      // 4 n x 4 p: per step one float4 of it and one of x feed 16 FMAs
+      float* Bv = Cs;
+      for (int i = tid; i < QS * N; i += kThreads) {
+        const int s2 = i / N, n = i % N;
+        Bv[i] = Bs[n * QS + s2] * av[s2];
+      }
+      __syncthreads();
+      const int ntile = (N / 4) * (P / 4);
+      for (int tile = tid; tile < ntile; tile += kThreads) {
+        const int p4 = (tile % (P / 4)) * 4, n4 = (tile / (P / 4)) * 4;
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+        for (int s2 = 0; s2 < qn; ++s2) {
+          const float4 bv = *reinterpret_cast<const float4*>(Bv + s2 * N + n4);
+          const float4 xv = *reinterpret_cast<const float4*>(xs + s2 * P + p4);
+          const float bb[4] = {bv.x, bv.y, bv.z, bv.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(bb[i], xx[j], acc[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float4* hrow = reinterpret_cast<float4*>(hs + (n4 + i) * P + p4);
+          const float4 ho = *hrow;
+          *hrow = make_float4(fmaf(dl, ho.x, acc[i][0]), fmaf(dl, ho.y, acc[i][1]),
+                              fmaf(dl, ho.z, acc[i][2]), fmaf(dl, ho.w, acc[i][3]));
+        }
+      }
+    } else
     for (int i = tid; i < N * P; i += kThreads) {
       const int n = i / P, p = i % P;
       float acc = 0.f;
