@@ -328,7 +328,7 @@ def check_device_status(device=None):
 
 
 def selective_scan(x, A_disc, B, C, ssm_state=None, log_a=None, out=None, out_dtype=None,
-                   ssm_state_out=None, write_ssm_state=True):
+                   ssm_state_out=None, write_ssm_state=True, reverse_time=False):
     """Scan on pre-discretised inputs (``MambaBlock._selective_scan``,
     alloy/models/mamba_block.py:287-366).
 
@@ -336,7 +336,9 @@ def selective_scan(x, A_disc, B, C, ssm_state=None, log_a=None, out=None, out_dt
     dividing H (G' = H for the reference's per-head repeated B/C), ssm_state
     [B, H, N, P] fp32 or None.  ``log_a`` (fp32), when given, is used in
     place of log(A_disc).  Returns (y, ssm_state_out); y has ``out_dtype``
-    (default: x's dtype).
+    (default: x's dtype).  ``reverse_time`` runs the scan from step L-1 down
+    to step 0 (the library walks every time-indexed tensor with a negative
+    time stride; y is still indexed by step), as the gradient scans need.
     """
     dev = _same_device(("x", x), ("A_disc", A_disc), ("B", B), ("C", C),
                        ("ssm_state", ssm_state), ("log_a", log_a), ("out", out),
@@ -354,6 +356,11 @@ def selective_scan(x, A_disc, B, C, ssm_state=None, log_a=None, out=None, out_dt
     args = [(x, "x"), (A_disc, "A_disc"), (_f32(log_a), "log_a"), (B, "B"), (C, "C"),
             (ssm_state, "ssm_state"), (out, "y"), (ssm_state_out, "ssm_state_out")]
     descs = [_lib.desc(t, n) for t, n in args]
+    if reverse_time and L > 1:
+        for (t, name), d in zip(args, descs):
+            if t is not None and name not in ("ssm_state", "ssm_state_out"):
+                d.data += (L - 1) * t.stride(1) * t.element_size()
+                d.stride[1] = -t.stride(1)
     with torch.cuda.device(dev):
         _lib.call("alloy_selective_scan", *(_lib.ref(d) for d in descs), _lib.stream_handle(dev))
     return out, ssm_state_out
@@ -386,9 +393,9 @@ def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dss
                        ("ssm_state", ssm_state), ("log_a", log_a),
                        ("dssm_state_out", dssm_state_out))
 
-    def scan(xs, Bs, Cs, h0, la, want_state):
+    def scan(xs, Bs, Cs, h0, la, want_state, reverse):
         return selective_scan(xs, None, Bs, Cs, ssm_state=h0, log_a=la, out_dtype=torch.float32,
-                              write_ssm_state=want_state)
+                              write_ssm_state=want_state, reverse_time=reverse)
 
     la = log_a.float() if log_a is not None else torch.log(torch.clamp(A_disc.float(), min=1e-10))
     dx, dla, dB, dC, dh0 = _scan_backward(
@@ -407,8 +414,9 @@ def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dss
 
 def _scan_backward(scan, x, la, B, C, dy, h0, dhT, device):
     """The gradient algebra of ``selective_scan_backward`` over a scan callable
-    ``scan(x, B, C, h0, log_a, want_state) -> (y, final state or None)``
-    (B/C per head or per group, states [B, H, N, P] in any axis order)."""
+    ``scan(x, B, C, h0, log_a, want_state, reverse) -> (y, final state or None)``
+    (B/C per head or per group, states [B, H, N, P] in any axis order; with
+    ``reverse`` the scan walks steps L-1 .. 0 of its step-indexed inputs)."""
     Bsz, L, H, P = x.shape
     G, N = B.shape[2], B.shape[3]
     r = H // G
@@ -417,18 +425,18 @@ def _scan_backward(scan, x, la, B, C, dy, h0, dhT, device):
     if dhT is None:
         dhT = torch.zeros((Bsz, H, N, P), dtype=x.dtype, device=device)
     # the forward's outputs (y without D, and the final state)
-    y, hT = scan(x, Bh, Ch, h0, la, True)
-    # the reversed scans: step u is step L-1-u, its decay the one of step L-u
-    la_rev = torch.zeros_like(la)
-    la_rev[:, 1:] = la.flip(1)[:, :-1]
-    dy_r, B_r, C_r, x_r = dy.flip(1), Bh.flip(1), Ch.flip(1), x.flip(1)
-    dx_r, g0 = scan(dy_r, C_r, B_r, dhT, la_rev, True)
-    dB_r, _ = scan(C_r, dy_r, x_r, dhT.transpose(2, 3), la_rev, False)
-    dx, dBh = dx_r.flip(1), dB_r.flip(1)
-    dCh, _ = scan(Bh, x, dy, None if h0 is None else h0.transpose(2, 3), la, False)
-    # log-decay gradient: a reverse cumulative sum
-    s = (dy * y).sum(-1) - (Bh * dBh).sum(-1)           # [B, L, H]
-    dla = s.flip(1).cumsum(1).flip(1) + (dhT * hT).sum((-1, -2))[:, None, :]
+    y, hT = scan(x, Bh, Ch, h0, la, True, False)
+    # the reversed scans walk steps L-1 .. 0; the decay applied on reaching step
+    # t is the one of step t+1 (none at the first step taken, t = L-1)
+    la_next = torch.zeros_like(la)
+    la_next[:, :-1] = la[:, 1:]
+    dx, g0 = scan(dy, Ch, Bh, dhT, la_next, True, True)
+    dBh, _ = scan(Ch, dy, x, dhT.transpose(2, 3), la_next, False, True)
+    dCh, _ = scan(Bh, x, dy, None if h0 is None else h0.transpose(2, 3), la, False, False)
+    # log-decay gradient: a reverse cumulative sum over the steps (along the
+    # last dimension of a [B, H, L] copy)
+    s = ((dy * y).sum(-1) - (Bh * dBh).sum(-1)).transpose(1, 2).contiguous()   # [B, H, L]
+    dla = s.flip(-1).cumsum(-1).flip(-1).transpose(1, 2) + (dhT * hT).sum((-1, -2))[:, None, :]
     dh0 = torch.exp(la[:, 0])[:, :, None, None] * g0
     return (dx, dla, dBh.view(Bsz, L, G, r, N).sum(3), dCh.view(Bsz, L, G, r, N).sum(3), dh0)
 

@@ -122,9 +122,13 @@ def test_streamed_prefill_rejects_unpinned_or_device_activations():
                                     head_dim=32, d_state=16, n_groups=1)
 
 
-def _torch_scan(x, B, C, h0, la, want_state):
+def _torch_scan(x, B, C, h0, la, want_state, reverse=False):
     """The per-step recurrence h_t = exp(la_t) h_{t-1} + B_t x_t^T, y_t = C_t h_t
-    (alloy/models/mamba_block.py:160-204), float64 on the CPU."""
+    (alloy/models/mamba_block.py:160-204), float64 on the CPU; ``reverse``
+    walks the steps from the last."""
+    if reverse:
+        y, h = _torch_scan(x.flip(1), B.flip(1), C.flip(1), h0, la.flip(1), want_state)
+        return y.flip(1), h
     b, L, H, _ = x.shape
     G = B.shape[2]
     Bh, Ch = B.repeat_interleave(H // G, 2), C.repeat_interleave(H // G, 2)
@@ -151,7 +155,7 @@ def test_scan_gradient_algebra_matches_autograd(with_state):
     leaves = [t.clone().requires_grad_() for t in (x, B, C, la)] + (
         [h0.clone().requires_grad_()] if with_state else [])
     y, hT = _torch_scan(leaves[0], leaves[1], leaves[2], leaves[4] if with_state else None,
-                        leaves[3], True)
+                        leaves[3], True, False)
     ((y * U).sum() + (hT * V).sum()).backward()
     dx, dla, dB, dC, dh0 = mixer._scan_backward(_torch_scan, x, la, B, C, U, h0, V, "cpu")
     got = [dx, dB, dC, dla] + ([dh0] if with_state else [])
