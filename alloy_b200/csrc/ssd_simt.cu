@@ -141,6 +141,29 @@ __global__ void __launch_bounds__(kThreads) ssd_simt_kernel(const SsdArgs a) {
     __syncthreads();
     const float cl = cum[qn - 1];
     // ---- decay-masked scores W and chunk-end decay per step ---------------
+    if ((N & 3) == 0) {
+      // 4 consecutive sources s of one step t a thread: per n one broadcast C
+      // and one float4 of B (stored [n][s]) feed 4 FMAs
+      for (int i = tid; i < QS * QS / 4; i += kThreads) {
+        const int t = i / (QS / 4), s4 = (i % (QS / 4)) * 4;
+        float dot[4] = {0.f, 0.f, 0.f, 0.f};
+        if (s4 <= t) {
+          for (int n = 0; n < N; ++n) {
+            const float cv = Cs[t * N + n];
+            const float4 bv = *reinterpret_cast<const float4*>(Bs + n * QS + s4);
+            dot[0] = fmaf(cv, bv.x, dot[0]);
+            dot[1] = fmaf(cv, bv.y, dot[1]);
+            dot[2] = fmaf(cv, bv.z, dot[2]);
+            dot[3] = fmaf(cv, bv.w, dot[3]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int s2 = s4 + j;
+          W[t * QS + s2] = s2 <= t ? dot[j] * expf(cum[t] - cum[s2]) : 0.f;
+        }
+      }
+    } else
     for (int i = tid; i < QS * QS; i += kThreads) {
       const int t = i / QS, s = i % QS;
       float v = 0.f;
