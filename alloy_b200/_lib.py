@@ -50,6 +50,7 @@ EXPORTS = (
     "alloy_gated_rmsnorm",
     "alloy_conv1d_silu_backward",
     "alloy_conv1d_silu_backward_workspace_size",
+    "alloy_decode_linear",
 )
 
 
@@ -120,6 +121,8 @@ def load():
         lib.alloy_conv1d_silu_backward.argtypes = [P] * 7 + [vp, ctypes.c_size_t, vp]
         lib.alloy_conv1d_silu_backward_workspace_size.argtypes = [ctypes.c_int64] * 4
         lib.alloy_conv1d_silu_backward_workspace_size.restype = ctypes.c_size_t
+        lib.alloy_decode_linear.argtypes = [P, P, P, vp]
+        lib.alloy_decode_linear.restype = ctypes.c_int
         lib.alloy_ssd_combined.argtypes = [P] * 12 + [vp, ctypes.c_size_t, D, vp]
         lib.alloy_ssd_combined_workspace_size.argtypes = [ctypes.c_int64, ctypes.c_int64,
                                                           ctypes.c_int32, D]

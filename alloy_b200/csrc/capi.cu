@@ -186,6 +186,30 @@ int alloy_conv1d_silu_backward(const alloy_tensor_t* x_padded, const alloy_tenso
                               (int)(Lp - K + 1), (int)C, (int)K, as_stream(stream));
 }
 
+int alloy_decode_linear(const alloy_tensor_t* x, const alloy_tensor_t* weight, alloy_tensor_t* y,
+                        void* stream) {
+  last_error().clear();
+  ALLOY_TRY(check_tensor(x, "x", 2, nullptr, kBF16));
+  ALLOY_TRY(check_tensor(weight, "weight", 2, nullptr, kBF16));
+  const int64_t NB = x->shape[0], in = x->shape[1], out = weight->shape[0];
+  if (weight->shape[1] != in)
+    return fail(ALLOY_ERR_INVALID_ARG, "weight: dim 1 is %lld, expected in = %lld",
+                (long long)weight->shape[1], (long long)in);
+  const int64_t ys[2] = {NB, out};
+  ALLOY_TRY(check_tensor(y, "y", 2, ys, kBF16));
+  if (NB < 1 || NB > 4) return fail(ALLOY_ERR_UNSUPPORTED, "decode_linear: 1 to 4 rows, got %lld", (long long)NB);
+  if (in % 8 != 0 || in * NB * 2 > 200 * 1024)
+    return fail(ALLOY_ERR_UNSUPPORTED, "decode_linear: in must be a multiple of 8 and rows fit shared memory");
+  if (x->stride[1] != 1 || weight->stride[1] != 1 || y->stride[1] != 1)
+    return fail(ALLOY_ERR_INVALID_ARG, "decode_linear: the last dimension must be contiguous");
+  if (!aligned16(x->data) || !aligned16(weight->data) || (x->stride[0] * 2) % 16 != 0 ||
+      (weight->stride[0] * 2) % 16 != 0)
+    return fail(ALLOY_ERR_ALIGNMENT, "decode_linear: x and weight rows must be 16-byte aligned");
+  if (out > (int64_t)1 << 30) return fail(ALLOY_ERR_UNSUPPORTED, "decode_linear: too many outputs");
+  ALLOY_TRY(current_device_checked(nullptr));
+  return decode_linear(x, weight, y, as_stream(stream));
+}
+
 int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t* dt_raw,
                        const alloy_tensor_t* conv_w, const alloy_tensor_t* conv_b,
                        const alloy_tensor_t* dt_bias, const alloy_tensor_t* A_log,

@@ -9,6 +9,11 @@
 // phase 2 streams the fp32 state of the group's heads once: 16-byte loads,
 // s' = exp(A dt) s + dt x B^T, y = C s' + D x, 16-byte stores.  The state
 // traffic (read + write of [heads, N, P] fp32) is the whole cost.
+//
+// When the batch is small (fewer (row, group) pairs than SMs) each group's
+// heads are split over several CTAs so that the state streams from most of
+// the SMs.  The B and C channels are then read by every slice of the group,
+// so the slices leave them unrolled and a second small kernel rolls them.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -149,12 +154,17 @@ __device__ __forceinline__ void state_rows_np(const DecodeArgs& a, float* st, co
 }
 
 template <int NV>
-__global__ void __launch_bounds__(kThreads) decode_step_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kThreads) decode_step_kernel(const DecodeArgs a, int hsplit, int roll_bc) {
   const int b = blockIdx.y;
   const int hpg = a.H / a.G;
-  const int g = a.head_begin / hpg + blockIdx.x;
-  const int hb = max(a.head_begin, g * hpg);
-  const int he = min(a.head_begin + a.head_count, (g + 1) * hpg);
+  const int g = a.head_begin / hpg + blockIdx.x / hsplit;
+  const int gb = max(a.head_begin, g * hpg);
+  const int ge = min(a.head_begin + a.head_count, (g + 1) * hpg);
+  // this CTA's slice of the group's heads (the whole group when hsplit == 1)
+  const int per = (ge - gb + hsplit - 1) / hsplit;
+  const int hb = gb + (blockIdx.x % hsplit) * per;
+  const int he = min(ge, hb + per);
+  if (hb >= he) return;
   const int nh = he - hb;
   const int P = a.P, N = a.N, K = a.K;
 
@@ -165,7 +175,10 @@ __global__ void __launch_bounds__(kThreads) decode_step_kernel(const DecodeArgs 
   float* Cs = Bs + n4;             // [N]
   float* xs = Cs + n4;             // [nh][P]
 
-  // ---- phase 1: conv-cache roll + conv + SiLU for this group's channels ----
+  // ---- phase 1: conv + SiLU for this CTA's channels ----------------------
+  // The CTA rolls the conv cache of its own x channels.  The group's B and C
+  // channels are shared by every slice of the group: with roll_bc == 0 they
+  // are only read here and decode_bc_roll_kernel rolls them afterwards.
   const int nx = nh * P;
   const int nch = nx + 2 * N;
   for (int i = threadIdx.x; i < nch; i += kThreads) {
@@ -178,7 +191,8 @@ __global__ void __launch_bounds__(kThreads) decode_step_kernel(const DecodeArgs 
     win[K - 1] = load_any(a.xbc, b * a.x_sb + c, a.x_bf16);
     float acc = a.conv_b ? a.conv_b[c * a.cb_s] : 0.f;
     for (int k = 0; k < K; ++k) acc = fmaf(win[k], a.conv_w[c * a.cw_sc + k * a.cw_sk], acc);
-    for (int k = 0; k < K - 1; ++k) store_any(a.conv_state, cs_base + k * a.cs_sk, a.cs_bf16, win[k + 1]);
+    if (i < nx || roll_bc)
+      for (int k = 0; k < K - 1; ++k) store_any(a.conv_state, cs_base + k * a.cs_sk, a.cs_bf16, win[k + 1]);
     const float v = silu_f32(acc);
     if (i < nx) xs[i] = v;
     else if (i < nx + N) Bs[i - nx] = v;
@@ -203,17 +217,47 @@ __global__ void __launch_bounds__(kThreads) decode_step_kernel(const DecodeArgs 
   }
 }
 
+// Conv-cache roll of the B and C channels of groups g0 .. g0 + ngroups - 1,
+// after decode_step_kernel has read them (split-head launches): one thread
+// per (batch row, channel).
+__global__ void __launch_bounds__(kThreads) decode_bc_roll_kernel(const DecodeArgs a, int g0, int ngroups) {
+  const int per_row = 2 * ngroups * a.N;
+  const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  if (i >= (int64_t)a.B * per_row) return;
+  const int b = (int)(i / per_row), r = (int)(i % per_row);
+  const int which = r / (ngroups * a.N), q = r % (ngroups * a.N);  // 0: B, 1: C
+  const int c = a.H * a.P + which * a.G * a.N + g0 * a.N + q;
+  const int64_t cs_base = b * a.cs_sb + (int64_t)c * a.cs_sc;
+  for (int k = 0; k + 1 < a.K - 1; ++k)
+    store_any(a.conv_state, cs_base + k * a.cs_sk, a.cs_bf16,
+              load_any(a.conv_state, cs_base + (k + 1) * a.cs_sk, a.cs_bf16));
+  if (a.K >= 2)
+    store_any(a.conv_state, cs_base + (a.K - 2) * a.cs_sk, a.cs_bf16, load_any(a.xbc, b * a.x_sb + c, a.x_bf16));
+}
+
 }  // namespace
 
 int ssd_decode_step(const DecodeArgs& a, cudaStream_t s) {
   if (a.B == 0 || a.head_count == 0) return ALLOY_OK;
   const int hpg = a.H / a.G;
   const int g0 = a.head_begin / hpg, g1 = (a.head_begin + a.head_count - 1) / hpg;
+  const int ngroups = g1 - g0 + 1;
   const int max_heads = std::min(hpg, a.head_count);
-  const size_t smem = sizeof(float) * ((size_t)max_heads * a.P + 2 * ((a.N + 3) & ~3) + kThreads * 4);
+  // Few (batch row, group) pairs leave most SMs idle: split each group's heads
+  // over several CTAs, aiming at two CTAs an SM of a 148-SM part.
+  const int64_t pairs = (int64_t)ngroups * a.B;
+  int hsplit = 1;
+  if (pairs < 148) {
+    hsplit = (int)std::min<int64_t>(max_heads, (296 + pairs - 1) / pairs);
+    const int per = (max_heads + hsplit - 1) / hsplit;
+    hsplit = (max_heads + per - 1) / per;
+  }
+  const int slice_heads = (max_heads + hsplit - 1) / hsplit;
+  const size_t smem = sizeof(float) * ((size_t)slice_heads * a.P + 2 * ((a.N + 3) & ~3) + kThreads * 4);
   if (smem > 200 * 1024)
     return fail(ALLOY_ERR_UNSUPPORTED, "decode: heads per group * head_dim too large");
-  dim3 grid(g1 - g0 + 1, a.B);
+  dim3 grid(ngroups * hsplit, a.B);
+  const int roll_bc = hsplit == 1;
   // vectorised PN rows need 16-byte aligned rows of N floats
   const bool pn_vec = a.state_pn && (a.N % 4 == 0) && (a.st_row % 4 == 0) &&
                       ((reinterpret_cast<uintptr_t>(a.state) & 15) == 0) &&
@@ -223,7 +267,7 @@ int ssd_decode_step(const DecodeArgs& a, cudaStream_t s) {
   do {                                                                                       \
     ALLOY_CUDA(cudaFuncSetAttribute(decode_step_kernel<NVV>,                                 \
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
-    decode_step_kernel<NVV><<<grid, kThreads, smem, s>>>(a);                                 \
+    decode_step_kernel<NVV><<<grid, kThreads, smem, s>>>(a, hsplit, roll_bc);                \
   } while (0)
   switch (nv) {
     case 4: ALLOY_DEC(4); break;
@@ -233,7 +277,11 @@ int ssd_decode_step(const DecodeArgs& a, cudaStream_t s) {
     default: ALLOY_DEC(0); break;
   }
 #undef ALLOY_DEC
-  return check_launch("decode_step_kernel");
+  int rc = check_launch("decode_step_kernel");
+  if (rc != ALLOY_OK || roll_bc) return rc;
+  const int64_t n = (int64_t)a.B * 2 * ngroups * a.N;
+  decode_bc_roll_kernel<<<(unsigned)((n + kThreads - 1) / kThreads), kThreads, 0, s>>>(a, g0, ngroups);
+  return check_launch("decode_bc_roll_kernel");
 }
 
 }  // namespace alloy

@@ -18,6 +18,9 @@ int conv1d_silu_backward(const alloy_tensor_t* x_padded, const alloy_tensor_t* w
                          alloy_tensor_t* dw, alloy_tensor_t* db, void* workspace, int B, int L, int C,
                          int K, cudaStream_t s);
 
+// linear.cu: y [NB, out] = x [NB, in] W^T for NB <= 4 bf16 tokens (decode projections)
+int decode_linear(const alloy_tensor_t* x, const alloy_tensor_t* w, alloy_tensor_t* y, cudaStream_t s);
+
 // Flattened view of one SSD call, shared by the SSD kernels.  Strides are in
 // elements.  mode 0: raw xBC (conv + discretisation fused); mode 1:
 // pre-discretised inputs (x, log decay, B, C).

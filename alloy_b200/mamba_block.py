@@ -195,9 +195,18 @@ class MambaBlock(torch.nn.Module):
         y = y.to(x.dtype).reshape(Bsz, L, self.d_inner) * F.silu(z)
         return self.out_proj(y)
 
+    def _project(self, layer, t):
+        """``layer(t)`` for an ``nn.Linear`` without bias; a step of one token per
+        sequence for up to 4 bf16 sequences (decoding) runs the library's GEMV."""
+        if (t.dim() == 3 and t.shape[1] == 1 and t.shape[0] <= 4 and t.dtype == torch.bfloat16
+                and layer.bias is None and t.shape[2] % 8 == 0 and t.is_cuda
+                and not _needs_grad(t, layer.weight)):
+            return mixer.decode_linear(t.reshape(t.shape[0], t.shape[2]), layer.weight).unsqueeze(1)
+        return layer(t)
+
     def _forward_combined(self, x, Bsz, L, cache):
         ng, N, K = self.n_groups, self.d_state, self.d_conv
-        proj = self.in_proj(x)
+        proj = self._project(self.in_proj, x)
         gate = proj[..., :self.d_inner]
         xBC = proj[..., self.d_inner:self.d_inner + self.conv_dim]
         dt = proj[..., self.d_inner + self.conv_dim:]
@@ -223,4 +232,4 @@ class MambaBlock(torch.nn.Module):
         # gate first, then the inner norm (:495-499), fused in one kernel
         y = mixer.gated_rmsnorm(y, gate, self.norm.weight if self.norm is not None else None,
                                 eps=self.norm.eps if self.norm is not None else 1e-5)
-        return self.out_proj(y)
+        return self._project(self.out_proj, y)

@@ -22,7 +22,7 @@ from . import _lib
 __all__ = [
     "conv1d_silu", "depthwise_conv1d", "ssd_combined", "selective_scan",
     "ssd_decode_step", "gated_rmsnorm", "ssd_combined_streamed", "conv1d_silu_backward",
-    "Conv1dSilu", "selective_scan_backward", "SelectiveScan",
+    "Conv1dSilu", "selective_scan_backward", "SelectiveScan", "decode_linear",
 ]
 
 
@@ -462,6 +462,19 @@ class SelectiveScan(torch.autograd.Function):
             x, A_disc if log_a is None else None, B, C, dy.contiguous(), ssm_state=ssm_state,
             log_a=log_a, dssm_state_out=dh)
         return dx, dA, dB, dC, dh0, dla
+
+
+def decode_linear(x, weight, out=None):
+    """``x @ weight.T`` for 1 to 4 bf16 rows (``x [NB, in]``, ``weight [out, in]``
+    as an ``nn.Linear`` holds it): the in_proj / out_proj of a decode step
+    (alloy/models/mamba_block.py:438, :501), a weight-streaming GEMV."""
+    dev = _same_device(("x", x), ("weight", weight), ("out", out))
+    if out is None:
+        out = torch.empty((x.shape[0], weight.shape[0]), dtype=x.dtype, device=dev)
+    descs = [_lib.desc(t, n) for t, n in ((x, "x"), (weight, "weight"), (out, "y"))]
+    with torch.cuda.device(dev):
+        _lib.call("alloy_decode_linear", *(_lib.ref(d) for d in descs), _lib.stream_handle(dev))
+    return out
 
 
 def ssd_decode_step(xBC_tok, dt_tok, conv_weight, conv_bias, dt_bias, A_log, D, conv_state,

@@ -138,6 +138,20 @@ ALLOY_API size_t alloy_conv1d_silu_backward_workspace_size(int64_t batch, int64_
                                                  int64_t channels, int64_t d_conv);
 
 /*
+ * The projections of a decode step for 1 to 4 tokens: y = x W^T.
+ * Replaces MambaBlock's in_proj / out_proj (alloy/models/mamba_block.py:438,
+ * :501, nn.Linear without bias) when a cached step runs one token per
+ * sequence, where the product is a weight-streaming GEMV.
+ *
+ *   x      [NB, in]   BF16, 1 <= NB <= 4, last dim contiguous, rows 16-byte aligned
+ *   weight [out, in]  BF16 (the nn.Linear weight), last dim contiguous, rows 16-byte aligned
+ *   y      [NB, out]  BF16, last dim contiguous
+ * in a multiple of 8; fp32 accumulation.
+ */
+ALLOY_API int alloy_decode_linear(const alloy_tensor_t* x, const alloy_tensor_t* weight,
+                                  alloy_tensor_t* y, void* stream);
+
+/*
  * Fused Mamba-2 mixer core in combined (Zamba2 / Nemotron-H) mode, prefill of
  * L >= 1 tokens: conv1d+SiLU with the conv-cache prefix, split into x|B|C,
  * discretisation, chunked SSD scan with state carry, D skip.

@@ -368,6 +368,34 @@ def test_decode_step_vs_fp64(state_layout, N, P, G, H):
     np.testing.assert_array_equal(np_(conv_store.transpose(1, 2)), cs64.astype(np.float32))
 
 
+@pytest.mark.parametrize("B", [1, 2, 150])   # heads split over CTAs (1, 2); a CTA a group (150)
+@pytest.mark.parametrize("ranges", [((0, 8),), ((0, 4), (4, 4))])
+def test_decode_step_batch_and_head_ranges(B, ranges):
+    """Small batches spread each group's heads over several CTAs (the B and C
+    conv-cache channels rolled by a second launch), large batches give a CTA a
+    whole group; a step taken as group-aligned head ranges, one call each,
+    equals the whole step."""
+    H, P, N, G = 8, 16, 16, 2
+    inp = oracle.make_inputs(B=B, L=1, H=H, P=P, N=N, G=G, dtype="bf16", seed=B, with_state=True)
+    y64, h64, cs64 = oracle.decode_step_fp64(
+        inp["xBC"][:, 0], inp["dt_raw"][:, 0], inp["conv_weight"], inp["conv_bias"],
+        inp["dt_bias"], inp["A_log"], inp["D"], inp["ssm_state"], inp["conv_state"],
+        n_heads=H, headdim=P, d_state=N, n_groups=G)
+    ssm = cu(inp["ssm_state"])
+    conv = cu(inp["conv_state"], torch.bfloat16)
+    y = torch.zeros(B, H, P, device=DEV, dtype=torch.bfloat16)
+    for h0, hc in ranges:
+        mixer.ssd_decode_step(
+            cu(inp["xBC"][:, 0], torch.bfloat16), cu(inp["dt_raw"][:, 0], torch.bfloat16),
+            cu(inp["conv_weight"]), cu(inp["conv_bias"]), cu(inp["dt_bias"]), cu(inp["A_log"]),
+            cu(inp["D"]), conv, ssm, n_heads=H, head_dim=P, d_state=N, n_groups=G, out=y,
+            head_begin=h0, head_count=hc)
+    torch.cuda.synchronize()
+    assert_close(np_(y), y64, True)
+    assert_close(np_(ssm), h64, True)
+    np.testing.assert_array_equal(np_(conv), cs64.astype(np.float32))
+
+
 # ------------------------------------------------------------ gate + inner norm
 @pytest.mark.parametrize("rows,D,group,dtype,with_w", [
     (64, 8192, 0, torch.bfloat16, True),      # Nemotron-H d_inner, full-width norm
@@ -680,3 +708,17 @@ def test_combined_block_training_gradients_vs_fp64():
     assert_close(np_(x_t.grad), x64.grad.numpy(), False)
     for n, t in blk.named_parameters():
         assert_close(np_(t.grad), p[n].grad.numpy(), False), n
+
+
+@pytest.mark.parametrize("NB,inp,out", [(1, 4096, 18560), (1, 8192, 4096), (2, 64, 37), (3, 136, 250),
+                                        (4, 4096, 4096)])
+def test_decode_linear_vs_fp64(NB, inp, out):
+    # the decode-step projections (mamba_block.py:438, :501) for 1-4 tokens
+    g = torch.Generator(device=DEV).manual_seed(NB * 7 + out)
+    x = torch.randn((NB, inp), generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn((out, inp), generator=g, device=DEV) / inp ** 0.5).to(torch.bfloat16)
+    y = mixer.decode_linear(x, w)
+    torch.cuda.synchronize()
+    ref = (x.double() @ w.double().T).cpu().numpy()
+    assert y.shape == (NB, out) and y.dtype == torch.bfloat16
+    assert_close(np_(y), ref, True)
