@@ -41,6 +41,7 @@ EXPORTS = (
     "alloy_depthwise_conv1d",
     "alloy_ssd_combined",
     "alloy_selective_scan",
+    "alloy_selective_scan_dot",
     "alloy_ssd_decode_step",
     "alloy_ssd_combined_workspace_size",
     "alloy_ssd_combined_min_workspace_size",
@@ -137,10 +138,12 @@ def load():
         lib.alloy_kernel_launch_count.restype = ctypes.c_uint64
         lib.alloy_ssd_combined_noalloc.argtypes = [P] * 12 + [D, vp]
         lib.alloy_selective_scan.argtypes = [P] * 8 + [vp]
+        lib.alloy_selective_scan_dot.argtypes = [P] * 9 + [vp]
         lib.alloy_ssd_decode_step.argtypes = [P] * 10 + [D, vp]
         for name in ("alloy_conv1d_silu", "alloy_depthwise_conv1d", "alloy_conv1d_silu_backward",
                      "alloy_ssd_combined",
-                     "alloy_selective_scan", "alloy_ssd_decode_step", "alloy_check_device_status",
+                     "alloy_selective_scan", "alloy_selective_scan_dot", "alloy_ssd_decode_step",
+                     "alloy_check_device_status",
                      "alloy_ssd_combined_noalloc"):
             getattr(lib, name).restype = ctypes.c_int
         if lib.alloy_abi_version() != ABI_VERSION:

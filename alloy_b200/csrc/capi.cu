@@ -349,6 +349,10 @@ int alloy_check_device_status(void* stream) {
   if (e[0] != 0)
     return fail(ALLOY_ERR_TIMEOUT, "ssd_tc_kernel: bounded wait at site %u ran out (block %u, %u)",
                 e[0] - 1, e[1], e[2]);
+  ALLOY_TRY(scan_tc_take_error(as_stream(stream), e));
+  if (e[0] != 0)
+    return fail(ALLOY_ERR_TIMEOUT, "scan_tc_kernel: bounded wait at site %u ran out (block %u, %u)",
+                e[0] - 1, e[1], e[2]);
   return ALLOY_OK;
 }
 
@@ -388,7 +392,7 @@ int alloy_selective_scan(const alloy_tensor_t* x, const alloy_tensor_t* A_disc,
   a.mode = 1;
   a.B = (int)B; a.L = (int)L; a.H = (int)H; a.P = (int)P; a.N = (int)N; a.G = 1; a.K = 1;
   a.head_begin = 0; a.head_count = (int)H; a.Gbc = (int)Gb;
-  a.x = x->data; a.x_bf16 = x->dtype == ALLOY_BF16;
+  a.x = x->data; a.x_bf16 = x->dtype == ALLOY_BF16; a.x_hpg = 1;
   a.x_sb = x->stride[0]; a.x_st = x->stride[1]; a.x_sh = x->stride[2];
   if (present(log_a)) {
     a.log_a = static_cast<const float*>(log_a->data);
@@ -413,7 +417,95 @@ int alloy_selective_scan(const alloy_tensor_t* x, const alloy_tensor_t* A_disc,
   }
   a.y = y->data; a.y_bf16 = y->dtype == ALLOY_BF16;
   a.y_sb = y->stride[0]; a.y_st = y->stride[1]; a.y_sh = y->stride[2]; a.y_sp = y->stride[3];
+  // bf16 operands of the tensor-core sizes: tcgen05 scan; otherwise the fp32 CUDA-core scan
+  if (scan_tc_supported(a)) return scan_tc(a, as_stream(stream));
   return ssd_simt(a, as_stream(stream));
+}
+
+int alloy_selective_scan_dot(const alloy_tensor_t* x, const alloy_tensor_t* log_a,
+                             const alloy_tensor_t* Bm, const alloy_tensor_t* Cm,
+                             const alloy_tensor_t* ssm_in, alloy_tensor_t* y, alloy_tensor_t* ssm_out,
+                             const alloy_tensor_t* z, alloy_tensor_t* dot, void* stream) {
+  last_error().clear();
+  if (!present(y) && !present(dot)) return fail(ALLOY_ERR_INVALID_ARG, "selective_scan_dot: neither y nor dot");
+  ALLOY_TRY(check_tensor(x, "x", 4, nullptr, kBF16));
+  const alloy_tensor_t* ref = present(y) ? y : dot;
+  const int64_t B = x->shape[0], L = x->shape[1], P = x->shape[3];
+  const int64_t H = ref->shape[2];
+  if (present(y)) {
+    ALLOY_TRY(check_tensor(y, "y", 4, nullptr, kAnyFloat));
+    const int64_t ys[4] = {B, L, y->shape[2], P};
+    ALLOY_TRY(check_tensor(y, "y", 4, ys, kAnyFloat));
+  }
+  const int64_t bh[3] = {B, L, H};
+  if (present(dot)) ALLOY_TRY(check_tensor(dot, "dot", 3, bh, kF32));
+  ALLOY_TRY(check_tensor(log_a, "log_a", 3, bh, kF32));
+  auto divides = [&](int64_t g, const char* name) {
+    return (g > 0 && H % g == 0) ? ALLOY_OK
+                                 : fail(ALLOY_ERR_INVALID_ARG, "%s: dim 2 (%lld) does not divide n_heads %lld",
+                                        name, (long long)g, (long long)H);
+  };
+  ALLOY_TRY(divides(x->shape[2], "x"));
+  ALLOY_TRY(check_tensor(Bm, "B", 4, nullptr, kBF16));
+  const int64_t Gb = Bm->shape[2], N = Bm->shape[3];
+  const int64_t bs[4] = {B, L, Gb, N};
+  ALLOY_TRY(check_tensor(Bm, "B", 4, bs, kBF16));
+  ALLOY_TRY(check_tensor(Cm, "C", 4, bs, kBF16));
+  ALLOY_TRY(divides(Gb, "B/C"));
+  if (present(dot)) {
+    ALLOY_TRY(check_tensor(z, "z", 4, nullptr, kAnyFloat));
+    const int64_t zs[4] = {B, L, z->shape[2], P};
+    ALLOY_TRY(check_tensor(z, "z", 4, zs, kAnyFloat));
+    ALLOY_TRY(divides(z->shape[2], "z"));
+    if (z->stride[3] != 1) return fail(ALLOY_ERR_INVALID_ARG, "z: head_dim stride must be 1");
+  }
+  const int64_t ss[4] = {B, H, N, P};
+  if (present(ssm_in)) ALLOY_TRY(check_tensor(ssm_in, "ssm_in", 4, ss, kF32));
+  if (present(ssm_out)) ALLOY_TRY(check_tensor(ssm_out, "ssm_out", 4, ss, kF32));
+  if (x->stride[3] != 1) return fail(ALLOY_ERR_INVALID_ARG, "x: head_dim stride must be 1");
+  if (B == 0 || H == 0) return ALLOY_OK;
+  if (L == 0) return fail(ALLOY_ERR_UNSUPPORTED, "selective_scan_dot: L = 0");
+  ALLOY_TRY(current_device_checked(nullptr));
+
+  SsdArgs a;
+  memset(&a, 0, sizeof(a));
+  a.mode = 1;
+  a.B = (int)B; a.L = (int)L; a.H = (int)H; a.P = (int)P; a.N = (int)N; a.G = 1; a.K = 1;
+  a.head_begin = 0; a.head_count = (int)H; a.Gbc = (int)Gb;
+  a.x = x->data; a.x_bf16 = 1; a.x_hpg = (int)(H / x->shape[2]);
+  a.x_sb = x->stride[0]; a.x_st = x->stride[1]; a.x_sh = x->stride[2];
+  a.log_a = static_cast<const float*>(log_a->data);
+  a.la_sb = log_a->stride[0]; a.la_st = log_a->stride[1]; a.la_sh = log_a->stride[2];
+  a.Bm = Bm->data; a.bm_bf16 = 1;
+  a.bm_sb = Bm->stride[0]; a.bm_st = Bm->stride[1]; a.bm_sg = Bm->stride[2]; a.bm_sn = Bm->stride[3];
+  a.Cm = Cm->data; a.cm_bf16 = 1;
+  a.cm_sb = Cm->stride[0]; a.cm_st = Cm->stride[1]; a.cm_sg = Cm->stride[2]; a.cm_sn = Cm->stride[3];
+  if (present(ssm_in)) {
+    a.ssm_in = static_cast<const float*>(ssm_in->data);
+    a.si_sb = ssm_in->stride[0]; a.si_sh = ssm_in->stride[1];
+    a.si_sn = ssm_in->stride[2]; a.si_sp = ssm_in->stride[3];
+  }
+  if (present(ssm_out)) {
+    a.ssm_out = static_cast<float*>(ssm_out->data);
+    a.so_sb = ssm_out->stride[0]; a.so_sh = ssm_out->stride[1];
+    a.so_sn = ssm_out->stride[2]; a.so_sp = ssm_out->stride[3];
+  }
+  if (present(y)) {
+    if (y->shape[2] != H) return fail(ALLOY_ERR_INVALID_ARG, "y: dim 2 must be n_heads");
+    a.y = y->data; a.y_bf16 = y->dtype == ALLOY_BF16;
+    a.y_sb = y->stride[0]; a.y_st = y->stride[1]; a.y_sh = y->stride[2]; a.y_sp = y->stride[3];
+  }
+  if (present(dot)) {
+    a.z = z->data; a.z_bf16 = z->dtype == ALLOY_BF16; a.z_hpg = (int)(H / z->shape[2]);
+    a.z_sb = z->stride[0]; a.z_st = z->stride[1]; a.z_sh = z->stride[2];
+    a.dot = static_cast<float*>(dot->data);
+    a.dot_sb = dot->stride[0]; a.dot_st = dot->stride[1]; a.dot_sh = dot->stride[2];
+  }
+  if (!scan_tc_supported(a))
+    return fail(ALLOY_ERR_UNSUPPORTED,
+                "selective_scan_dot: needs (head_dim, d_state) of (64, 64), (64, 128) or (128, 64), unit inner "
+                "strides and 16-byte aligned rows");
+  return scan_tc(a, as_stream(stream));
 }
 
 int alloy_ssd_decode_step(const alloy_tensor_t* xBC_tok, const alloy_tensor_t* dt_tok,

@@ -48,7 +48,21 @@ struct SsdArgs {
   const float* ssm_in; int64_t si_sb, si_sh, si_sn, si_sp;
   float* ssm_out; int64_t so_sb, so_sh, so_sn, so_sp;
   void* y; int y_bf16; int64_t y_sb, y_st, y_sh, y_sp;
+  // tensor-core scan only: x indexed by head / x_hpg (x shared by x_hpg
+  // consecutive heads; 1 = per head); optional row dot products
+  // dot[b, t, h] = sum_p y[b, t, h, p] z[b, t, h / z_hpg, p] (y may then be null)
+  int x_hpg;
+  const void* z; int z_bf16; int64_t z_sb, z_st, z_sh; int z_hpg;
+  float* dot; int64_t dot_sb, dot_st, dot_sh;
 };
+
+// scan_tc.cu: tcgen05 scan on pre-discretised bf16 inputs (mode 1: x, B, C
+// bf16 with unit inner strides and 16-byte aligned rows; (P, N) = (64, 64),
+// (64, 128) or (128, 64); log decays <= 0).
+bool scan_tc_supported(const SsdArgs& a);
+int scan_tc(const SsdArgs& a, cudaStream_t s);
+// Synchronises the stream, then reads and clears the error word of the scan.
+int scan_tc_take_error(cudaStream_t s, unsigned int out[3]);
 
 // ssd_simt.cu: fp32 CUDA-core SSD (any sizes that fit shared memory).
 int ssd_simt(const SsdArgs& a, cudaStream_t s);

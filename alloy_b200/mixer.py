@@ -22,7 +22,7 @@ from . import _lib
 __all__ = [
     "conv1d_silu", "depthwise_conv1d", "ssd_combined", "selective_scan",
     "ssd_decode_step", "gated_rmsnorm", "ssd_combined_streamed", "conv1d_silu_backward",
-    "Conv1dSilu", "selective_scan_backward", "SelectiveScan", "decode_linear",
+    "Conv1dSilu", "selective_scan_backward", "SelectiveScan", "decode_linear", "selective_scan_dot",
 ]
 
 
@@ -366,6 +366,42 @@ def selective_scan(x, A_disc, B, C, ssm_state=None, log_a=None, out=None, out_dt
     return out, ssm_state_out
 
 
+def selective_scan_dot(x, B, C, log_a, *, z=None, ssm_state=None, y_dtype=torch.float32, write_y=True,
+                       write_ssm_state=False, reverse_time=False):
+    """The scan of ``selective_scan`` on the tensor cores (``alloy_selective_scan_dot``)
+    for bf16 operands, with x and the dot operand shared across heads and the
+    row dot products fused: the gradient scans of ``selective_scan_backward``.
+
+    x [B, L, Gx, P] bf16 (Gx divides H: head h reads x row h // (H // Gx)),
+    B/C [B, L, G', N] bf16, log_a [B, L, H] fp32 (<= 0; H is its dim 2),
+    z [B, L, Gz, P] (optional).  Returns (y [B, L, H, P] of ``y_dtype`` or None,
+    final state [B, H, N, P] fp32 or None, dot [B, L, H] fp32 or None) with
+    dot[b, t, h] = sum_p y[b, t, h, p] z[b, t, h // (H // Gz), p].
+    """
+    dev = _same_device(("x", x), ("B", B), ("C", C), ("log_a", log_a), ("z", z),
+                       ("ssm_state", ssm_state))
+    Bsz, L, _, P = x.shape
+    H, N = log_a.shape[2], B.shape[-1]
+    y = torch.empty((Bsz, L, H, P), dtype=y_dtype, device=dev) if write_y else None
+    h_out = torch.empty((Bsz, H, N, P), dtype=torch.float32, device=dev) if write_ssm_state else None
+    dot = torch.empty((Bsz, L, H), dtype=torch.float32, device=dev) if z is not None else None
+    args = [(x, "x"), (log_a, "log_a"), (B, "B"), (C, "C"), (ssm_state, "ssm_state"), (y, "y"),
+            (h_out, "ssm_state_out"), (z, "z"), (dot, "dot")]
+    descs = [_lib.desc(t, n) for t, n in args]
+    if reverse_time and L > 1:
+        for (t, name), d in zip(args, descs):
+            if t is not None and name not in ("ssm_state", "ssm_state_out"):
+                d.data += (L - 1) * t.stride(1) * t.element_size()
+                d.stride[1] = -t.stride(1)
+    with torch.cuda.device(dev):
+        _lib.call("alloy_selective_scan_dot", *(_lib.ref(d) for d in descs), _lib.stream_handle(dev))
+    return y, h_out, dot
+
+
+# (head_dim, d_state) pairs whose forward and transposed gradient scans the tensor-core scan covers
+_DOT_SCAN_DIMS = ((64, 64), (64, 128), (128, 64))
+
+
 def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dssm_state_out=None):
     """Gradients of ``selective_scan``: ``(dx, dA_disc, dB, dC, dssm_state, dlog_a)``
     for the output cotangent ``dy [B, L, H, P]`` and (optional) the cotangent of
@@ -387,7 +423,10 @@ def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dss
       dla_t = <dssm_state_out, h_{L-1}> + sum_{u >= t} (dy_u . y_u - B_u . dB_u).
     ``dlog_a`` is returned when ``log_a`` was given (the decay came from it),
     else ``dA_disc`` = dla / A_disc.  All arithmetic in fp32; the gradients have
-    the dtypes of their inputs.
+    the dtypes of their inputs.  When x, B and C are bf16 the four scans take
+    bf16 operands (x, B, C and dy as given, dy rounded to bf16) and run on the
+    tensor-core scan, with fp32 outputs, states and decay arithmetic, as a bf16
+    model's autograd computes in bf16; otherwise everything is fp32.
     """
     dev = _same_device(("x", x), ("A_disc", A_disc), ("B", B), ("C", C), ("dy", dy),
                        ("ssm_state", ssm_state), ("log_a", log_a),
@@ -398,10 +437,16 @@ def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dss
                               write_ssm_state=want_state, reverse_time=reverse)
 
     la = log_a.float() if log_a is not None else torch.log(torch.clamp(A_disc.float(), min=1e-10))
-    dx, dla, dB, dC, dh0 = _scan_backward(
-        scan, x.float().contiguous(), la, B.float(), C.float(), dy.float().contiguous(),
-        None if ssm_state is None else ssm_state.float(),
-        None if dssm_state_out is None else dssm_state_out.float(), dev)
+    bf16 = all(t.dtype == torch.bfloat16 for t in (x, B, C))
+    h0 = None if ssm_state is None else ssm_state.float()
+    dhT = None if dssm_state_out is None else dssm_state_out.float()
+    if bf16 and (x.shape[-1], B.shape[-1]) in _DOT_SCAN_DIMS:
+        bf = lambda t: t.to(torch.bfloat16).contiguous()   # noqa: E731
+        dx, dla, dB, dC, dh0 = _scan_backward_dot(bf(x), la.contiguous(), bf(B), bf(C), bf(dy), h0, dhT,
+                                                  dev)
+    else:
+        op = (lambda t: t.to(torch.bfloat16).contiguous()) if bf16 else (lambda t: t.float().contiguous())
+        dx, dla, dB, dC, dh0 = _scan_backward(scan, op(x), la, op(B), op(C), op(dy), h0, dhT, dev)
     dA = dla_out = None
     if log_a is not None:
         dla_out = dla.to(log_a.dtype)
@@ -423,7 +468,7 @@ def _scan_backward(scan, x, la, B, C, dy, h0, dhT, device):
     Bh = B.repeat_interleave(r, dim=2)          # per head [B, L, H, N]
     Ch = C.repeat_interleave(r, dim=2)
     if dhT is None:
-        dhT = torch.zeros((Bsz, H, N, P), dtype=x.dtype, device=device)
+        dhT = torch.zeros((Bsz, H, N, P), dtype=torch.float32, device=device)
     # the forward's outputs (y without D, and the final state)
     y, hT = scan(x, Bh, Ch, h0, la, True, False)
     # the reversed scans walk steps L-1 .. 0; the decay applied on reaching step
@@ -439,6 +484,33 @@ def _scan_backward(scan, x, la, B, C, dy, h0, dhT, device):
     dla = s.flip(-1).cumsum(-1).flip(-1).transpose(1, 2) + (dhT * hT).sum((-1, -2))[:, None, :]
     dh0 = torch.exp(la[:, 0])[:, :, None, None] * g0
     return (dx, dla, dBh.view(Bsz, L, G, r, N).sum(3), dCh.view(Bsz, L, G, r, N).sum(3), dh0)
+
+
+def _scan_backward_dot(x, la, B, C, dy, h0, dhT, device):
+    """``_scan_backward`` on the tensor-core scan: B/C, and C / B where they
+    are the scanned operand, stay per group (no per-head copies), y of the
+    recomputed forward is never written (only its dot with dy is needed), and
+    the dot of dB with B comes out of the dB scan."""
+    Bsz, L, H, P = x.shape
+    G, N = B.shape[2], B.shape[3]
+    r = H // G
+    if dhT is None:
+        dhT = torch.zeros((Bsz, H, N, P), dtype=torch.float32, device=device)
+    la_next = torch.zeros_like(la)
+    la_next[:, :-1] = la[:, 1:]
+    _, hT, dot_y = selective_scan_dot(x, B, C, la, z=dy, ssm_state=h0, write_y=False,
+                                      write_ssm_state=True)
+    dx, g0, _ = selective_scan_dot(dy, C, B, la_next, ssm_state=dhT, y_dtype=x.dtype,
+                                   write_ssm_state=True, reverse_time=True)
+    dBh, _, dot_b = selective_scan_dot(C, dy, x, la_next, z=B, ssm_state=dhT.transpose(2, 3),
+                                       reverse_time=True)
+    dCh, _, _ = selective_scan_dot(B, x, dy, la, ssm_state=None if h0 is None else h0.transpose(2, 3))
+    s = (dot_y - dot_b).transpose(1, 2).contiguous()   # [B, H, L]
+    dla = s.flip(-1).cumsum(-1).flip(-1).transpose(1, 2) + (dhT * hT).sum((-1, -2))[:, None, :]
+    dh0 = torch.exp(la[:, 0])[:, :, None, None] * g0
+    if r > 1:
+        dBh, dCh = dBh.view(Bsz, L, G, r, N).sum(3), dCh.view(Bsz, L, G, r, N).sum(3)
+    return dx, dla, dBh, dCh, dh0
 
 
 class SelectiveScan(torch.autograd.Function):

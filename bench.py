@@ -58,6 +58,9 @@ WORKLOADS = {
     # the scan's backward (training) at the Zamba2 layer shape, fp32
     "scan_bwd": dict(name="zamba2_1.2b_mamba2_selective_scan_backward", B=8, L=4096, H=64, P=64,
                      N=64, G=1, K=4, Q=256),
+    # the same with bf16 activations: the gradient scans on the tcgen05 scan
+    "scan_bwd_bf16": dict(name="zamba2_1.2b_mamba2_selective_scan_backward_bf16", B=8, L=4096, H=64,
+                          P=64, N=64, G=1, K=4, Q=256, dtype="bf16"),
     # one whole Mamba layer (projections, cached step, gate + norm) decoding at batch 1
     "decode_block": dict(name="nemotron_h_8b_mamba2_layer_decode_b1", B=1, L=64, H=128, P=64,
                          N=128, G=8, K=4, Q=256),
@@ -574,14 +577,33 @@ def run_scan_bwd(args, w):
     Bl = B // world
     gen = torch.Generator(device=dev)
     gen.manual_seed(41 + rank)
-    x = torch.randn((Bl, L, H, P), generator=gen, device=dev) * 0.5
-    Bm = torch.randn((Bl, L, G, N), generator=gen, device=dev)
-    Cm = torch.randn((Bl, L, G, N), generator=gen, device=dev)
+    bf16 = w.get("dtype") == "bf16"
+    act = torch.bfloat16 if bf16 else torch.float32
+    x = (torch.randn((Bl, L, H, P), generator=gen, device=dev) * 0.5).to(act)
+    Bm = torch.randn((Bl, L, G, N), generator=gen, device=dev).to(act)
+    Cm = torch.randn((Bl, L, G, N), generator=gen, device=dev).to(act)
     la = -torch.rand((Bl, L, H), generator=gen, device=dev) * 0.1
-    dy = torch.randn((Bl, L, H, P), generator=gen, device=dev)
+    dy = torch.randn((Bl, L, H, P), generator=gen, device=dev).to(act)
 
     def step(i):
         mixer.selective_scan_backward(x, None, Bm, Cm, dy, log_a=la)
+
+    # one forward scan alone (the unit the backward runs four times), for its roofline:
+    # algorithmic bytes = x, B, C, log decay read once, y (fp32) written once
+    def one_scan():
+        mixer.selective_scan(x, None, Bm, Cm, log_a=la, out_dtype=torch.float32, write_ssm_state=False)
+
+    for i in range(3):
+        one_scan()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(max(args.steps, 5)):
+        one_scan()
+    e1.record()
+    torch.cuda.synchronize()
+    scan_ms = e0.elapsed_time(e1) / max(args.steps, 5)
+    scan_bytes = Bl * L * (H * P * x.element_size() + 2 * G * N * Bm.element_size() + 4 * H + 4 * H * P)
 
     for i in range(args.warmup):
         step(i)
@@ -606,14 +628,21 @@ def run_scan_bwd(args, w):
     ms = dist_max(ev0.elapsed_time(ev1) / args.steps, world)
     tokens = B * L
     if rank == 0:
+        peak, src = measured_peaks()
+        achieved = scan_bytes / (scan_ms * 1e-3) / 1e9
         print(json.dumps({
-            "metric": "Mamba-2 selective scan backward tokens/s (fp32)",
+            "metric": "Mamba-2 selective scan backward tokens/s (%s)" % ("bf16" if bf16 else "fp32"),
             "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16" if bf16 else "f32",
+            "data": "synthetic",
             "config": {"workload": w["name"], "batch": B, "seq_len": L, "n_heads": H,
                        "head_dim": P, "d_state": N, "n_groups": G,
-                       "path": "4 fp32 CUDA-core scans + reverse cumulative sum"},
+                       "path": ("4 tcgen05 scans (bf16 operands, fp32 accumulators)" if bf16 else
+                                "4 fp32 CUDA-core scans") + " + reverse cumulative sum"},
+            "one_scan": {"ms": scan_ms, "bytes": scan_bytes,
+                         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                                      "frac": achieved / peak, "peak_source": src}},
             "gpu_launches": launches, "clocks": clocks.summary(h0, h1)}), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -998,7 +1027,7 @@ def main():
         run_conv_bwd(args, w)
     elif args.workload == "conv":
         run_conv(args, w)
-    elif args.workload == "scan_bwd":
+    elif args.workload in ("scan_bwd", "scan_bwd_bf16"):
         run_scan_bwd(args, w)
     else:
         run_ours(args, w)

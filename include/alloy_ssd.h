@@ -302,6 +302,30 @@ ALLOY_API int alloy_selective_scan(const alloy_tensor_t* x, const alloy_tensor_t
                          alloy_tensor_t* y, alloy_tensor_t* ssm_out, void* stream);
 
 /*
+ * The scan of alloy_selective_scan on the tensor cores with operands shared
+ * across heads and fused row dot products, for the gradient scans of
+ * training (MLX autograd through MambaBlock._selective_scan,
+ * alloy/models/mamba_block.py:287-366; no kernel counterpart in the
+ * reference).  n_heads H is y's dim 2 (dot's when y is absent).
+ *
+ *   x       [B, L, Gx, P]  BF16, Gx divides H (head h reads x row h / (H/Gx)), P stride 1
+ *   log_a   [B, L, H]      F32, <= 0
+ *   Bm, Cm  [B, L, G', N]  BF16, G' divides H, N stride 1
+ *   ssm_in  [B, H, N, P]   F32 via strides (data NULL = zeros)
+ *   y       [B, L, H, P]   F32|BF16 (data NULL = not written)
+ *   ssm_out [B, H, N, P]   F32 via strides (data NULL = not written)
+ *   z       [B, L, Gz, P]  F32|BF16, Gz divides H, P stride 1, 16-byte aligned rows
+ *   dot     [B, L, H]      F32 (data NULL = not written): dot[b,t,h] = sum_p y[b,t,h,p] z[b,t,h/(H/Gz),p]
+ * (P, N) must be (64, 64), (64, 128) or (128, 64), the rows of x, Bm and Cm
+ * 16-byte aligned; other calls return ALLOY_ERR_UNSUPPORTED.
+ */
+ALLOY_API int alloy_selective_scan_dot(const alloy_tensor_t* x, const alloy_tensor_t* log_a,
+                                       const alloy_tensor_t* Bm, const alloy_tensor_t* Cm,
+                                       const alloy_tensor_t* ssm_in, alloy_tensor_t* y,
+                                       alloy_tensor_t* ssm_out, const alloy_tensor_t* z,
+                                       alloy_tensor_t* dot, void* stream);
+
+/*
  * One decode token through the conv cache and the SSM cache, in place.
  * Replaces the L = 1 path of MambaBlock._forward_combined: the conv-cache roll
  * (alloy/models/mamba_block.py:446-448), conv + silu (:454-455), split

@@ -660,6 +660,86 @@ def test_selective_scan_backward_vs_fp64_autograd(cfg):
         assert_close(np_(got), ref.numpy(), False)
 
 
+@pytest.mark.parametrize("P,N,G,H,L,reverse,with_h0,out,decay", [
+    (64, 64, 1, 3, 300, False, True, torch.float32, 0.3),     # ragged last chunk, initial state
+    (64, 128, 2, 4, 256, False, False, torch.bfloat16, 0.3),  # d_state 128, grouped B/C
+    (128, 64, 4, 4, 200, True, True, torch.float32, 2.0),     # the dB / dC scan shape, reversed
+    (64, 64, 2, 2, 77, True, False, torch.bfloat16, 2.0),     # one partial chunk, reversed
+])
+def test_tensor_core_scan_vs_fp64(P, N, G, H, L, reverse, with_h0, out, decay):
+    """bf16 x, B, C on the tcgen05 scan: y and the final state against the
+    float64 per-step recurrence on the same (bf16-rounded) values."""
+    g = torch.Generator().manual_seed(P + N + L)
+    b = 2
+    x = (torch.randn(b, L, H, P, generator=g) * 0.5).bfloat16()
+    Bm = torch.randn(b, L, G, N, generator=g).bfloat16()
+    Cm = torch.randn(b, L, G, N, generator=g).bfloat16()
+    la = -torch.rand(b, L, H, generator=g) * decay
+    h0 = torch.randn(b, H, N, P, generator=g) * 0.3 if with_h0 else torch.zeros(b, H, N, P)
+    y, h = mixer.selective_scan(x.to(DEV), None, Bm.to(DEV), Cm.to(DEV),
+                                ssm_state=h0.to(DEV) if with_h0 else None, log_a=la.to(DEV),
+                                out_dtype=out, reverse_time=reverse)
+    torch.cuda.synchronize()
+    f = (lambda t: t.flip(1)) if reverse else (lambda t: t)
+    y64, h64 = _scan64(f(x).double(), f(la).double(), f(Bm).double(), f(Cm).double(), h0.double())
+    assert y.dtype == out
+    assert_close(np_(y), f(y64).numpy(), True)
+    assert_close(np_(h), h64.numpy(), True)
+
+
+@pytest.mark.parametrize("P,N,Gx,Gz,reverse", [(64, 64, 1, 2, False), (128, 64, 2, 4, True),
+                                               (64, 128, 4, 1, False)])
+def test_selective_scan_dot_shared_operands(P, N, Gx, Gz, reverse):
+    """alloy_selective_scan_dot: x shared by groups of heads, the fused row dot
+    products with a grouped z, y written or not, against the float64 recurrence."""
+    g = torch.Generator().manual_seed(P + Gx)
+    b, L, H, G = 2, 260, 4, 2
+    x = (torch.randn(b, L, Gx, P, generator=g) * 0.5).bfloat16()
+    Bm, Cm = torch.randn(b, L, G, N, generator=g).bfloat16(), torch.randn(b, L, G, N, generator=g).bfloat16()
+    la = -torch.rand(b, L, H, generator=g) * 0.5
+    z = torch.randn(b, L, Gz, P, generator=g).bfloat16()
+    h0 = torch.randn(b, H, N, P, generator=g) * 0.3
+    y, h, dot = mixer.selective_scan_dot(x.to(DEV), Bm.to(DEV), Cm.to(DEV), la.to(DEV), z=z.to(DEV),
+                                         ssm_state=h0.to(DEV), write_ssm_state=True, reverse_time=reverse)
+    _, h2, dot2 = mixer.selective_scan_dot(x.to(DEV), Bm.to(DEV), Cm.to(DEV), la.to(DEV), z=z.to(DEV),
+                                           ssm_state=h0.to(DEV), write_y=False, write_ssm_state=True,
+                                           reverse_time=reverse)
+    torch.cuda.synchronize()
+    f = (lambda t: t.flip(1)) if reverse else (lambda t: t)
+    xh = x.repeat_interleave(H // Gx, 2)
+    y64, h64 = _scan64(f(xh).double(), f(la).double(), f(Bm).double(), f(Cm).double(), h0.double())
+    y64 = f(y64)
+    dot64 = (y64 * z.repeat_interleave(H // Gz, 2).double()).sum(-1)
+    assert_close(np_(y), y64.numpy(), True)
+    assert_close(np_(h), h64.numpy(), True)
+    assert_close(np_(dot), dot64.numpy(), True)
+    assert torch.equal(dot, dot2) and torch.equal(h, h2)
+
+
+def test_selective_scan_backward_bf16_on_tensor_cores():
+    """bf16 inputs: the gradient scans run on the tcgen05 scan with bf16
+    operands; gradients against float64 autograd on the same bf16 values,
+    within 2e-2 relative L2 (bf16 operands, the cotangent rounded to bf16)."""
+    g = torch.Generator().manual_seed(11)
+    b, L, H, P, N, G = 2, 200, 4, 64, 64, 2
+    x = (torch.randn(b, L, H, P, generator=g) * 0.5).bfloat16()
+    Bm, Cm = torch.randn(b, L, G, N, generator=g).bfloat16(), torch.randn(b, L, G, N, generator=g).bfloat16()
+    la = -torch.rand(b, L, H, generator=g) * 0.3
+    h0 = torch.randn(b, H, N, P, generator=g) * 0.3
+    U = torch.randn(b, L, H, P, generator=g).bfloat16()
+    V = torch.randn(b, H, N, P, generator=g)
+    leaves = [t.double().requires_grad_() for t in (x, la, Bm, Cm, h0)]
+    y64, h64 = _scan64(*leaves)
+    ((y64 * U.double()).sum() + (h64 * V.double()).sum()).backward()
+    xs = [t.to(DEV).requires_grad_() for t in (x, la, Bm, Cm, h0)]
+    y, h = mixer.SelectiveScan.apply(xs[0], None, xs[2], xs[3], xs[4], xs[1])
+    ((y.float() * U.to(DEV).float()).sum() + (h * V.to(DEV)).sum()).backward()
+    for got, ref in zip((xs[0].grad, xs[1].grad, xs[2].grad, xs[3].grad, xs[4].grad),
+                        (leaf.grad for leaf in leaves)):
+        assert got.dtype == (torch.bfloat16 if ref.shape in (x.shape, Bm.shape) else torch.float32)
+        assert oracle.rel_l2(np_(got), ref.numpy()) < 2e-2
+
+
 def test_combined_block_training_gradients_vs_fp64():
     """MambaBlock (combined projection, inner norm) under autograd: the forward
     equals the fused inference path, and every parameter's gradient matches a
