@@ -10,7 +10,7 @@
 //   cum[t]   = sum_{u<=t} la_u                               (score warps)
 //   CB       = C B^T                                         (tcgen05 -> TMEM)
 //   S[t,s]   = CB[t,s] exp(cum[t] - cum[s]) for s <= t, else 0  (bf16 pairs, in place over CB)
-//   C~[t,:]  = exp(cum[t]) C[t,:]                            (bf16 pairs, next to S)
+//   C~[t,:]  = exp(cum[t]) C[t,:]                            (bf16 pairs, beside S)
 //   H        = bf16(state); state *= exp(cum[Q-1])           (state warps)
 //   X'[s,:]  = exp(cum[Q-1] - cum[s]) x[s,:]                 (state warps)
 //   Y        = [S | C~] [x ; H]                              (tcgen05, A from TMEM)
@@ -26,9 +26,11 @@
 // second block, so the state MMA runs at M = 128 with the state's rows
 // 64..127 identically zero.
 //
-// Warp roles (17 warps): 0-3 cumulative decay, scores and C~ (row t = lane
-// quadrant); 4-7 state copy/decay (row n) and X' (row s); 8-11 output rows;
-// 12-15 loads; 16 TMEM allocation and MMA issue.  Every mbarrier wait is
+// Warp roles (21 warps): 0-7 scores and C~ (row t = lane quadrant, two warps
+// a quadrant splitting its columns; warps 0-3 also scan the decays); 8-11
+// state copy/decay (row n) and X' (row s); 12-15 output rows; 16-19 loads; 20
+// TMEM allocation and MMA issue.  CB is double-buffered in tensor memory, so
+// the next chunk's C B^T runs while this chunk's scores are computed.  Every mbarrier wait is
 // bounded: on timeout the CTA records an error word, drains its copies and
 // MMAs, frees its tensor memory and exits.
 #include <algorithm>
@@ -36,6 +38,11 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "tc_ptx.cuh"
+
+// Phase markers: no code unless a timing build defines ALLOY_SCAN_TRACE.
+#ifndef ALLOY_SCAN_TRACE
+#define ALLOY_SCAN_TRACE(id, chunk)
+#endif
 
 namespace alloy {
 
@@ -48,49 +55,65 @@ namespace {
 using namespace tc;
 
 constexpr int Q = 128;
-constexpr int kWarps = 17;
+constexpr int kWarps = 21;
 constexpr int kThreads = kWarps * 32;
-constexpr int kMmaWarp = 16;
+constexpr int kStateWarp0 = 8;
+constexpr int kOutWarp0 = 12;
+constexpr int kLoadWarp0 = 16;
+constexpr int kMmaWarp = 20;
 constexpr long long kWaitCycles = 4000000000LL;   // ~2 s at 1.9 GHz
+constexpr int kL2Ahead = 3;                         // chunks prefetched into L2 ahead of their loads
 constexpr float kLog2e = 1.4426950408889634f;
 
+constexpr int kMaxBuf = 3;   // load buffers (3 for head_dim = d_state = 64, else 2)
+
 enum {
-  B_FULL0 = 0, B_FULL1,      // loads -> all: x, B, C, la of a buffer (4 loader warps)
-  B_EMPTY0, B_EMPTY1,        // MMA -> loads: buffer read by every MMA
-  B_CB_FULL,                 // MMA -> score warps
-  B_CUM0, B_CUM1,            // score warps -> state warps: cum of a buffer (4)
-  B_S_READY,                 // score warps -> MMA: S and C~ in TMEM (4)
-  B_ST_READY,                // state warps -> MMA: H, X' written, state decayed (4)
-  B_Y_FULL0, B_Y_FULL1,      // MMA -> output warps (per TMEM buffer)
-  B_Y_EMPTY0, B_Y_EMPTY1,    // output warps -> MMA (4)
-  B_ST_DONE,                 // MMA -> state warps: state update complete
-  B_PWG,                     // score warps: warp totals of the decay scan (4)
+  B_FULL0 = 0,                         // loads -> all: x, B, C, la of buffer i (4 loader warps)
+  B_EMPTY0 = B_FULL0 + kMaxBuf,        // MMA -> loads: buffer i read by every MMA
+  B_CUM0 = B_EMPTY0 + kMaxBuf,         // score warps -> all: cum and column factors of buffer i (4)
+  B_CB_FULL0 = B_CUM0 + kMaxBuf,       // MMA -> score warps: CB in TMEM buffer j (2)
+  B_CB_FREE0 = B_CB_FULL0 + 2,         // MMA -> MMA: Y that read TMEM buffer j completed (2)
+  B_S_READY0 = B_CB_FREE0 + 2,         // score warps -> MMA: S and C~ in TMEM buffer j (2, 8 warps)
+  B_ST_READY = B_S_READY0 + 2,         // state warps -> MMA: H written, state decayed
+  B_XP_READY0,                         // X' warps -> MMA: X' buffer i written (2)
+  B_Y_FULL0 = B_XP_READY0 + 2,         // MMA -> output warps (per output accumulator, 2)
+  B_Y_EMPTY0 = B_Y_FULL0 + 2,          // output warps -> MMA (2, 4 warps)
+  B_ST_DONE = B_Y_EMPTY0 + 2,          // MMA -> state warps: state update complete
+  B_PWG,                               // score warps: warp totals of the decay scan (4)
   B_DRAIN,
   NBAR
 };
 
 template <int PP, int NN>
 struct Layout {
-  static constexpr uint32_t kX = PP * 256;           // x tile of one buffer
-  static constexpr uint32_t kB = 32768;              // B tile (two 64-column blocks)
+  static constexpr int NBUF = (PP == 64 && NN == 64) ? 3 : 2;
+  static constexpr uint32_t kX = PP * 256;           // x tile of one buffer [PP/64][128][64]
+  static constexpr uint32_t kB = NN * 256;           // B tile [NN/64][128][64]
   static constexpr uint32_t kC = NN * 256;
   static constexpr uint32_t kBuf = kX + kB + kC;
-  static constexpr uint32_t OFF_BUF = 0;             // 2 buffers [x | B | C]
-  static constexpr uint32_t OFF_XP = 2 * kBuf;       // X' [PP/64][128][64]
-  static constexpr uint32_t OFF_H = OFF_XP + kX;     // H [PP/64][NN][64]
-  static constexpr uint32_t OFF_LA = OFF_H + PP * NN * 2;   // [2][128] f32
-  static constexpr uint32_t OFF_CUM = OFF_LA + 1024;        // [2][128] f32
-  static constexpr uint32_t OFF_WSUM = OFF_CUM + 1024;      // [2][4] f32
+  static constexpr uint32_t OFF_BUF = 0;             // NBUF buffers [x | B | C]
+  static constexpr uint32_t OFF_ZERO = NBUF * kBuf;  // 16 KB of zeros: the B tile's second block for NN = 64
+  static constexpr int NXP = PP == 128 ? 1 : 2;      // X' buffers
+  static constexpr uint32_t OFF_XP = OFF_ZERO + (NN == 64 ? 16384 : 0);   // NXP x X' [PP/64][128][64]
+  static constexpr uint32_t OFF_H = OFF_XP + NXP * kX;   // H [PP/64][NN][64]
+  static constexpr uint32_t OFF_LA = OFF_H + PP * NN * 2;          // [NBUF][128] f32
+  static constexpr uint32_t OFF_CUM = OFF_LA + NBUF * 512;         // [NBUF][128] f32
+  static constexpr uint32_t OFF_CF = OFF_CUM + NBUF * 512;         // [NBUF][128] f32 column factors
+  static constexpr uint32_t OFF_WSUM = OFF_CF + NBUF * 512;        // [NBUF][4] f32
   static constexpr uint32_t OFF_BAR = OFF_WSUM + 64;
   static constexpr uint32_t OFF_TMEMPTR = OFF_BAR + NBAR * 8;
   static constexpr uint32_t OFF_ABORT = OFF_TMEMPTR + 8;
   static constexpr uint32_t kSmem = OFF_ABORT + 16 + 1024;  // + alignment slack
-  // tensor memory columns
-  static constexpr uint32_t T_CB = 0;                // CB, then S (cols 0-63) and C~ (64-)
-  static constexpr uint32_t T_Y = 128;               // 2 x PP: output accumulators
-  static constexpr uint32_t T_ST = 128 + 2 * PP;     // PP: state rows n
+  // tensor memory columns: two CB buffers (CB, then in place: K-step k of S in
+  // columns [16k, 16k+8) and of C~ in [16k+8, 16k+16)), NYB output
+  // accumulators, the state
+  static constexpr int NYB = PP == 128 ? 1 : 2;
+  static constexpr uint32_t T_CB = 0;                // + 128 * (chunk & 1)
+  static constexpr uint32_t T_Y = 256;               // + PP * (chunk % NYB)
+  static constexpr uint32_t T_ST = 256 + NYB * PP;   // PP: state rows n
   static_assert(T_ST + PP <= 512, "tensor memory");
   static_assert(kSmem <= 227 * 1024, "shared memory");
+  static_assert(NBUF <= kMaxBuf, "buffers");
 };
 
 __device__ __forceinline__ void signal_abort(volatile int* abort_flag, int site) {
@@ -99,18 +122,6 @@ __device__ __forceinline__ void signal_abort(volatile int* abort_flag, int site)
     g_scan_tc_error[1] = blockIdx.x;
     g_scan_tc_error[2] = blockIdx.y;
   }
-}
-
-// single-thread wait (MMA issuer)
-__device__ __forceinline__ bool wait1(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site) {
-  const long long t0 = clock64();
-  for (uint32_t it = 0; it < (1u << 30); ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) break;
-  }
-  signal_abort(abort_flag, site);
-  return false;
 }
 
 // warp-uniform wait: every lane polls (bounded by the clock and the CTA's
@@ -125,6 +136,19 @@ __device__ __forceinline__ bool waitw(uint32_t bar, uint32_t parity, volatile in
   if (!ok && (threadIdx.x & 31) == 0 && !*abort_flag) signal_abort(abort_flag, site);
   __syncwarp();
   return ok;
+}
+
+// non-blocking test of an mbarrier phase
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
 
 // byte offset of 16-byte chunk `chunk` (0..7) of row `row` in a 128-byte-swizzled block
@@ -169,19 +193,21 @@ __device__ __forceinline__ void load_rows(uint32_t tile, const __nv_bfloat16* sr
 template <int PP, int NN>
 __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, int y_vec) {
   using Lo = Layout<PP, NN>;
+  constexpr int NBUF = Lo::NBUF, NYB = Lo::NYB;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_base);
   float* la_s = reinterpret_cast<float*>(smem + Lo::OFF_LA);
   float* cum_s = reinterpret_cast<float*>(smem + Lo::OFF_CUM);
+  float* cf_s = reinterpret_cast<float*>(smem + Lo::OFF_CF);
   float* wsum = reinterpret_cast<float*>(smem + Lo::OFF_WSUM);
   volatile uint32_t* tmem_ptr = reinterpret_cast<volatile uint32_t*>(smem + Lo::OFF_TMEMPTR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Lo::OFF_ABORT);
   auto bar = [&](int i) { return base + Lo::OFF_BAR + 8u * i; };
-  auto xt = [&](int buf) { return base + Lo::OFF_BUF + buf * Lo::kBuf; };
-  auto bt = [&](int buf) { return xt(buf) + Lo::kX; };
-  auto ct = [&](int buf) { return bt(buf) + Lo::kB; };
+  auto xt = [&](int lb) { return base + Lo::OFF_BUF + lb * Lo::kBuf; };
+  auto bt = [&](int lb) { return xt(lb) + Lo::kX; };
+  auto ct = [&](int lb) { return bt(lb) + Lo::kB; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x, b = blockIdx.y;
@@ -191,17 +217,19 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    // FULL0/1 EMPTY0/1 CB_FULL CUM0/1 S_READY ST_READY Y_FULL0/1 Y_EMPTY0/1 ST_DONE PWG DRAIN
-    const int counts[NBAR] = {4, 4, 1, 1, 1, 4, 4, 4, 4, 1, 1, 4, 4, 1, 4, 1};
+    int counts[NBAR];
+    for (int i = 0; i < NBAR; ++i) counts[i] = 1;
+    for (int i = 0; i < kMaxBuf; ++i) counts[B_FULL0 + i] = counts[B_CUM0 + i] = 4;
+    counts[B_S_READY0] = counts[B_S_READY0 + 1] = 8;
+    counts[B_Y_EMPTY0] = counts[B_Y_EMPTY0 + 1] = counts[B_PWG] = 4;
+    // d_state 64: warps 8-9 copy the state, 10-11 write X'; 128: all four do both
+    counts[B_ST_READY] = counts[B_XP_READY0] = counts[B_XP_READY0 + 1] = NN == 64 ? 2 : 4;
     for (int i = 0; i < NBAR; ++i) mbar_init(bar(i), counts[i]);
     mbar_fence_init();
   }
   if (NN == 64) {
-    // the zero second block of both B tiles (never written by the loads)
-    for (int i = threadIdx.x; i < 2 * 1024; i += kThreads) {
-      const int buf = i >> 10;
-      st_shared_v4(bt(buf) + 16384 + (i & 1023) * 16, make_uint4(0u, 0u, 0u, 0u));
-    }
+    for (int i = threadIdx.x; i < 1024; i += kThreads)
+      st_shared_v4(base + Lo::OFF_ZERO + i * 16, make_uint4(0u, 0u, 0u, 0u));
     fence_async_smem();
   }
   if (warp == kMmaWarp) {
@@ -218,63 +246,111 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
 
   if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issue
+    // One thread polls the barriers and issues whichever MMA group is ready:
+    // CB of chunk `ncb` (at most one chunk ahead of the Y / state group), or
+    // Y and the state update of chunk `ny`.
     if (lane == 0) {
       constexpr uint32_t ID_CB = idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t ID_Y = idesc_bf16(128, PP, 0, 1);
       constexpr uint32_t ID_ST = idesc_bf16(128, PP, 1, 1);
-      for (int c = 0; c < nk; ++c) {
-        const int buf = c & 1, yb = c & 1;
-        if (!wait1(bar(B_FULL0 + buf), (c >> 1) & 1, abort_flag, 1)) break;
-        // CB overwrites the S / C~ columns that Y(c-1) read
-        if (c > 0 && !wait1(bar(B_Y_FULL0 + (yb ^ 1)), ((c - 1) >> 1) & 1, abort_flag, 2)) break;
-        tc_fence_after();
+      int ncb = 0, ny = 0;
+      long long t0 = clock64();
+      while (ny < nk) {
+        bool progress = false;
+        if (ncb < nk && ncb <= ny + 1) {
+          const int lb = ncb % NBUF, j = ncb & 1;
+          if (mbar_test(bar(B_FULL0 + lb), (ncb / NBUF) & 1) &&
+              (ncb < 2 || mbar_test(bar(B_CB_FREE0 + j), ((ncb >> 1) - 1) & 1))) {
+            ALLOY_SCAN_TRACE(2, ncb);
+            tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < NN / 16; ++k)
-          umma_bf16(tmem + Lo::T_CB, sw128_desc(ct(buf) + (k >> 2) * 16384 + 32 * (k & 3), 16, 1024),
-                    sw128_desc(bt(buf) + (k >> 2) * 16384 + 32 * (k & 3), 16, 1024), ID_CB, k != 0);
-        umma_commit(bar(B_CB_FULL));
-        if (!wait1(bar(B_S_READY), c & 1, abort_flag, 3)) break;
-        if (!wait1(bar(B_ST_READY), c & 1, abort_flag, 4)) break;
-        if (c >= 2 && !wait1(bar(B_Y_EMPTY0 + yb), ((c >> 1) - 1) & 1, abort_flag, 5)) break;
-        tc_fence_after();
-        // Y = S x + C~ H
-        const uint32_t ty = tmem + Lo::T_Y + yb * PP;
+            for (int k = 0; k < NN / 16; ++k)
+              umma_bf16(tmem + Lo::T_CB + 128 * j, sw128_desc(ct(lb) + (k >> 2) * 16384 + 32 * (k & 3), 16, 1024),
+                        sw128_desc(bt(lb) + (k >> 2) * 16384 + 32 * (k & 3), 16, 1024), ID_CB, k != 0);
+            umma_commit(bar(B_CB_FULL0 + j));
+            ++ncb;
+            progress = true;
+          }
+        }
+        if (ny < ncb) {
+          const int c = ny, lb = c % NBUF, j = c & 1, yb = c % NYB;
+          const int xb = c % Lo::NXP;
+          if (mbar_test(bar(B_S_READY0 + j), (c >> 1) & 1) && mbar_test(bar(B_ST_READY), c & 1) &&
+              mbar_test(bar(B_XP_READY0 + xb), (c / Lo::NXP) & 1) &&
+              (c < NYB || mbar_test(bar(B_Y_EMPTY0 + yb), ((c / NYB) - 1) & 1))) {
+            ALLOY_SCAN_TRACE(3, c);
+            tc_fence_after();
+            // Y = S x + C~ H
+            const uint32_t ty = tmem + Lo::T_Y + yb * PP, tcb = tmem + Lo::T_CB + 128 * j;
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_bf16_ta(ty, tmem + Lo::T_CB + 8 * k, sw128_desc(xt(buf) + 2048 * k, 16384, 1024), ID_Y, k != 0);
+            for (int k = 0; k < 8; ++k)
+              umma_bf16_ta(ty, tcb + 16 * k, sw128_desc(xt(lb) + 2048 * k, 16384, 1024), ID_Y, k != 0);
 #pragma unroll
-        for (int k = 0; k < NN / 16; ++k)
-          umma_bf16_ta(ty, tmem + Lo::T_CB + 64 + 8 * k,
-                       sw128_desc(base + Lo::OFF_H + 2048 * k, NN * 128, 1024), ID_Y, 1);
-        umma_commit(bar(B_Y_FULL0 + yb));
-        // state[n, p] += sum_s B[s, n] X'[s, p]
+            for (int k = 0; k < NN / 16; ++k)
+              umma_bf16_ta(ty, tcb + 16 * k + 8, sw128_desc(base + Lo::OFF_H + 2048 * k, NN * 128, 1024), ID_Y, 1);
+            umma_commit(bar(B_Y_FULL0 + yb));
+            umma_commit(bar(B_CB_FREE0 + j));
+            // state[n, p] += sum_s B[s, n] X'[s, p]; rows n >= NN of A read the zero block
+            const uint32_t lbo = NN == 64 ? Lo::OFF_ZERO - (bt(lb) - base) : 16384;
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          umma_bf16(tmem + Lo::T_ST, sw128_desc(bt(buf) + 2048 * k, 16384, 1024),
-                    sw128_desc(base + Lo::OFF_XP + 2048 * k, 16384, 1024), ID_ST, 1);
-        umma_commit(bar(B_ST_DONE));
-        umma_commit(bar(B_EMPTY0 + buf));
+            for (int k = 0; k < 8; ++k)
+              umma_bf16(tmem + Lo::T_ST, sw128_desc(bt(lb) + 2048 * k, lbo, 1024),
+                        sw128_desc(base + Lo::OFF_XP + xb * Lo::kX + 2048 * k, 16384, 1024), ID_ST, 1);
+            umma_commit(bar(B_ST_DONE));
+            umma_commit(bar(B_EMPTY0 + lb));
+            ALLOY_SCAN_TRACE(5, c);
+            ++ny;
+            progress = true;
+          }
+        }
+        if (progress) {
+          t0 = clock64();
+        } else {
+          if (*abort_flag) break;
+          if (clock64() - t0 > kWaitCycles) {
+            signal_abort(abort_flag, 1);
+            break;
+          }
+          __nanosleep(32);
+        }
       }
       // wait (bounded) for every MMA this thread issued
       umma_commit(bar(B_DRAIN));
-      const long long t0 = clock64();
-      while (!mbar_try_wait(bar(B_DRAIN), 0) && clock64() - t0 < kWaitCycles) {
+      const long long t1 = clock64();
+      while (!mbar_try_wait(bar(B_DRAIN), 0) && clock64() - t1 < kWaitCycles) {
       }
     }
-  } else if (warp >= 12) {
+  } else if (warp >= kLoadWarp0) {
     // ------------------------------------------------------------------ loads
-    const int i = threadIdx.x - 384;
+    const int i = threadIdx.x - 32 * kLoadWarp0;
     const int xh = a.x_hpg > 1 ? h / a.x_hpg : h;
     const __nv_bfloat16* xs = static_cast<const __nv_bfloat16*>(a.x) + (int64_t)b * a.x_sb + (int64_t)xh * a.x_sh;
     const __nv_bfloat16* bs = static_cast<const __nv_bfloat16*>(a.Bm) + (int64_t)b * a.bm_sb + (int64_t)g * a.bm_sg;
     const __nv_bfloat16* cs = static_cast<const __nv_bfloat16*>(a.Cm) + (int64_t)b * a.cm_sb + (int64_t)g * a.cm_sg;
+    // rows of a chunk a few chunks ahead into L2, so that the loads of a
+    // buffer, which wait for that buffer's last MMA, find them there
+    auto prefetch = [&](int cc) {
+      const int t = cc * Q + i;
+      if (cc >= nk || t >= L) return;
+      const char* rows[3] = {reinterpret_cast<const char*>(xs + (int64_t)t * a.x_st),
+                             reinterpret_cast<const char*>(bs + (int64_t)t * a.bm_st),
+                             reinterpret_cast<const char*>(cs + (int64_t)t * a.cm_st)};
+      const int bytes[3] = {PP * 2, NN * 2, NN * 2};
+#pragma unroll
+      for (int m = 0; m < 3; ++m)
+        for (int o = 0; o < bytes[m] + 127; o += 128) prefetch_l2(rows[m] + min(o, bytes[m] - 1));
+      if (a.log_a) prefetch_l2(a.log_a + (int64_t)b * a.la_sb + (int64_t)t * a.la_st + (int64_t)h * a.la_sh);
+    };
+    for (int cc = 1; cc < kL2Ahead; ++cc) prefetch(cc);
     for (int c = 0; c < nk; ++c) {
-      const int buf = c & 1;
-      if (c >= 2 && !waitw(bar(B_EMPTY0 + buf), ((c >> 1) - 1) & 1, abort_flag, 10)) break;
+      const int lb = c % NBUF;
+      prefetch(c + kL2Ahead);
+      if (c >= NBUF && !waitw(bar(B_EMPTY0 + lb), ((c / NBUF) - 1) & 1, abort_flag, 10)) break;
+      if (warp == kLoadWarp0) ALLOY_SCAN_TRACE(0, c);
       const int row0 = c * Q;
-      load_rows<PP>(xt(buf), xs, a.x_st, row0, L, i);
-      load_rows<NN>(bt(buf), bs, a.bm_st, row0, L, i);
-      load_rows<NN>(ct(buf), cs, a.cm_st, row0, L, i);
+      load_rows<PP>(xt(lb), xs, a.x_st, row0, L, i);
+      load_rows<NN>(bt(lb), bs, a.bm_st, row0, L, i);
+      load_rows<NN>(ct(lb), cs, a.cm_st, row0, L, i);
       {
         const int t = row0 + i;
         float la = 0.f;
@@ -285,102 +361,143 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
             la = logf(fmaxf(load_any(a.A_disc, (int64_t)b * a.ad_sb + (int64_t)t * a.ad_st + (int64_t)h * a.ad_sh,
                                      a.ad_bf16), 1e-10f));
         }
-        la_s[buf * 128 + i] = la;
+        la_s[lb * 128 + i] = la;
       }
       cp_async_wait_all();
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_FULL0 + buf));
+      if (warp == kLoadWarp0) ALLOY_SCAN_TRACE(1, c);
+      if (lane == 0) mbar_arrive(bar(B_FULL0 + lb));
     }
     cp_async_wait_all();
-  } else if (warp < 4) {
+  } else if (warp < kStateWarp0) {
     // ------------------------------------------------------------------ scores
-    const int t = r;
+    // Two warps a lane quadrant: `half` 0 (warps 0-3) also scans the decays;
+    // half 0 takes the even 16-column pieces of the row, half 1 the odd ones,
+    // and each stores its S and C~ K-steps inside pieces it read itself.
+    const int t = r, half = warp >> 2;
     for (int c = 0; c < nk; ++c) {
-      const int buf = c & 1;
-      if (!waitw(bar(B_FULL0 + buf), (c >> 1) & 1, abort_flag, 20)) break;
-      // cum[t] = inclusive sum of la over the chunk
-      float v = la_s[buf * 128 + t];
+      const int lb = c % NBUF, j = c & 1;
+      if (half == 0) {
+        if (!waitw(bar(B_FULL0 + lb), (c / NBUF) & 1, abort_flag, 20)) break;
+        // cum[t] = inclusive sum of la over the chunk
+        float v = la_s[lb * 128 + t];
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float u = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += u;
+        for (int o = 1; o < 32; o <<= 1) {
+          const float u = __shfl_up_sync(0xffffffffu, v, o);
+          if (lane >= o) v += u;
+        }
+        // warp totals: wsum[lb] for chunk c+NBUF is written only after every
+        // warp passed the PWG wait of a later chunk, which follows its reads
+        if (lane == 31) wsum[lb * 4 + q] = v;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_PWG));
+        if (!waitw(bar(B_PWG), c & 1, abort_flag, 21)) break;
+        float pre = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) pre += k < q ? wsum[lb * 4 + k] : 0.f;
+        const float cum = v + pre;
+        // column factor of source s = t inside its 16-column piece: exp(cum[m] -
+        // cum[s]) <= 1, m the piece's last column (decays <= 1)
+        const float cum_m = __shfl_sync(0xffffffffu, cum, lane | 15);
+        cum_s[lb * 128 + t] = cum;
+        cf_s[lb * 128 + t] = ex2_approx((cum_m - cum) * kLog2e);
+        __syncwarp();
+        if (warp == 3) ALLOY_SCAN_TRACE(6, c);
+        if (lane == 0) mbar_arrive(bar(B_CUM0 + lb));
       }
-      // warp totals: wsum[buf] for chunk c+2 is written only after every warp
-      // passed the PWG wait of chunk c+1, which follows its reads for chunk c
-      if (lane == 31) wsum[buf * 4 + q] = v;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_PWG));
-      if (!waitw(bar(B_PWG), c & 1, abort_flag, 21)) break;
-      float pre = 0.f;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) pre += k < q ? wsum[buf * 4 + k] : 0.f;
-      const float cum_t = v + pre;
-      cum_s[buf * 128 + t] = cum_t;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_CUM0 + buf));
-      if (!waitw(bar(B_CUM0 + buf), (c >> 1) & 1, abort_flag, 22)) break;
-      if (!waitw(bar(B_CB_FULL), c & 1, abort_flag, 23)) break;
+      if (!waitw(bar(B_CUM0 + lb), (c / NBUF) & 1, abort_flag, 22)) break;
+      if (!waitw(bar(B_CB_FULL0 + j), (c >> 1) & 1, abort_flag, 23)) break;
+      if (warp == 3) ALLOY_SCAN_TRACE(7, c);
       tc_fence_after();
-      // S: K-step k (sources 16k .. 16k+15) as bf16 pairs in columns [8k, 8k+8)
-      const float* cm = cum_s + buf * 128;
-      const float ct2 = cum_t * kLog2e;
+      const float* cm = cum_s + lb * 128;
+      const float* cf = cf_s + lb * 128;
+      const float ct2 = cm[t] * kLog2e;
+      const uint32_t tcb = lane_base + Lo::T_CB + 128 * j;
+      // S[t, s] = CB[t, s] exp(cum[t] - cum[s]) (s <= t) for piece k -> columns [16k, 16k+8)
       auto score = [&](int k, const uint32_t (&rv)[16]) {
         uint32_t o[8];
+        if (k < 2 * q) {
+          // left of the quadrant's diagonal block: exp(cum[t] - cum[s]) = R cf[s],
+          // R = exp(cum[t] - cum[m]) <= 1
+          const uint64_t R2 = f2_splat(ex2_approx(fmaf(-cm[16 * k + 15], kLog2e, ct2)));
+          const float4* cf4 = reinterpret_cast<const float4*>(cf + 16 * k);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int s = 16 * k + 2 * e;
-          const float f0 = s <= t ? __uint_as_float(rv[2 * e]) * ex2_approx(fmaf(-cm[s], kLog2e, ct2)) : 0.f;
-          const float f1 = s + 1 <= t ? __uint_as_float(rv[2 * e + 1]) * ex2_approx(fmaf(-cm[s + 1], kLog2e, ct2)) : 0.f;
-          o[e] = pack_bf16x2(f0, f1);
+          for (int i4 = 0; i4 < 4; ++i4) {
+            const float4 f = cf4[i4];
+            o[2 * i4] = f2_to_bf2(
+                f2_mul(f2_mul(f2_pack(__uint_as_float(rv[4 * i4]), __uint_as_float(rv[4 * i4 + 1])), R2),
+                       f2_pack(f.x, f.y)));
+            o[2 * i4 + 1] = f2_to_bf2(
+                f2_mul(f2_mul(f2_pack(__uint_as_float(rv[4 * i4 + 2]), __uint_as_float(rv[4 * i4 + 3])), R2),
+                       f2_pack(f.z, f.w)));
+          }
+        } else {
+          // the diagonal block: exact factors, zero right of the diagonal
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int s = 16 * k + 2 * e;
+            const float f0 = __uint_as_float(rv[2 * e]) * ex2_approx(fmaf(-cm[s], kLog2e, ct2));
+            const float f1 = __uint_as_float(rv[2 * e + 1]) * ex2_approx(fmaf(-cm[s + 1], kLog2e, ct2));
+            o[e] = pack_bf16x2(s <= t ? f0 : 0.f, s + 1 <= t ? f1 : 0.f);
+          }
         }
-        tmem_st8(lane_base + Lo::T_CB + 8 * k, o);
+        tmem_st8(tcb + 16 * k, o);
       };
-      const int kmax = 2 * q + 1;   // pieces at or left of this warp's diagonal block
+      // this warp's pieces at or left of the quadrant's diagonal: k = half, half + 2, .., 2q + half
       uint32_t ra[16], rb[16];
-      tmem_ld16(lane_base + Lo::T_CB, ra);
+      tmem_ld16(tcb + 16 * half, ra);
 #pragma unroll 1
-      for (int k = 0; k <= kmax; k += 2) {
+      for (int jj = 0; jj <= q; jj += 2) {
+        const int k = 2 * jj + half;
         tmem_ld_wait_regs(ra);
-        tmem_ld16(lane_base + Lo::T_CB + 16 * (k + 1), rb);
+        if (jj + 1 <= q) tmem_ld16(tcb + 16 * (k + 2), rb);
         score(k, ra);
+        if (jj + 1 > q) break;
         tmem_ld_wait_regs(rb);
-        if (k + 2 <= kmax) tmem_ld16(lane_base + Lo::T_CB + 16 * (k + 2), ra);
-        score(k + 1, rb);
+        if (jj + 2 <= q) tmem_ld16(tcb + 16 * (k + 4), ra);
+        score(k + 2, rb);
       }
       {
         uint32_t z[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) z[e] = 0u;
 #pragma unroll 1
-        for (int k = kmax + 1; k < 8; ++k) tmem_st8(lane_base + Lo::T_CB + 8 * k, z);
+        for (int k = 2 * (q + 1) + half; k < 8; k += 2) tmem_st8(tcb + 16 * k, z);
       }
-      // C~ = exp(cum[t]) C[t, :]: K-step k of the C~ H product in columns [64 + 8k, 64 + 8k + 8)
+      // C~ = exp(cum[t]) C[t, :]: K-step k of the C~ H product -> columns [16k+8, 16k+16)
       {
-        const float e = ex2_approx(ct2);
-        const uint32_t crow = ct(buf);
+        const uint64_t e2 = f2_splat(ex2_approx(ct2));
+        const uint32_t crow = ct(lb);
 #pragma unroll 1
-        for (int k = 0; k < NN / 16; ++k) {
+        for (int k = half; k < NN / 16; k += 2) {
           uint32_t o[8];
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            const int j = 2 * k + hh;   // 16-byte chunk of the row
-            const uint4 w = ld_shared_v4(crow + (j >> 3) * 16384 + sw_off(t, j & 7));
+            const int jc = 2 * k + hh;   // 16-byte chunk of the row
+            const uint4 w = ld_shared_v4(crow + (jc >> 3) * 16384 + sw_off(t, jc & 7));
             const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int m = 0; m < 4; ++m) o[4 * hh + m] = pack_bf16x2(e * bf16_lo(ww[m]), e * bf16_hi(ww[m]));
+            for (int m = 0; m < 4; ++m) o[4 * hh + m] = f2_to_bf2(f2_mul(f2_from_bf2(ww[m]), e2));
           }
-          tmem_st8(lane_base + Lo::T_CB + 64 + 8 * k, o);
+          tmem_st8(tcb + 16 * k + 8, o);
         }
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_S_READY));
+      if (warp == 3) ALLOY_SCAN_TRACE(8, c);
+      if (warp == 7) ALLOY_SCAN_TRACE(9, c);
+      if (warp == 0) ALLOY_SCAN_TRACE(14, c);
+      if (lane == 0) mbar_arrive(bar(B_S_READY0 + j));
     }
-  } else if (warp < 8) {
+  } else if (warp < kOutWarp0) {
     // ------------------------------------------------------------------ state and X'
+    // For d_state 64 the state rows live in lanes 0-63: warps 8-9 copy and
+    // decay them while warps 10-11 scale X' (two rows a thread); for 128 every
+    // warp does both for its own rows.
     const bool has_row = r < NN;   // warp-uniform
+    const bool does_xp = NN == 128 || q >= 2;
     // initial state (rows n >= NN stay zero)
 #pragma unroll 1
     for (int p0 = 0; p0 < PP; p0 += 16) {
@@ -396,26 +513,47 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
     }
     tmem_st_wait();
     for (int c = 0; c < nk; ++c) {
-      const int buf = c & 1;
-      if (!waitw(bar(B_FULL0 + buf), (c >> 1) & 1, abort_flag, 30)) break;
-      if (!waitw(bar(B_CUM0 + buf), (c >> 1) & 1, abort_flag, 31)) break;
-      // the previous state update (and Y(c-1), issued before it) has completed
-      if (c > 0 && !waitw(bar(B_ST_DONE), (c - 1) & 1, abort_flag, 32)) break;
-      tc_fence_after();
-      const float* cm = cum_s + buf * 128;
+      const int lb = c % NBUF, xb = c % Lo::NXP;
+      if (!waitw(bar(B_CUM0 + lb), (c / NBUF) & 1, abort_flag, 31)) break;
+      const float* cm = cum_s + lb * 128;
       const float last = cm[127];
+      if (does_xp) {
+        // X'[s, :] = exp(cum[Q-1] - cum[s]) x[s, :] into buffer c % NXP, once the
+        // state update that read that buffer (chunk c - NXP) has completed
+        if (c >= Lo::NXP &&
+            !waitw(bar(B_EMPTY0 + (c - Lo::NXP) % NBUF), ((c - Lo::NXP) / NBUF) & 1, abort_flag, 33))
+          break;
+        const uint32_t src = xt(lb), dst = base + Lo::OFF_XP + xb * Lo::kX;
+#pragma unroll 1
+        for (int rr = 0; rr < (NN == 128 ? 1 : 2); ++rr) {
+          const int s = NN == 128 ? r : (q - 2) * 32 + lane + 64 * rr;
+          const uint64_t w2 = f2_splat(ex2_approx((last - cm[s]) * kLog2e));
+#pragma unroll
+          for (int jc = 0; jc < PP / 8; ++jc) {
+            const uint32_t off = (jc >> 3) * 16384 + sw_off(s, jc & 7);
+            const uint4 u = ld_shared_v4(src + off);
+            st_shared_v4(dst + off, make_uint4(f2_to_bf2(f2_mul(f2_from_bf2(u.x), w2)),
+                                               f2_to_bf2(f2_mul(f2_from_bf2(u.y), w2)),
+                                               f2_to_bf2(f2_mul(f2_from_bf2(u.z), w2)),
+                                               f2_to_bf2(f2_mul(f2_from_bf2(u.w), w2))));
+          }
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_XP_READY0 + xb));
+      }
       if (has_row) {
+        // the previous state update (and Y(c-1), issued before it) has completed
+        if (c > 0 && !waitw(bar(B_ST_DONE), (c - 1) & 1, abort_flag, 32)) break;
+        if (warp == kStateWarp0) ALLOY_SCAN_TRACE(10, c);
+        tc_fence_after();
         const float e = ex2_approx(last * kLog2e);
         const uint32_t hrow = base + Lo::OFF_H;
-#pragma unroll 1
-        for (int p0 = 0; p0 < PP; p0 += 16) {
-          uint32_t v[16];
-          tmem_ld16(lane_base + Lo::T_ST + p0, v);
-          tmem_ld_wait();
+        auto copy = [&](int p0, uint32_t (&v)[16]) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            const int j = p0 / 8 + hh;   // 16-byte chunk of the state row (8 p)
-            st_shared_v4(hrow + (j >> 3) * (NN * 128) + sw_off(r, j & 7),
+            const int jc = p0 / 8 + hh;   // 16-byte chunk of the state row (8 p)
+            st_shared_v4(hrow + (jc >> 3) * (NN * 128) + sw_off(r, jc & 7),
                          make_uint4(pack_bf16x2(__uint_as_float(v[8 * hh + 0]), __uint_as_float(v[8 * hh + 1])),
                                     pack_bf16x2(__uint_as_float(v[8 * hh + 2]), __uint_as_float(v[8 * hh + 3])),
                                     pack_bf16x2(__uint_as_float(v[8 * hh + 4]), __uint_as_float(v[8 * hh + 5])),
@@ -424,30 +562,28 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
 #pragma unroll
           for (int k = 0; k < 16; ++k) v[k] = __float_as_uint(e * __uint_as_float(v[k]));
           tmem_st16(lane_base + Lo::T_ST + p0, v);
+        };
+        // two 16-column pieces in flight
+#pragma unroll 1
+        for (int p0 = 0; p0 < PP; p0 += 32) {
+          uint32_t va[16], vb[16];
+          tmem_ld16(lane_base + Lo::T_ST + p0, va);
+          tmem_ld16(lane_base + Lo::T_ST + p0 + 16, vb);
+          tmem_ld_wait_regs(va);
+          tmem_ld_wait_regs(vb);
+          copy(p0, va);
+          copy(p0 + 16, vb);
         }
+        fence_async_smem();
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (warp == kStateWarp0) ALLOY_SCAN_TRACE(11, c);
+        if (lane == 0) mbar_arrive(bar(B_ST_READY));
       }
-      {
-        // X'[s, :] = exp(cum[Q-1] - cum[s]) x[s, :]
-        const float w = ex2_approx((last - cm[r]) * kLog2e);
-        const uint32_t src = xt(buf), dst = base + Lo::OFF_XP;
-#pragma unroll
-        for (int j = 0; j < PP / 8; ++j) {
-          const uint32_t off = (j >> 3) * 16384 + sw_off(r, j & 7);
-          const uint4 u = ld_shared_v4(src + off);
-          st_shared_v4(dst + off, make_uint4(pack_bf16x2(w * bf16_lo(u.x), w * bf16_hi(u.x)),
-                                             pack_bf16x2(w * bf16_lo(u.y), w * bf16_hi(u.y)),
-                                             pack_bf16x2(w * bf16_lo(u.z), w * bf16_hi(u.z)),
-                                             pack_bf16x2(w * bf16_lo(u.w), w * bf16_hi(u.w))));
-        }
-      }
-      fence_async_smem();
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_ST_READY));
     }
     // the final state
-    if (!*abort_flag && a.ssm_out && nk > 0 && waitw(bar(B_ST_DONE), (nk - 1) & 1, abort_flag, 33)) {
+    if (has_row && !*abort_flag && a.ssm_out && nk > 0 && waitw(bar(B_ST_DONE), (nk - 1) & 1, abort_flag, 34)) {
       tc_fence_after();
       if (has_row) {
 #pragma unroll 1
@@ -467,8 +603,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
     // y (optional) and the row dot products with z (optional)
     const int zh = a.z_hpg > 1 ? h / a.z_hpg : h;
     for (int c = 0; c < nk; ++c) {
-      const int yb = c & 1;
-      if (!waitw(bar(B_Y_FULL0 + yb), (c >> 1) & 1, abort_flag, 40)) break;
+      const int yb = c % Lo::NYB;
+      if (!waitw(bar(B_Y_FULL0 + yb), (c / Lo::NYB) & 1, abort_flag, 40)) break;
+      if (warp == kOutWarp0) ALLOY_SCAN_TRACE(12, c);
       tc_fence_after();
       const int t = c * Q + r;
       const int64_t yoff = (int64_t)b * a.y_sb + (int64_t)t * a.y_st + (int64_t)h * a.y_sh;
@@ -531,6 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
       if (a.dot && t < L) a.dot[(int64_t)b * a.dot_sb + (int64_t)t * a.dot_st + (int64_t)h * a.dot_sh] = dot;
       tc_fence_before();
       __syncwarp();
+      if (warp == kOutWarp0) ALLOY_SCAN_TRACE(13, c);
       if (lane == 0) mbar_arrive(bar(B_Y_EMPTY0 + yb));
     }
   }
