@@ -55,12 +55,13 @@ namespace {
 using namespace tc;
 
 constexpr int Q = 128;
-constexpr int kWarps = 21;
+constexpr int kWarps = 23;
 constexpr int kThreads = kWarps * 32;
 constexpr int kStateWarp0 = 8;
 constexpr int kOutWarp0 = 12;
 constexpr int kLoadWarp0 = 16;
-constexpr int kMmaWarp = 20;
+constexpr int kStateWarpX0 = 20;   // two more state warps (lane quadrants 0 and 1)
+constexpr int kMmaWarp = 22;
 constexpr long long kWaitCycles = 4000000000LL;   // ~2 s at 1.9 GHz
 constexpr int kL2Ahead = 3;                         // chunks prefetched into L2 ahead of their loads
 constexpr float kLog2e = 1.4426950408889634f;
@@ -95,8 +96,10 @@ struct Layout {
   static constexpr uint32_t OFF_ZERO = NBUF * kBuf;  // 16 KB of zeros: the B tile's second block for NN = 64
   static constexpr int NXP = PP == 128 ? 1 : 2;      // X' buffers
   static constexpr uint32_t OFF_XP = OFF_ZERO + (NN == 64 ? 16384 : 0);   // NXP x X' [PP/64][128][64]
-  static constexpr uint32_t OFF_H = OFF_XP + NXP * kX;   // H [PP/64][NN][64]
-  static constexpr uint32_t OFF_LA = OFF_H + PP * NN * 2;          // [NBUF][128] f32
+  static constexpr int NH = (PP == 64 && NN == 128) ? 1 : 2;   // H buffers
+  static constexpr uint32_t kH = PP * NN * 2;
+  static constexpr uint32_t OFF_H = OFF_XP + NXP * kX;   // NH x H [PP/64][NN][64]
+  static constexpr uint32_t OFF_LA = OFF_H + NH * kH;              // [NBUF][128] f32
   static constexpr uint32_t OFF_CUM = OFF_LA + NBUF * 512;         // [NBUF][128] f32
   static constexpr uint32_t OFF_CF = OFF_CUM + NBUF * 512;         // [NBUF][128] f32 column factors
   static constexpr uint32_t OFF_WSUM = OFF_CF + NBUF * 512;        // [NBUF][4] f32
@@ -222,8 +225,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
     for (int i = 0; i < kMaxBuf; ++i) counts[B_FULL0 + i] = counts[B_CUM0 + i] = 4;
     counts[B_S_READY0] = counts[B_S_READY0 + 1] = 8;
     counts[B_Y_EMPTY0] = counts[B_Y_EMPTY0 + 1] = counts[B_PWG] = 4;
-    // d_state 64: warps 8-9 copy the state, 10-11 write X'; 128: all four do both
-    counts[B_ST_READY] = counts[B_XP_READY0] = counts[B_XP_READY0 + 1] = NN == 64 ? 2 : 4;
+    // four warps copy the state, two write X'
+    counts[B_ST_READY] = 4;
+    counts[B_XP_READY0] = counts[B_XP_READY0 + 1] = 2;
     for (int i = 0; i < NBAR; ++i) mbar_init(bar(i), counts[i]);
     mbar_fence_init();
   }
@@ -253,9 +257,13 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
       constexpr uint32_t ID_CB = idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t ID_Y = idesc_bf16(128, PP, 0, 1);
       constexpr uint32_t ID_ST = idesc_bf16(128, PP, 1, 1);
-      int ncb = 0, ny = 0;
+      // With two H buffers the state update of chunk c runs as soon as the
+      // state is decayed and X' written, ahead of Y (which reads H); with one,
+      // after Y.  The load buffer is released once both were issued.
+      constexpr int NH = Lo::NH;
+      int ncb = 0, ny = 0, nst = 0;
       long long t0 = clock64();
-      while (ny < nk) {
+      while (ny < nk || nst < nk) {
         bool progress = false;
         if (ncb < nk && ncb <= ny + 1) {
           const int lb = ncb % NBUF, j = ncb & 1;
@@ -272,24 +280,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
             progress = true;
           }
         }
-        if (ny < ncb) {
-          const int c = ny, lb = c % NBUF, j = c & 1, yb = c % NYB;
-          const int xb = c % Lo::NXP;
-          if (mbar_test(bar(B_S_READY0 + j), (c >> 1) & 1) && mbar_test(bar(B_ST_READY), c & 1) &&
-              mbar_test(bar(B_XP_READY0 + xb), (c / Lo::NXP) & 1) &&
-              (c < NYB || mbar_test(bar(B_Y_EMPTY0 + yb), ((c / NYB) - 1) & 1))) {
-            ALLOY_SCAN_TRACE(3, c);
+        if (nst < nk && (NH == 2 || ny > nst)) {
+          const int c = nst, lb = c % NBUF, xb = c % Lo::NXP;
+          if (mbar_test(bar(B_ST_READY), c & 1) && mbar_test(bar(B_XP_READY0 + xb), (c / Lo::NXP) & 1)) {
             tc_fence_after();
-            // Y = S x + C~ H
-            const uint32_t ty = tmem + Lo::T_Y + yb * PP, tcb = tmem + Lo::T_CB + 128 * j;
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-              umma_bf16_ta(ty, tcb + 16 * k, sw128_desc(xt(lb) + 2048 * k, 16384, 1024), ID_Y, k != 0);
-#pragma unroll
-            for (int k = 0; k < NN / 16; ++k)
-              umma_bf16_ta(ty, tcb + 16 * k + 8, sw128_desc(base + Lo::OFF_H + 2048 * k, NN * 128, 1024), ID_Y, 1);
-            umma_commit(bar(B_Y_FULL0 + yb));
-            umma_commit(bar(B_CB_FREE0 + j));
             // state[n, p] += sum_s B[s, n] X'[s, p]; rows n >= NN of A read the zero block
             const uint32_t lbo = NN == 64 ? Lo::OFF_ZERO - (bt(lb) - base) : 16384;
 #pragma unroll
@@ -297,7 +291,30 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
               umma_bf16(tmem + Lo::T_ST, sw128_desc(bt(lb) + 2048 * k, lbo, 1024),
                         sw128_desc(base + Lo::OFF_XP + xb * Lo::kX + 2048 * k, 16384, 1024), ID_ST, 1);
             umma_commit(bar(B_ST_DONE));
-            umma_commit(bar(B_EMPTY0 + lb));
+            if (ny > c) umma_commit(bar(B_EMPTY0 + lb));
+            ++nst;
+            progress = true;
+          }
+        }
+        if (ny < ncb && (NH == 1 || nst > ny)) {
+          const int c = ny, lb = c % NBUF, j = c & 1, yb = c % NYB;
+          if (mbar_test(bar(B_S_READY0 + j), (c >> 1) & 1) &&
+              (NH == 2 || mbar_test(bar(B_ST_READY), c & 1)) &&
+              (c < NYB || mbar_test(bar(B_Y_EMPTY0 + yb), ((c / NYB) - 1) & 1))) {
+            ALLOY_SCAN_TRACE(3, c);
+            tc_fence_after();
+            // Y = S x + C~ H
+            const uint32_t ty = tmem + Lo::T_Y + yb * PP, tcb = tmem + Lo::T_CB + 128 * j;
+            const uint32_t sh = base + Lo::OFF_H + (c % NH) * Lo::kH;
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              umma_bf16_ta(ty, tcb + 16 * k, sw128_desc(xt(lb) + 2048 * k, 16384, 1024), ID_Y, k != 0);
+#pragma unroll
+            for (int k = 0; k < NN / 16; ++k)
+              umma_bf16_ta(ty, tcb + 16 * k + 8, sw128_desc(sh + 2048 * k, NN * 128, 1024), ID_Y, 1);
+            umma_commit(bar(B_Y_FULL0 + yb));
+            umma_commit(bar(B_CB_FREE0 + j));
+            if (nst > c) umma_commit(bar(B_EMPTY0 + lb));
             ALLOY_SCAN_TRACE(5, c);
             ++ny;
             progress = true;
@@ -320,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
       while (!mbar_try_wait(bar(B_DRAIN), 0) && clock64() - t1 < kWaitCycles) {
       }
     }
-  } else if (warp >= kLoadWarp0) {
+  } else if (warp >= kLoadWarp0 && warp < kLoadWarp0 + 4) {
     // ------------------------------------------------------------------ loads
     const int i = threadIdx.x - 32 * kLoadWarp0;
     const int xh = a.x_hpg > 1 ? h / a.x_hpg : h;
@@ -491,33 +508,42 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
       if (warp == 0) ALLOY_SCAN_TRACE(14, c);
       if (lane == 0) mbar_arrive(bar(B_S_READY0 + j));
     }
-  } else if (warp < kOutWarp0) {
+  } else if (warp < kOutWarp0 || warp >= kStateWarpX0) {
     // ------------------------------------------------------------------ state and X'
-    // For d_state 64 the state rows live in lanes 0-63: warps 8-9 copy and
-    // decay them while warps 10-11 scale X' (two rows a thread); for 128 every
-    // warp does both for its own rows.
-    const bool has_row = r < NN;   // warp-uniform
-    const bool does_xp = NN == 128 || q >= 2;
-    // initial state (rows n >= NN stay zero)
+    // Four warps copy and decay the state, two write X'.  d_state 64 (state
+    // rows in lanes 0-63): warps 8 and 20 (quadrant 0) and 9 and 21 (quadrant 1)
+    // take half of the columns each, warps 10-11 write X'.  d_state 128: warps
+    // 8-11 take whole rows, warps 20-21 write X'.  X' rows: two a thread.
+    const bool extra = warp >= kStateWarpX0;
+    const bool h_role = NN == 64 ? (q < 2) : !extra;
+    const bool xp_role = !h_role;
+    const int p_lo = NN == 64 ? (extra ? PP / 2 : 0) : 0;
+    const int p_hi = NN == 64 ? (extra ? PP : PP / 2) : PP;
+    const int xq = NN == 64 ? q - 2 : q;   // X' warps: quadrants 2-3 (d_state 64) or 0-1 (128)
+    // initial state: each copy warp its own columns; for d_state 64 warps
+    // 10-11 zero the unused rows 64-127 (ordered before the first state update
+    // by their X' barrier)
+    if (h_role || (NN == 64 && !extra)) {
 #pragma unroll 1
-    for (int p0 = 0; p0 < PP; p0 += 16) {
-      uint32_t v[16];
+      for (int p0 = h_role ? p_lo : 0; p0 < (h_role ? p_hi : PP); p0 += 16) {
+        uint32_t v[16];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        float f = 0.f;
-        if (has_row && a.ssm_in)
-          f = a.ssm_in[(int64_t)b * a.si_sb + (int64_t)h * a.si_sh + (int64_t)r * a.si_sn + (int64_t)(p0 + k) * a.si_sp];
-        v[k] = __float_as_uint(f);
+        for (int k = 0; k < 16; ++k) {
+          float f = 0.f;
+          if (r < NN && a.ssm_in)
+            f = a.ssm_in[(int64_t)b * a.si_sb + (int64_t)h * a.si_sh + (int64_t)r * a.si_sn + (int64_t)(p0 + k) * a.si_sp];
+          v[k] = __float_as_uint(f);
+        }
+        tmem_st16(lane_base + Lo::T_ST + p0, v);
       }
-      tmem_st16(lane_base + Lo::T_ST + p0, v);
+      tmem_st_wait();
     }
-    tmem_st_wait();
     for (int c = 0; c < nk; ++c) {
       const int lb = c % NBUF, xb = c % Lo::NXP;
       if (!waitw(bar(B_CUM0 + lb), (c / NBUF) & 1, abort_flag, 31)) break;
       const float* cm = cum_s + lb * 128;
       const float last = cm[127];
-      if (does_xp) {
+      if (xp_role) {
         // X'[s, :] = exp(cum[Q-1] - cum[s]) x[s, :] into buffer c % NXP, once the
         // state update that read that buffer (chunk c - NXP) has completed
         if (c >= Lo::NXP &&
@@ -525,8 +551,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
           break;
         const uint32_t src = xt(lb), dst = base + Lo::OFF_XP + xb * Lo::kX;
 #pragma unroll 1
-        for (int rr = 0; rr < (NN == 128 ? 1 : 2); ++rr) {
-          const int s = NN == 128 ? r : (q - 2) * 32 + lane + 64 * rr;
+        for (int rr = 0; rr < 2; ++rr) {
+          const int s = xq * 32 + lane + 64 * rr;
           const uint64_t w2 = f2_splat(ex2_approx((last - cm[s]) * kLog2e));
 #pragma unroll
           for (int jc = 0; jc < PP / 8; ++jc) {
@@ -539,16 +565,18 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
           }
         }
         fence_async_smem();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_XP_READY0 + xb));
-      }
-      if (has_row) {
-        // the previous state update (and Y(c-1), issued before it) has completed
+      } else {
+        // the previous state update has completed, and (two H buffers) the Y
+        // that read this chunk's H buffer (chunk c - 2)
         if (c > 0 && !waitw(bar(B_ST_DONE), (c - 1) & 1, abort_flag, 32)) break;
+        if (Lo::NH == 2 && c >= 2 && !waitw(bar(B_CB_FREE0 + (c & 1)), ((c - 2) >> 1) & 1, abort_flag, 35)) break;
         if (warp == kStateWarp0) ALLOY_SCAN_TRACE(10, c);
         tc_fence_after();
         const float e = ex2_approx(last * kLog2e);
-        const uint32_t hrow = base + Lo::OFF_H;
+        const uint32_t hrow = base + Lo::OFF_H + (c % Lo::NH) * Lo::kH;
         auto copy = [&](int p0, uint32_t (&v)[16]) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
@@ -565,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
         };
         // two 16-column pieces in flight
 #pragma unroll 1
-        for (int p0 = 0; p0 < PP; p0 += 32) {
+        for (int p0 = p_lo; p0 < p_hi; p0 += 32) {
           uint32_t va[16], vb[16];
           tmem_ld16(lane_base + Lo::T_ST + p0, va);
           tmem_ld16(lane_base + Lo::T_ST + p0 + 16, vb);
@@ -583,11 +611,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
       }
     }
     // the final state
-    if (has_row && !*abort_flag && a.ssm_out && nk > 0 && waitw(bar(B_ST_DONE), (nk - 1) & 1, abort_flag, 34)) {
+    if (h_role && !*abort_flag && a.ssm_out && nk > 0 && waitw(bar(B_ST_DONE), (nk - 1) & 1, abort_flag, 34)) {
       tc_fence_after();
-      if (has_row) {
+      {
 #pragma unroll 1
-        for (int p0 = 0; p0 < PP; p0 += 16) {
+        for (int p0 = p_lo; p0 < p_hi; p0 += 16) {
           uint32_t v[16];
           tmem_ld16(lane_base + Lo::T_ST + p0, v);
           tmem_ld_wait();
