@@ -118,6 +118,35 @@ def test_selective_scan_rejects_group_mismatch():
     assert st == -1 and "does not divide" in _lib.last_error()
 
 
+def _scan_dot(**over):
+    B, L, H, P, N = 2, 16, 8, 64, 64
+    BF = _lib.BF16
+    t = dict(x=_t([B, L, 2, P], BF), la=_t([B, L, H]), Bm=_t([B, L, 1, N], BF), Cm=_t([B, L, 1, N], BF),
+             si=_lib.Tensor(), y=_t([B, L, H, P]), so=_lib.Tensor(), z=_t([B, L, H, P], BF),
+             dot=_t([B, L, H]))
+    t.update(over)
+    lib = _lib.load()
+    order = ["x", "la", "Bm", "Cm", "si", "y", "so", "z", "dot"]
+    st = lib.alloy_selective_scan_dot(*(ctypes.byref(t[k]) for k in order), None)
+    return st, _lib.last_error()
+
+
+@pytest.mark.parametrize("over,needle", [
+    (dict(y=_lib.Tensor(), dot=_lib.Tensor()), "neither y nor dot"),
+    (dict(x=_t([2, 16, 2, 64])), "x: unsupported dtype"),
+    (dict(x=_t([2, 16, 3, 64], _lib.BF16)), "x: dim 2 (3) does not divide"),
+    (dict(la=_lib.Tensor()), "log_a: null"),
+    (dict(Bm=_t([2, 16, 1, 64])), "B: unsupported dtype"),
+    (dict(z=_lib.Tensor()), "z: null"),
+    (dict(z=_t([2, 16, 8, 64], _lib.BF16, strides=[16 * 8 * 128, 8 * 128, 128, 2])), "z: head_dim stride"),
+    (dict(dot=_t([2, 16, 4])), "dot: dim 2"),
+])
+def test_selective_scan_dot_rejects_bad_arguments(over, needle):
+    st, msg = _scan_dot(**over)
+    assert st == -1, (st, msg)
+    assert needle in msg, msg
+
+
 def test_error_message_is_per_thread():
     import threading
     _combined(xBC=_lib.Tensor())
