@@ -7,7 +7,7 @@
 //
 // One CTA per (batch row, head) walks chunks of Q = 128 steps in order with
 // the fp32 state resident in tensor memory.  Per chunk (t, s < Q):
-//   cum[t]   = sum_{u<=t} la_u                               (score warps)
+//   cum[t]   = sum_{u<=t} la_u                               (load warps)
 //   CB       = C B^T                                         (tcgen05 -> TMEM)
 //   S[t,s]   = CB[t,s] exp(cum[t] - cum[s]) for s <= t, else 0  (bf16 pairs, in place over CB)
 //   C~[t,:]  = exp(cum[t]) C[t,:]                            (bf16 pairs, beside S)
@@ -26,10 +26,10 @@
 // second block, so the state MMA runs at M = 128 with the state's rows
 // 64..127 identically zero.
 //
-// Warp roles (21 warps): 0-7 scores and C~ (row t = lane quadrant, two warps
-// a quadrant splitting its columns; warps 0-3 also scan the decays); 8-11
-// state copy/decay (row n) and X' (row s); 12-15 output rows; 16-19 loads; 20
-// TMEM allocation and MMA issue.  CB is double-buffered in tensor memory, so
+// Warp roles (23 warps): 0-7 scores and C~ (row t = lane quadrant, two warps
+// a quadrant splitting its columns); 8-11 and 20-21 state copy/decay (row n)
+// and X' (row s); 12-15 output rows; 16-19 loads and the decay scan; 22 TMEM
+// allocation and MMA issue.  CB is double-buffered in tensor memory, so
 // the next chunk's C B^T runs while this chunk's scores are computed.  Every mbarrier wait is
 // bounded: on timeout the CTA records an error word, drains its copies and
 // MMAs, frees its tensor memory and exits.
@@ -69,10 +69,9 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMaxBuf = 3;   // load buffers (3 for head_dim = d_state = 64, else 2)
 
 enum {
-  B_FULL0 = 0,                         // loads -> all: x, B, C, la of buffer i (4 loader warps)
+  B_FULL0 = 0,                         // loads -> all: x, B, C, cum, column factors of buffer i (4 warps)
   B_EMPTY0 = B_FULL0 + kMaxBuf,        // MMA -> loads: buffer i read by every MMA
-  B_CUM0 = B_EMPTY0 + kMaxBuf,         // score warps -> all: cum and column factors of buffer i (4)
-  B_CB_FULL0 = B_CUM0 + kMaxBuf,       // MMA -> score warps: CB in TMEM buffer j (2)
+  B_CB_FULL0 = B_EMPTY0 + kMaxBuf,     // MMA -> score warps: CB in TMEM buffer j (2)
   B_CB_FREE0 = B_CB_FULL0 + 2,         // MMA -> MMA: Y that read TMEM buffer j completed (2)
   B_S_READY0 = B_CB_FREE0 + 2,         // score warps -> MMA: S and C~ in TMEM buffer j (2, 8 warps)
   B_ST_READY = B_S_READY0 + 2,         // state warps -> MMA: H written, state decayed
@@ -80,7 +79,7 @@ enum {
   B_Y_FULL0 = B_XP_READY0 + 2,         // MMA -> output warps (per output accumulator, 2)
   B_Y_EMPTY0 = B_Y_FULL0 + 2,          // output warps -> MMA (2, 4 warps)
   B_ST_DONE = B_Y_EMPTY0 + 2,          // MMA -> state warps: state update complete
-  B_PWG,                               // score warps: warp totals of the decay scan (4)
+  B_PWG,                               // loader warps: warp totals of the decay scan (4)
   B_DRAIN,
   NBAR
 };
@@ -99,8 +98,7 @@ struct Layout {
   static constexpr int NH = (PP == 64 && NN == 128) ? 1 : 2;   // H buffers
   static constexpr uint32_t kH = PP * NN * 2;
   static constexpr uint32_t OFF_H = OFF_XP + NXP * kX;   // NH x H [PP/64][NN][64]
-  static constexpr uint32_t OFF_LA = OFF_H + NH * kH;              // [NBUF][128] f32
-  static constexpr uint32_t OFF_CUM = OFF_LA + NBUF * 512;         // [NBUF][128] f32
+  static constexpr uint32_t OFF_CUM = OFF_H + NH * kH;             // [NBUF][128] f32
   static constexpr uint32_t OFF_CF = OFF_CUM + NBUF * 512;         // [NBUF][128] f32 column factors
   static constexpr uint32_t OFF_WSUM = OFF_CF + NBUF * 512;        // [NBUF][4] f32
   static constexpr uint32_t OFF_BAR = OFF_WSUM + 64;
@@ -201,7 +199,6 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_base);
-  float* la_s = reinterpret_cast<float*>(smem + Lo::OFF_LA);
   float* cum_s = reinterpret_cast<float*>(smem + Lo::OFF_CUM);
   float* cf_s = reinterpret_cast<float*>(smem + Lo::OFF_CF);
   float* wsum = reinterpret_cast<float*>(smem + Lo::OFF_WSUM);
@@ -222,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
     *abort_flag = 0;
     int counts[NBAR];
     for (int i = 0; i < NBAR; ++i) counts[i] = 1;
-    for (int i = 0; i < kMaxBuf; ++i) counts[B_FULL0 + i] = counts[B_CUM0 + i] = 4;
+    for (int i = 0; i < kMaxBuf; ++i) counts[B_FULL0 + i] = 4;
     counts[B_S_READY0] = counts[B_S_READY0 + 1] = 8;
     counts[B_Y_EMPTY0] = counts[B_Y_EMPTY0 + 1] = counts[B_PWG] = 4;
     // four warps copy the state, two write X'
@@ -378,7 +375,29 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
             la = logf(fmaxf(load_any(a.A_disc, (int64_t)b * a.ad_sb + (int64_t)t * a.ad_st + (int64_t)h * a.ad_sh,
                                      a.ad_bf16), 1e-10f));
         }
-        la_s[lb * 128 + i] = la;
+        // cum[t] = inclusive sum of la over the chunk, while the copies fly
+        float v = la;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float u = __shfl_up_sync(0xffffffffu, v, o);
+          if (lane >= o) v += u;
+        }
+        // warp totals: wsum[lb] for chunk c+NBUF is written only after every
+        // loader warp passed the PWG wait of chunk c+1, which follows its reads
+        const int ql = warp - kLoadWarp0;
+        if (lane == 31) wsum[lb * 4 + ql] = v;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_PWG));
+        if (!waitw(bar(B_PWG), c & 1, abort_flag, 11)) break;
+        float pre = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) pre += k < ql ? wsum[lb * 4 + k] : 0.f;
+        const float cum = v + pre;
+        // column factor of source s = i inside its 16-column piece: exp(cum[m] -
+        // cum[s]) <= 1, m the piece's last column (decays <= 1)
+        const float cum_m = __shfl_sync(0xffffffffu, cum, lane | 15);
+        cum_s[lb * 128 + i] = cum;
+        cf_s[lb * 128 + i] = ex2_approx((cum_m - cum) * kLog2e);
       }
       cp_async_wait_all();
       fence_async_smem();
@@ -389,41 +408,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
     cp_async_wait_all();
   } else if (warp < kStateWarp0) {
     // ------------------------------------------------------------------ scores
-    // Two warps a lane quadrant: `half` 0 (warps 0-3) also scans the decays;
-    // half 0 takes the even 16-column pieces of the row, half 1 the odd ones,
-    // and each stores its S and C~ K-steps inside pieces it read itself.
+    // Two warps a lane quadrant: `half` 0 (warps 0-3) takes the even
+    // 16-column pieces of the row, half 1 the odd ones, and each stores its S
+    // and C~ K-steps inside pieces it read itself.
     const int t = r, half = warp >> 2;
     for (int c = 0; c < nk; ++c) {
       const int lb = c % NBUF, j = c & 1;
-      if (half == 0) {
-        if (!waitw(bar(B_FULL0 + lb), (c / NBUF) & 1, abort_flag, 20)) break;
-        // cum[t] = inclusive sum of la over the chunk
-        float v = la_s[lb * 128 + t];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float u = __shfl_up_sync(0xffffffffu, v, o);
-          if (lane >= o) v += u;
-        }
-        // warp totals: wsum[lb] for chunk c+NBUF is written only after every
-        // warp passed the PWG wait of a later chunk, which follows its reads
-        if (lane == 31) wsum[lb * 4 + q] = v;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_PWG));
-        if (!waitw(bar(B_PWG), c & 1, abort_flag, 21)) break;
-        float pre = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) pre += k < q ? wsum[lb * 4 + k] : 0.f;
-        const float cum = v + pre;
-        // column factor of source s = t inside its 16-column piece: exp(cum[m] -
-        // cum[s]) <= 1, m the piece's last column (decays <= 1)
-        const float cum_m = __shfl_sync(0xffffffffu, cum, lane | 15);
-        cum_s[lb * 128 + t] = cum;
-        cf_s[lb * 128 + t] = ex2_approx((cum_m - cum) * kLog2e);
-        __syncwarp();
-        if (warp == 3) ALLOY_SCAN_TRACE(6, c);
-        if (lane == 0) mbar_arrive(bar(B_CUM0 + lb));
-      }
-      if (!waitw(bar(B_CUM0 + lb), (c / NBUF) & 1, abort_flag, 22)) break;
+      if (!waitw(bar(B_FULL0 + lb), (c / NBUF) & 1, abort_flag, 22)) break;
+      if (warp == 3) ALLOY_SCAN_TRACE(6, c);
       if (!waitw(bar(B_CB_FULL0 + j), (c >> 1) & 1, abort_flag, 23)) break;
       if (warp == 3) ALLOY_SCAN_TRACE(7, c);
       tc_fence_after();
@@ -540,7 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
     }
     for (int c = 0; c < nk; ++c) {
       const int lb = c % NBUF, xb = c % Lo::NXP;
-      if (!waitw(bar(B_CUM0 + lb), (c / NBUF) & 1, abort_flag, 31)) break;
+      if (!waitw(bar(B_FULL0 + lb), (c / NBUF) & 1, abort_flag, 31)) break;
       const float* cm = cum_s + lb * 128;
       const float last = cm[127];
       if (xp_role) {
