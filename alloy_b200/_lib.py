@@ -138,7 +138,7 @@ def load():
         lib.alloy_kernel_launch_count.restype = ctypes.c_uint64
         lib.alloy_ssd_combined_noalloc.argtypes = [P] * 12 + [D, vp]
         lib.alloy_selective_scan.argtypes = [P] * 8 + [vp]
-        lib.alloy_selective_scan_dot.argtypes = [P] * 9 + [vp]
+        lib.alloy_selective_scan_dot.argtypes = [P] * 9 + [ctypes.c_int32, vp]
         lib.alloy_ssd_decode_step.argtypes = [P] * 10 + [D, vp]
         for name in ("alloy_conv1d_silu", "alloy_depthwise_conv1d", "alloy_conv1d_silu_backward",
                      "alloy_ssd_combined",

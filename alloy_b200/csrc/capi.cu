@@ -425,9 +425,10 @@ int alloy_selective_scan(const alloy_tensor_t* x, const alloy_tensor_t* A_disc,
 int alloy_selective_scan_dot(const alloy_tensor_t* x, const alloy_tensor_t* log_a,
                              const alloy_tensor_t* Bm, const alloy_tensor_t* Cm,
                              const alloy_tensor_t* ssm_in, alloy_tensor_t* y, alloy_tensor_t* ssm_out,
-                             const alloy_tensor_t* z, alloy_tensor_t* dot, void* stream) {
+                             const alloy_tensor_t* z, alloy_tensor_t* dot, int32_t dot_mode, void* stream) {
   last_error().clear();
   if (!present(y) && !present(dot)) return fail(ALLOY_ERR_INVALID_ARG, "selective_scan_dot: neither y nor dot");
+  if (dot_mode != 0 && dot_mode != 1) return fail(ALLOY_ERR_INVALID_ARG, "selective_scan_dot: dot_mode must be 0 or 1");
   ALLOY_TRY(check_tensor(x, "x", 4, nullptr, kBF16));
   const alloy_tensor_t* ref = present(y) ? y : dot;
   const int64_t B = x->shape[0], L = x->shape[1], P = x->shape[3];
@@ -500,6 +501,7 @@ int alloy_selective_scan_dot(const alloy_tensor_t* x, const alloy_tensor_t* log_
     a.z_sb = z->stride[0]; a.z_st = z->stride[1]; a.z_sh = z->stride[2];
     a.dot = static_cast<float*>(dot->data);
     a.dot_sb = dot->stride[0]; a.dot_st = dot->stride[1]; a.dot_sh = dot->stride[2];
+    a.dot_nodiag = dot_mode;
   }
   if (!scan_tc_supported(a))
     return fail(ALLOY_ERR_UNSUPPORTED,

@@ -54,6 +54,9 @@ struct SsdArgs {
   int x_hpg;
   const void* z; int z_bf16; int64_t z_sb, z_st, z_sh; int z_hpg;
   float* dot; int64_t dot_sb, dot_st, dot_sh;
+  // dot_nodiag: the dot products leave out the step's own term, S[t,t] (x_t . z_t)
+  // with S[t,t] = C_t . B_t as the kernel rounds it
+  int dot_nodiag;
 };
 
 // scan_tc.cu: tcgen05 scan on pre-discretised bf16 inputs (mode 1: x, B, C

@@ -100,7 +100,8 @@ struct Layout {
   static constexpr uint32_t OFF_H = OFF_XP + NXP * kX;   // NH x H [PP/64][NN][64]
   static constexpr uint32_t OFF_CUM = OFF_H + NH * kH;             // [NBUF][128] f32
   static constexpr uint32_t OFF_CF = OFF_CUM + NBUF * 512;         // [NBUF][128] f32 column factors
-  static constexpr uint32_t OFF_WSUM = OFF_CF + NBUF * 512;        // [NBUF][4] f32
+  static constexpr uint32_t OFF_DIAG = OFF_CF + NBUF * 512;        // [4 chunks][128] f32: S[t,t] as rounded
+  static constexpr uint32_t OFF_WSUM = OFF_DIAG + 4 * 512;         // [NBUF][4] f32
   static constexpr uint32_t OFF_BAR = OFF_WSUM + 64;
   static constexpr uint32_t OFF_TMEMPTR = OFF_BAR + NBAR * 8;
   static constexpr uint32_t OFF_ABORT = OFF_TMEMPTR + 8;
@@ -201,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
   uint8_t* smem = smem_raw + (base - raw_base);
   float* cum_s = reinterpret_cast<float*>(smem + Lo::OFF_CUM);
   float* cf_s = reinterpret_cast<float*>(smem + Lo::OFF_CF);
+  float* diag_s = reinterpret_cast<float*>(smem + Lo::OFF_DIAG);
   float* wsum = reinterpret_cast<float*>(smem + Lo::OFF_WSUM);
   volatile uint32_t* tmem_ptr = reinterpret_cast<volatile uint32_t*>(smem + Lo::OFF_TMEMPTR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Lo::OFF_ABORT);
@@ -442,13 +444,17 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
                        f2_pack(f.z, f.w)));
           }
         } else {
-          // the diagonal block: exact factors, zero right of the diagonal
+          // the diagonal block: exact factors, zero right of the diagonal; S[t,t]
+          // as rounded is kept for the output rows (slot c % 4: the rows of
+          // chunk c are read out before the scores of chunk c + 4 start)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int s = 16 * k + 2 * e;
             const float f0 = __uint_as_float(rv[2 * e]) * ex2_approx(fmaf(-cm[s], kLog2e, ct2));
             const float f1 = __uint_as_float(rv[2 * e + 1]) * ex2_approx(fmaf(-cm[s + 1], kLog2e, ct2));
             o[e] = pack_bf16x2(s <= t ? f0 : 0.f, s + 1 <= t ? f1 : 0.f);
+            if (s == t) diag_s[(c & 3) * 128 + t] = bf16_lo(o[e]);
+            if (s + 1 == t) diag_s[(c & 3) * 128 + t] = bf16_hi(o[e]);
           }
         }
         tmem_st8(tcb + 16 * k, o);
@@ -685,7 +691,39 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
           }
         }
       }
-      if (a.dot && t < L) a.dot[(int64_t)b * a.dot_sb + (int64_t)t * a.dot_st + (int64_t)h * a.dot_sh] = dot;
+      if (a.dot && t < L) {
+        if (a.dot_nodiag) {
+          // leave out S[t,t] (x_t . z_t), the step's own term as the MMA saw it
+          const int xh = a.x_hpg > 1 ? h / a.x_hpg : h;
+          const uint4* xp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.x) + (int64_t)b * a.x_sb +
+                                                           (int64_t)t * a.x_st + (int64_t)xh * a.x_sh);
+          float xz = 0.f;
+#pragma unroll 2
+          for (int m = 0; m < PP / 8; ++m) {
+            const uint4 xx = __ldg(xp + m);
+            const uint32_t xw[4] = {xx.x, xx.y, xx.z, xx.w};
+            float zf[8];
+            if (a.z_bf16) {
+              const uint4 zz = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.z) + zoff) + m);
+              const uint32_t zw[4] = {zz.x, zz.y, zz.z, zz.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) { zf[2 * e] = bf16_lo(zw[e]); zf[2 * e + 1] = bf16_hi(zw[e]); }
+            } else {
+              const float4* zp = reinterpret_cast<const float4*>(static_cast<const float*>(a.z) + zoff) + 2 * m;
+              const float4 z0 = __ldg(zp), z1 = __ldg(zp + 1);
+              zf[0] = z0.x; zf[1] = z0.y; zf[2] = z0.z; zf[3] = z0.w;
+              zf[4] = z1.x; zf[5] = z1.y; zf[6] = z1.z; zf[7] = z1.w;
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              xz = fmaf(bf16_lo(xw[e]), zf[2 * e], xz);
+              xz = fmaf(bf16_hi(xw[e]), zf[2 * e + 1], xz);
+            }
+          }
+          dot = fmaf(-diag_s[(c & 3) * 128 + r], xz, dot);
+        }
+        a.dot[(int64_t)b * a.dot_sb + (int64_t)t * a.dot_st + (int64_t)h * a.dot_sh] = dot;
+      }
       tc_fence_before();
       __syncwarp();
       if (warp == kOutWarp0) ALLOY_SCAN_TRACE(13, c);

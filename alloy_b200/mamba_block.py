@@ -147,9 +147,15 @@ class MambaBlock(torch.nn.Module):
         xh = xs.reshape(Bsz, L, H, P).float()
         dtv = F.softplus(dt.float() + self.dt_bias)
         log_a = dtv * -torch.exp(self.A_log.float())
-        y, _ = mixer.SelectiveScan.apply(xh * dtv[..., None], None,
-                                         Bm.reshape(Bsz, L, G, N).float(),
-                                         Cm.reshape(Bsz, L, G, N).float(), None, log_a)
+        xin, Bin, Cin = xh * dtv[..., None], Bm.reshape(Bsz, L, G, N), Cm.reshape(Bsz, L, G, N)
+        if xBC.dtype == torch.bfloat16:
+            # bf16 operands, as the reference's bf16 arrays are: the scan and its
+            # gradient run on the tensor-core scan (fp32 state and accumulation)
+            xin = xin.to(torch.bfloat16)
+        else:
+            Bin, Cin = Bin.float(), Cin.float()
+        y, _ = mixer.SelectiveScan.apply(xin, None, Bin, Cin, None, log_a)
+        y = y.float()
         if self.D is not None:
             y = y + self.D.float()[:, None] * xh
         y = y.to(xBC.dtype).reshape(Bsz, L, self.d_inner)

@@ -367,7 +367,7 @@ def selective_scan(x, A_disc, B, C, ssm_state=None, log_a=None, out=None, out_dt
 
 
 def selective_scan_dot(x, B, C, log_a, *, z=None, ssm_state=None, y_dtype=torch.float32, write_y=True,
-                       write_ssm_state=False, reverse_time=False):
+                       write_ssm_state=False, reverse_time=False, dot_without_own_term=False):
     """The scan of ``selective_scan`` on the tensor cores (``alloy_selective_scan_dot``)
     for bf16 operands, with x and the dot operand shared across heads and the
     row dot products fused: the gradient scans of ``selective_scan_backward``.
@@ -376,7 +376,9 @@ def selective_scan_dot(x, B, C, log_a, *, z=None, ssm_state=None, y_dtype=torch.
     B/C [B, L, G', N] bf16, log_a [B, L, H] fp32 (<= 0; H is its dim 2),
     z [B, L, Gz, P] (optional).  Returns (y [B, L, H, P] of ``y_dtype`` or None,
     final state [B, H, N, P] fp32 or None, dot [B, L, H] fp32 or None) with
-    dot[b, t, h] = sum_p y[b, t, h, p] z[b, t, h // (H // Gz), p].
+    dot[b, t, h] = sum_p y[b, t, h, p] z[b, t, h // (H // Gz), p]; with
+    ``dot_without_own_term`` the step's own term S[t,t] (x_t . z_t), S[t,t] = C_t . B_t
+    as the kernel rounds it, is left out.
     """
     dev = _same_device(("x", x), ("B", B), ("C", C), ("log_a", log_a), ("z", z),
                        ("ssm_state", ssm_state))
@@ -394,7 +396,8 @@ def selective_scan_dot(x, B, C, log_a, *, z=None, ssm_state=None, y_dtype=torch.
                 d.data += (L - 1) * t.stride(1) * t.element_size()
                 d.stride[1] = -t.stride(1)
     with torch.cuda.device(dev):
-        _lib.call("alloy_selective_scan_dot", *(_lib.ref(d) for d in descs), _lib.stream_handle(dev))
+        _lib.call("alloy_selective_scan_dot", *(_lib.ref(d) for d in descs), int(dot_without_own_term),
+                  _lib.stream_handle(dev))
     return y, h_out, dot
 
 
@@ -423,10 +426,11 @@ def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dss
       dla_t = <dssm_state_out, h_{L-1}> + sum_{u >= t} (dy_u . y_u - B_u . dB_u).
     ``dlog_a`` is returned when ``log_a`` was given (the decay came from it),
     else ``dA_disc`` = dla / A_disc.  All arithmetic in fp32; the gradients have
-    the dtypes of their inputs.  When x, B and C are bf16 the four scans take
-    bf16 operands (x, B, C and dy as given, dy rounded to bf16) and run on the
-    tensor-core scan, with fp32 outputs, states and decay arithmetic, as a bf16
-    model's autograd computes in bf16; otherwise everything is fp32.
+    the dtypes of their inputs.  When x, B and C are bf16 (and dy is rounded to
+    bf16), the dB and dC scans run on the tensor-core scan with bf16 operands and
+    the recomputed forward and the dx scan, which the log-decay gradient depends
+    on, on the fp32 scan (see ``_scan_backward_dot``); otherwise everything is
+    fp32.
     """
     dev = _same_device(("x", x), ("A_disc", A_disc), ("B", B), ("C", C), ("dy", dy),
                        ("ssm_state", ssm_state), ("log_a", log_a),
@@ -487,10 +491,13 @@ def _scan_backward(scan, x, la, B, C, dy, h0, dhT, device):
 
 
 def _scan_backward_dot(x, la, B, C, dy, h0, dhT, device):
-    """``_scan_backward`` on the tensor-core scan: B/C, and C / B where they
-    are the scanned operand, stay per group (no per-head copies), y of the
-    recomputed forward is never written (only its dot with dy is needed), and
-    the dot of dB with B comes out of the dB scan."""
+    """``_scan_backward`` for bf16 operands.  dB and dC come from the tensor-core
+    scan (B/C kept per group, no per-head copies).  The log-decay gradient is a
+    reverse cumulative sum of dy_t . y_t - B_t . dB_t, two terms that cancel
+    nearly term by term at large decays, so the bf16 rounding of the scores
+    inside the tensor-core scan would reach it amplified; the two scans that
+    feed it -- the recomputed forward (y) and the dx scan (B_t . dB_t =
+    x_t . dx_t) -- run on the fp32 scan on the bf16 values, as does dx."""
     Bsz, L, H, P = x.shape
     G, N = B.shape[2], B.shape[3]
     r = H // G
@@ -498,14 +505,13 @@ def _scan_backward_dot(x, la, B, C, dy, h0, dhT, device):
         dhT = torch.zeros((Bsz, H, N, P), dtype=torch.float32, device=device)
     la_next = torch.zeros_like(la)
     la_next[:, :-1] = la[:, 1:]
-    _, hT, dot_y = selective_scan_dot(x, B, C, la, z=dy, ssm_state=h0, write_y=False,
-                                      write_ssm_state=True)
-    dx, g0, _ = selective_scan_dot(dy, C, B, la_next, ssm_state=dhT, y_dtype=x.dtype,
-                                   write_ssm_state=True, reverse_time=True)
-    dBh, _, dot_b = selective_scan_dot(C, dy, x, la_next, z=B, ssm_state=dhT.transpose(2, 3),
-                                       reverse_time=True)
+    xf, Bf, Cf, dyf = x.float(), B.float(), C.float(), dy.float()
+    y, hT = selective_scan(xf, None, Bf, Cf, ssm_state=h0, log_a=la, out_dtype=torch.float32)
+    dx, g0 = selective_scan(dyf, None, Cf, Bf, ssm_state=dhT, log_a=la_next, out_dtype=torch.float32,
+                            reverse_time=True)
+    dBh, _, _ = selective_scan_dot(C, dy, x, la_next, ssm_state=dhT.transpose(2, 3), reverse_time=True)
     dCh, _, _ = selective_scan_dot(B, x, dy, la, ssm_state=None if h0 is None else h0.transpose(2, 3))
-    s = (dot_y - dot_b).transpose(1, 2).contiguous()   # [B, H, L]
+    s = ((dyf * y).sum(-1) - (xf * dx).sum(-1)).transpose(1, 2).contiguous()   # [B, H, L]
     dla = s.flip(-1).cumsum(-1).flip(-1).transpose(1, 2) + (dhT * hT).sum((-1, -2))[:, None, :]
     dh0 = torch.exp(la[:, 0])[:, :, None, None] * g0
     if r > 1:

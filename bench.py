@@ -638,7 +638,8 @@ def run_scan_bwd(args, w):
             "data": "synthetic",
             "config": {"workload": w["name"], "batch": B, "seq_len": L, "n_heads": H,
                        "head_dim": P, "d_state": N, "n_groups": G,
-                       "path": ("4 tcgen05 scans (bf16 operands, fp32 accumulators)" if bf16 else
+                       "path": ("dB, dC on tcgen05 scans (bf16 operands); recomputed forward and dx "
+                                "on fp32 CUDA-core scans" if bf16 else
                                 "4 fp32 CUDA-core scans") + " + reverse cumulative sum"},
             "one_scan": {"ms": scan_ms, "bytes": scan_bytes,
                          "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

@@ -124,10 +124,10 @@ def _scan_dot(**over):
     t = dict(x=_t([B, L, 2, P], BF), la=_t([B, L, H]), Bm=_t([B, L, 1, N], BF), Cm=_t([B, L, 1, N], BF),
              si=_lib.Tensor(), y=_t([B, L, H, P]), so=_lib.Tensor(), z=_t([B, L, H, P], BF),
              dot=_t([B, L, H]))
-    t.update(over)
+    t.update({k: v for k, v in over.items() if k != "mode"})
     lib = _lib.load()
     order = ["x", "la", "Bm", "Cm", "si", "y", "so", "z", "dot"]
-    st = lib.alloy_selective_scan_dot(*(ctypes.byref(t[k]) for k in order), None)
+    st = lib.alloy_selective_scan_dot(*(ctypes.byref(t[k]) for k in order), over.get("mode", 0), None)
     return st, _lib.last_error()
 
 
@@ -140,6 +140,7 @@ def _scan_dot(**over):
     (dict(z=_lib.Tensor()), "z: null"),
     (dict(z=_t([2, 16, 8, 64], _lib.BF16, strides=[16 * 8 * 128, 8 * 128, 128, 2])), "z: head_dim stride"),
     (dict(dot=_t([2, 16, 4])), "dot: dim 2"),
+    (dict(mode=2), "dot_mode"),
 ])
 def test_selective_scan_dot_rejects_bad_arguments(over, needle):
     st, msg = _scan_dot(**over)

@@ -714,6 +714,15 @@ def test_selective_scan_dot_shared_operands(P, N, Gx, Gz, reverse):
     assert_close(np_(h), h64.numpy(), True)
     assert_close(np_(dot), dot64.numpy(), True)
     assert torch.equal(dot, dot2) and torch.equal(h, h2)
+    # without the step's own term (C_t . B_t)(x_t . z_t)
+    _, _, dot3 = mixer.selective_scan_dot(x.to(DEV), Bm.to(DEV), Cm.to(DEV), la.to(DEV), z=z.to(DEV),
+                                          ssm_state=h0.to(DEV), write_y=False, reverse_time=reverse,
+                                          dot_without_own_term=True)
+    r = H // G
+    own = ((Cm.double() * Bm.double()).sum(-1).repeat_interleave(r, 2)
+           * (xh.double() * z.repeat_interleave(H // Gz, 2).double()).sum(-1))
+    err = (dot3.double().cpu() - (dot64 - own)).abs().max() / dot64.abs().max()
+    assert err < 2e-2, float(err)
 
 
 def test_selective_scan_backward_bf16_on_tensor_cores():
@@ -788,6 +797,38 @@ def test_combined_block_training_gradients_vs_fp64():
     assert_close(np_(x_t.grad), x64.grad.numpy(), False)
     for n, t in blk.named_parameters():
         assert_close(np_(t.grad), p[n].grad.numpy(), False), n
+
+
+def test_combined_block_training_bf16_on_tensor_cores():
+    """A bf16 layer of tensor-core scan sizes (head_dim 64, d_state 64) under
+    autograd: its scan forward and backward run on the tcgen05 scan with bf16
+    operands; output and gradients against the same layer in fp32 (checked
+    against float64 by the test above), within 3e-2 relative L2."""
+    torch.manual_seed(3)
+    kw = dict(d_model=128, d_state=64, d_conv=4, expand=2, headdim=64, chunk_size=64,
+              combined_proj=True, n_groups=2, use_D=True, use_inner_norm=True, device=DEV)
+    b16 = MambaBlock(dtype=torch.bfloat16, **kw)
+    with torch.no_grad():
+        b16.A_log.uniform_(0, 2)
+        b16.dt_bias.uniform_(-3, -1)
+        b16.D.normal_()
+        b16.conv_weight.normal_(0, 0.5)
+    f32 = MambaBlock(dtype=torch.float32, **kw)
+    f32.load_state_dict({k: v.float() for k, v in b16.state_dict().items()})
+    x = torch.randn(2, 300, 128, device=DEV).to(torch.bfloat16)
+    U = torch.randn(2, 300, 128, device=DEV)
+    outs = []
+    for blk in (b16, f32):
+        xt = x.to(blk.in_proj.weight.dtype).clone().requires_grad_()
+        y = blk(xt)
+        (y.float() * U).sum().backward()
+        outs.append((y, xt.grad, {n: t.grad for n, t in blk.named_parameters()}))
+    (y16, gx16, g16), (y32, gx32, g32) = outs
+    assert y16.dtype == torch.bfloat16
+    assert oracle.rel_l2(np_(y16), np_(y32)) < 3e-2
+    assert oracle.rel_l2(np_(gx16), np_(gx32)) < 3e-2
+    for n in g32:
+        assert oracle.rel_l2(np_(g16[n]), np_(g32[n])) < 3e-2, n
 
 
 @pytest.mark.parametrize("NB,inp,out", [(1, 4096, 18560), (1, 8192, 4096), (2, 64, 37), (3, 136, 250),
