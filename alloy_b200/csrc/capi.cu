@@ -428,7 +428,7 @@ int alloy_selective_scan_dot(const alloy_tensor_t* x, const alloy_tensor_t* log_
                              const alloy_tensor_t* z, alloy_tensor_t* dot, int32_t dot_mode, void* stream) {
   last_error().clear();
   if (!present(y) && !present(dot)) return fail(ALLOY_ERR_INVALID_ARG, "selective_scan_dot: neither y nor dot");
-  if (dot_mode != 0 && dot_mode != 1) return fail(ALLOY_ERR_INVALID_ARG, "selective_scan_dot: dot_mode must be 0 or 1");
+  if (dot_mode < 0 || dot_mode > 3) return fail(ALLOY_ERR_INVALID_ARG, "selective_scan_dot: dot_mode must be in [0, 3]");
   ALLOY_TRY(check_tensor(x, "x", 4, nullptr, kBF16));
   const alloy_tensor_t* ref = present(y) ? y : dot;
   const int64_t B = x->shape[0], L = x->shape[1], P = x->shape[3];
@@ -501,12 +501,13 @@ int alloy_selective_scan_dot(const alloy_tensor_t* x, const alloy_tensor_t* log_
     a.z_sb = z->stride[0]; a.z_st = z->stride[1]; a.z_sh = z->stride[2];
     a.dot = static_cast<float*>(dot->data);
     a.dot_sb = dot->stride[0]; a.dot_st = dot->stride[1]; a.dot_sh = dot->stride[2];
-    a.dot_nodiag = dot_mode;
+    a.dot_nodiag = dot_mode & 1;
   }
+  a.precise_scores = (dot_mode >> 1) & 1;
   if (!scan_tc_supported(a))
     return fail(ALLOY_ERR_UNSUPPORTED,
-                "selective_scan_dot: needs (head_dim, d_state) of (64, 64), (64, 128) or (128, 64), unit inner "
-                "strides and 16-byte aligned rows");
+                "selective_scan_dot: needs (head_dim, d_state) of (64, 64), (64, 128) or (128, 64) (head_dim 64 "
+                "with precise scores), unit inner strides and 16-byte aligned rows");
   return scan_tc(a, as_stream(stream));
 }
 

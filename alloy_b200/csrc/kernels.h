@@ -57,6 +57,9 @@ struct SsdArgs {
   // dot_nodiag: the dot products leave out the step's own term, S[t,t] (x_t . z_t)
   // with S[t,t] = C_t . B_t as the kernel rounds it
   int dot_nodiag;
+  // precise_scores: the scores enter the output MMA as a bf16 pair (hi + lo),
+  // ~16 bits instead of 8 (head_dim 64 only)
+  int precise_scores;
 };
 
 // scan_tc.cu: tcgen05 scan on pre-discretised bf16 inputs (mode 1: x, B, C

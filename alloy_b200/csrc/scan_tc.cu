@@ -84,7 +84,7 @@ enum {
   NBAR
 };
 
-template <int PP, int NN>
+template <int PP, int NN, bool SPLIT = false>
 struct Layout {
   static constexpr int NBUF = (PP == 64 && NN == 64) ? 3 : 2;
   static constexpr uint32_t kX = PP * 256;           // x tile of one buffer [PP/64][128][64]
@@ -109,11 +109,14 @@ struct Layout {
   // tensor memory columns: two CB buffers (CB, then in place: K-step k of S in
   // columns [16k, 16k+8) and of C~ in [16k+8, 16k+16)), NYB output
   // accumulators, the state
-  static constexpr int NYB = PP == 128 ? 1 : 2;
+  // With SPLIT the scores take a piece's 16 columns (hi, lo) and C~ moves to
+  // its own columns after the state (two buffers of NN/2).
+  static constexpr int NYB = (PP == 128 || (SPLIT && NN == 128)) ? 1 : 2;
   static constexpr uint32_t T_CB = 0;                // + 128 * (chunk & 1)
   static constexpr uint32_t T_Y = 256;               // + PP * (chunk % NYB)
   static constexpr uint32_t T_ST = 256 + NYB * PP;   // PP: state rows n
-  static_assert(T_ST + PP <= 512, "tensor memory");
+  static constexpr uint32_t T_CT = T_ST + PP;        // SPLIT: + NN/2 * (chunk & 1)
+  static_assert(T_ST + PP + (SPLIT ? NN : 0) <= 512, "tensor memory");
   static_assert(kSmem <= 227 * 1024, "shared memory");
   static_assert(NBUF <= kMaxBuf, "buffers");
 };
@@ -192,9 +195,9 @@ __device__ __forceinline__ void load_rows(uint32_t tile, const __nv_bfloat16* sr
   }
 }
 
-template <int PP, int NN>
+template <int PP, int NN, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, int y_vec) {
-  using Lo = Layout<PP, NN>;
+  using Lo = Layout<PP, NN, SPLIT>;
   constexpr int NBUF = Lo::NBUF, NYB = Lo::NYB;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
@@ -306,11 +309,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
             const uint32_t ty = tmem + Lo::T_Y + yb * PP, tcb = tmem + Lo::T_CB + 128 * j;
             const uint32_t sh = base + Lo::OFF_H + (c % NH) * Lo::kH;
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
+            for (int k = 0; k < 8; ++k) {
               umma_bf16_ta(ty, tcb + 16 * k, sw128_desc(xt(lb) + 2048 * k, 16384, 1024), ID_Y, k != 0);
+              if (SPLIT) umma_bf16_ta(ty, tcb + 16 * k + 8, sw128_desc(xt(lb) + 2048 * k, 16384, 1024), ID_Y, 1);
+            }
+            const uint32_t tct = SPLIT ? tmem + Lo::T_CT + (NN / 2) * j : tcb + 8;
 #pragma unroll
             for (int k = 0; k < NN / 16; ++k)
-              umma_bf16_ta(ty, tcb + 16 * k + 8, sw128_desc(sh + 2048 * k, NN * 128, 1024), ID_Y, 1);
+              umma_bf16_ta(ty, tct + (SPLIT ? 8 : 16) * k, sw128_desc(sh + 2048 * k, NN * 128, 1024), ID_Y, 1);
             umma_commit(bar(B_Y_FULL0 + yb));
             umma_commit(bar(B_CB_FREE0 + j));
             if (nst > c) umma_commit(bar(B_EMPTY0 + lb));
@@ -427,7 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
       const uint32_t tcb = lane_base + Lo::T_CB + 128 * j;
       // S[t, s] = CB[t, s] exp(cum[t] - cum[s]) (s <= t) for piece k -> columns [16k, 16k+8)
       auto score = [&](int k, const uint32_t (&rv)[16]) {
-        uint32_t o[8];
+        float v[16];
+        float own = 0.f;   // S[t,t] before rounding
         if (k < 2 * q) {
           // left of the quadrant's diagonal block: exp(cum[t] - cum[s]) = R cf[s],
           // R = exp(cum[t] - cum[m]) <= 1
@@ -436,28 +443,35 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
 #pragma unroll
           for (int i4 = 0; i4 < 4; ++i4) {
             const float4 f = cf4[i4];
-            o[2 * i4] = f2_to_bf2(
-                f2_mul(f2_mul(f2_pack(__uint_as_float(rv[4 * i4]), __uint_as_float(rv[4 * i4 + 1])), R2),
-                       f2_pack(f.x, f.y)));
-            o[2 * i4 + 1] = f2_to_bf2(
-                f2_mul(f2_mul(f2_pack(__uint_as_float(rv[4 * i4 + 2]), __uint_as_float(rv[4 * i4 + 3])), R2),
-                       f2_pack(f.z, f.w)));
+            f2_unpack(f2_mul(f2_mul(f2_pack(__uint_as_float(rv[4 * i4]), __uint_as_float(rv[4 * i4 + 1])), R2),
+                             f2_pack(f.x, f.y)), v[4 * i4], v[4 * i4 + 1]);
+            f2_unpack(f2_mul(f2_mul(f2_pack(__uint_as_float(rv[4 * i4 + 2]), __uint_as_float(rv[4 * i4 + 3])), R2),
+                             f2_pack(f.z, f.w)), v[4 * i4 + 2], v[4 * i4 + 3]);
           }
         } else {
-          // the diagonal block: exact factors, zero right of the diagonal; S[t,t]
-          // as rounded is kept for the output rows (slot c % 4: the rows of
-          // chunk c are read out before the scores of chunk c + 4 start)
+          // the diagonal block: exact factors, zero right of the diagonal
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int s = 16 * k + 2 * e;
-            const float f0 = __uint_as_float(rv[2 * e]) * ex2_approx(fmaf(-cm[s], kLog2e, ct2));
-            const float f1 = __uint_as_float(rv[2 * e + 1]) * ex2_approx(fmaf(-cm[s + 1], kLog2e, ct2));
-            o[e] = pack_bf16x2(s <= t ? f0 : 0.f, s + 1 <= t ? f1 : 0.f);
-            if (s == t) diag_s[(c & 3) * 128 + t] = bf16_lo(o[e]);
-            if (s + 1 == t) diag_s[(c & 3) * 128 + t] = bf16_hi(o[e]);
+          for (int e = 0; e < 16; ++e) {
+            const int s = 16 * k + e;
+            const float f = __uint_as_float(rv[e]) * ex2_approx(fmaf(-cm[s], kLog2e, ct2));
+            v[e] = s <= t ? f : 0.f;
+            if (s == t) own = f;
           }
         }
+        uint32_t o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+        // S[t,t] as rounded, for the output rows (slot c % 4: the rows of chunk c
+        // are read out before the scores of chunk c + 4 start)
+        if (!SPLIT && k >= 2 * q && (t >> 4) == k)
+          diag_s[(c & 3) * 128 + t] = __bfloat162float(__float2bfloat16_rn(own));
         tmem_st8(tcb + 16 * k, o);
+        if (SPLIT) {
+          // the remainder, v - bf16(v), as a second bf16 K-step
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] = pack_bf16x2(v[2 * e] - bf16_lo(o[e]), v[2 * e + 1] - bf16_hi(o[e]));
+          tmem_st8(tcb + 16 * k + 8, o);
+        }
       };
       // this warp's pieces at or left of the quadrant's diagonal: k = half, half + 2, .., 2q + half
       uint32_t ra[16], rb[16];
@@ -478,7 +492,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
 #pragma unroll
         for (int e = 0; e < 8; ++e) z[e] = 0u;
 #pragma unroll 1
-        for (int k = 2 * (q + 1) + half; k < 8; k += 2) tmem_st8(tcb + 16 * k, z);
+        for (int k = 2 * (q + 1) + half; k < 8; k += 2) {
+          tmem_st8(tcb + 16 * k, z);
+          if (SPLIT) tmem_st8(tcb + 16 * k + 8, z);
+        }
       }
       // C~ = exp(cum[t]) C[t, :]: K-step k of the C~ H product -> columns [16k+8, 16k+16)
       {
@@ -495,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
 #pragma unroll
             for (int m = 0; m < 4; ++m) o[4 * hh + m] = f2_to_bf2(f2_mul(f2_from_bf2(ww[m]), e2));
           }
-          tmem_st8(tcb + 16 * k + 8, o);
+          tmem_st8(SPLIT ? lane_base + Lo::T_CT + (NN / 2) * j + 8 * k : tcb + 16 * k + 8, o);
         }
       }
       tmem_st_wait();
@@ -756,6 +773,7 @@ bool scan_tc_supported(const SsdArgs& a) {
   // every 16-byte row chunk starts on a 16-byte boundary: strides in multiples of 8 elements
   for (int64_t s : {a.x_sb, a.x_st, a.x_sh, a.bm_sb, a.bm_st, a.bm_sg, a.cm_sb, a.cm_st, a.cm_sg})
     if (s % 8 != 0) return false;
+  if (a.precise_scores && a.P != 64) return false;
   return a.B <= 65535 && a.H > 0 && a.L > 0 && scan_tc_dot_supported(a);
 }
 
@@ -769,9 +787,13 @@ int scan_tc(const SsdArgs& a, cudaStream_t s) {
     kernel<<<grid, kThreads, smem, s>>>(a, y_vec);
     return check_launch("scan_tc_kernel");
   };
-  if (a.P == 64 && a.N == 64) return launch(scan_tc_kernel<64, 64>, Layout<64, 64>::kSmem);
-  if (a.P == 64) return launch(scan_tc_kernel<64, 128>, Layout<64, 128>::kSmem);
-  return launch(scan_tc_kernel<128, 64>, Layout<128, 64>::kSmem);
+  if (a.precise_scores) {
+    if (a.N == 64) return launch(scan_tc_kernel<64, 64, true>, Layout<64, 64, true>::kSmem);
+    return launch(scan_tc_kernel<64, 128, true>, Layout<64, 128, true>::kSmem);
+  }
+  if (a.P == 64 && a.N == 64) return launch(scan_tc_kernel<64, 64, false>, Layout<64, 64>::kSmem);
+  if (a.P == 64) return launch(scan_tc_kernel<64, 128, false>, Layout<64, 128>::kSmem);
+  return launch(scan_tc_kernel<128, 64, false>, Layout<128, 64>::kSmem);
 }
 
 int scan_tc_take_error(cudaStream_t stream, unsigned int out[3]) {

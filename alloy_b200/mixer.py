@@ -367,7 +367,8 @@ def selective_scan(x, A_disc, B, C, ssm_state=None, log_a=None, out=None, out_dt
 
 
 def selective_scan_dot(x, B, C, log_a, *, z=None, ssm_state=None, y_dtype=torch.float32, write_y=True,
-                       write_ssm_state=False, reverse_time=False, dot_without_own_term=False):
+                       write_ssm_state=False, reverse_time=False, dot_without_own_term=False,
+                       precise_scores=False):
     """The scan of ``selective_scan`` on the tensor cores (``alloy_selective_scan_dot``)
     for bf16 operands, with x and the dot operand shared across heads and the
     row dot products fused: the gradient scans of ``selective_scan_backward``.
@@ -378,7 +379,8 @@ def selective_scan_dot(x, B, C, log_a, *, z=None, ssm_state=None, y_dtype=torch.
     final state [B, H, N, P] fp32 or None, dot [B, L, H] fp32 or None) with
     dot[b, t, h] = sum_p y[b, t, h, p] z[b, t, h // (H // Gz), p]; with
     ``dot_without_own_term`` the step's own term S[t,t] (x_t . z_t), S[t,t] = C_t . B_t
-    as the kernel rounds it, is left out.
+    as the kernel rounds it, is left out.  ``precise_scores`` (head_dim 64) feeds
+    the decayed scores to the output product as a bf16 pair (~16 bits).
     """
     dev = _same_device(("x", x), ("B", B), ("C", C), ("log_a", log_a), ("z", z),
                        ("ssm_state", ssm_state))
@@ -396,8 +398,8 @@ def selective_scan_dot(x, B, C, log_a, *, z=None, ssm_state=None, y_dtype=torch.
                 d.data += (L - 1) * t.stride(1) * t.element_size()
                 d.stride[1] = -t.stride(1)
     with torch.cuda.device(dev):
-        _lib.call("alloy_selective_scan_dot", *(_lib.ref(d) for d in descs), int(dot_without_own_term),
-                  _lib.stream_handle(dev))
+        _lib.call("alloy_selective_scan_dot", *(_lib.ref(d) for d in descs),
+                  int(dot_without_own_term) | (2 if precise_scores else 0), _lib.stream_handle(dev))
     return y, h_out, dot
 
 
@@ -405,7 +407,8 @@ def selective_scan_dot(x, B, C, log_a, *, z=None, ssm_state=None, y_dtype=torch.
 _DOT_SCAN_DIMS = ((64, 64), (64, 128), (128, 64))
 
 
-def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dssm_state_out=None):
+def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dssm_state_out=None,
+                            tensor_core_log_decay=False):
     """Gradients of ``selective_scan``: ``(dx, dA_disc, dB, dC, dssm_state, dlog_a)``
     for the output cotangent ``dy [B, L, H, P]`` and (optional) the cotangent of
     the final state ``dssm_state_out [B, H, N, P]``.  What the reference gets
@@ -426,11 +429,11 @@ def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dss
       dla_t = <dssm_state_out, h_{L-1}> + sum_{u >= t} (dy_u . y_u - B_u . dB_u).
     ``dlog_a`` is returned when ``log_a`` was given (the decay came from it),
     else ``dA_disc`` = dla / A_disc.  All arithmetic in fp32; the gradients have
-    the dtypes of their inputs.  When x, B and C are bf16 (and dy is rounded to
-    bf16), the dB and dC scans run on the tensor-core scan with bf16 operands and
-    the recomputed forward and the dx scan, which the log-decay gradient depends
-    on, on the fp32 scan (see ``_scan_backward_dot``); otherwise everything is
-    fp32.
+    the dtypes of their inputs.  When x, B and C are bf16 (dy rounded to bf16)
+    and the sizes suit the tensor-core scan, dB and dC run on it; the two scans
+    that the log-decay gradient depends on run on the fp32 scan, or with
+    ``tensor_core_log_decay`` on the tensor-core scan with ~16-bit scores (see
+    ``_scan_backward_dot``); otherwise everything is fp32.
     """
     dev = _same_device(("x", x), ("A_disc", A_disc), ("B", B), ("C", C), ("dy", dy),
                        ("ssm_state", ssm_state), ("log_a", log_a),
@@ -444,10 +447,10 @@ def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dss
     bf16 = all(t.dtype == torch.bfloat16 for t in (x, B, C))
     h0 = None if ssm_state is None else ssm_state.float()
     dhT = None if dssm_state_out is None else dssm_state_out.float()
-    if bf16 and (x.shape[-1], B.shape[-1]) in _DOT_SCAN_DIMS:
+    if bf16 and (x.shape[-1], B.shape[-1]) in _DOT_SCAN_DIMS and (x.shape[-1] == 64 or not tensor_core_log_decay):
         bf = lambda t: t.to(torch.bfloat16).contiguous()   # noqa: E731
         dx, dla, dB, dC, dh0 = _scan_backward_dot(bf(x), la.contiguous(), bf(B), bf(C), bf(dy), h0, dhT,
-                                                  dev)
+                                                  dev, tensor_core_log_decay)
     else:
         op = (lambda t: t.to(torch.bfloat16).contiguous()) if bf16 else (lambda t: t.float().contiguous())
         dx, dla, dB, dC, dh0 = _scan_backward(scan, op(x), la, op(B), op(C), op(dy), h0, dhT, dev)
@@ -490,14 +493,18 @@ def _scan_backward(scan, x, la, B, C, dy, h0, dhT, device):
     return (dx, dla, dBh.view(Bsz, L, G, r, N).sum(3), dCh.view(Bsz, L, G, r, N).sum(3), dh0)
 
 
-def _scan_backward_dot(x, la, B, C, dy, h0, dhT, device):
-    """``_scan_backward`` for bf16 operands.  dB and dC come from the tensor-core
-    scan (B/C kept per group, no per-head copies).  The log-decay gradient is a
-    reverse cumulative sum of dy_t . y_t - B_t . dB_t, two terms that cancel
-    nearly term by term at large decays, so the bf16 rounding of the scores
-    inside the tensor-core scan would reach it amplified; the two scans that
-    feed it -- the recomputed forward (y) and the dx scan (B_t . dB_t =
-    x_t . dx_t) -- run on the fp32 scan on the bf16 values, as does dx."""
+def _scan_backward_dot(x, la, B, C, dy, h0, dhT, device, tensor_core_log_decay=False):
+    """``_scan_backward`` for bf16 operands; dB and dC on the tensor-core scan
+    (B/C kept per group, no per-head copies).  The log-decay gradient is a
+    reverse cumulative sum of dy_t . y_t - B_t . dB_t (= x_t . dx_t), two terms
+    that cancel nearly term by term at large decays, so the rounding of the
+    scans that feed it -- the recomputed forward and the dx scan -- reaches it
+    amplified.  By default those two run on the fp32 scan (on the bf16 values).
+    With ``tensor_core_log_decay`` they run on the tensor-core scan with the
+    decayed scores carried as bf16 pairs (~16 bits): about 5x faster, but the
+    state and exp(cum) C still enter the products as single bf16 values, which
+    left a relative error of ~7e-2 in the A_log gradient of a test layer with
+    decays up to exp(-2) a step (single bf16 scores: ~0.5)."""
     Bsz, L, H, P = x.shape
     G, N = B.shape[2], B.shape[3]
     r = H // G
@@ -505,13 +512,20 @@ def _scan_backward_dot(x, la, B, C, dy, h0, dhT, device):
         dhT = torch.zeros((Bsz, H, N, P), dtype=torch.float32, device=device)
     la_next = torch.zeros_like(la)
     la_next[:, :-1] = la[:, 1:]
-    xf, Bf, Cf, dyf = x.float(), B.float(), C.float(), dy.float()
-    y, hT = selective_scan(xf, None, Bf, Cf, ssm_state=h0, log_a=la, out_dtype=torch.float32)
-    dx, g0 = selective_scan(dyf, None, Cf, Bf, ssm_state=dhT, log_a=la_next, out_dtype=torch.float32,
-                            reverse_time=True)
+    if tensor_core_log_decay:
+        _, hT, dot_y = selective_scan_dot(x, B, C, la, z=dy, ssm_state=h0, write_y=False,
+                                          write_ssm_state=True, precise_scores=True)
+        dx, g0, dot_x = selective_scan_dot(dy, C, B, la_next, z=x, ssm_state=dhT, y_dtype=x.dtype,
+                                           write_ssm_state=True, reverse_time=True, precise_scores=True)
+    else:
+        xf, Bf, Cf, dyf = x.float(), B.float(), C.float(), dy.float()
+        y, hT = selective_scan(xf, None, Bf, Cf, ssm_state=h0, log_a=la, out_dtype=torch.float32)
+        dx, g0 = selective_scan(dyf, None, Cf, Bf, ssm_state=dhT, log_a=la_next, out_dtype=torch.float32,
+                                reverse_time=True)
+        dot_y, dot_x = (dyf * y).sum(-1), (xf * dx).sum(-1)
     dBh, _, _ = selective_scan_dot(C, dy, x, la_next, ssm_state=dhT.transpose(2, 3), reverse_time=True)
     dCh, _, _ = selective_scan_dot(B, x, dy, la, ssm_state=None if h0 is None else h0.transpose(2, 3))
-    s = ((dyf * y).sum(-1) - (xf * dx).sum(-1)).transpose(1, 2).contiguous()   # [B, H, L]
+    s = (dot_y - dot_x).transpose(1, 2).contiguous()   # [B, H, L]
     dla = s.flip(-1).cumsum(-1).flip(-1).transpose(1, 2) + (dhT * hT).sum((-1, -2))[:, None, :]
     dh0 = torch.exp(la[:, 0])[:, :, None, None] * g0
     if r > 1:

@@ -588,6 +588,20 @@ def run_scan_bwd(args, w):
     def step(i):
         mixer.selective_scan_backward(x, None, Bm, Cm, dy, log_a=la)
 
+    # the opt-in variant with the log-decay gradient's scans on the tensor cores
+    fast_ms = None
+    if bf16:
+        for i in range(2):
+            mixer.selective_scan_backward(x, None, Bm, Cm, dy, log_a=la, tensor_core_log_decay=True)
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        f0.record()
+        for i in range(5):
+            mixer.selective_scan_backward(x, None, Bm, Cm, dy, log_a=la, tensor_core_log_decay=True)
+        f1.record()
+        torch.cuda.synchronize()
+        fast_ms = f0.elapsed_time(f1) / 5
+
     # one forward scan alone (the unit the backward runs four times), for its roofline:
     # algorithmic bytes = x, B, C, log decay read once, y (fp32) written once
     def one_scan():
@@ -641,6 +655,7 @@ def run_scan_bwd(args, w):
                        "path": ("dB, dC on tcgen05 scans (bf16 operands); recomputed forward and dx "
                                 "on fp32 CUDA-core scans" if bf16 else
                                 "4 fp32 CUDA-core scans") + " + reverse cumulative sum"},
+            "tensor_core_log_decay_ms": fast_ms,
             "one_scan": {"ms": scan_ms, "bytes": scan_bytes,
                          "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                                       "frac": achieved / peak, "peak_source": src}},

@@ -316,9 +316,10 @@ ALLOY_API int alloy_selective_scan(const alloy_tensor_t* x, const alloy_tensor_t
  *   ssm_out [B, H, N, P]   F32 via strides (data NULL = not written)
  *   z       [B, L, Gz, P]  F32|BF16, Gz divides H, P stride 1, 16-byte aligned rows
  *   dot     [B, L, H]      F32 (data NULL = not written): dot[b,t,h] = sum_p y[b,t,h,p] z[b,t,h/(H/Gz),p]
- *   dot_mode 0: as above; 1: without the step's own term S[t,t] (x_t . z_t), S[t,t] = C_t . B_t as
- *            the kernel rounds it (so that the difference of two such dots does not
- *            carry that term's rounding)
+ *   dot_mode bit 0: the dots without the step's own term S[t,t] (x_t . z_t), S[t,t] =
+ *            C_t . B_t as the kernel rounds it; bit 1: precise scores -- the decayed
+ *            scores enter the output product as a pair of bf16 values (~16 bits
+ *            instead of 8), for outputs whose differences cancel (head_dim 64 only)
  * (P, N) must be (64, 64), (64, 128) or (128, 64), the rows of x, Bm and Cm
  * 16-byte aligned; other calls return ALLOY_ERR_UNSUPPORTED.
  */
