@@ -506,8 +506,8 @@ int alloy_selective_scan_dot(const alloy_tensor_t* x, const alloy_tensor_t* log_
   a.precise_scores = (dot_mode >> 1) & 1;
   if (!scan_tc_supported(a))
     return fail(ALLOY_ERR_UNSUPPORTED,
-                "selective_scan_dot: needs (head_dim, d_state) of (64, 64), (64, 128) or (128, 64) (head_dim 64 "
-                "with precise scores), unit inner strides and 16-byte aligned rows");
+                "selective_scan_dot: needs (head_dim, d_state) of (64, 64), (64, 128) or (128, 64) (64, 64 "
+                "in the precise mode), unit inner strides and 16-byte aligned rows");
   return scan_tc(a, as_stream(stream));
 }
 

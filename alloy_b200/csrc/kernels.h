@@ -57,8 +57,8 @@ struct SsdArgs {
   // dot_nodiag: the dot products leave out the step's own term, S[t,t] (x_t . z_t)
   // with S[t,t] = C_t . B_t as the kernel rounds it
   int dot_nodiag;
-  // precise_scores: the scores enter the output MMA as a bf16 pair (hi + lo),
-  // ~16 bits instead of 8 (head_dim 64 only)
+  // precise_scores: the scores, exp(cum) C, the state copy and X' enter the
+  // MMAs as bf16 pairs (hi + lo), ~16 bits instead of 8 (head_dim = d_state = 64)
   int precise_scores;
 };
 

@@ -86,7 +86,7 @@ enum {
 
 template <int PP, int NN, bool SPLIT = false>
 struct Layout {
-  static constexpr int NBUF = (PP == 64 && NN == 64) ? 3 : 2;
+  static constexpr int NBUF = (PP == 64 && NN == 64 && !SPLIT) ? 3 : 2;
   static constexpr uint32_t kX = PP * 256;           // x tile of one buffer [PP/64][128][64]
   static constexpr uint32_t kB = NN * 256;           // B tile [NN/64][128][64]
   static constexpr uint32_t kC = NN * 256;
@@ -94,11 +94,15 @@ struct Layout {
   static constexpr uint32_t OFF_BUF = 0;             // NBUF buffers [x | B | C]
   static constexpr uint32_t OFF_ZERO = NBUF * kBuf;  // 16 KB of zeros: the B tile's second block for NN = 64
   static constexpr int NXP = PP == 128 ? 1 : 2;      // X' buffers
-  static constexpr uint32_t OFF_XP = OFF_ZERO + (NN == 64 ? 16384 : 0);   // NXP x X' [PP/64][128][64]
+  // SPLIT (precise mode, head_dim = d_state = 64): X' and H as bf16 pairs, a
+  // high tile and the remainder's tile
+  static constexpr uint32_t kXPB = kX * (SPLIT ? 2 : 1);
+  static constexpr uint32_t OFF_XP = OFF_ZERO + (NN == 64 ? 16384 : 0);   // NXP x X' [hi | lo][PP/64][128][64]
   static constexpr int NH = (PP == 64 && NN == 128) ? 1 : 2;   // H buffers
   static constexpr uint32_t kH = PP * NN * 2;
-  static constexpr uint32_t OFF_H = OFF_XP + NXP * kX;   // NH x H [PP/64][NN][64]
-  static constexpr uint32_t OFF_CUM = OFF_H + NH * kH;             // [NBUF][128] f32
+  static constexpr uint32_t kHB = kH * (SPLIT ? 2 : 1);
+  static constexpr uint32_t OFF_H = OFF_XP + NXP * kXPB;   // NH x H [hi | lo][PP/64][NN][64]
+  static constexpr uint32_t OFF_CUM = OFF_H + NH * kHB;            // [NBUF][128] f32
   static constexpr uint32_t OFF_CF = OFF_CUM + NBUF * 512;         // [NBUF][128] f32 column factors
   static constexpr uint32_t OFF_DIAG = OFF_CF + NBUF * 512;        // [4 chunks][128] f32: S[t,t] as rounded
   static constexpr uint32_t OFF_WSUM = OFF_DIAG + 4 * 512;         // [NBUF][4] f32
@@ -110,13 +114,14 @@ struct Layout {
   // columns [16k, 16k+8) and of C~ in [16k+8, 16k+16)), NYB output
   // accumulators, the state
   // With SPLIT the scores take a piece's 16 columns (hi, lo) and C~ moves to
-  // its own columns after the state (two buffers of NN/2).
-  static constexpr int NYB = (PP == 128 || (SPLIT && NN == 128)) ? 1 : 2;
+  // its own columns after the state (two buffers of NN: hi, lo).
+  static_assert(!SPLIT || (PP == 64 && NN == 64), "precise mode: head_dim = d_state = 64");
+  static constexpr int NYB = (PP == 128 || SPLIT) ? 1 : 2;
   static constexpr uint32_t T_CB = 0;                // + 128 * (chunk & 1)
   static constexpr uint32_t T_Y = 256;               // + PP * (chunk % NYB)
   static constexpr uint32_t T_ST = 256 + NYB * PP;   // PP: state rows n
-  static constexpr uint32_t T_CT = T_ST + PP;        // SPLIT: + NN/2 * (chunk & 1)
-  static_assert(T_ST + PP + (SPLIT ? NN : 0) <= 512, "tensor memory");
+  static constexpr uint32_t T_CT = T_ST + PP;        // SPLIT: + NN * (chunk & 1); lo at + NN/2
+  static_assert(T_ST + PP + (SPLIT ? 2 * NN : 0) <= 512, "tensor memory");
   static_assert(kSmem <= 227 * 1024, "shared memory");
   static_assert(NBUF <= kMaxBuf, "buffers");
 };
@@ -288,10 +293,15 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
             tc_fence_after();
             // state[n, p] += sum_s B[s, n] X'[s, p]; rows n >= NN of A read the zero block
             const uint32_t lbo = NN == 64 ? Lo::OFF_ZERO - (bt(lb) - base) : 16384;
+            const uint32_t sxp = base + Lo::OFF_XP + xb * Lo::kXPB;
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              umma_bf16(tmem + Lo::T_ST, sw128_desc(bt(lb) + 2048 * k, lbo, 1024),
-                        sw128_desc(base + Lo::OFF_XP + xb * Lo::kX + 2048 * k, 16384, 1024), ID_ST, 1);
+            for (int k = 0; k < 8; ++k) {
+              umma_bf16(tmem + Lo::T_ST, sw128_desc(bt(lb) + 2048 * k, lbo, 1024), sw128_desc(sxp + 2048 * k, 16384, 1024),
+                        ID_ST, 1);
+              if (SPLIT)
+                umma_bf16(tmem + Lo::T_ST, sw128_desc(bt(lb) + 2048 * k, lbo, 1024),
+                          sw128_desc(sxp + Lo::kX + 2048 * k, 16384, 1024), ID_ST, 1);
+            }
             umma_commit(bar(B_ST_DONE));
             if (ny > c) umma_commit(bar(B_EMPTY0 + lb));
             ++nst;
@@ -307,16 +317,22 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
             tc_fence_after();
             // Y = S x + C~ H
             const uint32_t ty = tmem + Lo::T_Y + yb * PP, tcb = tmem + Lo::T_CB + 128 * j;
-            const uint32_t sh = base + Lo::OFF_H + (c % NH) * Lo::kH;
+            const uint32_t sh = base + Lo::OFF_H + (c % NH) * Lo::kHB;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               umma_bf16_ta(ty, tcb + 16 * k, sw128_desc(xt(lb) + 2048 * k, 16384, 1024), ID_Y, k != 0);
               if (SPLIT) umma_bf16_ta(ty, tcb + 16 * k + 8, sw128_desc(xt(lb) + 2048 * k, 16384, 1024), ID_Y, 1);
             }
-            const uint32_t tct = SPLIT ? tmem + Lo::T_CT + (NN / 2) * j : tcb + 8;
+            const uint32_t tct = SPLIT ? tmem + Lo::T_CT + NN * j : tcb + 8;
 #pragma unroll
-            for (int k = 0; k < NN / 16; ++k)
+            for (int k = 0; k < NN / 16; ++k) {
               umma_bf16_ta(ty, tct + (SPLIT ? 8 : 16) * k, sw128_desc(sh + 2048 * k, NN * 128, 1024), ID_Y, 1);
+              if (SPLIT) {
+                // C~_lo H_hi + C~_hi H_lo (the lo x lo product is below the fp32 sums' precision)
+                umma_bf16_ta(ty, tct + NN / 2 + 8 * k, sw128_desc(sh + 2048 * k, NN * 128, 1024), ID_Y, 1);
+                umma_bf16_ta(ty, tct + 8 * k, sw128_desc(sh + Lo::kH + 2048 * k, NN * 128, 1024), ID_Y, 1);
+              }
+            }
             umma_commit(bar(B_Y_FULL0 + yb));
             umma_commit(bar(B_CB_FREE0 + j));
             if (nst > c) umma_commit(bar(B_EMPTY0 + lb));
@@ -503,16 +519,26 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
         const uint32_t crow = ct(lb);
 #pragma unroll 1
         for (int k = half; k < NN / 16; k += 2) {
-          uint32_t o[8];
+          uint32_t o[8], ol[8];
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             const int jc = 2 * k + hh;   // 16-byte chunk of the row
             const uint4 w = ld_shared_v4(crow + (jc >> 3) * 16384 + sw_off(t, jc & 7));
             const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int m = 0; m < 4; ++m) o[4 * hh + m] = f2_to_bf2(f2_mul(f2_from_bf2(ww[m]), e2));
+            for (int m = 0; m < 4; ++m) {
+              float lo, hi;
+              f2_unpack(f2_mul(f2_from_bf2(ww[m]), e2), lo, hi);
+              o[4 * hh + m] = pack_bf16x2(lo, hi);
+              if (SPLIT) ol[4 * hh + m] = pack_bf16x2(lo - bf16_lo(o[4 * hh + m]), hi - bf16_hi(o[4 * hh + m]));
+            }
           }
-          tmem_st8(SPLIT ? lane_base + Lo::T_CT + (NN / 2) * j + 8 * k : tcb + 16 * k + 8, o);
+          if (SPLIT) {
+            tmem_st8(lane_base + Lo::T_CT + NN * j + 8 * k, o);
+            tmem_st8(lane_base + Lo::T_CT + NN * j + NN / 2 + 8 * k, ol);
+          } else {
+            tmem_st8(tcb + 16 * k + 8, o);
+          }
         }
       }
       tmem_st_wait();
@@ -564,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
         if (c >= Lo::NXP &&
             !waitw(bar(B_EMPTY0 + (c - Lo::NXP) % NBUF), ((c - Lo::NXP) / NBUF) & 1, abort_flag, 33))
           break;
-        const uint32_t src = xt(lb), dst = base + Lo::OFF_XP + xb * Lo::kX;
+        const uint32_t src = xt(lb), dst = base + Lo::OFF_XP + xb * Lo::kXPB;
 #pragma unroll 1
         for (int rr = 0; rr < 2; ++rr) {
           const int s = xq * 32 + lane + 64 * rr;
@@ -573,10 +599,17 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
           for (int jc = 0; jc < PP / 8; ++jc) {
             const uint32_t off = (jc >> 3) * 16384 + sw_off(s, jc & 7);
             const uint4 u = ld_shared_v4(src + off);
-            st_shared_v4(dst + off, make_uint4(f2_to_bf2(f2_mul(f2_from_bf2(u.x), w2)),
-                                               f2_to_bf2(f2_mul(f2_from_bf2(u.y), w2)),
-                                               f2_to_bf2(f2_mul(f2_from_bf2(u.z), w2)),
-                                               f2_to_bf2(f2_mul(f2_from_bf2(u.w), w2))));
+            const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+              float lo, hi;
+              f2_unpack(f2_mul(f2_from_bf2(uw[m]), w2), lo, hi);
+              hw[m] = pack_bf16x2(lo, hi);
+              if (SPLIT) lw[m] = pack_bf16x2(lo - bf16_lo(hw[m]), hi - bf16_hi(hw[m]));
+            }
+            st_shared_v4(dst + off, make_uint4(hw[0], hw[1], hw[2], hw[3]));
+            if (SPLIT) st_shared_v4(dst + Lo::kX + off, make_uint4(lw[0], lw[1], lw[2], lw[3]));
           }
         }
         fence_async_smem();
@@ -591,16 +624,21 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
         if (warp == kStateWarp0) ALLOY_SCAN_TRACE(10, c);
         tc_fence_after();
         const float e = ex2_approx(last * kLog2e);
-        const uint32_t hrow = base + Lo::OFF_H + (c % Lo::NH) * Lo::kH;
+        const uint32_t hrow = base + Lo::OFF_H + (c % Lo::NH) * Lo::kHB;
         auto copy = [&](int p0, uint32_t (&v)[16]) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             const int jc = p0 / 8 + hh;   // 16-byte chunk of the state row (8 p)
-            st_shared_v4(hrow + (jc >> 3) * (NN * 128) + sw_off(r, jc & 7),
-                         make_uint4(pack_bf16x2(__uint_as_float(v[8 * hh + 0]), __uint_as_float(v[8 * hh + 1])),
-                                    pack_bf16x2(__uint_as_float(v[8 * hh + 2]), __uint_as_float(v[8 * hh + 3])),
-                                    pack_bf16x2(__uint_as_float(v[8 * hh + 4]), __uint_as_float(v[8 * hh + 5])),
-                                    pack_bf16x2(__uint_as_float(v[8 * hh + 6]), __uint_as_float(v[8 * hh + 7]))));
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+              const float lo = __uint_as_float(v[8 * hh + 2 * m]), hi = __uint_as_float(v[8 * hh + 2 * m + 1]);
+              hw[m] = pack_bf16x2(lo, hi);
+              if (SPLIT) lw[m] = pack_bf16x2(lo - bf16_lo(hw[m]), hi - bf16_hi(hw[m]));
+            }
+            const uint32_t off = (jc >> 3) * (NN * 128) + sw_off(r, jc & 7);
+            st_shared_v4(hrow + off, make_uint4(hw[0], hw[1], hw[2], hw[3]));
+            if (SPLIT) st_shared_v4(hrow + Lo::kH + off, make_uint4(lw[0], lw[1], lw[2], lw[3]));
           }
 #pragma unroll
           for (int k = 0; k < 16; ++k) v[k] = __float_as_uint(e * __uint_as_float(v[k]));
@@ -773,7 +811,7 @@ bool scan_tc_supported(const SsdArgs& a) {
   // every 16-byte row chunk starts on a 16-byte boundary: strides in multiples of 8 elements
   for (int64_t s : {a.x_sb, a.x_st, a.x_sh, a.bm_sb, a.bm_st, a.bm_sg, a.cm_sb, a.cm_st, a.cm_sg})
     if (s % 8 != 0) return false;
-  if (a.precise_scores && a.P != 64) return false;
+  if (a.precise_scores && (a.P != 64 || a.N != 64)) return false;
   return a.B <= 65535 && a.H > 0 && a.L > 0 && scan_tc_dot_supported(a);
 }
 
@@ -787,10 +825,7 @@ int scan_tc(const SsdArgs& a, cudaStream_t s) {
     kernel<<<grid, kThreads, smem, s>>>(a, y_vec);
     return check_launch("scan_tc_kernel");
   };
-  if (a.precise_scores) {
-    if (a.N == 64) return launch(scan_tc_kernel<64, 64, true>, Layout<64, 64, true>::kSmem);
-    return launch(scan_tc_kernel<64, 128, true>, Layout<64, 128, true>::kSmem);
-  }
+  if (a.precise_scores) return launch(scan_tc_kernel<64, 64, true>, Layout<64, 64, true>::kSmem);
   if (a.P == 64 && a.N == 64) return launch(scan_tc_kernel<64, 64, false>, Layout<64, 64>::kSmem);
   if (a.P == 64) return launch(scan_tc_kernel<64, 128, false>, Layout<64, 128>::kSmem);
   return launch(scan_tc_kernel<128, 64, false>, Layout<128, 64>::kSmem);

@@ -379,8 +379,9 @@ def selective_scan_dot(x, B, C, log_a, *, z=None, ssm_state=None, y_dtype=torch.
     final state [B, H, N, P] fp32 or None, dot [B, L, H] fp32 or None) with
     dot[b, t, h] = sum_p y[b, t, h, p] z[b, t, h // (H // Gz), p]; with
     ``dot_without_own_term`` the step's own term S[t,t] (x_t . z_t), S[t,t] = C_t . B_t
-    as the kernel rounds it, is left out.  ``precise_scores`` (head_dim 64) feeds
-    the decayed scores to the output product as a bf16 pair (~16 bits).
+    as the kernel rounds it, is left out.  ``precise_scores`` (head_dim = d_state
+    = 64) feeds the decayed scores, exp(cum) C, the state copy and X' to the
+    products as bf16 pairs (~16 bits) for outputs whose differences cancel.
     """
     dev = _same_device(("x", x), ("B", B), ("C", C), ("log_a", log_a), ("z", z),
                        ("ssm_state", ssm_state))
@@ -408,7 +409,7 @@ _DOT_SCAN_DIMS = ((64, 64), (64, 128), (128, 64))
 
 
 def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dssm_state_out=None,
-                            tensor_core_log_decay=False):
+                            tensor_core_log_decay=True):
     """Gradients of ``selective_scan``: ``(dx, dA_disc, dB, dC, dssm_state, dlog_a)``
     for the output cotangent ``dy [B, L, H, P]`` and (optional) the cotangent of
     the final state ``dssm_state_out [B, H, N, P]``.  What the reference gets
@@ -431,9 +432,9 @@ def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dss
     else ``dA_disc`` = dla / A_disc.  All arithmetic in fp32; the gradients have
     the dtypes of their inputs.  When x, B and C are bf16 (dy rounded to bf16)
     and the sizes suit the tensor-core scan, dB and dC run on it; the two scans
-    that the log-decay gradient depends on run on the fp32 scan, or with
-    ``tensor_core_log_decay`` on the tensor-core scan with ~16-bit scores (see
-    ``_scan_backward_dot``); otherwise everything is fp32.
+    that the log-decay gradient depends on run on the tensor-core scan with
+    ~16-bit operands (``tensor_core_log_decay``, head_dim = d_state = 64) or on
+    the fp32 scan (see ``_scan_backward_dot``); otherwise everything is fp32.
     """
     dev = _same_device(("x", x), ("A_disc", A_disc), ("B", B), ("C", C), ("dy", dy),
                        ("ssm_state", ssm_state), ("log_a", log_a),
@@ -447,7 +448,9 @@ def selective_scan_backward(x, A_disc, B, C, dy, ssm_state=None, log_a=None, dss
     bf16 = all(t.dtype == torch.bfloat16 for t in (x, B, C))
     h0 = None if ssm_state is None else ssm_state.float()
     dhT = None if dssm_state_out is None else dssm_state_out.float()
-    if bf16 and (x.shape[-1], B.shape[-1]) in _DOT_SCAN_DIMS and (x.shape[-1] == 64 or not tensor_core_log_decay):
+    # the tensor-core log-decay scans (bf16 pairs throughout) cover head_dim = d_state = 64
+    tensor_core_log_decay = tensor_core_log_decay and (x.shape[-1], B.shape[-1]) == (64, 64)
+    if bf16 and (x.shape[-1], B.shape[-1]) in _DOT_SCAN_DIMS:
         bf = lambda t: t.to(torch.bfloat16).contiguous()   # noqa: E731
         dx, dla, dB, dC, dh0 = _scan_backward_dot(bf(x), la.contiguous(), bf(B), bf(C), bf(dy), h0, dhT,
                                                   dev, tensor_core_log_decay)
@@ -499,12 +502,13 @@ def _scan_backward_dot(x, la, B, C, dy, h0, dhT, device, tensor_core_log_decay=F
     reverse cumulative sum of dy_t . y_t - B_t . dB_t (= x_t . dx_t), two terms
     that cancel nearly term by term at large decays, so the rounding of the
     scans that feed it -- the recomputed forward and the dx scan -- reaches it
-    amplified.  By default those two run on the fp32 scan (on the bf16 values).
-    With ``tensor_core_log_decay`` they run on the tensor-core scan with the
-    decayed scores carried as bf16 pairs (~16 bits): about 5x faster, but the
-    state and exp(cum) C still enter the products as single bf16 values, which
-    left a relative error of ~7e-2 in the A_log gradient of a test layer with
-    decays up to exp(-2) a step (single bf16 scores: ~0.5)."""
+    amplified.  With ``tensor_core_log_decay`` (the default; head_dim = d_state
+    = 64) those two run on the tensor-core scan in its precise mode: the decayed
+    scores, exp(cum) C, the state copy and X' all enter the products as bf16
+    pairs (~16 bits).  Otherwise they run on the fp32 scan (on the bf16 values),
+    about 5x slower.  (With single bf16 operands the A_log gradient of a test
+    layer with decays up to exp(-2) a step was off by ~0.5 relative; with the
+    scores alone as pairs, by ~7e-2.)"""
     Bsz, L, H, P = x.shape
     G, N = B.shape[2], B.shape[3]
     r = H // G

@@ -317,9 +317,10 @@ ALLOY_API int alloy_selective_scan(const alloy_tensor_t* x, const alloy_tensor_t
  *   z       [B, L, Gz, P]  F32|BF16, Gz divides H, P stride 1, 16-byte aligned rows
  *   dot     [B, L, H]      F32 (data NULL = not written): dot[b,t,h] = sum_p y[b,t,h,p] z[b,t,h/(H/Gz),p]
  *   dot_mode bit 0: the dots without the step's own term S[t,t] (x_t . z_t), S[t,t] =
- *            C_t . B_t as the kernel rounds it; bit 1: precise scores -- the decayed
- *            scores enter the output product as a pair of bf16 values (~16 bits
- *            instead of 8), for outputs whose differences cancel (head_dim 64 only)
+ *            C_t . B_t as the kernel rounds it; bit 1: precise mode -- the decayed
+ *            scores, exp(cum) C, the state copy and X' enter the products as pairs
+ *            of bf16 values (~16 bits instead of 8), for outputs whose differences
+ *            cancel (head_dim = d_state = 64 only)
  * (P, N) must be (64, 64), (64, 128) or (128, 64), the rows of x, Bm and Cm
  * 16-byte aligned; other calls return ALLOY_ERR_UNSUPPORTED.
  */

@@ -723,23 +723,26 @@ def test_selective_scan_dot_shared_operands(P, N, Gx, Gz, reverse):
            * (xh.double() * z.repeat_interleave(H // Gz, 2).double()).sum(-1))
     err = (dot3.double().cpu() - (dot64 - own)).abs().max() / dot64.abs().max()
     assert err < 2e-2, float(err)
-    if P == 64:
-        # scores as bf16 pairs: markedly closer to the float64 recurrence
+    if (P, N) == (64, 64):
+        # the precise mode (operands as bf16 pairs): markedly closer to the float64 recurrence
         y4, _, dot4 = mixer.selective_scan_dot(x.to(DEV), Bm.to(DEV), Cm.to(DEV), la.to(DEV), z=z.to(DEV),
                                                ssm_state=h0.to(DEV), reverse_time=reverse, precise_scores=True)
         assert oracle.rel_l2(np_(y4), y64.numpy()) < 0.5 * oracle.rel_l2(np_(y), y64.numpy())
         assert oracle.rel_l2(np_(dot4), dot64.numpy()) < 0.5 * oracle.rel_l2(np_(dot), dot64.numpy())
 
 
-def test_selective_scan_backward_bf16_on_tensor_cores():
-    """bf16 inputs: the gradient scans run on the tcgen05 scan with bf16
-    operands; gradients against float64 autograd on the same bf16 values,
-    within 2e-2 relative L2 (bf16 operands, the cotangent rounded to bf16)."""
+@pytest.mark.parametrize("decay,tensor_core_log_decay", [(0.3, False), (2.3, False), (2.3, True)])
+def test_selective_scan_backward_bf16_on_tensor_cores(decay, tensor_core_log_decay):
+    """bf16 inputs: dB and dC on the tcgen05 scan with bf16 operands, the
+    log-decay gradient's scans on the tcgen05 scan's precise mode (the default,
+    through autograd) or in fp32; gradients against float64 autograd on the same bf16 values, within
+    2e-2 relative L2 (bf16 operands, the cotangent rounded to bf16), at decays
+    up to exp(-decay) a step."""
     g = torch.Generator().manual_seed(11)
-    b, L, H, P, N, G = 2, 200, 4, 64, 64, 2
+    b, L, H, P, N, G = 2, 300, 4, 64, 64, 2
     x = (torch.randn(b, L, H, P, generator=g) * 0.5).bfloat16()
     Bm, Cm = torch.randn(b, L, G, N, generator=g).bfloat16(), torch.randn(b, L, G, N, generator=g).bfloat16()
-    la = -torch.rand(b, L, H, generator=g) * 0.3
+    la = -torch.rand(b, L, H, generator=g) * decay
     h0 = torch.randn(b, H, N, P, generator=g) * 0.3
     U = torch.randn(b, L, H, P, generator=g).bfloat16()
     V = torch.randn(b, H, N, P, generator=g)
@@ -747,10 +750,16 @@ def test_selective_scan_backward_bf16_on_tensor_cores():
     y64, h64 = _scan64(*leaves)
     ((y64 * U.double()).sum() + (h64 * V.double()).sum()).backward()
     xs = [t.to(DEV).requires_grad_() for t in (x, la, Bm, Cm, h0)]
-    y, h = mixer.SelectiveScan.apply(xs[0], None, xs[2], xs[3], xs[4], xs[1])
-    ((y.float() * U.to(DEV).float()).sum() + (h * V.to(DEV)).sum()).backward()
-    for got, ref in zip((xs[0].grad, xs[1].grad, xs[2].grad, xs[3].grad, xs[4].grad),
-                        (leaf.grad for leaf in leaves)):
+    if not tensor_core_log_decay:
+        dx, _, dB, dC, dh0, dla = mixer.selective_scan_backward(
+            xs[0].detach(), None, xs[2].detach(), xs[3].detach(), U.to(DEV), ssm_state=xs[4].detach(),
+            log_a=xs[1].detach(), dssm_state_out=V.to(DEV), tensor_core_log_decay=False)
+        grads = (dx, dla, dB, dC, dh0)
+    else:
+        y, h = mixer.SelectiveScan.apply(xs[0], None, xs[2], xs[3], xs[4], xs[1])
+        ((y.float() * U.to(DEV).float()).sum() + (h * V.to(DEV)).sum()).backward()
+        grads = (xs[0].grad, xs[1].grad, xs[2].grad, xs[3].grad, xs[4].grad)
+    for got, ref in zip(grads, (leaf.grad for leaf in leaves)):
         assert got.dtype == (torch.bfloat16 if ref.shape in (x.shape, Bm.shape) else torch.float32)
         assert oracle.rel_l2(np_(got), ref.numpy()) < 2e-2
 
@@ -831,7 +840,7 @@ def test_combined_block_training_bf16_on_tensor_cores():
         outs.append((y, xt.grad, {n: t.grad for n, t in blk.named_parameters()}))
     (y16, gx16, g16), (y32, gx32, g32) = outs
     assert y16.dtype == torch.bfloat16
-    # (the default backward: the log-decay gradient's scans in fp32)
+    # (the default backward: the log-decay gradient's scans on the precise tensor-core mode)
     assert oracle.rel_l2(np_(y16), np_(y32)) < 3e-2
     assert oracle.rel_l2(np_(gx16), np_(gx32)) < 3e-2
     for n in g32:
