@@ -428,7 +428,8 @@ int alloy_selective_scan_dot(const alloy_tensor_t* x, const alloy_tensor_t* log_
                              const alloy_tensor_t* z, alloy_tensor_t* dot, int32_t dot_mode, void* stream) {
   last_error().clear();
   if (!present(y) && !present(dot)) return fail(ALLOY_ERR_INVALID_ARG, "selective_scan_dot: neither y nor dot");
-  if (dot_mode < 0 || dot_mode > 3) return fail(ALLOY_ERR_INVALID_ARG, "selective_scan_dot: dot_mode must be in [0, 3]");
+  if (dot_mode < 0 || dot_mode > 2)
+    return fail(ALLOY_ERR_INVALID_ARG, "selective_scan_dot: dot_mode must be 0, 1 or 2 (the bits are exclusive)");
   ALLOY_TRY(check_tensor(x, "x", 4, nullptr, kBF16));
   const alloy_tensor_t* ref = present(y) ? y : dot;
   const int64_t B = x->shape[0], L = x->shape[1], P = x->shape[3];

@@ -381,7 +381,8 @@ def selective_scan_dot(x, B, C, log_a, *, z=None, ssm_state=None, y_dtype=torch.
     ``dot_without_own_term`` the step's own term S[t,t] (x_t . z_t), S[t,t] = C_t . B_t
     as the kernel rounds it, is left out.  ``precise_scores`` (head_dim = d_state
     = 64) feeds the decayed scores, exp(cum) C, the state copy and X' to the
-    products as bf16 pairs (~16 bits) for outputs whose differences cancel.
+    products as bf16 pairs (~16 bits) for outputs whose differences cancel; it
+    excludes ``dot_without_own_term``.
     """
     dev = _same_device(("x", x), ("B", B), ("C", C), ("log_a", log_a), ("z", z),
                        ("ssm_state", ssm_state))

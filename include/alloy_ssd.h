@@ -320,7 +320,7 @@ ALLOY_API int alloy_selective_scan(const alloy_tensor_t* x, const alloy_tensor_t
  *            C_t . B_t as the kernel rounds it; bit 1: precise mode -- the decayed
  *            scores, exp(cum) C, the state copy and X' enter the products as pairs
  *            of bf16 values (~16 bits instead of 8), for outputs whose differences
- *            cancel (head_dim = d_state = 64 only)
+ *            cancel (head_dim = d_state = 64 only); the two bits are exclusive
  * (P, N) must be (64, 64), (64, 128) or (128, 64), the rows of x, Bm and Cm
  * 16-byte aligned; other calls return ALLOY_ERR_UNSUPPORTED.
  */

@@ -141,6 +141,7 @@ def _scan_dot(**over):
     (dict(z=_t([2, 16, 8, 64], _lib.BF16, strides=[16 * 8 * 128, 8 * 128, 128, 2])), "z: head_dim stride"),
     (dict(dot=_t([2, 16, 4])), "dot: dim 2"),
     (dict(mode=4), "dot_mode"),
+    (dict(mode=3), "exclusive"),
 ])
 def test_selective_scan_dot_rejects_bad_arguments(over, needle):
     st, msg = _scan_dot(**over)
