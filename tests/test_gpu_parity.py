@@ -731,15 +731,17 @@ def test_selective_scan_dot_shared_operands(P, N, Gx, Gz, reverse):
         assert oracle.rel_l2(np_(dot4), dot64.numpy()) < 0.5 * oracle.rel_l2(np_(dot), dot64.numpy())
 
 
-@pytest.mark.parametrize("decay,tensor_core_log_decay", [(0.3, False), (2.3, False), (2.3, True)])
-def test_selective_scan_backward_bf16_on_tensor_cores(decay, tensor_core_log_decay):
+@pytest.mark.parametrize("decay,tensor_core_log_decay,N", [(0.3, False, 64), (2.3, False, 64), (2.3, True, 64),
+                                                          (2.3, True, 128)])
+def test_selective_scan_backward_bf16_on_tensor_cores(decay, tensor_core_log_decay, N):
     """bf16 inputs: dB and dC on the tcgen05 scan with bf16 operands, the
     log-decay gradient's scans on the tcgen05 scan's precise mode (the default,
     through autograd) or in fp32; gradients against float64 autograd on the same bf16 values, within
     2e-2 relative L2 (bf16 operands, the cotangent rounded to bf16), at decays
-    up to exp(-decay) a step."""
+    up to exp(-decay) a step.  d_state 128 (the Nemotron layer's shape): dB and
+    dC on the (128, 64) tensor-core scan, the log-decay scans in fp32."""
     g = torch.Generator().manual_seed(11)
-    b, L, H, P, N, G = 2, 300, 4, 64, 64, 2
+    b, L, H, P, G = 2, 300, 4, 64, 2
     x = (torch.randn(b, L, H, P, generator=g) * 0.5).bfloat16()
     Bm, Cm = torch.randn(b, L, G, N, generator=g).bfloat16(), torch.randn(b, L, G, N, generator=g).bfloat16()
     la = -torch.rand(b, L, H, generator=g) * decay
