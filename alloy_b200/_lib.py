@@ -52,6 +52,7 @@ EXPORTS = (
     "alloy_conv1d_silu_backward",
     "alloy_conv1d_silu_backward_workspace_size",
     "alloy_decode_linear",
+    "alloy_debug_set_wait_stall",
 )
 
 
@@ -132,6 +133,8 @@ def load():
                                                           ctypes.c_int32, D]
         lib.alloy_ssd_combined_min_workspace_size.restype = ctypes.c_size_t
         lib.alloy_check_device_status.argtypes = [vp]
+        lib.alloy_debug_set_wait_stall.argtypes = [ctypes.c_int64]
+        lib.alloy_debug_set_wait_stall.restype = ctypes.c_int
         lib.alloy_gated_rmsnorm.argtypes = [P, P, P, P, ctypes.c_float, ctypes.c_int64, vp]
         lib.alloy_gated_rmsnorm.restype = ctypes.c_int
         lib.alloy_kernel_launch_count.argtypes = []

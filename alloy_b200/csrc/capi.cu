@@ -356,6 +356,14 @@ int alloy_check_device_status(void* stream) {
   return ALLOY_OK;
 }
 
+int alloy_debug_set_wait_stall(int64_t cycles) {
+  last_error().clear();
+  if (cycles < 0 || cycles > (int64_t(1) << 32))
+    return fail(ALLOY_ERR_INVALID_ARG, "debug_set_wait_stall: cycles must be in [0, 2^32]");
+  ssd_tc_stall_cycles().store(cycles, std::memory_order_relaxed);
+  return ALLOY_OK;
+}
+
 int alloy_selective_scan(const alloy_tensor_t* x, const alloy_tensor_t* A_disc,
                          const alloy_tensor_t* log_a, const alloy_tensor_t* Bm,
                          const alloy_tensor_t* Cm, const alloy_tensor_t* ssm_in,

@@ -117,5 +117,8 @@ int ssd_tc(const SsdArgs& a, void* workspace, size_t workspace_bytes, cudaStream
 // Synchronises the stream, then reads and clears the error word that a CTA
 // of the tensor-core SSD writes when one of its bounded waits runs out.
 int ssd_tc_take_error(cudaStream_t s, unsigned int out[3]);
+// Cycles the consumer warps of every ssd_tc_kernel launched from now on first
+// wait on a barrier nothing completes (0 = off; the bounded-wait test hook).
+std::atomic<long long>& ssd_tc_stall_cycles();
 
 }  // namespace alloy

@@ -12,9 +12,15 @@
 //
 // The array is a file-scope __device__ variable: every device context that
 // loads the library holds kNoAllocScratchBytes of it until the process exits.
-// Its name is only a host-side handle, so the device address is looked up
-// here with cudaGetSymbolAddress, once per device, on the first call made with
-// that device current (which may also load the library's device code).
+// Its name is only a host-side handle, so its device address is looked up
+// with cudaGetSymbolAddress, with the call's device current, the first time a
+// call runs in a context, and kept per device together with that context's
+// unique id.  A context that is destroyed and created again (cudaDeviceReset)
+// gets a new id and loads the module anew, possibly at another address, so
+// the next call looks the address up again instead of using a stale one.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -27,20 +33,59 @@ constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;   // 8 MiB
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+struct ScratchSlot {
+  unsigned long long ctx_id;   // unique id of the context the address belongs to
+  void* addr;
+};
 std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {nullptr};
+ScratchSlot g_scratch[kMaxDevices] = {};
+
+// The current context's unique id in *id (cuCtxGetCurrent + cuCtxGetId,
+// through the runtime's driver entry points; the library links no driver
+// stub), or 0 when this thread has no current context yet.
+int current_context_id(unsigned long long* id) {
+  static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
+  if (get_current == nullptr || get_id == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return fail(ALLOY_ERR_CUDA, "ssd_combined_noalloc: cuCtxGetCurrent unavailable");
+    get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return fail(ALLOY_ERR_CUDA, "ssd_combined_noalloc: cuCtxGetId unavailable");
+    get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+  }
+  *id = 0;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS)
+    return fail(ALLOY_ERR_CUDA, "ssd_combined_noalloc: cuCtxGetCurrent failed");
+  if (ctx == nullptr) return ALLOY_OK;
+  if (get_id(ctx, id) != CUDA_SUCCESS) return fail(ALLOY_ERR_CUDA, "ssd_combined_noalloc: cuCtxGetId failed");
+  return ALLOY_OK;
+}
 
 int scratch_of_current_device(void** out) {
   int dev = 0;
   ALLOY_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return fail(ALLOY_ERR_DEVICE, "device index %d out of range", dev);
+  unsigned long long ctx = 0;
+  ALLOY_TRY(current_context_id(&ctx));
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+  ScratchSlot& s = g_scratch[dev];
+  if (ctx == 0 || s.addr == nullptr || s.ctx_id != ctx) {
+    // set-up for this device's context: the lookup makes the device's primary
+    // context current if nothing has yet, and may load the module into it
     void* p = nullptr;
     ALLOY_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-    g_scratch_addr[dev] = p;
+    if (ctx == 0) ALLOY_TRY(current_context_id(&ctx));
+    if (ctx == 0) return fail(ALLOY_ERR_CUDA, "ssd_combined_noalloc: no current CUDA context");
+    s.addr = p;
+    s.ctx_id = ctx;
   }
-  *out = g_scratch_addr[dev];
+  *out = s.addr;
   return ALLOY_OK;
 }
 

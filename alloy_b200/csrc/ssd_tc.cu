@@ -96,7 +96,7 @@ constexpr uint32_t OFF_WSUM = OFF_CF + 2048;        // [2 buffers][2 heads][4 wa
 constexpr uint32_t OFF_CW = OFF_WSUM + 64;          // x conv weights [2][4][16][4] + bias [2][16][4]
 constexpr uint32_t OFF_XF = OFF_CW + 2560;          // X' row factors [2 heads][128]
 constexpr uint32_t OFF_BAR = OFF_XF + 1024;         // mbarriers (8 bytes each)
-constexpr int NBAR = 17;
+constexpr int NBAR = 18;
 constexpr uint32_t OFF_TMEMPTR = OFF_BAR + NBAR * 8;
 constexpr uint32_t OFF_ABORT = OFF_TMEMPTR + 8;
 constexpr uint32_t kSmemBytes = OFF_ABORT + 16 + 1024;  // + alignment slack
@@ -113,9 +113,10 @@ enum {
   B_YI_DONE,                                  // MMA -> consumers: Yi done (H reusable; state update done)
   B_Y_EMPTY0, B_Y_EMPTY1,                     // producers -> MMA: y read out (per buffer)
   B_PWG0, B_PWG1,                             // producer warpgroup syncs
-  B_DRAIN
+  B_DRAIN,
+  B_NEVER                                     // nothing arrives: the wait-expiry test hook waits here
 };
-static_assert(B_DRAIN + 1 == NBAR, "barrier table");
+static_assert(B_NEVER + 1 == NBAR, "barrier table");
 // the state-only pass reuses barriers only the full pass needs otherwise
 constexpr int B_XF_FULL0 = B_HBF_READY;   // consumers -> producers: X' row factors of a chunk (per buffer)
 constexpr int B_XF_EMPTY0 = B_ST_DONE;    // producers -> consumers: row factors read (per buffer)
@@ -153,6 +154,9 @@ struct TcArgs {
   // later segments from zero), written by the state-only pass
   float* seg_state;
   float* seg_logdecay;       // [B][head pairs][nseg][2]: sum of A dt over segment s, per head
+  // > 0 only in a test of the bounded-wait error path: the consumer warps
+  // first wait this many cycles on B_NEVER, which nothing completes
+  long long stall_cycles;
 };
 
 // ----------------------------------------------------------------------------
@@ -183,12 +187,12 @@ __device__ __forceinline__ bool wait1(uint32_t bar, uint32_t parity, volatile in
 // warp-uniform wait: every lane polls (bounded by the clock limit and the
 // CTA's abort flag), then one vote makes the outcome the same on all lanes
 __device__ __forceinline__ bool waitw(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                      int site) {
+                                      int site, long long limit = kWaitCycles) {
   const long long t0 = clock64();
   bool ok;
   while (!(ok = mbar_try_wait(bar, parity) != 0)) {
     ALLOY_TRACE_SPIN();
-    if (*abort_flag || clock64() - t0 > kWaitCycles) break;
+    if (*abort_flag || clock64() - t0 > limit) break;
   }
   ok = __all_sync(0xffffffffu, ok);
   if (!ok && (threadIdx.x & 31) == 0 && !*abort_flag) signal_abort(abort_flag, site);
@@ -437,11 +441,11 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    // FULL0/1 EMPTY0/1 X_READY0/1 CB_FULL HBF_READY S_READY Y_FULL ST_DONE YI_DONE Y_EMPTY0/1 PWG0/1 DRAIN
+    // FULL0/1 EMPTY0/1 X_READY0/1 CB_FULL HBF_READY S_READY Y_FULL ST_DONE YI_DONE Y_EMPTY0/1 PWG0/1 DRAIN NEVER
     // (the state-only pass: XF_EMPTY0/1 in place of ST_DONE / YI_DONE,
     // XP_FREE0/1 in place of Y_EMPTY0/1)
     const int s8 = kStateOnly ? 8 : 1, s1 = kStateOnly ? 1 : 8;
-    const int counts[NBAR] = {1, 1, 1, 1, 8, 8, 1, 8, 8, 1, s8, s8, s1, s1, 4, 4, 1};
+    const int counts[NBAR] = {1, 1, 1, 1, 8, 8, 1, 8, 8, 1, s8, s8, s1, s1, 4, 4, 1, 1};
     for (int i = 0; i < NBAR; ++i) mbar_init(bar(i), counts[i]);
     mbar_fence_init();
   }
@@ -1043,7 +1047,11 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       const int npieces = q >= cw + 2 ? 4 : (q >= cw ? 2 : 0);
       auto piece_col = [&](int i) { return 32 * (cw + 2 * (i >> 1)) + 16 * (i & 1); };
 
-      for (int c = 0; c < nk; ++c) {
+      // test of the bounded-wait error path: a wait nothing completes runs
+      // out (site 50), the CTA takes its abort path and the chunk loop is
+      // skipped
+      const bool stalled = a.stall_cycles > 0 && !waitw(bar(B_NEVER), 0, abort_flag, 50, a.stall_cycles);
+      for (int c = 0; c < nk && !stalled; ++c) {
         const int buf = c & 1;
         if (!waitw(bar(B_X_READY0 + buf), (c >> 1) & 1, abort_flag, 30)) break;
         ALLOY_TRACE_POINT(cw, c, 0);
@@ -1345,6 +1353,7 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
   a.ssm_in = s.ssm_in; a.si_sb = s.si_sb; a.si_sh = s.si_sh; a.si_sn = s.si_sn; a.si_sp = s.si_sp;
   a.ssm_out = s.ssm_out; a.so_sb = s.so_sb; a.so_sh = s.so_sh; a.so_sn = s.so_sn; a.so_sp = s.so_sp;
   a.y = static_cast<__nv_bfloat16*>(s.y); a.y_sb = s.y_sb; a.y_st = s.y_st; a.y_sh = s.y_sh;
+  a.stall_cycles = ssd_tc_stall_cycles().load(std::memory_order_relaxed);
 
   // 1. B/C conv pre-pass into the workspace
   PFN_cuTensorMapEncodeTiled_v12000 encode = get_encode_fn();
@@ -1401,6 +1410,11 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
   }
   if (a.nseg > 1) ALLOY_TRY(launch(ssd_tc_kernel<64, true>, a.nseg - 1));
   return launch(ssd_tc_kernel<64, false>, a.nseg);
+}
+
+std::atomic<long long>& ssd_tc_stall_cycles() {
+  static std::atomic<long long> v{0};
+  return v;
 }
 
 int ssd_tc_take_error(cudaStream_t stream, unsigned int out[3]) {

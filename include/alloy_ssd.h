@@ -219,13 +219,20 @@ ALLOY_API size_t alloy_ssd_combined_min_workspace_size(int64_t batch, int64_t se
  * Same arguments and results as alloy_ssd_combined, without the workspace:
  * the scratch comes from one fixed 8 MiB array compiled into the library,
  * held by every device that loads it until the process exits.  Calls whose
- * smallest scratch (alloy_ssd_combined_min_workspace_size) would exceed 8 MiB
- * are rejected with ALLOY_ERR_UNSUPPORTED before anything is launched (the
- * array then holds the B/C tiles alone).  The call allocates and frees
- * nothing.
- *  - The first call on a device looks up the array's device address
- *    (cudaGetSymbolAddress) with that device current; make that first call
- *    before any stream capture begins.
+ * smallest scratch (alloy_ssd_combined_min_workspace_size: the B/C tiles
+ * alone) exceeds 8 MiB are rejected with ALLOY_ERR_UNSUPPORTED before
+ * anything is launched.  The whole 8 MiB is handed to alloy_ssd_combined as
+ * its workspace, so a call whose full workspace
+ * (alloy_ssd_combined_workspace_size) also fits runs the segmented schedule
+ * with its segment records in the array too; one whose full size does not
+ * fit walks each (batch row, head pair) with one CTA.  The call allocates and
+ * frees nothing.
+ *  - The first call in a device's context looks up the array's device
+ *    address (cudaGetSymbolAddress) with that device current and keeps it
+ *    with the context's unique id; after the context is destroyed and created
+ *    again (cudaDeviceReset) the next call looks it up anew.  Make the first
+ *    call on each device (and the first after a reset) before any stream
+ *    capture begins.
  *  - All calls on a device share the array, and it keeps the last call's
  *    contents: calls that may overlap on the device (different streams, or
  *    other host threads) race and must be serialised by the caller.  Nothing
@@ -248,6 +255,20 @@ ALLOY_API int alloy_ssd_combined_noalloc(const alloy_tensor_t* xBC, const alloy_
  * reference (MLX kernels have no device-side waits).
  */
 ALLOY_API int alloy_check_device_status(void* stream);
+
+/*
+ * Test hook for the bounded-wait error path of the tensor-core prefill.
+ * While cycles > 0, every ssd_tc_kernel launched afterwards (the bf16 path of
+ * alloy_ssd_combined) makes its consumer warps first wait, for that many
+ * clock cycles, on an mbarrier that nothing arrives on.  The wait runs out,
+ * the CTA records site 50 in the device error word, drains its copies and
+ * MMAs in flight, frees its tensor memory and returns, so the next
+ * alloy_check_device_status reports ALLOY_ERR_TIMEOUT; y and the states of
+ * such a call are not valid.  0 (the default) switches it off.  Process-wide;
+ * cycles in [0, 2^32].  No counterpart in the reference (MLX kernels have no
+ * device-side waits).
+ */
+ALLOY_API int alloy_debug_set_wait_stall(int64_t cycles);
 
 /*
  * Gated RMS norm of the mixer output:
@@ -295,6 +316,13 @@ ALLOY_API uint64_t alloy_kernel_launch_count(void);
  *   y       [B, L, H, P]   F32|BF16
  *   ssm_out [B, H, N, P]   F32 via strides (data NULL = not written), may alias ssm_in
  * h_t = a_t h_{t-1} + B_t x_t^T;  y_t = C_t h_t  (fp32 state and accumulation).
+ * Precondition for BF16 x, B and C at (P, N) = (64, 64), (64, 128), (128, 64)
+ * (the tensor-core scan): every decay is at most 1 (A_disc <= 1, log_a <= 0),
+ * as the reference's A_disc = exp(A dt) with A < 0 always is.  That scan
+ * factors exp(cum_t - cum_s) into exp(cum_t) and exp(-cum_s) pieces bounded
+ * only for non-increasing cumulative sums; larger decays overflow there
+ * without an error.  F32 inputs and other sizes run the fp32 scan, which has
+ * no such bound.
  */
 ALLOY_API int alloy_selective_scan(const alloy_tensor_t* x, const alloy_tensor_t* A_disc,
                          const alloy_tensor_t* log_a, const alloy_tensor_t* Bm,
@@ -309,7 +337,8 @@ ALLOY_API int alloy_selective_scan(const alloy_tensor_t* x, const alloy_tensor_t
  * reference).  n_heads H is y's dim 2 (dot's when y is absent).
  *
  *   x       [B, L, Gx, P]  BF16, Gx divides H (head h reads x row h / (H/Gx)), P stride 1
- *   log_a   [B, L, H]      F32, <= 0
+ *   log_a   [B, L, H]      F32, <= 0 (a precondition the kernel does not check:
+ *                          a positive log decay overflows its factored decays)
  *   Bm, Cm  [B, L, G', N]  BF16, G' divides H, N stride 1
  *   ssm_in  [B, H, N, P]   F32 via strides (data NULL = zeros)
  *   y       [B, L, H, P]   F32|BF16 (data NULL = not written)

@@ -861,3 +861,120 @@ def test_decode_linear_vs_fp64(NB, inp, out):
     ref = (x.double() @ w.double().T).cpu().numpy()
     assert y.shape == (NB, out) and y.dtype == torch.bfloat16
     assert_close(np_(y), ref, True)
+
+
+# ------------------------------------------------------- failure detection
+def test_bounded_wait_expiry_is_reported_and_the_context_stays_usable():
+    """A bounded device-side wait that runs out: with the test hook set, the
+    consumer warps of every prefill CTA wait on an mbarrier that nothing
+    completes; each CTA gives up after ~1 ms, drains its copies and MMAs,
+    frees its tensor memory and returns.  The host then reads
+    ALLOY_ERR_TIMEOUT with the site, and a normal call on the same stream
+    afterwards passes parity (no fault, no trap, the context stays usable)."""
+    from alloy_b200 import _lib
+    lib = _lib.load()
+    cfg = dict(B=1, L=512, H=4, P=64, N=64, G=1)
+    inp = oracle.make_inputs(**cfg, dtype="bf16", seed=41, with_state=True)
+    H, P, N, G = cfg["H"], cfg["P"], cfg["N"], cfg["G"]
+
+    def run():
+        return mixer.ssd_combined(
+            cu(inp["xBC"], torch.bfloat16), cu(inp["dt_raw"], torch.bfloat16),
+            cu(inp["conv_weight"]), cu(inp["conv_bias"]), cu(inp["dt_bias"]), cu(inp["A_log"]),
+            cu(inp["D"]), n_heads=H, head_dim=P, d_state=N, n_groups=G,
+            ssm_state=cu(inp["ssm_state"]), conv_state=cu(inp["conv_state"], torch.bfloat16))
+
+    mixer.check_device_status()   # nothing pending from earlier tests
+    assert lib.alloy_debug_set_wait_stall(2_000_000) == 0
+    try:
+        run()
+        with pytest.raises(_lib.AlloyError) as err:
+            mixer.check_device_status()
+    finally:
+        assert lib.alloy_debug_set_wait_stall(0) == 0
+    assert err.value.status == -6
+    assert "ssd_tc_kernel" in err.value.message and "site 50" in err.value.message
+    mixer.check_device_status()   # the record was cleared by the check
+    y_ref, h_ref, _ = oracle.mixer_core(
+        inp["xBC"], inp["dt_raw"], inp["conv_weight"], inp["conv_bias"], inp["dt_bias"],
+        inp["A_log"], inp["D"], n_heads=H, headdim=P, d_state=N, n_groups=G, chunk_size=256,
+        ssm_state=inp["ssm_state"], conv_state=inp["conv_state"])
+    y, h, _ = run()
+    mixer.check_device_status()
+    assert_close(np_(y), y_ref, True)
+    assert_close(np_(h), h_ref, True)
+
+
+def test_wait_stall_hook_rejects_out_of_range_values():
+    from alloy_b200 import _lib
+    lib = _lib.load()
+    assert lib.alloy_debug_set_wait_stall(-1) == -1
+    assert lib.alloy_debug_set_wait_stall((1 << 32) + 1) == -1
+    assert lib.alloy_debug_set_wait_stall(0) == 0
+
+
+# ------------------------------------------------- decode graph vs the oracle
+def _layer_step_fp64(blk, x_tok, h, cs, bf16):
+    """One decode token through a combined-mode layer in float64 on the
+    layer's own (possibly bf16-valued) weights: in-projection, the mixer step
+    (oracle.decode_step_fp64: mamba_block.py:446-448, :160-204, :492-493),
+    gate + inner RMS norm (:495-499), out-projection (:501).  Where the layer
+    stores an activation in bf16 (the projection's output, the mixer's y, the
+    norm's output), the value is rounded to bf16 here too."""
+    f = np.float64
+    rnd = (lambda a: oracle.bf16_round(a.astype(np.float32)).astype(f)) if bf16 else (lambda a: a)
+    W_in = np_(blk.in_proj.weight).astype(f)
+    W_out = np_(blk.out_proj.weight).astype(f)
+    di, cd = blk.d_inner, blk.conv_dim
+    proj = rnd(x_tok.astype(f) @ W_in.T)
+    gate, xBC, dt = proj[:, :di], proj[:, di:di + cd], proj[:, di + cd:]
+    y, h, cs = oracle.decode_step_fp64(
+        xBC, dt, np_(blk.conv_weight), np_(blk.conv_bias), np_(blk.dt_bias), np_(blk.A_log),
+        np_(blk.D), h, cs, n_heads=blk.n_heads, headdim=blk.headdim, d_state=blk.d_state,
+        n_groups=blk.n_groups)
+    v = rnd(y.reshape(y.shape[0], di)) * (gate / (1.0 + np.exp(-gate)))
+    v = v / np.sqrt((v * v).mean(axis=-1, keepdims=True) + blk.norm.eps) * np_(blk.norm.weight).astype(f)
+    return rnd(v) @ W_out.T, h, cs
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_decode_graph_steps_vs_oracle(dtype):
+    """16 decode steps replayed from the captured CUDA graph (the generation
+    loop of alloy/generate.py:84-94 with the cache in device memory) against
+    the float64 layer step of the oracle: each step's output and, after the
+    last, both caches."""
+    from alloy_b200.decode_graph import MambaDecodeGraph
+    torch.manual_seed(11)
+    blk = MambaBlock(d_model=256, d_state=64, d_conv=4, expand=2, headdim=64, n_groups=2,
+                     use_D=True, use_inner_norm=True, combined_proj=True, chunk_size=64,
+                     device=DEV, dtype=dtype)
+    bf16 = dtype == torch.bfloat16
+    with torch.no_grad():
+        blk.A_log.uniform_(0, 2)
+        blk.dt_bias.uniform_(-3, -1)
+        blk.D.normal_()
+        blk.conv_weight.normal_(0, 0.5)
+        blk.norm.weight.uniform_(0.5, 1.5)
+        blk.in_proj.weight.normal_(0, 0.06)
+        blk.out_proj.weight.normal_(0, 0.06)
+        x = torch.randn(3, 30, 256, device=DEV, dtype=dtype)
+        cache = MambaCache()
+        blk(x[:, :14], cache=cache)
+        h = np_(cache.ssm_state).astype(np.float64)
+        cs = np_(cache.conv_state).astype(np.float64)
+        g = MambaDecodeGraph(blk, cache, batch=3)
+        got, ref = [], []
+        for t in range(14, 30):
+            got.append(np_(g.step(x[:, t:t + 1])))
+            out, h, cs = _layer_step_fp64(blk, np_(x[:, t]), h, cs, bf16)
+            ref.append(out)
+        torch.cuda.synchronize()
+    got, ref = np.stack(got)[:, :, 0], np.stack(ref)
+    if bf16:
+        assert_close(got, ref, True)
+        assert_close(np_(cache.ssm_state), h, True)
+        assert_close(np_(cache.conv_state), cs, True)
+    else:
+        assert oracle.rel_l2(got, ref) < 1e-4
+        assert oracle.rel_l2(np_(cache.ssm_state), h) < 1e-4
+        assert oracle.rel_l2(np_(cache.conv_state), cs) < 1e-4

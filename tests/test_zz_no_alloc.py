@@ -20,8 +20,14 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 
 
-def _inputs(seed):
-    cfg = dict(B=2, L=300, H=4, P=64, N=128, G=2)
+# one walk per (batch row, head pair); and a long sequence over few head pairs,
+# whose full workspace (B/C tiles and segment records) fits the 8 MiB array,
+# so the call runs the segmented schedule with its records there too
+CASES = {"unsegmented": dict(B=2, L=300, H=4, P=64, N=128, G=2),
+         "segmented": dict(B=1, L=2048, H=4, P=64, N=64, G=2)}
+
+
+def _inputs(seed, cfg):
     inp = oracle.make_inputs(**cfg, dtype="bf16", seed=seed, with_state=True)
 
     def cu(a, dt=torch.float32):
@@ -31,7 +37,7 @@ def _inputs(seed):
              conv_w=cu(inp["conv_weight"]), conv_b=cu(inp["conv_bias"]), dt_bias=cu(inp["dt_bias"]),
              A_log=cu(inp["A_log"]), D=cu(inp["D"]), ssm=cu(inp["ssm_state"]),
              conv=cu(inp["conv_state"], torch.bfloat16))
-    return cfg, t
+    return t
 
 
 def _noalloc(cfg, t):
@@ -54,10 +60,18 @@ def _close(got, ref):
     assert oracle.max_rel(got, ref) <= TOL_BF16_MAX_REL
 
 
-def test_noalloc_matches_the_workspace_entry_point_on_two_calls():
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_noalloc_matches_the_workspace_entry_point_on_two_calls(case):
     torch.cuda.set_device(0)
+    cfg = CASES[case]
+    d = mixer._dims(cfg["H"], cfg["P"], cfg["N"], cfg["G"], 4, 256, 0, 0)
+    lib = _lib.load()
+    full = lib.alloy_ssd_combined_workspace_size(cfg["B"], cfg["L"], _lib.BF16, _lib.ref(d))
+    small = lib.alloy_ssd_combined_min_workspace_size(cfg["B"], cfg["L"], _lib.BF16, _lib.ref(d))
+    if case == "segmented":
+        assert small < full <= 8 << 20
     for seed in (31, 32):   # two calls in a row on the shared scratch array
-        cfg, t = _inputs(seed)
+        t = _inputs(seed, cfg)
         y_ref, h_ref, cs_ref = mixer.ssd_combined(
             t["xBC"], t["dt_raw"], t["conv_w"], t["conv_b"], t["dt_bias"], t["A_log"], t["D"],
             n_heads=cfg["H"], head_dim=cfg["P"], d_state=cfg["N"], n_groups=cfg["G"],
