@@ -51,6 +51,10 @@
 #ifndef ALLOY_TRACE_COPY_DONE
 #define ALLOY_TRACE_COPY_DONE(bar, parity, role, chunk, id)
 #endif
+#ifndef ALLOY_TRACE_CTA_BEGIN
+#define ALLOY_TRACE_CTA_BEGIN()
+#define ALLOY_TRACE_CTA_END()
+#endif
 
 namespace alloy {
 
@@ -76,6 +80,13 @@ constexpr int kRoleRegs = 64;
 constexpr int kProducerRegsS = 144;
 constexpr int kConsumerRegsS = 64;
 constexpr int kRoleRegsS = 56;
+// x conv + SiLU on packed f32x2 pairs: in the state-only pass (144 producer
+// registers); the full pass keeps the scalar form, which fits its 120
+#ifdef ALLOY_CONV_PACKED_ALL
+constexpr bool kPackedConvAll = true;
+#else
+constexpr bool kPackedConvAll = false;
+#endif
 constexpr int kTmaWarp = 16;           // B/C half tiles
 constexpr int kMmaWarp = 17;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -158,6 +169,21 @@ struct TcArgs {
   // first wait this many cycles on B_NEVER, which nothing completes
   long long stall_cycles;
 };
+
+#ifdef ALLOY_SOFTPLUS_LIB
+#define ALLOY_SOFTPLUS softplus_f32
+#else
+#define ALLOY_SOFTPLUS softplus_fast
+#endif
+// softplus(x) = max(x, 0) + ln(1 + e^-|x|) from the hardware base-2
+// exponential and logarithm (relative error ~1e-7 where the result is not
+// tiny; for x < -17 the e^x term is below fp32 resolution next to 1 and the
+// result is 0 instead of ~e^x, an absolute error below 4e-8)
+__device__ __forceinline__ float softplus_fast(float x) {
+  float l;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(l) : "f"(1.f + ex2_approx(-fabsf(x) * 1.4426950408889634f)));
+  return fmaxf(x, 0.f) + 0.6931471805599453f * l;
+}
 
 // ----------------------------------------------------------------------------
 // bounded waits
@@ -404,6 +430,7 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
 // and X'), Yi (after the previous epilogue), then Y (after the scores).
 template <int N, bool kStateOnly>
 __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
+  constexpr bool kPackedConv = kStateOnly || kPackedConvAll;
   constexpr int NK = N / 64;            // 64-column halves of B/C per chunk
   constexpr int NHALF = N / 2;          // state columns per consumer warpgroup
   extern __shared__ uint8_t smem_raw[];
@@ -439,6 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
   // the chunks already walked) and nothing rescales the state per chunk
   auto chunk_at = [&](int c) { return kStateOnly ? c_lo + nk - 1 - c : c_lo + c; };
 
+  if constexpr (!kStateOnly) ALLOY_TRACE_CTA_BEGIN();
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     // FULL0/1 EMPTY0/1 X_READY0/1 CB_FULL HBF_READY S_READY Y_FULL ST_DONE YI_DONE Y_EMPTY0/1 PWG0/1 DRAIN NEVER
@@ -542,10 +570,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
             tc_fence_after();
             const uint32_t sB = base + OFF_STAGE + cb * 16384;
             const uint32_t sXp = base + (cb ? OFF_X : OFF_XP);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma_bf16(tmem + T_ST, sw128_desc(sXp + 2048 * kk, 16384, 1024),
-                        sw128_desc(sB + 2048 * kk, kStageBytes, 1024), ID_ST, (c | kk) != 0);
+            umma_bf16_chain8<128, 128, sw128_hi(1024), sw128_hi(1024)>(
+                tmem + T_ST, sw128_lo(sXp, 16384), sw128_lo(sB, kStageBytes), ID_ST, c != 0);
             umma_commit(bar(B_EMPTY0 + cb));     // B halves of buffer cb free
             umma_commit(bar(B_XP_FREE0 + cb));   // X'[cb] free
           }
@@ -563,10 +589,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
             if (k == 0 && c > 0 && !wait1(bar(B_Y_FULL), pph, abort_flag, 4)) goto mma_done;
             tc_fence_after();
             const uint32_t sB = base + OFF_STAGE + slot * kStageBytes, sC = sB + 16384;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16(tmem + T_CB, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sB + 32 * kk, 16, 1024), ID_CB,
-                        (k | kk) != 0);
+            umma_bf16_chain4<2, 2, sw128_hi(1024), sw128_hi(1024)>(tmem + T_CB, sw128_lo(sC, 16), sw128_lo(sB, 16),
+                                                                    ID_CB, k != 0);
           }
           umma_commit(bar(B_CB_FULL));
           ALLOY_TRACE_POINT(3, c, 0);
@@ -581,10 +605,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
             // sit in the two stage slots, 32 KB apart (the MN-atom stride)
             const uint32_t sB = base + OFF_STAGE + ((c * NK) & 1) * kStageBytes;
             const uint32_t sXp = base + OFF_XP;
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma_bf16(tmem + T_ST, sw128_desc(sXp + 2048 * kk, 16384, 1024),
-                        sw128_desc(sB + 2048 * kk, kStageBytes, 1024), ID_ST, 1);
+            umma_bf16_chain8<128, 128, sw128_hi(1024), sw128_hi(1024)>(
+                tmem + T_ST, sw128_lo(sXp, 16384), sw128_lo(sB, kStageBytes), ID_ST, 1);
           }
           umma_commit(bar(B_ST_DONE));
           ALLOY_TRACE_POINT(3, c, 10);
@@ -596,10 +618,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           for (int k = 0; k < NK; ++k) {
             const uint32_t sC = base + OFF_STAGE + ((c * NK + k) & 1) * kStageBytes + 16384;
             const uint32_t sH = base + OFF_H + k * 16384;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16(tmem + T_YI, sw128_desc(sC + 32 * kk, 16, 1024), sw128_desc(sH + 32 * kk, 16, 1024),
-                        ID_YI, (k | kk) != 0);
+            umma_bf16_chain4<2, 2, sw128_hi(1024), sw128_hi(1024)>(tmem + T_YI, sw128_lo(sC, 16), sw128_lo(sH, 16),
+                                                                    ID_YI, k != 0);
           }
           // the last reads of this chunk's B/C stages and of H
           for (int k = 0; k < NK; ++k) umma_commit(bar(B_EMPTY0 + ((c * NK + k) & 1)));
@@ -612,10 +632,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const uint32_t sX = base + OFF_X + (buf * 2 + h) * 16384;
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              umma_bf16_ta(tmem + T_Y + 64 * h, tmem + T_CB + 16 * kk + 8 * h,
-                           sw128_desc(sX + 2048 * kk, 16, 1024), ID_Y, kk != 0);
+            umma_bf16_ta_chain8<16, 128, sw128_hi(1024)>(tmem + T_Y + 64 * h, tmem + T_CB + 8 * h, sw128_lo(sX, 16),
+                                                          ID_Y, 0);
           }
           umma_commit(bar(B_Y_FULL));
           ALLOY_TRACE_POINT(3, c, 2);
@@ -740,7 +758,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       auto scan_chunk = [&](int cc) {
         const int cbuf = cc & 1;
         const float dt = chunk_at(cc) * Q + t < L
-            ? softplus_f32((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
+            ? ALLOY_SOFTPLUS((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
             : 0.f;
         if (cc + 1 < nk) load_dt(cc + 1);
         float v = A * dt;
@@ -829,6 +847,48 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           const uint32_t sXp = base + (kStateOnly && buf ? OFF_X : OFF_XP) + hh * 16384;
           const float4* xf4 = reinterpret_cast<const float4*>(xfp + strip * 16);
           float4 fq;
+          if constexpr (kPackedConv) {
+          // the two channel pairs (0,1), (2,3) one after the other, as f32x2:
+          // a pair's taps and bias, and a window of its last three input rows
+          // (each row unpacked once)
+          const uint32_t sxf = smem_u32(xfp + strip * 16);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            uint64_t w2[4], b2, win[3];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) w2[k] = f2_pack(w[k][2 * i], w[k][2 * i + 1]);
+            b2 = f2_pack(bias[2 * i], bias[2 * i + 1]);
+#pragma unroll
+            for (int r = 0; r < 3; ++r) win[r] = f2_from_bf2(rr[r][i]);
+#pragma unroll
+            for (int r = 3; r < 19; ++r) {
+              const int srow = strip * 16 + r - 3;
+              // (volatile: the factor loads stay in row order instead of all
+              // 16 factors being live at once)
+              if (((r - 3) & 3) == 0)
+                asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                             : "=f"(fq.x), "=f"(fq.y), "=f"(fq.z), "=f"(fq.w) : "r"(sxf + 4 * (r - 3)));
+              const float fx = ((r - 3) & 3) == 0 ? fq.x : ((r - 3) & 3) == 1 ? fq.y : ((r - 3) & 3) == 2 ? fq.z : fq.w;
+              const uint64_t xin = f2_from_bf2(rr[r][i]);
+              uint64_t acc = f2_fma(win[0], w2[0], b2);
+              acc = f2_fma(win[1], w2[1], acc);
+              acc = f2_fma(win[2], w2[2], acc);
+              acc = f2_fma(xin, w2[3], acc);
+              // acc = h = x/2 (halved taps): silu(x) = h + h tanh(h)
+              float hl, hh2;
+              f2_unpack(acc, hl, hh2);
+              const uint64_t y2 = f2_fma(acc, f2_pack(tanh_approx(hl), tanh_approx(hh2)), acc);
+              const uint32_t off = srow * 128 + (((vc4 >> 1) ^ (srow & 7)) << 4) + ((vc4 & 1) << 3) + 4 * i;
+              if constexpr (!kStateOnly)   // (the state-only pass needs X' alone)
+                asm volatile("st.shared.b32 [%0], %1;" ::"r"(sX + off), "r"(f2_to_bf2(y2)) : "memory");
+              asm volatile("st.shared.b32 [%0], %1;" ::"r"(sXp + off), "r"(f2_to_bf2(f2_mul(y2, f2_splat(fx))))
+                           : "memory");
+              win[0] = win[1];
+              win[1] = win[2];
+              win[2] = xin;
+            }
+          }
+          } else {
 #pragma unroll
           for (int r = 3; r < 19; ++r) {
             const int srow = strip * 16 + r - 3;
@@ -856,6 +916,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
             if constexpr (!kStateOnly)   // (the state-only pass needs X' alone)
               asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(sX + off), "r"(o[0]), "r"(o[1]) : "memory");
             asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(sXp + off), "r"(ox[0]), "r"(ox[1]) : "memory");
+          }
           }
         }
         prefetch_rows(c + 1 + kL2Ahead);
@@ -959,7 +1020,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
           for (int c = 0; c < nk; ++c) {
             const int buf = c & 1;
             const float dt = chunk_at(c) * Q + t < L
-                ? softplus_f32((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
+                ? ALLOY_SOFTPLUS((a.dt_bf16 ? __uint_as_float(dt_bits << 16) : __uint_as_float(dt_bits)) + dtb)
                 : 0.f;
             if (c + 1 < nk) dt_bits = load_dt(c + 1);
             float v = A * dt;
@@ -1114,7 +1175,11 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         auto score_piece = [&](int i, const uint32_t (&r)[16]) {
           const int j = cw + 2 * (i >> 1);
           const int s0 = piece_col(i);
+#ifdef ALLOY_SCORE_UNROLL
+#pragma unroll
+#else
 #pragma unroll 1
+#endif
           for (int h = 0; h < 2; ++h) {
             const float* cm = cum_s + (buf * 2 + h) * 128;
             const float cum_t = cm[t];
@@ -1142,6 +1207,30 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
               const uint64_t R2 = f2_splat(ex2_approx((cum_t - cm[s0 + 15]) * kLog2e));
               const float4* cf4 = reinterpret_cast<const float4*>(cf_s + (buf * 2 + h) * 128 + s0);
               const float Dh = h ? D1 : D0;
+#ifdef ALLOY_DIAG_SAT
+              // mask and D as factors: m_u = [s0 + u <= t] = sat(t - s0 + 1 - u),
+              // d_u = [s0 + u == t] = m_u - m_{u+1}; S = CB R (cf m) + D d
+              const uint64_t D2 = f2_splat(Dh);
+              const float fdd = static_cast<float>(t - s0 + 1);
+#pragma unroll
+              for (int i4 = 0; i4 < 4; ++i4) {
+                const float4 f = cf4[i4];
+                float m[5];
+#pragma unroll
+                for (int u = 0; u < 5; ++u) {
+                  const float v = fdd - static_cast<float>(4 * i4 + u);
+                  asm("cvt.sat.f32.f32 %0, %1;" : "=f"(m[u]) : "f"(v));
+                }
+                const uint64_t m01 = f2_pack(m[0], m[1]), m23 = f2_pack(m[2], m[3]);
+                const uint64_t d01 = f2_pack(m[0] - m[1], m[1] - m[2]), d23 = f2_pack(m[2] - m[3], m[3] - m[4]);
+                o[2 * i4] = f2_to_bf2(f2_fma(
+                    f2_mul(f2_pack(__uint_as_float(r[4 * i4]), __uint_as_float(r[4 * i4 + 1])), R2),
+                    f2_mul(f2_pack(f.x, f.y), m01), f2_mul(d01, D2)));
+                o[2 * i4 + 1] = f2_to_bf2(f2_fma(
+                    f2_mul(f2_pack(__uint_as_float(r[4 * i4 + 2]), __uint_as_float(r[4 * i4 + 3])), R2),
+                    f2_mul(f2_pack(f.z, f.w), m23), f2_mul(d23, D2)));
+              }
+#else
 #pragma unroll
               for (int i4 = 0; i4 < 4; ++i4) {
                 const float4 f = cf4[i4];
@@ -1158,6 +1247,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
                 o[2 * i4] = pack_bf16x2(x[0], x[1]);
                 o[2 * i4 + 1] = pack_bf16x2(x[2], x[3]);
               }
+#endif
             } else {
               // the diagonal block at a larger decay range: exact factors (<= 1
               // for s <= t, at any range), zero right of the diagonal, D on it
@@ -1239,6 +1329,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if constexpr (!kStateOnly) ALLOY_TRACE_CTA_END();
 }
 
 // ----------------------------------------------------------------------------

@@ -225,6 +225,77 @@ __device__ __forceinline__ void umma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, u
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Low and high 32-bit words of sw128_desc (below): the high word holds only
+// the stride byte offset and the constant version / layout fields.
+__device__ __forceinline__ uint32_t sw128_lo(uint32_t saddr, uint32_t lbo) {
+  return ((saddr >> 4) & 0x3FFFu) | (((lbo >> 4) & 0x3FFFu) << 16);
+}
+__host__ __device__ constexpr uint32_t sw128_hi(uint32_t sbo) {
+  return ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+}
+
+// A chain of 4 or 8 MMAs D (+)= A_i B_i in one asm block (one issue sequence
+// for the issuing thread, no per-MMA descriptor arithmetic in C++).  The
+// operands are SW128 descriptors given by their low words (sw128_lo) and
+// constant high words (sw128_hi); operand i's start addresses are the first
+// ones advanced by i * A_STEP / i * B_STEP (units of 16 bytes; the 14-bit
+// start-address field cannot overflow for shared-memory addresses).  The
+// first MMA accumulates when `acc0` is nonzero, every later one always.
+template <int A_STEP, int B_STEP, uint32_t A_HI, uint32_t B_HI>
+__device__ __forceinline__ void umma_bf16_chain4(uint32_t d_tmem, uint32_t alo, uint32_t blo, uint32_t idesc,
+                                                 uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred p, t;\n\t.reg .b32 al, bl;\n\t.reg .b64 a, b;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\tsetp.eq.u32 t, 0, 0;\n\t"
+      "mov.b64 a, {%1, %7};\n\tmov.b64 b, {%2, %8};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p;\n\t"
+      "add.u32 al, %1, %5;\n\tadd.u32 bl, %2, %6;\n\t"
+      "mov.b64 a, {al, %7};\n\tmov.b64 b, {bl, %8};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.u32 al, al, %5;\n\tadd.u32 bl, bl, %6;\n\t"
+      "mov.b64 a, {al, %7};\n\tmov.b64 b, {bl, %8};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t"
+      "add.u32 al, al, %5;\n\tadd.u32 bl, bl, %6;\n\t"
+      "mov.b64 a, {al, %7};\n\tmov.b64 b, {bl, %8};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, t;\n\t}" ::"r"(d_tmem),
+      "r"(alo), "r"(blo), "r"(idesc), "r"(acc0), "n"(A_STEP), "n"(B_STEP), "r"(A_HI), "r"(B_HI)
+      : "memory");
+}
+template <int A_STEP, int B_STEP, uint32_t A_HI, uint32_t B_HI>
+__device__ __forceinline__ void umma_bf16_chain8(uint32_t d_tmem, uint32_t alo, uint32_t blo, uint32_t idesc,
+                                                 uint32_t acc0) {
+  umma_bf16_chain4<A_STEP, B_STEP, A_HI, B_HI>(d_tmem, alo, blo, idesc, acc0);
+  umma_bf16_chain4<A_STEP, B_STEP, A_HI, B_HI>(d_tmem, alo + 4 * A_STEP, blo + 4 * B_STEP, idesc, 1);
+}
+// 8 MMAs with A read from tensor memory: A_i at a_tmem + i * A_COLS columns,
+// B_i's start address advanced by i * B_STEP; the first accumulates when acc0 != 0.
+template <int A_COLS, int B_STEP, uint32_t B_HI>
+__device__ __forceinline__ void umma_bf16_ta_chain8(uint32_t d_tmem, uint32_t a_tmem, uint32_t blo, uint32_t idesc,
+                                                    uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred p, t;\n\t.reg .b32 a, bl;\n\t.reg .b64 b;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\tsetp.eq.u32 t, 0, 0;\n\t"
+      "mov.b64 b, {%2, %7};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], b, %3, p;\n\t"
+      "mov.b32 a, %1;\n\tmov.b32 bl, %2;\n\t"
+      "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+      "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+      "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+      "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+      "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+      "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+      "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(blo), "r"(idesc), "r"(acc0), "n"(A_COLS), "n"(B_STEP), "r"(B_HI)
+      : "memory");
+}
+
 // Arrive once on an mbarrier when all previously issued tcgen05.mma of this
 // thread have completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
