@@ -230,20 +230,18 @@ def make_prefill_inputs(B, L, H, P, N, G, K, seed, device):
                 A_log=A_log, D=D)
 
 
-def run_ours(args, w):
+def prefill_problem(w, world, rank, dev, shard_of=None):
+    """Inputs of this rank's share of a prefill workload: ``rot`` rotating
+    input/output sets (each step reads and writes memory the previous steps
+    did not touch, > 3x L2 in between), the call's keyword arguments and a
+    ``step(i)`` that runs one fused prefill on set i % rot."""
     import torch
-    from alloy_b200 import _lib, mixer
+    from alloy_b200 import mixer
 
-    world, rank, local = dist_setup(args.gpus)
-    dev = torch.device("cuda", local if world > 1 else 0)
-    # --shard-of N on one GPU: the share of one rank of an N-GPU run (profiling)
-    H_l, G_l = local_problem(w, args.shard_of if world == 1 and args.shard_of else world, rank)
+    H_l, G_l = local_problem(w, shard_of or world, rank)
     B, L, P, N, K, Q = w["B"], w["L"], w["P"], w["N"], w["K"], w["Q"]
     conv_dim = H_l * P + 2 * G_l * N
     kw = dict(n_heads=H_l, head_dim=P, d_state=N, n_groups=G_l, d_conv=K, chunk_size=Q)
-
-    # one input/output set per rotation slot, so that every step reads and
-    # writes memory not touched in the previous steps (> 3x L2 in between)
     step_bytes = B * L * (conv_dim + H_l) * 2 + B * L * H_l * P * 2
     rot = max(1, math.ceil(3 * L2_BYTES / step_bytes))
     sets = []
@@ -260,42 +258,127 @@ def run_ours(args, w):
                            inp["dt_bias"], inp["A_log"], inp["D"], out=out["y"],
                            ssm_state_out=out["h"], conv_state_out=out["cs"], **kw)
 
-    for i in range(args.warmup):
+    # algorithmic bytes of one step of this rank (one pass over the data)
+    alg = (B * L * conv_dim * 2 + B * L * H_l * 2 + B * L * H_l * P * 2 + B * H_l * N * P * 4
+           + B * (K - 1) * conv_dim * 2)
+    return dict(H_l=H_l, G_l=G_l, kw=kw, rot=rot, sets=sets, step=step, alg=alg,
+                step_bytes=step_bytes, tokens=B * L)
+
+
+def time_steps(step, steps, warmup, world, stream, per_step_events=True):
+    """Device time of ``steps`` calls of step(i) after ``warmup`` untimed ones,
+    bracketed by a barrier and a synchronize on both sides: (ms per step over
+    the whole region, ms per step summed over the per-step event pairs,
+    library kernel launches in the region); times are local to this rank."""
+    import torch
+    from alloy_b200 import _lib
+    for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
-
-    stream = torch.cuda.current_stream(dev)
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ke = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    clocks = ClockSampler(dev.index)
-    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ks = [torch.cuda.Event(enable_timing=True) for _ in range(steps)] if per_step_events else []
+    ke = [torch.cuda.Event(enable_timing=True) for _ in range(steps)] if per_step_events else []
     barrier(world)
     torch.cuda.synchronize()
-    h0 = time.perf_counter()
     launches0 = _lib.load().alloy_kernel_launch_count()
     ev0.record(stream)
-    for i in range(args.steps):
-        ks[i].record(stream)
+    for i in range(steps):
+        if ks:
+            ks[i].record(stream)
         step(i)
-        ke[i].record(stream)
+        if ke:
+            ke[i].record(stream)
     ev1.record(stream)
     launches = _lib.load().alloy_kernel_launch_count() - launches0
     torch.cuda.synchronize()
-    h1 = time.perf_counter()
     barrier(world)
+    ms = ev0.elapsed_time(ev1) / steps
+    kernel_ms = sum(a.elapsed_time(b) for a, b in zip(ks, ke)) / steps if ks else ms
+    return ms, kernel_ms, launches
+
+
+def sub_results(args, world, rank, dev, stream):
+    """The other workloads, measured in the same run at their own shapes and
+    sharded over the same ranks (heads for the one-group Zamba2 layers, batch
+    rows for decode), each device-timed with CUDA events (max over ranks):
+    the Zamba2-1.2B layer prefill, the 131,072-token Zamba2 sequence (with the
+    all-gather of y as well when N > 1), and 64 decode steps at batch 256 of
+    the Nemotron-H shape.  A few steps each, so the whole run stays short."""
+    import torch
+    peak, peak_kind = measured_peaks()
+    res = {}
+    steps, warm = max(5, min(args.steps, 20)), 3
+    for key in ("zamba2", "long"):
+        w = dict(WORKLOADS[key])
+        pb = prefill_problem(w, world, rank, dev)
+        ms, kernel_ms, launches = time_steps(pb["step"], steps, warm, world, stream)
+        ms, kernel_ms = dist_max(ms, world), dist_max(kernel_ms, world)
+        gbs = pb["alg"] / (kernel_ms * 1e-3) / 1e9
+        entry = {"value": pb["tokens"] / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+                 "steps": steps, "warmup": warm, "gpu_launches": launches,
+                 "config": {"batch": w["B"], "seq_len": w["L"], "n_heads": w["H"], "head_dim": w["P"],
+                            "d_state": w["N"], "n_groups": w["G"], "chunk_size": w["Q"],
+                            "shard": f"{pb['H_l']} heads / {pb['G_l']} groups per GPU",
+                            "l2": f"{pb['rot']} rotating input/output sets of "
+                                  f"{pb['step_bytes'] / 2**20:.0f} MiB"},
+                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                              "frac": gbs / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                              "algorithmic_bytes_per_gpu": pb["alg"]}}
+        if world > 1 and key == "long":
+            entry["with_gather"] = run_with_gather(argparse.Namespace(steps=steps, warmup=warm),
+                                                   pb["step"], pb["sets"], world, stream, pb["tokens"])
+        res[w["name"]] = entry
+        del pb
+        torch.cuda.empty_cache()
+    w = dict(WORKLOADS["decode"])
+    dp = decode_problem(w, world, rank, dev)
+    ms, _, launches = time_steps(dp["step"], 64, 4, world, stream, per_step_events=False)
+    ms = dist_max(ms, world)
+    gbs = dp["alg"] / (ms * 1e-3) / 1e9
+    res[w["name"]] = {"value": gbs * world, "unit": "GB/s (whole job)", "ms_per_step": ms,
+                      "tokens_per_s": w["B"] / (ms * 1e-3), "steps": 64, "warmup": 4,
+                      "gpu_launches": launches,
+                      "config": {"batch": w["B"], "batch_per_gpu": dp["B"], "n_heads": w["H"],
+                                 "head_dim": w["P"], "d_state": w["N"], "n_groups": w["G"],
+                                 "state_layout": "[B,H,P,N] f32", "conv_state_layout": "[B,C,K-1] bf16",
+                                 "tokens_cycled": 64},
+                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                                   "frac": gbs / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                                   "algorithmic_bytes_per_gpu": dp["alg"]}}
+    del dp
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_ours(args, w):
+    import torch
+    from alloy_b200 import _lib, mixer
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    # --shard-of N on one GPU: the share of one rank of an N-GPU run (profiling)
+    pb = prefill_problem(w, world, rank, dev,
+                         shard_of=args.shard_of if world == 1 and args.shard_of else None)
+    H_l, G_l, kw, rot, sets, step = pb["H_l"], pb["G_l"], pb["kw"], pb["rot"], pb["sets"], pb["step"]
+    B, L, P, N, K, Q = w["B"], w["L"], w["P"], w["N"], w["K"], w["Q"]
+    step_bytes = pb["step_bytes"]
+
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    h0 = time.perf_counter()
+    ms_local, kernel_ms_local, launches = time_steps(step, args.steps, 0, world, stream)
+    h1 = time.perf_counter()
     clocks.stop()
-    ms_local = ev0.elapsed_time(ev1) / args.steps
-    kernel_ms_local = sum(a.elapsed_time(b) for a, b in zip(ks, ke)) / args.steps
     ms = dist_max(ms_local, world)
     kernel_ms = dist_max(kernel_ms_local, world)
     tokens = B * L
     value = tokens / (ms * 1e-3)
 
-    # algorithmic bytes of one step of this rank (one pass over the data)
-    alg = (B * L * conv_dim * 2 + B * L * H_l * 2 + B * L * H_l * P * 2 + B * H_l * N * P * 4
-           + B * (K - 1) * conv_dim * 2)
+    alg = pb["alg"]
     peak, peak_kind = measured_peaks()
     achieved = alg / (kernel_ms_local * 1e-3) / 1e9
     achieved = dist_max(-achieved, world) * -1 if world > 1 else achieved  # slowest rank
@@ -308,6 +391,13 @@ def run_ours(args, w):
     gather = None
     if world > 1 and (args.gather or args.workload == "long"):
         gather = run_with_gather(args, step, sets, world, stream, B * L)
+    # ---- the other workloads, in the same run (default workload only) ----
+    subs = None
+    if args.workload == "nemotron" and not args.no_sub and not args.shard_of and args.batch is None \
+            and args.seqlen is None:
+        del pb, sets, step
+        torch.cuda.empty_cache()
+        subs = sub_results(args, world, rank, dev, stream)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -336,6 +426,8 @@ def run_ours(args, w):
             line["e2e"] = e2e
         if gather is not None:
             line["with_gather"] = gather
+        if subs is not None:
+            line["sub_results"] = subs
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -817,16 +909,12 @@ def run_decode_block(args, w):
         dist.destroy_process_group()
 
 
-def run_decode(args, w):
-    """Decode-step workload: B sequences advance one token per step through
-    the conv cache and the fp32 SSM cache ([B, H, P, N] storage), 64
-    sequential tokens cycled; reported as achieved HBM GB/s (the state is
-    read and written once per token)."""
+def decode_problem(w, world, rank, dev):
+    """This rank's share of the decode workload (batch rows split over the
+    ranks): B sequences advance one token per step through the conv cache and
+    the fp32 SSM cache ([B, H, P, N] storage), 64 tokens cycled."""
     import torch
-    from alloy_b200 import _lib, mixer
-
-    world, rank, local = dist_setup(args.gpus)
-    dev = torch.device("cuda", local if world > 1 else 0)
+    from alloy_b200 import mixer
     H, P, N, G, K = w["H"], w["P"], w["N"], w["G"], w["K"]
     if w["B"] % world:
         raise SystemExit("batch does not split over the GPUs")
@@ -848,29 +936,36 @@ def run_decode(args, w):
         mixer.ssd_decode_step(xtok[i % T], dtok[i % T], p["conv_w"], p["conv_b"], p["dt_bias"],
                               p["A_log"], p["D"], conv, ssm, **kw)
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    stream = torch.cuda.current_stream(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(dev.index)
-    clocks.start()
-    barrier(world)
-    torch.cuda.synchronize()
-    h0 = time.perf_counter()
-    launches0 = _lib.load().alloy_kernel_launch_count()
-    ev0.record(stream)
-    for i in range(args.steps):
-        step(i)
-    ev1.record(stream)
-    launches = _lib.load().alloy_kernel_launch_count() - launches0
-    torch.cuda.synchronize()
-    h1 = time.perf_counter()
-    barrier(world)
-    clocks.stop()
-    ms = dist_max(ev0.elapsed_time(ev1) / args.steps, world)
+    # state read + written, conv cache read + written, the token in, y out
     alg = (2 * B * H * P * N * 4 + 2 * B * C * (K - 1) * 2 + B * C * 2 + B * H * 2
            + B * H * P * 2)
+    return dict(B=B, C=C, T=T, step=step, alg=alg,
+                state_mib=B * H * P * N * 4 / 2**20)
+
+
+def run_decode(args, w):
+    """Decode-step workload: B sequences advance one token per step through
+    the conv cache and the fp32 SSM cache ([B, H, P, N] storage), 64
+    sequential tokens cycled; reported as achieved HBM GB/s (the state is
+    read and written once per token)."""
+    import torch
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    H, P, N, G, K = w["H"], w["P"], w["N"], w["G"], w["K"]
+    dp = decode_problem(w, world, rank, dev)
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        dp["step"](i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    h0 = time.perf_counter()
+    ms, _, launches = time_steps(dp["step"], args.steps, 0, world, stream, per_step_events=False)
+    h1 = time.perf_counter()
+    clocks.stop()
+    ms = dist_max(ms, world)
+    alg = dp["alg"]
     peak, peak_kind = measured_peaks()
     gbs = alg * world / (ms * 1e-3) / 1e9
     if rank == 0:
@@ -881,8 +976,8 @@ def run_decode(args, w):
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": w["name"], "batch": w["B"], "n_heads": H, "head_dim": P,
                        "d_state": N, "n_groups": G, "state_layout": "[B,H,P,N] f32",
-                       "conv_state_layout": "[B,C,K-1] bf16", "tokens_cycled": T,
-                       "l2": "state of %.0f MiB per GPU > L2" % (B * H * P * N * 4 / 2**20)},
+                       "conv_state_layout": "[B,C,K-1] bf16", "tokens_cycled": dp["T"],
+                       "l2": "state of %.0f MiB per GPU > L2" % dp["state_mib"]},
             "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
                          "frac": gbs / world / peak, "traffic": None,
                          "peak_source": f"{peak_kind} hbm_gbs"},
@@ -1007,6 +1102,8 @@ def main():
                          "the per-GPU work of a multi-GPU run; the line reports that shard's tokens)")
     ap.add_argument("--piece-tokens", type=int, default=2048,
                     help="tokens per piece of the end-to-end leg's host-streamed prefill")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="skip the other workloads' sub-results of the default run")
     ap.add_argument("--gather", action="store_true",
                     help="also time each step followed by the all-gather of y (N > 1; "
                          "always on for the long workload)")
