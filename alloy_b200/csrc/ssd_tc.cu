@@ -160,9 +160,10 @@ struct TcArgs {
   // sequence segments (gridDim.z of the full kernel): segment s of a (batch
   // row, head pair) covers chunks [s nchunks / nseg, (s+1) nchunks / nseg)
   int nseg;
-  // [B][head pairs][nseg][128 (h,p)][N]: record 0 the call's initial state,
-  // record s + 1 the end state of segment s (segment 0 from the initial state,
-  // later segments from zero), written by the state-only pass
+  // [B][head pairs][nseg][128 (h,p)][N]: the state-only pass writes record
+  // s + 1 = the end state of segment s walked from zero (s < nseg - 1);
+  // seg_carry_kernel then turns record s into the state carried into
+  // segment s (record 0 the call's initial state)
   float* seg_state;
   float* seg_logdecay;       // [B][head pairs][nseg][2]: sum of A dt over segment s, per head
   // > 0 only in a test of the bounded-wait error path: the consumer warps
@@ -404,6 +405,57 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
       *reinterpret_cast<uint4*>(dst + row * 128 + ((nn8 ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
     __syncthreads();   // buffer i & 1 is free for chunk i + 2
+  }
+}
+
+// ----------------------------------------------------------------------------
+// state carried into each sequence segment
+// ----------------------------------------------------------------------------
+// Runs between the state-only pass and the full pass of a segmented call.
+// Record 0 of a (batch row, head pair) becomes the call's initial state
+// (ssm_in, zeros without one); record s, the end state of segment s-1 walked
+// from zero, becomes the state carried into segment s:
+//   rec[s] = exp(sum of A dt over segment s-1) rec[s-1] + rec[s],  s = 1 .. nseg-1,
+// the chunk recurrence of alloy/models/mamba_block.py:340-357 at segment
+// granularity.  One thread per 4 consecutive (h,p,n) elements of a record;
+// the records of 8 segments are loaded per memory round trip, then folded in
+// order, so the pass takes about nseg / 8 round trips.  The full pass then
+// loads one record per segment.
+__global__ void __launch_bounds__(256) seg_carry_kernel(const TcArgs a, int pairs) {
+  const int N = a.N;
+  const int e = (blockIdx.x * 256 + threadIdx.x) * 4;   // (t, n .. n+3) of a [128][N] record
+  if (e >= 128 * N) return;
+  const int pair = blockIdx.y, b = blockIdx.z;
+  const int t = e / N, n = e % N, hr = t >> 6, pr = t & 63;
+  const size_t slot = ((size_t)b * pairs + pair) * a.nseg;
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (a.ssm_in) {
+    const float* src = a.ssm_in + (int64_t)b * a.si_sb + (int64_t)(a.head_begin + 2 * pair + hr) * a.si_sh +
+                       (int64_t)pr * a.si_sp + (int64_t)n * a.si_sn;
+    v = make_float4(src[0], src[a.si_sn], src[2 * a.si_sn], src[3 * a.si_sn]);
+  }
+  float4* rec = reinterpret_cast<float4*>(a.seg_state + slot * 128 * N + e);
+  const size_t rstride = (size_t)128 * N / 4;   // float4s between consecutive records
+  rec[0] = v;
+#pragma unroll 1
+  for (int s0 = 1; s0 < a.nseg; s0 += 8) {
+    float4 r[8];
+    float ld[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (s0 + k < a.nseg) {
+        r[k] = rec[(size_t)(s0 + k) * rstride];
+        ld[k] = a.seg_logdecay[(slot + s0 + k - 1) * 2 + hr];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (s0 + k < a.nseg) {
+        const float d = ex2_approx(ld[k] * kLog2e);
+        v = make_float4(fmaf(d, v.x, r[k].x), fmaf(d, v.y, r[k].y), fmaf(d, v.z, r[k].z), fmaf(d, v.w, r[k].w));
+        rec[(size_t)(s0 + k) * rstride] = v;
+      }
+    }
   }
 }
 
@@ -975,24 +1027,6 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         return reinterpret_cast<float4*>(a.seg_state + ((seg_slot + j) * 128 + t) * N + cw * NHALF + n8 * 8);
       };
       if constexpr (kStateOnly) {
-        // segment 0 keeps the call's initial state (zeros without one) as
-        // record 0, so that the full pass never reads ssm_in of a segmented
-        // call and an in-place update (ssm_out aliasing ssm_in) is safe
-        if (seg == 0) {
-#pragma unroll 1
-          for (int n8 = 0; n8 < NHALF / 8; ++n8) {
-            float v[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int n = cw * NHALF + n8 * 8 + i;
-              v[i] = a.ssm_in ? a.ssm_in[(int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh +
-                                         (int64_t)n * a.si_sn + (int64_t)pr * a.si_sp]
-                              : 0.f;
-            }
-            record(0, n8)[0] = make_float4(v[0], v[1], v[2], v[3]);
-            record(0, n8)[1] = make_float4(v[4], v[5], v[6], v[7]);
-          }
-        }
         // ---- per chunk of the walk: dt, its scan and the X' row factors ----
         // Warpgroup cw scans head h0 + cw, warp q rows [32q, 32q + 32).  The
         // factor of row t is exp(the sum of A dt after row t to the segment's
@@ -1036,6 +1070,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(B_PWG0 + cw));
             if (!waitw(bar(B_PWG0 + cw), c & 1, abort_flag, 24)) break;
+            ALLOY_TRACE_POINT(cw, c, 0);
             float pre = 0.f, tot = 0.f;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -1049,6 +1084,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
             suffix += tot;
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(B_XF_FULL0 + buf));
+            ALLOY_TRACE_POINT(cw, c, 1);
           }
           // the segment's log decay (head h0 + cw), for the full pass's carry
           if (t == 0) a.seg_logdecay[(seg_slot + seg) * 2 + cw] = suffix;
@@ -1069,36 +1105,40 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
         }
       } else {
       // initial state -> TMEM: the call's initial state (unsegmented), else
-      // record 0 carried over segments 0 .. seg-1 as state = exp(sum of A dt
-      // over segment j) state + (end state of segment j from zero).  sp: a
-      // strided view of ssm_in or record 0 (n stride 1), or none (zero).
+      // record seg, the state carried into this segment (seg_carry_kernel).
+      // sp: a strided view of ssm_in, or the record (n stride 1), or none
+      // (zero).  32 values a batch, every load of a batch issued before the
+      // first use (one memory round trip a batch).
       const float* sp = nullptr;
       int64_t sn = 1;
       if (a.nseg > 1) {
-        sp = reinterpret_cast<const float*>(record(0, 0));
+        sp = reinterpret_cast<const float*>(record(seg, 0));
       } else if (a.ssm_in) {
         sp = a.ssm_in + (int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh + (int64_t)pr * a.si_sp +
              (int64_t)(cw * NHALF) * a.si_sn;
         sn = a.si_sn;
       }
 #pragma unroll 1
-      for (int n8 = 0; n8 < NHALF / 8; ++n8) {
-        float v[8];
+      for (int h32 = 0; h32 < NHALF / 32; ++h32) {
+        uint32_t r[32];
+        if (sp == nullptr) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = sp ? sp[(int64_t)(n8 * 8 + i) * sn] : 0.f;
-#pragma unroll 1
-        for (int j = 0; j < seg; ++j) {
-          const float dj = ex2_approx(a.seg_logdecay[(seg_slot + j) * 2 + hr] * kLog2e);
-          const float4* sj = record(j + 1, n8);
-          const float4 w0 = sj[0], w1 = sj[1];
-          const float add[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        } else if (sn == 1) {
+          const float4* s4 = reinterpret_cast<const float4*>(sp + h32 * 32);
+          float4 w[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = fmaf(dj, v[i], add[i]);
+          for (int i = 0; i < 8; ++i) w[i] = s4[i];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            r[4 * i] = __float_as_uint(w[i].x); r[4 * i + 1] = __float_as_uint(w[i].y);
+            r[4 * i + 2] = __float_as_uint(w[i].z); r[4 * i + 3] = __float_as_uint(w[i].w);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(sp[(int64_t)(h32 * 32 + i) * sn]);
         }
-        uint32_t r[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) r[i] = __float_as_uint(v[i]);
-        tmem_st8(lane_base + T_ST + cw * NHALF + n8 * 8, r);
+        tmem_st32(lane_base + T_ST + cw * NHALF + h32 * 32, r);
       }
       tmem_st_wait();
 
@@ -1495,11 +1535,23 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
     kernel<<<dim3(s.head_count / 2, s.B, nz), kThreads, kSmemBytes, stream>>>(a);
     return check_launch("ssd_tc_kernel");
   };
+  // the states carried into the segments, from the state-only pass's records
+  auto carry = [&]() -> int {
+    const int pairs = s.head_count / 2;
+    seg_carry_kernel<<<dim3((128 * s.N / 4 + 255) / 256, pairs, s.B), 256, 0, stream>>>(a, pairs);
+    return check_launch("seg_carry_kernel");
+  };
   if (s.N == 128) {
-    if (a.nseg > 1) ALLOY_TRY(launch(ssd_tc_kernel<128, true>, a.nseg - 1));
+    if (a.nseg > 1) {
+      ALLOY_TRY(launch(ssd_tc_kernel<128, true>, a.nseg - 1));
+      ALLOY_TRY(carry());
+    }
     return launch(ssd_tc_kernel<128, false>, a.nseg);
   }
-  if (a.nseg > 1) ALLOY_TRY(launch(ssd_tc_kernel<64, true>, a.nseg - 1));
+  if (a.nseg > 1) {
+    ALLOY_TRY(launch(ssd_tc_kernel<64, true>, a.nseg - 1));
+    ALLOY_TRY(carry());
+  }
   return launch(ssd_tc_kernel<64, false>, a.nseg);
 }
 

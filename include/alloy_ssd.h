@@ -295,7 +295,8 @@ ALLOY_API int alloy_gated_rmsnorm(const alloy_tensor_t* y, const alloy_tensor_t*
  * Number of kernels this library has launched in this process (every thread
  * and device), for counting the launches of a timed region: a segmented
  * prefill (alloy_ssd_combined with fewer (batch row, head pair) units than
- * SMs) launches one more than an unsegmented one.  No counterpart in the
+ * SMs) launches two more than an unsegmented one (the state-only pass and
+ * the segment carry).  No counterpart in the
  * reference.
  */
 ALLOY_API uint64_t alloy_kernel_launch_count(void);
