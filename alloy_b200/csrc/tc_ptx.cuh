@@ -79,6 +79,20 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// The kernel launched after this one with programmatic stream serialization
+// may start once every CTA of this grid has executed pdl_trigger (or exited).
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Blocks until the grid this one depends on (the previous kernel on the
+// stream, when this one was launched with programmatic stream serialization)
+// has completed and its memory operations are visible; returns at once for
+// an ordinary launch.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- register split
 // Executed by all four warps of a warpgroup at one program point.  The block
 // is launched with R registers a thread; the decreases of some warpgroups must
