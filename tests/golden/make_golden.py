@@ -214,6 +214,106 @@ def case_conv_vjp(root, name, seed=43):
     print(f"{name}: dx {dx.shape}, dweight {dw.shape}")
 
 
+HOT_PATH = ("_depthwise_conv1d", "_selective_scan", "_scan_chunk", "_selective_scan_sequential")
+
+
+def case_bridge_trace(mb, cache_mod, name, seed=6):
+    """Every hot-path call the reference's own ``MambaBlock.__call__`` makes,
+    recorded with its arguments, its results and the cache's ssm_state before
+    and after, in both modes: combined (Zamba2 / Nemotron-H: ``_forward_combined``,
+    mamba_block.py:428-501) as a chunked prefill through a cache followed by
+    single-token cached steps, and split (``_forward_split``, :385-426) as a
+    prefill without a cache, a prefill with one and cached steps.  Nested
+    calls (``_scan_chunk`` inside ``_selective_scan``, :340-357, and the L <= 1
+    hand-off to ``_selective_scan_sequential``, :322-323) are recorded too.
+    A GPU test replays each call through ``alloy_b200.mlx_bridge`` (the
+    reference's source does not exist where the GPU tests run)."""
+    calls = []
+    saved = {n: getattr(mb.MambaBlock, n) for n in HOT_PATH}
+
+    def recorder(nm, fn):
+        def rec(self, *args, **kwargs):
+            cache = kwargs.get("cache", args[4] if nm in ("_selective_scan", "_selective_scan_sequential")
+                               and len(args) > 4 else None)
+            h0 = None if cache is None or cache.ssm_state is None else np.array(cache.ssm_state)
+            entry = dict(name=nm, args=[None if hasattr(a, "ssm_state") else a for a in args],
+                         kwargs={k: v for k, v in kwargs.items() if k != "cache"}, cache=cache is not None,
+                         h_before=h0, conv_weight=np.array(self.conv_weight), conv_bias=np.array(self.conv_bias),
+                         dims=(self.n_heads, self.headdim, self.d_state, self.chunk_size))
+            calls.append(entry)
+            out = fn(self, *args, **kwargs)
+            entry["out"] = out
+            entry["h_after"] = None if cache is None or cache.ssm_state is None else np.array(cache.ssm_state)
+            return out
+        return rec
+
+    for n_, f in saved.items():
+        setattr(mb.MambaBlock, n_, recorder(n_, f))
+    try:
+        # combined mode: chunked prefill of 40 tokens (chunk 16, ragged last
+        # chunk) with a cache, then 3 cached single-token steps
+        H, P, N, G, Q = 4, 16, 8, 2, 16
+        inp = make_inputs(B=2, L=43, H=H, P=P, N=N, G=G, seed=seed)
+        blk = make_block(mb, H, P, N, G, Q, inp)
+        cache = cache_mod.MambaCache()
+        run_block(blk, inp["xBC"][:, :40], inp["dt_raw"][:, :40], cache)
+        for t in range(40, 43):
+            run_block(blk, inp["xBC"][:, t:t + 1], inp["dt_raw"][:, t:t + 1], cache)
+        # split mode: in_proj returns a prepared [x | z], x_proj a fixed linear map
+        d_model, Hs, Ps, Ns = 32, 4, 16, 8
+        rng = np.random.default_rng(seed + 1)
+        sblk = mb.MambaBlock(d_model=d_model, d_state=Ns, d_conv=4, expand=2, headdim=Ps, chunk_size=8)
+        sblk.conv_weight = (rng.standard_normal((2 * d_model, 4)) * 0.5).astype(np.float32)
+        sblk.conv_bias = (rng.standard_normal(2 * d_model) * 0.1).astype(np.float32)
+        sblk.dt_bias = np.log(np.expm1(np.exp(rng.uniform(np.log(1e-3), np.log(0.1), Hs)))).astype(np.float32)
+        sblk.A_log = rng.uniform(0, np.log(16), Hs).astype(np.float32)
+        W = (rng.standard_normal((2 * d_model, Hs * (2 * Ns + 1))) * 0.2).astype(np.float32)
+        sblk.x_proj = lambda v: v @ W
+        sblk.in_proj = _Proj()
+        sblk.out_proj = lambda y: y
+
+        def run_split(L, cache):
+            sblk.in_proj.value = rng.standard_normal((2, L, 4 * d_model)).astype(np.float32)
+            return sblk(np.zeros((2, L, d_model), np.float32), cache=cache)
+
+        run_split(20, None)
+        scache = cache_mod.MambaCache()
+        run_split(20, scache)
+        for _ in range(2):
+            run_split(1, scache)
+    finally:
+        for n_, f in saved.items():
+            setattr(mb.MambaBlock, n_, f)
+
+    # flatten into npz entries: c{i}_name, c{i}_a{k} (array arguments, k-th
+    # positional), c{i}_L / c{i}_cs / c{i}_log_a, c{i}_out{k}, c{i}_h_before / _after
+    out = {"n_calls": np.array(len(calls))}
+    for i, c in enumerate(calls):
+        out[f"c{i}_name"] = np.array(c["name"])
+        out[f"c{i}_dims"] = np.array(c["dims"])
+        out[f"c{i}_conv_weight"] = c["conv_weight"]
+        out[f"c{i}_conv_bias"] = c["conv_bias"]
+        out[f"c{i}_cache"] = np.array(c["cache"])
+        for k, a in enumerate(c["args"]):
+            if isinstance(a, np.ndarray):
+                out[f"c{i}_a{k}"] = a
+            elif isinstance(a, (int, np.integer)):
+                out[f"c{i}_i{k}"] = np.array(int(a))
+        if c["kwargs"].get("log_a") is not None:
+            out[f"c{i}_log_a"] = c["kwargs"]["log_a"]
+        if c["kwargs"].get("log_a_direct") is not None:
+            out[f"c{i}_log_a"] = c["kwargs"]["log_a_direct"]
+        res = c["out"] if isinstance(c["out"], tuple) else (c["out"],)
+        for k, r in enumerate(res):
+            out[f"c{i}_out{k}"] = np.asarray(r, np.float32)
+        if c["h_before"] is not None:
+            out[f"c{i}_h_before"] = c["h_before"].astype(np.float32)
+        if c["h_after"] is not None:
+            out[f"c{i}_h_after"] = c["h_after"].astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), **out)
+    print(f"{name}: {len(calls)} calls: " + ", ".join(sorted({c['name'] for c in calls})))
+
+
 def main():
     root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     mb, cache_mod = load_reference(root)
@@ -236,6 +336,8 @@ def main():
     # chunked prefill, then single-token decode steps through the cache
     case_decode(mb, cache_mod, "decode_steps", B=2, L0=40, steps=8, H=4, P=16, N=8, G=2,
                 Q=16, seed=5)
+    # the hot-path calls of the reference's MambaBlock, for the bridge's GPU test
+    case_bridge_trace(mb, cache_mod, "bridge_trace", seed=6)
 
 
 if __name__ == "__main__":

@@ -7,8 +7,10 @@ vectors are produced by executing the reference's own source files
 files call are provided, with MLX's dtype conventions: Python floats and
 default-constructed arrays are float32 (numpy would use float64).
 
-This module is used only by ``make_golden.py``; nothing at test time or in
-the product imports it.
+This module is test infrastructure: ``make_golden.py`` runs the reference
+under it, and ``tests/test_gpu_bridge.py`` installs it as ``mlx`` so that
+the MLX bridge's wrappers can be driven with the reference's recorded calls
+on a machine without MLX.  Nothing in the product imports it.
 """
 
 from __future__ import annotations
