@@ -14,6 +14,8 @@
 // heads are split over several CTAs so that the state streams from most of
 // the SMs.  The B and C channels are then read by every slice of the group,
 // so the slices leave them unrolled and a second small kernel rolls them.
+#include <cmath>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -246,23 +248,49 @@ int ssd_decode_step(const DecodeArgs& a, cudaStream_t s) {
   // Few (batch row, group) pairs leave most SMs idle: split each group's heads
   // over several CTAs, aiming at two CTAs an SM of a 148-SM part.
   const int64_t pairs = (int64_t)ngroups * a.B;
-  int hsplit = 1;
-  if (pairs < 148) {
-    hsplit = (int)std::min<int64_t>(max_heads, (296 + pairs - 1) / pairs);
-    const int per = (max_heads + hsplit - 1) / hsplit;
-    hsplit = (max_heads + per - 1) / per;
-  }
-  const int slice_heads = (max_heads + hsplit - 1) / hsplit;
-  const size_t smem = sizeof(float) * ((size_t)slice_heads * a.P + 2 * ((a.N + 3) & ~3) + kThreads * 4);
-  if (smem > 200 * 1024)
-    return fail(ALLOY_ERR_UNSUPPORTED, "decode: heads per group * head_dim too large");
-  dim3 grid(ngroups * hsplit, a.B);
-  const int roll_bc = hsplit == 1;
   // vectorised PN rows need 16-byte aligned rows of N floats
   const bool pn_vec = a.state_pn && (a.N % 4 == 0) && (a.st_row % 4 == 0) &&
                       ((reinterpret_cast<uintptr_t>(a.state) & 15) == 0) &&
                       (a.st_sb % 4 == 0) && (a.st_sh % 4 == 0);
   const int nv = pn_vec ? a.N / 4 : 0;
+  auto smem_for = [&](int hs) {
+    const int slice_heads = (max_heads + hs - 1) / hs;
+    return sizeof(float) * ((size_t)slice_heads * a.P + 2 * ((a.N + 3) & ~3) + kThreads * 4);
+  };
+  auto kernel_of = [&](int v) -> void (*)(const DecodeArgs, int, int) {
+    switch (v) {
+      case 4: return decode_step_kernel<4>;
+      case 8: return decode_step_kernel<8>;
+      case 16: return decode_step_kernel<16>;
+      case 32: return decode_step_kernel<32>;
+      default: return decode_step_kernel<0>;
+    }
+  };
+  int hsplit = 1;
+  if (pairs < 148) {
+    hsplit = (int)std::min<int64_t>(max_heads, (296 + pairs - 1) / pairs);
+    const int per = (max_heads + hsplit - 1) / hsplit;
+    hsplit = (max_heads + per - 1) / per;
+  } else if (max_heads >= 2) {
+    // Many pairs: one CTA a pair can leave the last wave mostly empty (the
+    // Nemotron shape at batch 256: 2,048 CTAs at 4 an SM on 148 SMs are 3.46
+    // waves).  Split the heads in two when that packs the waves better.
+    const int sms = sm_count_of_current_device();
+    auto waste = [&](int hs) {   // idle fraction of the last wave
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel_of(nv), kThreads, smem_for(hs)) !=
+              cudaSuccess || per_sm <= 0 || sms <= 0)
+        return 0.0;
+      const double waves = (double)(pairs * hs) / ((double)sms * per_sm);
+      return (std::ceil(waves) - waves) / std::ceil(waves);
+    };
+    if (waste(2) + 0.02 < waste(1)) hsplit = 2;
+  }
+  const size_t smem = smem_for(hsplit);
+  if (smem > 200 * 1024)
+    return fail(ALLOY_ERR_UNSUPPORTED, "decode: heads per group * head_dim too large");
+  dim3 grid(ngroups * hsplit, a.B);
+  const int roll_bc = hsplit == 1;
 #define ALLOY_DEC(NVV)                                                                       \
   do {                                                                                       \
     ALLOY_CUDA(cudaFuncSetAttribute(decode_step_kernel<NVV>,                                 \

@@ -104,6 +104,9 @@ int ssd_decode_step(const DecodeArgs& a, cudaStream_t s);
 int gated_rmsnorm(const alloy_tensor_t* y, const alloy_tensor_t* gate, const alloy_tensor_t* w,
                   alloy_tensor_t* out, float eps, int group, cudaStream_t s);
 
+// SMs of the current device (cached per device; 0 if the query fails).
+int sm_count_of_current_device();
+
 // ssd_tc.cu: tcgen05 tensor-core SSD for bf16 inputs (mode 0 only).
 // Returns ALLOY_ERR_UNSUPPORTED (and launches nothing) for sizes it does not cover.
 bool ssd_tc_supported(const SsdArgs& a);
