@@ -422,48 +422,71 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
 // from zero, becomes the state carried into segment s:
 //   rec[s] = exp(sum of A dt over segment s-1) rec[s-1] + rec[s],  s = 1 .. nseg-1,
 // the chunk recurrence of alloy/models/mamba_block.py:340-357 at segment
-// granularity.  One thread per 4 consecutive (h,p,n) elements of a record;
-// the records of 8 segments are loaded per memory round trip, then folded in
-// order, so the pass takes about nseg / 8 round trips.  The full pass then
-// loads one record per segment.
-__global__ void __launch_bounds__(256) seg_carry_kernel(const TcArgs a, int pairs) {
+// granularity, computed as an fp32 associative scan over the segments with
+// warp shuffles.  Segment s contributes the affine map h -> d_s h + r_s
+// (d_0 = 0, r_0 = the initial state; d_s = exp(log decay of segment s-1),
+// r_s = record s); composing (d2, r2) o (d1, r1) = (d2 d1, d2 r1 + r2) is
+// associative, so a Hillis-Steele scan over S lanes (S the power of two >=
+// the segment count, at most 32) gives every segment's carried state at once.
+// A warp scans G = 32 / S groups of 4 consecutive (h,p,n) elements: lane
+// j G + g holds segment j of group g, so the lanes holding one segment read
+// G consecutive groups (coalesced) and the scan shuffles by multiples of G.
+// More than 32 segments take passes of 32, each chained to the last state of
+// the one before.
+__global__ void __launch_bounds__(256) seg_carry_kernel(const TcArgs a, int pairs, int S) {
   pdl_trigger();
   // the records and log decays of the state-only pass
   pdl_wait();
   const int N = a.N;
-  const int e = (blockIdx.x * 256 + threadIdx.x) * 4;   // (t, n .. n+3) of a [128][N] record
-  if (e >= 128 * N) return;
+  const int quads = 128 * N / 4;
+  const int G = 32 / S, lane = threadIdx.x & 31;
+  const int j = lane / G, sub = (threadIdx.x >> 5) * G + lane % G;
+  const int eq = blockIdx.x * (256 / S) + sub;
+  const bool valid = eq < quads;   // uniform over a sub-warp
+  const int e = (valid ? eq : 0) * 4;
   const int pair = blockIdx.y, b = blockIdx.z;
   const int t = e / N, n = e % N, hr = t >> 6, pr = t & 63;
   const size_t slot = ((size_t)b * pairs + pair) * a.nseg;
-  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (a.ssm_in) {
-    const float* src = a.ssm_in + (int64_t)b * a.si_sb + (int64_t)(a.head_begin + 2 * pair + hr) * a.si_sh +
-                       (int64_t)pr * a.si_sp + (int64_t)n * a.si_sn;
-    v = make_float4(src[0], src[a.si_sn], src[2 * a.si_sn], src[3 * a.si_sn]);
-  }
   float4* rec = reinterpret_cast<float4*>(a.seg_state + slot * 128 * N + e);
   const size_t rstride = (size_t)128 * N / 4;   // float4s between consecutive records
-  rec[0] = v;
+  float4 carry = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-  for (int s0 = 1; s0 < a.nseg; s0 += 8) {
-    float4 r[8];
-    float ld[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      if (s0 + k < a.nseg) {
-        r[k] = rec[(size_t)(s0 + k) * rstride];
-        ld[k] = a.seg_logdecay[(slot + s0 + k - 1) * 2 + hr];
+  for (int p0 = 0; p0 < a.nseg; p0 += S) {
+    const int sg = p0 + j;
+    float d = 1.f;                                   // identity for lanes past the last segment
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (valid && sg < a.nseg) {
+      if (sg == 0) {
+        d = 0.f;
+        if (a.ssm_in) {
+          const float* src = a.ssm_in + (int64_t)b * a.si_sb + (int64_t)(a.head_begin + 2 * pair + hr) * a.si_sh +
+                             (int64_t)pr * a.si_sp + (int64_t)n * a.si_sn;
+          r = make_float4(src[0], src[a.si_sn], src[2 * a.si_sn], src[3 * a.si_sn]);
+        }
+      } else {
+        d = ex2_approx(a.seg_logdecay[(slot + sg - 1) * 2 + hr] * kLog2e);
+        r = rec[(size_t)sg * rstride];
       }
     }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      if (s0 + k < a.nseg) {
-        const float d = ex2_approx(ld[k] * kLog2e);
-        v = make_float4(fmaf(d, v.x, r[k].x), fmaf(d, v.y, r[k].y), fmaf(d, v.z, r[k].z), fmaf(d, v.w, r[k].w));
-        rec[(size_t)(s0 + k) * rstride] = v;
+    if (j == 0 && p0 > 0) {   // chain to the last state of the previous pass
+      r = make_float4(fmaf(d, carry.x, r.x), fmaf(d, carry.y, r.y), fmaf(d, carry.z, r.z), fmaf(d, carry.w, r.w));
+      d = 0.f;
+    }
+#pragma unroll 1
+    for (int o = 1; o < S; o <<= 1) {
+      const int og = o * G;
+      const float dp = __shfl_up_sync(0xffffffffu, d, og);
+      const float rx = __shfl_up_sync(0xffffffffu, r.x, og), ry = __shfl_up_sync(0xffffffffu, r.y, og);
+      const float rz = __shfl_up_sync(0xffffffffu, r.z, og), rw = __shfl_up_sync(0xffffffffu, r.w, og);
+      if (j >= o) {
+        r = make_float4(fmaf(d, rx, r.x), fmaf(d, ry, r.y), fmaf(d, rz, r.z), fmaf(d, rw, r.w));
+        d *= dp;
       }
     }
+    if (valid && sg < a.nseg) rec[(size_t)sg * rstride] = r;
+    const int last = (S - 1) * G + lane % G;   // segment p0 + S - 1 of this group
+    carry = make_float4(__shfl_sync(0xffffffffu, r.x, last), __shfl_sync(0xffffffffu, r.y, last),
+                        __shfl_sync(0xffffffffu, r.z, last), __shfl_sync(0xffffffffu, r.w, last));
   }
 }
 
@@ -1121,7 +1144,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       } else {
       pdl_wait();   // the segment records (segmented calls)
       // initial state -> TMEM: the call's initial state (unsegmented), else
-      // record seg, the state carried into this segment (seg_carry_kernel).
+      // record seg, the state carried into this segment (seg_carry_kernel's
+      // associative scan over the segments).
       // sp: a strided view of ssm_in, or the record (n stride 1), or none
       // (zero).  32 values a batch, every load of a batch issued before the
       // first use (one memory round trip a batch).
@@ -1589,7 +1613,11 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
   // the states carried into the segments, from the state-only pass's records
   auto carry = [&]() -> int {
     const int pairs = s.head_count / 2;
-    seg_carry_kernel<<<dim3((128 * s.N / 4 + 255) / 256, pairs, s.B), 256, 0, stream>>>(a, pairs);
+    int S = 1;
+    while (S < a.nseg && S < 32) S <<= 1;   // lanes a sub-warp: a segment each
+    const int quads = 128 * s.N / 4;
+    const int per_cta = 256 / S;
+    seg_carry_kernel<<<dim3((quads + per_cta - 1) / per_cta, pairs, s.B), 256, 0, stream>>>(a, pairs, S);
     return check_launch("seg_carry_kernel");
   };
   if (s.N == 128) {
