@@ -52,6 +52,7 @@ EXPORTS = (
     "alloy_conv1d_silu_backward",
     "alloy_conv1d_silu_backward_workspace_size",
     "alloy_decode_linear",
+    "alloy_linear",
     "alloy_debug_set_wait_stall",
 )
 
@@ -125,6 +126,8 @@ def load():
         lib.alloy_conv1d_silu_backward_workspace_size.restype = ctypes.c_size_t
         lib.alloy_decode_linear.argtypes = [P, P, P, vp]
         lib.alloy_decode_linear.restype = ctypes.c_int
+        lib.alloy_linear.argtypes = [P, P, P, P, vp]
+        lib.alloy_linear.restype = ctypes.c_int
         lib.alloy_ssd_combined.argtypes = [P] * 12 + [vp, ctypes.c_size_t, D, vp]
         lib.alloy_ssd_combined_workspace_size.argtypes = [ctypes.c_int64, ctypes.c_int64,
                                                           ctypes.c_int32, D]

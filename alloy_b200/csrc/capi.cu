@@ -210,6 +210,34 @@ int alloy_decode_linear(const alloy_tensor_t* x, const alloy_tensor_t* weight, a
   return decode_linear(x, weight, y, as_stream(stream));
 }
 
+int alloy_linear(const alloy_tensor_t* x, const alloy_tensor_t* weight, const alloy_tensor_t* bias,
+                 alloy_tensor_t* y, void* stream) {
+  last_error().clear();
+  ALLOY_TRY(check_tensor(x, "x", 2, nullptr, kBF16));
+  ALLOY_TRY(check_tensor(weight, "weight", 2, nullptr, kBF16));
+  const int64_t M = x->shape[0], K = x->shape[1], N = weight->shape[0];
+  if (weight->shape[1] != K)
+    return fail(ALLOY_ERR_INVALID_ARG, "weight: dim 1 is %lld, expected in = %lld", (long long)weight->shape[1],
+                (long long)K);
+  if (present(bias)) ALLOY_TRY(check_vec(bias, "bias", N, kBF16, false));
+  if (present(bias) && bias->stride[0] != 1) return fail(ALLOY_ERR_INVALID_ARG, "linear: bias must be contiguous");
+  const int64_t ys[2] = {M, N};
+  ALLOY_TRY(check_tensor(y, "y", 2, ys, kBF16));
+  if (x->stride[1] != 1 || weight->stride[1] != 1 || y->stride[1] != 1)
+    return fail(ALLOY_ERR_INVALID_ARG, "linear: the last dimension must be contiguous");
+  if (M >= ((int64_t)1 << 31) || N >= ((int64_t)1 << 31) || K >= ((int64_t)1 << 31))
+    return fail(ALLOY_ERR_UNSUPPORTED, "linear: extents must be below 2^31");
+  if (M == 0 || N == 0) return ALLOY_OK;
+  if (K == 0) return fail(ALLOY_ERR_UNSUPPORTED, "linear: K = 0");
+  if (K % 8 != 0 || N % 8 != 0 || x->stride[0] % 8 != 0 || weight->stride[0] % 8 != 0 || y->stride[0] % 8 != 0 ||
+      !aligned16(x->data) || !aligned16(weight->data) || !aligned16(y->data) ||
+      (present(bias) && (reinterpret_cast<uintptr_t>(bias->data) & 3u) != 0))
+    return fail(ALLOY_ERR_ALIGNMENT,
+                "linear: K, N and the row strides must be multiples of 8 elements and the data 16-byte aligned");
+  ALLOY_TRY(current_device_checked(nullptr));
+  return linear_tc(x, weight, bias, y, as_stream(stream));
+}
+
 int alloy_ssd_combined(const alloy_tensor_t* xBC, const alloy_tensor_t* dt_raw,
                        const alloy_tensor_t* conv_w, const alloy_tensor_t* conv_b,
                        const alloy_tensor_t* dt_bias, const alloy_tensor_t* A_log,
@@ -352,6 +380,10 @@ int alloy_check_device_status(void* stream) {
   ALLOY_TRY(scan_tc_take_error(as_stream(stream), e));
   if (e[0] != 0)
     return fail(ALLOY_ERR_TIMEOUT, "scan_tc_kernel: bounded wait at site %u ran out (block %u, %u)",
+                e[0] - 1, e[1], e[2]);
+  ALLOY_TRY(linear_tc_take_error(as_stream(stream), e));
+  if (e[0] != 0)
+    return fail(ALLOY_ERR_TIMEOUT, "linear_tc_kernel: bounded wait at site %u ran out (block %u, tile %u)",
                 e[0] - 1, e[1], e[2]);
   return ALLOY_OK;
 }

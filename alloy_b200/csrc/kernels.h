@@ -2,6 +2,8 @@
 // validated by capi.cu before any of these is called.
 #pragma once
 
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 
 namespace alloy {
@@ -20,6 +22,18 @@ int conv1d_silu_backward(const alloy_tensor_t* x_padded, const alloy_tensor_t* w
 
 // linear.cu: y [NB, out] = x [NB, in] W^T for NB <= 4 bf16 tokens (decode projections)
 int decode_linear(const alloy_tensor_t* x, const alloy_tensor_t* w, alloy_tensor_t* y, cudaStream_t s);
+
+// linear_tc.cu: y [M, N] = x [M, K] W^T (+ bias) on the tensor cores (prefill
+// projections).  Supported: bf16 throughout, unit inner strides, row strides
+// and K multiples of 8 elements, 16-byte aligned data.
+bool linear_tc_supported(const alloy_tensor_t* x, const alloy_tensor_t* w, const alloy_tensor_t* y);
+int linear_tc(const alloy_tensor_t* x, const alloy_tensor_t* w, const alloy_tensor_t* bias, alloy_tensor_t* y,
+              cudaStream_t s);
+// Synchronises the stream, then reads and clears the error word of the GEMM.
+int linear_tc_take_error(cudaStream_t s, unsigned int out[3]);
+
+// ssd_tc.cu: the driver's cuTensorMapEncodeTiled (null when unavailable)
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encode_fn();
 
 // Flattened view of one SSD call, shared by the SSD kernels.  Strides are in
 // elements.  mode 0: raw xBC (conv + discretisation fused); mode 1:

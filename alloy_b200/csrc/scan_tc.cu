@@ -278,10 +278,12 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
               (ncb < 2 || mbar_test(bar(B_CB_FREE0 + j), ((ncb >> 1) - 1) & 1))) {
             ALLOY_SCAN_TRACE(2, ncb);
             tc_fence_after();
+            // K = d_state in 64-column swizzle blocks of 4 K16 steps (32 bytes apart)
 #pragma unroll
-            for (int k = 0; k < NN / 16; ++k)
-              umma_bf16(tmem + Lo::T_CB + 128 * j, sw128_desc(ct(lb) + (k >> 2) * 16384 + 32 * (k & 3), 16, 1024),
-                        sw128_desc(bt(lb) + (k >> 2) * 16384 + 32 * (k & 3), 16, 1024), ID_CB, k != 0);
+            for (int kb = 0; kb < NN / 64; ++kb)
+              umma_bf16_chain4<2, 2, sw128_hi(1024), sw128_hi(1024)>(
+                  tmem + Lo::T_CB + 128 * j, sw128_lo(ct(lb) + kb * 16384, 16), sw128_lo(bt(lb) + kb * 16384, 16),
+                  ID_CB, kb != 0);
             umma_commit(bar(B_CB_FULL0 + j));
             ++ncb;
             progress = true;
@@ -294,14 +296,11 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
             // state[n, p] += sum_s B[s, n] X'[s, p]; rows n >= NN of A read the zero block
             const uint32_t lbo = NN == 64 ? Lo::OFF_ZERO - (bt(lb) - base) : 16384;
             const uint32_t sxp = base + Lo::OFF_XP + xb * Lo::kXPB;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              umma_bf16(tmem + Lo::T_ST, sw128_desc(bt(lb) + 2048 * k, lbo, 1024), sw128_desc(sxp + 2048 * k, 16384, 1024),
-                        ID_ST, 1);
-              if (SPLIT)
-                umma_bf16(tmem + Lo::T_ST, sw128_desc(bt(lb) + 2048 * k, lbo, 1024),
-                          sw128_desc(sxp + Lo::kX + 2048 * k, 16384, 1024), ID_ST, 1);
-            }
+            umma_bf16_chain8<128, 128, sw128_hi(1024), sw128_hi(1024)>(tmem + Lo::T_ST, sw128_lo(bt(lb), lbo),
+                                                                        sw128_lo(sxp, 16384), ID_ST, 1);
+            if (SPLIT)
+              umma_bf16_chain8<128, 128, sw128_hi(1024), sw128_hi(1024)>(tmem + Lo::T_ST, sw128_lo(bt(lb), lbo),
+                                                                          sw128_lo(sxp + Lo::kX, 16384), ID_ST, 1);
             umma_commit(bar(B_ST_DONE));
             if (ny > c) umma_commit(bar(B_EMPTY0 + lb));
             ++nst;
@@ -318,19 +317,18 @@ __global__ void __launch_bounds__(kThreads, 1) scan_tc_kernel(const SsdArgs a, i
             // Y = S x + C~ H
             const uint32_t ty = tmem + Lo::T_Y + yb * PP, tcb = tmem + Lo::T_CB + 128 * j;
             const uint32_t sh = base + Lo::OFF_H + (c % NH) * Lo::kHB;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              umma_bf16_ta(ty, tcb + 16 * k, sw128_desc(xt(lb) + 2048 * k, 16384, 1024), ID_Y, k != 0);
-              if (SPLIT) umma_bf16_ta(ty, tcb + 16 * k + 8, sw128_desc(xt(lb) + 2048 * k, 16384, 1024), ID_Y, 1);
-            }
+            umma_bf16_ta_chain8<16, 128, sw128_hi(1024)>(ty, tcb, sw128_lo(xt(lb), 16384), ID_Y, 0);
+            if (SPLIT) umma_bf16_ta_chain8<16, 128, sw128_hi(1024)>(ty, tcb + 8, sw128_lo(xt(lb), 16384), ID_Y, 1);
             const uint32_t tct = SPLIT ? tmem + Lo::T_CT + NN * j : tcb + 8;
-#pragma unroll
-            for (int k = 0; k < NN / 16; ++k) {
-              umma_bf16_ta(ty, tct + (SPLIT ? 8 : 16) * k, sw128_desc(sh + 2048 * k, NN * 128, 1024), ID_Y, 1);
+            constexpr int CT_COLS = SPLIT ? 8 : 16;
+            if (NN == 128) {
+              umma_bf16_ta_chain8<CT_COLS, 128, sw128_hi(1024)>(ty, tct, sw128_lo(sh, NN * 128), ID_Y, 1);
+            } else {
+              umma_bf16_ta_chain4<CT_COLS, 128, sw128_hi(1024)>(ty, tct, sw128_lo(sh, NN * 128), ID_Y, 1);
               if (SPLIT) {
                 // C~_lo H_hi + C~_hi H_lo (the lo x lo product is below the fp32 sums' precision)
-                umma_bf16_ta(ty, tct + NN / 2 + 8 * k, sw128_desc(sh + 2048 * k, NN * 128, 1024), ID_Y, 1);
-                umma_bf16_ta(ty, tct + 8 * k, sw128_desc(sh + Lo::kH + 2048 * k, NN * 128, 1024), ID_Y, 1);
+                umma_bf16_ta_chain4<8, 128, sw128_hi(1024)>(ty, tct + NN / 2, sw128_lo(sh, NN * 128), ID_Y, 1);
+                umma_bf16_ta_chain4<8, 128, sw128_hi(1024)>(ty, tct, sw128_lo(sh + Lo::kH, NN * 128), ID_Y, 1);
               }
             }
             umma_commit(bar(B_Y_FULL0 + yb));

@@ -1415,17 +1415,6 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
 // ----------------------------------------------------------------------------
 // host side
 // ----------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
 
 // Launches `kernel` on `stream` with programmatic stream serialization: it may
 // start while the previous kernel on the stream finishes (once every CTA of
@@ -1457,6 +1446,18 @@ int group_range(const SsdArgs& a, int* g0, int* gs) {
 }
 
 }  // namespace
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
 
 bool ssd_tc_supported(const SsdArgs& a) {
   if (a.mode != 0 || !a.xbc_bf16 || !a.y_bf16) return false;
@@ -1549,7 +1550,7 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
   a.stall_cycles = ssd_tc_stall_cycles().load(std::memory_order_relaxed);
 
   // 1. B/C conv pre-pass into the workspace
-  PFN_cuTensorMapEncodeTiled_v12000 encode = get_encode_fn();
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encode_fn();
   if (!encode) return fail(ALLOY_ERR_CUDA, "ssd_tc: cuTensorMapEncodeTiled unavailable");
   const cuuint32_t estride[3] = {1, 1, 1};
   const cuuint64_t xd[3] = {(cuuint64_t)(s.H * 64 + 2 * s.G * s.N), (cuuint64_t)s.L, (cuuint64_t)s.B};

@@ -52,6 +52,29 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+// shared -> global tile store (writes outside the tensor's bounds are dropped),
+// tracked by this thread's bulk async-groups
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// waits until at most N of this thread's bulk groups still read their shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// waits until all of this thread's bulk groups have completed
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // contiguous global -> shared copy (addresses 16-byte aligned, size a multiple of 16)
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile(
@@ -300,6 +323,25 @@ __device__ __forceinline__ void umma_bf16_ta_chain8(uint32_t d_tmem, uint32_t a_
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
       "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+      "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+      "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
+      "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(blo), "r"(idesc), "r"(acc0), "n"(A_COLS), "n"(B_STEP), "r"(B_HI)
+      : "memory");
+}
+// The same with 4 MMAs.
+template <int A_COLS, int B_STEP, uint32_t B_HI>
+__device__ __forceinline__ void umma_bf16_ta_chain4(uint32_t d_tmem, uint32_t a_tmem, uint32_t blo, uint32_t idesc,
+                                                    uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred p, t;\n\t.reg .b32 a, bl;\n\t.reg .b64 b;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\tsetp.eq.u32 t, 0, 0;\n\t"
+      "mov.b64 b, {%2, %7};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], b, %3, p;\n\t"
+      "mov.b32 a, %1;\n\tmov.b32 bl, %2;\n\t"
       "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n\t"
       "add.u32 a, a, %5;\n\tadd.u32 bl, bl, %6;\n\tmov.b64 b, {bl, %7};\n\t"

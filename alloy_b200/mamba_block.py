@@ -183,7 +183,7 @@ class MambaBlock(torch.nn.Module):
         return x_padded
 
     def _forward_split(self, x, Bsz, L, cache):
-        xz = self.in_proj(x)
+        xz = self._project(self.in_proj, x)
         x_branch, z = xz[..., :self.d_inner], xz[..., self.d_inner:]
         x_padded = self._conv_input_padded(x_branch, cache)
         # (:399-404: the differentiable kernel without a cache, the plain one with)
@@ -199,15 +199,20 @@ class MambaBlock(torch.nn.Module):
         y = self._selective_scan(x_conv.reshape(Bsz, L, self.n_heads, self.headdim), A_disc,
                                  B_param, C_param, cache)
         y = y.to(x.dtype).reshape(Bsz, L, self.d_inner) * F.silu(z)
-        return self.out_proj(y)
+        return self._project(self.out_proj, y)
 
     def _project(self, layer, t):
-        """``layer(t)`` for an ``nn.Linear`` without bias; a step of one token per
-        sequence for up to 4 bf16 sequences (decoding) runs the library's GEMV."""
-        if (t.dim() == 3 and t.shape[1] == 1 and t.shape[0] <= 4 and t.dtype == torch.bfloat16
-                and layer.bias is None and t.shape[2] % 8 == 0 and t.is_cuda
-                and not _needs_grad(t, layer.weight)):
-            return mixer.decode_linear(t.reshape(t.shape[0], t.shape[2]), layer.weight).unsqueeze(1)
+        """``layer(t)`` for an ``nn.Linear``.  Without autograd, bf16 on the GPU:
+        a step of one token per sequence for up to 4 sequences (decoding) runs
+        the library's GEMV, anything larger its tensor-core GEMM."""
+        w = layer.weight
+        if (t.is_cuda and t.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+                and t.shape[-1] % 8 == 0 and w.shape[0] % 8 == 0 and w.stride(1) == 1
+                and w.stride(0) % 8 == 0 and not _needs_grad(t, w, layer.bias)):
+            if t.dim() == 3 and t.shape[1] == 1 and t.shape[0] <= 4 and layer.bias is None:
+                return mixer.decode_linear(t.reshape(t.shape[0], t.shape[2]), w).unsqueeze(1)
+            if layer.bias is None or layer.bias.dtype == torch.bfloat16:
+                return mixer.linear(t, w, layer.bias)
         return layer(t)
 
     def _forward_combined(self, x, Bsz, L, cache):

@@ -23,6 +23,7 @@ __all__ = [
     "conv1d_silu", "depthwise_conv1d", "ssd_combined", "selective_scan",
     "ssd_decode_step", "gated_rmsnorm", "ssd_combined_streamed", "conv1d_silu_backward",
     "Conv1dSilu", "selective_scan_backward", "SelectiveScan", "decode_linear", "selective_scan_dot",
+    "linear",
 ]
 
 
@@ -572,6 +573,28 @@ def decode_linear(x, weight, out=None):
     with torch.cuda.device(dev):
         _lib.call("alloy_decode_linear", *(_lib.ref(d) for d in descs), _lib.stream_handle(dev))
     return out
+
+
+def linear(x, weight, bias=None, out=None):
+    """``x @ weight.T (+ bias)`` on the tensor cores: the in_proj / out_proj of
+    a prefill or training step (alloy/models/mamba_block.py:438, :501) over
+    all tokens at once.  ``x [..., in]`` bf16 (leading dims flattened; a
+    layout that does not flatten to one row stride is copied), ``weight
+    [out, in]`` bf16 as an ``nn.Linear`` holds it, ``bias [out]`` bf16 or
+    None; in, out and the row strides multiples of 8.  Returns ``[..., out]``
+    bf16.  No autograd: the backward of a projection stays with torch."""
+    dev = _same_device(("x", x), ("weight", weight), ("bias", bias), ("out", out))
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    n_out = weight.shape[0]
+    if out is None:
+        out = torch.empty((x2.shape[0], n_out), dtype=x.dtype, device=dev)
+    descs = [_lib.desc(t, n) for t, n in ((x2, "x"), (weight, "weight"), (bias, "bias"), (out, "y"))]
+    with torch.cuda.device(dev):
+        _lib.call("alloy_linear", *(_lib.ref(d) for d in descs), _lib.stream_handle(dev))
+    return out.reshape(*lead, n_out)
 
 
 def ssd_decode_step(xBC_tok, dt_tok, conv_weight, conv_bias, dt_bias, A_log, D, conv_state,

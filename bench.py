@@ -2,7 +2,7 @@
 """Mamba-2 SSD prefill benchmark on B200 (tokens/s, fraction of roofline).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
-                    [--workload nemotron|zamba2|long|decode]
+                    [--workload nemotron|zamba2|long|decode|proj|...]
 
 One step is one fused mixer-core prefill (conv1d+SiLU -> discretise ->
 chunked SSD scan -> D skip, plus the conv-cache roll) over one batch of
@@ -68,6 +68,9 @@ WORKLOADS = {
     # the same with bf16 activations: the gradient scans on the tcgen05 scan
     "scan_bwd_bf16": dict(name="zamba2_1.2b_mamba2_selective_scan_backward_bf16", B=8, L=4096, H=64,
                           P=64, N=64, G=1, K=4, Q=256, dtype="bf16"),
+    # the layer's in_proj and out_proj over the prefill's tokens (d_model 4096, d_inner 8192)
+    "proj": dict(name="nemotron_h_8b_mamba2_projections_prefill", B=4, L=8192, H=128, P=64, N=128,
+                 G=8, K=4, Q=256, d_model=4096),
     # one whole Mamba layer (projections, cached step, gate + norm) decoding at batch 1
     "decode_block": dict(name="nemotron_h_8b_mamba2_layer_decode_b1", B=1, L=64, H=128, P=64,
                          N=128, G=8, K=4, Q=256),
@@ -92,6 +95,19 @@ def measured_peaks():
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tensor_peak(sustained):
+    """Dense bf16 TFLOP/s: the measured cuBLAS figure (burst, or sustained for
+    kernels timed inside a long loop), else the fallback."""
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d[key]), f"measured {key}"
+    except Exception:
+        return (1400.0 if sustained else 1590.0), f"fallback {key}"
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -624,6 +640,97 @@ def run_gated_norm(args, w):
             "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
                          "frac": gbs / world / peak, "traffic": None,
                          "peak_source": f"{peak_kind} hbm_gbs"},
+            "gpu_launches": launches, "clocks": clocks.summary(h0, h1)}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_proj(args, w):
+    """The layer's two projections over all tokens of the prefill step:
+    in_proj [B*L, d_model] x [d_model, 2*d_inner + 2*G*N + H] and out_proj
+    [B*L, d_inner] x [d_inner, d_model] (``mixer.linear``, the tcgen05 GEMM);
+    tokens split over the GPUs.  Reported as TFLOP/s of the two products; the
+    same step through torch (cuBLAS) is timed beside it in the same run."""
+    import torch
+    from alloy_b200 import _lib, mixer
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    d_model, d_inner = w["d_model"], w["H"] * w["P"]
+    n_in = 2 * d_inner + 2 * w["G"] * w["N"] + w["H"]
+    rows_total = w["B"] * w["L"]
+    if rows_total % world:
+        raise SystemExit("rows do not split over the GPUs")
+    M = rows_total // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(13 + rank)
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(shape, generator=gen, device=dev) * scale).to(torch.bfloat16)
+
+    x_in, w_in = rnd(M, d_model), rnd(n_in, d_model, scale=d_model ** -0.5)
+    x_out, w_out = rnd(M, d_inner), rnd(d_model, d_inner, scale=d_inner ** -0.5)
+    y_in = torch.empty((M, n_in), dtype=torch.bfloat16, device=dev)
+    y_out = torch.empty((M, d_model), dtype=torch.bfloat16, device=dev)
+    flops = 2.0 * M * (d_model * n_in + d_inner * d_model)
+
+    def ours(i):
+        mixer.linear(x_in, w_in, out=y_in)
+        mixer.linear(x_out, w_out, out=y_out)
+
+    def cublas(i):
+        torch.matmul(x_in, w_in.t(), out=y_in)
+        torch.matmul(x_out, w_out.t(), out=y_out)
+
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(step, clocks=None):
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if clocks:
+            clocks.start()
+        barrier(world)
+        torch.cuda.synchronize()
+        h0 = time.perf_counter()
+        n0 = _lib.load().alloy_kernel_launch_count()
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        n = _lib.load().alloy_kernel_launch_count() - n0
+        torch.cuda.synchronize()
+        h1 = time.perf_counter()
+        barrier(world)
+        if clocks:
+            clocks.stop()
+        return dist_max(ev0.elapsed_time(ev1) / args.steps, world), n, (h0, h1)
+
+    ref_ms, _, _ = timed(cublas)
+    clocks = ClockSampler(dev.index)
+    ms, launches, (h0, h1) = timed(ours, clocks)
+    # parity on a slice of rows against the fp32 product
+    rows = slice(0, 512)
+    ref = x_in[rows].float() @ w_in.float().t()
+    rel = ((y_in[rows].float() - ref).norm() / ref.norm()).item()
+    tflops = flops * world / (ms * 1e-3) / 1e12
+    peak, peak_kind = measured_tensor_peak(sustained=True)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Mamba-2 layer in_proj + out_proj (prefill) TFLOP/s",
+            "value": tflops, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": w["name"], "tokens": rows_total, "d_model": d_model,
+                       "in_features_out": n_in, "d_inner": d_inner,
+                       "l2": "operands 1.3 GB a step, larger than L2"},
+            "cublas_ms_per_step": ref_ms, "speedup_vs_cublas": ref_ms / ms,
+            "rel_l2_vs_fp32": rel,
+            "roofline": {"bound": "tensor", "achieved": tflops / world, "peak": peak,
+                         "unit": "TFLOP/s", "frac": tflops / world / peak, "traffic": None,
+                         "peak_source": peak_kind},
             "gpu_launches": launches, "clocks": clocks.summary(h0, h1)}), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -1188,6 +1295,8 @@ def main():
         run_conv_bwd(args, w)
     elif args.workload == "conv":
         run_conv(args, w)
+    elif args.workload == "proj":
+        run_proj(args, w)
     elif args.workload in ("scan_bwd", "scan_bwd_bf16"):
         run_scan_bwd(args, w)
     else:

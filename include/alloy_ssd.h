@@ -152,6 +152,23 @@ ALLOY_API int alloy_decode_linear(const alloy_tensor_t* x, const alloy_tensor_t*
                                   alloy_tensor_t* y, void* stream);
 
 /*
+ * The projections of a prefill or a training step: y = x W^T (+ bias) on the
+ * tensor cores.  Replaces MambaBlock's in_proj / out_proj
+ * (alloy/models/mamba_block.py:438, :501, nn.Linear) over all B x L tokens
+ * of a call (x flattened to [B*L, in]).
+ *
+ *   x      [M, K]  BF16, last dim contiguous
+ *   weight [N, K]  BF16 (the nn.Linear weight [out, in]), last dim contiguous
+ *   bias   [N]     BF16, contiguous, or data NULL for none
+ *   y      [M, N]  BF16, last dim contiguous; must not overlap x or weight
+ * K and every row stride a multiple of 8 elements, N a multiple of 8, data
+ * 16-byte aligned (ALLOY_ERR_ALIGNMENT otherwise); fp32 accumulation, one
+ * bf16 rounding of the result.
+ */
+ALLOY_API int alloy_linear(const alloy_tensor_t* x, const alloy_tensor_t* weight,
+                           const alloy_tensor_t* bias, alloy_tensor_t* y, void* stream);
+
+/*
  * Fused Mamba-2 mixer core in combined (Zamba2 / Nemotron-H) mode, prefill of
  * L >= 1 tokens: conv1d+SiLU with the conv-cache prefix, split into x|B|C,
  * discretisation, chunked SSD scan with state carry, D skip.

@@ -149,6 +149,33 @@ def test_selective_scan_dot_rejects_bad_arguments(over, needle):
     assert needle in msg, msg
 
 
+def _linear(**over):
+    BF = _lib.BF16
+    t = dict(x=_t([300, 64], BF), w=_t([136, 64], BF), b=_lib.Tensor(), y=_t([300, 136], BF))
+    t.update(over)
+    lib = _lib.load()
+    st = lib.alloy_linear(*(ctypes.byref(t[k]) for k in ("x", "w", "b", "y")), None)
+    return st, _lib.last_error()
+
+
+@pytest.mark.parametrize("over,needle,status", [
+    (dict(x=_t([300, 64])), "x: unsupported dtype", -1),
+    (dict(w=_t([136, 72], _lib.BF16)), "weight: dim 1 is 72", -1),
+    (dict(y=_t([300, 128], _lib.BF16)), "y: dim 1 is 128", -1),
+    (dict(b=_t([128], _lib.BF16)), "bias: dim 0 is 128", -1),
+    (dict(x=_t([300, 64], _lib.BF16, strides=[64, 2])), "last dimension must be contiguous", -1),
+    (dict(x=_t([300, 60], _lib.BF16), w=_t([136, 60], _lib.BF16)), "multiples of 8", -3),
+    (dict(w=_t([132, 64], _lib.BF16), y=_t([300, 132], _lib.BF16)), "multiples of 8", -3),
+    (dict(x=_t([300, 64], _lib.BF16, strides=[68, 1])), "multiples of 8", -3),
+    (dict(x=_t([300, 64], _lib.BF16, ptr=0x1008)), "16-byte aligned", -3),
+    (dict(x=_t([300, 0], _lib.BF16), w=_t([136, 0], _lib.BF16)), "K = 0", -2),
+])
+def test_linear_rejects_bad_arguments(over, needle, status):
+    st, msg = _linear(**over)
+    assert st == status, (st, msg)
+    assert needle in msg, msg
+
+
 def test_error_message_is_per_thread():
     import threading
     _combined(xBC=_lib.Tensor())
