@@ -204,14 +204,16 @@ class MambaBlock(torch.nn.Module):
     def _project(self, layer, t):
         """``layer(t)`` for an ``nn.Linear``.  Without autograd, bf16 on the GPU:
         a step of one token per sequence for up to 4 sequences (decoding) runs
-        the library's GEMV, anything larger its tensor-core GEMM."""
+        the library's GEMV, a product with at least one 256 x 256 output tile
+        per SM its tensor-core GEMM; other sizes stay with torch (cuBLAS)."""
         w = layer.weight
         if (t.is_cuda and t.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
                 and t.shape[-1] % 8 == 0 and w.shape[0] % 8 == 0 and w.stride(1) == 1
                 and w.stride(0) % 8 == 0 and not _needs_grad(t, w, layer.bias)):
             if t.dim() == 3 and t.shape[1] == 1 and t.shape[0] <= 4 and layer.bias is None:
                 return mixer.decode_linear(t.reshape(t.shape[0], t.shape[2]), w).unsqueeze(1)
-            if layer.bias is None or layer.bias.dtype == torch.bfloat16:
+            if ((layer.bias is None or layer.bias.dtype == torch.bfloat16)
+                    and mixer.linear_fills_device(t.numel() // t.shape[-1], w.shape[0], t.device)):
                 return mixer.linear(t, w, layer.bias)
         return layer(t)
 

@@ -23,7 +23,7 @@ __all__ = [
     "conv1d_silu", "depthwise_conv1d", "ssd_combined", "selective_scan",
     "ssd_decode_step", "gated_rmsnorm", "ssd_combined_streamed", "conv1d_silu_backward",
     "Conv1dSilu", "selective_scan_backward", "SelectiveScan", "decode_linear", "selective_scan_dot",
-    "linear",
+    "linear", "linear_fills_device",
 ]
 
 
@@ -573,6 +573,14 @@ def decode_linear(x, weight, out=None):
     with torch.cuda.device(dev):
         _lib.call("alloy_decode_linear", *(_lib.ref(d) for d in descs), _lib.stream_handle(dev))
     return out
+
+
+def linear_fills_device(rows, n_out, device):
+    """Whether ``linear`` over ``rows`` x ``n_out`` outputs has at least one
+    256 x 256 output tile per SM of ``device`` (the GEMM's persistent grid is
+    one CTA per SM; with fewer tiles the weights stream through too few SMs)."""
+    tiles = -(-rows // 256) * -(-n_out // 256)
+    return tiles >= torch.cuda.get_device_properties(device).multi_processor_count
 
 
 def linear(x, weight, bias=None, out=None):

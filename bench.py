@@ -708,9 +708,16 @@ def run_proj(args, w):
             clocks.stop()
         return dist_max(ev0.elapsed_time(ev1) / args.steps, world), n, (h0, h1)
 
-    ref_ms, _, _ = timed(cublas)
+    # the reported number first; then cuBLAS and the library again in both
+    # orders, so that neither side gets the cooler GPU (a 1 kW part runs these
+    # products at its power cap)
     clocks = ClockSampler(dev.index)
     ms, launches, (h0, h1) = timed(ours, clocks)
+    ref_a, _, _ = timed(cublas)
+    ref_b, _, _ = timed(cublas)
+    ms_b, _, _ = timed(ours)
+    ref_ms = (ref_a + ref_b) / 2
+    ours_pair_ms = (ms + ms_b) / 2
     # parity on a slice of rows against the fp32 product
     rows = slice(0, 512)
     ref = x_in[rows].float() @ w_in.float().t()
@@ -726,7 +733,9 @@ def run_proj(args, w):
             "config": {"workload": w["name"], "tokens": rows_total, "d_model": d_model,
                        "in_features_out": n_in, "d_inner": d_inner,
                        "l2": "operands 1.3 GB a step, larger than L2"},
-            "cublas_ms_per_step": ref_ms, "speedup_vs_cublas": ref_ms / ms,
+            "cublas_ms_per_step": ref_ms, "ours_ms_per_step_interleaved": ours_pair_ms,
+            "speedup_vs_cublas": ref_ms / ours_pair_ms,
+            "comparison": "library, cuBLAS, cuBLAS, library: K steps each, means of the two of each",
             "rel_l2_vs_fp32": rel,
             "roofline": {"bound": "tensor", "achieved": tflops / world, "peak": peak,
                          "unit": "TFLOP/s", "frac": tflops / world / peak, "traffic": None,

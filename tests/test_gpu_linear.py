@@ -87,14 +87,16 @@ def test_block_projections_use_the_gemm_and_match_torch(combined):
                      combined_proj=combined, n_groups=1, use_D=combined,
                      use_inner_norm=combined).to(DEV, torch.bfloat16)
     calls = []
-    orig = mixer.linear
+    orig, orig_fills = mixer.linear, mixer.linear_fills_device
     mixer.linear = lambda *a, **k: (calls.append(1), orig(*a, **k))[1]
+    # a toy layer has fewer output tiles than SMs: route it through the GEMM anyway
+    mixer.linear_fills_device = lambda *a: True
     x = _rand(2, 300, 256, seed=8)
     with torch.no_grad():
         try:
             y = blk(x)
         finally:
-            mixer.linear = orig
+            mixer.linear, mixer.linear_fills_device = orig, orig_fills
         assert len(calls) == 2, calls
         proj = blk._project
         blk._project = lambda layer, t: layer(t)
@@ -105,3 +107,14 @@ def test_block_projections_use_the_gemm_and_match_torch(combined):
     err = ((y.float() - y_ref.float()).norm() / y_ref.float().norm()).item()
     print("block rel-L2 vs torch projections", err)
     assert err <= 1e-2, err
+
+
+def test_small_products_stay_with_torch():
+    """Products with fewer 256 x 256 output tiles than SMs (a short prefill)
+    are left to torch; the Nemotron layer's projections over 4 x 8192 tokens
+    fill the GPU."""
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    assert not mixer.linear_fills_device(64, 18560, torch.device(DEV))
+    assert not mixer.linear_fills_device(2048, 4096, torch.device(DEV))
+    assert mixer.linear_fills_device(32768, 4096, torch.device(DEV))
+    assert mixer.linear_fills_device(256 * sms, 256, torch.device(DEV))
