@@ -168,6 +168,13 @@ struct TcArgs {
   // segment s (record 0 the call's initial state)
   float* seg_state;
   float* seg_logdecay;       // [B][head pairs][nseg][2]: sum of A dt over segment s, per head
+  // split walk (split_units > 0): the nseg segments of every (batch row, head
+  // pair) unit are walked one after another by successive launches, each CTA
+  // of a launch one (unit, segment) task: task split_base + blockIdx.x is
+  // segment tau / split_units of unit tau % split_units (unit = b * pairs +
+  // pair).  Segment s > 0 starts from the end state of segment s - 1, handed
+  // over exactly (fp32) in the unit's record [128 (h,p)][N] of seg_state.
+  int split_units, split_base, pairs;
   // > 0 only in a test of the bounded-wait error path: the consumer warps
   // first wait this many cycles on B_NEVER, which nothing completes
   long long stall_cycles;
@@ -532,15 +539,20 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
   auto bar = [&](int i) { return base + OFF_BAR + 8u * i; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.y;
-  const int h0 = a.head_begin + 2 * blockIdx.x;   // first head of the pair
+  // this CTA's (batch row, head pair, segment)
+  const bool split = a.split_units > 0;
+  const int task = a.split_base + (int)blockIdx.x;
+  const int seg = split ? task / a.split_units : (int)blockIdx.z;
+  const int unit = split ? task - seg * a.split_units : 0;
+  const int b = split ? unit / a.pairs : (int)blockIdx.y;
+  const int pair = split ? unit - b * a.pairs : (int)blockIdx.x;
+  const int h0 = a.head_begin + 2 * pair;   // first head of the pair
   const int hpg = a.H / a.G;
   const int gl = h0 / hpg - a.group_begin;        // group index inside the workspace
   const int L = a.L;
   const int nchunks = (L + Q - 1) / Q;
   // this CTA's segment: chunks [c_lo, c_lo + nk); the loops below count c from 0
   // (32-bit unsigned: nseg <= the SM count and nchunks < 2^24 keep the products in range)
-  const int seg = blockIdx.z;
   const int c_lo = (int)((unsigned)seg * (unsigned)nchunks / (unsigned)a.nseg);
   const int nk = (int)((unsigned)(seg + 1) * (unsigned)nchunks / (unsigned)a.nseg) - c_lo;
   // the chunk of walk step c: the full pass walks its segment forward, the
@@ -1059,8 +1071,9 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       const int hr = t >> 6, pr = t & 63;
 
       // segment records of this (batch row, head pair): record 0 the call's
-      // initial state, record j + 1 the end state of segment j from zero
-      const size_t seg_slot = ((size_t)b * gridDim.x + blockIdx.x) * a.nseg;
+      // initial state, record j + 1 the end state of segment j from zero (a
+      // split walk: one record, the state handed from segment to segment)
+      const size_t seg_slot = split ? (size_t)unit : ((size_t)b * a.pairs + pair) * a.nseg;
       auto record = [&](int j, int n8) {
         return reinterpret_cast<float4*>(a.seg_state + ((seg_slot + j) * 128 + t) * N + cw * NHALF + n8 * 8);
       };
@@ -1151,8 +1164,8 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       // first use (one memory round trip a batch).
       const float* sp = nullptr;
       int64_t sn = 1;
-      if (a.nseg > 1) {
-        sp = reinterpret_cast<const float*>(record(seg, 0));
+      if (split ? seg > 0 : a.nseg > 1) {
+        sp = reinterpret_cast<const float*>(record(split ? 0 : seg, 0));
       } else if (a.ssm_in) {
         sp = a.ssm_in + (int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh + (int64_t)pr * a.si_sp +
              (int64_t)(cw * NHALF) * a.si_sn;
@@ -1399,6 +1412,20 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
                       (int64_t)pr * a.so_sp] = __uint_as_float(r[i]);
         }
       }
+      // ---- a split walk: this segment's end state -> the unit's record ----
+      if (!*abort_flag && split && seg < a.nseg - 1 && waitw(bar(B_YI_DONE), (nk - 1) & 1, abort_flag, 37)) {
+        tc_fence_after();
+#pragma unroll 1
+        for (int n8 = 0; n8 < NHALF / 8; ++n8) {
+          uint32_t r[8];
+          tmem_ld8(lane_base + T_ST + cw * NHALF + n8 * 8, r);
+          tmem_ld_wait();
+          record(0, n8)[0] = make_float4(__uint_as_float(r[0]), __uint_as_float(r[1]), __uint_as_float(r[2]),
+                                         __uint_as_float(r[3]));
+          record(0, n8)[1] = make_float4(__uint_as_float(r[4]), __uint_as_float(r[5]), __uint_as_float(r[6]),
+                                         __uint_as_float(r[7]));
+        }
+      }
       }   // full pass
     }
     tc_fence_before();
@@ -1495,8 +1522,43 @@ int sm_count_of_current_device() {
 
 struct TcLayout {
   int nseg;
+  bool split;                                     // segments walked in order (split walk)
   size_t tiles, seg_state, seg_logdecay, total;   // byte offsets / sizes in the workspace
 };
+
+// The split walk: with at least as many (batch row, head pair) units as SMs,
+// one CTA per unit runs in ceil(units / SMs) waves of the whole sequence (256
+// units on 148 SMs: 2 waves where 1.73 would do).  Cutting every unit into k
+// segments walked one after another, the k * units (unit, segment) tasks run
+// as ceil(k * units / SMs) launches ("slots") of at most one CTA per SM,
+// segment s + 1 of a unit in a later slot than segment s (task s * units + u
+// sits in slot (s * units + u) / SMs, and units >= SMs), each starting from
+// the exact state its predecessor handed over.  Estimated cost in chunk walks
+// (fitted to the Nemotron and Zamba2 layer shapes at 256 units: one wave of
+// 64 / 32 chunks costs ~1.5 chunks more, a slot of 16 / 8 chunks ~4.4 / 2.6
+// more, as a slot ends with its slowest CTA and the next starts cold):
+// waves * (chunks + 1.5) unsplit, slots * (1.1 * chunks per segment + 2.3)
+// split; k is taken when it beats the others by 3 %.
+constexpr double kWaveOverheadChunks = 1.5, kSlotOverheadChunks = 2.3, kSlotSpread = 1.1;
+
+int split_segments(int units, int nchunks, int sms) {
+  if (units < sms || sms <= 0) return 1;
+  auto cost = [&](int k) {
+    const double slots = (double)(((int64_t)k * units + sms - 1) / sms);
+    return k == 1 ? slots * (nchunks + kWaveOverheadChunks)
+                  : slots * (kSlotSpread * nchunks / k + kSlotOverheadChunks);
+  };
+  int best = 1;
+  double best_cost = cost(1);
+  for (int k = 2; k <= 8 && nchunks / k >= kMinSegChunks; ++k) {
+    const double c = cost(k);
+    if (c < 0.97 * best_cost) {
+      best = k;
+      best_cost = c;
+    }
+  }
+  return best;
+}
 
 TcLayout tc_layout(const SsdArgs& a) {
   int g0, gs;
@@ -1506,13 +1568,20 @@ TcLayout tc_layout(const SsdArgs& a) {
   const int units = a.B * (a.head_count / 2);
   const int sms = sm_count_of_current_device();
   l.nseg = 1;
-  if (units > 0 && sms > units) l.nseg = std::max(1, std::min(sms / units, nchunks / kMinSegChunks));
+  l.split = false;
+  if (units > 0 && sms > units) {
+    l.nseg = std::max(1, std::min(sms / units, nchunks / kMinSegChunks));
+  } else if (units > 0) {
+    l.nseg = split_segments(units, nchunks, sms);
+    l.split = l.nseg > 1;
+  }
   // B/C tiles of every chunk, the last one padded to Q rows
   l.tiles = (size_t)a.B * nchunks * Q * 2 * gs * a.N * sizeof(__nv_bfloat16);
-  const size_t nslots = (size_t)units * l.nseg;
+  // segment records: nseg a unit (segmented), one a unit (split walk)
+  const size_t nslots = (size_t)units * (l.split ? 1 : l.nseg);
   l.seg_state = (l.tiles + 255) & ~size_t(255);
   l.seg_logdecay = l.seg_state + nslots * 128 * a.N * sizeof(float);
-  l.total = l.nseg > 1 ? l.seg_logdecay + nslots * 2 * sizeof(float) : l.tiles;
+  l.total = l.split ? l.seg_logdecay : l.nseg > 1 ? l.seg_logdecay + nslots * 2 * sizeof(float) : l.tiles;
   return l;
 }
 
@@ -1591,6 +1660,7 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
   a.nseg = workspace_bytes >= lay.total ? lay.nseg : 1;
   a.seg_state = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + lay.seg_state);
   a.seg_logdecay = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + lay.seg_logdecay);
+  a.pairs = s.head_count / 2;
   // 4. the SSD kernel: the state-only pass over all segments but the last,
   // then the full pass over all
   // An unsegmented call's SSD kernel is launched with programmatic stream
@@ -1621,6 +1691,26 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
     seg_carry_kernel<<<dim3((quads + per_cta - 1) / per_cta, pairs, s.B), 256, 0, stream>>>(a, pairs, S);
     return check_launch("seg_carry_kernel");
   };
+  // the split walk: slots of at most one CTA per SM, the first after the pre-pass
+  auto split_walk = [&](auto kernel) -> int {
+    ALLOY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    a.split_units = s.B * a.pairs;
+    const int tasks = a.split_units * a.nseg;
+    const int slot = std::max(1, sm_count_of_current_device());
+    for (int first = 0; first < tasks; first += slot) {
+      a.split_base = first;
+      const dim3 grid(std::min(slot, tasks - first));
+      if (first == 0) {
+        ALLOY_TRY(launch_after_previous(kernel, grid, dim3(kThreads), kSmemBytes, stream, a));
+      } else {
+        kernel<<<grid, kThreads, kSmemBytes, stream>>>(a);
+      }
+      ALLOY_TRY(check_launch("ssd_tc_kernel"));
+    }
+    return ALLOY_OK;
+  };
+  if (lay.split && a.nseg > 1)
+    return s.N == 128 ? split_walk(ssd_tc_kernel<128, false>) : split_walk(ssd_tc_kernel<64, false>);
   if (s.N == 128) {
     if (a.nseg > 1) {
       ALLOY_TRY(launch(ssd_tc_kernel<128, true>, a.nseg - 1, false));

@@ -313,8 +313,10 @@ ALLOY_API int alloy_gated_rmsnorm(const alloy_tensor_t* y, const alloy_tensor_t*
  * and device), for counting the launches of a timed region: a segmented
  * prefill (alloy_ssd_combined with fewer (batch row, head pair) units than
  * SMs) launches two more than an unsegmented one (the state-only pass and
- * the segment carry).  No counterpart in the
- * reference.
+ * the segment carry); a split walk (at least as many units as SMs, each
+ * unit's sequence walked in segments by successive launches of at most one
+ * CTA per SM, when the workspace holds the units' handover states) launches
+ * one SSD kernel per slot instead of one.  No counterpart in the reference.
  */
 ALLOY_API uint64_t alloy_kernel_launch_count(void);
 

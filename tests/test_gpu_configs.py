@@ -182,3 +182,32 @@ def test_nemotron_decode_64_steps_batch_256():
     check("decode state after 64 steps (rows 0 and 255)", np32(ssm[rows]), h64)
     # the conv cache after 64 steps holds the last K-1 inputs, bit-exact
     np.testing.assert_array_equal(np32(conv[rows]), cs64.astype(np.float32))
+
+
+def test_split_walk_between_one_and_two_waves():
+    """Batch 3 of the Nemotron-H layer shape (L 2048): 192 (batch row, head
+    pair) units, between one and two per SM, which the library walks split
+    (each unit's chunks in segments run by successive launches of one CTA per
+    SM, the state handed over exactly).  Checked against the oracle on slices
+    whose units sit in different segments' launches, and against the same call
+    with the smallest workspace (one CTA per unit, no split)."""
+    from alloy_b200 import _lib
+    cfg = dict(B=3, L=2048, H=128, P=64, N=128, G=8)
+    t = gen_layer(**cfg, seed=104)
+    lib = _lib.load()
+    n0 = lib.alloy_kernel_launch_count()
+    y, h, _ = run_layer(t, 128, 64, 128, 8, 256)
+    split_launches = lib.alloy_kernel_launch_count() - n0
+    n0 = lib.alloy_kernel_launch_count()
+    y1, h1, _ = run_layer(t, 128, 64, 128, 8, 256, workspace="min")
+    plain_launches = lib.alloy_kernel_launch_count() - n0
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    print(f"split walk: {split_launches} launches, one CTA per unit: {plain_launches}")
+    if 3 * 64 >= sms:
+        assert split_launches > plain_launches
+    # the split walk hands the fp32 state over exactly: the same chunks in the same order
+    ry = ((y.float() - y1.float()).norm() / y1.float().norm()).item()
+    rh = ((h - h1).norm() / h1.norm()).item()
+    print(f"split walk vs one CTA per unit: y rel-L2 {ry:.3e}, state rel-L2 {rh:.3e}")
+    assert ry == 0.0 and rh == 0.0
+    check_slices("split walk", t, y, h, cfg, [(0, 0, 2), (2, 126, 2), (1, 64, 4)])
