@@ -175,6 +175,12 @@ struct TcArgs {
   // pair).  Segment s > 0 starts from the end state of segment s - 1, handed
   // over exactly (fp32) in the unit's record [128 (h,p)][N] of seg_state.
   int split_units, split_base, pairs;
+  // state-only pieces: each of segments 0..nseg-2 is walked by `pieces` CTAs of
+  // the state-only pass (piece p: part p % pieces of segment p / pieces), so
+  // that pass fills more SMs; a unit then has nrec = (nseg - 1) pieces + 1
+  // records, the carry scans over pieces and the full pass's segment s starts
+  // from record s * pieces
+  int pieces, nrec;
   // > 0 only in a test of the bounded-wait error path: the consumer warps
   // first wait this many cycles on B_NEVER, which nothing completes
   long long stall_cycles;
@@ -453,16 +459,16 @@ __global__ void __launch_bounds__(256) seg_carry_kernel(const TcArgs a, int pair
   const int e = (valid ? eq : 0) * 4;
   const int pair = blockIdx.y, b = blockIdx.z;
   const int t = e / N, n = e % N, hr = t >> 6, pr = t & 63;
-  const size_t slot = ((size_t)b * pairs + pair) * a.nseg;
+  const size_t slot = ((size_t)b * pairs + pair) * a.nrec;
   float4* rec = reinterpret_cast<float4*>(a.seg_state + slot * 128 * N + e);
   const size_t rstride = (size_t)128 * N / 4;   // float4s between consecutive records
   float4 carry = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-  for (int p0 = 0; p0 < a.nseg; p0 += S) {
+  for (int p0 = 0; p0 < a.nrec; p0 += S) {
     const int sg = p0 + j;
     float d = 1.f;                                   // identity for lanes past the last segment
     float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (valid && sg < a.nseg) {
+    if (valid && sg < a.nrec) {
       if (sg == 0) {
         d = 0.f;
         if (a.ssm_in) {
@@ -490,7 +496,7 @@ __global__ void __launch_bounds__(256) seg_carry_kernel(const TcArgs a, int pair
         d *= dp;
       }
     }
-    if (valid && sg < a.nseg) rec[(size_t)sg * rstride] = r;
+    if (valid && sg < a.nrec) rec[(size_t)sg * rstride] = r;
     const int last = (S - 1) * G + lane % G;   // segment p0 + S - 1 of this group
     carry = make_float4(__shfl_sync(0xffffffffu, r.x, last), __shfl_sync(0xffffffffu, r.y, last),
                         __shfl_sync(0xffffffffu, r.z, last), __shfl_sync(0xffffffffu, r.w, last));
@@ -553,8 +559,13 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
   const int nchunks = (L + Q - 1) / Q;
   // this CTA's segment: chunks [c_lo, c_lo + nk); the loops below count c from 0
   // (32-bit unsigned: nseg <= the SM count and nchunks < 2^24 keep the products in range)
-  const int c_lo = (int)((unsigned)seg * (unsigned)nchunks / (unsigned)a.nseg);
-  const int nk = (int)((unsigned)(seg + 1) * (unsigned)nchunks / (unsigned)a.nseg) - c_lo;
+  // (the state-only pass: seg is a piece, part seg % pieces of segment seg / pieces)
+  const int sg_of = kStateOnly ? seg / a.pieces : seg, part = kStateOnly ? seg - sg_of * a.pieces : 0;
+  const int parts = kStateOnly ? a.pieces : 1;
+  const int s_lo = (int)((unsigned)sg_of * (unsigned)nchunks / (unsigned)a.nseg);
+  const int s_len = (int)((unsigned)(sg_of + 1) * (unsigned)nchunks / (unsigned)a.nseg) - s_lo;
+  const int c_lo = s_lo + part * s_len / parts;
+  const int nk = s_lo + (part + 1) * s_len / parts - c_lo;
   // the chunk of walk step c: the full pass walks its segment forward, the
   // state-only pass backward, so that each chunk's contribution to the
   // segment's end state carries its decay to that end (the sum of A dt over
@@ -1073,7 +1084,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       // segment records of this (batch row, head pair): record 0 the call's
       // initial state, record j + 1 the end state of segment j from zero (a
       // split walk: one record, the state handed from segment to segment)
-      const size_t seg_slot = split ? (size_t)unit : ((size_t)b * a.pairs + pair) * a.nseg;
+      const size_t seg_slot = split ? (size_t)unit : ((size_t)b * a.pairs + pair) * a.nrec;
       auto record = [&](int j, int n8) {
         return reinterpret_cast<float4*>(a.seg_state + ((seg_slot + j) * 128 + t) * N + cw * NHALF + n8 * 8);
       };
@@ -1165,7 +1176,7 @@ __global__ void __launch_bounds__(kThreads, 1) ssd_tc_kernel(const TcArgs a) {
       const float* sp = nullptr;
       int64_t sn = 1;
       if (split ? seg > 0 : a.nseg > 1) {
-        sp = reinterpret_cast<const float*>(record(split ? 0 : seg, 0));
+        sp = reinterpret_cast<const float*>(record(split ? 0 : seg * a.pieces, 0));
       } else if (a.ssm_in) {
         sp = a.ssm_in + (int64_t)b * a.si_sb + (int64_t)(h0 + hr) * a.si_sh + (int64_t)pr * a.si_sp +
              (int64_t)(cw * NHALF) * a.si_sn;
@@ -1522,6 +1533,7 @@ int sm_count_of_current_device() {
 
 struct TcLayout {
   int nseg;
+  int pieces, nrec;                               // state-only pieces a segment, records a unit
   bool split;                                     // segments walked in order (split walk)
   size_t tiles, seg_state, seg_logdecay, total;   // byte offsets / sizes in the workspace
 };
@@ -1568,9 +1580,14 @@ TcLayout tc_layout(const SsdArgs& a) {
   const int units = a.B * (a.head_count / 2);
   const int sms = sm_count_of_current_device();
   l.nseg = 1;
+  l.pieces = 1;
   l.split = false;
   if (units > 0 && sms > units) {
     l.nseg = std::max(1, std::min(sms / units, nchunks / kMinSegChunks));
+    // the state-only pass over segments 0..nseg-2 in as many pieces a segment
+    // as the SMs take (pieces of at least kMinSegChunks chunks)
+    if (l.nseg > 1)
+      l.pieces = std::max(1, std::min(sms / ((l.nseg - 1) * units), nchunks / l.nseg / kMinSegChunks));
   } else if (units > 0) {
     l.nseg = split_segments(units, nchunks, sms);
     l.split = l.nseg > 1;
@@ -1578,7 +1595,8 @@ TcLayout tc_layout(const SsdArgs& a) {
   // B/C tiles of every chunk, the last one padded to Q rows
   l.tiles = (size_t)a.B * nchunks * Q * 2 * gs * a.N * sizeof(__nv_bfloat16);
   // segment records: nseg a unit (segmented), one a unit (split walk)
-  const size_t nslots = (size_t)units * (l.split ? 1 : l.nseg);
+  l.nrec = l.split ? 1 : l.nseg > 1 ? (l.nseg - 1) * l.pieces + 1 : 1;
+  const size_t nslots = (size_t)units * l.nrec;
   l.seg_state = (l.tiles + 255) & ~size_t(255);
   l.seg_logdecay = l.seg_state + nslots * 128 * a.N * sizeof(float);
   l.total = l.split ? l.seg_logdecay : l.nseg > 1 ? l.seg_logdecay + nslots * 2 * sizeof(float) : l.tiles;
@@ -1658,6 +1676,8 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
   // segments: only with the workspace for their states (a workspace of the
   // B/C tiles alone runs one CTA per head pair)
   a.nseg = workspace_bytes >= lay.total ? lay.nseg : 1;
+  a.pieces = a.nseg > 1 ? lay.pieces : 1;
+  a.nrec = a.nseg > 1 ? lay.nrec : 1;
   a.seg_state = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + lay.seg_state);
   a.seg_logdecay = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + lay.seg_logdecay);
   a.pairs = s.head_count / 2;
@@ -1685,7 +1705,7 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
   auto carry = [&]() -> int {
     const int pairs = s.head_count / 2;
     int S = 1;
-    while (S < a.nseg && S < 32) S <<= 1;   // lanes a sub-warp: a segment each
+    while (S < a.nrec && S < 32) S <<= 1;   // lanes a sub-warp: a piece each
     const int quads = 128 * s.N / 4;
     const int per_cta = 256 / S;
     seg_carry_kernel<<<dim3((quads + per_cta - 1) / per_cta, pairs, s.B), 256, 0, stream>>>(a, pairs, S);
@@ -1713,13 +1733,13 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
     return s.N == 128 ? split_walk(ssd_tc_kernel<128, false>) : split_walk(ssd_tc_kernel<64, false>);
   if (s.N == 128) {
     if (a.nseg > 1) {
-      ALLOY_TRY(launch(ssd_tc_kernel<128, true>, a.nseg - 1, false));
+      ALLOY_TRY(launch(ssd_tc_kernel<128, true>, (a.nseg - 1) * a.pieces, false));
       ALLOY_TRY(carry());
     }
     return launch(ssd_tc_kernel<128, false>, a.nseg, a.nseg == 1);
   }
   if (a.nseg > 1) {
-    ALLOY_TRY(launch(ssd_tc_kernel<64, true>, a.nseg - 1, false));
+    ALLOY_TRY(launch(ssd_tc_kernel<64, true>, (a.nseg - 1) * a.pieces, false));
     ALLOY_TRY(carry());
   }
   return launch(ssd_tc_kernel<64, false>, a.nseg, a.nseg == 1);
