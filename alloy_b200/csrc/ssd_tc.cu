@@ -1686,9 +1686,10 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
   // An unsegmented call's SSD kernel is launched with programmatic stream
   // serialization after the pre-pass: its prologue (TMEM, barriers, weights,
   // the first chunk's x rows and dt) overlaps the pre-pass's tail (measured:
-  // -0.8 % at the Nemotron layer, -1.3 % at the Zamba2 layer).  The segmented
-  // chain (state-only pass, carry, full pass) uses ordinary launches: there
-  // the early start measured slower (+6 % for the 131k-token sequence).  The
+  // -0.8 % at the Nemotron layer, -1.3 % at the Zamba2 layer).  In the
+  // segmented chain (state-only pass, carry, full pass) the carry and the
+  // full pass use ordinary launches: there the early start measured slower
+  // (+6 % for the 131k-token sequence).  The
   // pre-pass itself is always an ordinary launch, so a call never overlaps
   // the previous one, which used the same workspace.
   auto launch = [&](auto kernel, int nz, bool after_prepass) -> int {
@@ -1701,6 +1702,11 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
     }
     return check_launch("ssd_tc_kernel");
   };
+  // The state-only pass of short segments (at most 64 chunks: the 4- and 8-GPU
+  // shards) is launched programmatically after the pre-pass too, its prologue
+  // overlapping the pre-pass's tail (-1.1 % at both shards); with long
+  // segments (one 131k-token sequence: 256 chunks) that measured +0.5 %.
+  const bool pdl_state_only = (s.L + Q - 1) / Q <= 64 * a.nseg;
   // the states carried into the segments, from the state-only pass's records
   auto carry = [&]() -> int {
     const int pairs = s.head_count / 2;
@@ -1733,13 +1739,13 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
     return s.N == 128 ? split_walk(ssd_tc_kernel<128, false>) : split_walk(ssd_tc_kernel<64, false>);
   if (s.N == 128) {
     if (a.nseg > 1) {
-      ALLOY_TRY(launch(ssd_tc_kernel<128, true>, (a.nseg - 1) * a.pieces, false));
+      ALLOY_TRY(launch(ssd_tc_kernel<128, true>, (a.nseg - 1) * a.pieces, pdl_state_only));
       ALLOY_TRY(carry());
     }
     return launch(ssd_tc_kernel<128, false>, a.nseg, a.nseg == 1);
   }
   if (a.nseg > 1) {
-    ALLOY_TRY(launch(ssd_tc_kernel<64, true>, (a.nseg - 1) * a.pieces, false));
+    ALLOY_TRY(launch(ssd_tc_kernel<64, true>, (a.nseg - 1) * a.pieces, pdl_state_only));
     ALLOY_TRY(carry());
   }
   return launch(ssd_tc_kernel<64, false>, a.nseg, a.nseg == 1);
