@@ -446,6 +446,7 @@ bc_conv_kernel(const __grid_constant__ CUtensorMap src_map, const TcArgs a, __nv
 // G consecutive groups (coalesced) and the scan shuffles by multiples of G.
 // More than 32 segments take passes of 32, each chained to the last state of
 // the one before.
+constexpr int kCarryQuads = 4;   // groups of 4 state elements a carry thread
 __global__ void __launch_bounds__(256) seg_carry_kernel(const TcArgs a, int pairs, int S) {
   pdl_trigger();
   // the records and log decays of the state-only pass
@@ -454,52 +455,71 @@ __global__ void __launch_bounds__(256) seg_carry_kernel(const TcArgs a, int pair
   const int quads = 128 * N / 4;
   const int G = 32 / S, lane = threadIdx.x & 31;
   const int j = lane / G, sub = (threadIdx.x >> 5) * G + lane % G;
-  const int eq = blockIdx.x * (256 / S) + sub;
-  const bool valid = eq < quads;   // uniform over a sub-warp
-  const int e = (valid ? eq : 0) * 4;
   const int pair = blockIdx.y, b = blockIdx.z;
-  const int t = e / N, n = e % N, hr = t >> 6, pr = t & 63;
   const size_t slot = ((size_t)b * pairs + pair) * a.nrec;
-  float4* rec = reinterpret_cast<float4*>(a.seg_state + slot * 128 * N + e);
   const size_t rstride = (size_t)128 * N / 4;   // float4s between consecutive records
-  float4 carry = make_float4(0.f, 0.f, 0.f, 0.f);
+  // kCarryQuads groups of quads a thread, every load of a pass issued before
+  // the scans (the kernel is bound by memory latency, not bandwidth)
+  int e[kCarryQuads];
+  bool valid[kCarryQuads];
+#pragma unroll
+  for (int u = 0; u < kCarryQuads; ++u) {
+    const int eq = (blockIdx.x * kCarryQuads + u) * (256 / S) + sub;
+    valid[u] = eq < quads;   // uniform over a sub-warp
+    e[u] = (valid[u] ? eq : 0) * 4;
+  }
+  float4* rec = reinterpret_cast<float4*>(a.seg_state + slot * 128 * N);
+  float4 carry[kCarryQuads];
+#pragma unroll
+  for (int u = 0; u < kCarryQuads; ++u) carry[u] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
   for (int p0 = 0; p0 < a.nrec; p0 += S) {
     const int sg = p0 + j;
-    float d = 1.f;                                   // identity for lanes past the last segment
-    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (valid && sg < a.nrec) {
-      if (sg == 0) {
-        d = 0.f;
-        if (a.ssm_in) {
-          const float* src = a.ssm_in + (int64_t)b * a.si_sb + (int64_t)(a.head_begin + 2 * pair + hr) * a.si_sh +
-                             (int64_t)pr * a.si_sp + (int64_t)n * a.si_sn;
-          r = make_float4(src[0], src[a.si_sn], src[2 * a.si_sn], src[3 * a.si_sn]);
+    float d[kCarryQuads];
+    float4 r[kCarryQuads];
+#pragma unroll
+    for (int u = 0; u < kCarryQuads; ++u) {
+      const int t = e[u] / N, n = e[u] % N, hr = t >> 6, pr = t & 63;
+      d[u] = 1.f;                                   // identity for lanes past the last piece
+      r[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (valid[u] && sg < a.nrec) {
+        if (sg == 0) {
+          d[u] = 0.f;
+          if (a.ssm_in) {
+            const float* src = a.ssm_in + (int64_t)b * a.si_sb + (int64_t)(a.head_begin + 2 * pair + hr) * a.si_sh +
+                               (int64_t)pr * a.si_sp + (int64_t)n * a.si_sn;
+            r[u] = make_float4(src[0], src[a.si_sn], src[2 * a.si_sn], src[3 * a.si_sn]);
+          }
+        } else {
+          d[u] = ex2_approx(a.seg_logdecay[(slot + sg - 1) * 2 + hr] * kLog2e);
+          r[u] = rec[(size_t)sg * rstride + e[u] / 4];
         }
-      } else {
-        d = ex2_approx(a.seg_logdecay[(slot + sg - 1) * 2 + hr] * kLog2e);
-        r = rec[(size_t)sg * rstride];
       }
     }
-    if (j == 0 && p0 > 0) {   // chain to the last state of the previous pass
-      r = make_float4(fmaf(d, carry.x, r.x), fmaf(d, carry.y, r.y), fmaf(d, carry.z, r.z), fmaf(d, carry.w, r.w));
-      d = 0.f;
-    }
+#pragma unroll
+    for (int u = 0; u < kCarryQuads; ++u) {
+      if (j == 0 && p0 > 0) {   // chain to the last state of the previous pass
+        r[u] = make_float4(fmaf(d[u], carry[u].x, r[u].x), fmaf(d[u], carry[u].y, r[u].y),
+                           fmaf(d[u], carry[u].z, r[u].z), fmaf(d[u], carry[u].w, r[u].w));
+        d[u] = 0.f;
+      }
 #pragma unroll 1
-    for (int o = 1; o < S; o <<= 1) {
-      const int og = o * G;
-      const float dp = __shfl_up_sync(0xffffffffu, d, og);
-      const float rx = __shfl_up_sync(0xffffffffu, r.x, og), ry = __shfl_up_sync(0xffffffffu, r.y, og);
-      const float rz = __shfl_up_sync(0xffffffffu, r.z, og), rw = __shfl_up_sync(0xffffffffu, r.w, og);
-      if (j >= o) {
-        r = make_float4(fmaf(d, rx, r.x), fmaf(d, ry, r.y), fmaf(d, rz, r.z), fmaf(d, rw, r.w));
-        d *= dp;
+      for (int o = 1; o < S; o <<= 1) {
+        const int og = o * G;
+        const float dp = __shfl_up_sync(0xffffffffu, d[u], og);
+        const float rx = __shfl_up_sync(0xffffffffu, r[u].x, og), ry = __shfl_up_sync(0xffffffffu, r[u].y, og);
+        const float rz = __shfl_up_sync(0xffffffffu, r[u].z, og), rw = __shfl_up_sync(0xffffffffu, r[u].w, og);
+        if (j >= o) {
+          r[u] = make_float4(fmaf(d[u], rx, r[u].x), fmaf(d[u], ry, r[u].y), fmaf(d[u], rz, r[u].z),
+                             fmaf(d[u], rw, r[u].w));
+          d[u] *= dp;
+        }
       }
+      if (valid[u] && sg < a.nrec) rec[(size_t)sg * rstride + e[u] / 4] = r[u];
+      const int last = (S - 1) * G + lane % G;   // piece p0 + S - 1 of this group
+      carry[u] = make_float4(__shfl_sync(0xffffffffu, r[u].x, last), __shfl_sync(0xffffffffu, r[u].y, last),
+                             __shfl_sync(0xffffffffu, r[u].z, last), __shfl_sync(0xffffffffu, r[u].w, last));
     }
-    if (valid && sg < a.nrec) rec[(size_t)sg * rstride] = r;
-    const int last = (S - 1) * G + lane % G;   // segment p0 + S - 1 of this group
-    carry = make_float4(__shfl_sync(0xffffffffu, r.x, last), __shfl_sync(0xffffffffu, r.y, last),
-                        __shfl_sync(0xffffffffu, r.z, last), __shfl_sync(0xffffffffu, r.w, last));
   }
 }
 
@@ -1713,7 +1733,7 @@ int ssd_tc(const SsdArgs& s, void* workspace, size_t workspace_bytes, cudaStream
     int S = 1;
     while (S < a.nrec && S < 32) S <<= 1;   // lanes a sub-warp: a piece each
     const int quads = 128 * s.N / 4;
-    const int per_cta = 256 / S;
+    const int per_cta = 256 / S * kCarryQuads;
     seg_carry_kernel<<<dim3((quads + per_cta - 1) / per_cta, pairs, s.B), 256, 0, stream>>>(a, pairs, S);
     return check_launch("seg_carry_kernel");
   };
